@@ -1,0 +1,870 @@
+// Fused KV block transfer kernels for sm_100a.
+//
+// One kernel family covers every KV movement the block manager needs:
+// layout permutes (block stack <-> universal <-> operational, NHD <-> HND),
+// KV-head resharding for heterogeneous tensor parallelism, block-scaled fp8
+// e4m3 quantisation / dequantisation, and the destination being local HBM,
+// mapped pinned host memory (G2) or a peer GPU's HBM mapped through CUDA IPC
+// (the prefill -> decode path over NVLink 5 / NVSwitch).
+//
+// The unit of work is a tile: the [page_size, head_dim] slab of one KV head
+// of one (block pair, layer, outer) chunk. Rows of a tile (one token's
+// head_dim vector) are contiguous on both sides for every layout the block
+// manager uses, so every access is a 16-byte vector and a row maps to
+// head_dim*elem/16 consecutive lanes.
+//
+// Parity: behaviour of crates/kvbm-kernels/cuda/tensor_kernels.cu:171-259
+// (universal <-> block), :416-461 (NHD <-> HND) and :667-714 (vectorized
+// copy), re-designed as one tiled, warp-per-tile kernel family with
+// fusion of the transforms the reference performs in separate passes or not
+// at all (fp8 arithmetic, head resharding, peer stores).
+#include "common.cuh"
+#include "kvbm_kernels.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+
+using namespace kvbm;
+
+namespace {
+
+constexpr int kWarpsPerCta = 8;
+constexpr int kThreads = kWarpsPerCta * 32;
+constexpr float kE4M3Max = 448.0f;
+
+enum TileKind : int {
+  kCopy = 0,
+  kQuantBf16 = 1,
+  kQuantF16 = 2,
+  kQuantF32 = 3,
+  kDequantBf16 = 4,
+  kDequantF16 = 5,
+  kDequantF32 = 6,
+};
+
+struct XferParams {
+  KvbmSide src;
+  KvbmSide dst;
+  KvbmTileShape shape;
+  int64_t total_tiles;
+  int32_t src_row_bytes;
+  int32_t dst_row_bytes;
+  FastDiv fd_heads, fd_outer, fd_layers;
+  FastDiv fd_upr;  // 16-byte (or U-byte for copies) source units per row
+};
+
+__device__ __forceinline__ const uint8_t* chunk_addr(const KvbmSide& s, int64_t p, int64_t i, int64_t o) {
+  switch (s.mode) {
+    case KVBM_ADDR_LAYER_BASES:
+      return reinterpret_cast<const uint8_t*>(s.layer_base[i]) + static_cast<int64_t>(s.ids[p]) * s.block_stride +
+             o * s.outer_stride;
+    case KVBM_ADDR_BLOCK_TABLE:
+      return reinterpret_cast<const uint8_t*>(s.table[p]) + (s.layer_offset + i) * s.layer_stride +
+             o * s.outer_stride;
+    default:
+      return reinterpret_cast<const uint8_t*>(s.table[(p * s.chunk_layers + i) * s.chunk_outer + o]);
+  }
+}
+
+__device__ __forceinline__ float* scale_addr(const KvbmSide& s, int64_t p, int64_t i, int64_t o, int64_t head) {
+  if (s.scales == nullptr) return nullptr;
+  const int64_t blk = (s.mode == KVBM_ADDR_LAYER_BASES) ? static_cast<int64_t>(s.ids[p]) : p;
+  return s.scales + blk * s.s_block + (s.s_layer_offset + i) * s.s_layer + o * s.s_outer + head * s.s_head;
+}
+
+template <int U>
+struct UnitT;
+template <>
+struct UnitT<16> { using T = int4; };
+template <>
+struct UnitT<8> { using T = int2; };
+template <>
+struct UnitT<4> { using T = int; };
+template <>
+struct UnitT<2> { using T = short; };
+template <>
+struct UnitT<1> { using T = char; };
+
+// ---- per-tile bodies (one warp) --------------------------------------------
+//
+// `src` / `dst` point at row 0 of the tile; rows are `*_rs` bytes apart.
+
+template <int U>
+__device__ __forceinline__ void tile_copy(const uint8_t* src, int64_t src_rs, uint8_t* dst, int64_t dst_rs, int rows,
+                                          const FastDiv& upr, int lane) {
+  using V = typename UnitT<U>::T;
+  constexpr int kBatch = 8;
+  const int n = rows * static_cast<int>(upr.d);
+  for (int base = 0; base < n; base += 32 * kBatch) {
+    V v[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int u = base + k * 32 + lane;
+      if (u < n) {
+        const int r = upr.div(u), c = upr.mod(u, r);
+        v[k] = *reinterpret_cast<const V*>(src + r * src_rs + c * U);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int u = base + k * 32 + lane;
+      if (u < n) {
+        const int r = upr.div(u), c = upr.mod(u, r);
+        *reinterpret_cast<V*>(dst + r * dst_rs + c * U) = v[k];
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void unpack8_16bit(const int4& v, float* f, bool bf16) {
+  const uint32_t w[4] = {(uint32_t)v.x, (uint32_t)v.y, (uint32_t)v.z, (uint32_t)v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 p;
+    if (bf16) {
+      __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
+      p = __bfloat1622float2(b);
+    } else {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[j]);
+      p = __half22float2(h);
+    }
+    f[2 * j] = p.x;
+    f[2 * j + 1] = p.y;
+  }
+}
+
+__device__ __forceinline__ uint16_t pack_fp8x2(float a, float b) {
+  return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
+}
+
+__device__ __forceinline__ float2 unpack_fp8x2(uint16_t x) {
+  __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(x), __NV_E4M3);
+  __half2 h = *reinterpret_cast<__half2*>(&hr);
+  return __half22float2(h);
+}
+
+// Quantise a tile of 16-bit or f32 values to e4m3 with one fp32 scale per
+// tile (per block, layer, outer, head): scale = amax / 448, q = sat(x / scale).
+template <int KIND>
+__device__ __forceinline__ float unit_amax(const int4& v) {
+  if (KIND == kQuantF32) {
+    return fmaxf(fmaxf(fabsf(__int_as_float(v.x)), fabsf(__int_as_float(v.y))),
+                 fmaxf(fabsf(__int_as_float(v.z)), fabsf(__int_as_float(v.w))));
+  }
+  float f[8];
+  unpack8_16bit(v, f, KIND == kQuantBf16);
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(f[j]));
+  return m;
+}
+
+template <int KIND>
+__device__ __forceinline__ void unit_quant_store(const int4& v, float inv, uint8_t* d) {
+  if (KIND == kQuantF32) {
+    const uint16_t a = pack_fp8x2(__int_as_float(v.x) * inv, __int_as_float(v.y) * inv);
+    const uint16_t b = pack_fp8x2(__int_as_float(v.z) * inv, __int_as_float(v.w) * inv);
+    *reinterpret_cast<uint32_t*>(d) = (uint32_t)a | ((uint32_t)b << 16);
+  } else {
+    float f[8];
+    unpack8_16bit(v, f, KIND == kQuantBf16);
+    const uint32_t w0 =
+        (uint32_t)pack_fp8x2(f[0] * inv, f[1] * inv) | ((uint32_t)pack_fp8x2(f[2] * inv, f[3] * inv) << 16);
+    const uint32_t w1 =
+        (uint32_t)pack_fp8x2(f[4] * inv, f[5] * inv) | ((uint32_t)pack_fp8x2(f[6] * inv, f[7] * inv) << 16);
+    *reinterpret_cast<uint2*>(d) = make_uint2(w0, w1);
+  }
+}
+
+// Quantise a tile of 16-bit or f32 values to e4m3 with one fp32 scale per
+// tile (per block, layer, outer, head): scale = amax / 448, q = sat(x / scale).
+// The first 8 units of each lane stay in registers; larger tiles re-read the
+// remainder (an L1/L2 hit) in the second pass.
+template <int KIND>
+__device__ __forceinline__ void tile_quant(const uint8_t* src, int64_t src_rs, uint8_t* dst, int64_t dst_rs,
+                                           int rows, const FastDiv& upr, float* scale_out, int lane) {
+  constexpr int kElems = (KIND == kQuantF32) ? 4 : 8;  // elements per 16-byte source unit
+  constexpr int kOut = kElems;                          // fp8 bytes written per unit
+  constexpr int kCache = 8;
+  const int n = rows * static_cast<int>(upr.d);
+  int4 cache[kCache];
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < kCache; ++k) {
+    const int u = k * 32 + lane;
+    if (u < n) {
+      const int r = upr.div(u), c = upr.mod(u, r);
+      cache[k] = *reinterpret_cast<const int4*>(src + r * src_rs + c * 16);
+      amax = fmaxf(amax, unit_amax<KIND>(cache[k]));
+    }
+  }
+  for (int u = kCache * 32 + lane; u < n; u += 32) {
+    const int r = upr.div(u), c = upr.mod(u, r);
+    amax = fmaxf(amax, unit_amax<KIND>(*reinterpret_cast<const int4*>(src + r * src_rs + c * 16)));
+  }
+  amax = warp_max(amax);
+  const float scale = amax > 0.f ? amax / kE4M3Max : 1.0f;
+  const float inv = amax > 0.f ? kE4M3Max / amax : 1.0f;
+#pragma unroll
+  for (int k = 0; k < kCache; ++k) {
+    const int u = k * 32 + lane;
+    if (u < n) {
+      const int r = upr.div(u), c = upr.mod(u, r);
+      unit_quant_store<KIND>(cache[k], inv, dst + r * dst_rs + c * kOut);
+    }
+  }
+  for (int u = kCache * 32 + lane; u < n; u += 32) {
+    const int r = upr.div(u), c = upr.mod(u, r);
+    unit_quant_store<KIND>(*reinterpret_cast<const int4*>(src + r * src_rs + c * 16), inv, dst + r * dst_rs + c * kOut);
+  }
+  if (lane == 0 && scale_out != nullptr) *scale_out = scale;
+}
+
+// Dequantise an e4m3 tile into 16-bit or f32 values: x = q * scale.
+template <int KIND>
+__device__ __forceinline__ void tile_dequant(const uint8_t* src, int64_t src_rs, uint8_t* dst, int64_t dst_rs,
+                                             int rows, const FastDiv& upr, const float* scale_in, int lane) {
+  const float scale = scale_in ? *scale_in : 1.0f;
+  const int n = rows * static_cast<int>(upr.d);  // 16 fp8 per source unit
+  for (int u = lane; u < n; u += 32) {
+    const int r = upr.div(u), c = upr.mod(u, r);
+    const int4 v = *reinterpret_cast<const int4*>(src + r * src_rs + c * 16);
+    const uint32_t w[4] = {(uint32_t)v.x, (uint32_t)v.y, (uint32_t)v.z, (uint32_t)v.w};
+    float f[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 a = unpack_fp8x2(static_cast<uint16_t>(w[j] & 0xffffu));
+      const float2 b = unpack_fp8x2(static_cast<uint16_t>(w[j] >> 16));
+      f[4 * j + 0] = a.x * scale;
+      f[4 * j + 1] = a.y * scale;
+      f[4 * j + 2] = b.x * scale;
+      f[4 * j + 3] = b.y * scale;
+    }
+    uint8_t* d = dst + r * dst_rs;
+    if (KIND == kDequantF32) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<float4*>(d + c * 64 + q * 16) = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+    } else {
+      uint32_t o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (KIND == kDequantBf16) {
+          __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+          o[j] = *reinterpret_cast<uint32_t*>(&b);
+        } else {
+          __half2 h = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+          o[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+      }
+      *reinterpret_cast<int4*>(d + c * 32) = make_int4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<int4*>(d + c * 32 + 16) = make_int4(o[4], o[5], o[6], o[7]);
+    }
+  }
+}
+
+template <int KIND, int U>
+__device__ __forceinline__ void run_tile(const XferParams& P, const uint8_t* s, int64_t s_rs, uint8_t* d,
+                                         int64_t d_rs, int64_t p, int64_t i, int64_t o, int h, int lane) {
+  const int rows = P.shape.page_size;
+  const int hd = P.shape.head_dim;
+  if constexpr (KIND == kCopy) {
+    tile_copy<U>(s, s_rs, d, d_rs, rows, P.fd_upr, lane);
+    // fp8 -> fp8 copies carry their scales along.
+    if (lane == 0 && P.src.scales != nullptr && P.dst.scales != nullptr) {
+      *scale_addr(P.dst, p, i, o, h + P.dst.head_offset) = *scale_addr(P.src, p, i, o, h + P.src.head_offset);
+    }
+  } else if constexpr (KIND == kQuantBf16 || KIND == kQuantF16 || KIND == kQuantF32) {
+    tile_quant<KIND>(s, s_rs, d, d_rs, rows, P.fd_upr, scale_addr(P.dst, p, i, o, h + P.dst.head_offset), lane);
+  } else {
+    tile_dequant<KIND>(s, s_rs, d, d_rs, rows, P.fd_upr, scale_addr(P.src, p, i, o, h + P.src.head_offset), lane);
+  }
+}
+
+// Warp-per-tile kernel. Tiles are ordered (pair, layer, outer, head) with
+// head fastest so the warps of one CTA sweep one contiguous chunk together.
+template <int KIND, int U>
+__global__ void __launch_bounds__(kThreads) kv_tile_xfer_kernel(const __grid_constant__ XferParams P) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerCta;
+  for (int64_t t = warp; t < P.total_tiles; t += nwarps) {
+    // 32-bit decode through precomputed reciprocals (total_tiles < 2^31)
+    const uint32_t t32 = static_cast<uint32_t>(t);
+    const uint32_t q1 = P.fd_heads.div(t32);
+    const int h = static_cast<int>(P.fd_heads.mod(t32, q1));
+    const uint32_t q2 = P.fd_outer.div(q1);
+    const int64_t o = P.fd_outer.mod(q1, q2);
+    const uint32_t q3 = P.fd_layers.div(q2);
+    const int64_t i = P.fd_layers.mod(q2, q3);
+    const int64_t p = q3;
+    const uint8_t* s = chunk_addr(P.src, p, i, o) + static_cast<int64_t>(h + P.src.head_offset) * P.src.head_stride;
+    uint8_t* d = const_cast<uint8_t*>(chunk_addr(P.dst, p, i, o)) +
+                 static_cast<int64_t>(h + P.dst.head_offset) * P.dst.head_stride;
+    run_tile<KIND, U>(P, s, P.src.token_stride, d, P.dst.token_stride, p, i, o, h, lane);
+  }
+}
+
+int g_sm_count = 0;
+
+int sm_count() {
+  if (g_sm_count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (g_sm_count <= 0) g_sm_count = 148;
+  }
+  return g_sm_count;
+}
+
+int dtype_bytes(int dt) {
+  switch (dt) {
+    case KVBM_F16:
+    case KVBM_BF16:
+      return 2;
+    case KVBM_F32:
+      return 4;
+    case KVBM_F64:
+      return 8;
+    case KVBM_FP8_E4M3:
+      return 1;
+    default:
+      return 0;
+  }
+}
+
+int pick_kind(int sdt, int ddt) {
+  if (sdt == ddt) return kCopy;
+  if (ddt == KVBM_FP8_E4M3) {
+    if (sdt == KVBM_BF16) return kQuantBf16;
+    if (sdt == KVBM_F16) return kQuantF16;
+    if (sdt == KVBM_F32) return kQuantF32;
+  }
+  if (sdt == KVBM_FP8_E4M3) {
+    if (ddt == KVBM_BF16) return kDequantBf16;
+    if (ddt == KVBM_F16) return kDequantF16;
+    if (ddt == KVBM_F32) return kDequantF32;
+  }
+  return -1;
+}
+
+bool side_ok(const KvbmSide& s, int layers) {
+  if (s.mode == KVBM_ADDR_LAYER_BASES) {
+    if (s.ids == nullptr || layers > KVBM_MAX_LAYERS) return false;
+    for (int i = 0; i < layers; ++i)
+      if (s.layer_base[i] == 0) return false;
+    return true;
+  }
+  if (s.mode == KVBM_ADDR_BLOCK_TABLE) return s.table != nullptr;
+  if (s.mode == KVBM_ADDR_CHUNK_TABLE) return s.table != nullptr && s.chunk_layers > 0 && s.chunk_outer > 0;
+  return false;
+}
+
+// Largest power-of-two unit (<= 16) dividing every byte quantity given.
+int common_align(std::initializer_list<int64_t> xs) {
+  int a = 16;
+  for (int64_t x : xs) {
+    while (a > 1 && (x % a) != 0) a >>= 1;
+  }
+  return a;
+}
+
+template <int KIND, int U>
+cudaError_t launch_tile(const XferParams& P, int max_ctas, cudaStream_t stream) {
+  const int64_t ctas_needed = (P.total_tiles + kWarpsPerCta - 1) / kWarpsPerCta;
+  int64_t cap = max_ctas > 0 ? max_ctas : static_cast<int64_t>(sm_count()) * 8;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min(ctas_needed, cap)));
+  kv_tile_xfer_kernel<KIND, U><<<grid, kThreads, 0, stream>>>(P);
+  return cudaGetLastError();
+}
+
+cudaError_t dispatch_tile(const XferParams& P, int kind, int unit, int max_ctas, cudaStream_t stream) {
+  switch (kind) {
+    case kCopy:
+      switch (unit) {
+        case 16: return launch_tile<kCopy, 16>(P, max_ctas, stream);
+        case 8: return launch_tile<kCopy, 8>(P, max_ctas, stream);
+        case 4: return launch_tile<kCopy, 4>(P, max_ctas, stream);
+        case 2: return launch_tile<kCopy, 2>(P, max_ctas, stream);
+        default: return launch_tile<kCopy, 1>(P, max_ctas, stream);
+      }
+    case kQuantBf16: return launch_tile<kQuantBf16, 16>(P, max_ctas, stream);
+    case kQuantF16: return launch_tile<kQuantF16, 16>(P, max_ctas, stream);
+    case kQuantF32: return launch_tile<kQuantF32, 16>(P, max_ctas, stream);
+    case kDequantBf16: return launch_tile<kDequantBf16, 16>(P, max_ctas, stream);
+    case kDequantF16: return launch_tile<kDequantF16, 16>(P, max_ctas, stream);
+    case kDequantF32: return launch_tile<kDequantF32, 16>(P, max_ctas, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// Validates the request and fills P; returns the tile kind or -1.
+int prepare(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape, XferParams& P, int* unit_out) {
+  if (!src || !dst || !shape) return -1;
+  const KvbmTileShape& S = *shape;
+  if (S.num_pairs < 0 || S.num_layers < 0 || S.num_outer <= 0 || S.num_heads <= 0 || S.page_size <= 0 ||
+      S.head_dim <= 0)
+    return -1;
+  if (S.num_layers > KVBM_MAX_LAYERS && (src->mode == KVBM_ADDR_LAYER_BASES || dst->mode == KVBM_ADDR_LAYER_BASES))
+    return -1;
+  if (src->head_offset < 0 || dst->head_offset < 0) return -1;
+  const int kind = pick_kind(S.src_dtype, S.dst_dtype);
+  if (kind < 0) return -1;
+  const int sb = dtype_bytes(S.src_dtype), db = dtype_bytes(S.dst_dtype);
+  std::memcpy(&P.src, src, sizeof(KvbmSide));
+  std::memcpy(&P.dst, dst, sizeof(KvbmSide));
+  P.shape = S;
+  P.total_tiles = static_cast<int64_t>(S.num_pairs) * S.num_layers * S.num_outer * S.num_heads;
+  P.src_row_bytes = S.head_dim * sb;
+  P.dst_row_bytes = S.head_dim * db;
+  if (P.total_tiles >= (int64_t(1) << 31)) return -1;  // callers split larger batches
+  P.fd_heads = FastDiv(static_cast<uint32_t>(S.num_heads));
+  P.fd_outer = FastDiv(static_cast<uint32_t>(S.num_outer));
+  P.fd_layers = FastDiv(static_cast<uint32_t>(std::max(1, S.num_layers)));
+  if (P.total_tiles == 0) {
+    *unit_out = 16;
+    return kind;
+  }
+  if (!side_ok(P.src, S.num_layers) || !side_ok(P.dst, S.num_layers)) return -1;
+  if (kind == kCopy) {
+    int64_t a = common_align({P.src_row_bytes, P.src.token_stride, P.src.head_stride, P.dst.token_stride,
+                              P.dst.head_stride, P.src.block_stride, P.dst.block_stride, P.src.outer_stride,
+                              P.dst.outer_stride, P.src.layer_stride, P.dst.layer_stride});
+    for (int i = 0; i < S.num_layers && P.src.mode == KVBM_ADDR_LAYER_BASES; ++i)
+      a = std::min<int64_t>(a, common_align({static_cast<int64_t>(P.src.layer_base[i])}));
+    for (int i = 0; i < S.num_layers && P.dst.mode == KVBM_ADDR_LAYER_BASES; ++i)
+      a = std::min<int64_t>(a, common_align({static_cast<int64_t>(P.dst.layer_base[i])}));
+    // Table-mode base pointers are device-resident; the caller guarantees the
+    // element alignment, so the unit never drops below the element size.
+    *unit_out = static_cast<int>(std::max<int64_t>(a, sb));
+    if (*unit_out > 16) *unit_out = 16;
+  } else {
+    // Conversions work on 16-byte source units and need 16 fp8 / 8 x 16-bit
+    // elements per unit, with every row start 16-byte aligned on both sides.
+    if (S.head_dim % 16 != 0) return -1;
+    const int64_t a = common_align({P.src.token_stride, P.src.head_stride, P.dst.token_stride, P.dst.head_stride,
+                                    P.src.block_stride, P.dst.block_stride, P.src.outer_stride, P.dst.outer_stride,
+                                    P.src.layer_stride, P.dst.layer_stride});
+    if (a < 16) return -1;
+    *unit_out = 16;
+  }
+  P.fd_upr = FastDiv(static_cast<uint32_t>(P.src_row_bytes / *unit_out));
+  return kind;
+}
+
+}  // namespace
+
+extern "C" int kvbm_sm_count(void) { return sm_count(); }
+
+extern "C" int kvbm_kv_tile_xfer(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape, int max_ctas,
+                                 cudaStream_t stream) {
+  XferParams P;
+  int unit = 16;
+  const int kind = prepare(src, dst, shape, P, &unit);
+  if (kind < 0) return cudaErrorInvalidValue;
+  if (P.total_tiles == 0) return cudaSuccess;
+  return dispatch_tile(P, kind, unit, max_ctas, stream);
+}
+
+// ---------------------------------------------------------------------------
+// TMA-staged chunk pipeline.
+//
+// One CTA = 1 producer warp + 8 consumer warps. The producer's elected lane
+// issues 1-D bulk async copies (cp.async.bulk, local source) of a whole
+// (pair, layer, outer) chunk, or of its per-token / per-head contiguous runs,
+// into a ring of shared-memory stages; completion is counted in bytes on a
+// "full" mbarrier per stage. Consumer warps take one head tile each from the
+// staged chunk, convert it and store it to the destination, then arrive on
+// the stage's "empty" mbarrier. Every wait is bounded by %globaltimer.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kPipeThreads = (kConsumerWarps + 1) * 32;
+constexpr uint64_t kPipeWaitNs = 2000000000ull;  // 2 s
+
+struct PipeParams {
+  XferParams x;
+  int32_t stages;
+  int32_t stage_bytes;
+  int32_t chunk_bytes;      // bytes copied per chunk
+  int32_t run_bytes;        // bytes per contiguous run
+  int32_t num_runs;         // runs per chunk
+  int32_t src_nhd;          // 1: smem rows ordered [token][head], 0: [head][token]
+  int64_t run_stride;       // global-memory stride between runs
+  int64_t total_chunks;
+  int* status;              // device status word (may be null)
+};
+
+template <int KIND>
+__global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __grid_constant__ PipeParams Q) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const XferParams& P = Q.x;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* empty_bar = full_bar + Q.stages;
+  uint8_t* stage_base = smem_raw + 1024;  // barriers live in the first 1 KiB
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Q.stages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int H = P.shape.num_heads, O = P.shape.num_outer, L = P.shape.num_layers;
+  const int T = P.shape.page_size;
+  const int64_t row = P.src_row_bytes;
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int64_t k = 0;
+      bool ok = true;
+      for (int64_t c = blockIdx.x; c < Q.total_chunks && ok; c += gridDim.x, ++k) {
+        const int s = static_cast<int>(k % Q.stages);
+        const uint32_t phase = static_cast<uint32_t>((k / Q.stages) & 1);
+        if (k >= Q.stages && !mbar_wait_bounded(&empty_bar[s], phase ^ 1u, kPipeWaitNs)) {
+          ok = false;
+          break;
+        }
+        int64_t r = c;
+        const int64_t o = r % O;
+        r /= O;
+        const int64_t i = r % L;
+        const int64_t p = r / L;
+        const uint8_t* base = chunk_addr(P.src, p, i, o) +
+                              (Q.src_nhd ? static_cast<int64_t>(P.src.head_offset) * row
+                                         : static_cast<int64_t>(P.src.head_offset) * P.src.head_stride);
+        if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) {
+          // Never issue a misaligned bulk copy: record it and stop.
+          if (Q.status) atomicExch(Q.status, kStatusBadIndex);
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(Q.chunk_bytes));
+        uint8_t* dst = stage_base + static_cast<int64_t>(s) * Q.stage_bytes;
+        for (int j = 0; j < Q.num_runs; ++j)
+          bulk_g2s(dst + static_cast<int64_t>(j) * Q.run_bytes, base + j * Q.run_stride,
+                   static_cast<uint32_t>(Q.run_bytes), &full_bar[s]);
+      }
+      if (!ok) {
+        if (Q.status) atomicCAS(Q.status, kStatusOk, kStatusPipelineTimeout);
+        // Drain: wait (bounded) for the copies already issued so none are in
+        // flight when the CTA exits.
+        const int64_t issued = k;
+        const int64_t first = issued > Q.stages ? issued - Q.stages : 0;
+        for (int64_t kk = first; kk < issued; ++kk) {
+          const int s = static_cast<int>(kk % Q.stages);
+          mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>((kk / Q.stages) & 1), kPipeWaitNs);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  int64_t k = 0;
+  for (int64_t c = blockIdx.x; c < Q.total_chunks; c += gridDim.x, ++k) {
+    const int s = static_cast<int>(k % Q.stages);
+    const uint32_t phase = static_cast<uint32_t>((k / Q.stages) & 1);
+    if (!mbar_wait_bounded(&full_bar[s], phase, kPipeWaitNs)) {
+      if (Q.status && lane == 0) atomicCAS(Q.status, kStatusOk, kStatusPipelineTimeout);
+      break;
+    }
+    int64_t r = c;
+    const int64_t o = r % O;
+    r /= O;
+    const int64_t i = r % L;
+    const int64_t p = r / L;
+    const uint8_t* sbuf = stage_base + static_cast<int64_t>(s) * Q.stage_bytes;
+    uint8_t* dchunk = const_cast<uint8_t*>(chunk_addr(P.dst, p, i, o));
+    for (int h = warp; h < H; h += kConsumerWarps) {
+      const uint8_t* srow = Q.src_nhd ? sbuf + h * row : sbuf + static_cast<int64_t>(h) * T * row;
+      const int64_t s_rs = Q.src_nhd ? static_cast<int64_t>(H) * row : row;
+      uint8_t* d = dchunk + static_cast<int64_t>(h + P.dst.head_offset) * P.dst.head_stride;
+      run_tile<KIND, 16>(P, srow, s_rs, d, P.dst.token_stride, p, i, o, h, lane);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);
+  }
+}
+
+template <int KIND>
+cudaError_t launch_pipe(PipeParams& Q, int max_ctas, cudaStream_t stream) {
+  const size_t smem = 1024 + static_cast<size_t>(Q.stages) * Q.stage_bytes;
+  cudaError_t e = cudaFuncSetAttribute(kv_chunk_pipe_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const int64_t cap = max_ctas > 0 ? max_ctas : sm_count();
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(Q.total_chunks, cap)));
+  kv_chunk_pipe_kernel<KIND><<<grid, kPipeThreads, smem, stream>>>(Q);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" int kvbm_kv_chunk_xfer_tma(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape,
+                                      int max_ctas, cudaStream_t stream) {
+  PipeParams Q;
+  std::memset(&Q, 0, sizeof(Q));
+  int unit = 16;
+  const int kind = prepare(src, dst, shape, Q.x, &unit);
+  if (kind < 0) return cudaErrorInvalidValue;
+  if (Q.x.total_tiles == 0) return cudaSuccess;
+  const KvbmTileShape& S = Q.x.shape;
+  const int64_t row = Q.x.src_row_bytes;
+  const KvbmSide& s = Q.x.src;
+  if (row % 16 != 0 || (kind == kCopy && Q.x.dst_row_bytes % 16 != 0)) return cudaErrorInvalidValue;
+  // Find the contiguous runs of one chunk on the source side.
+  if (s.head_stride == row) {
+    // NHD-like: each token holds its heads back to back.
+    Q.src_nhd = 1;
+    if (s.token_stride == row * S.num_heads) {
+      Q.num_runs = 1;
+      Q.run_bytes = static_cast<int32_t>(row * S.num_heads * S.page_size);
+    } else {
+      Q.num_runs = S.page_size;
+      Q.run_bytes = static_cast<int32_t>(row * S.num_heads);
+      Q.run_stride = s.token_stride;
+    }
+  } else if (s.token_stride == row) {
+    // HND-like: each head holds its tokens back to back.
+    Q.src_nhd = 0;
+    if (s.head_stride == row * S.page_size) {
+      Q.num_runs = 1;
+      Q.run_bytes = static_cast<int32_t>(row * S.num_heads * S.page_size);
+    } else {
+      Q.num_runs = S.num_heads;
+      Q.run_bytes = static_cast<int32_t>(row * S.page_size);
+      Q.run_stride = s.head_stride;
+    }
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  if (Q.run_bytes % 16 != 0 || Q.run_stride % 16 != 0) return cudaErrorInvalidValue;
+  Q.chunk_bytes = Q.run_bytes * Q.num_runs;
+  Q.stage_bytes = (Q.chunk_bytes + 127) / 128 * 128;
+  const int budget = 200 * 1024;
+  Q.stages = std::min(4, budget / Q.stage_bytes);
+  if (Q.stages < 2) return cudaErrorInvalidValue;
+  Q.total_chunks = static_cast<int64_t>(S.num_pairs) * S.num_layers * S.num_outer;
+  Q.status = nullptr;
+  switch (kind) {
+    case kCopy: return launch_pipe<kCopy>(Q, max_ctas, stream);
+    case kQuantBf16: return launch_pipe<kQuantBf16>(Q, max_ctas, stream);
+    case kQuantF16: return launch_pipe<kQuantF16>(Q, max_ctas, stream);
+    case kQuantF32: return launch_pipe<kQuantF32>(Q, max_ctas, stream);
+    case kDequantBf16: return launch_pipe<kDequantBf16>(Q, max_ctas, stream);
+    case kDequantF16: return launch_pipe<kDequantF16>(Q, max_ctas, stream);
+    case kDequantF32: return launch_pipe<kDequantF32>(Q, max_ctas, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Reference-compatible permutes (pointer-table API), expressed as tile
+// transfers.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+void fill_universal(KvbmSide& u, const void* const* ptrs, size_t nh, size_t no, size_t nt, size_t hd, size_t nl_full,
+                    size_t nl_offset, int eb) {
+  std::memset(&u, 0, sizeof(u));
+  u.mode = KVBM_ADDR_BLOCK_TABLE;
+  u.table = reinterpret_cast<const uint64_t*>(ptrs);
+  u.token_stride = static_cast<int64_t>(hd) * eb;
+  u.outer_stride = static_cast<int64_t>(nt * hd) * eb;
+  u.layer_stride = static_cast<int64_t>(no * nt * hd) * eb;
+  u.head_stride = static_cast<int64_t>(nl_full * no * nt * hd) * eb;
+  u.layer_offset = static_cast<int64_t>(nl_offset);
+  (void)nh;
+}
+
+void fill_stack(KvbmSide& b, const void* const* ptrs, size_t nl, size_t no, size_t nt, size_t nh, size_t hd,
+                int layout, int eb) {
+  std::memset(&b, 0, sizeof(b));
+  b.mode = KVBM_ADDR_CHUNK_TABLE;
+  b.table = reinterpret_cast<const uint64_t*>(ptrs);
+  b.chunk_layers = static_cast<int32_t>(nl);
+  b.chunk_outer = static_cast<int32_t>(no);
+  if (layout == KVBM_NHD) {
+    b.token_stride = static_cast<int64_t>(nh * hd) * eb;
+    b.head_stride = static_cast<int64_t>(hd) * eb;
+  } else {
+    b.token_stride = static_cast<int64_t>(hd) * eb;
+    b.head_stride = static_cast<int64_t>(nt * hd) * eb;
+  }
+}
+
+int permute_common(const KvbmSide& src, const KvbmSide& dst, size_t num_blocks, size_t nh, size_t nl, size_t no,
+                   size_t nt, size_t hd, int dtype, cudaStream_t stream) {
+  if (dtype_bytes(dtype) == 0) return cudaErrorInvalidValue;
+  if (num_blocks == 0 || nh == 0 || nl == 0 || no == 0 || nt == 0 || hd == 0) return cudaSuccess;
+  KvbmTileShape S;
+  S.num_pairs = static_cast<int32_t>(num_blocks);
+  S.num_layers = static_cast<int32_t>(nl);
+  S.num_outer = static_cast<int32_t>(no);
+  S.num_heads = static_cast<int32_t>(nh);
+  S.page_size = static_cast<int32_t>(nt);
+  S.head_dim = static_cast<int32_t>(hd);
+  S.src_dtype = dtype;
+  S.dst_dtype = dtype;
+  return kvbm_kv_tile_xfer(&src, &dst, &S, 0, stream);
+}
+
+}  // namespace
+
+extern "C" int kvbm_universal_from_block(void* const* universal_ptrs, const void* const* block_ptrs,
+                                         size_t num_blocks, size_t nh, size_t nl, size_t no, size_t nt, size_t hd,
+                                         size_t nl_full, size_t nl_offset, int dtype, int layout,
+                                         cudaStream_t stream) {
+  if (num_blocks == 0) return cudaSuccess;
+  if (!universal_ptrs || !block_ptrs || nl_offset + nl > nl_full) return cudaErrorInvalidValue;
+  if (layout != KVBM_NHD && layout != KVBM_HND) return cudaErrorInvalidValue;
+  const int eb = dtype_bytes(dtype);
+  if (eb == 0) return cudaErrorInvalidValue;
+  KvbmSide src, dst;
+  fill_stack(src, block_ptrs, nl, no, nt, nh, hd, layout, eb);
+  fill_universal(dst, const_cast<const void* const*>(universal_ptrs), nh, no, nt, hd, nl_full, nl_offset, eb);
+  return permute_common(src, dst, num_blocks, nh, nl, no, nt, hd, dtype, stream);
+}
+
+extern "C" int kvbm_block_from_universal(const void* const* universal_ptrs, void* const* block_ptrs,
+                                         size_t num_blocks, size_t nh, size_t nl, size_t no, size_t nt, size_t hd,
+                                         size_t nl_full, size_t nl_offset, int dtype, int layout,
+                                         cudaStream_t stream) {
+  if (num_blocks == 0) return cudaSuccess;
+  if (!universal_ptrs || !block_ptrs || nl_offset + nl > nl_full) return cudaErrorInvalidValue;
+  if (layout != KVBM_NHD && layout != KVBM_HND) return cudaErrorInvalidValue;
+  const int eb = dtype_bytes(dtype);
+  if (eb == 0) return cudaErrorInvalidValue;
+  KvbmSide src, dst;
+  fill_universal(src, universal_ptrs, nh, no, nt, hd, nl_full, nl_offset, eb);
+  fill_stack(dst, const_cast<const void* const*>(block_ptrs), nl, no, nt, nh, hd, layout, eb);
+  return permute_common(src, dst, num_blocks, nh, nl, no, nt, hd, dtype, stream);
+}
+
+extern "C" int kvbm_nhd_hnd_transpose(const void* const* src_chunks, void* const* dst_chunks, size_t num_blocks,
+                                      size_t nl, size_t no, size_t nt, size_t nh, size_t hd, int dtype,
+                                      int src_layout, cudaStream_t stream) {
+  if (num_blocks == 0) return cudaSuccess;
+  if (!src_chunks || !dst_chunks) return cudaErrorInvalidValue;
+  if (src_layout != KVBM_NHD && src_layout != KVBM_HND) return cudaErrorInvalidValue;
+  const int eb = dtype_bytes(dtype);
+  if (eb == 0) return cudaErrorInvalidValue;
+  KvbmSide src, dst;
+  fill_stack(src, src_chunks, nl, no, nt, nh, hd, src_layout, eb);
+  fill_stack(dst, const_cast<const void* const*>(dst_chunks), nl, no, nt, nh, hd,
+             src_layout == KVBM_NHD ? KVBM_HND : KVBM_NHD, eb);
+  return permute_common(src, dst, num_blocks, nh, nl, no, nt, hd, dtype, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Split-by-bytes batched copy (replaces one-CTA-per-pair copying).
+// ---------------------------------------------------------------------------
+
+namespace {
+
+template <int U>
+__global__ void __launch_bounds__(kThreads) copy_pairs_kernel(const uint64_t* __restrict__ src_ptrs,
+                                                             const uint64_t* __restrict__ dst_ptrs,
+                                                             uint64_t num_pairs, uint64_t bytes,
+                                                             uint64_t chunks_per_pair) {
+  using V = typename UnitT<U>::T;
+  constexpr int kBatch = 8;
+  constexpr uint64_t kChunk = 32ull * kBatch * U;  // bytes per warp work item
+  const int lane = threadIdx.x & 31;
+  const uint64_t warp = static_cast<uint64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+  const uint64_t nwarps = static_cast<uint64_t>(gridDim.x) * kWarpsPerCta;
+  const uint64_t total = num_pairs * chunks_per_pair;
+  for (uint64_t w = warp; w < total; w += nwarps) {
+    const uint64_t p = w / chunks_per_pair;
+    const uint64_t off = (w - p * chunks_per_pair) * kChunk;
+    const uint8_t* s = reinterpret_cast<const uint8_t*>(src_ptrs[p]) + off;
+    uint8_t* d = reinterpret_cast<uint8_t*>(dst_ptrs[p]) + off;
+    const uint64_t n = min(kChunk, bytes - off) / U;
+    V v[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const uint64_t u = k * 32 + lane;
+      if (u < n) v[k] = *reinterpret_cast<const V*>(s + u * U);
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const uint64_t u = k * 32 + lane;
+      if (u < n) *reinterpret_cast<V*>(d + u * U) = v[k];
+    }
+  }
+}
+
+template <int U>
+cudaError_t launch_copy(const uint64_t* s, const uint64_t* d, uint64_t n, uint64_t bytes, int max_ctas,
+                        cudaStream_t stream) {
+  constexpr uint64_t kChunk = 32ull * 8 * U;
+  const uint64_t cpp = (bytes + kChunk - 1) / kChunk;
+  const uint64_t work = n * cpp;
+  const uint64_t need = (work + kWarpsPerCta - 1) / kWarpsPerCta;
+  const uint64_t cap = max_ctas > 0 ? static_cast<uint64_t>(max_ctas) : static_cast<uint64_t>(sm_count()) * 8;
+  const int grid = static_cast<int>(std::max<uint64_t>(1, std::min(need, cap)));
+  copy_pairs_kernel<U><<<grid, kThreads, 0, stream>>>(s, d, n, bytes, cpp);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" int kvbm_copy_pairs(const uint64_t* src_ptrs, const uint64_t* dst_ptrs, uint64_t num_pairs,
+                               uint64_t bytes_per_pair, int align, int max_ctas, cudaStream_t stream) {
+  if (num_pairs == 0 || bytes_per_pair == 0) return cudaSuccess;
+  if (!src_ptrs || !dst_ptrs) return cudaErrorInvalidValue;
+  int a = 16;
+  while (a > 1 && (align % a != 0 || bytes_per_pair % a != 0)) a >>= 1;
+  switch (a) {
+    case 16: return launch_copy<16>(src_ptrs, dst_ptrs, num_pairs, bytes_per_pair, max_ctas, stream);
+    case 8: return launch_copy<8>(src_ptrs, dst_ptrs, num_pairs, bytes_per_pair, max_ctas, stream);
+    case 4: return launch_copy<4>(src_ptrs, dst_ptrs, num_pairs, bytes_per_pair, max_ctas, stream);
+    case 2: return launch_copy<2>(src_ptrs, dst_ptrs, num_pairs, bytes_per_pair, max_ctas, stream);
+    default: return launch_copy<1>(src_ptrs, dst_ptrs, num_pairs, bytes_per_pair, max_ctas, stream);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// System-scope completion flags.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+__global__ void signal_kernel(uint64_t* flag, uint64_t value) {
+  fence_acq_rel_sys();
+  st_release_sys_u64(flag, value);
+}
+
+__global__ void wait_kernel(const uint64_t* flag, uint64_t expected, uint64_t timeout_ns, int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_sys_u64(flag) < expected) {
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      if (status) atomicExch(status, kStatusWaitTimeout);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
+}  // namespace
+
+extern "C" int kvbm_signal_flag(uint64_t* flag, uint64_t value, cudaStream_t stream) {
+  if (!flag) return cudaErrorInvalidValue;
+  signal_kernel<<<1, 1, 0, stream>>>(flag, value);
+  return cudaGetLastError();
+}
+
+extern "C" int kvbm_wait_flag(const uint64_t* flag, uint64_t expected, uint64_t timeout_ns, int* status,
+                              cudaStream_t stream) {
+  if (!flag) return cudaErrorInvalidValue;
+  wait_kernel<<<1, 1, 0, stream>>>(flag, expected, timeout_ns, status);
+  return cudaGetLastError();
+}

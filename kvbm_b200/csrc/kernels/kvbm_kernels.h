@@ -1,0 +1,114 @@
+// C ABI of the kvbm_b200 sm_100a kernel library (libkvbm_cuda.so).
+//
+// Every entry point returns a cudaError_t value as int (0 = success) and is
+// asynchronous on the given stream. Pointer tables passed to kernels must be
+// device-accessible (device memory or mapped pinned host memory).
+//
+// Behavioural parity (not code) with the reference kernel ABI:
+//   kvbm_universal_from_block   <-> crates/kvbm-kernels/cuda/tensor_kernels.cu:347 (K1)
+//   kvbm_block_from_universal   <-> crates/kvbm-kernels/cuda/tensor_kernels.cu:376 (K2)
+//   kvbm_nhd_hnd_transpose      <-> crates/kvbm-kernels/cuda/tensor_kernels.cu:502 (K3)
+//   kvbm_copy_pairs             <-> crates/kvbm-kernels/cuda/tensor_kernels.cu:724 (K4)
+// Dtype codes keep the reference's numbering (crates/kvbm-kernels/src/tensor_kernels.rs:40)
+// and the block layout codes keep NHD=0 / HND=1 (tensor_kernels.rs:51).
+#pragma once
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVBM_MAX_LAYERS 128
+
+enum KvbmDtype { KVBM_F16 = 0, KVBM_BF16 = 1, KVBM_F32 = 2, KVBM_F64 = 3, KVBM_FP8_E4M3 = 4 };
+enum KvbmBlockLayout { KVBM_NHD = 0, KVBM_HND = 1 };
+
+// How one side of a tile transfer turns (pair p, layer i, outer o) into a
+// base address. A tile is the [page_size, head_dim] slab of one head.
+enum KvbmAddrMode {
+  // layer_base[i] + ids[p] * block_stride + o * outer_stride
+  KVBM_ADDR_LAYER_BASES = 0,
+  // table[p] + (layer_offset + i) * layer_stride + o * outer_stride
+  KVBM_ADDR_BLOCK_TABLE = 1,
+  // table[(p * chunk_layers + i) * chunk_outer + o]
+  KVBM_ADDR_CHUNK_TABLE = 2,
+};
+
+typedef struct KvbmSide {
+  int32_t mode;
+  int32_t head_offset;     // added to the tile's head index on this side
+  int32_t chunk_layers;    // CHUNK_TABLE: layers per block in the table
+  int32_t chunk_outer;     // CHUNK_TABLE: outer chunks per layer in the table
+  const uint64_t* table;   // BLOCK_TABLE / CHUNK_TABLE pointer table (device-accessible)
+  const int32_t* ids;      // LAYER_BASES block ids (device-accessible), one per pair
+  int64_t block_stride;    // bytes
+  int64_t layer_stride;    // bytes (BLOCK_TABLE)
+  int64_t layer_offset;    // layers (BLOCK_TABLE)
+  int64_t outer_stride;    // bytes
+  int64_t token_stride;    // bytes
+  int64_t head_stride;     // bytes
+  // Optional fp32 scales for fp8 data, one per (block, layer, outer, head):
+  // scales[blk * s_block + (s_layer_offset + i) * s_layer + o * s_outer + head * s_head]
+  // where blk = ids[p] in LAYER_BASES mode and p otherwise.
+  float* scales;
+  int64_t s_block, s_layer, s_outer, s_head, s_layer_offset;
+  uint64_t layer_base[KVBM_MAX_LAYERS];
+} KvbmSide;
+
+typedef struct KvbmTileShape {
+  int32_t num_pairs;
+  int32_t num_layers;
+  int32_t num_outer;
+  int32_t num_heads;   // heads moved per tile set
+  int32_t page_size;   // tokens per block
+  int32_t head_dim;    // elements
+  int32_t src_dtype;
+  int32_t dst_dtype;
+} KvbmTileShape;
+
+// Generic fused gather -> (layout transform, head reshard, fp8 quant/dequant)
+// -> scatter. The destination may be local HBM, mapped pinned host memory or
+// a peer GPU's memory mapped through CUDA IPC. One warp per tile.
+int kvbm_kv_tile_xfer(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape, int max_ctas,
+                      cudaStream_t stream);
+
+// Same contract, staged through shared memory: one elected thread issues 1-D
+// bulk async copies (TMA engine, local source only) of whole contiguous
+// (pair, layer, outer) chunks into a multi-stage ring; consumer warps convert
+// and store. Requires the source chunk [page, heads, head_dim] (or its HND
+// transpose) to be contiguous and 16-byte aligned; returns
+// cudaErrorInvalidValue otherwise so callers fall back to kvbm_kv_tile_xfer.
+int kvbm_kv_chunk_xfer_tma(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape, int max_ctas,
+                           cudaStream_t stream);
+
+// Split-by-bytes batched copy of num_pairs (src, dst) regions of equal size.
+// `align` is the alignment (16, 8, 4, 2 or 1) that every pointer and
+// `bytes_per_pair` is guaranteed to have.
+int kvbm_copy_pairs(const uint64_t* src_ptrs, const uint64_t* dst_ptrs, uint64_t num_pairs, uint64_t bytes_per_pair,
+                    int align, int max_ctas, cudaStream_t stream);
+
+// Reference-compatible permutes over pointer tables.
+int kvbm_universal_from_block(void* const* universal_ptrs, const void* const* block_ptrs, size_t num_blocks, size_t nh,
+                              size_t nl, size_t no, size_t nt, size_t hd, size_t nl_full, size_t nl_offset,
+                              int dtype, int layout, cudaStream_t stream);
+int kvbm_block_from_universal(const void* const* universal_ptrs, void* const* block_ptrs, size_t num_blocks,
+                              size_t nh, size_t nl, size_t no, size_t nt, size_t hd, size_t nl_full,
+                              size_t nl_offset, int dtype, int layout, cudaStream_t stream);
+int kvbm_nhd_hnd_transpose(const void* const* src_chunks, void* const* dst_chunks, size_t num_blocks, size_t nl,
+                           size_t no, size_t nt, size_t nh, size_t hd, int dtype, int src_layout,
+                           cudaStream_t stream);
+
+// Completion flags at system scope. signal: release-store `value` into
+// `flag` (which may live on a peer GPU). wait: spin (bounded by timeout_ns of
+// %globaltimer) until *flag >= expected; on timeout writes 1 to *status and
+// returns so the context stays usable.
+int kvbm_signal_flag(uint64_t* flag, uint64_t value, cudaStream_t stream);
+int kvbm_wait_flag(const uint64_t* flag, uint64_t expected, uint64_t timeout_ns, int* status, cudaStream_t stream);
+
+// Number of SMs of the current device (cached).
+int kvbm_sm_count(void);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,452 @@
+// Fused Llama-architecture ops for the prefill/decode driver harness
+// (sm_100a): RMSNorm with fused residual add, RoPE fused with the paged KV
+// cache write, SiLU-and-multiply, and split-KV paged decode attention with
+// grouped-query heads.
+//
+// The reference (crates/kvbm-kernels) ships no model kernels; vLLM computes
+// attention there. These exist so the block manager can be exercised end to
+// end on a PyTorch Llama model whose KV cache lives in the block manager's
+// paged layout, with GEMMs left to cuBLAS.
+#include "common.cuh"
+
+#include <algorithm>
+
+using namespace kvbm;
+
+namespace {
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float t = (lane < nw) ? red[lane] : 0.f;
+  t = warp_sum(t);
+  __syncthreads();
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm (+ residual). If `residual` is given: residual <- x + residual
+// (rounded to bf16, as the unfused model does) and out <- norm(residual) * w.
+// One CTA per row; each thread owns 8-element (16-byte) vectors.
+// ---------------------------------------------------------------------------
+constexpr int kNormMaxVec = 4;  // up to 4 x 8 = 32 elements per thread
+
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                      __nv_bfloat16* __restrict__ residual,
+                                                      const __nv_bfloat16* __restrict__ w,
+                                                      __nv_bfloat16* __restrict__ out, int D, float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int nvec = D / 8;
+  const int4* xr = reinterpret_cast<const int4*>(x + row * D);
+  int4* rr = residual ? reinterpret_cast<int4*>(residual + row * D) : nullptr;
+  float vals[kNormMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormMaxVec; ++k) {
+    const int v = threadIdx.x + k * blockDim.x;
+    if (v < nvec) {
+      int4 a = xr[v];
+      uint32_t wa[4] = {(uint32_t)a.x, (uint32_t)a.y, (uint32_t)a.z, (uint32_t)a.w};
+      if (rr) {
+        const int4 b = rr[v];
+        const uint32_t wb[4] = {(uint32_t)b.x, (uint32_t)b.y, (uint32_t)b.z, (uint32_t)b.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          wa[j] = pack_bf16(bf16_lo(wa[j]) + bf16_lo(wb[j]), bf16_hi(wa[j]) + bf16_hi(wb[j]));
+        rr[v] = make_int4(wa[0], wa[1], wa[2], wa[3]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        vals[k][2 * j] = bf16_lo(wa[j]);
+        vals[k][2 * j + 1] = bf16_hi(wa[j]);
+        ss += vals[k][2 * j] * vals[k][2 * j] + vals[k][2 * j + 1] * vals[k][2 * j + 1];
+      }
+    }
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / D + eps);
+  const int4* wr = reinterpret_cast<const int4*>(w);
+  int4* orow = reinterpret_cast<int4*>(out + row * D);
+#pragma unroll
+  for (int k = 0; k < kNormMaxVec; ++k) {
+    const int v = threadIdx.x + k * blockDim.x;
+    if (v < nvec) {
+      const int4 g = wr[v];
+      const uint32_t wg[4] = {(uint32_t)g.x, (uint32_t)g.y, (uint32_t)g.z, (uint32_t)g.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        // round the normalised value to bf16 before the weight multiply, as
+        // the reference model does
+        const float n0 = __bfloat162float(__float2bfloat16(vals[k][2 * j] * inv));
+        const float n1 = __bfloat162float(__float2bfloat16(vals[k][2 * j + 1] * inv));
+        o[j] = pack_bf16(n0 * bf16_lo(wg[j]), n1 * bf16_hi(wg[j]));
+      }
+      orow[v] = make_int4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// RoPE (rotate-half convention) applied in place to the q and k heads of a
+// packed qkv row [Hq + 2*Hkv, hd], fused with the write of k (rotated) and v
+// into the paged cache at slot_mapping[t] (slot = block * page + offset).
+// One warp per (token, head); cos/sin come from a [max_pos, hd] fp32 table
+// holding cos in [0, hd/2) and sin in [hd/2, hd).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rope_kv_write_kernel(
+    __nv_bfloat16* __restrict__ qkv, int T, int Hq, int Hkv, int hd, const int32_t* __restrict__ positions,
+    const float* __restrict__ cos_sin, uint8_t* k_base, uint8_t* v_base, int64_t block_stride, int64_t token_stride,
+    int64_t head_stride, int page, const int64_t* __restrict__ slots) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int H = Hq + 2 * Hkv;
+  if (w >= static_cast<int64_t>(T) * H) return;
+  const int64_t t = w / H;
+  const int h = static_cast<int>(w - t * H);
+  __nv_bfloat16* row = qkv + (t * H + h) * hd;
+  const int64_t slot = slots ? slots[t] : -1;
+  uint8_t* cache_row = nullptr;
+  if (h >= Hq && slot >= 0) {
+    const int64_t blk = slot / page, off = slot - blk * page;
+    const int kvh = (h < Hq + Hkv) ? (h - Hq) : (h - Hq - Hkv);
+    uint8_t* base = (h < Hq + Hkv) ? k_base : v_base;
+    cache_row = base + blk * block_stride + off * token_stride + kvh * head_stride;
+  }
+  if (h < Hq + Hkv) {
+    const int half = hd / 2;
+    const float* cs = cos_sin + static_cast<int64_t>(positions[t]) * hd;
+    for (int i = lane; i < half; i += 32) {
+      const float x1 = __bfloat162float(row[i]);
+      const float x2 = __bfloat162float(row[i + half]);
+      const float c = cs[i], s = cs[half + i];
+      const __nv_bfloat16 y1 = __float2bfloat16(x1 * c - x2 * s);
+      const __nv_bfloat16 y2 = __float2bfloat16(x2 * c + x1 * s);
+      row[i] = y1;
+      row[i + half] = y2;
+      if (cache_row) {
+        reinterpret_cast<__nv_bfloat16*>(cache_row)[i] = y1;
+        reinterpret_cast<__nv_bfloat16*>(cache_row)[i + half] = y2;
+      }
+    }
+  } else if (cache_row) {
+    const int nv = hd / 8;
+    for (int i = lane; i < nv; i += 32)
+      reinterpret_cast<int4*>(cache_row)[i] = reinterpret_cast<const int4*>(row)[i];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// out[t, i] = silu(gate_up[t, i]) * gate_up[t, I + i]
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu,
+                                                       __nv_bfloat16* __restrict__ out, int64_t T, int I) {
+  const int nv = I / 8;
+  const int64_t total = T * nv;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = v / nv;
+    const int c = static_cast<int>(v - t * nv);
+    const int4 g = reinterpret_cast<const int4*>(gu + t * 2 * I)[c];
+    const int4 u = reinterpret_cast<const int4*>(gu + t * 2 * I + I)[c];
+    const uint32_t wg[4] = {(uint32_t)g.x, (uint32_t)g.y, (uint32_t)g.z, (uint32_t)g.w};
+    const uint32_t wu[4] = {(uint32_t)u.x, (uint32_t)u.y, (uint32_t)u.z, (uint32_t)u.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = bf16_lo(wg[j]), b = bf16_hi(wg[j]);
+      const float sa = __bfloat162float(__float2bfloat16(a / (1.f + __expf(-a))));
+      const float sb = __bfloat162float(__float2bfloat16(b / (1.f + __expf(-b))));
+      o[j] = pack_bf16(sa * bf16_lo(wu[j]), sb * bf16_hi(wu[j]));
+    }
+    reinterpret_cast<int4*>(out + t * I)[c] = make_int4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Paged decode attention, split over the KV sequence (flash-decoding).
+//
+// grid = (splits, Hkv, B), 4 warps per CTA. A CTA owns the GROUP query heads
+// that share one KV head, so each K/V row is loaded once for GROUP heads.
+// Within a 16-token sub-block, lane (t = lane % 16, half = lane / 16) loads
+// half of token t's key (64 dims, 8 x 16 B) for the score, and for P.V lane
+// (c = lane % 16, parity = lane / 16) loads dims [8c, 8c+8) of the value rows
+// of its token parity. Online softmax in base 2 (q pre-scaled by
+// softmax_scale * log2 e). Each split writes unnormalised partials
+// (acc[hd], m, l) into the caller's scratch; attn_combine merges them.
+// ---------------------------------------------------------------------------
+constexpr int kHD = 128;
+constexpr int kAttnWarps = 4;
+
+template <int GROUP>
+__global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
+    const __nv_bfloat16* __restrict__ q, const uint8_t* __restrict__ k_base, const uint8_t* __restrict__ v_base,
+    int64_t block_stride, int64_t token_stride, int64_t head_stride, int page, const int32_t* __restrict__ block_table,
+    int max_blocks, const int32_t* __restrict__ seq_lens, float qscale, int splits, float* __restrict__ part_acc,
+    float* __restrict__ part_ml) {
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int Hkv = gridDim.y;
+  const int Hq = Hkv * GROUP;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float q_s[GROUP][kHD + 4];
+  __shared__ float red_m[kAttnWarps][GROUP];
+  __shared__ float red_l[kAttnWarps][GROUP];
+  __shared__ float red_acc[kAttnWarps][GROUP][kHD];
+
+  for (int i = threadIdx.x; i < GROUP * kHD; i += blockDim.x) {
+    const int g = i / kHD, d = i - g * kHD;
+    q_s[g][d] = __bfloat162float(q[(static_cast<int64_t>(b) * Hq + kvh * GROUP + g) * kHD + d]) * qscale;
+  }
+  __syncthreads();
+
+  const int seq = seq_lens[b];
+  const int nblk = (seq + page - 1) / page;
+  const int per = (nblk + splits - 1) / splits;
+  const int b0 = split * per;
+  const int b1 = min(nblk, b0 + per);
+
+  float m[GROUP], l[GROUP], acc[GROUP][8];
+#pragma unroll
+  for (int g = 0; g < GROUP; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
+  }
+  const int tl = lane & 15, half = lane >> 4;
+  for (int blk = b0 + warp; blk < b1; blk += kAttnWarps) {
+    const int64_t phys = block_table[static_cast<int64_t>(b) * max_blocks + blk];
+    const uint8_t* kb = k_base + phys * block_stride + static_cast<int64_t>(kvh) * head_stride;
+    const uint8_t* vb = v_base + phys * block_stride + static_cast<int64_t>(kvh) * head_stride;
+    for (int sub = 0; sub < page; sub += 16) {
+      const int tok = blk * page + sub + tl;
+      const bool valid = tok < seq;
+      float s[GROUP];
+#pragma unroll
+      for (int g = 0; g < GROUP; ++g) s[g] = 0.f;
+      if (valid) {
+        const int4* kr = reinterpret_cast<const int4*>(kb + static_cast<int64_t>(sub + tl) * token_stride + half * 128);
+        int4 kv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) kv[j] = kr[j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t w4[4] = {(uint32_t)kv[j].x, (uint32_t)kv[j].y, (uint32_t)kv[j].z, (uint32_t)kv[j].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float k0 = bf16_lo(w4[e]), k1 = bf16_hi(w4[e]);
+            const int d = half * 64 + j * 8 + e * 2;
+#pragma unroll
+            for (int g = 0; g < GROUP; ++g) s[g] += q_s[g][d] * k0 + q_s[g][d + 1] * k1;
+          }
+        }
+      }
+      float p[GROUP];
+#pragma unroll
+      for (int g = 0; g < GROUP; ++g) {
+        s[g] += __shfl_xor_sync(0xffffffffu, s[g], 16);
+        if (!valid) s[g] = -INFINITY;
+        float mx = s[g];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float m_new = fmaxf(m[g], mx);
+        if (m_new == -INFINITY) {
+          p[g] = 0.f;
+          continue;
+        }
+        const float alpha = exp2f(m[g] - m_new);
+        p[g] = valid ? exp2f(s[g] - m_new) : 0.f;
+        float ps = p[g];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        l[g] = l[g] * alpha + ps;
+        m[g] = m_new;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
+      }
+      // P.V: lane (c = tl, parity = half) takes tokens 2j + parity.
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int tt = 2 * j + half;
+        float pt[GROUP];
+#pragma unroll
+        for (int g = 0; g < GROUP; ++g) pt[g] = __shfl_sync(0xffffffffu, p[g], tt);
+        if (blk * page + sub + tt < seq) {
+          const int4 vv = *reinterpret_cast<const int4*>(vb + static_cast<int64_t>(sub + tt) * token_stride + tl * 16);
+          const uint32_t w4[4] = {(uint32_t)vv.x, (uint32_t)vv.y, (uint32_t)vv.z, (uint32_t)vv.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float v0 = bf16_lo(w4[e]), v1 = bf16_hi(w4[e]);
+#pragma unroll
+            for (int g = 0; g < GROUP; ++g) {
+              acc[g][2 * e] += pt[g] * v0;
+              acc[g][2 * e + 1] += pt[g] * v1;
+            }
+          }
+        }
+      }
+    }
+  }
+  // Merge the two token parities, then the warps.
+#pragma unroll
+  for (int g = 0; g < GROUP; ++g)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[g][e] += __shfl_xor_sync(0xffffffffu, acc[g][e], 16);
+  if (half == 0) {
+#pragma unroll
+    for (int g = 0; g < GROUP; ++g)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) red_acc[warp][g][tl * 8 + e] = acc[g][e];
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < GROUP; ++g) {
+      red_m[warp][g] = m[g];
+      red_l[warp][g] = l[g];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < GROUP * kHD; i += blockDim.x) {
+    const int g = i / kHD, d = i - g * kHD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, red_m[w][g]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float f = exp2f(red_m[w][g] - M);
+        L += red_l[w][g] * f;
+        A += red_acc[w][g][d] * f;
+      }
+    }
+    const int64_t row = (static_cast<int64_t>(b) * Hq + kvh * GROUP + g) * splits + split;
+    part_acc[row * kHD + d] = A;
+    if (d == 0) {
+      part_ml[row * 2] = M;
+      part_ml[row * 2 + 1] = L;
+    }
+  }
+}
+
+// out[b, h, :] = sum_s acc_s * 2^(m_s - M) / sum_s l_s * 2^(m_s - M)
+__global__ void __launch_bounds__(kHD) attn_combine_kernel(const float* __restrict__ part_acc,
+                                                           const float* __restrict__ part_ml, int splits,
+                                                           __nv_bfloat16* __restrict__ out) {
+  const int64_t bh = blockIdx.x;
+  const int d = threadIdx.x;
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, part_ml[(bh * splits + s) * 2]);
+  float L = 0.f, A = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < splits; ++s) {
+      const float f = exp2f(part_ml[(bh * splits + s) * 2] - M);
+      L += part_ml[(bh * splits + s) * 2 + 1] * f;
+      A += part_acc[(bh * splits + s) * kHD + d] * f;
+    }
+  }
+  out[bh * kHD + d] = __float2bfloat16(L > 0.f ? A / L : 0.f);
+}
+
+}  // namespace
+
+extern "C" int kvbm_rmsnorm(const void* x, void* residual, const void* weight, void* out, int64_t rows, int dim,
+                            float eps, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  if (!x || !weight || !out || dim % 8 != 0 || dim / 8 > 256 * kNormMaxVec) return cudaErrorInvalidValue;
+  const int threads = std::min(256, std::max(32, (dim / 8 + 31) / 32 * 32));
+  rmsnorm_kernel<<<static_cast<unsigned>(rows), threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(residual),
+      static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out), dim, eps);
+  return cudaGetLastError();
+}
+
+extern "C" int kvbm_rope_kv_write(void* qkv, int64_t tokens, int hq, int hkv, int hd, const int32_t* positions,
+                                  const float* cos_sin, void* k_base, void* v_base, int64_t block_stride,
+                                  int64_t token_stride, int64_t head_stride, int page, const int64_t* slots,
+                                  cudaStream_t stream) {
+  if (tokens == 0) return cudaSuccess;
+  if (!qkv || !positions || !cos_sin || hd % 8 != 0) return cudaErrorInvalidValue;
+  if (slots && (!k_base || !v_base || page <= 0)) return cudaErrorInvalidValue;
+  const int64_t warps = tokens * (hq + 2 * hkv);
+  const unsigned grid = static_cast<unsigned>((warps + 7) / 8);
+  rope_kv_write_kernel<<<grid, 256, 0, stream>>>(static_cast<__nv_bfloat16*>(qkv), static_cast<int>(tokens), hq, hkv,
+                                                 hd, positions, cos_sin, static_cast<uint8_t*>(k_base),
+                                                 static_cast<uint8_t*>(v_base), block_stride, token_stride,
+                                                 head_stride, page, slots);
+  return cudaGetLastError();
+}
+
+extern "C" int kvbm_silu_mul(const void* gate_up, void* out, int64_t tokens, int inter, cudaStream_t stream) {
+  if (tokens == 0) return cudaSuccess;
+  if (!gate_up || !out || inter % 8 != 0) return cudaErrorInvalidValue;
+  int sms = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t work = tokens * (inter / 8);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(sms) * 16));
+  silu_mul_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(gate_up),
+                                            static_cast<__nv_bfloat16*>(out), tokens, inter);
+  return cudaGetLastError();
+}
+
+// Scratch: part_acc holds batch*hq*splits*128 floats, part_ml batch*hq*splits*2.
+extern "C" int kvbm_paged_decode_attn(const void* q, const void* k_base, const void* v_base, int64_t block_stride,
+                                      int64_t token_stride, int64_t head_stride, int page, const int32_t* block_table,
+                                      int max_blocks, const int32_t* seq_lens, int batch, int hq, int hkv, int hd,
+                                      float softmax_scale, int splits, float* part_acc, float* part_ml, void* out,
+                                      cudaStream_t stream) {
+  if (batch == 0) return cudaSuccess;
+  if (!q || !k_base || !v_base || !block_table || !seq_lens || !part_acc || !part_ml || !out)
+    return cudaErrorInvalidValue;
+  if (hd != kHD || hkv <= 0 || hq % hkv != 0 || page % 16 != 0 || splits <= 0 || splits > 65535)
+    return cudaErrorInvalidValue;
+  if (token_stride % 16 != 0 || head_stride % 16 != 0 || block_stride % 16 != 0) return cudaErrorInvalidValue;
+  const float qscale = softmax_scale * 1.4426950408889634f;  // log2(e)
+  dim3 grid(splits, hkv, batch);
+  const int group = hq / hkv;
+  const auto* qq = static_cast<const __nv_bfloat16*>(q);
+  const auto* kb = static_cast<const uint8_t*>(k_base);
+  const auto* vb = static_cast<const uint8_t*>(v_base);
+  switch (group) {
+    case 1:
+      paged_decode_kernel<1><<<grid, kAttnWarps * 32, 0, stream>>>(qq, kb, vb, block_stride, token_stride, head_stride,
+                                                                   page, block_table, max_blocks, seq_lens, qscale,
+                                                                   splits, part_acc, part_ml);
+      break;
+    case 2:
+      paged_decode_kernel<2><<<grid, kAttnWarps * 32, 0, stream>>>(qq, kb, vb, block_stride, token_stride, head_stride,
+                                                                   page, block_table, max_blocks, seq_lens, qscale,
+                                                                   splits, part_acc, part_ml);
+      break;
+    case 4:
+      paged_decode_kernel<4><<<grid, kAttnWarps * 32, 0, stream>>>(qq, kb, vb, block_stride, token_stride, head_stride,
+                                                                   page, block_table, max_blocks, seq_lens, qscale,
+                                                                   splits, part_acc, part_ml);
+      break;
+    case 8:
+      paged_decode_kernel<8><<<grid, kAttnWarps * 32, 0, stream>>>(qq, kb, vb, block_stride, token_stride, head_stride,
+                                                                   page, block_table, max_blocks, seq_lens, qscale,
+                                                                   splits, part_acc, part_ml);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  attn_combine_kernel<<<static_cast<unsigned>(batch) * hq, kHD, 0, stream>>>(part_acc, part_ml, splits,
+                                                                            static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
+}

@@ -1,0 +1,169 @@
+"""Python entry points of the KV transfer kernels (sm_100a, libkvbm_cuda.so).
+
+All functions are asynchronous on the given (or current) CUDA stream and take
+torch tensors / :class:`~kvbm_b200.physical.layout.KvLayout` pools. Block-id
+tensors must be int32 and device-accessible.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def _ids(ids, device) -> torch.Tensor:
+    if isinstance(ids, torch.Tensor) and ids.dtype == torch.int32 and (ids.is_cuda or ids.is_pinned()):
+        return ids
+    t = torch.as_tensor(ids, dtype=torch.int32)
+    return t.to(device, non_blocking=True) if device is not None else t
+
+
+def kv_transfer(src, src_ids, dst, dst_ids, *, layer_begin: int = 0, num_layers: int | None = None,
+                dst_layer_begin: int | None = None, src_head_offset: int = 0, dst_head_offset: int = 0,
+                num_heads: int | None = None, engine: str = "tile", max_ctas: int = 0, stream=None) -> None:
+    """Copy blocks ``src_ids`` of ``src`` into blocks ``dst_ids`` of ``dst``.
+
+    Fuses, in one launch: the layout transform between the two pools (FC/LW,
+    NHD/HND/universal), a KV-head slice (``num_heads`` heads starting at
+    ``src_head_offset`` land at ``dst_head_offset``: heterogeneous-TP
+    resharding), and fp8 e4m3 block-scaled quantisation or dequantisation when
+    the pool dtypes differ. ``dst`` may be a peer GPU's pool mapped over
+    NVLink (``KvLayout.from_descriptor``) or a pinned host pool (G2).
+
+    ``engine``: ``"tile"`` (warp per head tile, direct 16-byte loads) or
+    ``"tma"`` (bulk async copies staged through shared memory; falls back to
+    ``"tile"`` when the source chunk is not contiguous).
+    """
+    n_pairs = len(src_ids)
+    if n_pairs != len(dst_ids):
+        raise ValueError("src_ids and dst_ids differ in length")
+    if n_pairs == 0:
+        return
+    sc, dc = src.config, dst.config
+    nl = sc.num_layers - layer_begin if num_layers is None else num_layers
+    dlb = layer_begin if dst_layer_begin is None else dst_layer_begin
+    nh = num_heads if num_heads is not None else min(sc.num_heads - src_head_offset, dc.num_heads - dst_head_offset)
+    if src_head_offset + nh > sc.num_heads or dst_head_offset + nh > dc.num_heads:
+        raise ValueError("head slice out of range")
+    if sc.head_dim != dc.head_dim or sc.page_size != dc.page_size or sc.outer_dim != dc.outer_dim:
+        raise ValueError("pools differ in head_dim, page_size or outer_dim")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    sid = _ids(src_ids, dev)
+    did = _ids(dst_ids, dev)
+    s = src.side(sid, layer_begin, nl, src_head_offset)
+    d = dst.side(did, dlb, nl, dst_head_offset)
+    shape = _lib.KvbmTileShape(n_pairs, nl, sc.outer_dim, nh, sc.page_size, sc.head_dim, src.dtype_code,
+                               dst.dtype_code)
+    lib = _lib.load()
+    st = _stream(stream)
+    if stream is not None and isinstance(stream, torch.cuda.Stream):
+        # temporaries uploaded here are read by the kernel on `stream`
+        for t in (sid, did):
+            if t.is_cuda:
+                t.record_stream(stream)
+    if engine == "tma":
+        # falls through to the tile engine when the source chunks are not
+        # contiguous / aligned (the TMA entry point rejects before launching)
+        if lib.kvbm_kv_chunk_xfer_tma(C.byref(s), C.byref(d), C.byref(shape), max_ctas, st) == 0:
+            return
+    _lib.check(lib.kvbm_kv_tile_xfer(C.byref(s), C.byref(d), C.byref(shape), max_ctas, st), "kvbm_kv_tile_xfer")
+
+
+def kv_transfer_sides(src_side, dst_side, shape, *, engine: str = "tile", max_ctas: int = 0, stream=None) -> None:
+    """Low-level launch with prebuilt ``KvbmSide`` / ``KvbmTileShape`` structs."""
+    lib = _lib.load()
+    st = _stream(stream)
+    if engine == "tma":
+        if lib.kvbm_kv_chunk_xfer_tma(C.byref(src_side), C.byref(dst_side), C.byref(shape), max_ctas, st) == 0:
+            return
+    _lib.check(lib.kvbm_kv_tile_xfer(C.byref(src_side), C.byref(dst_side), C.byref(shape), max_ctas, st),
+               "kvbm_kv_tile_xfer")
+
+
+def _ptr_align(ptrs: list[int], nbytes: int) -> int:
+    a = 16
+    for p in [*ptrs, nbytes]:
+        while a > 1 and p % a:
+            a >>= 1
+    return a
+
+
+def copy_pairs(src_ptrs, dst_ptrs, nbytes: int, *, align: int | None = None, max_ctas: int = 0,
+               stream=None) -> None:
+    """Batched copy of equal-size regions split by bytes across all SMs.
+
+    ``src_ptrs``/``dst_ptrs`` are int64 device tensors (or lists, uploaded
+    here). Regions may be device, mapped pinned host or peer memory.
+    """
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if not isinstance(src_ptrs, torch.Tensor):
+        if align is None:
+            align = _ptr_align(list(src_ptrs) + list(dst_ptrs), nbytes)
+        src_ptrs = torch.tensor(list(src_ptrs), dtype=torch.int64).to(dev, non_blocking=True)
+        dst_ptrs = torch.tensor(list(dst_ptrs), dtype=torch.int64).to(dev, non_blocking=True)
+    if align is None:
+        align = 16 if nbytes % 16 == 0 else 1
+    _lib.call("kvbm_copy_pairs", src_ptrs.data_ptr(), dst_ptrs.data_ptr(), src_ptrs.numel(), nbytes, align,
+              max_ctas, _stream(stream))
+
+
+def memcpy_pairs_ce(src_ptrs: list[int], dst_ptrs: list[int], nbytes: int, stream=None) -> None:
+    """Copy-engine baseline: one cudaMemcpyAsync per region."""
+    n = len(src_ptrs)
+    s = (C.c_uint64 * n)(*src_ptrs)
+    d = (C.c_uint64 * n)(*dst_ptrs)
+    _lib.call("kvbm_memcpy_pairs_ce", C.cast(s, C.c_void_p), C.cast(d, C.c_void_p), n, nbytes, _stream(stream))
+
+
+def _dt(t: torch.dtype) -> int:
+    from ..physical.layout import DTYPE_CODE
+
+    return DTYPE_CODE[t]
+
+
+def universal_from_block(universal_ptrs: torch.Tensor, block_ptrs: torch.Tensor, nh: int, nl: int, no: int, nt: int,
+                         hd: int, dtype: torch.dtype, layout: int, nl_full: int | None = None, nl_offset: int = 0,
+                         stream=None) -> None:
+    """Block stack (nl*no chunk pointers per block) -> universal [nh, nl_full, no, nt, hd]."""
+    nb = universal_ptrs.numel()
+    _lib.call("kvbm_universal_from_block", universal_ptrs.data_ptr(), block_ptrs.data_ptr(), nb, nh, nl, no, nt, hd,
+              nl if nl_full is None else nl_full, nl_offset, _dt(dtype), layout, _stream(stream))
+
+
+def block_from_universal(universal_ptrs: torch.Tensor, block_ptrs: torch.Tensor, nh: int, nl: int, no: int, nt: int,
+                         hd: int, dtype: torch.dtype, layout: int, nl_full: int | None = None, nl_offset: int = 0,
+                         stream=None) -> None:
+    """Universal [nh, nl_full, no, nt, hd] -> block stack."""
+    nb = universal_ptrs.numel()
+    _lib.call("kvbm_block_from_universal", universal_ptrs.data_ptr(), block_ptrs.data_ptr(), nb, nh, nl, no, nt, hd,
+              nl if nl_full is None else nl_full, nl_offset, _dt(dtype), layout, _stream(stream))
+
+
+def nhd_hnd_transpose(src_chunks: torch.Tensor, dst_chunks: torch.Tensor, nb: int, nl: int, no: int, nt: int,
+                      nh: int, hd: int, dtype: torch.dtype, src_layout: int, stream=None) -> None:
+    """Per chunk, swap [nt, nh, hd] <-> [nh, nt, hd]."""
+    _lib.call("kvbm_nhd_hnd_transpose", src_chunks.data_ptr(), dst_chunks.data_ptr(), nb, nl, no, nt, nh, hd,
+              _dt(dtype), src_layout, _stream(stream))
+
+
+def signal_flag(flag_ptr: int, value: int, stream=None) -> None:
+    _lib.call("kvbm_signal_flag", flag_ptr, value, _stream(stream))
+
+
+def wait_flag(flag_ptr: int, expected: int, timeout_ns: int, status_ptr: int, stream=None) -> None:
+    _lib.call("kvbm_wait_flag", flag_ptr, expected, timeout_ns, status_ptr, _stream(stream))
+
+
+def sm_count() -> int:
+    return _lib.load().kvbm_sm_count()

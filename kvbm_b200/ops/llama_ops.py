@@ -1,0 +1,68 @@
+"""Python entry points of the fused Llama ops (sm_100a, libkvbm_cuda.so)."""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .kv_ops import _stream
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
+            out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """out = rmsnorm(x [+ residual]) * weight; updates ``residual`` in place when given."""
+    assert x.dtype == torch.bfloat16 and x.is_contiguous()
+    D = x.shape[-1]
+    rows = x.numel() // D
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.call("kvbm_rmsnorm", x.data_ptr(), residual.data_ptr() if residual is not None else None,
+              weight.data_ptr(), out.data_ptr(), rows, D, float(eps), _stream(stream))
+    return out
+
+
+def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, hq: int, hkv: int, hd: int,
+                  k_base: int = 0, v_base: int = 0, block_stride: int = 0, token_stride: int = 0,
+                  head_stride: int = 0, page: int = 16, slots: torch.Tensor | None = None, stream=None) -> None:
+    """In-place RoPE on the q/k heads of ``qkv`` [T, hq+2*hkv, hd]; writes k/v into the paged cache."""
+    T = qkv.shape[0]
+    _lib.call("kvbm_rope_kv_write", qkv.data_ptr(), T, hq, hkv, hd, positions.data_ptr(), cos_sin.data_ptr(),
+              k_base or None, v_base or None, block_stride, token_stride, head_stride, page,
+              slots.data_ptr() if slots is not None else None, _stream(stream))
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    T = gate_up.numel() // gate_up.shape[-1]
+    inter = gate_up.shape[-1] // 2
+    if out is None:
+        out = torch.empty(*gate_up.shape[:-1], inter, dtype=gate_up.dtype, device=gate_up.device)
+    _lib.call("kvbm_silu_mul", gate_up.data_ptr(), out.data_ptr(), T, inter, _stream(stream))
+    return out
+
+
+def decode_splits(batch: int, hkv: int, max_seq: int, page: int, sm_count: int = 148) -> int:
+    """Number of KV splits so that batch*hkv*splits fills the SMs a few times."""
+    blocks = max(1, (max_seq + page - 1) // page)
+    target = 4 * sm_count
+    splits = max(1, min(blocks, (target + batch * hkv - 1) // (batch * hkv)))
+    return int(splits)
+
+
+def paged_decode_attn(q: torch.Tensor, k_base: int, v_base: int, block_stride: int, token_stride: int,
+                      head_stride: int, page: int, block_table: torch.Tensor, seq_lens: torch.Tensor, hkv: int,
+                      softmax_scale: float, splits: int, scratch: torch.Tensor | None = None,
+                      out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Split-KV paged decode attention. q: [B, Hq, 128] bf16; returns [B, Hq, 128]."""
+    B, Hq, hd = q.shape
+    if out is None:
+        out = torch.empty_like(q)
+    rows = B * Hq * splits
+    need = rows * (hd + 2)
+    if scratch is None or scratch.numel() < need:
+        scratch = torch.empty(need, dtype=torch.float32, device=q.device)
+    part_acc = scratch.data_ptr()
+    part_ml = scratch.data_ptr() + rows * hd * 4
+    _lib.call("kvbm_paged_decode_attn", q.data_ptr(), k_base, v_base, block_stride, token_stride, head_stride, page,
+              block_table.data_ptr(), block_table.shape[1], seq_lens.data_ptr(), B, Hq, hkv, hd,
+              float(softmax_scale), splits, part_acc, part_ml, out.data_ptr(), _stream(stream))
+    return out

@@ -1,0 +1,148 @@
+"""Storage for the KV tiers: G1 device pools, G2 mapped pinned host pools,
+CUDA IPC export/import of pools between the processes of one node.
+
+Pools are allocated directly with the CUDA runtime (through
+``libkvbm_cuda.so``) rather than through the PyTorch caching allocator so that
+
+* an IPC handle maps exactly one pool (no allocator segment offsets), and
+* G2 host memory is mapped into the device address space, letting SM kernels
+  gather/scatter it directly.
+
+The buffers expose ``__cuda_array_interface__`` (device) or the buffer
+protocol (host) so they can be viewed as torch tensors without copies.
+
+Parity: crates/kvbm-physical/src/layout/builder.rs (allocate_device /
+allocate_pinned / external regions) and the NIXL registration step, which
+on one node reduces to CUDA IPC here.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from ..ops import _lib
+
+
+class StorageKind:
+    DEVICE = "device"      # G1
+    PINNED = "pinned"      # G2
+    DISK = "disk"          # G3
+    OBJECT = "object"      # G4
+    SYSTEM = "system"      # unpinned host
+
+
+class DeviceBuffer:
+    """A cudaMalloc'd region owned by this object (freed on close/GC)."""
+
+    def __init__(self, nbytes: int, device: int | None = None, zero: bool = False):
+        if device is not None:
+            torch.cuda.set_device(device)
+        self.device = torch.cuda.current_device()
+        self.nbytes = int(nbytes)
+        p = C.c_void_p()
+        _lib.check(_lib.load().kvbm_device_alloc(self.nbytes, C.byref(p)), "cudaMalloc")
+        self.ptr = int(p.value or 0)
+        self._owned = True
+        if zero:
+            _lib.check(_lib.load().kvbm_memset_async(self.ptr, 0, self.nbytes, None), "memset")
+            torch.cuda.synchronize()
+
+    @property
+    def __cuda_array_interface__(self):
+        return {"shape": (self.nbytes,), "typestr": "|u1", "data": (self.ptr, False), "version": 3,
+                "strides": None, "stream": None}
+
+    def tensor(self, dtype: torch.dtype = torch.uint8, shape: tuple | None = None) -> torch.Tensor:
+        t = torch.as_tensor(self, device=f"cuda:{self.device}")
+        if dtype != torch.uint8:
+            t = t.view(dtype)
+        if shape is not None:
+            t = t.view(shape)
+        return t
+
+    def ipc_handle(self) -> bytes:
+        buf = C.create_string_buffer(64)
+        _lib.check(_lib.load().kvbm_ipc_get_handle(self.ptr, buf), "cudaIpcGetMemHandle")
+        return bytes(buf.raw[:64])
+
+    def close(self) -> None:
+        if self._owned and self.ptr:
+            _lib.load().kvbm_device_free(self.ptr)
+        self.ptr = 0
+        self._owned = False
+
+    def __del__(self):  # pragma: no cover - GC timing
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class PeerBuffer:
+    """A peer process's DeviceBuffer mapped into this process through CUDA IPC."""
+
+    def __init__(self, handle: bytes, nbytes: int, device: int | None = None):
+        if device is not None:
+            torch.cuda.set_device(device)
+        self.device = torch.cuda.current_device()
+        p = C.c_void_p()
+        _lib.check(_lib.load().kvbm_ipc_open_handle(bytes(handle), C.byref(p)), "cudaIpcOpenMemHandle")
+        self.ptr = int(p.value or 0)
+        self.nbytes = int(nbytes)
+
+    def close(self) -> None:
+        if self.ptr:
+            _lib.load().kvbm_ipc_close(self.ptr)
+        self.ptr = 0
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class PinnedBuffer:
+    """Pinned host memory mapped into the device address space (G2)."""
+
+    def __init__(self, nbytes: int):
+        self.nbytes = int(nbytes)
+        p = C.c_void_p()
+        _lib.check(_lib.load().kvbm_host_alloc_mapped(self.nbytes, C.byref(p)), "cudaHostAlloc")
+        self.ptr = int(p.value or 0)
+        d = C.c_void_p()
+        _lib.check(_lib.load().kvbm_host_device_pointer(self.ptr, C.byref(d)), "cudaHostGetDevicePointer")
+        self.device_ptr = int(d.value or 0)
+
+    def tensor(self, dtype: torch.dtype = torch.uint8, shape: tuple | None = None) -> torch.Tensor:
+        arr = (C.c_uint8 * self.nbytes).from_address(self.ptr)
+        t = torch.frombuffer(arr, dtype=torch.uint8)
+        if dtype != torch.uint8:
+            t = t.view(dtype)
+        if shape is not None:
+            t = t.view(shape)
+        return t
+
+    def close(self) -> None:
+        if self.ptr:
+            _lib.load().kvbm_host_free(self.ptr)
+        self.ptr = 0
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+@dataclass
+class ExportedPool:
+    """Everything a peer needs to map a pool: IPC handle, size, owner device."""
+
+    handle: bytes
+    nbytes: int
+    device: int
+    rank: int = 0

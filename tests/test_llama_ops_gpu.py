@@ -1,0 +1,114 @@
+"""GPU numerics of the fused Llama ops against plain PyTorch fp32 references."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from kvbm_b200.ops import llama_ops
+from kvbm_b200.physical.layout import KvBlockLayout, KvLayout, LayoutConfig
+
+
+def test_rmsnorm_with_residual():
+    torch.manual_seed(0)
+    x = torch.randn(37, 4096, device="cuda", dtype=torch.bfloat16)
+    r = torch.randn(37, 4096, device="cuda", dtype=torch.bfloat16)
+    w = torch.rand(4096, device="cuda", dtype=torch.bfloat16) + 0.5
+    r_ref = (x.float() + r.float()).to(torch.bfloat16)
+    var = r_ref.float().pow(2).mean(-1, keepdim=True)
+    ref = (r_ref.float() * torch.rsqrt(var + 1e-5)).to(torch.bfloat16).float() * w.float()
+    r2 = r.clone()
+    out = llama_ops.rmsnorm(x, w, 1e-5, residual=r2)
+    torch.cuda.synchronize()
+    assert torch.equal(r2, r_ref)
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
+    out2 = llama_ops.rmsnorm(x, w, 1e-5)
+    var = x.float().pow(2).mean(-1, keepdim=True)
+    ref2 = (x.float() * torch.rsqrt(var + 1e-5)).to(torch.bfloat16).float() * w.float()
+    torch.testing.assert_close(out2.float(), ref2, rtol=1e-2, atol=1e-2)
+
+
+def _cos_sin(max_pos, hd, theta=500000.0):
+    inv = 1.0 / (theta ** (torch.arange(0, hd, 2, dtype=torch.float64) / hd))
+    f = torch.outer(torch.arange(max_pos, dtype=torch.float64), inv)
+    return torch.cat([f.cos(), f.sin()], dim=-1).float().cuda()
+
+
+def _rope_ref(x, pos, cs):
+    hd = x.shape[-1]
+    c = cs[pos][:, None, : hd // 2]
+    s = cs[pos][:, None, hd // 2:]
+    x1, x2 = x[..., : hd // 2].float(), x[..., hd // 2:].float()
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+def test_rope_kv_write_paged():
+    torch.manual_seed(1)
+    T, hq, hkv, hd, page = 50, 32, 8, 128, 16
+    cfg = LayoutConfig.for_model(16, 2, hkv, hd, page)
+    pool = KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.OPERATIONAL_NHD, zero=True)
+    qkv = torch.randn(T, hq + 2 * hkv, hd, device="cuda", dtype=torch.bfloat16)
+    orig = qkv.clone()
+    pos = torch.arange(100, 100 + T, device="cuda", dtype=torch.int32)
+    cs = _cos_sin(4096, hd)
+    blocks = torch.tensor([5, 2, 9, 11], device="cuda")
+    slots = (blocks[torch.arange(T, device="cuda") // page] * page + torch.arange(T, device="cuda") % page).long()
+    layer = 1
+    kb = pool.layer_base(layer)
+    vb = kb + pool.outer_stride
+    llama_ops.rope_kv_write(qkv, pos, cs, hq, hkv, hd, kb, vb, pool.block_stride, pool.token_stride,
+                            pool.head_stride, page, slots)
+    torch.cuda.synchronize()
+    q_ref = _rope_ref(orig[:, :hq], pos.long(), cs)
+    k_ref = _rope_ref(orig[:, hq:hq + hkv], pos.long(), cs)
+    torch.testing.assert_close(qkv[:, :hq].float(), q_ref, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(qkv[:, hq:hq + hkv].float(), k_ref, rtol=1e-2, atol=1e-2)
+    assert torch.equal(qkv[:, hq + hkv:], orig[:, hq + hkv:])
+    view = pool.layer_view(layer)  # [blocks, outer, page, heads, hd]
+    for t in range(T):
+        b, o = int(blocks[t // page]), t % page
+        assert torch.equal(view[b, 0, o], qkv[t, hq:hq + hkv])
+        assert torch.equal(view[b, 1, o], orig[t, hq + hkv:])
+
+
+def test_silu_mul():
+    torch.manual_seed(2)
+    gu = torch.randn(33, 2 * 1024, device="cuda", dtype=torch.bfloat16)
+    out = llama_ops.silu_mul(gu)
+    g, u = gu[:, :1024].float(), gu[:, 1024:].float()
+    ref = torch.nn.functional.silu(g).to(torch.bfloat16).float() * u
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("group", [1, 4, 8])
+@pytest.mark.parametrize("splits", [1, 3, 8])
+def test_paged_decode_attention(group, splits):
+    torch.manual_seed(3)
+    B, hkv, hd, page = 5, 2, 128, 16
+    hq = hkv * group
+    seq = torch.tensor([1, 17, 64, 100, 333], dtype=torch.int32, device="cuda")
+    max_blocks = int((seq.max() + page - 1) // page)
+    nb = B * max_blocks + 3
+    cfg = LayoutConfig.for_model(nb, 1, hkv, hd, page)
+    pool = KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.OPERATIONAL_NHD)
+    pool.layer_view(0).copy_(torch.randn(pool.layer_view(0).shape, device="cuda").to(torch.bfloat16))
+    perm = torch.randperm(nb, device="cuda")[: B * max_blocks].view(B, max_blocks).to(torch.int32)
+    q = torch.randn(B, hq, hd, device="cuda", dtype=torch.bfloat16)
+    scale = 1.0 / math.sqrt(hd)
+    kb = pool.layer_base(0)
+    out = llama_ops.paged_decode_attn(q, kb, kb + pool.outer_stride, pool.block_stride, pool.token_stride,
+                                      pool.head_stride, page, perm, seq, hkv, scale, splits)
+    torch.cuda.synchronize()
+    view = pool.layer_view(0)
+    for b in range(B):
+        n = int(seq[b])
+        blks = perm[b, : (n + page - 1) // page].long()
+        k = view[blks, 0].reshape(-1, hkv, hd)[:n].float()  # [n, hkv, hd]
+        v = view[blks, 1].reshape(-1, hkv, hd)[:n].float()
+        qq = q[b].float().view(hkv, group, hd)
+        s = torch.einsum("hgd,nhd->hgn", qq, k) * scale
+        p = torch.softmax(s, dim=-1)
+        ref = torch.einsum("hgn,nhd->hgd", p, v).reshape(hq, hd)
+        torch.testing.assert_close(out[b].float(), ref, rtol=2e-2, atol=2e-2)
