@@ -1,0 +1,165 @@
+"""Isolated prefill -> decode KV transfer over NVLink (2 ranks, one box).
+
+Rank 0 (prefill) maps rank 1's (decode) paged G1 pool through CUDA IPC and
+moves whole requests' KV (all layers, non-contiguous block ids on both
+sides) with the fused transfer kernel, nothing else running. Baselines on
+the same bytes:
+
+* ``nccl_contig``: one NCCL send/recv of a contiguous buffer (the bus
+  ceiling NCCL reaches, without any paging);
+* ``nccl_paged``: what a NCCL-based P->D path has to do with paged KV -
+  gather the blocks into a staging buffer, send/recv, scatter on the decode
+  side (gather/scatter done with the same SM kernel).
+
+Device time with CUDA events (max over the two ranks), L2 flushed before
+every timed iteration. Roofline: the measured peer copy bandwidth of this
+pool (770 GB/s per direction).
+
+    torchrun --nproc-per-node 2 -m kvbm_b200.bench.p2p_bench
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+from ..ops import kv_ops
+from ..physical.layout import KvBlockLayout, KvLayout, LayoutConfig, LayoutDescriptor
+
+PEER_COPY_GBPS = 770.0
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--blocks", type=int, default=512, help="blocks per request (512 = 8192 tokens)")
+    p.add_argument("--requests", default="1,4")
+    p.add_argument("--layers", type=int, default=32)
+    p.add_argument("--heads", type=int, default=8)
+    p.add_argument("--engines", default="tile,tma")
+    p.add_argument("--ctas", default="0,32,64")
+    p.add_argument("--iters", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--dst-layout", default="nhd", choices=["nhd", "hnd"])
+    p.add_argument("--out", default=None)
+    args = p.parse_args(argv)
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    assert world == 2
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", rank))
+    gloo = dist.new_group(backend="gloo")
+    reqs = [int(x) for x in args.requests.split(",")]
+    nmax = max(reqs) * args.blocks
+    pool_blocks = 2 * nmax + 8
+    cfg = LayoutConfig.for_model(pool_blocks, args.layers, args.heads, 128, 16)
+    nhd = KvBlockLayout.OPERATIONAL_NHD
+    dst_bl = nhd if args.dst_layout == "nhd" else KvBlockLayout.OPERATIONAL_HND
+    local = KvLayout.allocate(cfg, "fully_contiguous", nhd if rank == 0 else dst_bl)
+    local._flat().random_(0, 256)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    # exchange pools
+    descs = [None, None]
+    dist.all_gather_object(descs, local.descriptor().to_dict(), group=gloo)
+    remote = KvLayout.from_descriptor(LayoutDescriptor.from_dict(descs[1])) if rank == 0 else None
+    rng = random.Random(7)
+    results = []
+
+    def timed(fn) -> float:
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier(group=gloo)
+        ts = []
+        for _ in range(args.iters):
+            flush.fill_(1)
+            dist.barrier(group=gloo)
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            ts.append(s.elapsed_time(e))
+        ts.sort()
+        mine = ts[len(ts) // 2]
+        both = [None, None]
+        dist.all_gather_object(both, mine, group=gloo)
+        return max(both)
+
+    for nreq in reqs:
+        n = nreq * args.blocks
+        s_ids = torch.tensor(rng.sample(range(pool_blocks), n), dtype=torch.int32, device="cuda")
+        d_ids = torch.tensor(rng.sample(range(pool_blocks), n), dtype=torch.int32, device="cuda")
+        nbytes = n * cfg.bytes_per_block
+        for engine in args.engines.split(","):
+            for ctas in [int(c) for c in args.ctas.split(",")]:
+                def fn(engine=engine, ctas=ctas):
+                    if rank == 0:
+                        kv_ops.kv_transfer(local, s_ids, remote, d_ids, engine=engine, max_ctas=ctas)
+                ms = timed(fn)
+                r = {"path": f"fused_{engine}", "max_ctas": ctas, "requests": nreq, "bytes": nbytes,
+                     "ms": round(ms, 4), "gbps": round(nbytes / ms / 1e6, 1),
+                     "frac_of_peer_copy": round(nbytes / ms / 1e6 / PEER_COPY_GBPS, 3)}
+                results.append(r)
+                if rank == 0:
+                    print(json.dumps(r), flush=True)
+        # correctness of the last fused transfer: compare a sample of blocks
+        torch.cuda.synchronize()
+        dist.barrier(group=gloo)
+        sample = list(range(0, n, max(1, n // 16)))
+        if rank == 0:
+            data = local.gather_blocks(s_ids[sample].tolist()).cpu()
+            dist.send(data.view(torch.uint8).reshape(-1), dst=1, group=gloo)
+        else:
+            got = local.gather_blocks(d_ids[sample].tolist()).cpu()
+            ref = torch.empty_like(got.view(torch.uint8).reshape(-1))
+            dist.recv(ref, src=0, group=gloo)
+            ok = torch.equal(got.view(torch.uint8).reshape(-1), ref)
+            print(json.dumps({"check": "fused_transfer_exact", "requests": nreq, "ok": bool(ok)}), flush=True)
+        # NCCL baselines
+        contig = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+
+        def nccl_contig():
+            if rank == 0:
+                dist.send(contig, dst=1)
+            else:
+                dist.recv(contig, src=0)
+        ms = timed(nccl_contig)
+        r = {"path": "nccl_contig", "requests": nreq, "bytes": nbytes, "ms": round(ms, 4),
+             "gbps": round(nbytes / ms / 1e6, 1), "frac_of_peer_copy": round(nbytes / ms / 1e6 / PEER_COPY_GBPS, 3)}
+        results.append(r)
+        if rank == 0:
+            print(json.dumps(r), flush=True)
+        staging = KvLayout.over_tensor(LayoutConfig.for_model(n, args.layers, args.heads, 128, 16), contig)
+        seq_ids = torch.arange(n, dtype=torch.int32, device="cuda")
+
+        def nccl_paged():
+            if rank == 0:
+                kv_ops.kv_transfer(local, s_ids, staging, seq_ids)
+                dist.send(contig, dst=1)
+            else:
+                dist.recv(contig, src=0)
+                kv_ops.kv_transfer(staging, seq_ids, local, d_ids)
+        ms = timed(nccl_paged)
+        r = {"path": "nccl_paged", "requests": nreq, "bytes": nbytes, "ms": round(ms, 4),
+             "gbps": round(nbytes / ms / 1e6, 1), "frac_of_peer_copy": round(nbytes / ms / 1e6 / PEER_COPY_GBPS, 3)}
+        results.append(r)
+        if rank == 0:
+            print(json.dumps(r), flush=True)
+        del contig, staging
+    if rank == 0 and args.out:
+        with open(args.out, "w") as f:
+            for r in results:
+                f.write(json.dumps(r) + "\n")
+    dist.barrier(group=gloo)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

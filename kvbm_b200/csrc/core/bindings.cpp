@@ -8,6 +8,7 @@
 #include <pybind11/stl.h>
 
 #include "block_pool.hpp"
+#include "disk_pool.hpp"
 #include "hash.hpp"
 #include "registry.hpp"
 #include "tinylfu.hpp"
@@ -324,4 +325,18 @@ PYBIND11_MODULE(_kvbm_core, m) {
       .def("num_positions", &PositionalIndex::num_positions)
       .def("dropped_out_of_range", &PositionalIndex::dropped)
       .def("num_entries", &PositionalIndex::num_entries);
+
+  py::class_<DiskPool, std::shared_ptr<DiskPool>>(m, "DiskPool")
+      .def(py::init<const std::string&, uint64_t, uint64_t, bool, bool, int>(), py::arg("path"),
+           py::arg("num_blocks"), py::arg("block_bytes"), py::arg("direct") = false, py::arg("persistent") = false,
+           py::arg("threads") = 4)
+      .def("write", &DiskPool::write, py::call_guard<py::gil_scoped_release>())
+      .def("read", &DiskPool::read, py::call_guard<py::gil_scoped_release>())
+      .def_property_readonly("num_blocks", &DiskPool::num_blocks)
+      .def_property_readonly("block_bytes", &DiskPool::block_bytes)
+      .def_property_readonly("direct", &DiskPool::direct)
+      .def_property_readonly("persistent", &DiskPool::persistent)
+      .def_property_readonly("path", &DiskPool::path)
+      .def("bytes_written", &DiskPool::bytes_written)
+      .def("bytes_read", &DiskPool::bytes_read);
 }

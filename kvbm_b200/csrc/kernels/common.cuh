@@ -1,8 +1,8 @@
 // Shared device helpers for the kvbm_b200 sm_100a kernel library.
 //
 // Everything here is written for Blackwell (sm_100a): 16-byte vector global
-// accesses, 1-D bulk async copies (cp.async.bulk, local source only, never
-// with .multicast::cluster) tracked by shared-memory mbarriers, and
+// accesses, 1-D bulk async copies (cp.async.bulk into this CTA's own shared
+// memory from this GPU's own memory) tracked by shared-memory mbarriers, and
 // %globaltimer-bounded spin waits that give up with an error status instead
 // of hanging the GPU.
 #pragma once

@@ -843,6 +843,28 @@ __global__ void signal_kernel(uint64_t* flag, uint64_t value) {
   st_release_sys_u64(flag, value);
 }
 
+// Copy `n` 64-bit payload words (e.g. the first generated token) to the
+// peer, then publish the flag with release semantics at system scope.
+__global__ void signal_payload_kernel(uint64_t* flag, uint64_t value, uint64_t* dst, const uint64_t* src, int n) {
+  for (int i = 0; i < n; ++i) dst[i] = src[i];
+  fence_acq_rel_sys();
+  st_release_sys_u64(flag, value);
+}
+
+// Wait until every flags[i] >= expected (one thread, bounded by timeout_ns).
+__global__ void wait_all_kernel(const uint64_t* flags, int n, uint64_t expected, uint64_t timeout_ns, int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int i = 0; i < n; ++i) {
+    while (ld_acquire_sys_u64(flags + i) < expected) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        if (status) atomicExch(status, kStatusWaitTimeout);
+        return;
+      }
+      __nanosleep(256);
+    }
+  }
+}
+
 __global__ void wait_kernel(const uint64_t* flag, uint64_t expected, uint64_t timeout_ns, int* status) {
   const uint64_t t0 = globaltimer_ns();
   while (ld_acquire_sys_u64(flag) < expected) {
@@ -859,6 +881,21 @@ __global__ void wait_kernel(const uint64_t* flag, uint64_t expected, uint64_t ti
 extern "C" int kvbm_signal_flag(uint64_t* flag, uint64_t value, cudaStream_t stream) {
   if (!flag) return cudaErrorInvalidValue;
   signal_kernel<<<1, 1, 0, stream>>>(flag, value);
+  return cudaGetLastError();
+}
+
+extern "C" int kvbm_signal_flag_payload(uint64_t* flag, uint64_t value, uint64_t* payload_dst,
+                                        const uint64_t* payload_src, int n_words, cudaStream_t stream) {
+  if (!flag || n_words < 0 || (n_words > 0 && (!payload_dst || !payload_src))) return cudaErrorInvalidValue;
+  signal_payload_kernel<<<1, 1, 0, stream>>>(flag, value, payload_dst, payload_src, n_words);
+  return cudaGetLastError();
+}
+
+extern "C" int kvbm_wait_flags_all(const uint64_t* flags, int n, uint64_t expected, uint64_t timeout_ns, int* status,
+                                   cudaStream_t stream) {
+  if (!flags || n < 0) return cudaErrorInvalidValue;
+  if (n == 0) return cudaSuccess;
+  wait_all_kernel<<<1, 1, 0, stream>>>(flags, n, expected, timeout_ns, status);
   return cudaGetLastError();
 }
 

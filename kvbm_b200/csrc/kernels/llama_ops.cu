@@ -225,31 +225,36 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
     for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
   }
   const int tl = lane & 15, half = lane >> 4;
+  // All K and V loads of a 16-token sub-block are issued before any use, so
+  // each warp keeps 8 KiB in flight per sub-block (one memory round trip).
+  // Rows past seq_len are still inside the allocated block: they are loaded
+  // and then masked (score -inf, value zeroed).
   for (int blk = b0 + warp; blk < b1; blk += kAttnWarps) {
     const int64_t phys = block_table[static_cast<int64_t>(b) * max_blocks + blk];
     const uint8_t* kb = k_base + phys * block_stride + static_cast<int64_t>(kvh) * head_stride;
     const uint8_t* vb = v_base + phys * block_stride + static_cast<int64_t>(kvh) * head_stride;
     for (int sub = 0; sub < page; sub += 16) {
-      const int tok = blk * page + sub + tl;
-      const bool valid = tok < seq;
+      const int tok0 = blk * page + sub;
+      int4 kv[8], vv[8];
+      const uint8_t* kr = kb + static_cast<int64_t>(sub + tl) * token_stride + half * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) kv[j] = ld_v4_stream(kr + j * 16);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        vv[j] = ld_v4_stream(vb + static_cast<int64_t>(sub + 2 * j + half) * token_stride + tl * 16);
+      const bool valid = tok0 + tl < seq;
       float s[GROUP];
 #pragma unroll
       for (int g = 0; g < GROUP; ++g) s[g] = 0.f;
-      if (valid) {
-        const int4* kr = reinterpret_cast<const int4*>(kb + static_cast<int64_t>(sub + tl) * token_stride + half * 128);
-        int4 kv[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) kv[j] = kr[j];
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t w4[4] = {(uint32_t)kv[j].x, (uint32_t)kv[j].y, (uint32_t)kv[j].z, (uint32_t)kv[j].w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t w4[4] = {(uint32_t)kv[j].x, (uint32_t)kv[j].y, (uint32_t)kv[j].z, (uint32_t)kv[j].w};
+        for (int e = 0; e < 4; ++e) {
+          const float k0 = bf16_lo(w4[e]), k1 = bf16_hi(w4[e]);
+          const int d = half * 64 + j * 8 + e * 2;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float k0 = bf16_lo(w4[e]), k1 = bf16_hi(w4[e]);
-            const int d = half * 64 + j * 8 + e * 2;
-#pragma unroll
-            for (int g = 0; g < GROUP; ++g) s[g] += q_s[g][d] * k0 + q_s[g][d + 1] * k1;
-          }
+          for (int g = 0; g < GROUP; ++g) s[g] += q_s[g][d] * k0 + q_s[g][d + 1] * k1;
         }
       }
       float p[GROUP];
@@ -275,24 +280,23 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_kernel(
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
       }
-      // P.V: lane (c = tl, parity = half) takes tokens 2j + parity.
+      // P.V: lane (c = tl, parity = half) holds value rows 2j + parity.
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int tt = 2 * j + half;
         float pt[GROUP];
 #pragma unroll
         for (int g = 0; g < GROUP; ++g) pt[g] = __shfl_sync(0xffffffffu, p[g], tt);
-        if (blk * page + sub + tt < seq) {
-          const int4 vv = *reinterpret_cast<const int4*>(vb + static_cast<int64_t>(sub + tt) * token_stride + tl * 16);
-          const uint32_t w4[4] = {(uint32_t)vv.x, (uint32_t)vv.y, (uint32_t)vv.z, (uint32_t)vv.w};
+        const bool vvalid = tok0 + tt < seq;
+        const uint32_t w4[4] = {vvalid ? (uint32_t)vv[j].x : 0u, vvalid ? (uint32_t)vv[j].y : 0u,
+                                vvalid ? (uint32_t)vv[j].z : 0u, vvalid ? (uint32_t)vv[j].w : 0u};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float v0 = bf16_lo(w4[e]), v1 = bf16_hi(w4[e]);
+        for (int e = 0; e < 4; ++e) {
+          const float v0 = bf16_lo(w4[e]), v1 = bf16_hi(w4[e]);
 #pragma unroll
-            for (int g = 0; g < GROUP; ++g) {
-              acc[g][2 * e] += pt[g] * v0;
-              acc[g][2 * e + 1] += pt[g] * v1;
-            }
+          for (int g = 0; g < GROUP; ++g) {
+            acc[g][2 * e] += pt[g] * v0;
+            acc[g][2 * e + 1] += pt[g] * v1;
           }
         }
       }

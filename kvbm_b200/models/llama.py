@@ -1,0 +1,247 @@
+"""Llama-architecture driver harness (random-init weights) whose KV cache
+lives in a block manager pool.
+
+The model exists to exercise the block manager the way a serving engine
+does: prefill writes K/V into paged blocks layer by layer (and lets a
+callback start the transfer of each finished layer), decode attends over
+paged blocks through a block table. GEMMs go to cuBLAS (``F.linear``),
+prefill attention to PyTorch SDPA (flash / cuDNN backends only), and the
+fused ops (RMSNorm+residual, RoPE+paged KV write, SiLU-mul, paged decode
+attention) to the sm_100a kernels in ``libkvbm_cuda.so``.
+
+The reference ships no model (vLLM provides it there); this harness plays
+vLLM's role for the benchmarks, calling the same connector hooks.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch.nn.attention import SDPBackend, sdpa_kernel
+
+from ..ops import llama_ops
+from ..physical.layout import KvBlockLayout, KvLayout, LayoutConfig
+
+
+@dataclass(frozen=True)
+class LlamaConfig:
+    hidden: int = 4096
+    layers: int = 32
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    intermediate: int = 14336
+    vocab: int = 128256
+    rope_theta: float = 500000.0
+    eps: float = 1e-5
+    max_position: int = 16384
+
+    @classmethod
+    def llama3_8b(cls) -> "LlamaConfig":
+        return cls()
+
+    @classmethod
+    def tiny(cls, layers: int = 2) -> "LlamaConfig":
+        return cls(hidden=512, layers=layers, heads=8, kv_heads=2, head_dim=128, intermediate=1024, vocab=1024,
+                   max_position=4096)
+
+    @property
+    def q_size(self) -> int:
+        return self.heads * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return self.kv_heads * self.head_dim
+
+    def kv_layout_config(self, num_blocks: int, page_size: int = 16,
+                         dtype: torch.dtype = torch.bfloat16) -> LayoutConfig:
+        return LayoutConfig.for_model(num_blocks, self.layers, self.kv_heads, self.head_dim, page_size, dtype)
+
+    def num_params(self) -> int:
+        per_layer = (self.hidden * (self.q_size + 2 * self.kv_size) + self.q_size * self.hidden
+                     + 3 * self.hidden * self.intermediate + 2 * self.hidden)
+        return self.layers * per_layer + 2 * self.vocab * self.hidden + self.hidden
+
+
+class LlamaModel:
+    """Weights + forward passes. Not an nn.Module: no autograd, inference only."""
+
+    def __init__(self, cfg: LlamaConfig, device: torch.device | str = "cuda", seed: int = 0,
+                 dtype: torch.dtype = torch.bfloat16):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        std = 0.02
+
+        def w(*shape, scale=std):
+            t = torch.empty(shape, device=self.device, dtype=dtype)
+            t.normal_(0.0, scale, generator=g)
+            return t
+
+        c = cfg
+        self.embed = w(c.vocab, c.hidden)
+        self.layers = []
+        for _ in range(c.layers):
+            self.layers.append({
+                "wqkv": w(c.q_size + 2 * c.kv_size, c.hidden),
+                "wo": w(c.hidden, c.q_size, scale=std / math.sqrt(2 * c.layers)),
+                "wgu": w(2 * c.intermediate, c.hidden),
+                "wd": w(c.hidden, c.intermediate, scale=std / math.sqrt(2 * c.layers)),
+                "n1": torch.ones(c.hidden, device=self.device, dtype=dtype),
+                "n2": torch.ones(c.hidden, device=self.device, dtype=dtype),
+            })
+        self.norm = torch.ones(c.hidden, device=self.device, dtype=dtype)
+        self.lm_head = w(c.vocab, c.hidden)
+        inv = 1.0 / (c.rope_theta ** (torch.arange(0, c.head_dim, 2, dtype=torch.float64) / c.head_dim))
+        f = torch.outer(torch.arange(c.max_position, dtype=torch.float64), inv)
+        self.cos_sin = torch.cat([f.cos(), f.sin()], dim=-1).float().to(self.device)
+        self.scale = 1.0 / math.sqrt(c.head_dim)
+        self._decode_scratch: torch.Tensor | None = None
+
+    # ------------------------------------------------------------ helpers
+    @staticmethod
+    def kv_bases(pool: KvLayout, layer: int) -> tuple[int, int]:
+        k = pool.layer_base(layer)
+        return k, k + pool.outer_stride
+
+    def allocate_pool(self, num_blocks: int, page_size: int = 16, kind: str = "fully_contiguous",
+                      block_layout: KvBlockLayout = KvBlockLayout.OPERATIONAL_NHD) -> KvLayout:
+        return KvLayout.allocate(self.cfg.kv_layout_config(num_blocks, page_size), kind, block_layout,
+                                 device=self.device.index)
+
+    # ------------------------------------------------------------ prefill
+    @torch.inference_mode()
+    def prefill(self, tokens: torch.Tensor, pool: KvLayout, block_ids: torch.Tensor, start_pos: int = 0,
+                on_layer_done=None) -> torch.Tensor:
+        """Prefill ``tokens`` [T] at positions [start_pos, start_pos+T).
+
+        K/V land in ``pool`` blocks ``block_ids`` (int32, device; block j holds
+        positions [16j, 16j+16) of the sequence). ``on_layer_done(layer)`` is
+        called on the host right after layer ``layer``'s K/V writes are enqueued
+        on the current stream. Returns the greedy next token (int64 [1]).
+        """
+        c = self.cfg
+        T = tokens.numel()
+        page = pool.config.page_size
+        pos = torch.arange(start_pos, start_pos + T, device=self.device, dtype=torch.int32)
+        slots = (block_ids.long()[pos.long() // page] * page + pos.long() % page)
+        x = F.embedding(tokens.long(), self.embed)
+        residual = x
+        h = torch.empty_like(x)
+        first = True
+        for li, L in enumerate(self.layers):
+            if first:
+                llama_ops.rmsnorm(x, L["n1"], c.eps, out=h)
+                first = False
+            else:
+                llama_ops.rmsnorm(x, L["n1"], c.eps, residual=residual, out=h)
+            qkv = F.linear(h, L["wqkv"]).view(T, c.heads + 2 * c.kv_heads, c.head_dim)
+            kb, vb = self.kv_bases(pool, li)
+            llama_ops.rope_kv_write(qkv, pos, self.cos_sin, c.heads, c.kv_heads, c.head_dim, kb, vb,
+                                    pool.block_stride, pool.token_stride, pool.head_stride, page, slots)
+            if on_layer_done is not None:
+                on_layer_done(li)
+            q = qkv[:, : c.heads].transpose(0, 1).unsqueeze(0)
+            k = qkv[:, c.heads: c.heads + c.kv_heads].transpose(0, 1)
+            v = qkv[:, c.heads + c.kv_heads:].transpose(0, 1)
+            rep = c.heads // c.kv_heads
+            k = k.repeat_interleave(rep, dim=0).unsqueeze(0)
+            v = v.repeat_interleave(rep, dim=0).unsqueeze(0)
+            with sdpa_kernel([SDPBackend.FLASH_ATTENTION, SDPBackend.CUDNN_ATTENTION,
+                              SDPBackend.EFFICIENT_ATTENTION]):
+                a = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=self.scale)
+            a = a.squeeze(0).transpose(0, 1).reshape(T, c.q_size)
+            x = F.linear(a, L["wo"])
+            llama_ops.rmsnorm(x, L["n2"], c.eps, residual=residual, out=h)
+            gu = F.linear(h, L["wgu"])
+            x = F.linear(llama_ops.silu_mul(gu), L["wd"])
+        last = torch.empty(1, c.hidden, device=self.device, dtype=self.dtype)
+        res_last = residual[-1:].contiguous()
+        llama_ops.rmsnorm(x[-1:].contiguous(), self.norm, c.eps, residual=res_last, out=last)
+        logits = F.linear(last, self.lm_head)
+        return logits.argmax(dim=-1)
+
+    # ------------------------------------------------------------- decode
+    def decode_scratch(self, batch: int, splits: int) -> torch.Tensor:
+        need = batch * self.cfg.heads * splits * (self.cfg.head_dim + 2)
+        if self._decode_scratch is None or self._decode_scratch.numel() < need:
+            self._decode_scratch = torch.empty(need, dtype=torch.float32, device=self.device)
+        return self._decode_scratch
+
+    @torch.inference_mode()
+    def decode_step(self, tokens: torch.Tensor, positions: torch.Tensor, pool: KvLayout, block_table: torch.Tensor,
+                    seq_lens: torch.Tensor, splits: int) -> torch.Tensor:
+        """One decode step for a batch: tokens [B] int64, positions [B] int32
+        (position of each input token), block_table [B, max_blocks] int32,
+        seq_lens [B] int32 (= positions + 1). Returns next tokens [B] int64.
+        All shapes static, so the step can be captured in a CUDA graph."""
+        c = self.cfg
+        B = tokens.numel()
+        page = pool.config.page_size
+        pl = positions.long()
+        slots = block_table.gather(1, (pl // page).unsqueeze(1)).squeeze(1).long() * page + pl % page
+        x = F.embedding(tokens, self.embed)
+        residual = x
+        h = torch.empty_like(x)
+        scratch = self.decode_scratch(B, splits)
+        attn = torch.empty(B, c.heads, c.head_dim, device=self.device, dtype=self.dtype)
+        for li, L in enumerate(self.layers):
+            if li == 0:
+                llama_ops.rmsnorm(x, L["n1"], c.eps, out=h)
+            else:
+                llama_ops.rmsnorm(x, L["n1"], c.eps, residual=residual, out=h)
+            qkv = F.linear(h, L["wqkv"]).view(B, c.heads + 2 * c.kv_heads, c.head_dim)
+            kb, vb = self.kv_bases(pool, li)
+            llama_ops.rope_kv_write(qkv, positions, self.cos_sin, c.heads, c.kv_heads, c.head_dim, kb, vb,
+                                    pool.block_stride, pool.token_stride, pool.head_stride, page, slots)
+            q = qkv[:, : c.heads].contiguous()
+            llama_ops.paged_decode_attn(q, kb, vb, pool.block_stride, pool.token_stride, pool.head_stride, page,
+                                        block_table, seq_lens, c.kv_heads, self.scale, splits, scratch=scratch,
+                                        out=attn)
+            x = F.linear(attn.view(B, c.q_size), L["wo"])
+            llama_ops.rmsnorm(x, L["n2"], c.eps, residual=residual, out=h)
+            x = F.linear(llama_ops.silu_mul(F.linear(h, L["wgu"])), L["wd"])
+        out = torch.empty_like(h)
+        llama_ops.rmsnorm(x, self.norm, c.eps, residual=residual, out=out)
+        return F.linear(out, self.lm_head).argmax(dim=-1)
+
+    # ---------------------------------------------------- torch reference
+    @torch.inference_mode()
+    def reference_forward(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Plain PyTorch (fp32 accumulate) causal forward; logits of every position."""
+        c = self.cfg
+        T = tokens.numel()
+        x = F.embedding(tokens.long(), self.embed).float()
+        pos = torch.arange(T, device=self.device)
+        cs = self.cos_sin[pos]
+        cos, sin = cs[:, None, : c.head_dim // 2], cs[:, None, c.head_dim // 2:]
+
+        def rope(t):
+            t1, t2 = t[..., : c.head_dim // 2], t[..., c.head_dim // 2:]
+            return torch.cat([t1 * cos - t2 * sin, t2 * cos + t1 * sin], dim=-1)
+
+        def norm(t, wgt):
+            return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + c.eps) * wgt.float()
+
+        for L in self.layers:
+            hN = norm(x, L["n1"])
+            qkv = (hN @ L["wqkv"].float().t()).view(T, -1, c.head_dim)
+            q = rope(qkv[:, : c.heads])
+            k = rope(qkv[:, c.heads: c.heads + c.kv_heads])
+            v = qkv[:, c.heads + c.kv_heads:]
+            rep = c.heads // c.kv_heads
+            k = k.repeat_interleave(rep, dim=1)
+            v = v.repeat_interleave(rep, dim=1)
+            s = torch.einsum("thd,shd->hts", q, k) * self.scale
+            mask = torch.triu(torch.ones(T, T, device=self.device, dtype=torch.bool), 1)
+            s = s.masked_fill(mask, float("-inf"))
+            a = torch.einsum("hts,shd->thd", s.softmax(-1), v).reshape(T, c.q_size)
+            x = x + a @ L["wo"].float().t()
+            hN = norm(x, L["n2"])
+            gu = hN @ L["wgu"].float().t()
+            x = x + (F.silu(gu[:, : c.intermediate]) * gu[:, c.intermediate:]) @ L["wd"].float().t()
+        return norm(x, self.norm) @ self.lm_head.float().t()

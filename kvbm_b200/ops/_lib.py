@@ -76,6 +76,8 @@ _SIGS = {
     "kvbm_nhd_hnd_transpose": (_INT, [_VP, _VP, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _INT, _INT, _VP]),
     "kvbm_signal_flag": (_INT, [_VP, _U64, _VP]),
     "kvbm_wait_flag": (_INT, [_VP, _U64, _U64, _VP, _VP]),
+    "kvbm_signal_flag_payload": (_INT, [_VP, _U64, _VP, _VP, _INT, _VP]),
+    "kvbm_wait_flags_all": (_INT, [_VP, _INT, _U64, _U64, _VP, _VP]),
     "kvbm_sm_count": (_INT, []),
     "kvbm_rmsnorm": (_INT, [_VP, _VP, _VP, _VP, _I64, _INT, _F32, _VP]),
     "kvbm_rope_kv_write": (
@@ -113,6 +115,26 @@ class KvbmCudaError(RuntimeError):
     pass
 
 
+# Kernels launched per successful call of each entry point. The benchmark
+# reports how many of this library's kernels ran inside its timed region.
+_KERNELS_PER_CALL = {
+    "kvbm_kv_tile_xfer": 1, "kvbm_kv_chunk_xfer_tma": 1, "kvbm_copy_pairs": 1, "kvbm_universal_from_block": 1,
+    "kvbm_block_from_universal": 1, "kvbm_nhd_hnd_transpose": 1, "kvbm_signal_flag": 1, "kvbm_wait_flag": 1,
+    "kvbm_signal_flag_payload": 1, "kvbm_wait_flags_all": 1, "kvbm_rmsnorm": 1, "kvbm_rope_kv_write": 1,
+    "kvbm_silu_mul": 1, "kvbm_paged_decode_attn": 2,
+}
+_launches = 0
+
+
+def count_launches(n: int) -> None:
+    global _launches
+    _launches += n
+
+
+def launch_count() -> int:
+    return _launches
+
+
 def lib_path() -> Path:
     return _build.CUDA_LIB
 
@@ -147,3 +169,4 @@ def check(code: int, what: str = "") -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args), name)
+    count_launches(_KERNELS_PER_CALL.get(name, 0))

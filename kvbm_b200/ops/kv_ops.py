@@ -76,8 +76,10 @@ def kv_transfer(src, src_ids, dst, dst_ids, *, layer_begin: int = 0, num_layers:
         # falls through to the tile engine when the source chunks are not
         # contiguous / aligned (the TMA entry point rejects before launching)
         if lib.kvbm_kv_chunk_xfer_tma(C.byref(s), C.byref(d), C.byref(shape), max_ctas, st) == 0:
+            _lib.count_launches(1)
             return
     _lib.check(lib.kvbm_kv_tile_xfer(C.byref(s), C.byref(d), C.byref(shape), max_ctas, st), "kvbm_kv_tile_xfer")
+    _lib.count_launches(1)
 
 
 def kv_transfer_sides(src_side, dst_side, shape, *, engine: str = "tile", max_ctas: int = 0, stream=None) -> None:
@@ -163,6 +165,17 @@ def signal_flag(flag_ptr: int, value: int, stream=None) -> None:
 
 def wait_flag(flag_ptr: int, expected: int, timeout_ns: int, status_ptr: int, stream=None) -> None:
     _lib.call("kvbm_wait_flag", flag_ptr, expected, timeout_ns, status_ptr, _stream(stream))
+
+
+def signal_flag_payload(flag_ptr: int, value: int, payload_dst: int, payload_src: int, n_words: int,
+                        stream=None) -> None:
+    """Copy ``n_words`` u64 words to ``payload_dst`` (peer memory), then release-store the flag."""
+    _lib.call("kvbm_signal_flag_payload", flag_ptr, value, payload_dst, payload_src, n_words, _stream(stream))
+
+
+def wait_flags_all(flags_ptr: int, n: int, expected: int, timeout_ns: int, status_ptr: int, stream=None) -> None:
+    """Block ``stream`` until all ``n`` u64 flags reach ``expected`` (bounded; status=1 on timeout)."""
+    _lib.call("kvbm_wait_flags_all", flags_ptr, n, expected, timeout_ns, status_ptr, _stream(stream))
 
 
 def sm_count() -> int:

@@ -43,7 +43,7 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None, stream=None
 def decode_splits(batch: int, hkv: int, max_seq: int, page: int, sm_count: int = 148) -> int:
     """Number of KV splits so that batch*hkv*splits fills the SMs a few times."""
     blocks = max(1, (max_seq + page - 1) // page)
-    target = 4 * sm_count
+    target = 8 * sm_count
     splits = max(1, min(blocks, (target + batch * hkv - 1) // (batch * hkv)))
     return int(splits)
 
