@@ -96,7 +96,8 @@ def main(argv=None) -> int:
         role, peer = "prefill", rank + half
     else:
         role, peer = "decode", rank - half
-    server = DisaggServer(cfg, role, local, peer_rank=peer, group=gloo)
+    store = dist.distributed_c10d._get_default_store() if world > 1 else None
+    server = DisaggServer(cfg, role, local, peer_rank=peer, group=gloo, store=store, pair_id=rank % max(1, half))
     server.connect()
     server.warmup_graphs()
 
@@ -114,15 +115,17 @@ def main(argv=None) -> int:
             dist.barrier(group=gloo)
         torch.cuda.synchronize()
 
+    # decode ranks dispatch wave k+1 before decoding wave k (prefill/decode
+    # pipelining across the pair); the last timed wave dispatches nothing
     for _ in range(args.warmup):
-        server.serve_wave(prompts())
+        server.serve_wave(prompts(), more=True)
     inputs = [prompts() for _ in range(args.steps)]
     barrier()
     sampler = ClockSampler(gpus=None).start() if local == 0 else None
     launches0 = _lib.launch_count()
     results = []
     for k in range(args.steps):
-        results.append(server.serve_wave(inputs[k]))
+        results.append(server.serve_wave(inputs[k], more=k < args.steps - 1))
     barrier()
     launches = _lib.launch_count() - launches0
     clocks = sampler.stop() if sampler else None

@@ -31,7 +31,8 @@ import torch.distributed as dist
 from .. import _core_native as core
 from ..models.llama import LlamaConfig, LlamaModel
 from ..ops import llama_ops
-from ..parallel.pd import Mailbox, MailboxDescriptor, PdSender
+from ..ops import kv_ops
+from ..parallel.pd import WAIT_TIMEOUT_NS, Mailbox, MailboxDescriptor, PdSender
 from ..physical.layout import KvLayout, LayoutDescriptor
 
 
@@ -63,17 +64,24 @@ class DisaggConfig:
 
 
 class DecodeInstance:
-    """Decode side: G1 pool + block pool, mailbox, graph-captured decode step."""
+    """Decode side: G1 pool + block pool, mailbox, graph-captured decode step.
 
-    def __init__(self, model: LlamaModel, cfg: DisaggConfig):
+    With ``buffers=2`` two waves can be in flight: wave k+1's destination
+    blocks are allocated and dispatched to prefill before wave k is decoded,
+    so prefill of k+1 overlaps decode of k on the other GPU.
+    """
+
+    def __init__(self, model: LlamaModel, cfg: DisaggConfig, buffers: int = 1):
         self.model, self.cfg = model, cfg
         C, bpr = cfg.concurrency, cfg.request_blocks
-        self.num_blocks = C * bpr + 1
+        self.buffers = buffers
+        self.num_blocks = buffers * C * bpr + 1
         self.pool = model.allocate_pool(self.num_blocks, cfg.page_size)
         self.blocks = core.BlockPool(self.num_blocks, cfg.page_size, "lru", 0)
-        self.mailbox = Mailbox(C, device=model.device.index)
+        self.mailbox = Mailbox(buffers * C, device=model.device.index)
         dev = model.device
         self.block_table = torch.zeros(C, bpr, dtype=torch.int32, device=dev)
+        self.tables = [torch.zeros(C, bpr, dtype=torch.int32, device=dev) for _ in range(buffers)]
         self.tok = torch.zeros(C, dtype=torch.int64, device=dev)
         self.pos = torch.zeros(C, dtype=torch.int32, device=dev)
         self.seq_lens = torch.zeros(C, dtype=torch.int32, device=dev)
@@ -81,25 +89,25 @@ class DecodeInstance:
         self.tokens_out = torch.zeros(C, cfg.gen_len, dtype=torch.int64, device=dev)
         self.splits = cfg.decode_splits or llama_ops.decode_splits(C, model.cfg.kv_heads,
                                                                     cfg.prompt_len + cfg.gen_len, cfg.page_size)
-        self.stream = torch.cuda.Stream(device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
-        self._ids: list[int] = []
+        self._ids: list[list[int]] = [[] for _ in range(buffers)]
         self.graph_launches = 0
 
-    def begin_wave(self) -> torch.Tensor:
-        """Allocate destination blocks for every request; returns the [C, blocks] id table (CPU)."""
+    def begin_wave(self, buf: int = 0) -> torch.Tensor:
+        """Allocate destination blocks for every request of wave buffer ``buf``;
+        returns the [C, blocks] id table (CPU)."""
         C, bpr = self.cfg.concurrency, self.cfg.request_blocks
         got = self.blocks.allocate(C * bpr)
         if got is None:
             raise RuntimeError("decode pool exhausted")
-        self._ids = got[0]
-        table = torch.tensor(self._ids, dtype=torch.int32).view(C, bpr)
-        self.block_table.copy_(table, non_blocking=False)
+        self._ids[buf] = got[0]
+        table = torch.tensor(self._ids[buf], dtype=torch.int32).view(C, bpr)
+        self.tables[buf].copy_(table)
         return table
 
-    def end_wave(self) -> None:
-        self.blocks.release_mutable_many(self._ids)
-        self._ids = []
+    def end_wave(self, buf: int = 0) -> None:
+        self.blocks.release_mutable_many(self._ids[buf])
+        self._ids[buf] = []
 
     def _step(self) -> None:
         nxt = self.model.decode_step(self.tok, self.pos, self.pool, self.block_table, self.seq_lens, self.splits)
@@ -133,17 +141,19 @@ class DecodeInstance:
         self.graph_launches = _lib.launch_count() - before
         self.graph = g
 
-    def decode(self, seq: int, stream: torch.cuda.Stream) -> tuple[torch.cuda.Event, torch.cuda.Event]:
+    def decode(self, seq: int, stream: torch.cuda.Stream, buf: int = 0) -> tuple[torch.cuda.Event, torch.cuda.Event]:
         """Wait for every request's KV + first token, then generate. Returns (start, end) events."""
         from ..ops import _lib
 
         C, cfg = self.cfg.concurrency, self.cfg
+        base = buf * C
         with torch.cuda.stream(stream):
-            self.mailbox.wait_all(C, seq, stream=stream)
-            _lib.count_launches(1)
+            kv_ops.wait_flags_all(self.mailbox.flags + base * 8, C, seq, WAIT_TIMEOUT_NS, self.mailbox.status,
+                                  stream=stream)
             start = torch.cuda.Event(enable_timing=True)
             start.record(stream)
-            self.tok.copy_(self.mailbox.payload_t[:C])
+            self.block_table.copy_(self.tables[buf])
+            self.tok.copy_(self.mailbox.payload_t[base: base + C])
             self.pos.fill_(cfg.prompt_len)
             self.seq_lens.fill_(cfg.prompt_len + 1)
             self.step_idx.zero_()
@@ -171,10 +181,9 @@ class PrefillInstance:
         ids = torch.tensor(got[0], dtype=torch.int32).view(cfg.prefill_buffers, cfg.prompt_blocks)
         self.slot_ids = [ids[i].to(model.device) for i in range(cfg.prefill_buffers)]
         self.first_tok = torch.zeros(cfg.concurrency, dtype=torch.int64, device=model.device)
-        self.stream = torch.cuda.Stream(device=model.device)
 
     def prefill_wave(self, prompts: torch.Tensor, dst_table: torch.Tensor, seq: int, sender: PdSender,
-                     stream: torch.cuda.Stream) -> list[torch.cuda.Event]:
+                     stream: torch.cuda.Stream, slot_base: int = 0) -> list[torch.cuda.Event]:
         """Prefill every request, streaming KV layer by layer; returns per-request delivery events."""
         cfg = self.cfg
         done: list[torch.cuda.Event] = []
@@ -190,7 +199,7 @@ class PrefillInstance:
                                              l, s, d, after=stream))
                 self.first_tok[r: r + 1].copy_(nxt)
                 sender.stream.wait_stream(stream)
-                done.append(sender.complete(r, seq, payload=self.first_tok[r: r + 1]))
+                done.append(sender.complete(slot_base + r, seq, payload=self.first_tok[r: r + 1]))
         return done
 
 
@@ -205,26 +214,32 @@ class WaveResult:
 
 
 class DisaggServer:
-    """One P/D pair (colocated on one GPU, or split over two ranks)."""
+    """One P/D pair (colocated on one GPU, or split over two ranks).
+
+    Control messages (wave dispatch: sequence number, mailbox slot base and
+    destination block table) go through a key-value store (the
+    torch.distributed TCPStore); KV and first tokens never leave the GPUs.
+    """
 
     def __init__(self, cfg: DisaggConfig, role: str, device: int, peer_rank: int | None = None,
-                 group=None):
+                 group=None, store=None, pair_id: int = 0):
         assert role in ("colocated", "prefill", "decode")
         self.cfg, self.role = cfg, role
-        self.peer, self.group = peer_rank, group
+        self.peer, self.group, self.store, self.pair = peer_rank, group, store, pair_id
         torch.cuda.set_device(device)
         self.device = torch.device("cuda", device)
         self.model = LlamaModel(cfg.model, self.device, seed=cfg.seed)
         self.seq = 0
         self.prefill = self.decoder = self.sender = None
         if role in ("colocated", "decode"):
-            self.decoder = DecodeInstance(self.model, cfg)
+            self.decoder = DecodeInstance(self.model, cfg, buffers=2 if role == "decode" else 1)
         if role in ("colocated", "prefill"):
             self.prefill = PrefillInstance(self.model, cfg)
         if role == "colocated":
             self.sender = PdSender(self.prefill.pool, self.decoder.pool, None, 0, engine=cfg.engine,
                                    max_ctas=cfg.max_ctas)
         self.main = torch.cuda.Stream(device=self.device)
+        self._pending: tuple[int, int] | None = None
 
     # ---------------------------------------------------------- set-up
     def connect(self) -> None:
@@ -246,44 +261,74 @@ class DisaggServer:
             self.decoder.capture()
         torch.cuda.synchronize()
 
-    # ----------------------------------------------------------- a wave
-    def serve_wave(self, prompts_host: torch.Tensor | None) -> WaveResult:
-        """Serve one wave. Prefill/colocated ranks pass pinned host prompts [C, S]
-        (int32); decode/colocated ranks get the host output tokens back."""
-        cfg = self.cfg
+    # ----------------------------------------------------- control plane
+    def _key(self, seq: int) -> str:
+        return f"kvbm/pd/{self.pair}/wave/{seq}"
+
+    def _dispatch(self) -> tuple[int, int]:
+        """Decode side: allocate the next wave's blocks and hand them to prefill."""
         self.seq += 1
         seq = self.seq
+        buf = seq % self.decoder.buffers
+        table = self.decoder.begin_wave(buf)
+        header = torch.tensor([seq, buf * self.cfg.concurrency], dtype=torch.int32)
+        self.store.set(self._key(seq), torch.cat([header, table.view(-1)]).numpy().tobytes())
+        return seq, buf
+
+    def _receive(self) -> tuple[int, int, torch.Tensor]:
+        """Prefill side: block until the next wave is dispatched."""
+        seq = self.seq + 1
+        raw = self.store.get(self._key(seq))
+        self.store.delete_key(self._key(seq))
+        arr = torch.frombuffer(bytearray(raw), dtype=torch.int32)
+        self.seq = int(arr[0])
+        return int(arr[0]), int(arr[1]), arr[2:].view(self.cfg.concurrency, self.cfg.request_blocks)
+
+    # ----------------------------------------------------------- a wave
+    def serve_wave(self, prompts_host: torch.Tensor | None, more: bool = False) -> WaveResult:
+        """Serve one wave. Prefill/colocated ranks pass pinned host prompts [C, S]
+        (int32); decode/colocated ranks get the host output tokens back.
+
+        On a decode rank ``more=True`` dispatches the following wave before
+        decoding this one (pipelining prefill of k+1 with decode of k)."""
+        cfg = self.cfg
         C = cfg.concurrency
         st = self.main
-        t0 = torch.cuda.Event(enable_timing=True)
-        t0.record(st)
-        # decode side allocates the destination blocks and tells prefill
-        if self.decoder is not None:
-            table = self.decoder.begin_wave()
-        if self.role == "decode":
-            dist.send(table, dst=self.peer, group=self.group)
-        elif self.role == "prefill":
-            table = torch.empty(C, cfg.request_blocks, dtype=torch.int32)
-            dist.recv(table, src=self.peer, group=self.group)
         res = WaveResult(tokens=None, step_ms=0.0)
+        t0 = torch.cuda.Event(enable_timing=True)
         done: list[torch.cuda.Event] = []
-        if self.prefill is not None:
+        if self.role == "prefill":
+            seq, slot_base, table = self._receive()
+            t0.record(st)  # the wave arrives when decode dispatches it
             with torch.cuda.stream(st):
                 prompts = prompts_host.to(self.device, non_blocking=True)
-                dst = table.to(self.device, non_blocking=True) if self.role == "prefill" else \
-                    self.decoder.block_table
-            done = self.prefill.prefill_wave(prompts, dst, seq, self.sender, st)
-            if self.role == "prefill" and done:
-                st.wait_event(done[-1])
+                dst = table.to(self.device, non_blocking=True)
+            done = self.prefill.prefill_wave(prompts, dst, seq, self.sender, st, slot_base)
+            st.wait_event(done[-1])
+        elif self.role == "decode":
+            t0.record(st)
+            if self._pending is None:
+                self._pending = self._dispatch()
+            seq, buf = self._pending
+            self._pending = self._dispatch() if more else None
+            dec_s, dec_e = self.decoder.decode(seq, st, buf)
+        else:
+            self.seq += 1
+            seq = self.seq
+            t0.record(st)
+            self.decoder.begin_wave(0)
+            with torch.cuda.stream(st):
+                prompts = prompts_host.to(self.device, non_blocking=True)
+            done = self.prefill.prefill_wave(prompts, self.decoder.tables[0], seq, self.sender, st)
+            for ev in done:
+                st.wait_event(ev)
+            with torch.cuda.stream(st):
+                # colocated: the first tokens stay local
+                self.decoder.mailbox.payload_t[:C].copy_(self.prefill.first_tok)
+                self.decoder.mailbox.flags_t[:C].fill_(seq)
+            dec_s, dec_e = self.decoder.decode(seq, st, 0)
+            buf = 0
         if self.decoder is not None:
-            if self.role == "colocated":
-                for ev in done:
-                    st.wait_event(ev)
-                with torch.cuda.stream(st):
-                    # first tokens: payload stays local
-                    self.decoder.mailbox.payload_t[:C].copy_(self.prefill.first_tok)
-                    self.decoder.mailbox.flags_t[:C].fill_(seq)
-            dec_s, dec_e = self.decoder.decode(seq, st)
             with torch.cuda.stream(st):
                 out = torch.empty(C, cfg.gen_len, dtype=torch.int64, pin_memory=True)
                 out.copy_(self.decoder.tokens_out, non_blocking=True)
@@ -295,7 +340,7 @@ class DisaggServer:
             self.decoder.mailbox.check()
             res.tokens = out
             res.decode_ms = dec_s.elapsed_time(dec_e)
-            self.decoder.end_wave()
+            self.decoder.end_wave(buf)
         if self.prefill is not None:
             for ev in done:
                 ev.synchronize()
