@@ -1,0 +1,188 @@
+"""vLLM v1 KV-connector adapter (``kv_connector_module_path=kvbm_b200.connector.vllm_connector``,
+``kv_connector=KvbmConnector``).
+
+Importing this module does not import vLLM until a connector is built, so
+the package stays importable without vLLM (the reference tests the same
+lazy-import property: python/tests/test_connector_lazy_import.py).
+
+Role dispatch and hook set follow python/kvbm/vllm/connector/base.py:55-473
+(KvbmConnector), leader.py and worker.py; the scheduler process runs a
+:class:`~kvbm_b200.connector.leader.ConnectorLeader` over an
+:class:`~kvbm_b200.engine.leader.InstanceLeader`, each GPU worker a
+:class:`~kvbm_b200.connector.worker.ConnectorWorker`.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from typing import Any
+
+from .config import extract_vllm_config_for_kvbm, kv_block_bytes
+from .leader import ConnectorLeader, KvbmRequest, SchedulerOutputLite
+
+
+def process_scheduler_output(step: int, so, slots: dict) -> SchedulerOutputLite:
+    """vLLM SchedulerOutput -> the connector's framework-neutral step view."""
+    out = SchedulerOutputLite(step=step)
+    sched = dict(getattr(so, "num_scheduled_tokens", {}) or {})
+    for nr in getattr(so, "scheduled_new_reqs", []) or []:
+        blocks = list(nr.block_ids[0]) if nr.block_ids else []
+        out.scheduled[nr.req_id] = ([], blocks, nr.num_computed_tokens + sched.get(nr.req_id, 0))
+    cached = getattr(so, "scheduled_cached_reqs", None)
+    if cached is not None:
+        all_tok = getattr(cached, "all_token_ids", {}) or {}
+        for i, rid in enumerate(cached.req_ids):
+            nb = cached.new_block_ids[i]
+            new_blocks = list(nb[0]) if nb else []
+            slot = slots.get(rid)
+            toks: list[int] = []
+            if slot is not None:
+                full = all_tok.get(rid)
+                if full is not None:
+                    toks = list(full[len(slot.seq):])
+                elif cached.new_token_ids and i < len(cached.new_token_ids):
+                    toks = list(cached.new_token_ids[i])
+            out.scheduled[rid] = (toks, new_blocks, cached.num_computed_tokens[i] + sched.get(rid, 0))
+    out.finished_req_ids = list(getattr(so, "finished_req_ids", []) or [])
+    return out
+
+
+def _base():
+    from vllm.distributed.kv_transfer.kv_connector.v1.base import (KVConnectorBase_V1, KVConnectorMetadata,
+                                                                  KVConnectorRole)
+    return KVConnectorBase_V1, KVConnectorMetadata, KVConnectorRole
+
+
+def __getattr__(name):  # lazily build the vLLM subclasses on first access
+    if name in ("KvbmConnector", "KvbmConnectorMetadata"):
+        _define()
+        return globals()[name]
+    raise AttributeError(name)
+
+
+def _define():
+    if "KvbmConnector" in globals():
+        return
+    Base, MetaBase, Role = _base()
+
+    class KvbmConnectorMetadata(MetaBase):
+        def __init__(self, metadata: bytes):
+            assert isinstance(metadata, bytes)
+            self.metadata = metadata
+
+    class KvbmConnector(Base):
+        """KV Block Manager connector for vLLM (scheduler and worker roles)."""
+
+        def __init__(self, vllm_config, role, kv_cache_config=None):
+            super().__init__(vllm_config=vllm_config, role=role, kv_cache_config=kv_cache_config)
+            from ..engine.leader import InstanceLeader, ParallelWorkers
+            from ..logical.manager import BlockManager, Tier
+            from ..utils.config import KvbmConfig
+            from .worker import ConnectorWorker, blocks_for_bytes
+
+            ktc = vllm_config.kv_transfer_config
+            extra = getattr(ktc, "kv_connector_extra_config", {}) or {}
+            self.info = extract_vllm_config_for_kvbm(vllm_config)
+            bs = self.info["block_size"]
+            self._step = 0
+            if role == Role.SCHEDULER:
+                cfg = KvbmConfig.for_leader(json.dumps(extra) if extra else None)
+                bpb = kv_block_bytes(self.info)
+                g2n = blocks_for_bytes(cfg.cache.host.cache_size_gb, cfg.cache.host.num_blocks, bpb)
+                g3n = blocks_for_bytes(cfg.cache.disk.cache_size_gb, cfg.cache.disk.num_blocks, bpb)
+                g2 = BlockManager(max(1, g2n), bs, cfg.cache.inactive_backend, Tier.G2,
+                                  duplicate_policy=cfg.cache.duplicate_policy)
+                g3 = BlockManager(g3n, bs, cfg.cache.inactive_backend, Tier.G3, registry=g2.registry) if g3n else None
+                self._leader = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([]), g3=g3), bs,
+                                               offload_enabled=g2n > 0,
+                                               decode_offload=os.getenv("KVBM_DECODE_OFFLOAD", "false") == "true")
+                self._worker = None
+            else:
+                cfg = KvbmConfig.for_worker(json.dumps(extra) if extra else None)
+                self._worker = ConnectorWorker(cfg, rank=self.info.get("rank", 0), block_size=bs,
+                                               num_kv_heads=self.info["num_kv_heads"],
+                                               head_size=self.info["head_size"])
+                self._leader = None
+
+        # ------------------------------------------------ scheduler side
+        @property
+        def prefer_cross_layer_blocks(self) -> bool:
+            return os.getenv("KVBM_PREFER_FULLY_CONTIGUOUS_BLOCKS", "false") == "true"
+
+        def _slot(self, request):
+            if not self._leader.has_slot(request.request_id):
+                salt = getattr(request, "cache_salt", None)
+                lora = getattr(getattr(request, "lora_request", None), "lora_name", None)
+                self._leader.create_slot(KvbmRequest(request.request_id, list(request.prompt_token_ids),
+                                                     lora_name=lora, salt=salt,
+                                                     kv_transfer_params=getattr(request, "kv_transfer_params",
+                                                                                None)))
+
+        def get_num_new_matched_tokens(self, request, num_computed_tokens: int):
+            self._slot(request)
+            return self._leader.get_num_new_matched_tokens(request.request_id, num_computed_tokens)
+
+        def update_state_after_alloc(self, request, blocks, num_external_tokens: int):
+            self._slot(request)
+            ids = [int(b) for b in blocks.get_block_ids()[0]]
+            self._leader.update_state_after_alloc(request.request_id, ids, num_external_tokens)
+
+        def build_connector_meta(self, scheduler_output):
+            self._step += 1
+            lite = process_scheduler_output(self._step, scheduler_output, self._leader.slots)
+            return KvbmConnectorMetadata(self._leader.build_connector_meta(lite))
+
+        def update_connector_output(self, connector_output):
+            self._leader.update_connector_output(getattr(connector_output, "finished_sending", None),
+                                                 getattr(connector_output, "finished_recving", None))
+
+        def request_finished(self, request, block_ids):
+            return self._leader.request_finished(request.request_id, list(block_ids))
+
+        def build_kv_connector_stats(self, data=None):
+            return None
+
+        # --------------------------------------------------- worker side
+        def register_kv_caches(self, kv_caches):
+            self._worker.register_kv_caches(dict(kv_caches))
+
+        def register_cross_layers_kv_cache(self, kv_cache, attn_backend=None):
+            self._worker.register_cross_layers_kv_cache(kv_cache)
+
+        def bind_connector_metadata(self, connector_metadata):
+            super().bind_connector_metadata(connector_metadata)
+            self._worker.bind_connector_metadata(connector_metadata.metadata)
+
+        def clear_connector_metadata(self):
+            super().clear_connector_metadata()
+            self._worker.clear_connector_metadata()
+
+        def handle_preemptions(self, kv_connector_metadata):
+            pass
+
+        def start_load_kv(self, forward_context, **kwargs: Any) -> None:
+            self._worker.start_load_kv()
+
+        def wait_for_layer_load(self, layer_name: str) -> None:
+            self._worker.wait_for_layer_load(layer_name)
+
+        def save_kv_layer(self, layer_name, kv_layer, attn_metadata, **kwargs) -> None:
+            self._worker.save_kv_layer(layer_name)
+
+        def wait_for_save(self):
+            self._worker.wait_for_save()
+
+        def get_finished(self, finished_req_ids):
+            sending, recving = self._worker.get_finished(set(finished_req_ids))
+            return (sending or None), (recving or None)
+
+        def get_block_ids_with_load_errors(self):
+            return self._worker.get_block_ids_with_load_errors()
+
+        def shutdown(self):
+            if self._worker is not None:
+                self._worker.shutdown()
+
+    globals()["KvbmConnector"] = KvbmConnector
+    globals()["KvbmConnectorMetadata"] = KvbmConnectorMetadata

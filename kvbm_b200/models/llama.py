@@ -148,12 +148,26 @@ class LlamaModel:
             q = qkv[:, : c.heads].transpose(0, 1).unsqueeze(0)
             k = qkv[:, c.heads: c.heads + c.kv_heads].transpose(0, 1)
             v = qkv[:, c.heads + c.kv_heads:].transpose(0, 1)
+            mask = None
+            if start_pos > 0:
+                # cached prefix (e.g. onboarded from G2): read its K/V from the pool
+                nb = (start_pos + page - 1) // page
+                view = pool.layer_view(li)[block_ids[:nb].long()]  # [nb, 2, page, Hkv, D]
+                pk = view[:, 0].reshape(-1, c.kv_heads, c.head_dim)[:start_pos].transpose(0, 1)
+                pv = view[:, 1].reshape(-1, c.kv_heads, c.head_dim)[:start_pos].transpose(0, 1)
+                k = torch.cat([pk, k], dim=1)
+                v = torch.cat([pv, v], dim=1)
+                qi = torch.arange(T, device=self.device).unsqueeze(1) + start_pos
+                mask = torch.arange(start_pos + T, device=self.device).unsqueeze(0) <= qi
             rep = c.heads // c.kv_heads
             k = k.repeat_interleave(rep, dim=0).unsqueeze(0)
             v = v.repeat_interleave(rep, dim=0).unsqueeze(0)
             with sdpa_kernel([SDPBackend.FLASH_ATTENTION, SDPBackend.CUDNN_ATTENTION,
                               SDPBackend.EFFICIENT_ATTENTION]):
-                a = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=self.scale)
+                if mask is None:
+                    a = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=self.scale)
+                else:
+                    a = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=self.scale)
             a = a.squeeze(0).transpose(0, 1).reshape(T, c.q_size)
             x = F.linear(a, L["wo"])
             llama_ops.rmsnorm(x, L["n2"], c.eps, residual=residual, out=h)

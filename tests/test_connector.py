@@ -1,0 +1,104 @@
+"""Connector leader logic on CPU (no GPU): matching, onboard planning,
+save-cursor offloads, delayed frees; and the step-metadata wire format."""
+
+import pytest
+
+from kvbm_b200.connector.leader import ConnectorLeader, KvbmRequest, SchedulerOutputLite
+from kvbm_b200.connector.protocol import ConnectorMetadata, OffloadOp, OnboardOp
+from kvbm_b200.engine.leader import InstanceLeader, ParallelWorkers
+from kvbm_b200.logical.manager import BlockManager, Tier
+
+
+def make_leader(g2_blocks=64, bs=16):
+    g2 = BlockManager(g2_blocks, bs, "lineage", Tier.G2)
+    return ConnectorLeader(InstanceLeader(g2, ParallelWorkers([])), bs)
+
+
+def step(leader, n, sched):
+    return ConnectorMetadata.decode(leader.build_connector_meta(SchedulerOutputLite(n, sched)))
+
+
+def test_cold_request_offloads_complete_blocks():
+    L = make_leader()
+    prompt = list(range(100))
+    L.create_slot(KvbmRequest("a", prompt))
+    assert L.get_num_new_matched_tokens("a", 0) == (0, False)
+    L.update_state_after_alloc("a", list(range(7)), 0)
+    # chunked prefill: 48 tokens, then the rest
+    m = step(L, 1, {"a": ([], [], 48)})
+    assert [o.g1_ids for o in m.offload] == [[0, 1, 2]] and not m.onboard
+    m = step(L, 2, {"a": ([], [], 100)})
+    assert m.offload[0].g1_ids == [3, 4, 5]  # 100 tokens -> 6 complete blocks
+    assert L.request_finished("a") == (True, None)  # offload still in flight
+    L.update_connector_output(finished_sending={"a"})
+    assert L.num_slots() == 0
+
+
+def test_warm_request_onboards_and_skips_present_blocks():
+    L = make_leader()
+    prompt = list(range(100))
+    L.create_slot(KvbmRequest("a", prompt))
+    L.get_num_new_matched_tokens("a", 0)
+    L.update_state_after_alloc("a", list(range(7)), 0)
+    step(L, 1, {"a": ([], [], 100)})
+    L.update_connector_output(finished_sending={"a"})
+    L.request_finished("a")
+    # same prompt again: 6 cached blocks, but the last prompt token must be computed -> 6 blocks (96 < 99)
+    L.create_slot(KvbmRequest("b", prompt))
+    n, is_async = L.get_num_new_matched_tokens("b", 0)
+    assert (n, is_async) == (96, True)
+    L.update_state_after_alloc("b", list(range(20, 27)), n)
+    m = step(L, 2, {"b": ([], [], 100)})
+    assert len(m.onboard) == 1 and m.onboard[0].g1_ids == list(range(20, 26))
+    assert m.offload == []  # everything already in G2
+    L.update_connector_output(finished_recving={"b"})
+    assert L.request_finished("b") == (False, None)
+
+
+def test_framework_prefix_hit_is_skipped():
+    L = make_leader()
+    prompt = list(range(64))
+    L.create_slot(KvbmRequest("a", prompt))
+    L.update_state_after_alloc("a", list(range(4)), 0)
+    step(L, 1, {"a": ([], [], 64)})
+    L.create_slot(KvbmRequest("b", prompt + list(range(1000, 1040))))
+    # the framework already has 32 tokens in G1: KVBM contributes blocks 2..3
+    n, _ = L.get_num_new_matched_tokens("b", 32)
+    assert n == 32
+
+
+def test_salt_separates_caches():
+    L = make_leader()
+    prompt = list(range(64))
+    L.create_slot(KvbmRequest("a", prompt, lora_name="x"))
+    L.update_state_after_alloc("a", list(range(4)), 0)
+    step(L, 1, {"a": ([], [], 64)})
+    L.create_slot(KvbmRequest("b", prompt, lora_name="y"))
+    assert L.get_num_new_matched_tokens("b", 0) == (0, False)
+
+
+def test_decode_tokens_extend_sequence_when_enabled():
+    L = make_leader()
+    L.decode_offload = True
+    L.create_slot(KvbmRequest("a", list(range(30))))
+    L.update_state_after_alloc("a", [0, 1, 2], 0)
+    m = step(L, 1, {"a": ([], [], 30)})
+    assert [o.g1_ids for o in m.offload] == [[0]]
+    m = step(L, 2, {"a": ([7, 8], [], 32)})
+    assert [o.g1_ids for o in m.offload] == [[1]]
+
+
+def test_metadata_roundtrip():
+    m = ConnectorMetadata(3, [OnboardOp("r", [1, 2], [5, 6])], [OffloadOp("q", [7], [9])], ["z"])
+    d = ConnectorMetadata.decode(m.encode())
+    assert d == m
+
+
+def test_lazy_import_does_not_pull_vllm():
+    import subprocess
+    import sys
+
+    code = ("import sys; import kvbm_b200.connector.vllm_connector as m; "
+            "print('vllm' in sys.modules)")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True)
+    assert out.stdout.strip() == "False"

@@ -1,0 +1,210 @@
+"""Control-plane services on CPU: hub (registry/TTL, indexer, CD queue,
+prefill routing with a real prefill handler over the messenger), messenger
+RPC/events, config layering, offload pipelines, metrics, strategy matrix."""
+
+import time
+
+import pytest
+
+from kvbm_b200 import _core_native as core
+from kvbm_b200.engine.offload import (AllOf, AnyOf, OffloadEngine, OffloadItem, OffloadPipeline, OffloadState,
+                                      PassAll, PresenceAndLFUFilter, PresenceFilter)
+from kvbm_b200.hub.client import CompletionEvent, HubClient, HubRegistration, PrefillRouterHandler
+from kvbm_b200.hub.kvbmctl import main as kvbmctl
+from kvbm_b200.hub.prefill_router import BreakerConfig, BreakerTier, Calibration, CircuitBreaker, Selector
+from kvbm_b200.hub.server import HubServer
+from kvbm_b200.logical.manager import BlockManager, Tier
+from kvbm_b200.logical.sequence import sequence_hashes
+from kvbm_b200.physical.transfer import StorageKind, TransferStrategy, select_strategy, TransferCapabilities
+from kvbm_b200.runtime.messenger import EventPoisoned, MessengerPair, RpcError, wait_until
+from kvbm_b200.utils.config import KvbmConfig
+from kvbm_b200.utils.metrics import KvbmCollector, make_registry
+
+
+@pytest.fixture
+def hub():
+    h = HubServer(max_seq_len=4096, ttl=0.3).start()
+    yield h
+    h.stop()
+
+
+def test_hub_registry_ttl_and_guard(hub):
+    c = HubClient(hub.url)
+    assert c.health()["status"] == "ok"
+    c.register(11, role="decode", features=["indexer"], address="tcp://x")
+    assert [i["instance_id"] for i in c.instances()] == ["11"]
+    assert wait_until(lambda: c.instances() == [], 3.0)  # no heartbeat -> evicted after ttl
+    with HubRegistration(c, 12, heartbeat_s=0.05, role="prefill") as reg:
+        time.sleep(0.6)
+        assert [i["instance_id"] for i in c.instances()] == ["12"]  # heartbeats keep it alive
+    assert c.instances() == []  # the guard deregistered
+
+
+def test_hub_indexer_deepest_holder(hub):
+    c = HubClient(hub.url)
+    for iid in (1, 2):
+        c.register(iid, features=["indexer"])
+    hs = sequence_hashes(list(range(16 * 6)), 16)
+    c.publish_events(1, [("create", hs[:5])])
+    c.publish_events(2, [("create", hs[:2])])
+    q = c.query(hs)
+    assert q["hit"] and q["hash"] == hs[4] and q["holders"] == [1]
+    c.publish_events(1, [("remove", hs[2:5])])
+    q = c.query(hs)
+    assert q["position"] == 1 and sorted(q["holders"]) == [1, 2]
+    c.unregister(1)
+    assert c.query(hs)["holders"] == [2]
+
+
+def test_hub_cd_queue_and_dispatch_to_prefill_handler(hub):
+    c = HubClient(hub.url)
+    c.cd_enqueue({"request_id": "r1", "num_tokens": 100})
+    assert c.cd_dequeue()["request_id"] == "r1" and c.cd_dequeue() is None
+
+    seen = []
+
+    def dispatch(req, done: CompletionEvent):
+        seen.append(req["request_id"])
+        done.complete({"first_token": 42})
+
+    h = PrefillRouterHandler(hub.url, dispatch, calibrate=lambda: {"ttft": [(1000, 0.1), (2000, 0.25),
+                                                                           (4000, 0.7)]})
+    try:
+        assert wait_until(lambda: len(c.targets()) == 1, 3.0)
+        out = c.dispatch(4096, 1024, {"request_id": "r2"})
+        assert out["forwarded"] and out["result"]["result"] == {"first_token": 42}
+        assert seen == ["r2"]
+        counters = c.router_counters()
+        assert counters["counters"]["dispatched"] == 1
+        assert "ttft_coeffs" in counters["calibration"][str(h.instance_id)]
+    finally:
+        h.close()
+
+
+def test_kvbmctl_renders(hub, capsys):
+    HubClient(hub.url).register(5, role="both", features=["indexer"])
+    assert kvbmctl(["--hub", hub.url, "instances"]) == 0
+    assert "INSTANCE_ID" in capsys.readouterr().out
+
+
+def test_selector_and_breaker():
+    s = Selector(max_inflight=1)
+    s.add_worker(1)
+    s.add_worker(2)
+    a = s.pick(1000, 0)
+    b = s.pick(500, 0)
+    assert {a.slot.instance_id, b.slot.instance_id} == {1, 2}
+    with pytest.raises(TimeoutError):
+        s.pick(10, 0, timeout=0.05)
+    a.release()
+    c = s.pick(10, 0)
+    assert c.slot.instance_id == a.slot.instance_id
+    br = CircuitBreaker(BreakerConfig(warm_enter=10, hot_enter=20, warm_exit=5, hot_exit=15))
+    assert br.evaluate(12) == BreakerTier.WARM
+    assert br.evaluate(25) == BreakerTier.HOT
+    assert br.evaluate(16) == BreakerTier.HOT     # hysteresis
+    assert br.evaluate(10) == BreakerTier.WARM
+    assert br.evaluate(1) == BreakerTier.CALM
+    cal = Calibration()
+    for x in (100, 200, 400, 800):
+        cal.add_ttft(x, 0.01 + 1e-4 * x + 1e-7 * x * x)
+    assert abs(cal.predict_ttft(600) - (0.01 + 0.06 + 0.036)) < 1e-6
+
+
+def test_messenger_rpc_events_and_errors():
+    p = MessengerPair()
+    try:
+        p.b.register_handler("echo", lambda x: x)
+        assert p.a.call(p.b.instance_id, "echo", {"k": [1, 2]}) == {"k": [1, 2]}
+        with pytest.raises(RpcError):
+            p.a.call(p.b.instance_id, "missing")
+        ev = p.a.new_event()
+        p.b.poison(ev, "pull failed", owner=p.a.instance_id)
+        with pytest.raises(EventPoisoned):
+            p.a.wait_event(ev, timeout=1)
+        with pytest.raises(TimeoutError):
+            p.a.wait_event(p.a.new_event(), timeout=0.05)
+    finally:
+        p.close()
+
+
+def test_config_layering(tmp_path):
+    toml = tmp_path / "k.toml"
+    toml.write_text('[cache.host]\ncache_size_gb = 2.0\n[onboard]\nmode = "intra"\n')
+    env = {"DYN_KVBM_CPU_CACHE_GB": "1", "KVBM_CONFIG_PATH": str(toml), "KVBM_CACHE_DISK_NUM_BLOCKS": "7"}
+    c = KvbmConfig.load({"default": {"block_size": 32}, "worker": {"cache": {"host": {"num_blocks": 9}}}},
+                        role="worker", env=env, system_toml=None)
+    assert c.cache.host.cache_size_gb == 2.0       # TOML beats DYN_KVBM_*
+    assert c.cache.disk.num_blocks == 7            # KVBM_* env
+    assert c.cache.host.num_blocks == 9            # JSON worker profile
+    assert c.block_size == 32 and c.onboard.mode == "intra"
+    with pytest.raises(ValueError):
+        KvbmConfig.load({"block_layout": "weird"}, env={}, system_toml=None)
+    with pytest.raises(ValueError):
+        KvbmConfig.load({"nonsense": 1}, env={}, system_toml=None)
+
+
+def test_offload_pipeline_policies_batching_cancel():
+    dst = BlockManager(32, 16, "lru", Tier.G2, registry=core.Registry(frequency=core.TinyLfu(64)))
+    calls = []
+
+    def executor(items):
+        calls.append(len(items))
+        blocks = dst.allocate_blocks(len(items))
+        return dst.register_mutable(blocks, [i.seq_hash for i in items])
+
+    hs = sequence_hashes(list(range(16 * 10)), 16)
+    p = OffloadPipeline("g1_to_g2", dst, executor, PresenceFilter(dst))
+    p.cfg.max_batch = 4
+    h = p.enqueue([OffloadItem(x, i) for i, x in enumerate(hs[:6])])
+    assert h.wait(5) == OffloadState.DONE and calls == [4, 2]
+    h2 = p.enqueue([OffloadItem(x, i) for i, x in enumerate(hs[:8])])
+    assert h2.wait(5) == OffloadState.DONE and len(h2.skipped) == 6  # presence filter
+    gate = {"open": False}
+    h3 = p.enqueue([OffloadItem(hs[9], 9)], precondition=lambda: gate["open"])
+    time.sleep(0.05)
+    assert h3.cancel() and h3.wait(5) == OffloadState.CANCELLED
+    assert not h2.cancel()  # already final
+    lfu = PresenceAndLFUFilter(dst, min_frequency=3)
+    assert not lfu.keep(OffloadItem(hs[9], 0))
+    assert AnyOf(PassAll(), lfu).keep(OffloadItem(hs[9], 0)) and not AllOf(PassAll(), lfu).keep(OffloadItem(hs[9], 0))
+    p.close()
+
+
+def test_metrics_collector_names():
+    mgr = BlockManager(8, 16, "lru", Tier.G2)
+    blocks = mgr.allocate_blocks(2)
+    mgr.register_mutable(blocks, sequence_hashes(list(range(32)), 16))
+    col = KvbmCollector()
+    col.add_pool("g2", mgr)
+    col.transfer.observe(0.002, 1 << 20)
+    from prometheus_client import generate_latest
+
+    text = generate_latest(make_registry(col)).decode()
+    for name in ("kvbm_allocations_total", "kvbm_registrations_total", "kvbm_inactive_pool_size",
+                 "kvbm_transfer_duration_seconds_bucket", "kvbm_host_cache_hit_rate", "kvbm_cd_decisions_total"):
+        assert name in text, name
+
+
+def test_strategy_matrix():
+    K, S = StorageKind, TransferStrategy
+    assert select_strategy(K.PINNED, K.DEVICE).first == S.KERNEL_H2D
+    assert select_strategy(K.DEVICE, K.PINNED, TransferCapabilities(prefer_copy_engine=True)).first == S.CUDA_ASYNC_D2H
+    p = select_strategy(K.DEVICE, K.DISK)
+    assert p.is_two_hop and p.bounce == K.PINNED and p.second == S.DISK_WRITE
+    assert not select_strategy(K.DEVICE, K.DISK, TransferCapabilities(allow_gds=True)).is_two_hop
+    assert select_strategy(K.DEVICE, K.PEER).first == S.KERNEL_P2P
+    assert select_strategy(K.DISK, K.DISK).first == S.INVALID
+
+
+def test_disk_pool_roundtrip(tmp_path):
+    import numpy as np
+
+    d = core.DiskPool(str(tmp_path / "g3.bin"), 8, 4096, direct=False, persistent=True)
+    a = np.random.randint(0, 255, 4096 * 3, dtype=np.uint8)
+    b = np.zeros_like(a)
+    d.write([1, 4, 7], [a.ctypes.data + i * 4096 for i in range(3)])
+    d.read([1, 4, 7], [b.ctypes.data + i * 4096 for i in range(3)])
+    assert (a == b).all() and d.bytes_written() == 3 * 4096
+    with pytest.raises(IndexError):
+        d.read([8], [b.ctypes.data])
