@@ -35,7 +35,8 @@ CUDA_SOURCES = [
     CSRC / "kernels" / "llama_ops.cu",
     CSRC / "kernels" / "kvbm_mem.cu",
 ]
-CUDA_HEADERS = [CSRC / "kernels" / "common.cuh", CSRC / "kernels" / "kvbm_kernels.h"]
+CUDA_HEADERS = [CSRC / "kernels" / "common.cuh", CSRC / "kernels" / "kvbm_kernels.h",
+                CSRC / "kernels" / "decode_attn_mma.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -8,6 +8,7 @@
 // end on a PyTorch Llama model whose KV cache lives in the block manager's
 // paged layout, with GEMMs left to cuBLAS.
 #include "common.cuh"
+#include "decode_attn_mma.cuh"
 
 #include <algorithm>
 
@@ -407,7 +408,7 @@ extern "C" int kvbm_silu_mul(const void* gate_up, void* out, int64_t tokens, int
 }
 
 // Scratch: part_acc holds batch*hq*splits*128 floats, part_ml batch*hq*splits*2.
-extern "C" int kvbm_paged_decode_attn(const void* q, const void* k_base, const void* v_base, int64_t block_stride,
+extern "C" int kvbm_paged_decode_attn_simt(const void* q, const void* k_base, const void* v_base, int64_t block_stride,
                                       int64_t token_stride, int64_t head_stride, int page, const int32_t* block_table,
                                       int max_blocks, const int32_t* seq_lens, int batch, int hq, int hkv, int hd,
                                       float softmax_scale, int splits, float* part_acc, float* part_ml, void* out,
@@ -449,6 +450,53 @@ extern "C" int kvbm_paged_decode_attn(const void* q, const void* k_base, const v
       return cudaErrorInvalidValue;
   }
   cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  attn_combine_kernel<<<static_cast<unsigned>(batch) * hq, kHD, 0, stream>>>(part_acc, part_ml, splits,
+                                                                            static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
+}
+
+// Tensor-core paged decode attention (mma.sync + cp.async staging); falls
+// back to the SIMT kernel for shapes it does not cover. Same scratch layout.
+extern "C" int kvbm_paged_decode_attn(const void* q, const void* k_base, const void* v_base, int64_t block_stride,
+                                      int64_t token_stride, int64_t head_stride, int page, const int32_t* block_table,
+                                      int max_blocks, const int32_t* seq_lens, int batch, int hq, int hkv, int hd,
+                                      float softmax_scale, int splits, float* part_acc, float* part_ml, void* out,
+                                      cudaStream_t stream) {
+  const int group = hkv > 0 ? hq / hkv : 0;
+  const bool mma_ok = hd == kvbm::attn::kHD && hkv > 0 && hq % hkv == 0 &&
+                      (group == 1 || group == 2 || group == 4 || group == 8) && page % 16 == 0 &&
+                      token_stride % 16 == 0 && head_stride % 16 == 0 && block_stride % 16 == 0 &&
+                      (reinterpret_cast<uintptr_t>(k_base) % 16) == 0 && (reinterpret_cast<uintptr_t>(v_base) % 16) == 0;
+  if (!mma_ok)
+    return kvbm_paged_decode_attn_simt(q, k_base, v_base, block_stride, token_stride, head_stride, page, block_table,
+                                       max_blocks, seq_lens, batch, hq, hkv, hd, softmax_scale, splits, part_acc,
+                                       part_ml, out, stream);
+  if (batch == 0) return cudaSuccess;
+  if (!q || !block_table || !seq_lens || !part_acc || !part_ml || !out || splits <= 0 || splits > 65535)
+    return cudaErrorInvalidValue;
+  const float qscale = softmax_scale * 1.4426950408889634f;
+  dim3 grid(splits, hkv, batch);
+  const auto* qq = static_cast<const __nv_bfloat16*>(q);
+  const auto* kb = static_cast<const uint8_t*>(k_base);
+  const auto* vb = static_cast<const uint8_t*>(v_base);
+  const size_t smem = kvbm::attn::kSmemBytes;
+  cudaError_t e = cudaSuccess;
+#define KVBM_LAUNCH_MMA(G)                                                                                      \
+  e = cudaFuncSetAttribute(kvbm::attn::paged_decode_mma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                           static_cast<int>(smem));                                                              \
+  if (e != cudaSuccess) return e;                                                                                \
+  kvbm::attn::paged_decode_mma_kernel<G><<<grid, kvbm::attn::kWarps * 32, smem, stream>>>(                      \
+      qq, kb, vb, block_stride, token_stride, head_stride, page, block_table, max_blocks, seq_lens, qscale, splits, \
+      part_acc, part_ml);
+  switch (group) {
+    case 1: KVBM_LAUNCH_MMA(1) break;
+    case 2: KVBM_LAUNCH_MMA(2) break;
+    case 4: KVBM_LAUNCH_MMA(4) break;
+    default: KVBM_LAUNCH_MMA(8) break;
+  }
+#undef KVBM_LAUNCH_MMA
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   attn_combine_kernel<<<static_cast<unsigned>(batch) * hq, kHD, 0, stream>>>(part_acc, part_ml, splits,
                                                                             static_cast<__nv_bfloat16*>(out));

@@ -82,9 +82,10 @@ def test_silu_mul():
     torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
 
 
+@pytest.mark.parametrize("impl", ["mma", "simt"])
 @pytest.mark.parametrize("group", [1, 4, 8])
 @pytest.mark.parametrize("splits", [1, 3, 8])
-def test_paged_decode_attention(group, splits):
+def test_paged_decode_attention(group, splits, impl):
     torch.manual_seed(3)
     B, hkv, hd, page = 5, 2, 128, 16
     hq = hkv * group
@@ -99,7 +100,7 @@ def test_paged_decode_attention(group, splits):
     scale = 1.0 / math.sqrt(hd)
     kb = pool.layer_base(0)
     out = llama_ops.paged_decode_attn(q, kb, kb + pool.outer_stride, pool.block_stride, pool.token_stride,
-                                      pool.head_stride, page, perm, seq, hkv, scale, splits)
+                                      pool.head_stride, page, perm, seq, hkv, scale, splits, impl=impl)
     torch.cuda.synchronize()
     view = pool.layer_view(0)
     for b in range(B):
