@@ -146,3 +146,66 @@ class ExportedPool:
     nbytes: int
     device: int
     rank: int = 0
+
+
+class SharedPinnedBuffer:
+    """A G2 pool in a named shared-memory file, page-locked and mapped into the
+    device address space of every process that opens it.
+
+    Any process on the node can map another instance's G2 pool by name, so a
+    copy kernel can read a peer's pinned blocks directly (cross-instance
+    prefix reuse without an intermediate hop). Hugepage-backed files
+    (``/dev/hugepages``) work the same way.
+    """
+
+    def __init__(self, name: str, nbytes: int, create: bool = True, directory: str = "/dev/shm"):
+        import mmap
+        import os
+
+        self.name, self.nbytes = name, int(nbytes)
+        self.path = os.path.join(directory, name)
+        flags = os.O_RDWR | (os.O_CREAT if create else 0)
+        fd = os.open(self.path, flags, 0o600)
+        try:
+            if create:
+                os.ftruncate(fd, self.nbytes)
+            self._mm = mmap.mmap(fd, self.nbytes, mmap.MAP_SHARED, mmap.PROT_READ | mmap.PROT_WRITE)
+        finally:
+            os.close(fd)
+        self.owner = create
+        buf = (C.c_uint8 * self.nbytes).from_buffer(self._mm)
+        self.ptr = C.addressof(buf)
+        del buf
+        _lib.check(_lib.load().kvbm_host_register(self.ptr, self.nbytes), "cudaHostRegister")
+        d = C.c_void_p()
+        _lib.check(_lib.load().kvbm_host_device_pointer(self.ptr, C.byref(d)), "cudaHostGetDevicePointer")
+        self.device_ptr = int(d.value or 0)
+
+    def tensor(self, dtype: torch.dtype = torch.uint8, shape: tuple | None = None) -> torch.Tensor:
+        arr = (C.c_uint8 * self.nbytes).from_address(self.ptr)
+        t = torch.frombuffer(arr, dtype=torch.uint8)
+        if dtype != torch.uint8:
+            t = t.view(dtype)
+        return t.view(shape) if shape is not None else t
+
+    def close(self) -> None:
+        import os
+
+        if self.ptr:
+            _lib.load().kvbm_host_unregister(self.ptr)
+            self.ptr = 0
+            try:
+                self._mm.close()
+            except BufferError:
+                pass
+            if self.owner:
+                try:
+                    os.unlink(self.path)
+                except FileNotFoundError:
+                    pass
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
