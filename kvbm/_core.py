@@ -1,0 +1,4 @@
+"""``kvbm._core`` names, implemented by :mod:`kvbm_b200._core`."""
+
+from kvbm_b200._core import *  # noqa: F401,F403
+from kvbm_b200._core import hub  # noqa: F401

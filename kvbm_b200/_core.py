@@ -1,0 +1,227 @@
+"""The binding surface the reference exposes as ``kvbm._core``.
+
+Classes: ``KvbmRuntime`` (config + messenger + optional hub registration;
+``build_leader`` / ``build_worker``), ``ConnectorLeader``,
+``ConnectorWorker``, ``KvbmRequest``, ``SchedulerOutput`` (builder),
+``Tensor`` (data_ptr/shape/stride/device view), ``KvbmVllmConfig``;
+functions ``is_available``; submodule ``hub`` with ``PrefillRouterHandler``
+and ``CompletionEvent``.
+
+Parity: src/lib.rs:74-105 (module contents), src/runtime.rs:57-177
+(build_worker, build_leader, peer_info, register_peer),
+src/connector/leader/mod.rs:40-347, leader/request.rs:8,
+leader/scheduler.rs:18-122, src/connector/worker/mod.rs:26-342,
+src/torch/mod.rs:140, src/vllm/config.rs:246, src/hub/prefill_router.rs.
+"""
+
+from __future__ import annotations
+
+import json
+import types
+import uuid
+from dataclasses import dataclass, field
+
+from . import __version__
+from .connector.leader import ConnectorLeader as _Leader
+from .connector.leader import KvbmRequest
+from .connector.leader import SchedulerOutputLite
+from .engine.leader import InstanceLeader, ParallelWorkers
+from .hub import client as _hub_client
+from .logical.manager import BlockManager, Tier
+from .runtime.messenger import Messenger
+from .utils.config import KvbmConfig
+
+LAYOUT_HANDLER = "kvbm.connector.worker.get_layout_config"
+
+
+def is_available() -> bool:
+    """True when the native core and the CUDA kernel library load."""
+    try:
+        from . import _core_native  # noqa: F401
+        from .ops import _lib
+
+        _lib.load(build_if_missing=False)
+        return True
+    except Exception:  # noqa: BLE001
+        return False
+
+
+class KvbmRuntime:
+    def __init__(self, config: KvbmConfig, role: str):
+        self.config, self.role = config, role
+        self.messenger = Messenger()
+        self.hub = None
+        if config.hub is not None and config.hub.url:
+            self.hub = _hub_client.HubClient(config.hub.url)
+
+    @classmethod
+    def build_leader(cls, json_config: str | None = None) -> "KvbmRuntime":
+        return cls(KvbmConfig.for_leader(json_config), "leader")
+
+    @classmethod
+    def build_worker(cls, json_config: str | None = None) -> "KvbmRuntime":
+        return cls(KvbmConfig.for_worker(json_config), "worker")
+
+    def instance_id(self) -> bytes:
+        return self.messenger.instance_id.to_bytes(16, "big")
+
+    def peer_info(self) -> tuple[int, str]:
+        return self.messenger.instance_id, self.messenger.address
+
+    def register_peer(self, instance_id: int, address: str) -> None:
+        self.messenger.register_peer(instance_id, address)
+
+    def shutdown(self) -> None:
+        self.messenger.close()
+
+
+class Tensor:
+    """A framework tensor as the block manager sees it."""
+
+    def __init__(self, t):
+        self._t = t
+
+    def data_ptr(self) -> int:
+        return self._t.data_ptr()
+
+    @property
+    def shape(self) -> list[int]:
+        return list(self._t.shape)
+
+    @property
+    def stride(self) -> list[int]:
+        return list(self._t.stride())
+
+    @property
+    def device(self) -> int:
+        return self._t.device.index if self._t.is_cuda else -1
+
+    @property
+    def element_size(self) -> int:
+        return self._t.element_size()
+
+    def torch(self):
+        return self._t
+
+
+@dataclass
+class KvbmVllmConfig:
+    info: dict = field(default_factory=dict)
+
+    @classmethod
+    def from_vllm(cls, vllm_config) -> "KvbmVllmConfig":
+        from .connector.config import extract_vllm_config_for_kvbm
+
+        return cls(extract_vllm_config_for_kvbm(vllm_config))
+
+
+class SchedulerOutput:
+    """Builder for one scheduler step (what vLLM's SchedulerOutput carries)."""
+
+    def __init__(self, iteration: int = 0):
+        self.iteration = iteration
+        self._lite = SchedulerOutputLite(step=iteration)
+        self._sched: dict[str, int] = {}
+
+    def add_new_request(self, request_id: str, prompt_token_ids: list[int], block_ids: list[int],
+                        num_computed_tokens: int) -> None:
+        self._lite.scheduled[request_id] = ([], list(block_ids), num_computed_tokens)
+
+    def add_cached_request(self, request_id: str, new_token_ids: list[int], new_block_ids: list[int],
+                           num_computed_tokens: int) -> None:
+        self._lite.scheduled[request_id] = (list(new_token_ids), list(new_block_ids), num_computed_tokens)
+
+    def add_num_scheduled_tokens(self, counts: dict[str, int]) -> None:
+        self._sched.update(counts)
+
+    def add_finished(self, request_ids: list[str]) -> None:
+        self._lite.finished_req_ids.extend(request_ids)
+
+    def lite(self) -> SchedulerOutputLite:
+        out = SchedulerOutputLite(self.iteration)
+        for rid, (toks, blocks, computed) in self._lite.scheduled.items():
+            out.scheduled[rid] = (toks, blocks, computed + self._sched.get(rid, 0))
+        out.finished_req_ids = list(self._lite.finished_req_ids)
+        return out
+
+
+class ConnectorLeader:
+    """Scheduler-side connector bound to a runtime; sized from the workers' layouts."""
+
+    def __init__(self, runtime: KvbmRuntime, block_size: int, consolidator_endpoints=None):
+        self.runtime, self.block_size = runtime, block_size
+        self.consolidator_endpoints = consolidator_endpoints
+        self._workers: dict[int, tuple[int, str]] = {}
+        self._impl: _Leader | None = None
+
+    def register_worker(self, rank: int, instance_id: int, address: str) -> None:
+        self.runtime.register_peer(instance_id, address)
+        self._workers[rank] = (instance_id, address)
+
+    def initialize_workers(self, layout: dict | None = None) -> None:
+        """Query one worker's layout (or use ``layout``) and build the G2/G3 pools."""
+        if layout is None:
+            if not self._workers:
+                raise RuntimeError("no workers registered")
+            iid, _ = self._workers[min(self._workers)]
+            layout = self.runtime.messenger.call(iid, LAYOUT_HANDLER)
+        cfg = self.runtime.config
+        g2n = max(1, int(layout.get("g2_blocks", 0)))
+        g3n = int(layout.get("g3_blocks", 0))
+        g2 = BlockManager(g2n, self.block_size, cfg.cache.inactive_backend, Tier.G2,
+                          duplicate_policy=cfg.cache.duplicate_policy)
+        g3 = BlockManager(g3n, self.block_size, cfg.cache.inactive_backend, Tier.G3,
+                          registry=g2.registry) if g3n else None
+        self._impl = _Leader(InstanceLeader(g2, ParallelWorkers([]), g3=g3), self.block_size,
+                             offload_enabled=layout.get("g2_blocks", 0) > 0)
+
+    def _need(self) -> _Leader:
+        if self._impl is None:
+            raise RuntimeError("ConnectorLeader not initialized: call initialize_workers()")
+        return self._impl
+
+    def create_slot(self, request: KvbmRequest) -> None:
+        self._need().create_slot(request)
+
+    def has_slot(self, request_id: str) -> bool:
+        return self._impl is not None and self._impl.has_slot(request_id)
+
+    def get_num_new_matched_tokens(self, request_id: str, num_computed_tokens: int):
+        return self._need().get_num_new_matched_tokens(request_id, num_computed_tokens)
+
+    def update_state_after_alloc(self, request_id: str, block_ids: list[int], num_external_tokens: int) -> None:
+        self._need().update_state_after_alloc(request_id, block_ids, num_external_tokens)
+
+    def build_connector_metadata(self, output: SchedulerOutput | SchedulerOutputLite) -> bytes:
+        lite = output.lite() if isinstance(output, SchedulerOutput) else output
+        return self._need().build_connector_meta(lite)
+
+    def update_connector_output(self, finished_sending=None, finished_recving=None) -> None:
+        self._need().update_connector_output(finished_sending, finished_recving)
+
+    def request_finished(self, request_id: str):
+        return self._need().request_finished(request_id)
+
+
+class ConnectorWorker:
+    """Worker-side connector bound to a runtime; serves its layout to the leader."""
+
+    def __init__(self, runtime: KvbmRuntime, block_size: int = 16, num_kv_heads: int | None = None,
+                 head_size: int | None = None, rank: int = 0):
+        from .connector.worker import ConnectorWorker as _Worker
+
+        self.runtime = runtime
+        self._impl = _Worker(runtime.config, rank=rank, block_size=block_size, num_kv_heads=num_kv_heads,
+                             head_size=head_size)
+        runtime.messenger.register_handler(LAYOUT_HANDLER, lambda _p: self._impl.handshake_metadata())
+
+    def __getattr__(self, name):
+        return getattr(self._impl, name)
+
+
+hub = types.ModuleType("kvbm_b200._core.hub")
+hub.PrefillRouterHandler = _hub_client.PrefillRouterHandler
+hub.CompletionEvent = _hub_client.CompletionEvent
+
+__all__ = ["KvbmRuntime", "ConnectorLeader", "ConnectorWorker", "KvbmRequest", "SchedulerOutput", "Tensor",
+           "KvbmVllmConfig", "is_available", "hub", "__version__"]

@@ -271,10 +271,12 @@ class KvLayout:
         if len(tensors) != config.num_layers:
             raise ValueError("one tensor per layer expected")
         _, bs, os_, ts, hs, _ = cls._strides(config, "layer_separate", block_layout, block_first)
-        base = tensors[0].data_ptr()
+        # per-layer allocations may sit in any address order: offsets are taken
+        # from the lowest one so they are never negative
+        base = min(t.data_ptr() for t in tensors)
         offsets = [t.data_ptr() - base for t in tensors]
-        lay = cls(config, "layer_separate", block_layout, base, offsets, bs, os_, ts, hs,
-                  max(offsets) + tensors[-1].numel() * tensors[-1].element_size(),
+        end = max(t.data_ptr() + t.numel() * t.element_size() for t in tensors)
+        lay = cls(config, "layer_separate", block_layout, base, offsets, bs, os_, ts, hs, end - base,
                   "device" if tensors[0].is_cuda else "pinned",
                   tensors[0].device.index if tensors[0].is_cuda else None, tensors)
         lay._block_first = block_first
