@@ -502,3 +502,111 @@ extern "C" int kvbm_paged_decode_attn(const void* q, const void* k_base, const v
                                                                             static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }
+
+// ===========================================================================
+// Allocation-free paged decode attention.
+//
+// This entry point is an addition of this library; the reference block
+// manager has no counterpart to it.
+//
+// kvbm_paged_decode_attn_noalloc returns exactly what kvbm_paged_decode_attn
+// returns, but it takes no scratch buffers: the per-split partial results it
+// needs live in one fixed array in device global memory that belongs to this
+// library (kNoAllocMaxRows rows of 130 floats, about 4.3 MB). Every GPU that
+// loads the library holds that array until the process exits.
+//
+// Who needs it: callers that cannot allocate device memory when they call in.
+// For example, a host application that owns all device memory through its own
+// arena and does not allow other components to call cudaMalloc; code that runs
+// inside an allocator's callback, where allocating again would re-enter (or
+// deadlock) that allocator; or a latency-critical path that cannot afford the
+// device-wide synchronization cudaMalloc and cudaFree may perform. The caller
+// still provides q, the KV pool, the block table, the sequence lengths and the
+// output buffer.
+//
+// Set-up: the first call on each device, made while that device is current,
+// looks up the array's device address with cudaGetSymbolAddress and caches
+// it (the array's name in host code is only a host-side stand-in, never a
+// device address). Make that first call before any stream capture starts.
+// After set-up a call performs no allocation and calls no allocating routine.
+//
+// Limit: batch * hq * splits must not exceed kNoAllocMaxRows; a larger request
+// is rejected with cudaErrorInvalidValue, and kvbm_last_error_message() says
+// why.
+//
+// Sharing: all calls on one device use the same array, which still holds the
+// previous call's partials. Nothing has to be cleared first, because each
+// call's split kernel writes every partial row its combine kernel reads. Two
+// calls whose kernels can overlap on the GPU (different streams with no
+// ordering between them) race on the array and give wrong results: order them
+// on one stream or with events.
+// ===========================================================================
+
+#include <cstdio>
+#include <mutex>
+
+namespace {
+
+constexpr int kNoAllocMaxRows = 8192;
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMaxRows * (kHD + 2)];
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+thread_local char g_last_error[256] = "";
+
+}  // namespace
+
+extern "C" const char* kvbm_last_error_message(void) { return g_last_error; }
+
+extern "C" int kvbm_paged_decode_attn_noalloc_max_rows(void) { return kNoAllocMaxRows; }
+
+extern "C" int kvbm_paged_decode_attn_noalloc(const void* q, const void* k_base, const void* v_base,
+                                              int64_t block_stride, int64_t token_stride, int64_t head_stride,
+                                              int page, const int32_t* block_table, int max_blocks,
+                                              const int32_t* seq_lens, int batch, int hq, int hkv, int hd,
+                                              float softmax_scale, int splits, void* out, cudaStream_t stream) {
+  g_last_error[0] = '\0';
+  if (batch < 0 || hq < 0 || splits <= 0) {
+    std::snprintf(g_last_error, sizeof(g_last_error), "kvbm_paged_decode_attn_noalloc: invalid batch/hq/splits");
+    return cudaErrorInvalidValue;
+  }
+  const int64_t rows = static_cast<int64_t>(batch) * hq * splits;
+  if (rows > kNoAllocMaxRows) {
+    std::snprintf(g_last_error, sizeof(g_last_error),
+                  "kvbm_paged_decode_attn_noalloc: batch*hq*splits = %lld exceeds the static scratch capacity of %d "
+                  "rows; use fewer splits or kvbm_paged_decode_attn with caller-provided scratch",
+                  static_cast<long long>(rows), kNoAllocMaxRows);
+    return cudaErrorInvalidValue;
+  }
+  if (hd != kHD) {
+    std::snprintf(g_last_error, sizeof(g_last_error), "kvbm_paged_decode_attn_noalloc: head_dim must be %d", kHD);
+    return cudaErrorInvalidValue;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) {
+    std::snprintf(g_last_error, sizeof(g_last_error), "kvbm_paged_decode_attn_noalloc: device %d unsupported", dev);
+    return cudaErrorInvalidDevice;
+  }
+  float* base = nullptr;
+  {
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess) {
+        std::snprintf(g_last_error, sizeof(g_last_error),
+                      "kvbm_paged_decode_attn_noalloc: cudaGetSymbolAddress failed (%s)", cudaGetErrorString(e));
+        return e;
+      }
+      g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    base = g_noalloc_ptr[dev];
+  }
+  float* part_acc = base;
+  float* part_ml = base + rows * kHD;
+  return kvbm_paged_decode_attn(q, k_base, v_base, block_stride, token_stride, head_stride, page, block_table,
+                                max_blocks, seq_lens, batch, hq, hkv, hd, softmax_scale, splits, part_acc, part_ml,
+                                out, stream);
+}
