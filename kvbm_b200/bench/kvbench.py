@@ -74,7 +74,8 @@ def run(args) -> list[dict]:
         "lw": lambda loc: KvLayout.allocate(cfg, "layer_separate", nhd, location=loc),
     }
     results = []
-    for g1_kind in args.layouts.split(","):
+    sections = set(args.sections.split(","))
+    for g1_kind in (args.layouts.split(",") if "g12" in sections else []):
         g1 = layouts[g1_kind]("device")
         g2 = KvLayout.allocate(cfg, "fully_contiguous", nhd, location="pinned")
         g1._flat().random_(0, 256)
@@ -98,6 +99,8 @@ def run(args) -> list[dict]:
                     results.append(r)
                     print(json.dumps(r), flush=True)
         del g1, g2
+    if "d2d" not in sections:
+        return results
     # device-local transform (HND <- NHD) and copy, HBM bound
     a = KvLayout.allocate(cfg, "fully_contiguous", nhd)
     a._flat().random_(0, 256)
@@ -110,7 +113,9 @@ def run(args) -> list[dict]:
         "g1_to_g1_universal": KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.UNIVERSAL),
     }
     for name, b in dsts.items():
-        for engine in ("tile", "tma"):
+        if args.d2d and name not in args.d2d.split(","):
+            continue
+        for engine in [e for e in ("tile", "tma") if e in args.engines.split(",")]:
             ms = _time(lambda: kv_ops.kv_transfer(a, s_ids, b, d_ids, engine=engine), args.iters, args.warmup,
                        flush)
             nbytes = n * cfg.bytes_per_block
@@ -118,7 +123,7 @@ def run(args) -> list[dict]:
                  "ms": round(ms, 4), "gbps_rw": round(2 * nbytes / ms / 1e6, 2)}
             results.append(r)
             print(json.dumps(r), flush=True)
-        if name == "g1_to_g1_copy":
+        if name == "g1_to_g1_copy" and "ce" in args.engines.split(","):
             src_p = [a.layer_base(0) + int(x) * a.block_stride for x in s_ids.tolist()]
             dst_p = [b.layer_base(0) + int(x) * b.block_stride for x in d_ids.tolist()]
             sp = torch.tensor(src_p, dtype=torch.int64, device="cuda")
@@ -149,6 +154,8 @@ def main(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--max-ctas", type=int, default=0)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--sections", default="g12,d2d", help="g12 (G1<->G2), d2d (on-device transforms)")
+    p.add_argument("--d2d", default="", help="subset of d2d cases (comma list); empty = all")
     p.add_argument("--out", default=None)
     args = p.parse_args(argv)
     res = run(args)
