@@ -1,0 +1,174 @@
+"""Heterogeneous-TP prefill -> decode KV transfer with KV-head resharding
+(and optional fp8 e4m3 quantisation in flight).
+
+World of W ranks (W >= 4, even): ranks [0, W/2) form one prefill instance
+with TP = W/2; ranks [W/2, W) form two decode instances with TP = W/4 each.
+Requests alternate between the decode instances. Every prefill rank pushes
+the KV heads it owns straight into the decode ranks that own them (head
+offsets from ``parallel.tp.plan_push``) with the fused NVLink kernel - one
+launch per (request, destination rank), all layers. With ``--fp8`` the
+decode pools hold e4m3 KV with one fp32 scale per (block, layer, K/V, head)
+and the kernel quantises while storing.
+
+Geometry: Llama-3-70B KV (80 layers, 8 KV heads, head_dim 128, 16-token
+blocks); prompt lengths log-uniform in [4096, 32768] (seeded).
+Device time with CUDA events, max over prefill ranks; a sampled check on the
+decode side verifies every head landed at the right place.
+
+    torchrun --nproc-per-node 8 -m kvbm_b200.bench.reshard_bench [--fp8]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import random
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+from ..ops import kv_ops
+from ..parallel.tp import ParallelismTemplate, plan_push
+from ..physical.layout import KvBlockLayout, KvLayout, LayoutConfig, LayoutDescriptor
+
+PEER_COPY_GBPS = 770.0
+
+
+def head_value(global_head: int) -> float:
+    return 0.25 * (global_head + 1)
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--layers", type=int, default=80)
+    p.add_argument("--heads", type=int, default=8)
+    p.add_argument("--requests", type=int, default=8)
+    p.add_argument("--min-len", type=int, default=4096)
+    p.add_argument("--max-len", type=int, default=32768)
+    p.add_argument("--fp8", action="store_true")
+    p.add_argument("--engine", default="tile")
+    p.add_argument("--warmup", type=int, default=1)
+    p.add_argument("--out", default=None)
+    a = p.parse_args(argv)
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    assert world >= 4 and world % 4 == 0, "needs 4 or 8 ranks"
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    gloo = dist.new_group(backend="gloo")
+    ptp, dtp = world // 2, world // 4
+    P = ParallelismTemplate(ptp, a.heads, a.layers)
+    D = ParallelismTemplate(dtp, a.heads, a.layers)
+    rng = random.Random(11)
+    lens = [int(math.exp(rng.uniform(math.log(a.min_len), math.log(a.max_len)))) // 16 * 16
+            for _ in range(a.requests)]
+    blocks = [n // 16 for n in lens]
+    is_prefill = rank < ptp
+    page, hd = 16, 128
+    if is_prefill:
+        heads = P.heads_per_rank
+        nb = max(blocks) + 1
+        cfg = LayoutConfig.for_model(nb, a.layers, heads, hd, page, torch.bfloat16)
+        pool = KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.OPERATIONAL_NHD)
+        for l in range(a.layers):
+            v = pool.layer_view(l)
+            for h in range(heads):
+                v[:, :, :, h].fill_(head_value(rank * heads + h))
+        desc = None
+    else:
+        heads = D.heads_per_rank
+        inst, drank = divmod(rank - ptp, dtp)
+        mine = [i for i in range(a.requests) if i % 2 == inst]
+        nb = sum(blocks[i] for i in mine) + 1
+        dt = torch.float8_e4m3fn if a.fp8 else torch.bfloat16
+        cfg = LayoutConfig.for_model(nb, a.layers, heads, hd, page, dt)
+        pool = KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.OPERATIONAL_HND, fp8_scales=a.fp8,
+                                 zero=True)
+        desc = pool.descriptor().to_dict()
+    descs = [None] * world
+    dist.all_gather_object(descs, desc, group=gloo)
+    # destination block ids: each decode instance packs its requests back to back
+    dst_ids = {}
+    for inst in range(2):
+        off = 0
+        for i in range(a.requests):
+            if i % 2 == inst:
+                dst_ids[i] = list(range(off, off + blocks[i]))
+                off += blocks[i]
+    results = {}
+    if is_prefill:
+        remote = {r: KvLayout.from_descriptor(LayoutDescriptor.from_dict(descs[r])) for r in range(ptp, world)}
+        targets = plan_push(P, D)[rank]
+        dev = torch.device("cuda", local)
+        src = {i: torch.arange(blocks[i], dtype=torch.int32, device=dev) for i in range(a.requests)}
+        dst = {i: torch.tensor(dst_ids[i], dtype=torch.int32, device=dev) for i in range(a.requests)}
+        stream = torch.cuda.Stream(priority=-100)
+
+        def run_all():
+            for i in range(a.requests):
+                inst = i % 2
+                for t in targets:
+                    r = ptp + inst * dtp + t.dst_rank
+                    kv_ops.kv_transfer(pool, src[i], remote[r], dst[i], src_head_offset=t.src_head_offset,
+                                       dst_head_offset=t.dst_head_offset, num_heads=t.num_heads, engine=a.engine,
+                                       stream=stream)
+
+        for _ in range(a.warmup):
+            run_all()
+        stream.synchronize()
+        dist.barrier(group=gloo)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        run_all()
+        e.record(stream)
+        e.synchronize()
+        ms = s.elapsed_time(e)
+        src_bytes = sum(blocks) * cfg.bytes_per_block  # this rank's shard of every request
+        results = {"rank": rank, "ms": ms, "src_bytes": src_bytes}
+    else:
+        dist.barrier(group=gloo)
+    dist.barrier(group=gloo)
+    torch.cuda.synchronize()
+    ok = True
+    if not is_prefill:
+        inst, drank = divmod(rank - ptp, dtp)
+        for i in [i for i in range(a.requests) if i % 2 == inst][:2]:
+            b = dst_ids[i][len(dst_ids[i]) // 2]
+            data = pool.gather_blocks([b])  # [1, L, O, T, H, D]
+            if a.fp8:
+                sc = pool.scales_view()[b]  # [L, O, H]
+                vals = data.view(torch.float8_e4m3fn).float() * sc[None, :, :, None, :, None]
+            else:
+                vals = data.float()
+            for h in range(heads):
+                want = head_value(drank * heads + h)
+                got = vals[..., h, :]
+                ok &= bool(torch.allclose(got, torch.full_like(got, want), rtol=0.07 if a.fp8 else 0))
+        results = {"rank": rank, "check_ok": ok}
+    allr = [None] * world
+    dist.all_gather_object(allr, results, group=gloo)
+    if rank == 0:
+        pre = [r for r in allr if "ms" in r]
+        ms = max(r["ms"] for r in pre)
+        src_bytes = sum(r["src_bytes"] for r in pre)
+        wire = src_bytes // 2 if a.fp8 else src_bytes
+        line = {"bench": "reshard_p2d", "world": world, "prefill_tp": ptp, "decode_tp": dtp,
+                "decode_instances": 2, "kv_dtype": "fp8_e4m3" if a.fp8 else "bf16", "layers": a.layers,
+                "requests": a.requests, "tokens": sum(lens), "ms": round(ms, 3),
+                "src_gbps": round(src_bytes / ms / 1e6, 1), "wire_gbps": round(wire / ms / 1e6, 1),
+                "per_prefill_rank_wire_gbps": round(wire / ptp / ms / 1e6, 1),
+                "frac_of_peer_copy": round(wire / ptp / ms / 1e6 / PEER_COPY_GBPS, 3),
+                "check_ok": all(r.get("check_ok", True) for r in allr)}
+        print(json.dumps(line), flush=True)
+        if a.out:
+            with open(a.out, "a") as f:
+                f.write(json.dumps(line) + "\n")
+    dist.barrier(group=gloo)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,123 @@
+"""CPU tests: consolidator service over ZeroMQ, G4 object store, conditional
+disaggregation policy, KV dimension probing, the ``kvbm._core`` surface."""
+
+import time
+
+import msgpack
+import numpy as np
+import pytest
+import zmq
+
+from kvbm_b200.connector.dim_probe import KvDim, derive_block_layout, infer_from_shape, probe_kv_dim_layout
+from kvbm_b200.consolidator.service import Consolidator, source_id
+from kvbm_b200.engine.cd import ConditionalDisagg, Decision, InflightBudget, RemotePrefillParams, SelectionPolicy
+from kvbm_b200.logical.sequence import sequence_hashes
+from kvbm_b200.object.store import FsObjectStore
+from kvbm_b200.physical.layout import KvBlockLayout
+from kvbm_b200.utils.metrics import CdMetrics
+
+
+def _vllm_batch(events):
+    return msgpack.packb([time.time(), events, None], use_bin_type=True)
+
+
+def test_consolidator_dedups_engine_and_kvbm_sources():
+    c = Consolidator("tcp://127.0.0.1:0", block_size=4)
+    sub = zmq.Context.instance().socket(zmq.SUB)
+    sub.setsockopt(zmq.SUBSCRIBE, b"")
+    sub.connect(c.endpoint)
+    time.sleep(0.2)
+    stored = {"type": "BlockStored", "block_hashes": [111, 222], "parent_block_hash": None,
+              "token_ids": list(range(8)), "block_size": 4}
+    c.ingest_engine_batch(_vllm_batch([stored]), "vllm")
+    c.ingest_engine_batch(_vllm_batch([stored]), "trtllm")  # second source: no new STORE
+    out = c.flush()
+    assert [e["type"] for e in out] == ["BlockStored", "BlockStored"]
+    assert out[1]["parent_block_hash"] == out[0]["block_hashes"][0]
+    # the wire message reached the subscriber
+    assert sub.poll(2000)
+    topic, payload = sub.recv_multipart()
+    ts, events, dp = msgpack.unpackb(payload, raw=False)
+    assert len(events) == 2 and events[0]["block_size"] == 4
+    c.ingest_engine_batch(_vllm_batch([{"type": "BlockRemoved", "block_hashes": [111, 222]}]), "vllm")
+    assert c.flush() == []  # trtllm still holds them
+    c.ingest_engine_batch(_vllm_batch([["BlockRemoved", [111, 222], None]]), "trtllm")
+    assert [e["type"] for e in c.flush()] == ["BlockRemoved", "BlockRemoved"]
+    c.ingest_engine_batch(b"\xc1not-msgpack", "vllm")
+    assert c.stats["bad_batches"] == 1
+    c.ingest_engine_batch(_vllm_batch([{"type": "AllBlocksCleared"}]), "vllm")
+    assert c.flush()[-1]["type"] == "AllBlocksCleared"
+    with pytest.raises(ValueError):
+        source_id("gpu2")
+    sub.close(0)
+    c.close()
+
+
+def test_object_store_put_get_lock(tmp_path):
+    s = FsObjectStore(str(tmp_path))
+    h = sequence_hashes(list(range(16)), 16)[0]
+    k = s.key(h, rank=1)
+    assert not s.has(k) and s.get(k) is None
+    assert s.try_lock(k) and not s.try_lock(k)
+    buf = np.arange(4096, dtype=np.uint8)
+    [f.result() for f in s.put_blocks([k], [buf.ctypes.data], 4096)]
+    assert s.has(k) and s.try_lock(k)  # put released the lock
+    out = np.zeros_like(buf)
+    assert s.get_blocks([k, k + "x"], [out.ctypes.data, out.ctypes.data], 4096) == [True, False]
+    assert (out == buf).all()
+    s.close()
+
+
+def test_conditional_disagg_policy_budget_and_breaker():
+    assert SelectionPolicy("threshold", 100).decide(1000, computed=850, connector=100) == Decision.LOCAL
+    assert SelectionPolicy("threshold", 100).decide(1000, computed=500) == Decision.REMOTE
+    m = CdMetrics()
+    cd = ConditionalDisagg(SelectionPolicy("always"), InflightBudget(2), metrics=m)
+    assert cd.decide(100) == Decision.REMOTE and cd.decide(100) == Decision.REMOTE
+    assert cd.decide(100) == Decision.LOCAL  # budget exhausted
+    cd.finish_remote()
+    cd.breaker_tier = 2
+    assert cd.decide(100) == Decision.LOCAL  # hot breaker forces local
+    cd.breaker_tier = 1
+    assert cd.decide(100) == Decision.LOCAL  # warm halves the budget (1 in flight already)
+    assert m.decisions["remote"] == 2
+    p = RemotePrefillParams(initiator_instance_id="7", num_provided_tokens=64)
+    assert RemotePrefillParams.from_dict(p.to_dict()) == p
+
+
+def test_dim_probe_labels_common_backends():
+    flash = probe_kv_dim_layout(lambda nb, bs, h, d: (2, nb, bs, h, d))
+    assert flash == [KvDim.OUTER, KvDim.BLOCK, KvDim.PAGE, KvDim.HEAD, KvDim.HEAD_SIZE]
+    dl = derive_block_layout(flash)
+    assert not dl.block_first and dl.inner == KvBlockLayout.OPERATIONAL_NHD
+    finfer = probe_kv_dim_layout(lambda nb, bs, h, d: (nb, 2, h, bs, d))
+    dl = derive_block_layout(finfer)
+    assert dl.block_first and dl.inner == KvBlockLayout.OPERATIONAL_HND
+    assert infer_from_shape((2, 100, 16, 8, 128), 100, 16, 8, 128)[0] == KvDim.OUTER
+    assert infer_from_shape((100, 32, 2, 16, 8, 128), 100, 16, 8, 128, num_layers=32)[:3] == [
+        KvDim.BLOCK, KvDim.LAYER, KvDim.OUTER]
+
+
+def test_core_surface_leader_from_layout():
+    import kvbm._core as kc
+    from kvbm_b200.connector.protocol import ConnectorMetadata
+
+    rt = kc.KvbmRuntime.build_leader('{"cache": {"host": {"num_blocks": 32}}}')
+    try:
+        iid, addr = rt.peer_info()
+        assert len(rt.instance_id()) == 16 and addr.startswith("tcp://")
+        leader = kc.ConnectorLeader(rt, 16)
+        with pytest.raises(RuntimeError):
+            leader.get_num_new_matched_tokens("x", 0)
+        leader.initialize_workers(layout={"g2_blocks": 32, "g3_blocks": 0})
+        leader.create_slot(kc.KvbmRequest("r", list(range(48))))
+        assert leader.get_num_new_matched_tokens("r", 0) == (0, False)
+        leader.update_state_after_alloc("r", [4, 5, 6], 0)
+        so = kc.SchedulerOutput(1)
+        so.add_new_request("r", list(range(48)), [], 0)
+        so.add_num_scheduled_tokens({"r": 48})
+        meta = ConnectorMetadata.decode(leader.build_connector_metadata(so))
+        assert meta.offload[0].g1_ids == [4, 5, 6]
+        assert kc.hub.CompletionEvent is not None
+    finally:
+        rt.shutdown()
