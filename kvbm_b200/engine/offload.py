@@ -35,6 +35,7 @@ from typing import Callable, Sequence
 
 from ..logical.manager import BlockManager, ImmutableBlock, Tier
 from ..utils.config import PipelineConfig
+from ..utils.tracing import audit, nvtx_range
 
 
 @dataclass
@@ -229,7 +230,8 @@ class OffloadPipeline:
                 if h.state == OffloadState.CANCELLED:
                     self.stats["cancelled"] += len(h.items)
                 else:
-                    kept = self.policy.filter(h.items)
+                    with nvtx_range(f"kvbm.offload.{self.name}.policy"):
+                        kept = self.policy.filter(h.items)
                     h.skipped = [i.seq_hash for i in h.items if i not in kept]
                     self.stats["filtered"] += len(h.items) - len(kept)
                     if not self._await_precondition(h):
@@ -265,7 +267,8 @@ class OffloadPipeline:
         for s in range(0, len(batch), self.cfg.max_batch):
             chunk = batch[s: s + self.cfg.max_batch]
             try:
-                reg = self.executor([i for _, i in chunk])
+                with nvtx_range(f"kvbm.offload.{self.name}.transfer"):
+                    reg = self.executor([i for _, i in chunk])
                 self.stats["batches"] += 1
                 if reg is not None:
                     for (h, _), r in zip(chunk, reg):
@@ -275,6 +278,7 @@ class OffloadPipeline:
                     ok[id(h)] = False
                     h.error = e
         for h, items in live:
+            audit("offload_batch", pipeline=self.name, blocks=len(items), ok=ok[id(h)])
             with h._lock:
                 if ok[id(h)]:
                     h.registered = [r for r in results[id(h)] if r is not None]

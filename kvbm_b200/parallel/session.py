@@ -28,6 +28,8 @@ import time
 import uuid
 from dataclasses import dataclass, field
 
+from ..utils.tracing import audit
+
 
 class Lifecycle(str, enum.Enum):
     OPEN = "open"
@@ -148,6 +150,7 @@ class Session:
             self._cv.notify_all()
 
     def close(self, reason: str) -> None:
+        audit("session_close", session=self.session_id, reason=reason)
         with self._cv:
             if self.lifecycle not in (Lifecycle.FINISHED,):
                 self.failure = reason

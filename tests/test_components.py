@@ -121,3 +121,50 @@ def test_core_surface_leader_from_layout():
         assert kc.hub.CompletionEvent is not None
     finally:
         rt.shutdown()
+
+
+def test_host_memory_service_over_grpc(tmp_path):
+    from kvbm_b200.service.client import KvbmServiceClient, ServiceError
+    from kvbm_b200.service.server import serve
+
+    sock = str(tmp_path / "kvbm.sock")
+    server, svc = serve(sock, directory=str(tmp_path))
+    try:
+        a = KvbmServiceClient(sock)
+        b = KvbmServiceClient(sock)
+        assert a.health()["status"] == "ok"
+        pa = a.create_pool("g2", 8, 4096)
+        ids = a.allocate("g2", 3)
+        assert ids == [0, 1, 2] and a.allocate("g2", 6) is None
+        pa.block(ids[1])[:4] = b"kvbm"
+        h = sequence_hashes(list(range(16)), 16)[0]
+        a.register("g2", [h], [ids[1]])
+        pb = b.create_pool("g2", 8, 4096)  # a second process maps the same pool
+        [slot] = b.lookup("g2", [h])
+        assert slot == ids[1] and bytes(pb.block(slot)[:4]) == b"kvbm"
+        assert b.free("g2", ids) == 8 and b.lookup("g2", [h]) == [-1]
+        with pytest.raises(ServiceError):
+            b.allocate("nope", 1)
+        assert a.stats()["g2"]["free"] == 8
+        pa.close()
+        pb.close()
+    finally:
+        server.stop(0)
+        svc.close()
+
+
+def test_events_manager_batches_to_sinks():
+    from kvbm_b200.logical.events import EventsManager
+    from kvbm_b200.logical.manager import BlockManager, Tier
+
+    em = EventsManager(instance_id=9, policy="all", window_ms=5)
+    got = []
+    em.add_sink(lambda iid, batches: got.append((iid, batches)))
+    mgr = BlockManager(8, 16, "lru", Tier.G2, registry=em.registry())
+    blocks = mgr.allocate_blocks(3)
+    imm = mgr.register_mutable(blocks, sequence_hashes(list(range(48)), 16))
+    em.start()
+    time.sleep(0.1)
+    em.stop()
+    assert got and got[0][0] == 9 and got[0][1][0][0] == "create" and len(got[0][1][0][1]) == 3
+    del imm
