@@ -13,8 +13,12 @@ then decoded together for ``gen_len`` tokens. Weights are random-init bf16.
 
 Reported (rank 0, one JSON line):
   value   aggregate P->D KV transfer GB/s: KV bytes moved by all pairs over
-          the summed device time of the transfer kernels (max over prefill
-          ranks), CUDA events on the transfer stream.
+          the summed device time of the kernels that move them (max over
+          prefill ranks), CUDA events around each kernel. With the default
+          ``--engine fused`` that kernel is the per-layer RoPE + KV write,
+          which stores the layer's K/V straight into the decode pool (its
+          time includes the RoPE of the query heads); with ``tma``/``tile``
+          it is a separate copy kernel per layer on a side stream.
   ttft_p50_ms  p50 over requests of the device time from the wave start to
           the request's KV + first token landing in the decode pool.
   e2e     the same KV bytes over the whole step, timed per rank from before
@@ -53,7 +57,8 @@ def main(argv=None) -> int:
     p.add_argument("--concurrency", type=int, default=32)
     p.add_argument("--prompt-len", type=int, default=8192)
     p.add_argument("--gen-len", type=int, default=256)
-    p.add_argument("--engine", default="tma", choices=["tma", "tile"])
+    p.add_argument("--engine", default="fused", choices=["fused", "tma", "tile"],
+                   help="fused: the RoPE/KV kernel stores into the decode pool; tma/tile: a copy kernel per layer")
     p.add_argument("--max-ctas", type=int, default=0)
     p.add_argument("--layers", type=int, default=None, help="override layer count (debug only: invalid for the metric)")
     p.add_argument("--no-graphs", action="store_true")

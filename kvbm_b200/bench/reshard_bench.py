@@ -6,7 +6,10 @@ with TP = W/2; ranks [W/2, W) form two decode instances with TP = W/4 each.
 Requests alternate between the decode instances. Every prefill rank pushes
 the KV heads it owns straight into the decode ranks that own them (head
 offsets from ``parallel.tp.plan_push``) with the fused NVLink kernel - one
-launch per (request, destination rank), all layers. With ``--fp8`` the
+launch per (request, destination rank), all layers. Each destination
+instance gets its own stream and half of the SMs, so a prefill rank feeds
+both decode instances at once and no decode GPU's inbound link is shared
+by every sender at the same time. With ``--fp8`` the
 decode pools hold e4m3 KV with one fp32 scale per (block, layer, K/V, head)
 and the kernel quantises while storing.
 
@@ -49,7 +52,8 @@ def main(argv=None):
     p.add_argument("--min-len", type=int, default=4096)
     p.add_argument("--max-len", type=int, default=32768)
     p.add_argument("--fp8", action="store_true")
-    p.add_argument("--engine", default="tile")
+    p.add_argument("--engine", default="tma")
+    p.add_argument("--max-ctas", type=int, default=0, help="CTAs per launch (0: SMs / 2)")
     p.add_argument("--warmup", type=int, default=1)
     p.add_argument("--out", default=None)
     a = p.parse_args(argv)
@@ -105,7 +109,8 @@ def main(argv=None):
         dev = torch.device("cuda", local)
         src = {i: torch.arange(blocks[i], dtype=torch.int32, device=dev) for i in range(a.requests)}
         dst = {i: torch.tensor(dst_ids[i], dtype=torch.int32, device=dev) for i in range(a.requests)}
-        stream = torch.cuda.Stream(priority=-100)
+        streams = [torch.cuda.Stream(priority=-100) for _ in range(2)]  # one per decode instance
+        ctas = a.max_ctas or max(1, kv_ops.sm_count() // 2)
 
         def run_all():
             for i in range(a.requests):
@@ -114,16 +119,24 @@ def main(argv=None):
                     r = ptp + inst * dtp + t.dst_rank
                     kv_ops.kv_transfer(pool, src[i], remote[r], dst[i], src_head_offset=t.src_head_offset,
                                        dst_head_offset=t.dst_head_offset, num_heads=t.num_heads, engine=a.engine,
-                                       stream=stream)
+                                       max_ctas=ctas, stream=streams[inst])
 
         for _ in range(a.warmup):
             run_all()
-        stream.synchronize()
+        for st in streams:
+            st.synchronize()
         dist.barrier(group=gloo)
+        main_stream = torch.cuda.current_stream()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
+        s.record(main_stream)
+        for st in streams:
+            st.wait_event(s)
         run_all()
-        e.record(stream)
+        for st in streams:
+            done = torch.cuda.Event()
+            done.record(st)
+            main_stream.wait_event(done)
+        e.record(main_stream)
         e.synchronize()
         ms = s.elapsed_time(e)
         src_bytes = sum(blocks) * cfg.bytes_per_block  # this rank's shard of every request

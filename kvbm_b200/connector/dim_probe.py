@@ -15,22 +15,13 @@ probe_kv_dim_layout :90, derive_block_layout :198, build_dim_layout_from_tensor
 
 from __future__ import annotations
 
-import enum
 from dataclasses import dataclass
 from typing import Callable, Sequence
 
 import torch
 
+from ..common.tensor import KvDim
 from ..physical.layout import KvBlockLayout, KvLayout, LayoutConfig
-
-
-class KvDim(str, enum.Enum):
-    BLOCK = "block"
-    LAYER = "layer"
-    OUTER = "outer"
-    PAGE = "page"
-    HEAD = "head_count"
-    HEAD_SIZE = "head_size"
 
 
 # pairwise-distinct primes, none equal to 1 or 2 (2 is the K/V outer size)
@@ -93,7 +84,10 @@ def infer_from_shape(shape: Sequence[int], num_blocks: int, block_size: int, num
     pref = [KvDim.BLOCK, KvDim.LAYER, KvDim.PAGE, KvDim.HEAD]
     used = {KvDim.HEAD_SIZE}
     for i, d in enumerate(shape[:-1]):
-        if d == 2 and KvDim.OUTER not in used and (i == 0 or labels[i - 1] in (KvDim.BLOCK, KvDim.LAYER)):
+        layer_here = (sizes.get(KvDim.LAYER) == d and KvDim.LAYER not in used and i > 0
+                      and labels[i - 1] == KvDim.BLOCK)  # cross-layer caches are [blocks, layers, ...]
+        if (d == 2 and not layer_here and KvDim.OUTER not in used
+                and (i == 0 or labels[i - 1] in (KvDim.BLOCK, KvDim.LAYER))):
             labels[i] = KvDim.OUTER
             used.add(KvDim.OUTER)
             continue

@@ -453,7 +453,67 @@ int prepare(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape
   return kind;
 }
 
+// ---- checksums ---------------------------------------------------------------
+// splitmix64 finalizer (Steele, Lea, Flood: "Fast splittable pseudorandom
+// number generators", OOPSLA 2014), applied to (word, index) pairs.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+
+__global__ void __launch_bounds__(kThreads) kv_checksum_kernel(const __grid_constant__ XferParams P,
+                                                                unsigned long long* out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerCta;
+  const int wpr = P.src_row_bytes / 4;  // 4-byte words per row
+  const int page = P.shape.page_size, H = P.shape.num_heads, O = P.shape.num_outer;
+  const int n = page * wpr;
+  for (int64_t t = warp; t < P.total_tiles; t += nwarps) {
+    const uint32_t t32 = static_cast<uint32_t>(t);
+    const uint32_t q1 = P.fd_heads.div(t32);
+    const int h = static_cast<int>(P.fd_heads.mod(t32, q1));
+    const uint32_t q2 = P.fd_outer.div(q1);
+    const int64_t o = P.fd_outer.mod(q1, q2);
+    const uint32_t q3 = P.fd_layers.div(q2);
+    const int64_t i = P.fd_layers.mod(q2, q3);
+    const int64_t p = q3;
+    const uint8_t* s = chunk_addr(P.src, p, i, o) + static_cast<int64_t>(h + P.src.head_offset) * P.src.head_stride;
+    uint64_t acc = 0;
+    for (int u = lane; u < n; u += 32) {
+      const int r = P.fd_upr.div(static_cast<uint32_t>(u)), c = P.fd_upr.mod(static_cast<uint32_t>(u), r);
+      const uint32_t wv = *reinterpret_cast<const uint32_t*>(s + r * P.src.token_stride + c * 4);
+      const uint64_t idx = ((static_cast<uint64_t>(i * O + o) * page + r) * H + h) * wpr + c;
+      acc += mix64((idx << 32) ^ wv ^ 0x9e3779b97f4a7c15ull);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) atomicAdd(out + p, static_cast<unsigned long long>(acc));
+  }
+}
+
 }  // namespace
+
+extern "C" int kvbm_kv_checksum(const KvbmSide* side, const KvbmTileShape* shape, uint64_t* out,
+                                cudaStream_t stream) {
+  if (!side || !shape || !out) return cudaErrorInvalidValue;
+  KvbmTileShape S = *shape;
+  S.dst_dtype = S.src_dtype;
+  XferParams P;
+  int unit = 16;
+  if (prepare(side, side, &S, P, &unit) < 0) return cudaErrorInvalidValue;
+  if (P.src_row_bytes % 4 != 0 || P.src.token_stride % 4 != 0 || P.src.head_stride % 4 != 0)
+    return cudaErrorInvalidValue;
+  if (S.num_pairs == 0) return cudaSuccess;
+  cudaError_t e = cudaMemsetAsync(out, 0, sizeof(uint64_t) * S.num_pairs, stream);
+  if (e != cudaSuccess) return e;
+  P.fd_upr = FastDiv(static_cast<uint32_t>(P.src_row_bytes / 4));
+  const int64_t ctas = (P.total_tiles + kWarpsPerCta - 1) / kWarpsPerCta;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas, int64_t{sm_count()} * 8)));
+  kv_checksum_kernel<<<grid, kThreads, 0, stream>>>(P, reinterpret_cast<unsigned long long*>(out));
+  return cudaGetLastError();
+}
 
 extern "C" int kvbm_sm_count(void) { return sm_count(); }
 

@@ -106,6 +106,14 @@ int kvbm_nhd_hnd_transpose(const void* const* src_chunks, void* const* dst_chunk
 int kvbm_signal_flag(uint64_t* flag, uint64_t value, cudaStream_t stream);
 int kvbm_wait_flag(const uint64_t* flag, uint64_t expected, uint64_t timeout_ns, int* status, cudaStream_t stream);
 
+// Layout-independent 64-bit checksum per block: the wrapping sum over every
+// 4-byte word w of the block's selected layers/heads of mix64(w, i), with i
+// the word's index in canonical [layer, outer, token, head, word] order.
+// Blocks holding the same values hash equal whatever their physical layout
+// (NHD / HND, fully contiguous / layer separate / universal). `out` gets
+// shape->num_pairs values; src_dtype gives the element size.
+int kvbm_kv_checksum(const KvbmSide* side, const KvbmTileShape* shape, uint64_t* out, cudaStream_t stream);
+
 // Number of SMs of the current device (cached).
 int kvbm_sm_count(void);
 

@@ -149,6 +149,113 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Fused RoPE + KV write + KV push (head_dim 128).
+//
+// One half-warp per head row: lane l of the half holds elements [8l, 8l+8)
+// (one 16-byte load). Rotate-half RoPE pairs element i with i+64, i.e. lane
+// l with lane l^8 of the same half, exchanged with one shuffle. Q and K rows
+// are rotated in place (the attention that follows reads them from qkv);
+// K and V rows are stored to the local paged cache (``slots``, optional)
+// and to a second paged cache (``rslots``, optional) that may live in a
+// peer GPU's memory: the prefill -> decode KV transfer happens inside the
+// kernel that produces the KV, so the bytes cross NVLink while the rest of
+// the grid is still rotating Q heads, and there is no separate copy kernel
+// competing with the next GEMM for SMs. Work items are token-major, so the
+// peer stores are spread evenly over the whole launch.
+// Parity: the per-layer save path of the reference's connector
+// (crates/kvbm-connector/src/connector/worker/mod.rs, save_kv_layer) fused
+// with the write that produces the layer's KV.
+// ---------------------------------------------------------------------------
+struct RopeKvParams {
+  __nv_bfloat16* qkv;
+  int T, Hq, Hkv;
+  const int32_t* positions;
+  const float* cos_sin;
+  uint8_t* k_base;
+  uint8_t* v_base;
+  int64_t block_stride, token_stride, head_stride;
+  int page;
+  const int64_t* slots;
+  uint8_t* rk_base;
+  uint8_t* rv_base;
+  int64_t r_block_stride, r_token_stride, r_head_stride;
+  int r_page;
+  int r_head_offset;
+  const int64_t* rslots;
+  FastDiv pairs_div;
+  FastDiv page_div;
+  FastDiv r_page_div;
+};
+
+__device__ __forceinline__ uint8_t* cache_row(uint8_t* kb, uint8_t* vb, bool is_k, int kvh, int64_t slot,
+                                              const FastDiv& pd, int64_t bs, int64_t ts, int64_t hs) {
+  const uint32_t blk = pd.div(static_cast<uint32_t>(slot));
+  const uint32_t off = pd.mod(static_cast<uint32_t>(slot), blk);
+  return (is_k ? kb : vb) + static_cast<int64_t>(blk) * bs + static_cast<int64_t>(off) * ts +
+         static_cast<int64_t>(kvh) * hs;
+}
+
+__global__ void __launch_bounds__(256) rope_kv_fused_kernel(const __grid_constant__ RopeKvParams P) {
+  const int lane = threadIdx.x & 31;
+  const int hl = lane & 15;  // lane within the half-warp
+  const int H = P.Hq + 2 * P.Hkv;
+  const uint32_t pairs = static_cast<uint32_t>((H + 1) >> 1);
+  const uint32_t items = static_cast<uint32_t>(P.T) * pairs;
+  const uint32_t stride = gridDim.x * (blockDim.x >> 5);
+  for (uint32_t w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < items; w += stride) {
+    const uint32_t t = P.pairs_div.div(w);
+    const int h = static_cast<int>(P.pairs_div.mod(w, t)) * 2 + (lane >> 4);
+    const bool valid = h < H;
+    __nv_bfloat16* row = P.qkv + (static_cast<int64_t>(t) * H + h) * 128 + hl * 8;
+    int4 x = valid ? *reinterpret_cast<const int4*>(row) : make_int4(0, 0, 0, 0);
+    // partner half of the rotation (lane ^ 8 stays inside the half-warp)
+    int4 p;
+    p.x = __shfl_xor_sync(0xffffffffu, x.x, 8);
+    p.y = __shfl_xor_sync(0xffffffffu, x.y, 8);
+    p.z = __shfl_xor_sync(0xffffffffu, x.z, 8);
+    p.w = __shfl_xor_sync(0xffffffffu, x.w, 8);
+    if (!valid) continue;
+    if (h < P.Hq + P.Hkv) {
+      const float* cs = P.cos_sin + static_cast<int64_t>(P.positions[t]) * 128 + (hl & 7) * 8;
+      const float4 c0 = reinterpret_cast<const float4*>(cs)[0], c1 = reinterpret_cast<const float4*>(cs)[1];
+      const float4 s0 = reinterpret_cast<const float4*>(cs + 64)[0];
+      const float4 s1 = reinterpret_cast<const float4*>(cs + 64)[1];
+      const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      const uint32_t xm[4] = {(uint32_t)x.x, (uint32_t)x.y, (uint32_t)x.z, (uint32_t)x.w};
+      const uint32_t xp[4] = {(uint32_t)p.x, (uint32_t)p.y, (uint32_t)p.z, (uint32_t)p.w};
+      // first half: y = x*c - partner*s ; second half: y = x*c + partner*s
+      const float sign = hl < 8 ? -1.f : 1.f;
+      uint32_t y[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = bf16_lo(xm[j]), b = bf16_hi(xm[j]);
+        const float pa = bf16_lo(xp[j]), pb = bf16_hi(xp[j]);
+        y[j] = pack_bf16(a * c[2 * j] + sign * (pa * s[2 * j]), b * c[2 * j + 1] + sign * (pb * s[2 * j + 1]));
+      }
+      x = make_int4((int)y[0], (int)y[1], (int)y[2], (int)y[3]);
+      *reinterpret_cast<int4*>(row) = x;
+    }
+    if (h >= P.Hq) {
+      const bool is_k = h < P.Hq + P.Hkv;
+      const int kvh = is_k ? h - P.Hq : h - P.Hq - P.Hkv;
+      if (P.slots) {
+        const int64_t slot = P.slots[t];
+        if (slot >= 0)
+          reinterpret_cast<int4*>(cache_row(P.k_base, P.v_base, is_k, kvh, slot, P.page_div, P.block_stride,
+                                            P.token_stride, P.head_stride))[hl] = x;
+      }
+      if (P.rslots) {
+        const int64_t slot = P.rslots[t];
+        if (slot >= 0)
+          reinterpret_cast<int4*>(cache_row(P.rk_base, P.rv_base, is_k, kvh + P.r_head_offset, slot, P.r_page_div,
+                                            P.r_block_stride, P.r_token_stride, P.r_head_stride))[hl] = x;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // out[t, i] = silu(gate_up[t, i]) * gate_up[t, I + i]
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu,
@@ -377,6 +484,30 @@ extern "C" int kvbm_rmsnorm(const void* x, void* residual, const void* weight, v
   return cudaGetLastError();
 }
 
+namespace {
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int launch_rope_fused(RopeKvParams& P, cudaStream_t stream) {
+  const int H = P.Hq + 2 * P.Hkv;
+  const int64_t items = static_cast<int64_t>(P.T) * ((H + 1) / 2);
+  if (items >= (int64_t{1} << 31)) return cudaErrorInvalidValue;
+  P.pairs_div = FastDiv(static_cast<uint32_t>((H + 1) / 2));
+  P.page_div = FastDiv(static_cast<uint32_t>(P.page > 0 ? P.page : 1));
+  P.r_page_div = FastDiv(static_cast<uint32_t>(P.r_page > 0 ? P.r_page : 1));
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t ctas = (items + 7) / 8;
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ctas, int64_t{sms} * 16)));
+  rope_kv_fused_kernel<<<grid, 256, 0, stream>>>(P);
+  return cudaGetLastError();
+}
+
+bool cache_ok(const void* kb, const void* vb, int64_t bs, int64_t ts, int64_t hs, int page) {
+  return kb && vb && page > 0 && aligned16(kb) && aligned16(vb) && bs % 16 == 0 && ts % 16 == 0 && hs % 16 == 0;
+}
+}  // namespace
+
 extern "C" int kvbm_rope_kv_write(void* qkv, int64_t tokens, int hq, int hkv, int hd, const int32_t* positions,
                                   const float* cos_sin, void* k_base, void* v_base, int64_t block_stride,
                                   int64_t token_stride, int64_t head_stride, int page, const int64_t* slots,
@@ -384,6 +515,24 @@ extern "C" int kvbm_rope_kv_write(void* qkv, int64_t tokens, int hq, int hkv, in
   if (tokens == 0) return cudaSuccess;
   if (!qkv || !positions || !cos_sin || hd % 8 != 0) return cudaErrorInvalidValue;
   if (slots && (!k_base || !v_base || page <= 0)) return cudaErrorInvalidValue;
+  if (hd == 128 && aligned16(qkv) && aligned16(cos_sin) &&
+      (!slots || cache_ok(k_base, v_base, block_stride, token_stride, head_stride, page))) {
+    RopeKvParams P{};
+    P.qkv = static_cast<__nv_bfloat16*>(qkv);
+    P.T = static_cast<int>(tokens);
+    P.Hq = hq;
+    P.Hkv = hkv;
+    P.positions = positions;
+    P.cos_sin = cos_sin;
+    P.k_base = static_cast<uint8_t*>(k_base);
+    P.v_base = static_cast<uint8_t*>(v_base);
+    P.block_stride = block_stride;
+    P.token_stride = token_stride;
+    P.head_stride = head_stride;
+    P.page = page;
+    P.slots = slots;
+    return launch_rope_fused(P, stream);
+  }
   const int64_t warps = tokens * (hq + 2 * hkv);
   const unsigned grid = static_cast<unsigned>((warps + 7) / 8);
   rope_kv_write_kernel<<<grid, 256, 0, stream>>>(static_cast<__nv_bfloat16*>(qkv), static_cast<int>(tokens), hq, hkv,
@@ -391,6 +540,45 @@ extern "C" int kvbm_rope_kv_write(void* qkv, int64_t tokens, int hq, int hkv, in
                                                  static_cast<uint8_t*>(v_base), block_stride, token_stride,
                                                  head_stride, page, slots);
   return cudaGetLastError();
+}
+
+// RoPE + KV write into the local cache (optional) and a second cache that
+// may be a peer GPU's (mapped through CUDA IPC or peer access); head_dim 128.
+extern "C" int kvbm_rope_kv_push(void* qkv, int64_t tokens, int hq, int hkv, const int32_t* positions,
+                                 const float* cos_sin, void* k_base, void* v_base, int64_t block_stride,
+                                 int64_t token_stride, int64_t head_stride, int page, const int64_t* slots,
+                                 void* rk_base, void* rv_base, int64_t r_block_stride, int64_t r_token_stride,
+                                 int64_t r_head_stride, int r_page, int r_head_offset, const int64_t* rslots,
+                                 cudaStream_t stream) {
+  if (tokens == 0) return cudaSuccess;
+  if (!qkv || !positions || !cos_sin || !aligned16(qkv) || !aligned16(cos_sin)) return cudaErrorInvalidValue;
+  if (slots && !cache_ok(k_base, v_base, block_stride, token_stride, head_stride, page)) return cudaErrorInvalidValue;
+  if (rslots && !cache_ok(rk_base, rv_base, r_block_stride, r_token_stride, r_head_stride, r_page))
+    return cudaErrorInvalidValue;
+  if (r_head_offset < 0) return cudaErrorInvalidValue;
+  RopeKvParams P{};
+  P.qkv = static_cast<__nv_bfloat16*>(qkv);
+  P.T = static_cast<int>(tokens);
+  P.Hq = hq;
+  P.Hkv = hkv;
+  P.positions = positions;
+  P.cos_sin = cos_sin;
+  P.k_base = static_cast<uint8_t*>(k_base);
+  P.v_base = static_cast<uint8_t*>(v_base);
+  P.block_stride = block_stride;
+  P.token_stride = token_stride;
+  P.head_stride = head_stride;
+  P.page = page;
+  P.slots = slots;
+  P.rk_base = static_cast<uint8_t*>(rk_base);
+  P.rv_base = static_cast<uint8_t*>(rv_base);
+  P.r_block_stride = r_block_stride;
+  P.r_token_stride = r_token_stride;
+  P.r_head_stride = r_head_stride;
+  P.r_page = r_page;
+  P.r_head_offset = r_head_offset;
+  P.rslots = rslots;
+  return launch_rope_fused(P, stream);
 }
 
 extern "C" int kvbm_silu_mul(const void* gate_up, void* out, int64_t tokens, int inter, cudaStream_t stream) {

@@ -29,7 +29,7 @@ import torch
 import torch.distributed as dist
 
 from .. import _core_native as core
-from ..models.llama import LlamaConfig, LlamaModel
+from ..models.llama import KvPush, LlamaConfig, LlamaModel
 from ..ops import llama_ops
 from ..ops import kv_ops
 from ..parallel.pd import WAIT_TIMEOUT_NS, Mailbox, MailboxDescriptor, PdSender
@@ -194,9 +194,14 @@ class PrefillInstance:
                     stream.wait_event(done[r - nbuf])  # staging blocks free once delivered
                 src_ids = self.slot_ids[r % nbuf]
                 dst_ids = dst_table[r, : cfg.prompt_blocks]
-                nxt = self.model.prefill(prompts[r], self.pool, src_ids,
-                                         on_layer_done=lambda l, s=src_ids, d=dst_ids: sender.send_layer(
-                                             l, s, d, after=stream))
+                if sender.engine == "fused":
+                    # the RoPE/KV kernel of every layer stores straight into the decode pool
+                    push = KvPush(sender.remote, dst_ids, timers=sender._timers if sender.timing else None)
+                    nxt = self.model.prefill(prompts[r], self.pool, src_ids, kv_push=push)
+                else:
+                    nxt = self.model.prefill(prompts[r], self.pool, src_ids,
+                                             on_layer_done=lambda l, s=src_ids, d=dst_ids: sender.send_layer(
+                                                 l, s, d, after=stream))
                 self.first_tok[r: r + 1].copy_(nxt)
                 sender.stream.wait_stream(stream)
                 done.append(sender.complete(slot_base + r, seq, payload=self.first_tok[r: r + 1]))

@@ -269,7 +269,7 @@ class HubServer:
             site = web.TCPSite(self._runner, self.host, self.port)
             await site.start()
             self.port = site._server.sockets[0].getsockname()[1]
-            self._loop.create_task(self._sweeper())
+            self._sweep_task = self._loop.create_task(self._sweeper())
             self._started.set()
 
         self._loop.run_until_complete(start())
@@ -294,6 +294,13 @@ class HubServer:
             self._ticker.stop()
         if self._loop is not None:
             async def shutdown():
+                task = getattr(self, "_sweep_task", None)
+                if task is not None:
+                    task.cancel()
+                    try:
+                        await task
+                    except asyncio.CancelledError:
+                        pass
                 await self._runner.cleanup()
             fut = asyncio.run_coroutine_threadsafe(shutdown(), self._loop)
             try:

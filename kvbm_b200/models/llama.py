@@ -66,6 +66,49 @@ class LlamaConfig:
         return self.layers * per_layer + 2 * self.vocab * self.hidden + self.hidden
 
 
+class KvPush:
+    """Destination of the K/V a prefill produces, written by the RoPE/KV kernel itself.
+
+    ``remote`` is the decode instance's pool (mapped through CUDA IPC when it
+    is on another GPU); ``block_ids`` (int32, device) are its blocks for the
+    request, one per ``page`` tokens. With ``timers`` set, each layer's
+    kernel is bracketed by CUDA events and ``(start, end, kv_bytes)`` is
+    appended, so callers can report the device time of the transfer.
+    """
+
+    def __init__(self, remote: KvLayout, block_ids: torch.Tensor, *, start_pos: int = 0, head_offset: int = 0,
+                 local_write: bool = False, timers: list | None = None):
+        if remote.dtype != torch.bfloat16:
+            raise ValueError("the fused push writes bf16 pools; use the transfer kernels for fp8")
+        self.remote, self.block_ids = remote, block_ids
+        self.start_pos, self.head_offset = start_pos, head_offset
+        self.local_write, self.timers = local_write, timers
+        self._slots: torch.Tensor | None = None
+
+    def slots(self, pos: torch.Tensor) -> torch.Tensor:
+        if self._slots is None or self._slots.numel() != pos.numel():
+            page = self.remote.config.page_size
+            p = pos.long()
+            self._slots = self.block_ids.long()[p // page] * page + p % page
+        return self._slots
+
+    def layer(self, model: "LlamaModel", li: int, qkv: torch.Tensor, pos: torch.Tensor, local: tuple) -> None:
+        c = model.cfg
+        r = self.remote
+        rk = r.layer_base(li)
+        remote = (rk, rk + r.outer_stride, r.block_stride, r.token_stride, r.head_stride, r.config.page_size,
+                  self.slots(pos))
+        ev = None
+        if self.timers is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        llama_ops.rope_kv_push(qkv, pos, model.cos_sin, c.heads, c.kv_heads, local if self.local_write else None,
+                               remote, r_head_offset=self.head_offset)
+        if ev is not None:
+            ev[1].record()
+            self.timers.append((ev[0], ev[1], qkv.shape[0] * 2 * c.kv_heads * c.head_dim * 2))
+
+
 class LlamaModel:
     """Weights + forward passes. Not an nn.Module: no autograd, inference only."""
 
@@ -116,13 +159,17 @@ class LlamaModel:
     # ------------------------------------------------------------ prefill
     @torch.inference_mode()
     def prefill(self, tokens: torch.Tensor, pool: KvLayout, block_ids: torch.Tensor, start_pos: int = 0,
-                on_layer_done=None) -> torch.Tensor:
+                on_layer_done=None, kv_push: "KvPush | None" = None) -> torch.Tensor:
         """Prefill ``tokens`` [T] at positions [start_pos, start_pos+T).
 
         K/V land in ``pool`` blocks ``block_ids`` (int32, device; block j holds
         positions [16j, 16j+16) of the sequence). ``on_layer_done(layer)`` is
         called on the host right after layer ``layer``'s K/V writes are enqueued
-        on the current stream. Returns the greedy next token (int64 [1]).
+        on the current stream. With ``kv_push`` the kernel that rotates and
+        writes each layer's K/V also stores it into ``kv_push.remote`` (a
+        decode pool, possibly a peer GPU's), and the local pool write is
+        skipped unless ``kv_push.local_write``. Returns the greedy next token
+        (int64 [1]).
         """
         c = self.cfg
         T = tokens.numel()
@@ -141,8 +188,12 @@ class LlamaModel:
                 llama_ops.rmsnorm(x, L["n1"], c.eps, residual=residual, out=h)
             qkv = F.linear(h, L["wqkv"]).view(T, c.heads + 2 * c.kv_heads, c.head_dim)
             kb, vb = self.kv_bases(pool, li)
-            llama_ops.rope_kv_write(qkv, pos, self.cos_sin, c.heads, c.kv_heads, c.head_dim, kb, vb,
-                                    pool.block_stride, pool.token_stride, pool.head_stride, page, slots)
+            if kv_push is None:
+                llama_ops.rope_kv_write(qkv, pos, self.cos_sin, c.heads, c.kv_heads, c.head_dim, kb, vb,
+                                        pool.block_stride, pool.token_stride, pool.head_stride, page, slots)
+            else:
+                kv_push.layer(self, li, qkv, pos, (kb, vb, pool.block_stride, pool.token_stride, pool.head_stride,
+                                                   page, slots))
             if on_layer_done is not None:
                 on_layer_done(li)
             q = qkv[:, : c.heads].transpose(0, 1).unsqueeze(0)

@@ -82,6 +82,31 @@ def kv_transfer(src, src_ids, dst, dst_ids, *, layer_begin: int = 0, num_layers:
     _lib.count_launches(1)
 
 
+def kv_checksum(layout, ids, *, layer_begin: int = 0, num_layers: int | None = None, head_offset: int = 0,
+                num_heads: int | None = None, stream=None) -> torch.Tensor:
+    """Layout-independent 64-bit checksum of each block in ``ids`` (int64 tensor on the device).
+
+    Two blocks holding the same values hash equal whatever their pools'
+    physical layouts; see ``physical.verify.checksum_reference`` for the
+    definition. Works on device pools and on mapped pinned (G2) pools.
+    """
+    c = layout.config
+    nl = c.num_layers - layer_begin if num_layers is None else num_layers
+    nh = c.num_heads - head_offset if num_heads is None else num_heads
+    dev = torch.device("cuda", torch.cuda.current_device())
+    out = torch.empty(len(ids), dtype=torch.int64, device=dev)
+    if len(ids) == 0:
+        return out
+    sid = _ids(ids, dev)
+    side = layout.side(sid, layer_begin, nl, head_offset)
+    shape = _lib.KvbmTileShape(len(ids), nl, c.outer_dim, nh, c.page_size, c.head_dim, layout.dtype_code,
+                               layout.dtype_code)
+    _lib.check(_lib.load().kvbm_kv_checksum(C.byref(side), C.byref(shape), C.c_void_p(out.data_ptr()),
+                                            _stream(stream)), "kvbm_kv_checksum")
+    _lib.count_launches(1)
+    return out
+
+
 def kv_transfer_sides(src_side, dst_side, shape, *, engine: str = "tile", max_ctas: int = 0, stream=None) -> None:
     """Low-level launch with prebuilt ``KvbmSide`` / ``KvbmTileShape`` structs."""
     lib = _lib.load()

@@ -31,6 +31,27 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
               slots.data_ptr() if slots is not None else None, _stream(stream))
 
 
+def rope_kv_push(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, hq: int, hkv: int,
+                 local: tuple | None, remote: tuple, r_head_offset: int = 0, stream=None) -> None:
+    """RoPE + KV write into ``local`` (optional) and ``remote`` paged caches in one kernel (head_dim 128).
+
+    Each cache is ``(k_base, v_base, block_stride, token_stride, head_stride,
+    page, slots)`` with ``slots`` an int64 [T] tensor of block*page+offset
+    (negative: skip). The remote cache may be a peer GPU's memory; its heads
+    start at ``r_head_offset`` (a decode rank holding more KV heads than this
+    prefill rank).
+    """
+    T = qkv.shape[0]
+    if qkv.shape[-1] != 128:
+        raise ValueError("rope_kv_push needs head_dim 128")
+    lk = local or (0, 0, 0, 0, 0, 0, None)
+    rk, rv, rbs, rts, rhs, rpage, rslots = remote
+    _lib.call("kvbm_rope_kv_push", qkv.data_ptr(), T, hq, hkv, positions.data_ptr(), cos_sin.data_ptr(),
+              lk[0] or None, lk[1] or None, lk[2], lk[3], lk[4], lk[5],
+              lk[6].data_ptr() if lk[6] is not None else None,
+              rk or None, rv or None, rbs, rts, rhs, rpage, r_head_offset, rslots.data_ptr(), _stream(stream))
+
+
 def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     T = gate_up.numel() // gate_up.shape[-1]
     inter = gate_up.shape[-1] // 2

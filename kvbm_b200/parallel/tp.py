@@ -25,6 +25,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass, field
 
+from ..common.tensor import AxisSlice, KvDim, intersect_axis
+
 
 class CompatError(ValueError):
     pass
@@ -91,16 +93,13 @@ def plan_pull(local: ParallelismTemplate, remote: ParallelismTemplate) -> list[W
     L, R, G = local.tp_size, remote.tp_size, local.global_heads
     plans = []
     for i in range(L):
+        mine = AxisSlice.shard(KvDim.HEAD, i, L, G)
         p = WorkerPullPlan(i)
-        if L == R:
-            p.shards.append(Shard(i, 0, 0, G // L))
-        elif L < R:
-            n = R // L
-            for k in range(n):
-                p.shards.append(Shard(i * n + k, 0, k * (G // R), G // R))
-        else:
-            n = L // R
-            p.shards.append(Shard(i // n, (i % n) * (G // L), 0, G // L))
+        # remote ranks whose head windows overlap ours (contiguous run of ranks)
+        for j in range(mine.start * R // G, (mine.end * R + G - 1) // G):
+            inter = intersect_axis(AxisSlice.shard(KvDim.HEAD, j, R, G), mine)
+            if inter is not None:
+                p.shards.append(Shard(j, inter.src_local.start, inter.dst_local.start, len(inter)))
         plans.append(p)
     return plans
 

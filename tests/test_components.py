@@ -96,6 +96,9 @@ def test_dim_probe_labels_common_backends():
     assert infer_from_shape((2, 100, 16, 8, 128), 100, 16, 8, 128)[0] == KvDim.OUTER
     assert infer_from_shape((100, 32, 2, 16, 8, 128), 100, 16, 8, 128, num_layers=32)[:3] == [
         KvDim.BLOCK, KvDim.LAYER, KvDim.OUTER]
+    # two layers, two KV heads: the sizes alone are ambiguous; the cross-layer convention decides
+    assert infer_from_shape((40, 2, 2, 16, 2, 128), 40, 16, 2, 128, num_layers=2) == [
+        KvDim.BLOCK, KvDim.LAYER, KvDim.OUTER, KvDim.PAGE, KvDim.HEAD, KvDim.HEAD_SIZE]
 
 
 def test_core_surface_leader_from_layout():

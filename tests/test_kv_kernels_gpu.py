@@ -237,3 +237,23 @@ def test_flag_signal_wait_and_timeout():
     # the context stays usable
     x = torch.ones(4, device="cuda")
     assert float(x.sum()) == 4.0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float8_e4m3fn])
+def test_checksum_kernel_matches_reference_across_layouts(dtype):
+    from kvbm_b200.physical.verify import FillPattern, checksum_blocks, checksum_reference, fill_blocks
+
+    cfg = LayoutConfig.for_model(10, 3, 4, 128, 16, dtype)
+    a = KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.OPERATIONAL_NHD, zero=True)
+    b = KvLayout.allocate(cfg, "layer_separate", KvBlockLayout.OPERATIONAL_HND, zero=True)
+    h = KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.OPERATIONAL_HND, location="pinned", zero=True)
+    fill_blocks(a, [1, 4, 7], FillPattern.RANDOM, seed=5)
+    kv_ops.kv_transfer(a, [1, 4, 7], b, [0, 2, 9])
+    kv_ops.kv_transfer(a, [1, 4, 7], h, [3, 5, 6])
+    torch.cuda.synchronize()
+    ca = checksum_blocks(a, [1, 4, 7])
+    assert ca == checksum_blocks(b, [0, 2, 9]) == checksum_blocks(h, [3, 5, 6])
+    assert ca == [checksum_reference(x) for x in a.gather_blocks([1, 4, 7])]
+    assert len(set(ca)) == 3
+    sub = checksum_blocks(b, [2], layer_begin=1, num_layers=2)
+    assert sub == [checksum_reference(a.gather_blocks([4])[0, 1:3])]

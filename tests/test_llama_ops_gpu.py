@@ -73,6 +73,58 @@ def test_rope_kv_write_paged():
         assert torch.equal(view[b, 1, o], orig[t, hq + hkv:])
 
 
+@pytest.mark.parametrize("local_write", [False, True])
+def test_rope_kv_push_into_second_pool(local_write):
+    """The fused kernel rotates q/k in place and stores K/V into a second
+    (HND, wider-headed) pool at a head offset, optionally also the local one."""
+    torch.manual_seed(3)
+    T, hq, hkv, hd, page = 70, 32, 4, 128, 16
+    local = KvLayout.allocate(LayoutConfig.for_model(8, 2, hkv, hd, page), "fully_contiguous",
+                              KvBlockLayout.OPERATIONAL_NHD, zero=True)
+    remote = KvLayout.allocate(LayoutConfig.for_model(12, 2, 2 * hkv, hd, page), "fully_contiguous",
+                               KvBlockLayout.OPERATIONAL_HND, zero=True)
+    qkv = torch.randn(T, hq + 2 * hkv, hd, device="cuda", dtype=torch.bfloat16)
+    orig = qkv.clone()
+    pos = torch.arange(7, 7 + T, device="cuda", dtype=torch.int32)
+    cs = _cos_sin(4096, hd)
+    lblocks = torch.tensor([1, 0, 6, 3, 2], device="cuda")
+    rblocks = torch.tensor([10, 4, 0, 7, 11], device="cuda")
+    ar = torch.arange(T, device="cuda")
+    lslots = (lblocks[ar // page] * page + ar % page).long()
+    rslots = (rblocks[ar // page] * page + ar % page).long()
+    rslots[3] = -1  # a skipped token
+    layer = 1
+    lk = local.layer_base(layer)
+    rk = remote.layer_base(layer)
+    llama_ops.rope_kv_push(qkv, pos, cs, hq, hkv,
+                           (lk, lk + local.outer_stride, local.block_stride, local.token_stride, local.head_stride,
+                            page, lslots) if local_write else None,
+                           (rk, rk + remote.outer_stride, remote.block_stride, remote.token_stride,
+                            remote.head_stride, page, rslots), r_head_offset=hkv)
+    torch.cuda.synchronize()
+    q_ref = _rope_ref(orig[:, :hq], pos.long(), cs)
+    k_ref = _rope_ref(orig[:, hq:hq + hkv], pos.long(), cs)
+    torch.testing.assert_close(qkv[:, :hq].float(), q_ref, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(qkv[:, hq:hq + hkv].float(), k_ref, rtol=1e-2, atol=1e-2)
+    assert torch.equal(qkv[:, hq + hkv:], orig[:, hq + hkv:])
+    rv = remote.layer_view(layer)  # [blocks, outer, page, heads, hd] whatever the physical order
+    lv = local.layer_view(layer)
+    for t in range(T):
+        b, o = int(rblocks[t // page]), t % page
+        if t == 3:
+            assert not rv[b, :, o].any()
+        else:
+            assert not rv[b, :, o, :hkv].any()  # heads below the offset untouched
+            assert torch.equal(rv[b, 0, o, hkv:], qkv[t, hq:hq + hkv])
+            assert torch.equal(rv[b, 1, o, hkv:], orig[t, hq + hkv:])
+        lb = int(lblocks[t // page])
+        if local_write:
+            assert torch.equal(lv[lb, 0, o], qkv[t, hq:hq + hkv])
+            assert torch.equal(lv[lb, 1, o], orig[t, hq + hkv:])
+    if not local_write:
+        assert not lv.any()
+
+
 def test_silu_mul():
     torch.manual_seed(2)
     gu = torch.randn(33, 2 * 1024, device="cuda", dtype=torch.bfloat16)

@@ -35,8 +35,9 @@ def test_prefill_decode_matches_reference():
     _check_greedy(model, seq, T)
 
 
-def test_colocated_wave_and_graphs():
-    cfg = DisaggConfig(model=LlamaConfig.tiny(layers=2), concurrency=3, prompt_len=80, gen_len=5)
+@pytest.mark.parametrize("engine", ["fused", "tma"])
+def test_colocated_wave_and_graphs(engine):
+    cfg = DisaggConfig(model=LlamaConfig.tiny(layers=2), concurrency=3, prompt_len=80, gen_len=5, engine=engine)
     server = DisaggServer(cfg, "colocated", 0)
     server.warmup_graphs()
     prompts = torch.randint(0, cfg.model.vocab, (3, 80), dtype=torch.int32).pin_memory()
