@@ -3,9 +3,10 @@
 Every rank serves ``sessions`` chat sessions for ``turns`` turns on its own
 GPU (weak scaling). All sessions share a 2,048-token system prefix; each
 turn appends 256-1,024 uniform-random user tokens, is prefilled, then
-decodes ``gen`` tokens (batched across the turn's sessions). G1 is a paged
-pool with its own prefix cache (the serving framework's, an LRU block
-manager) capped at ``g1_fraction`` of the live KV, so most KV spills: the
+decodes ``gen`` tokens, batched across a wave of sessions (as many as fit
+G1 at once; a turn is several waves). G1 is a paged pool with its own
+prefix cache (the serving framework's, an LRU block manager) capped at
+``g1_fraction`` of the live KV, so most KV spills: the
 connector offloads every completed block G1 -> G2 (pinned host) after the
 forward pass and, on the next turn, onboards the G2 hits back into fresh G1
 blocks with the SM gather kernel before the prefill of the new tokens.
@@ -51,7 +52,11 @@ def run(a, rank: int = 0) -> dict:
     prefix = rng.integers(0, vocab, a.prefix, dtype=np.int32).tolist()
     avg_ctx = a.prefix + a.turns * ((256 + 1024) // 2 + a.gen) // 2
     live_blocks = a.sessions * math.ceil(avg_ctx * 2 / bs)
-    g1_blocks = max(int(live_blocks * a.g1_fraction), 4 * math.ceil((a.prefix + a.turns * (1024 + a.gen)) / bs))
+    max_req_blocks = math.ceil((a.prefix + a.turns * (1024 + a.gen)) / bs)
+    g1_blocks = max(int(live_blocks * a.g1_fraction), 2 * max_req_blocks)
+    # sessions resident at once: a turn is served in waves whose live KV fits G1, so
+    # the prefix-cached blocks of earlier waves get evicted (spilled) by later ones
+    wave = max(1, g1_blocks // max_req_blocks)
     g2_blocks = int(live_blocks * 1.2) + 64
     pool = model.allocate_pool(g1_blocks, bs)
     g1 = BlockManager(g1_blocks, bs, "lru", Tier.G1)  # the framework's own G1 prefix cache
@@ -67,10 +72,11 @@ def run(a, rank: int = 0) -> dict:
     hit_g1 = hit_g2 = total_prompt = prefilled = 0
     step = 0
     bpb = pool.config.bytes_per_block
-    for turn in range(a.turns):
+    waves = [list(range(w, min(a.sessions, w + wave))) for w in range(0, a.sessions, wave)]
+    for turn, members in ((t, m) for t in range(a.turns) for m in waves):
         held: list[list] = []
         tables, lens = [], []
-        for s in range(a.sessions):
+        for s in members:
             hist[s] += rng.integers(0, vocab, int(rng.integers(256, 1025)), dtype=np.int32).tolist()
             toks = hist[s]
             hashes = sequence_hashes(toks, bs)
@@ -121,9 +127,9 @@ def run(a, rank: int = 0) -> dict:
         # batched decode of the turn (eager; contexts differ per session)
         maxb = max(len(t) for t in tables)
         table = torch.tensor([t + [t[-1]] * (maxb - len(t)) for t in tables], dtype=torch.int32, device="cuda")
-        tok = torch.tensor([h[-1] for h in hist], dtype=torch.int64, device="cuda")
+        tok = torch.tensor([hist[s][-1] for s in members], dtype=torch.int64, device="cuda")
         pos = torch.tensor(lens, dtype=torch.int32, device="cuda")
-        splits = llama_ops.decode_splits(a.sessions, cfg.kv_heads, max(lens) + a.gen, bs)
+        splits = llama_ops.decode_splits(len(members), cfg.kv_heads, max(lens) + a.gen, bs)
         gen_out = []
         for _ in range(a.gen - 1):
             nt = model.decode_step(tok, pos, pool, table, pos + 1, splits)
@@ -132,8 +138,8 @@ def run(a, rank: int = 0) -> dict:
             pos = pos + 1
         if gen_out:
             gen = torch.stack(gen_out, 1).tolist()
-            for s in range(a.sessions):
-                hist[s] += gen[s]
+            for k, s in enumerate(members):
+                hist[s] += gen[k]
         for blocks in held:
             for b in blocks:
                 b.release()
@@ -141,7 +147,7 @@ def run(a, rank: int = 0) -> dict:
     ttft.sort()
     return {"rank": rank, "ttft": ttft, "onboard_ms": onboard_ms, "onboard_bytes": onboard_bytes,
             "hit_g1": hit_g1, "hit_g2": hit_g2, "total_prompt": total_prompt, "prefilled": prefilled,
-            "g1_blocks": g1_blocks, "g2_blocks": g2_blocks, "live_blocks_est": live_blocks}
+            "g1_blocks": g1_blocks, "g2_blocks": g2_blocks, "live_blocks_est": live_blocks, "wave": wave}
 
 
 def main(argv=None):

@@ -30,6 +30,7 @@ from ..engine.leader import FindMatchesOptions, InstanceLeader
 from ..logical.manager import ImmutableBlock
 from ..logical.sequence import TokenBlockSequence
 from ..utils.metrics import CacheStatsTracker
+from ..utils.tracing import audit
 from .protocol import ConnectorMetadata, OffloadOp, OnboardOp
 
 
@@ -55,6 +56,8 @@ class RequestSlot:
     save_cursor: int = 0                      # blocks already offloaded (or skipped)
     pending_offload_steps: set[int] = field(default_factory=set)
     finished: bool = False
+    remote_future: object = None              # in-flight remote search + pull (concurrent.futures.Future)
+    remote_done: bool = False
 
 
 @dataclass
@@ -69,8 +72,9 @@ class SchedulerOutputLite:
 
 class ConnectorLeader:
     def __init__(self, leader: InstanceLeader, block_size: int, offload_enabled: bool = True,
-                 decode_offload: bool = False, stats: CacheStatsTracker | None = None):
+                 decode_offload: bool = False, stats: CacheStatsTracker | None = None, remote_search=None):
         self.leader = leader
+        self.remote = remote_search  # engine.remote_search.RemoteSearch, or None
         self.block_size = block_size
         self.offload_enabled = offload_enabled
         self.decode_offload = decode_offload
@@ -106,6 +110,26 @@ class ConnectorLeader:
         blocks = res.g2_blocks
         # the framework must compute at least the last prompt token itself
         max_blocks = (len(slot.request.tokens) - 1 - num_computed_tokens) // self.block_size
+        if self.remote is not None and not slot.remote_done and len(blocks) < max_blocks:
+            # stall the request while another instance's copy of the missing prefix is pulled
+            fut = slot.remote_future
+            if fut is None:
+                slot.remote_future = self.remote.start(hashes[start + len(blocks): start + max_blocks])
+            if not slot.remote_future.done():
+                for b in blocks:
+                    b.release()
+                audit("gnmt_pending", request=req_id)
+                return None, False
+            slot.remote_done = True
+            try:
+                pulled = slot.remote_future.result()
+            except Exception as e:  # noqa: BLE001 - a failed pull falls back to recompute
+                audit("remote_pull_failed", request=req_id, error=str(e))
+                pulled = 0
+            if pulled:
+                for b in blocks:
+                    b.release()
+                blocks = self.leader.find_matches(hashes[start:], FindMatchesOptions()).g2_blocks
         for b in blocks[max(0, max_blocks):]:
             b.release()
         blocks = blocks[: max(0, max_blocks)]
@@ -114,6 +138,8 @@ class ConnectorLeader:
             return 0, False
         slot.matched = blocks
         slot.matched_start_block = start
+        if slot.remote_done:
+            audit("gnmt_matched", request=req_id, matched_tokens=len(blocks) * self.block_size)
         return len(blocks) * self.block_size, True
 
     # ----------------------------------------------------------------- USAA

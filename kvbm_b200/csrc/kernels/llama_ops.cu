@@ -182,74 +182,103 @@ struct RopeKvParams {
   int r_page;
   int r_head_offset;
   const int64_t* rslots;
-  FastDiv pairs_div;
+  int group;          // head pairs per work item
+  FastDiv pairs_div;  // divides by the number of groups per token
   FastDiv page_div;
   FastDiv r_page_div;
 };
 
-__device__ __forceinline__ uint8_t* cache_row(uint8_t* kb, uint8_t* vb, bool is_k, int kvh, int64_t slot,
-                                              const FastDiv& pd, int64_t bs, int64_t ts, int64_t hs) {
+__device__ __forceinline__ uint8_t* cache_base(uint8_t* kb, int64_t slot, const FastDiv& pd, int64_t bs, int64_t ts) {
   const uint32_t blk = pd.div(static_cast<uint32_t>(slot));
   const uint32_t off = pd.mod(static_cast<uint32_t>(slot), blk);
-  return (is_k ? kb : vb) + static_cast<int64_t>(blk) * bs + static_cast<int64_t>(off) * ts +
-         static_cast<int64_t>(kvh) * hs;
+  return kb + static_cast<int64_t>(blk) * bs + static_cast<int64_t>(off) * ts;
 }
+
+// Work item = (token, group of `P.group` head pairs). Head pairs are visited
+// K first, then V, then Q (pair j covers heads (Hq + 2j + {0,1}) mod H), so
+// the KV stores - the ones that may cross NVLink - are issued first. The
+// warp loads the token's cos/sin once and keeps kUnroll pairs of rows in
+// flight per lane.
+constexpr int kRopeUnroll = 4;
 
 __global__ void __launch_bounds__(256) rope_kv_fused_kernel(const __grid_constant__ RopeKvParams P) {
   const int lane = threadIdx.x & 31;
-  const int hl = lane & 15;  // lane within the half-warp
+  const int hl = lane & 15;  // lane within the half-warp: elements [8*hl, 8*hl+8)
+  const int half = lane >> 4;
   const int H = P.Hq + 2 * P.Hkv;
-  const uint32_t pairs = static_cast<uint32_t>((H + 1) >> 1);
-  const uint32_t items = static_cast<uint32_t>(P.T) * pairs;
+  const int pairs = (H + 1) >> 1;
+  const int groups = static_cast<int>(P.pairs_div.d);  // head-pair groups per token
+  const uint32_t items = static_cast<uint32_t>(P.T) * static_cast<uint32_t>(groups);
   const uint32_t stride = gridDim.x * (blockDim.x >> 5);
+  const float sign = hl < 8 ? -1.f : 1.f;
   for (uint32_t w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < items; w += stride) {
     const uint32_t t = P.pairs_div.div(w);
-    const int h = static_cast<int>(P.pairs_div.mod(w, t)) * 2 + (lane >> 4);
-    const bool valid = h < H;
-    __nv_bfloat16* row = P.qkv + (static_cast<int64_t>(t) * H + h) * 128 + hl * 8;
-    int4 x = valid ? *reinterpret_cast<const int4*>(row) : make_int4(0, 0, 0, 0);
-    // partner half of the rotation (lane ^ 8 stays inside the half-warp)
-    int4 p;
-    p.x = __shfl_xor_sync(0xffffffffu, x.x, 8);
-    p.y = __shfl_xor_sync(0xffffffffu, x.y, 8);
-    p.z = __shfl_xor_sync(0xffffffffu, x.z, 8);
-    p.w = __shfl_xor_sync(0xffffffffu, x.w, 8);
-    if (!valid) continue;
-    if (h < P.Hq + P.Hkv) {
-      const float* cs = P.cos_sin + static_cast<int64_t>(P.positions[t]) * 128 + (hl & 7) * 8;
-      const float4 c0 = reinterpret_cast<const float4*>(cs)[0], c1 = reinterpret_cast<const float4*>(cs)[1];
-      const float4 s0 = reinterpret_cast<const float4*>(cs + 64)[0];
-      const float4 s1 = reinterpret_cast<const float4*>(cs + 64)[1];
-      const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-      const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-      const uint32_t xm[4] = {(uint32_t)x.x, (uint32_t)x.y, (uint32_t)x.z, (uint32_t)x.w};
-      const uint32_t xp[4] = {(uint32_t)p.x, (uint32_t)p.y, (uint32_t)p.z, (uint32_t)p.w};
-      // first half: y = x*c - partner*s ; second half: y = x*c + partner*s
-      const float sign = hl < 8 ? -1.f : 1.f;
-      uint32_t y[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float a = bf16_lo(xm[j]), b = bf16_hi(xm[j]);
-        const float pa = bf16_lo(xp[j]), pb = bf16_hi(xp[j]);
-        y[j] = pack_bf16(a * c[2 * j] + sign * (pa * s[2 * j]), b * c[2 * j + 1] + sign * (pb * s[2 * j + 1]));
-      }
-      x = make_int4((int)y[0], (int)y[1], (int)y[2], (int)y[3]);
-      *reinterpret_cast<int4*>(row) = x;
+    const int g = static_cast<int>(P.pairs_div.mod(w, t));
+    const int j_begin = g * P.group, j_end = min(pairs, j_begin + P.group);
+    // per-token state: rotation table row and cache row bases
+    const float* cs = P.cos_sin + static_cast<int64_t>(P.positions[t]) * 128 + (hl & 7) * 8;
+    const float4 c0 = reinterpret_cast<const float4*>(cs)[0], c1 = reinterpret_cast<const float4*>(cs)[1];
+    const float4 s0 = reinterpret_cast<const float4*>(cs + 64)[0];
+    const float4 s1 = reinterpret_cast<const float4*>(cs + 64)[1];
+    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sn[8] = {sign * s0.x, sign * s0.y, sign * s0.z, sign * s0.w,
+                         sign * s1.x, sign * s1.y, sign * s1.z, sign * s1.w};
+    uint8_t* lrow = nullptr;
+    uint8_t* rrow = nullptr;
+    if (P.slots) {
+      const int64_t slot = P.slots[t];
+      if (slot >= 0) lrow = cache_base(P.k_base, slot, P.page_div, P.block_stride, P.token_stride);
     }
-    if (h >= P.Hq) {
-      const bool is_k = h < P.Hq + P.Hkv;
-      const int kvh = is_k ? h - P.Hq : h - P.Hq - P.Hkv;
-      if (P.slots) {
-        const int64_t slot = P.slots[t];
-        if (slot >= 0)
-          reinterpret_cast<int4*>(cache_row(P.k_base, P.v_base, is_k, kvh, slot, P.page_div, P.block_stride,
-                                            P.token_stride, P.head_stride))[hl] = x;
+    if (P.rslots) {
+      const int64_t slot = P.rslots[t];
+      if (slot >= 0) rrow = cache_base(P.rk_base, slot, P.r_page_div, P.r_block_stride, P.r_token_stride);
+    }
+    __nv_bfloat16* trow = P.qkv + static_cast<int64_t>(t) * H * 128 + hl * 8;
+    for (int j0 = j_begin; j0 < j_end; j0 += kRopeUnroll) {
+      int4 x[kRopeUnroll];
+      int hh[kRopeUnroll];
+#pragma unroll
+      for (int u = 0; u < kRopeUnroll; ++u) {
+        const int hp = 2 * (j0 + u) + half;  // position in K,V,Q order
+        const bool valid = (j0 + u) < j_end && hp < H;
+        int h = hp + P.Hq;
+        if (h >= H) h -= H;
+        hh[u] = valid ? h : -1;
+        x[u] = valid ? *reinterpret_cast<const int4*>(trow + static_cast<int64_t>(h) * 128) : make_int4(0, 0, 0, 0);
       }
-      if (P.rslots) {
-        const int64_t slot = P.rslots[t];
-        if (slot >= 0)
-          reinterpret_cast<int4*>(cache_row(P.rk_base, P.rv_base, is_k, kvh + P.r_head_offset, slot, P.r_page_div,
-                                            P.r_block_stride, P.r_token_stride, P.r_head_stride))[hl] = x;
+#pragma unroll
+      for (int u = 0; u < kRopeUnroll; ++u) {
+        int4 p;  // rotation partner: lane ^ 8 of the same half-warp
+        p.x = __shfl_xor_sync(0xffffffffu, x[u].x, 8);
+        p.y = __shfl_xor_sync(0xffffffffu, x[u].y, 8);
+        p.z = __shfl_xor_sync(0xffffffffu, x[u].z, 8);
+        p.w = __shfl_xor_sync(0xffffffffu, x[u].w, 8);
+        const int h = hh[u];
+        if (h < 0) continue;
+        __nv_bfloat16* row = trow + static_cast<int64_t>(h) * 128;
+        if (h < P.Hq + P.Hkv) {
+          const uint32_t xm[4] = {(uint32_t)x[u].x, (uint32_t)x[u].y, (uint32_t)x[u].z, (uint32_t)x[u].w};
+          const uint32_t xp[4] = {(uint32_t)p.x, (uint32_t)p.y, (uint32_t)p.z, (uint32_t)p.w};
+          uint32_t y[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            // first half: x*c - partner*s ; second half: x*c + partner*s (sign folded into sn)
+            y[k] = pack_bf16(bf16_lo(xm[k]) * c[2 * k] + bf16_lo(xp[k]) * sn[2 * k],
+                             bf16_hi(xm[k]) * c[2 * k + 1] + bf16_hi(xp[k]) * sn[2 * k + 1]);
+          }
+          x[u] = make_int4((int)y[0], (int)y[1], (int)y[2], (int)y[3]);
+          *reinterpret_cast<int4*>(row) = x[u];
+        }
+        if (h >= P.Hq) {
+          const bool is_k = h < P.Hq + P.Hkv;
+          const int kvh = is_k ? h - P.Hq : h - P.Hq - P.Hkv;
+          if (lrow)
+            reinterpret_cast<int4*>(lrow + (is_k ? 0 : P.v_base - P.k_base) +
+                                    static_cast<int64_t>(kvh) * P.head_stride)[hl] = x[u];
+          if (rrow)
+            reinterpret_cast<int4*>(rrow + (is_k ? 0 : P.rv_base - P.rk_base) +
+                                    static_cast<int64_t>(kvh + P.r_head_offset) * P.r_head_stride)[hl] = x[u];
+        }
       }
     }
   }
@@ -489,16 +518,25 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 int launch_rope_fused(RopeKvParams& P, cudaStream_t stream) {
   const int H = P.Hq + 2 * P.Hkv;
-  const int64_t items = static_cast<int64_t>(P.T) * ((H + 1) / 2);
-  if (items >= (int64_t{1} << 31)) return cudaErrorInvalidValue;
-  P.pairs_div = FastDiv(static_cast<uint32_t>((H + 1) / 2));
-  P.page_div = FastDiv(static_cast<uint32_t>(P.page > 0 ? P.page : 1));
-  P.r_page_div = FastDiv(static_cast<uint32_t>(P.r_page > 0 ? P.r_page : 1));
+  const int pairs = (H + 1) / 2;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // whole tokens per warp when there are enough tokens to fill the GPU,
+  // otherwise split each token's heads over several warps (decode)
+  const int groups_max = (pairs + kRopeUnroll - 1) / kRopeUnroll;
+  int groups = 1;
+  while (groups < groups_max && static_cast<int64_t>(P.T) * groups < int64_t{sms} * 64) groups *= 2;
+  groups = std::min(groups, groups_max);
+  P.group = (pairs + groups - 1) / groups;
+  groups = (pairs + P.group - 1) / P.group;
+  const int64_t items = static_cast<int64_t>(P.T) * groups;
+  if (items >= (int64_t{1} << 31)) return cudaErrorInvalidValue;
+  P.pairs_div = FastDiv(static_cast<uint32_t>(groups));
+  P.page_div = FastDiv(static_cast<uint32_t>(P.page > 0 ? P.page : 1));
+  P.r_page_div = FastDiv(static_cast<uint32_t>(P.r_page > 0 ? P.r_page : 1));
   const int64_t ctas = (items + 7) / 8;
-  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ctas, int64_t{sms} * 16)));
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ctas, int64_t{sms} * 32)));
   rope_kv_fused_kernel<<<grid, 256, 0, stream>>>(P);
   return cudaGetLastError();
 }

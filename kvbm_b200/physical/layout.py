@@ -29,7 +29,7 @@ from dataclasses import asdict, dataclass, field
 import torch
 
 from ..ops import _lib
-from .memory import DeviceBuffer, PeerBuffer, PinnedBuffer
+from .memory import DeviceBuffer, PeerBuffer, PinnedBuffer, SharedHostBuffer, SharedPinnedBuffer
 
 DTYPE_CODE = {
     torch.float16: _lib.F16,
@@ -222,7 +222,10 @@ class KvLayout:
     def allocate(cls, config: LayoutConfig, kind: str = "fully_contiguous",
                  block_layout: KvBlockLayout = KvBlockLayout.OPERATIONAL_NHD, location: str = "device",
                  block_first: bool = True, fp8_scales: bool = False, device: int | None = None,
-                 zero: bool = False) -> "KvLayout":
+                 zero: bool = False, shm_name: str | None = None) -> "KvLayout":
+        """Allocate a pool. ``location``: ``device`` (HBM), ``pinned`` (page-locked
+        host memory mapped for the GPU) or ``shared`` (a named ``/dev/shm`` file
+        other processes on the node can map; page-locked when CUDA is present)."""
         layer_off, bs, os_, ts, hs, data_bytes = cls._strides(config, kind, block_layout, block_first)
         scales_offset = None
         total = data_bytes
@@ -239,8 +242,18 @@ class KvLayout:
                 buf.tensor().zero_()
             base = buf.device_ptr
             dev = None
+        elif location == "shared":
+            import os
+            import uuid
+
+            name = shm_name or f"kvbm_g2_{os.getpid()}_{uuid.uuid4().hex[:8]}"
+            buf = SharedPinnedBuffer(name, total) if torch.cuda.is_available() else SharedHostBuffer(name, total)
+            # a new file reads as zeros
+            base = getattr(buf, "device_ptr", buf.ptr)
+            dev = None
+            location = "pinned"
         else:
-            raise ValueError("location must be 'device' or 'pinned'")
+            raise ValueError("location must be 'device', 'pinned' or 'shared'")
         lay = cls(config, kind, block_layout, base, layer_off, bs, os_, ts, hs, total, location, dev, buf,
                   scales_offset)
         lay._block_first = block_first
@@ -377,7 +390,7 @@ class KvLayout:
             if self.location == "device":
                 t = torch.as_tensor(_RawDev(self.base_ptr, self.nbytes), device=f"cuda:{self.device}")
             elif self.location == "pinned":
-                if isinstance(self.backing, PinnedBuffer):
+                if isinstance(self.backing, (PinnedBuffer, SharedHostBuffer)):
                     t = self.backing.tensor()
                 else:
                     t = self.backing.view(torch.uint8).reshape(-1)

@@ -148,14 +148,10 @@ class ExportedPool:
     rank: int = 0
 
 
-class SharedPinnedBuffer:
-    """A G2 pool in a named shared-memory file, page-locked and mapped into the
-    device address space of every process that opens it.
-
-    Any process on the node can map another instance's G2 pool by name, so a
-    copy kernel can read a peer's pinned blocks directly (cross-instance
-    prefix reuse without an intermediate hop). Hugepage-backed files
-    (``/dev/hugepages``) work the same way.
+class SharedHostBuffer:
+    """A named shared-memory file (``/dev/shm`` or a hugepage mount) mapped
+    into this process. Another process on the node maps the same pool by
+    path; :class:`SharedPinnedBuffer` additionally page-locks it for the GPU.
     """
 
     def __init__(self, name: str, nbytes: int, create: bool = True, directory: str = "/dev/shm"):
@@ -176,10 +172,6 @@ class SharedPinnedBuffer:
         buf = (C.c_uint8 * self.nbytes).from_buffer(self._mm)
         self.ptr = C.addressof(buf)
         del buf
-        _lib.check(_lib.load().kvbm_host_register(self.ptr, self.nbytes), "cudaHostRegister")
-        d = C.c_void_p()
-        _lib.check(_lib.load().kvbm_host_device_pointer(self.ptr, C.byref(d)), "cudaHostGetDevicePointer")
-        self.device_ptr = int(d.value or 0)
 
     def tensor(self, dtype: torch.dtype = torch.uint8, shape: tuple | None = None) -> torch.Tensor:
         arr = (C.c_uint8 * self.nbytes).from_address(self.ptr)
@@ -188,11 +180,14 @@ class SharedPinnedBuffer:
             t = t.view(dtype)
         return t.view(shape) if shape is not None else t
 
+    def _release(self) -> None:
+        pass
+
     def close(self) -> None:
         import os
 
         if self.ptr:
-            _lib.load().kvbm_host_unregister(self.ptr)
+            self._release()
             self.ptr = 0
             try:
                 self._mm.close()
@@ -209,3 +204,24 @@ class SharedPinnedBuffer:
             self.close()
         except Exception:
             pass
+
+
+class SharedPinnedBuffer(SharedHostBuffer):
+    """A G2 pool in a named shared-memory file, page-locked and mapped into the
+    device address space of every process that opens it.
+
+    Any process on the node can map another instance's G2 pool by name, so a
+    copy kernel can read a peer's pinned blocks directly (cross-instance
+    prefix reuse without an intermediate hop). Hugepage-backed files
+    (``/dev/hugepages``) work the same way.
+    """
+
+    def __init__(self, name: str, nbytes: int, create: bool = True, directory: str = "/dev/shm"):
+        super().__init__(name, nbytes, create, directory)
+        _lib.check(_lib.load().kvbm_host_register(self.ptr, self.nbytes), "cudaHostRegister")
+        d = C.c_void_p()
+        _lib.check(_lib.load().kvbm_host_device_pointer(self.ptr, C.byref(d)), "cudaHostGetDevicePointer")
+        self.device_ptr = int(d.value or 0)
+
+    def _release(self) -> None:
+        _lib.load().kvbm_host_unregister(self.ptr)

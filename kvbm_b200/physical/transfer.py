@@ -225,6 +225,7 @@ class TransferManager:
         self._io = cf.ThreadPoolExecutor(max_workers=io_threads, thread_name_prefix="kvbm-io")
         self._bounce: PhysicalLayout | None = None
         self._plan_cache: dict[tuple, str] = {}
+        self._bench = None  # StartupBenchmark, created by calibrate() when caps.startup_benchmark is on
         self.stats = {"transfers": 0, "bytes": 0, "failures": 0}
 
     # ------------------------------------------------------------ registry
@@ -333,7 +334,19 @@ class TransferManager:
                 and same_geometry and src.block_stride == a.bytes_per_block and dst.block_stride == b.bytes_per_block)
         if same:
             return "pairs"
+        if self.caps.startup_benchmark and self._bench is not None:
+            best = self._bench.lookup(src, dst)
+            if best is not None:
+                return best
         return "tma"
+
+    def calibrate(self, src_handle: int, dst_handle: int) -> str:
+        """Run (or load from the cache) the startup benchmark for a layout pair; returns the chosen engine."""
+        from .verify import StartupBenchmark
+
+        if self._bench is None:
+            self._bench = StartupBenchmark()
+        return self._bench.run(self, src_handle, dst_handle)
 
     def _direct(self, src: PhysicalLayout, s_ids, dst: PhysicalLayout, d_ids, strat: TransferStrategy,
                 opts: TransferOptions) -> TransferCompleteNotification:

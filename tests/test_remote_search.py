@@ -1,0 +1,106 @@
+"""Remote search on CPU: instance B finds instance A's prefix through the hub
+indexer, pulls it from A's shared-memory G2 pool (or over the messenger),
+and the connector stalls the request until the blocks are local."""
+
+import time
+
+import pytest
+import torch
+
+from kvbm_b200.connector.leader import ConnectorLeader, KvbmRequest
+from kvbm_b200.engine.leader import InstanceLeader, ParallelWorkers
+from kvbm_b200.engine.remote_search import RemoteHolder, RemoteSearch, RemoteSearchConfig
+from kvbm_b200.hub.client import HubClient
+from kvbm_b200.hub.server import HubServer
+from kvbm_b200.logical.manager import BlockManager, Tier
+from kvbm_b200.logical.sequence import sequence_hashes
+from kvbm_b200.physical.layout import KvBlockLayout, KvLayout, LayoutConfig
+from kvbm_b200.physical.verify import FillPattern, checksum_blocks, fill_blocks
+from kvbm_b200.runtime.messenger import Messenger
+
+BS = 16
+
+
+class _Instance:
+    def __init__(self, iid, hub, block_layout, shared=True):
+        self.iid = iid
+        self.g2 = BlockManager(32, BS, "lru", Tier.G2)
+        self.leader = InstanceLeader(self.g2, ParallelWorkers([]), instance_id=iid)
+        cfg = LayoutConfig.for_model(32, 2, 2, 64, BS)
+        self.layout = KvLayout.allocate(cfg, "fully_contiguous", block_layout, location="shared")
+        self.msg = Messenger(iid)
+        # shared=False: the pool is exported without its file (as across nodes)
+        self.holder = RemoteHolder(self.leader, [self.layout], self.msg, shareable=shared)
+        hub.register(iid, features=["indexer", "p2p"], address=self.msg.address)
+
+    def close(self):
+        self.msg.close()
+        self.layout.backing.close()
+
+
+@pytest.fixture
+def hub():
+    h = HubServer(max_seq_len=4096).start()
+    yield h
+    h.stop()
+
+
+@pytest.mark.parametrize("shared", [True, False])
+def test_cold_instance_pulls_prefix_from_holder(hub, shared):
+    c = HubClient(hub.url)
+    a = _Instance(101, c, KvBlockLayout.OPERATIONAL_NHD, shared=shared)
+    b = _Instance(202, c, KvBlockLayout.OPERATIONAL_HND)
+    try:
+        tokens = list(range(1000, 1000 + 6 * BS + 5))
+        hashes = sequence_hashes(tokens, BS)
+        # A computed the prompt: 6 full blocks in its G2, announced to the indexer
+        blocks = a.g2.allocate_blocks(6)
+        fill_blocks(a.layout, [x.block_id for x in blocks], FillPattern.RANDOM, seed=9)
+        imm = a.g2.register_mutable(blocks, hashes[:6])
+        want = checksum_blocks(a.layout, [x.block_id for x in imm])
+        for x in imm:
+            x.release()
+        c.publish_events(a.iid, [("create", hashes[:6])])
+
+        rs = RemoteSearch(b.leader, [b.layout], b.msg, c, BS, RemoteSearchConfig(enabled=True))
+        conn = ConnectorLeader(b.leader, BS, remote_search=rs)
+        conn.create_slot(KvbmRequest("r1", tokens))
+        assert conn.get_num_new_matched_tokens("r1", 0) == (None, False)  # stalled on the pull
+        conn.slots["r1"].remote_future.result(timeout=10)
+        n, async_load = conn.get_num_new_matched_tokens("r1", 0)
+        assert (n, async_load) == (6 * BS, True)
+        got = checksum_blocks(b.layout, [x.block_id for x in conn.slots["r1"].matched])
+        assert got == want  # same bytes, NHD on A, HND on B
+        assert rs.stats["pulled_blocks"] == 6 and (rs.stats["rpc_reads"] == 0) == shared
+        assert a.holder.open_sessions() == 0 and len(a.holder.sessions) == 0
+        # A's blocks were released by the session close: all 32 allocatable again
+        assert a.g2.allocate_blocks(32) is not None
+
+        # a second request on B is a plain local hit (no new search)
+        conn.create_slot(KvbmRequest("r2", tokens))
+        assert conn.get_num_new_matched_tokens("r2", 0) == (6 * BS, True)
+        assert rs.stats["searches"] == 1
+        rs.close()
+    finally:
+        a.close()
+        b.close()
+
+
+def test_warm_and_unknown_prefixes_skip_or_miss(hub):
+    c = HubClient(hub.url)
+    a = _Instance(303, c, KvBlockLayout.OPERATIONAL_NHD)
+    try:
+        rs = RemoteSearch(a.leader, [a.layout], a.msg, c, BS, RemoteSearchConfig(enabled=True,
+                                                                                   min_remote_tokens=3 * BS))
+        hashes = sequence_hashes(list(range(5 * BS)), BS)
+        # only this instance holds the prefix: the self filter leaves no holder
+        c.publish_events(a.iid, [("create", hashes[:2])])
+        assert rs.search(hashes) is None
+        assert rs.search(sequence_hashes(list(range(7, 7 + 5 * BS)), BS)) is None
+        # decimated query over a long prompt still finds the deepest probed block
+        long_h = sequence_hashes(list(range(200 * BS)), BS)
+        rs.config.max_query_hashes = 16
+        assert len(rs._query_set(long_h)) <= 17 and rs._query_set(long_h)[-1] == long_h[-1]
+        rs.close()
+    finally:
+        a.close()
