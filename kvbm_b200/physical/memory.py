@@ -169,6 +169,10 @@ class SharedHostBuffer:
         finally:
             os.close(fd)
         self.owner = create
+        if create:
+            from ..utils import disk_cleanup
+
+            disk_cleanup.register(self.path)  # unlinked if the process is told to stop
         buf = (C.c_uint8 * self.nbytes).from_buffer(self._mm)
         self.ptr = C.addressof(buf)
         del buf
@@ -194,6 +198,9 @@ class SharedHostBuffer:
             except BufferError:
                 pass
             if self.owner:
+                from ..utils import disk_cleanup
+
+                disk_cleanup.deregister(self.path)
                 try:
                     os.unlink(self.path)
                 except FileNotFoundError:

@@ -134,6 +134,21 @@ class DisaggSettings:
 
 
 @dataclass
+class RemoteSearchSettings:
+    enabled: bool = False
+    min_remote_tokens: int | None = None   # None: any remote match (one block)
+    max_query_hashes: int = 64
+    timeout_secs: float = 10.0
+
+
+@dataclass
+class MessengerConfig:
+    bind: str = "tcp://127.0.0.1:0"        # ZeroMQ endpoint of this instance's RPC server
+    discovery: str = "hub"                 # hub | static
+    peers: dict = field(default_factory=dict)  # static discovery: instance id -> address
+
+
+@dataclass
 class TransferConfig:
     engine: str = "auto"               # auto | tile | tma | pairs | ce
     max_ctas: int = 0
@@ -155,6 +170,8 @@ class KvbmConfig:
     hub: HubConfig | None = None
     disagg: DisaggSettings | None = None
     transfer: TransferConfig = field(default_factory=TransferConfig)
+    remote_search: RemoteSearchSettings = field(default_factory=RemoteSearchSettings)
+    messenger: MessengerConfig = field(default_factory=MessengerConfig)
     max_seq_len: int | None = None
     block_layout: str = "operational"   # operational | universal
     block_size: int = 16
@@ -240,6 +257,9 @@ SHORT_ENV = {
     "KVBM_TRANSFER_ENGINE": "transfer.engine",
     "KVBM_HUB_URL": "hub.url",
     "KVBM_MAX_SEQ_LEN": "max_seq_len",
+    "KVBM_REMOTE_SEARCH_ENABLED": "remote_search.enabled",
+    "KVBM_REMOTE_SEARCH_MIN_REMOTE_TOKENS": "remote_search.min_remote_tokens",
+    "KVBM_MESSENGER_BIND": "messenger.bind",
 }
 
 
@@ -327,7 +347,8 @@ def _build(cls, data: dict):
 def _dataclass_of(tp):
     names = {c.__name__: c for c in (HostCacheConfig, DiskCacheConfig, CacheConfig, PipelineConfig, OffloadConfig,
                                      OnboardConfig, ObjectConfig, EventsConfig, MetricsConfig, DebugConfig,
-                                     HubConfig, DisaggSettings, TransferConfig)}
+                                     HubConfig, DisaggSettings, TransferConfig, RemoteSearchSettings,
+                                     MessengerConfig)}
     s = tp if isinstance(tp, str) else getattr(tp, "__name__", str(tp))
     for name, c in names.items():
         if name in s.replace("None", "").replace("|", " ").split():

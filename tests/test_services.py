@@ -142,6 +142,10 @@ def test_config_layering(tmp_path):
         KvbmConfig.load({"block_layout": "weird"}, env={}, system_toml=None)
     with pytest.raises(ValueError):
         KvbmConfig.load({"nonsense": 1}, env={}, system_toml=None)
+    c = KvbmConfig.load({"leader": {"remote_search": {"enabled": True, "min_remote_tokens": 64}}}, role="leader",
+                        env={"KVBM_MESSENGER_BIND": "tcp://0.0.0.0:5555"}, system_toml=None)
+    assert c.remote_search.enabled and c.remote_search.min_remote_tokens == 64
+    assert c.messenger.bind == "tcp://0.0.0.0:5555" and c.messenger.discovery == "hub"
 
 
 def test_offload_pipeline_policies_batching_cancel():
