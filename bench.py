@@ -195,6 +195,7 @@ def main(argv=None) -> int:
                 "gen_len": cfg.gen_len,
                 "parallelism": "colocated" if world == 1 else f"{pairs}P{pairs}D tp1",
                 "engine": cfg.engine,
+                "prefill_attention": server.model.attention_backend,
                 "l2": "inputs larger than L2 (1 GiB KV per request, 16 GB weights)",
             },
             "impl": "kvbm_b200",

@@ -35,6 +35,64 @@ from ..physical.layout import KvBlockLayout, KvLayout, LayoutConfig, LayoutDescr
 PEER_COPY_GBPS = 770.0
 
 
+def gloo_of(args):
+    return args._gloo
+
+
+def rope_push_section(args, rank, local, remote, cfg, pool_blocks, timed, rng) -> list[dict]:
+    """One prefill's worth of layers (``--blocks`` x 16 tokens, 32 query / ``--heads`` KV heads):
+    the RoPE/KV kernel stores every layer's K/V into the peer's pool."""
+    from ..ops import llama_ops
+
+    T = args.blocks * 16
+    hq = 4 * args.heads
+    out = []
+    dev = torch.device("cuda", rank)
+    qkv = torch.randn(T, hq + 2 * args.heads, 128, device=dev, dtype=torch.bfloat16)
+    pos = torch.arange(T, dtype=torch.int32, device=dev)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, 128, 2, dtype=torch.float64) / 128))
+    f = torch.outer(torch.arange(T, dtype=torch.float64), inv)
+    cs = torch.cat([f.cos(), f.sin()], dim=-1).float().to(dev)
+    d_blocks = torch.tensor(rng.sample(range(pool_blocks), args.blocks), dtype=torch.long, device=dev)
+    rslots = d_blocks[pos.long() // 16] * 16 + pos.long() % 16
+    hog_a = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    hog_b = torch.empty_like(hog_a)
+    nbytes = T * 2 * args.heads * 128 * 2 * args.layers
+    for busy in (False, True):
+        def fn():
+            if rank == 0:
+                for l in range(args.layers):
+                    rk = remote.layer_base(l)
+                    llama_ops.rope_kv_push(qkv, pos, cs, hq, args.heads, None,
+                                           (rk, rk + remote.outer_stride, remote.block_stride, remote.token_stride,
+                                            remote.head_stride, 16, rslots))
+            elif busy:
+                for _ in range(24):  # ~8 ms of 1 GiB copies: the decode GPU's HBM stays loaded meanwhile
+                    hog_b.copy_(hog_a)
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.iters):
+            dist.barrier(group=gloo_of(args))
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            ts.append(s.elapsed_time(e))
+        both = [None, None]
+        dist.all_gather_object(both, sorted(ts)[len(ts) // 2], group=gloo_of(args))
+        ms = both[0]  # the pushing rank's device time
+        r = {"path": "rope_push", "decode_gpu": "streaming_hbm" if busy else "idle", "tokens": T,
+             "layers": args.layers, "bytes": nbytes, "ms": round(ms, 4), "gbps": round(nbytes / ms / 1e6, 1),
+             "frac_of_peer_copy": round(nbytes / ms / 1e6 / PEER_COPY_GBPS, 3)}
+        out.append(r)
+        if rank == 0:
+            print(json.dumps(r), flush=True)
+    return out
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--blocks", type=int, default=512, help="blocks per request (512 = 8192 tokens)")
@@ -46,6 +104,9 @@ def main(argv=None):
     p.add_argument("--iters", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--dst-layout", default="nhd", choices=["nhd", "hnd"])
+    p.add_argument("--rope-push", action="store_true",
+                   help="also time the fused RoPE + KV push kernel (the bench's prefill path), with the decode "
+                        "GPU idle and with it streaming HBM (a stand-in for decode)")
     p.add_argument("--out", default=None)
     args = p.parse_args(argv)
     rank = int(os.environ["RANK"])
@@ -54,6 +115,7 @@ def main(argv=None):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", rank))
     gloo = dist.new_group(backend="gloo")
+    args._gloo = gloo
     reqs = [int(x) for x in args.requests.split(",")]
     nmax = max(reqs) * args.blocks
     pool_blocks = 2 * nmax + 8
@@ -153,6 +215,8 @@ def main(argv=None):
         if rank == 0:
             print(json.dumps(r), flush=True)
         del contig, staging
+    if args.rope_push:
+        results += rope_push_section(args, rank, local, remote, cfg, pool_blocks, timed, rng)
     if rank == 0 and args.out:
         with open(args.out, "w") as f:
             for r in results:

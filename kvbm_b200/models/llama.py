@@ -21,6 +21,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 from torch.nn.attention import SDPBackend, sdpa_kernel
+from torch.nn.attention.bias import causal_lower_right
 
 from ..ops import llama_ops
 from ..physical.layout import KvBlockLayout, KvLayout, LayoutConfig
@@ -144,6 +145,7 @@ class LlamaModel:
         self.cos_sin = torch.cat([f.cos(), f.sin()], dim=-1).float().to(self.device)
         self.scale = 1.0 / math.sqrt(c.head_dim)
         self._decode_scratch: torch.Tensor | None = None
+        self._attn_backends: dict[bool, list] = {}
 
     # ------------------------------------------------------------ helpers
     @staticmethod
@@ -199,7 +201,6 @@ class LlamaModel:
             q = qkv[:, : c.heads].transpose(0, 1).unsqueeze(0)
             k = qkv[:, c.heads: c.heads + c.kv_heads].transpose(0, 1)
             v = qkv[:, c.heads + c.kv_heads:].transpose(0, 1)
-            mask = None
             if start_pos > 0:
                 # cached prefix (e.g. onboarded from G2): read its K/V from the pool
                 nb = (start_pos + page - 1) // page
@@ -208,17 +209,7 @@ class LlamaModel:
                 pv = view[:, 1].reshape(-1, c.kv_heads, c.head_dim)[:start_pos].transpose(0, 1)
                 k = torch.cat([pk, k], dim=1)
                 v = torch.cat([pv, v], dim=1)
-                qi = torch.arange(T, device=self.device).unsqueeze(1) + start_pos
-                mask = torch.arange(start_pos + T, device=self.device).unsqueeze(0) <= qi
-            rep = c.heads // c.kv_heads
-            k = k.repeat_interleave(rep, dim=0).unsqueeze(0)
-            v = v.repeat_interleave(rep, dim=0).unsqueeze(0)
-            with sdpa_kernel([SDPBackend.FLASH_ATTENTION, SDPBackend.CUDNN_ATTENTION,
-                              SDPBackend.EFFICIENT_ATTENTION]):
-                if mask is None:
-                    a = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=self.scale)
-                else:
-                    a = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=self.scale)
+            a = self._attention(q, k.unsqueeze(0), v.unsqueeze(0), start_pos)
             a = a.squeeze(0).transpose(0, 1).reshape(T, c.q_size)
             x = F.linear(a, L["wo"])
             llama_ops.rmsnorm(x, L["n2"], c.eps, residual=residual, out=h)
@@ -229,6 +220,44 @@ class LlamaModel:
         llama_ops.rmsnorm(x[-1:].contiguous(), self.norm, c.eps, residual=res_last, out=last)
         logits = F.linear(last, self.lm_head)
         return logits.argmax(dim=-1)
+
+    @property
+    def attention_backend(self) -> str:
+        """Backend the no-prefix prefill attention resolved to (after the first prefill)."""
+        order = self._attn_backends.get(False, [SDPBackend.CUDNN_ATTENTION])
+        return "expanded-heads" if not order or order[0] is None else order[0].name.lower()
+
+    def _attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, offset: int) -> torch.Tensor:
+        """Causal prefill attention, q [1, Hq, T, D] against k/v [1, Hkv, offset + T, D].
+
+        cuDNN's fused attention with grouped-query heads runs this shape at
+        about four times the rate of the flash backend on sm_100 (0.39 ms vs
+        1.59 ms for 8,192 tokens, 32/8 heads). Backends that cannot take the
+        shape (strides, GQA, the lower-right causal mask of a prefix) are
+        skipped once and the next one is used from then on.
+        """
+        T, S = q.shape[2], k.shape[2]
+        mask = None if offset == 0 else causal_lower_right(T, S)
+        key = offset > 0
+        order = self._attn_backends.get(key, [SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, None])
+        for i, be in enumerate(order):
+            try:
+                if be is None:  # last resort: explicit head expansion for backends without GQA
+                    rep = q.shape[1] // k.shape[1]
+                    kk, vv = k.repeat_interleave(rep, dim=1), v.repeat_interleave(rep, dim=1)
+                    with sdpa_kernel([SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION,
+                                      SDPBackend.MATH]):
+                        if mask is None:
+                            return F.scaled_dot_product_attention(q, kk, vv, is_causal=True, scale=self.scale)
+                        return F.scaled_dot_product_attention(q, kk, vv, attn_mask=mask, scale=self.scale)
+                with sdpa_kernel([be]):
+                    if mask is None:
+                        return F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=self.scale,
+                                                              enable_gqa=True)
+                    return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=self.scale, enable_gqa=True)
+            except RuntimeError:
+                self._attn_backends[key] = order[i + 1:]
+        raise RuntimeError("no attention backend accepted the prefill shape")
 
     # ------------------------------------------------------------- decode
     def decode_scratch(self, batch: int, splits: int) -> torch.Tensor:
