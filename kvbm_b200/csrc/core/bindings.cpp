@@ -326,6 +326,17 @@ PYBIND11_MODULE(_kvbm_core, m) {
       .def("dropped_out_of_range", &PositionalIndex::dropped)
       .def("num_entries", &PositionalIndex::num_entries);
 
+  py::register_exception<LockOrderError>(m, "LockOrderError", PyExc_RuntimeError);
+  m.def("lock_check_enabled", &lock_check_enabled);
+  // Takes a BlockPool-rank mutex, then a Registry-rank one: must raise
+  // LockOrderError when checking is on (the registry ranks below the pool).
+  m.def("lock_order_selftest", []() {
+    RankedMutex pool(kRankBlockPool, "BlockPool"), reg(kRankRegistry, "Registry");
+    std::lock_guard<RankedMutex> a(pool);
+    std::lock_guard<RankedMutex> b(reg);
+    return RankedMutex::held().size();
+  });
+
   py::class_<DiskPool, std::shared_ptr<DiskPool>>(m, "DiskPool")
       .def(py::init<const std::string&, uint64_t, uint64_t, bool, bool, int>(), py::arg("path"),
            py::arg("num_blocks"), py::arg("block_bytes"), py::arg("direct") = false, py::arg("persistent") = false,

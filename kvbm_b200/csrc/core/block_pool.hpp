@@ -28,6 +28,8 @@
 #include <deque>
 #include <memory>
 #include <mutex>
+
+#include "ranked_mutex.hpp"
 #include <optional>
 #include <stdexcept>
 #include <string>
@@ -73,7 +75,7 @@ class BlockPool {
     std::vector<SeqHash> evicted;
     std::vector<BlockId> out;
     {
-      std::lock_guard<std::mutex> g(mu_);
+      std::lock_guard<RankedMutex> g(mu_);
       if (count == 0) return out;
       if (free_.size() + inactive_->size() < count) {
         metrics_.allocate_failures++;
@@ -109,26 +111,26 @@ class BlockPool {
   }
 
   void release_mutable(BlockId id) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     expect(id, SlotState::Mutable, "release_mutable");
     reset_locked(id);
   }
 
   void stage(BlockId id, const SeqHash& h) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     expect(id, SlotState::Mutable, "stage");
     slots_[id].state = SlotState::Staged;
     slots_[id].hash = h;
   }
 
   void unstage(BlockId id) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     expect(id, SlotState::Staged, "unstage");
     slots_[id].state = SlotState::Mutable;
   }
 
   void release_staged(BlockId id) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     expect(id, SlotState::Staged, "release_staged");
     reset_locked(id);
   }
@@ -139,7 +141,7 @@ class BlockPool {
     SeqHash h;
     bool presence = false;
     {
-      std::lock_guard<std::mutex> g(mu_);
+      std::lock_guard<RankedMutex> g(mu_);
       expect(id, SlotState::Staged, "register_block");
       h = slots_[id].hash;
       metrics_.registrations++;
@@ -178,7 +180,7 @@ class BlockPool {
   std::vector<BlockId> match_prefix(const std::vector<SeqHash>& hashes) {
     std::vector<BlockId> out;
     {
-      std::lock_guard<std::mutex> g(mu_);
+      std::lock_guard<RankedMutex> g(mu_);
       metrics_.match_hashes_requested += hashes.size();
       for (auto& h : hashes) {
         auto id = acquire_locked(h);
@@ -194,7 +196,7 @@ class BlockPool {
   std::vector<std::pair<SeqHash, BlockId>> scan(const std::vector<SeqHash>& hashes, bool touch) {
     std::vector<std::pair<SeqHash, BlockId>> out;
     {
-      std::lock_guard<std::mutex> g(mu_);
+      std::lock_guard<RankedMutex> g(mu_);
       metrics_.scan_hashes_requested += hashes.size();
       for (auto& h : hashes) {
         auto id = acquire_locked(h);
@@ -209,7 +211,7 @@ class BlockPool {
 
   // Number of leading hashes present (active or inactive), no references taken.
   size_t count_prefix(const std::vector<SeqHash>& hashes) const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     size_t n = 0;
     for (auto& h : hashes) {
       if (active_.count(h) == 0 && !inactive_->has(h)) break;
@@ -219,13 +221,13 @@ class BlockPool {
   }
 
   bool contains(const SeqHash& h) const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     return active_.count(h) != 0 || inactive_->has(h);
   }
 
   // ------------------------------------------------------------ references
   void add_ref(BlockId id) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     check_id(id);
     Slot& s = slots_[id];
     if (s.state != SlotState::Primary && s.state != SlotState::Duplicate)
@@ -236,14 +238,14 @@ class BlockPool {
   void release(BlockId id) {
     std::vector<SeqHash> absent;
     {
-      std::lock_guard<std::mutex> g(mu_);
+      std::lock_guard<RankedMutex> g(mu_);
       release_locked(id, absent);
     }
     for (auto& h : absent) registry_->mark_absent(h, tier_);
   }
 
   void set_reset_on_release(BlockId id, bool v) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     check_id(id);
     slots_[id].reset_on_release = v;
   }
@@ -252,7 +254,7 @@ class BlockPool {
   size_t reset_inactive() {
     std::vector<SeqHash> absent;
     {
-      std::lock_guard<std::mutex> g(mu_);
+      std::lock_guard<RankedMutex> g(mu_);
       auto all = inactive_->evict(inactive_->size());
       for (auto& [h, id] : all) {
         reset_locked(id);
@@ -268,33 +270,33 @@ class BlockPool {
   size_t block_size() const { return block_size_; }
   int tier() const { return tier_; }
   size_t reset_len() const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     return free_.size();
   }
   size_t inactive_len() const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     return inactive_->size();
   }
   size_t available() const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     return free_.size() + inactive_->size();
   }
   size_t active_len() const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     return active_.size();
   }
   SlotState state(BlockId id) const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     check_id(id);
     return slots_[id].state;
   }
   uint32_t refs(BlockId id) const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     check_id(id);
     return slots_[id].refs;
   }
   SeqHash hash_of(BlockId id) const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     check_id(id);
     return slots_[id].hash;
   }
@@ -377,7 +379,7 @@ class BlockPool {
   int tier_;
   DupPolicy policy_;
   std::shared_ptr<Registry> registry_;
-  mutable std::mutex mu_;
+  mutable RankedMutex mu_{kRankBlockPool, "BlockPool"};
   std::vector<Slot> slots_;
   std::deque<BlockId> free_;
   std::unique_ptr<InactiveIndex> inactive_;

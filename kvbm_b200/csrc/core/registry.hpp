@@ -22,6 +22,8 @@
 #include <deque>
 #include <memory>
 #include <mutex>
+
+#include "ranked_mutex.hpp"
 #include <unordered_map>
 #include <unordered_set>
 #include <vector>
@@ -55,22 +57,22 @@ class EventQueue {
  public:
   explicit EventQueue(EventPolicy policy = {}) : policy_(policy) {}
   void set_policy(EventPolicy p) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     policy_ = p;
   }
   void on_present(const SeqHash& h) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     if (!enabled_ || !policy_.should_emit(h)) return;
     emitted_.insert(h);
     q_.push_back({EventKind::Create, h});
   }
   void on_absent(const SeqHash& h) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     if (emitted_.erase(h) == 0) return;
     q_.push_back({EventKind::Remove, h});
   }
   std::vector<KvEvent> drain(size_t max = SIZE_MAX) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     std::vector<KvEvent> out;
     while (!q_.empty() && out.size() < max) {
       out.push_back(q_.front());
@@ -96,16 +98,16 @@ class EventQueue {
     return out;
   }
   size_t pending() const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     return q_.size();
   }
   void set_enabled(bool e) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     enabled_ = e;
   }
 
  private:
-  mutable std::mutex mu_;
+  mutable RankedMutex mu_{kRankEventQueue, "EventQueue"};
   EventPolicy policy_;
   bool enabled_ = true;
   std::deque<KvEvent> q_;
@@ -120,7 +122,7 @@ class Registry {
   void mark_present(const SeqHash& h, int tier) {
     bool first = false;
     {
-      std::lock_guard<std::mutex> g(mu_);
+      std::lock_guard<RankedMutex> g(mu_);
       auto& e = map_[h];
       first = (e.total == 0);
       ++e.count[tier];
@@ -131,7 +133,7 @@ class Registry {
   void mark_absent(const SeqHash& h, int tier) {
     bool last = false;
     {
-      std::lock_guard<std::mutex> g(mu_);
+      std::lock_guard<RankedMutex> g(mu_);
       auto it = map_.find(h);
       if (it == map_.end() || it->second.count[tier] == 0) return;
       --it->second.count[tier];
@@ -143,13 +145,13 @@ class Registry {
     if (last && events_) events_->on_absent(h);
   }
   bool is_present(const SeqHash& h, int tier) const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     auto it = map_.find(h);
     if (it == map_.end()) return false;
     return tier < 0 ? it->second.total > 0 : it->second.count[tier] > 0;
   }
   uint32_t presence_mask(const SeqHash& h) const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     auto it = map_.find(h);
     if (it == map_.end()) return 0;
     uint32_t m = 0;
@@ -162,7 +164,7 @@ class Registry {
   }
   uint32_t frequency(const SeqHash& h) const { return freq_ ? freq_->estimate(h.lineage) : 0; }
   size_t size() const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     return map_.size();
   }
   std::shared_ptr<EventQueue> events() const { return events_; }
@@ -173,7 +175,7 @@ class Registry {
     std::array<uint32_t, kMaxTiers> count{};
     uint32_t total = 0;
   };
-  mutable std::mutex mu_;
+  mutable RankedMutex mu_{kRankRegistry, "Registry"};
   std::unordered_map<SeqHash, Entry, SeqHashHasher> map_;
   std::shared_ptr<EventQueue> events_;
   std::shared_ptr<TinyLfu> freq_;

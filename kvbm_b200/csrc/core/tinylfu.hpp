@@ -11,6 +11,8 @@
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
+
+#include "ranked_mutex.hpp"
 #include <vector>
 
 #include "hash.hpp"
@@ -26,7 +28,7 @@ class TinyLfu {
   }
 
   void touch(uint64_t key) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     bool added = false;
     for (int i = 0; i < 4; ++i) {
       const uint64_t h = splitmix64(key ^ kSeeds[i]);
@@ -36,7 +38,7 @@ class TinyLfu {
   }
 
   uint32_t estimate(uint64_t key) const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     uint32_t m = 15;
     for (int i = 0; i < 4; ++i) {
       const uint64_t h = splitmix64(key ^ kSeeds[i]);
@@ -62,7 +64,7 @@ class TinyLfu {
     size_ /= 2;
   }
 
-  mutable std::mutex mu_;
+  mutable RankedMutex mu_{kRankTinyLfu, "TinyLfu"};
   std::vector<uint64_t> table_;
   size_t words_;
   uint64_t size_ = 0;

@@ -23,6 +23,8 @@
 #include <deque>
 #include <map>
 #include <mutex>
+
+#include "ranked_mutex.hpp"
 #include <optional>
 #include <set>
 #include <string>
@@ -161,11 +163,11 @@ class PositionalIndex {
     max_positions_ = max_seq_len / block_size;
   }
   void grow_to(uint64_t max_seq_len) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     max_positions_ = std::max(max_positions_, max_seq_len / block_size_);
   }
   void apply_create(const InstanceId& inst, const std::vector<SeqHash>& hs) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     for (auto& h : hs) {
       if (h.position >= max_positions_) {
         ++dropped_;
@@ -175,7 +177,7 @@ class PositionalIndex {
     }
   }
   void apply_remove(const InstanceId& inst, const std::vector<SeqHash>& hs) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     for (auto& h : hs) {
       auto b = buckets_.find(h.position);
       if (b == buckets_.end()) continue;
@@ -186,7 +188,7 @@ class PositionalIndex {
     }
   }
   void remove_instance(const InstanceId& inst) {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     for (auto& [pos, m] : buckets_) {
       for (auto it = m.begin(); it != m.end();) {
         it->second.erase(inst);
@@ -196,7 +198,7 @@ class PositionalIndex {
   }
   // Deepest hash present and its holders.
   std::optional<std::pair<SeqHash, std::vector<InstanceId>>> query(const std::vector<SeqHash>& hs) const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     std::vector<SeqHash> sorted(hs);
     std::sort(sorted.begin(), sorted.end(), [](auto& a, auto& b) { return a.position > b.position; });
     for (auto& h : sorted) {
@@ -209,22 +211,22 @@ class PositionalIndex {
     return std::nullopt;
   }
   uint64_t num_positions() const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     return max_positions_;
   }
   uint64_t dropped() const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     return dropped_;
   }
   size_t num_entries() const {
-    std::lock_guard<std::mutex> g(mu_);
+    std::lock_guard<RankedMutex> g(mu_);
     size_t n = 0;
     for (auto& [p, m] : buckets_) n += m.size();
     return n;
   }
 
  private:
-  mutable std::mutex mu_;
+  mutable RankedMutex mu_{kRankPositionalIndex, "PositionalIndex"};
   uint64_t block_size_;
   uint64_t max_positions_;
   uint64_t dropped_ = 0;

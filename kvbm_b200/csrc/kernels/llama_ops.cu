@@ -183,6 +183,7 @@ struct RopeKvParams {
   int r_head_offset;
   const int64_t* rslots;
   int group;          // head pairs per work item
+  int q_per_kv;       // query pairs visited after each K/V pair (0: K/V pairs first)
   FastDiv pairs_div;  // divides by the number of groups per token
   FastDiv page_div;
   FastDiv r_page_div;
@@ -194,11 +195,13 @@ __device__ __forceinline__ uint8_t* cache_base(uint8_t* kb, int64_t slot, const 
   return kb + static_cast<int64_t>(blk) * bs + static_cast<int64_t>(off) * ts;
 }
 
-// Work item = (token, group of `P.group` head pairs). Head pairs are visited
-// K first, then V, then Q (pair j covers heads (Hq + 2j + {0,1}) mod H), so
-// the KV stores - the ones that may cross NVLink - are issued first. The
-// warp loads the token's cos/sin once and keeps kUnroll pairs of rows in
-// flight per lane.
+// Work item = (token, group of `P.group` head pairs). With GQA (Hq/2 query
+// pairs a multiple of the Hkv K/V pairs) the visiting order interleaves one
+// K/V pair with every (Hq/2)/Hkv query pairs, so the stores that may cross
+// NVLink are spread evenly over the launch instead of arriving in bursts;
+// otherwise K/V pairs come first (pair j covers heads (Hq + 2j + {0,1}) mod H).
+// The warp loads the token's cos/sin once and keeps kRopeUnroll pairs of
+// rows in flight per lane.
 constexpr int kRopeUnroll = 4;
 
 __global__ void __launch_bounds__(256) rope_kv_fused_kernel(const __grid_constant__ RopeKvParams P) {
@@ -239,10 +242,16 @@ __global__ void __launch_bounds__(256) rope_kv_fused_kernel(const __grid_constan
       int hh[kRopeUnroll];
 #pragma unroll
       for (int u = 0; u < kRopeUnroll; ++u) {
-        const int hp = 2 * (j0 + u) + half;  // position in K,V,Q order
-        const bool valid = (j0 + u) < j_end && hp < H;
-        int h = hp + P.Hq;
-        if (h >= H) h -= H;
+        const int j = j0 + u;
+        int h;
+        if (P.q_per_kv > 0) {  // interleaved: [KV, Q x q_per_kv] repeated
+          const int b = j / (P.q_per_kv + 1), r = j - b * (P.q_per_kv + 1);
+          h = (r == 0 ? P.Hq + 2 * b : 2 * (b * P.q_per_kv + r - 1)) + half;
+        } else {
+          h = 2 * j + half + P.Hq;
+          if (h >= H) h -= H;
+        }
+        const bool valid = j < j_end && h < H && (P.q_per_kv > 0 || 2 * j + half < H);
         hh[u] = valid ? h : -1;
         x[u] = valid ? *reinterpret_cast<const int4*>(trow + static_cast<int64_t>(h) * 128) : make_int4(0, 0, 0, 0);
       }
@@ -287,27 +296,48 @@ __global__ void __launch_bounds__(256) rope_kv_fused_kernel(const __grid_constan
 // ---------------------------------------------------------------------------
 // out[t, i] = silu(gate_up[t, i]) * gate_up[t, I + i]
 // ---------------------------------------------------------------------------
+constexpr int kSiluUnroll = 4;
+
+__device__ __forceinline__ int4 silu_mul_vec(const int4 g, const int4 u) {
+  const uint32_t wg[4] = {(uint32_t)g.x, (uint32_t)g.y, (uint32_t)g.z, (uint32_t)g.w};
+  const uint32_t wu[4] = {(uint32_t)u.x, (uint32_t)u.y, (uint32_t)u.z, (uint32_t)u.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float a = bf16_lo(wg[j]), b = bf16_hi(wg[j]);
+    const float sa = __bfloat162float(__float2bfloat16(a / (1.f + __expf(-a))));
+    const float sb = __bfloat162float(__float2bfloat16(b / (1.f + __expf(-b))));
+    o[j] = pack_bf16(sa * bf16_lo(wu[j]), sb * bf16_hi(wu[j]));
+  }
+  return make_int4(o[0], o[1], o[2], o[3]);
+}
+
+// Each thread keeps kSiluUnroll gate/up vector pairs in flight: all loads of
+// a batch are issued before any math, so a thread has 8 x 16 B outstanding.
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu,
                                                        __nv_bfloat16* __restrict__ out, int64_t T, int I) {
   const int nv = I / 8;
   const int64_t total = T * nv;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
-       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t t = v / nv;
-    const int c = static_cast<int>(v - t * nv);
-    const int4 g = reinterpret_cast<const int4*>(gu + t * 2 * I)[c];
-    const int4 u = reinterpret_cast<const int4*>(gu + t * 2 * I + I)[c];
-    const uint32_t wg[4] = {(uint32_t)g.x, (uint32_t)g.y, (uint32_t)g.z, (uint32_t)g.w};
-    const uint32_t wu[4] = {(uint32_t)u.x, (uint32_t)u.y, (uint32_t)u.z, (uint32_t)u.w};
-    uint32_t o[4];
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; base < total;
+       base += step * kSiluUnroll) {
+    int4 g[kSiluUnroll], u[kSiluUnroll];
+    int64_t t[kSiluUnroll];
+    int c[kSiluUnroll];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float a = bf16_lo(wg[j]), b = bf16_hi(wg[j]);
-      const float sa = __bfloat162float(__float2bfloat16(a / (1.f + __expf(-a))));
-      const float sb = __bfloat162float(__float2bfloat16(b / (1.f + __expf(-b))));
-      o[j] = pack_bf16(sa * bf16_lo(wu[j]), sb * bf16_hi(wu[j]));
+    for (int k = 0; k < kSiluUnroll; ++k) {
+      const int64_t v = base + k * step;
+      t[k] = v / nv;
+      c[k] = static_cast<int>(v - t[k] * nv);
+      if (v < total) {
+        g[k] = reinterpret_cast<const int4*>(gu + t[k] * 2 * I)[c[k]];
+        u[k] = reinterpret_cast<const int4*>(gu + t[k] * 2 * I + I)[c[k]];
+      }
     }
-    reinterpret_cast<int4*>(out + t * I)[c] = make_int4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+    for (int k = 0; k < kSiluUnroll; ++k) {
+      if (base + k * step < total) reinterpret_cast<int4*>(out + t[k] * I)[c[k]] = silu_mul_vec(g[k], u[k]);
+    }
   }
 }
 
@@ -528,6 +558,7 @@ int launch_rope_fused(RopeKvParams& P, cudaStream_t stream) {
   int groups = 1;
   while (groups < groups_max && static_cast<int64_t>(P.T) * groups < int64_t{sms} * 64) groups *= 2;
   groups = std::min(groups, groups_max);
+  P.q_per_kv = (P.Hq % 2 == 0 && P.Hkv > 0 && (P.Hq / 2) % P.Hkv == 0) ? (P.Hq / 2) / P.Hkv : 0;
   P.group = (pairs + groups - 1) / groups;
   groups = (pairs + P.group - 1) / P.group;
   const int64_t items = static_cast<int64_t>(P.T) * groups;
@@ -627,7 +658,9 @@ extern "C" int kvbm_silu_mul(const void* gate_up, void* out, int64_t tokens, int
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t work = tokens * (inter / 8);
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(sms) * 16));
+  const unsigned grid = static_cast<unsigned>(
+      std::max<int64_t>(1, std::min<int64_t>((work + 256 * kSiluUnroll - 1) / (256 * kSiluUnroll),
+                                             static_cast<int64_t>(sms) * 8)));
   silu_mul_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(gate_up),
                                             static_cast<__nv_bfloat16*>(out), tokens, inter);
   return cudaGetLastError();

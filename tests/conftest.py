@@ -3,6 +3,9 @@ import sys
 
 import pytest
 
+# every core mutex acquisition is checked against the lock hierarchy in tests
+os.environ.setdefault("KVBM_LOCK_CHECK", "1")
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)

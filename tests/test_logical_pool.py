@@ -303,3 +303,14 @@ def test_tinylfu_counts_and_ages():
     for i in range(2000):
         f.touch(1000 + i)
     assert f.estimate(42) < 7  # halved by ageing
+
+
+def test_lock_hierarchy_is_checked():
+    assert core.lock_check_enabled()  # turned on for the whole test run
+    with pytest.raises(core.LockOrderError, match="Registry .* while holding BlockPool"):
+        core.lock_order_selftest()
+    # a full allocate / register / match / release cycle respects the hierarchy
+    mgr = BlockManager(8, 16, "multi_lru", Tier.G2)
+    blocks = mgr.allocate_blocks(2)
+    imm = mgr.register_mutable(blocks, sequence_hashes(list(range(32)), 16))
+    assert len(mgr.match_blocks([b.sequence_hash for b in imm])) == 2
