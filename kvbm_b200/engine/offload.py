@@ -326,17 +326,27 @@ class OffloadEngine:
             p.close()
 
 
-def make_tier_executor(src_handle: int, dst_manager: BlockManager, dst_handle: int, transfer_manager) -> Executor:
-    """Executor that allocates destination blocks, transfers, and registers them."""
+def make_tier_executor(src_handle: int, dst_manager: BlockManager, dst_handle: int, transfer_manager,
+                       journal=None) -> Executor:
+    """Executor that allocates destination blocks, transfers, and registers them.
+
+    With a ``journal`` (``engine.tier_journal.TierJournal``, for a persistent
+    G3) the destination ids are logged as invalid before the write and as
+    committed with their hashes after it.
+    """
 
     def run(items: list[OffloadItem]) -> list[ImmutableBlock]:
         got = dst_manager.allocate_blocks_with_evictions(len(items))
         if got is None:
             raise RuntimeError(f"{dst_manager.tier.name} pool has no free or evictable blocks")
         blocks, _evicted = got
-        note = transfer_manager.execute_transfer(src_handle, [i.src_block_id for i in items], dst_handle,
-                                                 [b.block_id for b in blocks])
+        dst_ids = [b.block_id for b in blocks]
+        if journal is not None:
+            journal.invalidate(dst_ids)
+        note = transfer_manager.execute_transfer(src_handle, [i.src_block_id for i in items], dst_handle, dst_ids)
         note.wait()
+        if journal is not None:
+            journal.commit(dst_ids, [i.seq_hash for i in items])
         imm = dst_manager.register_mutable(blocks, [i.seq_hash for i in items])
         # the registered blocks are cached in the destination's inactive pool
         out = list(imm)

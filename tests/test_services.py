@@ -212,3 +212,34 @@ def test_disk_pool_roundtrip(tmp_path):
     assert (a == b).all() and d.bytes_written() == 3 * 4096
     with pytest.raises(IndexError):
         d.read([8], [b.ctypes.data])
+
+
+def test_tier_journal_restores_g3_registrations(tmp_path):
+    from kvbm_b200.engine.tier_journal import TierJournal, restore
+
+    path = str(tmp_path / "g3.journal")
+    hs = sequence_hashes(list(range(16 * 6)), 16)
+    j = TierJournal(path)
+    j.invalidate([0, 1, 2])
+    j.commit([0, 1, 2], hs[:3])
+    j.invalidate([1])            # block 1 is being overwritten ...
+    j.commit([4], hs[3:4])
+    j.invalidate([5])            # ... and block 5's write never completed (crash)
+    j.close()
+    with open(path, "ab") as f:
+        f.write(b"\x85\xa2op")   # torn tail
+    live = TierJournal.replay(path)
+    assert live == {0: hs[0], 2: hs[2], 4: hs[3]}
+    g3 = BlockManager(8, 16, "lru", Tier.G3)
+    assert restore(g3, live) == 3
+    got = g3.match_blocks(hs[:1])
+    assert [b.block_id for b in got] == [0]
+    for b in got:
+        b.release()
+    assert g3.allocate_blocks(5) is not None  # the 5 unjournaled ids were freed
+    j2 = TierJournal(path)
+    j2.compact()
+    assert TierJournal.replay(path) == live
+    j2.close()
+    with pytest.raises(RuntimeError):
+        restore(g3, live)  # not a fresh pool
