@@ -202,7 +202,7 @@ __device__ __forceinline__ uint8_t* cache_base(uint8_t* kb, int64_t slot, const 
 // otherwise K/V pairs come first (pair j covers heads (Hq + 2j + {0,1}) mod H).
 // The warp loads the token's cos/sin once and keeps kRopeUnroll pairs of
 // rows in flight per lane.
-constexpr int kRopeUnroll = 4;  // pairs in flight per lane for short groups (decode)
+constexpr int kRopeUnroll = 4;  // head pairs in flight per lane (64 registers: 32 warps per SM)
 
 template <int kUnroll>
 __global__ void __launch_bounds__(256) rope_kv_fused_kernel(const __grid_constant__ RopeKvParams P) {
@@ -297,121 +297,6 @@ __global__ void __launch_bounds__(256) rope_kv_fused_kernel(const __grid_constan
 // ---------------------------------------------------------------------------
 // out[t, i] = silu(gate_up[t, i]) * gate_up[t, I + i]
 // ---------------------------------------------------------------------------
-// Bulk-staged variant for prefill-sized batches: each warp owns whole tokens;
-// lane 0 brings a token's packed qkv row (H x 256 B, contiguous) into the
-// warp's slot of a two-stage shared-memory ring with one cp.async.bulk (TMA,
-// this GPU's own memory) while the warp rotates and stores the previous
-// token from shared memory. Bytes in flight no longer cost registers, so the
-// HBM reads overlap the stores - including the peer stores over NVLink.
-// Waits on the ring's mbarriers are bounded (%globaltimer); a warp that gives
-// up records kStatusPipelineTimeout in g_rope_status, waits (bounded) for its
-// own copy in flight and returns.
-constexpr int kStagedWarps = 4;
-constexpr uint64_t kStagedWaitNs = 2000000000ull;  // 2 s: far above any copy of a 16 KB row
-__device__ int g_rope_status = 0;
-
-__global__ void __launch_bounds__(kStagedWarps * 32) rope_kv_staged_kernel(const __grid_constant__ RopeKvParams P) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bars[kStagedWarps][2];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hl = lane & 15, half = lane >> 4;
-  const int H = P.Hq + 2 * P.Hkv;
-  const int pairs = (H + 1) >> 1;
-  const uint32_t row_bytes = static_cast<uint32_t>(H) * 256u;
-  uint8_t* ring = smem + static_cast<size_t>(warp) * 2 * row_bytes;
-  if (lane == 0) {
-    mbar_init(&bars[warp][0], 1);
-    mbar_init(&bars[warp][1], 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
-  const float sign = hl < 8 ? -1.f : 1.f;
-  const uint32_t nw = gridDim.x * kStagedWarps;
-  uint32_t t = blockIdx.x * kStagedWarps + warp;
-  const uint8_t* qkv_bytes = reinterpret_cast<const uint8_t*>(P.qkv);
-  if (t < static_cast<uint32_t>(P.T) && lane == 0) {
-    mbar_arrive_expect_tx(&bars[warp][0], row_bytes);
-    bulk_g2s(ring, qkv_bytes + static_cast<int64_t>(t) * row_bytes, row_bytes, &bars[warp][0]);
-  }
-  for (uint32_t k = 0; t < static_cast<uint32_t>(P.T); t += nw, ++k) {
-    const int st = k & 1;
-    const uint32_t tn = t + nw;
-    // the other stage was read in the previous iteration: every lane is done with it
-    __syncwarp();
-    fence_proxy_async_smem();
-    const bool prefetch = tn < static_cast<uint32_t>(P.T);
-    if (prefetch && lane == 0) {
-      mbar_arrive_expect_tx(&bars[warp][st ^ 1], row_bytes);
-      bulk_g2s(ring + (st ^ 1) * row_bytes, qkv_bytes + static_cast<int64_t>(tn) * row_bytes, row_bytes,
-               &bars[warp][st ^ 1]);
-    }
-    if (!mbar_wait_bounded(&bars[warp][st], (k >> 1) & 1, kStagedWaitNs)) {
-      if (lane == 0) atomicExch(&g_rope_status, kStatusPipelineTimeout);
-      if (prefetch) mbar_wait_bounded(&bars[warp][st ^ 1], ((k + 1) >> 1) & 1, kStagedWaitNs);
-      return;
-    }
-    const uint8_t* row = ring + st * row_bytes;
-    const float* cs = P.cos_sin + static_cast<int64_t>(P.positions[t]) * 128 + (hl & 7) * 8;
-    const float4 c0 = reinterpret_cast<const float4*>(cs)[0], c1 = reinterpret_cast<const float4*>(cs)[1];
-    const float4 s0 = reinterpret_cast<const float4*>(cs + 64)[0];
-    const float4 s1 = reinterpret_cast<const float4*>(cs + 64)[1];
-    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-    const float sn[8] = {sign * s0.x, sign * s0.y, sign * s0.z, sign * s0.w,
-                         sign * s1.x, sign * s1.y, sign * s1.z, sign * s1.w};
-    uint8_t* lrow = nullptr;
-    uint8_t* rrow = nullptr;
-    if (P.slots) {
-      const int64_t slot = P.slots[t];
-      if (slot >= 0) lrow = cache_base(P.k_base, slot, P.page_div, P.block_stride, P.token_stride);
-    }
-    if (P.rslots) {
-      const int64_t slot = P.rslots[t];
-      if (slot >= 0) rrow = cache_base(P.rk_base, slot, P.r_page_div, P.r_block_stride, P.r_token_stride);
-    }
-    __nv_bfloat16* grow = P.qkv + static_cast<int64_t>(t) * H * 128 + hl * 8;
-#pragma unroll 4
-    for (int j = 0; j < pairs; ++j) {
-      int h;
-      if (P.q_per_kv > 0) {
-        const int b = j / (P.q_per_kv + 1), r = j - b * (P.q_per_kv + 1);
-        h = (r == 0 ? P.Hq + 2 * b : 2 * (b * P.q_per_kv + r - 1)) + half;
-      } else {
-        h = 2 * j + half + P.Hq;
-        if (h >= H) h -= H;
-      }
-      const bool valid = h < H && (P.q_per_kv > 0 || 2 * j + half < H);
-      int4 x = valid ? *reinterpret_cast<const int4*>(row + h * 256 + hl * 16) : make_int4(0, 0, 0, 0);
-      int4 p;
-      p.x = __shfl_xor_sync(0xffffffffu, x.x, 8);
-      p.y = __shfl_xor_sync(0xffffffffu, x.y, 8);
-      p.z = __shfl_xor_sync(0xffffffffu, x.z, 8);
-      p.w = __shfl_xor_sync(0xffffffffu, x.w, 8);
-      if (!valid) continue;
-      if (h < P.Hq + P.Hkv) {
-        const uint32_t xm[4] = {(uint32_t)x.x, (uint32_t)x.y, (uint32_t)x.z, (uint32_t)x.w};
-        const uint32_t xp[4] = {(uint32_t)p.x, (uint32_t)p.y, (uint32_t)p.z, (uint32_t)p.w};
-        uint32_t y[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          y[q] = pack_bf16(bf16_lo(xm[q]) * c[2 * q] + bf16_lo(xp[q]) * sn[2 * q],
-                           bf16_hi(xm[q]) * c[2 * q + 1] + bf16_hi(xp[q]) * sn[2 * q + 1]);
-        x = make_int4((int)y[0], (int)y[1], (int)y[2], (int)y[3]);
-        *reinterpret_cast<int4*>(grow + static_cast<int64_t>(h) * 128) = x;
-      }
-      if (h >= P.Hq) {
-        const bool is_k = h < P.Hq + P.Hkv;
-        const int kvh = is_k ? h - P.Hq : h - P.Hq - P.Hkv;
-        if (lrow)
-          reinterpret_cast<int4*>(lrow + (is_k ? 0 : P.v_base - P.k_base) +
-                                  static_cast<int64_t>(kvh) * P.head_stride)[hl] = x;
-        if (rrow)
-          reinterpret_cast<int4*>(rrow + (is_k ? 0 : P.rv_base - P.rk_base) +
-                                  static_cast<int64_t>(kvh + P.r_head_offset) * P.r_head_stride)[hl] = x;
-      }
-    }
-  }
-}
-
 constexpr int kSiluUnroll = 4;
 
 __device__ __forceinline__ int4 silu_mul_vec(const int4 g, const int4 u) {
@@ -662,8 +547,6 @@ extern "C" int kvbm_rmsnorm(const void* x, void* residual, const void* weight, v
 namespace {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-bool g_rope_staged = true;  // prefill-sized batches use the bulk-staged kernel
-
 int launch_rope_fused(RopeKvParams& P, cudaStream_t stream) {
   const int H = P.Hq + 2 * P.Hkv;
   const int pairs = (H + 1) / 2;
@@ -684,28 +567,9 @@ int launch_rope_fused(RopeKvParams& P, cudaStream_t stream) {
   P.pairs_div = FastDiv(static_cast<uint32_t>(groups));
   P.page_div = FastDiv(static_cast<uint32_t>(P.page > 0 ? P.page : 1));
   P.r_page_div = FastDiv(static_cast<uint32_t>(P.r_page > 0 ? P.r_page : 1));
-  const size_t staged_smem = static_cast<size_t>(kStagedWarps) * 2 * H * 256;
-  if (g_rope_staged && static_cast<int64_t>(P.T) >= int64_t{sms} * 2 * kStagedWarps * 2 && H <= 64 &&
-      (reinterpret_cast<uintptr_t>(P.qkv) & 15) == 0) {
-    static thread_local int configured_dev = -1;
-    if (configured_dev != dev) {
-      cudaError_t e = cudaFuncSetAttribute(rope_kv_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(kStagedWarps * 2 * 64 * 256));
-      if (e != cudaSuccess) return e;
-      configured_dev = dev;
-    }
-    const int per_sm = static_cast<int>(std::max<size_t>(1, (200u << 10) / staged_smem));
-    const int64_t want = (static_cast<int64_t>(P.T) + kStagedWarps - 1) / kStagedWarps;
-    const unsigned sgrid = static_cast<unsigned>(std::min<int64_t>(want, int64_t{sms} * per_sm));
-    rope_kv_staged_kernel<<<sgrid, kStagedWarps * 32, staged_smem, stream>>>(P);
-    return cudaGetLastError();
-  }
   const int64_t ctas = (items + 7) / 8;
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ctas, int64_t{sms} * 32)));
-  if (P.group >= 8)
-    rope_kv_fused_kernel<8><<<grid, 256, 0, stream>>>(P);
-  else
-    rope_kv_fused_kernel<kRopeUnroll><<<grid, 256, 0, stream>>>(P);
+  rope_kv_fused_kernel<kRopeUnroll><<<grid, 256, 0, stream>>>(P);
   return cudaGetLastError();
 }
 
@@ -713,26 +577,6 @@ bool cache_ok(const void* kb, const void* vb, int64_t bs, int64_t ts, int64_t hs
   return kb && vb && page > 0 && aligned16(kb) && aligned16(vb) && bs % 16 == 0 && ts % 16 == 0 && hs % 16 == 0;
 }
 }  // namespace
-
-// Selects the RoPE/KV kernel for prefill-sized batches: 1 = bulk-staged
-// (default), 0 = register-only. Returns the previous setting.
-extern "C" int kvbm_rope_set_staged(int on) {
-  const int prev = g_rope_staged ? 1 : 0;
-  g_rope_staged = on != 0;
-  return prev;
-}
-
-// Status of the bulk-staged RoPE/KV kernel (0 = ok, 3 = a ring wait gave up);
-// synchronizes the device. With reset != 0 the status is cleared.
-extern "C" int kvbm_rope_status(int reset) {
-  int v = -1;
-  if (cudaMemcpyFromSymbol(&v, g_rope_status, sizeof(int)) != cudaSuccess) return -1;
-  if (reset) {
-    const int zero = 0;
-    cudaMemcpyToSymbol(g_rope_status, &zero, sizeof(int));
-  }
-  return v;
-}
 
 extern "C" int kvbm_rope_kv_write(void* qkv, int64_t tokens, int hq, int hkv, int hd, const int32_t* positions,
                                   const float* cos_sin, void* k_base, void* v_base, int64_t block_stride,

@@ -91,8 +91,6 @@ _SIGS = {
          _INT, _VP, _VP],
     ),
     "kvbm_silu_mul": (_INT, [_VP, _VP, _I64, _INT, _VP]),
-    "kvbm_rope_set_staged": (_INT, [_INT]),
-    "kvbm_rope_status": (_INT, [_INT]),
     "kvbm_paged_decode_attn": (
         _INT,
         [_VP, _VP, _VP, _I64, _I64, _I64, _INT, _VP, _INT, _VP, _INT, _INT, _INT, _INT, _F32, _INT, _VP, _VP, _VP,

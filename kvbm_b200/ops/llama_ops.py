@@ -52,16 +52,6 @@ def rope_kv_push(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tens
               rk or None, rv or None, rbs, rts, rhs, rpage, r_head_offset, rslots.data_ptr(), _stream(stream))
 
 
-def set_rope_staged(on: bool) -> bool:
-    """Use the bulk-staged RoPE/KV kernel for prefill-sized batches (default on); returns the old setting."""
-    return bool(_lib.load().kvbm_rope_set_staged(1 if on else 0))
-
-
-def rope_status(reset: bool = False) -> int:
-    """0, or the error status a bulk-staged RoPE/KV launch recorded (synchronizes the device)."""
-    return int(_lib.load().kvbm_rope_status(1 if reset else 0))
-
-
 def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     T = gate_up.numel() // gate_up.shape[-1]
     inter = gate_up.shape[-1] // 2

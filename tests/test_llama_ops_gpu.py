@@ -125,41 +125,6 @@ def test_rope_kv_push_into_second_pool(local_write):
         assert not lv.any()
 
 
-def test_rope_kv_push_staged_matches_register_kernel():
-    """Prefill-sized batches take the bulk-staged kernel; it must agree with the register one."""
-    torch.manual_seed(4)
-    T, hq, hkv, hd, page = 4096, 32, 8, 128, 16
-    nb = T // page
-    cfg = LayoutConfig.for_model(nb + 3, 1, hkv, hd, page)
-    outs = []
-    base = torch.randn(T, hq + 2 * hkv, hd, device="cuda", dtype=torch.bfloat16)
-    pos = torch.arange(T, device="cuda", dtype=torch.int32)
-    cs = _cos_sin(8192, hd)
-    blocks = torch.randperm(nb + 3, device="cuda")[:nb]
-    ar = torch.arange(T, device="cuda")
-    slots = (blocks[ar // page] * page + ar % page).long()
-    for staged in (True, False):
-        prev = llama_ops.set_rope_staged(staged)
-        pool = KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.OPERATIONAL_HND, zero=True)
-        qkv = base.clone()
-        kb = pool.layer_base(0)
-        llama_ops.rope_kv_push(qkv, pos, cs, hq, hkv, None,
-                               (kb, kb + pool.outer_stride, pool.block_stride, pool.token_stride, pool.head_stride,
-                                page, slots))
-        assert llama_ops.rope_status(reset=True) == 0
-        llama_ops.set_rope_staged(prev)
-        outs.append((qkv, pool.layer_view(0)[blocks.long()].clone()))
-    (q1, v1), (q2, v2) = outs
-    torch.testing.assert_close(q1.float(), q2.float(), rtol=0, atol=1e-2)
-    torch.testing.assert_close(v1.float(), v2.float(), rtol=0, atol=1e-2)
-    ref = _rope_ref(base[:, :hq].float(), pos.long(), cs)
-    torch.testing.assert_close(q1[:, :hq].float(), ref, rtol=1e-2, atol=1e-2)
-    # the pool holds exactly what the kernel left in qkv (K rotated, V copied)
-    k_cache = v1[:, 0].reshape(T, hkv, hd)
-    assert torch.equal(k_cache, q1[:, hq:hq + hkv])
-    assert torch.equal(v1[:, 1].reshape(T, hkv, hd), base[:, hq + hkv:])
-
-
 def test_silu_mul():
     torch.manual_seed(2)
     gu = torch.randn(33, 2 * 1024, device="cuda", dtype=torch.bfloat16)

@@ -1,0 +1,76 @@
+"""The vLLM v1 adapter on CPU: the scheduler-role connector, built on vLLM's
+real ``KVConnectorBase_V1``, answers the scheduler hooks from a stub
+config and stub requests (no engine, no GPU)."""
+
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+vllm_base = pytest.importorskip("vllm.distributed.kv_transfer.kv_connector.v1.base")
+
+from kvbm_b200.connector.protocol import ConnectorMetadata  # noqa: E402
+
+
+class _ModelConfig:
+    dtype = torch.bfloat16
+    max_model_len = 4096
+    use_mla = False
+    hf_config = SimpleNamespace(num_hidden_layers=2)
+
+    def get_num_kv_heads(self, pc):
+        return 2
+
+    def get_num_layers(self, pc):
+        return 2
+
+    def get_head_size(self):
+        return 64
+
+
+def _vllm_config(extra):
+    return SimpleNamespace(
+        model_config=_ModelConfig(),
+        parallel_config=SimpleNamespace(tensor_parallel_size=1, pipeline_parallel_size=1, rank=0),
+        cache_config=SimpleNamespace(block_size=16, cache_dtype="auto"),
+        kv_transfer_config=SimpleNamespace(kv_connector="KvbmConnector", kv_role="kv_both",
+                                           kv_connector_extra_config=extra))
+
+
+def _request(rid, tokens):
+    return SimpleNamespace(request_id=rid, prompt_token_ids=tokens, cache_salt=None, lora_request=None,
+                           kv_transfer_params=None)
+
+
+def _sched_output(new_reqs, computed, finished=()):
+    news = [SimpleNamespace(req_id=r, block_ids=(b,), num_computed_tokens=0) for r, b in new_reqs]
+    return SimpleNamespace(scheduled_new_reqs=news, scheduled_cached_reqs=None,
+                           num_scheduled_tokens=computed, finished_req_ids=set(finished))
+
+
+def test_scheduler_role_offloads_then_matches():
+    from kvbm_b200.connector import vllm_connector as vc
+
+    Role = vllm_base.KVConnectorRole
+    conn = vc.KvbmConnector(_vllm_config({"leader": {"cache": {"host": {"num_blocks": 64}}}}), Role.SCHEDULER)
+    assert isinstance(conn, vllm_base.KVConnectorBase_V1)
+    tokens = list(range(5 * 16 + 3))
+    r1 = _request("a", tokens)
+    assert conn.get_num_new_matched_tokens(r1, 0) == (0, False)  # cold
+    blocks = SimpleNamespace(get_block_ids=lambda: ([10, 11, 12, 13, 14, 15],))
+    conn.update_state_after_alloc(r1, blocks, 0)
+    meta = conn.build_connector_meta(_sched_output([("a", [10, 11, 12, 13, 14, 15])], {"a": len(tokens)}))
+    assert isinstance(meta, vc.KvbmConnectorMetadata)
+    m = ConnectorMetadata.decode(meta.metadata)
+    assert [op.g1_ids for op in m.offload] == [[10, 11, 12, 13, 14]]  # the five full prompt blocks
+    conn.update_connector_output(SimpleNamespace(finished_sending={"a"}, finished_recving=None))
+    assert conn.request_finished(r1, [10, 11, 12, 13, 14, 15]) == (False, None)
+
+    # the same prompt again: five blocks come from G2 (the last token is always computed)
+    r2 = _request("b", tokens)
+    assert conn.get_num_new_matched_tokens(r2, 0) == (5 * 16, True)
+    conn.update_state_after_alloc(r2, SimpleNamespace(get_block_ids=lambda: ([20, 21, 22, 23, 24, 25],)), 5 * 16)
+    m2 = ConnectorMetadata.decode(conn.build_connector_meta(_sched_output([("b", [20, 21, 22, 23, 24, 25])],
+                                                                          {"b": 3})).metadata)
+    assert len(m2.onboard) == 1 and m2.onboard[0].g1_ids == [20, 21, 22, 23, 24]
+    assert conn.build_kv_connector_stats() is None
