@@ -264,19 +264,41 @@ class OffloadPipeline:
         batch: list[tuple[OffloadHandle, OffloadItem]] = [(h, i) for h, items in live for i in items]
         results: dict[int, list] = {id(h): [] for h, _ in live}
         ok = {id(h): True for h, _ in live}
-        for s in range(0, len(batch), self.cfg.max_batch):
-            chunk = batch[s: s + self.cfg.max_batch]
-            try:
-                with nvtx_range(f"kvbm.offload.{self.name}.transfer"):
-                    reg = self.executor([i for _, i in chunk])
-                self.stats["batches"] += 1
-                if reg is not None:
-                    for (h, _), r in zip(chunk, reg):
-                        results[id(h)].append(r)
-            except Exception as e:  # noqa: BLE001 - surfaced on the handle
-                for h, _ in chunk:
-                    ok[id(h)] = False
-                    h.error = e
+        chunks = [batch[s: s + self.cfg.max_batch] for s in range(0, len(batch), self.cfg.max_batch)]
+
+        def fail(chunk, e):
+            for h, _ in chunk:
+                ok[id(h)] = False
+                h.error = e
+
+        def collect(chunk, reg):
+            self.stats["batches"] += 1
+            if reg is not None:
+                for (h, _), r in zip(chunk, reg):
+                    results[id(h)].append(r)
+
+        if hasattr(self.executor, "submit"):
+            # launch every batch's copy first, then wait and register in order
+            tokens = []
+            with nvtx_range(f"kvbm.offload.{self.name}.transfer"):
+                for chunk in chunks:
+                    try:
+                        tokens.append((chunk, self.executor.submit([i for _, i in chunk])))
+                    except Exception as e:  # noqa: BLE001 - surfaced on the handle
+                        fail(chunk, e)
+                for chunk, tok in tokens:
+                    try:
+                        collect(chunk, self.executor.complete(tok))
+                    except Exception as e:  # noqa: BLE001
+                        fail(chunk, e)
+        else:
+            for chunk in chunks:
+                try:
+                    with nvtx_range(f"kvbm.offload.{self.name}.transfer"):
+                        reg = self.executor([i for _, i in chunk])
+                    collect(chunk, reg)
+                except Exception as e:  # noqa: BLE001 - surfaced on the handle
+                    fail(chunk, e)
         for h, items in live:
             audit("offload_batch", pipeline=self.name, blocks=len(items), ok=ok[id(h)])
             with h._lock:
@@ -326,30 +348,57 @@ class OffloadEngine:
             p.close()
 
 
-def make_tier_executor(src_handle: int, dst_manager: BlockManager, dst_handle: int, transfer_manager,
-                       journal=None) -> Executor:
-    """Executor that allocates destination blocks, transfers, and registers them.
+class TierExecutor:
+    """Allocates destination blocks, transfers into them and registers them.
 
-    With a ``journal`` (``engine.tier_journal.TierJournal``, for a persistent
-    G3) the destination ids are logged as invalid before the write and as
+    ``submit`` allocates and launches the copy without waiting; ``complete``
+    waits for it and registers the blocks, so a pipeline can keep several
+    batches' copies in flight. Calling the executor does both. With a
+    ``journal`` (``engine.tier_journal.TierJournal``, for a persistent G3)
+    the destination ids are logged as invalid before the write and as
     committed with their hashes after it.
     """
 
-    def run(items: list[OffloadItem]) -> list[ImmutableBlock]:
-        got = dst_manager.allocate_blocks_with_evictions(len(items))
+    def __init__(self, src_handle: int, dst_manager: BlockManager, dst_handle: int, transfer_manager,
+                 journal=None):
+        self.src_handle, self.dst, self.dst_handle = src_handle, dst_manager, dst_handle
+        self.tm, self.journal = transfer_manager, journal
+
+    def submit(self, items: list[OffloadItem]):
+        got = self.dst.allocate_blocks_with_evictions(len(items))
         if got is None:
-            raise RuntimeError(f"{dst_manager.tier.name} pool has no free or evictable blocks")
+            raise RuntimeError(f"{self.dst.tier.name} pool has no free or evictable blocks")
         blocks, _evicted = got
         dst_ids = [b.block_id for b in blocks]
-        if journal is not None:
-            journal.invalidate(dst_ids)
-        note = transfer_manager.execute_transfer(src_handle, [i.src_block_id for i in items], dst_handle, dst_ids)
-        note.wait()
-        if journal is not None:
-            journal.commit(dst_ids, [i.seq_hash for i in items])
-        imm = dst_manager.register_mutable(blocks, [i.seq_hash for i in items])
-        # the registered blocks are cached in the destination's inactive pool
-        out = list(imm)
-        return out
+        if self.journal is not None:
+            self.journal.invalidate(dst_ids)
+        try:
+            note = self.tm.execute_transfer(self.src_handle, [i.src_block_id for i in items], self.dst_handle,
+                                            dst_ids)
+        except Exception:
+            for b in blocks:
+                b.release()
+            raise
+        return items, blocks, note
 
-    return run
+    def complete(self, token) -> list[ImmutableBlock]:
+        items, blocks, note = token
+        try:
+            note.wait()
+        except Exception:
+            for b in blocks:
+                b.release()
+            raise
+        if self.journal is not None:
+            self.journal.commit([b.block_id for b in blocks], [i.seq_hash for i in items])
+        # the registered blocks are cached in the destination's inactive pool
+        return list(self.dst.register_mutable(blocks, [i.seq_hash for i in items]))
+
+    def __call__(self, items: list[OffloadItem]) -> list[ImmutableBlock]:
+        return self.complete(self.submit(items))
+
+
+def make_tier_executor(src_handle: int, dst_manager: BlockManager, dst_handle: int, transfer_manager,
+                       journal=None) -> TierExecutor:
+    """Executor that allocates destination blocks, transfers, and registers them."""
+    return TierExecutor(src_handle, dst_manager, dst_handle, transfer_manager, journal)

@@ -26,7 +26,7 @@ def _ids(ids, device) -> torch.Tensor:
     if isinstance(ids, torch.Tensor) and ids.dtype == torch.int32 and (ids.is_cuda or ids.is_pinned()):
         return ids
     t = torch.as_tensor(ids, dtype=torch.int32)
-    return t.to(device, non_blocking=True) if device is not None else t
+    return t.pin_memory().to(device, non_blocking=True) if device is not None else t
 
 
 def kv_transfer(src, src_ids, dst, dst_ids, *, layer_begin: int = 0, num_layers: int | None = None,
@@ -137,8 +137,9 @@ def copy_pairs(src_ptrs, dst_ptrs, nbytes: int, *, align: int | None = None, max
     if not isinstance(src_ptrs, torch.Tensor):
         if align is None:
             align = _ptr_align(list(src_ptrs) + list(dst_ptrs), nbytes)
-        src_ptrs = torch.tensor(list(src_ptrs), dtype=torch.int64).to(dev, non_blocking=True)
-        dst_ptrs = torch.tensor(list(dst_ptrs), dtype=torch.int64).to(dev, non_blocking=True)
+        # staged through page-locked memory so the upload does not wait for the stream's earlier work
+        src_ptrs = torch.tensor(list(src_ptrs), dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        dst_ptrs = torch.tensor(list(dst_ptrs), dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
     if align is None:
         align = 16 if nbytes % 16 == 0 else 1
     _lib.call("kvbm_copy_pairs", src_ptrs.data_ptr(), dst_ptrs.data_ptr(), src_ptrs.numel(), nbytes, align,
