@@ -170,6 +170,7 @@ def main(argv=None):
         wire = src_bytes // 2 if a.fp8 else src_bytes
         line = {"bench": "reshard_p2d", "world": world, "prefill_tp": ptp, "decode_tp": dtp,
                 "decode_instances": 2, "kv_dtype": "fp8_e4m3" if a.fp8 else "bf16", "layers": a.layers,
+                "kv_heads": a.heads, "engine": a.engine,
                 "requests": a.requests, "tokens": sum(lens), "ms": round(ms, 3),
                 "src_gbps": round(src_bytes / ms / 1e6, 1), "wire_gbps": round(wire / ms / 1e6, 1),
                 "per_prefill_rank_wire_gbps": round(wire / ptp / ms / 1e6, 1),

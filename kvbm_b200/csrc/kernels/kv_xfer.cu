@@ -566,16 +566,21 @@ __global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __
   uint64_t* empty_bar = full_bar + Q.stages;
   uint8_t* stage_base = smem_raw + 1024;  // barriers live in the first 1 KiB
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = P.shape.num_heads, O = P.shape.num_outer, L = P.shape.num_layers;
+  // Consumer warps form groups of wc warps; each group takes every groups-th
+  // staged chunk and splits its head tiles, so chunks with fewer heads than
+  // consumer warps (KV-head slices of a TP rank) keep every warp busy.
+  const int wc = H < kConsumerWarps ? H : kConsumerWarps;
+  const int groups = kConsumerWarps / wc;
   if (threadIdx.x == 0) {
     for (int s = 0; s < Q.stages; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kConsumerWarps);
+      mbar_init(&empty_bar[s], wc);
     }
     fence_mbar_init();
   }
   __syncthreads();
 
-  const int H = P.shape.num_heads, O = P.shape.num_outer, L = P.shape.num_layers;
   const int T = P.shape.page_size;
   const int64_t row = P.src_row_bytes;
 
@@ -627,8 +632,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __
   }
 
   // ---------------- consumers ----------------
-  int64_t k = 0;
-  for (int64_t c = blockIdx.x; c < Q.total_chunks; c += gridDim.x, ++k) {
+  const int group = warp / wc, gw = warp - group * wc;
+  if (group >= groups) return;  // H does not divide the consumer warps: the remainder idles
+  int64_t k = group;
+  for (int64_t c = blockIdx.x + static_cast<int64_t>(group) * gridDim.x; c < Q.total_chunks;
+       c += static_cast<int64_t>(groups) * gridDim.x, k += groups) {
     const int s = static_cast<int>(k % Q.stages);
     const uint32_t phase = static_cast<uint32_t>((k / Q.stages) & 1);
     if (!mbar_wait_bounded(&full_bar[s], phase, kPipeWaitNs)) {
@@ -642,7 +650,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __
     const int64_t p = r / L;
     const uint8_t* sbuf = stage_base + static_cast<int64_t>(s) * Q.stage_bytes;
     uint8_t* dchunk = const_cast<uint8_t*>(chunk_addr(P.dst, p, i, o));
-    for (int h = warp; h < H; h += kConsumerWarps) {
+    for (int h = gw; h < H; h += wc) {
       const uint8_t* srow = Q.src_nhd ? sbuf + h * row : sbuf + static_cast<int64_t>(h) * T * row;
       const int64_t s_rs = Q.src_nhd ? static_cast<int64_t>(H) * row : row;
       uint8_t* d = dchunk + static_cast<int64_t>(h + P.dst.head_offset) * P.dst.head_stride;
@@ -709,7 +717,7 @@ extern "C" int kvbm_kv_chunk_xfer_tma(const KvbmSide* src, const KvbmSide* dst, 
   Q.chunk_bytes = Q.run_bytes * Q.num_runs;
   Q.stage_bytes = (Q.chunk_bytes + 127) / 128 * 128;
   const int budget = 200 * 1024;
-  Q.stages = std::min(4, budget / Q.stage_bytes);
+  Q.stages = std::min(16, budget / Q.stage_bytes);
   if (Q.stages < 2) return cudaErrorInvalidValue;
   Q.total_chunks = static_cast<int64_t>(S.num_pairs) * S.num_layers * S.num_outer;
   Q.status = nullptr;

@@ -257,3 +257,29 @@ def test_checksum_kernel_matches_reference_across_layouts(dtype):
     assert len(set(ca)) == 3
     sub = checksum_blocks(b, [2], layer_begin=1, num_layers=2)
     assert sub == [checksum_reference(a.gather_blocks([4])[0, 1:3])]
+
+
+@pytest.mark.parametrize("nh", [1, 2, 3, 8])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_tma_head_slices_match_tile_engine(nh, fp8):
+    """Head slices narrower than the TMA pipeline's 8 consumer warps (a TP rank's
+    share): grouped consumers must store exactly what the tile engine stores."""
+    src_cfg = _cfg(nb=20, nl=3, nh=nh)
+    dst_cfg = _cfg(nb=20, nl=3, nh=2 * nh, dtype=torch.float8_e4m3fn if fp8 else torch.bfloat16)
+    src = KvLayout.allocate(src_cfg, "fully_contiguous", NHD)
+    _fill(src, 11)
+    s_ids, d_ids = _pairs(13, 20, 12)
+    outs = []
+    for engine in ("tile", "tma"):
+        dst = KvLayout.allocate(dst_cfg, "fully_contiguous", HND, fp8_scales=fp8)
+        _poison(dst)
+        kv_ops.kv_transfer(src, s_ids, dst, d_ids, dst_head_offset=nh, num_heads=nh, engine=engine)
+        torch.cuda.synchronize()
+        got = dst.gather_blocks(d_ids).view(torch.uint8)
+        outs.append((got, dst.scales_view()[torch.tensor(d_ids, device="cuda")].clone() if fp8 else None))
+    assert torch.equal(outs[0][0], outs[1][0])
+    if fp8:
+        assert torch.equal(outs[0][1][..., nh:], outs[1][1][..., nh:])
+    else:
+        ref = src.gather_blocks(s_ids)
+        assert torch.equal(outs[1][0].view(torch.bfloat16)[..., nh:, :], ref.view(torch.bfloat16))
