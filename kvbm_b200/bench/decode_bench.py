@@ -27,6 +27,8 @@ def main(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--eager", action="store_true")
     p.add_argument("--splits", type=int, default=0)
+    p.add_argument("--profile", action="store_true",
+                   help="bracket one extra eager step with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     args = p.parse_args(argv)
     torch.cuda.set_device(0)
     cfg = LlamaConfig(layers=args.layers)
@@ -62,6 +64,11 @@ def main(argv=None):
     e.record()
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / args.steps
+    if args.profile:
+        torch.cuda.profiler.start()
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     # attention alone, all layers, same inputs
     q = torch.randn(B, cfg.heads, cfg.head_dim, device="cuda", dtype=torch.bfloat16)
     scratch = model.decode_scratch(B, splits)
