@@ -184,6 +184,7 @@ struct RopeKvParams {
   const int64_t* rslots;
   int group;          // head pairs per work item
   int q_per_kv;       // query pairs visited after each K/V pair (0: K/V pairs first)
+  __nv_bfloat16* q_out;  // optional [T, Hq, 128]: rotated query rows go here instead of back into qkv
   FastDiv pairs_div;  // divides by the number of groups per token
   FastDiv page_div;
   FastDiv r_page_div;
@@ -277,7 +278,10 @@ __global__ void __launch_bounds__(256) rope_kv_fused_kernel(const __grid_constan
                              bf16_hi(xm[k]) * c[2 * k + 1] + bf16_hi(xp[k]) * sn[2 * k + 1]);
           }
           x[u] = make_int4((int)y[0], (int)y[1], (int)y[2], (int)y[3]);
-          *reinterpret_cast<int4*>(row) = x[u];
+          if (P.q_out != nullptr && h < P.Hq)
+            reinterpret_cast<int4*>(P.q_out + (static_cast<int64_t>(t) * P.Hq + h) * 128)[hl] = x[u];
+          else
+            *reinterpret_cast<int4*>(row) = x[u];
         }
         if (h >= P.Hq) {
           const bool is_k = h < P.Hq + P.Hkv;
@@ -610,6 +614,35 @@ extern "C" int kvbm_rope_kv_write(void* qkv, int64_t tokens, int hq, int hkv, in
                                                  static_cast<uint8_t*>(v_base), block_stride, token_stride,
                                                  head_stride, page, slots);
   return cudaGetLastError();
+}
+
+// Decode form: RoPE + paged KV write, with the rotated query rows written to
+// a separate contiguous q_out [tokens, hq, 128] (the attention's input), so
+// no copy of the strided q slice follows; head_dim 128.
+extern "C" int kvbm_rope_kv_write_qout(void* qkv, int64_t tokens, int hq, int hkv, const int32_t* positions,
+                                       const float* cos_sin, void* k_base, void* v_base, int64_t block_stride,
+                                       int64_t token_stride, int64_t head_stride, int page, const int64_t* slots,
+                                       void* q_out, cudaStream_t stream) {
+  if (tokens == 0) return cudaSuccess;
+  if (!qkv || !positions || !cos_sin || !q_out || !aligned16(qkv) || !aligned16(cos_sin) || !aligned16(q_out))
+    return cudaErrorInvalidValue;
+  if (slots && !cache_ok(k_base, v_base, block_stride, token_stride, head_stride, page)) return cudaErrorInvalidValue;
+  RopeKvParams P{};
+  P.qkv = static_cast<__nv_bfloat16*>(qkv);
+  P.T = static_cast<int>(tokens);
+  P.Hq = hq;
+  P.Hkv = hkv;
+  P.positions = positions;
+  P.cos_sin = cos_sin;
+  P.k_base = static_cast<uint8_t*>(k_base);
+  P.v_base = static_cast<uint8_t*>(v_base);
+  P.block_stride = block_stride;
+  P.token_stride = token_stride;
+  P.head_stride = head_stride;
+  P.page = page;
+  P.slots = slots;
+  P.q_out = static_cast<__nv_bfloat16*>(q_out);
+  return launch_rope_fused(P, stream);
 }
 
 // RoPE + KV write into the local cache (optional) and a second cache that

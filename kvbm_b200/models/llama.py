@@ -283,6 +283,7 @@ class LlamaModel:
         h = torch.empty_like(x)
         scratch = self.decode_scratch(B, splits)
         attn = torch.empty(B, c.heads, c.head_dim, device=self.device, dtype=self.dtype)
+        q = torch.empty(B, c.heads, c.head_dim, device=self.device, dtype=self.dtype)
         for li, L in enumerate(self.layers):
             if li == 0:
                 llama_ops.rmsnorm(x, L["n1"], c.eps, out=h)
@@ -290,9 +291,13 @@ class LlamaModel:
                 llama_ops.rmsnorm(x, L["n1"], c.eps, residual=residual, out=h)
             qkv = F.linear(h, L["wqkv"]).view(B, c.heads + 2 * c.kv_heads, c.head_dim)
             kb, vb = self.kv_bases(pool, li)
-            llama_ops.rope_kv_write(qkv, positions, self.cos_sin, c.heads, c.kv_heads, c.head_dim, kb, vb,
-                                    pool.block_stride, pool.token_stride, pool.head_stride, page, slots)
-            q = qkv[:, : c.heads].contiguous()
+            if c.head_dim == 128:
+                llama_ops.rope_kv_write_qout(qkv, positions, self.cos_sin, c.heads, c.kv_heads, kb, vb,
+                                             pool.block_stride, pool.token_stride, pool.head_stride, page, slots, q)
+            else:
+                llama_ops.rope_kv_write(qkv, positions, self.cos_sin, c.heads, c.kv_heads, c.head_dim, kb, vb,
+                                        pool.block_stride, pool.token_stride, pool.head_stride, page, slots)
+                q.copy_(qkv[:, : c.heads])
             llama_ops.paged_decode_attn(q, kb, vb, pool.block_stride, pool.token_stride, pool.head_stride, page,
                                         block_table, seq_lens, c.kv_heads, self.scale, splits, scratch=scratch,
                                         out=attn)

@@ -22,11 +22,36 @@ def _stream(stream) -> int:
     return int(stream)
 
 
-def _ids(ids, device) -> torch.Tensor:
+_upload_streams: dict[int, torch.cuda.Stream] = {}
+
+
+def upload(host: torch.Tensor, device: torch.device, stream=None) -> torch.Tensor:
+    """Copy a small host tensor (block ids, pointer tables) to ``device`` for use on ``stream``.
+
+    The copy runs on a dedicated idle stream, so it does not wait behind the
+    target stream's queued transfers (a pageable copy is synchronous with the
+    work already in its stream) and needs no page-locked staging allocation;
+    the target stream waits on an event for it.
+    """
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    us = _upload_streams.get(idx)
+    if us is None:
+        us = _upload_streams[idx] = torch.cuda.Stream(device=idx)
+    target = stream if isinstance(stream, torch.cuda.Stream) else torch.cuda.current_stream(idx)
+    with torch.cuda.stream(us):
+        d = host.to(device, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(us)
+    target.wait_event(ev)
+    d.record_stream(target)
+    return d
+
+
+def _ids(ids, device, stream=None) -> torch.Tensor:
     if isinstance(ids, torch.Tensor) and ids.dtype == torch.int32 and (ids.is_cuda or ids.is_pinned()):
         return ids
     t = torch.as_tensor(ids, dtype=torch.int32)
-    return t.pin_memory().to(device, non_blocking=True) if device is not None else t
+    return upload(t, device, stream) if device is not None else t
 
 
 def kv_transfer(src, src_ids, dst, dst_ids, *, layer_begin: int = 0, num_layers: int | None = None,
@@ -59,8 +84,8 @@ def kv_transfer(src, src_ids, dst, dst_ids, *, layer_begin: int = 0, num_layers:
     if sc.head_dim != dc.head_dim or sc.page_size != dc.page_size or sc.outer_dim != dc.outer_dim:
         raise ValueError("pools differ in head_dim, page_size or outer_dim")
     dev = torch.device("cuda", torch.cuda.current_device())
-    sid = _ids(src_ids, dev)
-    did = _ids(dst_ids, dev)
+    sid = _ids(src_ids, dev, stream)
+    did = _ids(dst_ids, dev, stream)
     s = src.side(sid, layer_begin, nl, src_head_offset)
     d = dst.side(did, dlb, nl, dst_head_offset)
     shape = _lib.KvbmTileShape(n_pairs, nl, sc.outer_dim, nh, sc.page_size, sc.head_dim, src.dtype_code,
@@ -137,9 +162,8 @@ def copy_pairs(src_ptrs, dst_ptrs, nbytes: int, *, align: int | None = None, max
     if not isinstance(src_ptrs, torch.Tensor):
         if align is None:
             align = _ptr_align(list(src_ptrs) + list(dst_ptrs), nbytes)
-        # staged through page-locked memory so the upload does not wait for the stream's earlier work
-        src_ptrs = torch.tensor(list(src_ptrs), dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
-        dst_ptrs = torch.tensor(list(dst_ptrs), dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        src_ptrs = upload(torch.tensor(list(src_ptrs), dtype=torch.int64), dev, stream)
+        dst_ptrs = upload(torch.tensor(list(dst_ptrs), dtype=torch.int64), dev, stream)
     if align is None:
         align = 16 if nbytes % 16 == 0 else 1
     _lib.call("kvbm_copy_pairs", src_ptrs.data_ptr(), dst_ptrs.data_ptr(), src_ptrs.numel(), nbytes, align,

@@ -31,6 +31,19 @@ def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Ten
               slots.data_ptr() if slots is not None else None, _stream(stream))
 
 
+def rope_kv_write_qout(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, hq: int, hkv: int,
+                       k_base: int, v_base: int, block_stride: int, token_stride: int, head_stride: int, page: int,
+                       slots: torch.Tensor, q_out: torch.Tensor, stream=None) -> torch.Tensor:
+    """Decode form of the RoPE/KV kernel: K/V into the paged cache, rotated q into ``q_out`` [T, hq, 128]."""
+    T = qkv.shape[0]
+    if qkv.shape[-1] != 128 or q_out.shape != (T, hq, 128) or not q_out.is_contiguous():
+        raise ValueError("rope_kv_write_qout needs head_dim 128 and a contiguous [T, hq, 128] q_out")
+    _lib.call("kvbm_rope_kv_write_qout", qkv.data_ptr(), T, hq, hkv, positions.data_ptr(), cos_sin.data_ptr(),
+              k_base or None, v_base or None, block_stride, token_stride, head_stride, page, slots.data_ptr(),
+              q_out.data_ptr(), _stream(stream))
+    return q_out
+
+
 def rope_kv_push(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, hq: int, hkv: int,
                  local: tuple | None, remote: tuple, r_head_offset: int = 0, stream=None) -> None:
     """RoPE + KV write into ``local`` (optional) and ``remote`` paged caches in one kernel (head_dim 128).

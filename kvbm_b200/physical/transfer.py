@@ -370,8 +370,8 @@ class TransferManager:
                 kv_ops.copy_pairs(sp, dp, a.config.bytes_per_block, max_ctas=opts.max_ctas, stream=stream)
             else:
                 hr = opts.head_range
-                sid = torch.tensor(s_ids, dtype=torch.int32).pin_memory().to(stream.device, non_blocking=True)
-                did = torch.tensor(d_ids, dtype=torch.int32).pin_memory().to(stream.device, non_blocking=True)
+                sid = kv_ops.upload(torch.tensor(s_ids, dtype=torch.int32), stream.device, stream)
+                did = kv_ops.upload(torch.tensor(d_ids, dtype=torch.int32), stream.device, stream)
                 kv_ops.kv_transfer(a, sid, b, did, layer_begin=lb, num_layers=le - lb,
                                    src_head_offset=hr[0] if hr else 0, dst_head_offset=hr[1] if hr else 0,
                                    num_heads=hr[2] if hr else None, engine=engine, max_ctas=opts.max_ctas,

@@ -125,6 +125,30 @@ def test_rope_kv_push_into_second_pool(local_write):
         assert not lv.any()
 
 
+def test_rope_kv_write_qout_decode_form():
+    torch.manual_seed(5)
+    T, hq, hkv, hd, page = 33, 32, 8, 128, 16
+    cfg = LayoutConfig.for_model(8, 1, hkv, hd, page)
+    pool = KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.OPERATIONAL_NHD, zero=True)
+    qkv = torch.randn(T, hq + 2 * hkv, hd, device="cuda", dtype=torch.bfloat16)
+    orig = qkv.clone()
+    pos = torch.randint(0, 4000, (T,), device="cuda", dtype=torch.int32)
+    cs = _cos_sin(4096, hd)
+    slots = torch.randperm(8 * page, device="cuda")[:T].long()
+    q_out = torch.empty(T, hq, hd, device="cuda", dtype=torch.bfloat16)
+    kb = pool.layer_base(0)
+    llama_ops.rope_kv_write_qout(qkv, pos, cs, hq, hkv, kb, kb + pool.outer_stride, pool.block_stride,
+                                 pool.token_stride, pool.head_stride, page, slots, q_out)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(q_out.float(), _rope_ref(orig[:, :hq], pos.long(), cs), rtol=1e-2, atol=1e-2)
+    assert torch.equal(qkv[:, :hq], orig[:, :hq])  # the q slice of qkv is left alone
+    view = pool.layer_view(0)
+    for t in range(T):
+        b, o = int(slots[t]) // page, int(slots[t]) % page
+        assert torch.equal(view[b, 0, o], qkv[t, hq:hq + hkv])
+        assert torch.equal(view[b, 1, o], orig[t, hq + hkv:])
+
+
 def test_silu_mul():
     torch.manual_seed(2)
     gu = torch.randn(33, 2 * 1024, device="cuda", dtype=torch.bfloat16)
