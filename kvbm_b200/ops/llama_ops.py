@@ -2,6 +2,8 @@
 
 from __future__ import annotations
 
+import math
+
 import torch
 
 from . import _lib
@@ -74,12 +76,26 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None, stream=None
     return out
 
 
-def decode_splits(batch: int, hkv: int, max_seq: int, page: int, sm_count: int = 148) -> int:
-    """Number of KV splits so that batch*hkv*splits fills the SMs a few times."""
+def decode_splits(batch: int, hkv: int, max_seq: int, page: int, sm_count: int = 148,
+                  resident_per_sm: int = 2) -> int:
+    """Number of KV splits for the decode attention grid (batch x hkv x splits CTAs).
+
+    Starts from enough splits to fill the SMs about four times over, then
+    looks at up to four times as many and keeps the one whose last wave of
+    CTAs is fullest (``resident_per_sm`` CTAs of the tensor-core kernel fit
+    on an SM), so the GPU does not idle on a ragged final wave.
+    """
     blocks = max(1, (max_seq + page - 1) // page)
-    target = 8 * sm_count
-    splits = max(1, min(blocks, (target + batch * hkv - 1) // (batch * hkv)))
-    return int(splits)
+    groups = max(1, batch * hkv)
+    slots = resident_per_sm * sm_count
+    base = max(1, min(blocks, (4 * slots + groups - 1) // groups))
+    best, best_eff = base, -1.0
+    for s in range(base, min(blocks, 4 * base) + 1):
+        waves = groups * s / slots
+        eff = waves / math.ceil(waves)
+        if eff > best_eff + 0.02:  # more splits cost partial writes: only for a clearly fuller last wave
+            best, best_eff = s, eff
+    return int(best)
 
 
 def paged_decode_attn(q: torch.Tensor, k_base: int, v_base: int, block_stride: int, token_stride: int,
