@@ -90,6 +90,40 @@ def rope_push_section(args, rank, local, remote, cfg, pool_blocks, timed, rng) -
         out.append(r)
         if rank == 0:
             print(json.dumps(r), flush=True)
+    # copy-engine baseline: the RoPE kernel writes K/V into a local per-layer staging area, then one
+    # cudaMemcpy2DAsync per layer moves the request's rows (K+V of one layer of a block are adjacent
+    # in the fully contiguous layout) into consecutive destination blocks of the peer pool
+    bpl = 2 * 16 * args.heads * 128 * 2  # K+V bytes of one layer of one block
+    staging = torch.empty(args.layers * args.blocks * bpl, dtype=torch.uint8, device=dev)
+    first = pool_blocks - args.blocks
+
+    def ce():
+        if rank == 0:
+            for l in range(args.layers):
+                kv_ops.memcpy_2d_ce(remote.layer_base(l) + first * remote.block_stride, remote.block_stride,
+                                    staging.data_ptr() + l * args.blocks * bpl, bpl, bpl, args.blocks)
+
+    for _ in range(args.warmup):
+        ce()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(args.iters):
+        dist.barrier(group=gloo_of(args))
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        ce()
+        e.record()
+        torch.cuda.synchronize()
+        ts.append(s.elapsed_time(e))
+    both = [None, None]
+    dist.all_gather_object(both, sorted(ts)[len(ts) // 2], group=gloo_of(args))
+    ms = both[0]
+    r = {"path": "ce_2d_per_layer", "tokens": T, "layers": args.layers, "bytes": nbytes, "ms": round(ms, 4),
+         "gbps": round(nbytes / ms / 1e6, 1), "frac_of_peer_copy": round(nbytes / ms / 1e6 / PEER_COPY_GBPS, 3),
+         "note": "copy engines only; needs the K/V staged locally first and consecutive destination blocks"}
+    out.append(r)
+    if rank == 0:
+        print(json.dumps(r), flush=True)
     return out
 
 

@@ -92,6 +92,13 @@ int kvbm_memcpy_pairs_ce(const uint64_t* src, const uint64_t* dst, uint64_t n, u
   return cudaSuccess;
 }
 
+// Copy-engine baseline for a strided batch: `height` rows of `width` bytes,
+// `spitch` / `dpitch` bytes apart (one request's layer of KV blocks).
+int kvbm_memcpy_2d_async(void* dst, uint64_t dpitch, const void* src, uint64_t spitch, uint64_t width,
+                         uint64_t height, cudaStream_t stream) {
+  return cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, cudaMemcpyDefault, stream);
+}
+
 int kvbm_get_device(int* dev) { return cudaGetDevice(dev); }
 
 const char* kvbm_error_string(int code) { return cudaGetErrorString(static_cast<cudaError_t>(code)); }

@@ -120,6 +120,7 @@ _SIGS = {
     "kvbm_can_access_peer": (_INT, [_INT, _INT, C.POINTER(_INT)]),
     "kvbm_enable_peer_access": (_INT, [_INT]),
     "kvbm_memcpy_async": (_INT, [_VP, _VP, _U64, _VP]),
+    "kvbm_memcpy_2d_async": (_INT, [_VP, _U64, _VP, _U64, _U64, _U64, _VP]),
     "kvbm_memcpy_pairs_ce": (_INT, [_VP, _VP, _U64, _U64, _VP]),
     "kvbm_get_device": (_INT, [C.POINTER(_INT)]),
     "kvbm_error_string": (C.c_char_p, [_INT]),

@@ -170,6 +170,12 @@ def copy_pairs(src_ptrs, dst_ptrs, nbytes: int, *, align: int | None = None, max
               max_ctas, _stream(stream))
 
 
+def memcpy_2d_ce(dst: int, dpitch: int, src: int, spitch: int, width: int, height: int, stream=None) -> None:
+    """Copy-engine baseline for a strided batch of equal rows (one cudaMemcpy2DAsync)."""
+    _lib.check(_lib.load().kvbm_memcpy_2d_async(dst, dpitch, src, spitch, width, height, _stream(stream)),
+               "kvbm_memcpy_2d_async")
+
+
 def memcpy_pairs_ce(src_ptrs: list[int], dst_ptrs: list[int], nbytes: int, stream=None) -> None:
     """Copy-engine baseline: one cudaMemcpyAsync per region."""
     n = len(src_ptrs)
