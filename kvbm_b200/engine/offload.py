@@ -197,7 +197,8 @@ class OffloadPipeline:
         self.on_registered = on_registered
         self._q: "queue.Queue[OffloadHandle | None]" = queue.Queue()
         self._stop = False
-        self.stats = {"enqueued": 0, "offloaded": 0, "filtered": 0, "cancelled": 0, "failed": 0, "batches": 0}
+        self.stats = {"enqueued": 0, "offloaded": 0, "filtered": 0, "cancelled": 0, "failed": 0, "batches": 0,
+                      "submit_s": 0.0, "complete_s": 0.0}
         self._thread = threading.Thread(target=self._run, name=f"kvbm-offload-{name}", daemon=True)
         self._thread.start()
 
@@ -281,16 +282,20 @@ class OffloadPipeline:
             # launch every batch's copy first, then wait and register in order
             tokens = []
             with nvtx_range(f"kvbm.offload.{self.name}.transfer"):
+                t0 = time.perf_counter()
                 for chunk in chunks:
                     try:
                         tokens.append((chunk, self.executor.submit([i for _, i in chunk])))
                     except Exception as e:  # noqa: BLE001 - surfaced on the handle
                         fail(chunk, e)
+                t1 = time.perf_counter()
                 for chunk, tok in tokens:
                     try:
                         collect(chunk, self.executor.complete(tok))
                     except Exception as e:  # noqa: BLE001
                         fail(chunk, e)
+                self.stats["submit_s"] += t1 - t0
+                self.stats["complete_s"] += time.perf_counter() - t1
         else:
             for chunk in chunks:
                 try:
