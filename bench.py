@@ -15,10 +15,11 @@ Reported (rank 0, one JSON line):
   value   aggregate P->D KV transfer GB/s: KV bytes moved by all pairs over
           the summed device time of the kernels that move them (max over
           prefill ranks), CUDA events around each kernel. With the default
-          ``--engine fused`` that kernel is the per-layer RoPE + KV write,
-          which stores the layer's K/V straight into the decode pool (its
-          time includes the RoPE of the query heads); with ``tma``/``tile``
-          it is a separate copy kernel per layer on a side stream.
+          ``--engine fused`` that kernel is the per-layer RoPE + KV launch
+          over the K/V heads, which rotates K and stores the layer's K/V
+          straight into the decode pool (the query heads are rotated by a
+          second launch, outside the timed kernel); with ``tma``/``tile`` it
+          is a separate copy kernel per layer on a side stream.
   ttft_p50_ms  p50 over requests of the device time from the wave start to
           the request's KV + first token landing in the decode pool.
   e2e     the same KV bytes over the whole step, timed per rank from before

@@ -58,14 +58,14 @@ def rope_push_section(args, rank, local, remote, cfg, pool_blocks, timed, rng) -
     hog_a = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
     hog_b = torch.empty_like(hog_a)
     nbytes = T * 2 * args.heads * 128 * 2 * args.layers
-    for busy in (False, True):
+    for heads, busy in (("kv", False), ("kv", True), ("all", False)):
         def fn():
             if rank == 0:
                 for l in range(args.layers):
                     rk = remote.layer_base(l)
                     llama_ops.rope_kv_push(qkv, pos, cs, hq, args.heads, None,
                                            (rk, rk + remote.outer_stride, remote.block_stride, remote.token_stride,
-                                            remote.head_stride, 16, rslots))
+                                            remote.head_stride, 16, rslots), heads=heads)
             elif busy:
                 for _ in range(24):  # ~8 ms of 1 GiB copies: the decode GPU's HBM stays loaded meanwhile
                     hog_b.copy_(hog_a)
@@ -84,7 +84,7 @@ def rope_push_section(args, rank, local, remote, cfg, pool_blocks, timed, rng) -
         both = [None, None]
         dist.all_gather_object(both, sorted(ts)[len(ts) // 2], group=gloo_of(args))
         ms = both[0]  # the pushing rank's device time
-        r = {"path": "rope_push", "decode_gpu": "streaming_hbm" if busy else "idle", "tokens": T,
+        r = {"path": "rope_push", "heads": heads, "decode_gpu": "streaming_hbm" if busy else "idle", "tokens": T,
              "layers": args.layers, "bytes": nbytes, "ms": round(ms, 4), "gbps": round(nbytes / ms / 1e6, 1),
              "frac_of_peer_copy": round(nbytes / ms / 1e6 / PEER_COPY_GBPS, 3)}
         out.append(r)

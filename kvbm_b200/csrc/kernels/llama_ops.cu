@@ -185,6 +185,8 @@ struct RopeKvParams {
   int group;          // head pairs per work item
   int q_per_kv;       // query pairs visited after each K/V pair (0: K/V pairs first)
   __nv_bfloat16* q_out;  // optional [T, Hq, 128]: rotated query rows go here instead of back into qkv
+  int pair_base;      // head-pair subset in K,V-first order: [pair_base, pair_base + npairs)
+  int npairs;         // 0: all pairs
   FastDiv pairs_div;  // divides by the number of groups per token
   FastDiv page_div;
   FastDiv r_page_div;
@@ -211,7 +213,7 @@ __global__ void __launch_bounds__(256) rope_kv_fused_kernel(const __grid_constan
   const int hl = lane & 15;  // lane within the half-warp: elements [8*hl, 8*hl+8)
   const int half = lane >> 4;
   const int H = P.Hq + 2 * P.Hkv;
-  const int pairs = (H + 1) >> 1;
+  const int pairs = P.npairs > 0 ? P.npairs : (H + 1) >> 1;
   const int groups = static_cast<int>(P.pairs_div.d);  // head-pair groups per token
   const uint32_t items = static_cast<uint32_t>(P.T) * static_cast<uint32_t>(groups);
   const uint32_t stride = gridDim.x * (blockDim.x >> 5);
@@ -250,10 +252,10 @@ __global__ void __launch_bounds__(256) rope_kv_fused_kernel(const __grid_constan
           const int b = j / (P.q_per_kv + 1), r = j - b * (P.q_per_kv + 1);
           h = (r == 0 ? P.Hq + 2 * b : 2 * (b * P.q_per_kv + r - 1)) + half;
         } else {
-          h = 2 * j + half + P.Hq;
+          h = 2 * (P.pair_base + j) + half + P.Hq;
           if (h >= H) h -= H;
         }
-        const bool valid = j < j_end && h < H && (P.q_per_kv > 0 || 2 * j + half < H);
+        const bool valid = j < j_end && h < H && (P.q_per_kv > 0 || 2 * (P.pair_base + j) + half < H);
         hh[u] = valid ? h : -1;
         x[u] = valid ? *reinterpret_cast<const int4*>(trow + static_cast<int64_t>(h) * 128) : make_int4(0, 0, 0, 0);
       }
@@ -553,7 +555,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 int launch_rope_fused(RopeKvParams& P, cudaStream_t stream) {
   const int H = P.Hq + 2 * P.Hkv;
-  const int pairs = (H + 1) / 2;
+  const int pairs = P.npairs > 0 ? P.npairs : (H + 1) / 2;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -563,7 +565,7 @@ int launch_rope_fused(RopeKvParams& P, cudaStream_t stream) {
   int groups = 1;
   while (groups < groups_max && static_cast<int64_t>(P.T) * groups < int64_t{sms} * 64) groups *= 2;
   groups = std::min(groups, groups_max);
-  P.q_per_kv = (P.Hq % 2 == 0 && P.Hkv > 0 && (P.Hq / 2) % P.Hkv == 0) ? (P.Hq / 2) / P.Hkv : 0;
+  P.q_per_kv = (P.npairs == 0 && P.Hq % 2 == 0 && P.Hkv > 0 && (P.Hq / 2) % P.Hkv == 0) ? (P.Hq / 2) / P.Hkv : 0;
   P.group = (pairs + groups - 1) / groups;
   groups = (pairs + P.group - 1) / P.group;
   const int64_t items = static_cast<int64_t>(P.T) * groups;
@@ -645,14 +647,33 @@ extern "C" int kvbm_rope_kv_write_qout(void* qkv, int64_t tokens, int hq, int hk
   return launch_rope_fused(P, stream);
 }
 
+// Head subsets for kvbm_rope_kv_push_heads: 0 = every head, 1 = the K and
+// V heads only (requires an even Hq), 2 = the query heads only.
+namespace {
+int set_subset(RopeKvParams& P, int subset) {
+  if (subset == 0) return cudaSuccess;
+  if (P.Hq % 2 != 0) return cudaErrorInvalidValue;
+  if (subset == 1) {
+    P.pair_base = 0;
+    P.npairs = P.Hkv;
+  } else if (subset == 2) {
+    P.pair_base = P.Hkv;
+    P.npairs = P.Hq / 2;
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return P.npairs > 0 ? cudaSuccess : cudaErrorInvalidValue;
+}
+}  // namespace
+
 // RoPE + KV write into the local cache (optional) and a second cache that
 // may be a peer GPU's (mapped through CUDA IPC or peer access); head_dim 128.
-extern "C" int kvbm_rope_kv_push(void* qkv, int64_t tokens, int hq, int hkv, const int32_t* positions,
-                                 const float* cos_sin, void* k_base, void* v_base, int64_t block_stride,
-                                 int64_t token_stride, int64_t head_stride, int page, const int64_t* slots,
-                                 void* rk_base, void* rv_base, int64_t r_block_stride, int64_t r_token_stride,
-                                 int64_t r_head_stride, int r_page, int r_head_offset, const int64_t* rslots,
-                                 cudaStream_t stream) {
+extern "C" int kvbm_rope_kv_push_heads(void* qkv, int64_t tokens, int hq, int hkv, const int32_t* positions,
+                                       const float* cos_sin, void* k_base, void* v_base, int64_t block_stride,
+                                       int64_t token_stride, int64_t head_stride, int page, const int64_t* slots,
+                                       void* rk_base, void* rv_base, int64_t r_block_stride, int64_t r_token_stride,
+                                       int64_t r_head_stride, int r_page, int r_head_offset, const int64_t* rslots,
+                                       int subset, cudaStream_t stream) {
   if (tokens == 0) return cudaSuccess;
   if (!qkv || !positions || !cos_sin || !aligned16(qkv) || !aligned16(cos_sin)) return cudaErrorInvalidValue;
   if (slots && !cache_ok(k_base, v_base, block_stride, token_stride, head_stride, page)) return cudaErrorInvalidValue;
@@ -681,7 +702,20 @@ extern "C" int kvbm_rope_kv_push(void* qkv, int64_t tokens, int hq, int hkv, con
   P.r_page = r_page;
   P.r_head_offset = r_head_offset;
   P.rslots = rslots;
+  const int e = set_subset(P, subset);
+  if (e != cudaSuccess) return e;
   return launch_rope_fused(P, stream);
+}
+
+extern "C" int kvbm_rope_kv_push(void* qkv, int64_t tokens, int hq, int hkv, const int32_t* positions,
+                                 const float* cos_sin, void* k_base, void* v_base, int64_t block_stride,
+                                 int64_t token_stride, int64_t head_stride, int page, const int64_t* slots,
+                                 void* rk_base, void* rv_base, int64_t r_block_stride, int64_t r_token_stride,
+                                 int64_t r_head_stride, int r_page, int r_head_offset, const int64_t* rslots,
+                                 cudaStream_t stream) {
+  return kvbm_rope_kv_push_heads(qkv, tokens, hq, hkv, positions, cos_sin, k_base, v_base, block_stride,
+                                 token_stride, head_stride, page, slots, rk_base, rv_base, r_block_stride,
+                                 r_token_stride, r_head_stride, r_page, r_head_offset, rslots, 0, stream);
 }
 
 extern "C" int kvbm_silu_mul(const void* gate_up, void* out, int64_t tokens, int inter, cudaStream_t stream) {

@@ -72,9 +72,12 @@ class KvPush:
 
     ``remote`` is the decode instance's pool (mapped through CUDA IPC when it
     is on another GPU); ``block_ids`` (int32, device) are its blocks for the
-    request, one per ``page`` tokens. With ``timers`` set, each layer's
-    kernel is bracketed by CUDA events and ``(start, end, kv_bytes)`` is
-    appended, so callers can report the device time of the transfer.
+    request, one per ``page`` tokens. Each layer is two launches of the
+    RoPE/KV kernel: the K/V heads (rotated K and V stored into ``remote``,
+    K rotated in place for the attention) and then the query heads. With
+    ``timers`` set, the K/V launch is bracketed by CUDA events and
+    ``(start, end, kv_bytes)`` appended, so callers can report the device
+    time of the transfer.
     """
 
     def __init__(self, remote: KvLayout, block_ids: torch.Tensor, *, start_pos: int = 0, head_offset: int = 0,
@@ -100,14 +103,17 @@ class KvPush:
         remote = (rk, rk + r.outer_stride, r.block_stride, r.token_stride, r.head_stride, r.config.page_size,
                   self.slots(pos))
         ev = None
+        split = c.heads % 2 == 0  # K/V heads in their own launch, query heads after it
         if self.timers is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
         llama_ops.rope_kv_push(qkv, pos, model.cos_sin, c.heads, c.kv_heads, local if self.local_write else None,
-                               remote, r_head_offset=self.head_offset)
+                               remote, r_head_offset=self.head_offset, heads="kv" if split else "all")
         if ev is not None:
             ev[1].record()
             self.timers.append((ev[0], ev[1], qkv.shape[0] * 2 * c.kv_heads * c.head_dim * 2))
+        if split:
+            llama_ops.rope_kv_push(qkv, pos, model.cos_sin, c.heads, c.kv_heads, None, None, heads="q")
 
 
 class LlamaModel:

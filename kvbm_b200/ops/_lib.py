@@ -90,6 +90,11 @@ _SIGS = {
         [_VP, _I64, _INT, _INT, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _INT, _VP, _VP, _VP, _I64, _I64, _I64, _INT,
          _INT, _VP, _VP],
     ),
+    "kvbm_rope_kv_push_heads": (
+        _INT,
+        [_VP, _I64, _INT, _INT, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _INT, _VP, _VP, _VP, _I64, _I64, _I64, _INT,
+         _INT, _VP, _INT, _VP],
+    ),
     "kvbm_rope_kv_write_qout": (
         _INT,
         [_VP, _I64, _INT, _INT, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _INT, _VP, _VP, _VP],
@@ -137,7 +142,7 @@ _KERNELS_PER_CALL = {
     "kvbm_kv_tile_xfer": 1, "kvbm_kv_chunk_xfer_tma": 1, "kvbm_copy_pairs": 1, "kvbm_universal_from_block": 1,
     "kvbm_block_from_universal": 1, "kvbm_nhd_hnd_transpose": 1, "kvbm_signal_flag": 1, "kvbm_wait_flag": 1,
     "kvbm_signal_flag_payload": 1, "kvbm_wait_flags_all": 1, "kvbm_rmsnorm": 1, "kvbm_rope_kv_write": 1,
-    "kvbm_rope_kv_push": 1, "kvbm_rope_kv_write_qout": 1,
+    "kvbm_rope_kv_push": 1, "kvbm_rope_kv_write_qout": 1, "kvbm_rope_kv_push_heads": 1,
     "kvbm_silu_mul": 1, "kvbm_paged_decode_attn": 2, "kvbm_paged_decode_attn_simt": 2,
 }
 _launches = 0

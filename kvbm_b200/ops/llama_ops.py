@@ -46,25 +46,31 @@ def rope_kv_write_qout(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torc
     return q_out
 
 
+_SUBSETS = {"all": 0, "kv": 1, "q": 2}
+
+
 def rope_kv_push(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, hq: int, hkv: int,
-                 local: tuple | None, remote: tuple, r_head_offset: int = 0, stream=None) -> None:
-    """RoPE + KV write into ``local`` (optional) and ``remote`` paged caches in one kernel (head_dim 128).
+                 local: tuple | None, remote: tuple | None, r_head_offset: int = 0, heads: str = "all",
+                 stream=None) -> None:
+    """RoPE + KV write into ``local`` (optional) and ``remote`` (optional) paged caches in one kernel.
 
     Each cache is ``(k_base, v_base, block_stride, token_stride, head_stride,
     page, slots)`` with ``slots`` an int64 [T] tensor of block*page+offset
     (negative: skip). The remote cache may be a peer GPU's memory; its heads
     start at ``r_head_offset`` (a decode rank holding more KV heads than this
-    prefill rank).
+    prefill rank). ``heads`` restricts the launch to the K/V heads (``"kv"``:
+    the part that moves KV) or the query heads (``"q"``). head_dim 128.
     """
     T = qkv.shape[0]
     if qkv.shape[-1] != 128:
         raise ValueError("rope_kv_push needs head_dim 128")
     lk = local or (0, 0, 0, 0, 0, 0, None)
-    rk, rv, rbs, rts, rhs, rpage, rslots = remote
-    _lib.call("kvbm_rope_kv_push", qkv.data_ptr(), T, hq, hkv, positions.data_ptr(), cos_sin.data_ptr(),
+    rk = remote or (0, 0, 0, 0, 0, 0, None)
+    _lib.call("kvbm_rope_kv_push_heads", qkv.data_ptr(), T, hq, hkv, positions.data_ptr(), cos_sin.data_ptr(),
               lk[0] or None, lk[1] or None, lk[2], lk[3], lk[4], lk[5],
               lk[6].data_ptr() if lk[6] is not None else None,
-              rk or None, rv or None, rbs, rts, rhs, rpage, r_head_offset, rslots.data_ptr(), _stream(stream))
+              rk[0] or None, rk[1] or None, rk[2], rk[3], rk[4], rk[5], r_head_offset,
+              rk[6].data_ptr() if rk[6] is not None else None, _SUBSETS[heads], _stream(stream))
 
 
 def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:

@@ -73,8 +73,9 @@ def test_rope_kv_write_paged():
         assert torch.equal(view[b, 1, o], orig[t, hq + hkv:])
 
 
+@pytest.mark.parametrize("split", [False, True])
 @pytest.mark.parametrize("local_write", [False, True])
-def test_rope_kv_push_into_second_pool(local_write):
+def test_rope_kv_push_into_second_pool(local_write, split):
     """The fused kernel rotates q/k in place and stores K/V into a second
     (HND, wider-headed) pool at a head offset, optionally also the local one."""
     torch.manual_seed(3)
@@ -100,7 +101,10 @@ def test_rope_kv_push_into_second_pool(local_write):
                            (lk, lk + local.outer_stride, local.block_stride, local.token_stride, local.head_stride,
                             page, lslots) if local_write else None,
                            (rk, rk + remote.outer_stride, remote.block_stride, remote.token_stride,
-                            remote.head_stride, page, rslots), r_head_offset=hkv)
+                            remote.head_stride, page, rslots), r_head_offset=hkv, heads="kv" if split else "all")
+    if split:
+        assert torch.equal(qkv[:, :hq], orig[:, :hq])  # the K/V launch leaves the query heads alone
+        llama_ops.rope_kv_push(qkv, pos, cs, hq, hkv, None, None, heads="q")
     torch.cuda.synchronize()
     q_ref = _rope_ref(orig[:, :hq], pos.long(), cs)
     k_ref = _rope_ref(orig[:, hq:hq + hkv], pos.long(), cs)
