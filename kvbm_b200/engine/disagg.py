@@ -43,7 +43,7 @@ class DisaggConfig:
     prompt_len: int = 8192
     gen_len: int = 256
     page_size: int = 16
-    engine: str = "tma"
+    engine: str = "fused"               # fused (RoPE/KV kernel pushes) | tma | tile (copy kernel per layer)
     max_ctas: int = 0
     prefill_buffers: int = 2
     decode_splits: int | None = None
