@@ -56,8 +56,15 @@ def _h(x) -> int:
 class HubServer:
     def __init__(self, host: str = "127.0.0.1", port: int = 0, block_size: int = 16, max_seq_len: int = 0,
                  ttl: float = 30.0, features=("indexer", "p2p", "disagg", "prefill_router"),
-                 max_inflight_per_worker: int = 4, breaker: bool = True):
+                 max_inflight_per_worker: int = 4, breaker: bool = True, control_port: int | None = None,
+                 messenger_port: int | None = None, layout: str = "operational",
+                 advertise_host: str | None = None, g2_memory_gb: float = 0.0):
         self.host, self.port = host, port
+        # the control port serves health, metrics and the status page apart from
+        # the discovery / data routes (None: everything on the discovery port)
+        self.control_port = control_port
+        self.messenger_port = messenger_port
+        self.layout, self.advertise_host, self.g2_memory_gb = layout, advertise_host or host, g2_memory_gb
         self.block_size, self.max_seq_len = block_size, max_seq_len
         self.features = list(features)
         self.index = core.PositionalIndex(max_seq_len - max_seq_len % block_size, block_size)
@@ -119,7 +126,19 @@ class HubServer:
 
     async def _config(self, req):
         return web.json_response({"block_size": self.block_size, "max_seq_len": self.max_seq_len,
-                                  "features": self.features, "ttl": self.registry.ttl})
+                                  "features": self.features, "ttl": self.registry.ttl, "layout": self.layout,
+                                  "advertise_host": self.advertise_host, "g2_memory_gb": self.g2_memory_gb,
+                                  "control_port": self.control_port,
+                                  "messenger": self.messenger.address if self.messenger else None})
+
+    def control_app(self) -> web.Application:
+        a = web.Application()
+        a.router.add_get("/", self._index_page)
+        a.router.add_get("/health", self._health)
+        a.router.add_get("/v1/config", self._config)
+        a.router.add_get("/v1/metrics", self._metrics)
+        a.router.add_get("/v1/instances", self._list)
+        return a
 
     async def _register(self, req):
         d = await req.json()
@@ -269,6 +288,12 @@ class HubServer:
             site = web.TCPSite(self._runner, self.host, self.port)
             await site.start()
             self.port = site._server.sockets[0].getsockname()[1]
+            if self.control_port is not None:
+                self._control_runner = web.AppRunner(self.control_app())
+                await self._control_runner.setup()
+                csite = web.TCPSite(self._control_runner, self.host, self.control_port)
+                await csite.start()
+                self.control_port = csite._server.sockets[0].getsockname()[1]
             self._sweep_task = self._loop.create_task(self._sweeper())
             self._started.set()
 
@@ -276,7 +301,8 @@ class HubServer:
         self._loop.run_forever()
 
     def start(self) -> "HubServer":
-        self.messenger = Messenger()
+        bind = f"tcp://{self.host}:{self.messenger_port}" if self.messenger_port is not None else "tcp://127.0.0.1:0"
+        self.messenger = Messenger(bind=bind)
         if self.breaker is not None:
             self._ticker = BreakerTicker(self.breaker, self.selector)
         self._thread = threading.Thread(target=self._serve, daemon=True, name="kvbm-hub")
@@ -302,6 +328,8 @@ class HubServer:
                     except asyncio.CancelledError:
                         pass
                 await self._runner.cleanup()
+                if getattr(self, "_control_runner", None) is not None:
+                    await self._control_runner.cleanup()
             fut = asyncio.run_coroutine_threadsafe(shutdown(), self._loop)
             try:
                 fut.result(5)
@@ -323,9 +351,17 @@ def main(argv=None) -> None:
     p.add_argument("--max-seq-len", type=int, default=131072)
     p.add_argument("--ttl", type=float, default=30.0)
     p.add_argument("--features", default="indexer,p2p,disagg,prefill_router")
+    p.add_argument("--control-port", type=int, default=DEFAULT_CONTROL_PORT)
+    p.add_argument("--velo-port", "--messenger-port", dest="messenger_port", type=int, default=None,
+                   help="port of the hub's RPC messenger (prefill-router dispatch)")
+    p.add_argument("--layout", default="operational", choices=["operational", "universal"])
+    p.add_argument("--kv-index-advertise-host", default=None)
+    p.add_argument("--g2-memory", type=float, default=0.0, help="GB of host memory the hub reports for P2P staging")
     a = p.parse_args(argv)
-    hub = HubServer(a.host, a.discovery_port, a.block_size, a.max_seq_len, a.ttl, a.features.split(",")).start()
-    print(json.dumps({"hub": hub.url}), flush=True)
+    hub = HubServer(a.host, a.discovery_port, a.block_size, a.max_seq_len, a.ttl, a.features.split(","),
+                    control_port=a.control_port, messenger_port=a.messenger_port, layout=a.layout,
+                    advertise_host=a.kv_index_advertise_host, g2_memory_gb=a.g2_memory).start()
+    print(json.dumps({"hub": hub.url, "control": f"http://{a.host}:{hub.control_port}"}), flush=True)
     try:
         while True:
             time.sleep(3600)

@@ -243,3 +243,21 @@ def test_tier_journal_restores_g3_registrations(tmp_path):
     j2.close()
     with pytest.raises(RuntimeError):
         restore(g3, live)  # not a fresh pool
+
+
+def test_hub_control_port_and_cli_settings():
+    import requests
+
+    h = HubServer(max_seq_len=1024, control_port=0, layout="universal", advertise_host="10.0.0.7",
+                  g2_memory_gb=4.0).start()
+    try:
+        ctl = f"http://127.0.0.1:{h.control_port}"
+        assert h.control_port and h.control_port != h.port
+        assert requests.get(ctl + "/health", timeout=5).json()["status"] == "ok"
+        cfg = requests.get(h.url + "/v1/config", timeout=5).json()
+        assert cfg["layout"] == "universal" and cfg["advertise_host"] == "10.0.0.7" and cfg["g2_memory_gb"] == 4.0
+        assert cfg["messenger"].startswith("tcp://")
+        # registration and indexer routes are not on the control port
+        assert requests.post(ctl + "/v1/indexer/query", json={"hashes": []}, timeout=5).status_code == 404
+    finally:
+        h.stop()
