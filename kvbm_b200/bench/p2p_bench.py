@@ -58,7 +58,11 @@ def rope_push_section(args, rank, local, remote, cfg, pool_blocks, timed, rng) -
     hog_a = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
     hog_b = torch.empty_like(hog_a)
     nbytes = T * 2 * args.heads * 128 * 2 * args.layers
-    for heads, busy in (("kv", False), ("kv", True), ("all", False)):
+    cases = [("kv", False, 4), ("kv", True, 4), ("all", False, 4)] + [
+        (h, False, u) for u in args.rope_unrolls for h in ("kv", "all") if u != 4]
+    for heads, busy, unroll in cases:
+        llama_ops.set_rope_unroll(unroll)
+
         def fn():
             if rank == 0:
                 for l in range(args.layers):
@@ -84,12 +88,14 @@ def rope_push_section(args, rank, local, remote, cfg, pool_blocks, timed, rng) -
         both = [None, None]
         dist.all_gather_object(both, sorted(ts)[len(ts) // 2], group=gloo_of(args))
         ms = both[0]  # the pushing rank's device time
-        r = {"path": "rope_push", "heads": heads, "decode_gpu": "streaming_hbm" if busy else "idle", "tokens": T,
+        r = {"path": "rope_push", "heads": heads, "unroll": unroll, "decode_gpu": "streaming_hbm" if busy else "idle",
+             "tokens": T,
              "layers": args.layers, "bytes": nbytes, "ms": round(ms, 4), "gbps": round(nbytes / ms / 1e6, 1),
              "frac_of_peer_copy": round(nbytes / ms / 1e6 / PEER_COPY_GBPS, 3)}
         out.append(r)
         if rank == 0:
             print(json.dumps(r), flush=True)
+    llama_ops.set_rope_unroll(4)
     # copy-engine baseline: the RoPE kernel writes K/V into a local per-layer staging area, then one
     # cudaMemcpy2DAsync per layer moves the request's rows (K+V of one layer of a block are adjacent
     # in the fully contiguous layout) into consecutive destination blocks of the peer pool
@@ -141,8 +147,10 @@ def main(argv=None):
     p.add_argument("--rope-push", action="store_true",
                    help="also time the fused RoPE + KV push kernel (the bench's prefill path), with the decode "
                         "GPU idle and with it streaming HBM (a stand-in for decode)")
+    p.add_argument("--rope-unrolls", default="2,8", help="extra RoPE/KV kernel unroll depths to time")
     p.add_argument("--out", default=None)
     args = p.parse_args(argv)
+    args.rope_unrolls = [int(x) for x in args.rope_unrolls.split(",") if x]
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     assert world == 2

@@ -553,6 +553,8 @@ extern "C" int kvbm_rmsnorm(const void* x, void* residual, const void* weight, v
 namespace {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+int g_rope_unroll = kRopeUnroll;  // head pairs in flight per lane: 2, 4 (default) or 8
+
 int launch_rope_fused(RopeKvParams& P, cudaStream_t stream) {
   const int H = P.Hq + 2 * P.Hkv;
   const int pairs = P.npairs > 0 ? P.npairs : (H + 1) / 2;
@@ -561,7 +563,8 @@ int launch_rope_fused(RopeKvParams& P, cudaStream_t stream) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   // whole tokens per warp when there are enough tokens to fill the GPU,
   // otherwise split each token's heads over several warps (decode)
-  const int groups_max = (pairs + kRopeUnroll - 1) / kRopeUnroll;
+  const int unroll = g_rope_unroll;
+  const int groups_max = (pairs + unroll - 1) / unroll;
   int groups = 1;
   while (groups < groups_max && static_cast<int64_t>(P.T) * groups < int64_t{sms} * 64) groups *= 2;
   groups = std::min(groups, groups_max);
@@ -576,7 +579,11 @@ int launch_rope_fused(RopeKvParams& P, cudaStream_t stream) {
   const int64_t ctas = (items + 7) / 8;
   // one item per warp (a grid capped at one resident wave measured 6% slower on prefill batches)
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ctas, int64_t{sms} * 32)));
-  rope_kv_fused_kernel<kRopeUnroll><<<grid, 256, 0, stream>>>(P);
+  switch (g_rope_unroll) {
+    case 2: rope_kv_fused_kernel<2><<<grid, 256, 0, stream>>>(P); break;
+    case 8: rope_kv_fused_kernel<8><<<grid, 256, 0, stream>>>(P); break;
+    default: rope_kv_fused_kernel<kRopeUnroll><<<grid, 256, 0, stream>>>(P); break;
+  }
   return cudaGetLastError();
 }
 
@@ -617,6 +624,16 @@ extern "C" int kvbm_rope_kv_write(void* qkv, int64_t tokens, int hq, int hkv, in
                                                  static_cast<uint8_t*>(v_base), block_stride, token_stride,
                                                  head_stride, page, slots);
   return cudaGetLastError();
+}
+
+// Head pairs each lane keeps in flight in the RoPE/KV kernel (2, 4 or 8; more
+// loads in flight cost registers and so resident warps). Returns the previous
+// value, or -1 for an unsupported one. For tuning; the default is 4.
+extern "C" int kvbm_rope_set_unroll(int unroll) {
+  if (unroll != 2 && unroll != 4 && unroll != 8) return -1;
+  const int prev = g_rope_unroll;
+  g_rope_unroll = unroll;
+  return prev;
 }
 
 // Decode form: RoPE + paged KV write, with the rotated query rows written to

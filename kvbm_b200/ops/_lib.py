@@ -99,6 +99,7 @@ _SIGS = {
         _INT,
         [_VP, _I64, _INT, _INT, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _INT, _VP, _VP, _VP],
     ),
+    "kvbm_rope_set_unroll": (_INT, [_INT]),
     "kvbm_silu_mul": (_INT, [_VP, _VP, _I64, _INT, _VP]),
     "kvbm_paged_decode_attn": (
         _INT,

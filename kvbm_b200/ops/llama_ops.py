@@ -73,6 +73,14 @@ def rope_kv_push(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tens
               rk[6].data_ptr() if rk[6] is not None else None, _SUBSETS[heads], _stream(stream))
 
 
+def set_rope_unroll(unroll: int) -> int:
+    """Head pairs per lane the RoPE/KV kernel keeps in flight (2, 4 or 8); returns the previous value."""
+    prev = int(_lib.load().kvbm_rope_set_unroll(int(unroll)))
+    if prev < 0:
+        raise ValueError("unroll must be 2, 4 or 8")
+    return prev
+
+
 def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     T = gate_up.numel() // gate_up.shape[-1]
     inter = gate_up.shape[-1] // 2
