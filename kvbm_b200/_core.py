@@ -49,10 +49,22 @@ def is_available() -> bool:
 class KvbmRuntime:
     def __init__(self, config: KvbmConfig, role: str):
         self.config, self.role = config, role
-        self.messenger = Messenger()
+        self.messenger = Messenger(bind=config.messenger.bind)
+        for iid, addr in (config.messenger.peers or {}).items():  # static discovery
+            self.messenger.register_peer(int(iid), addr)
         self.hub = None
+        self._registration = None
         if config.hub is not None and config.hub.url:
             self.hub = _hub_client.HubClient(config.hub.url)
+
+    def register_with_hub(self, features=("indexer", "p2p"), **info):
+        """Register this instance on the hub and keep it alive with heartbeats (until shutdown)."""
+        if self.hub is None:
+            raise RuntimeError("no hub configured (hub.url)")
+        self._registration = _hub_client.HubRegistration(
+            self.hub, self.messenger.instance_id, heartbeat_s=self.config.hub.heartbeat_secs,
+            features=list(features), address=self.messenger.address, role=self.role, **info)
+        return self._registration
 
     @classmethod
     def build_leader(cls, json_config: str | None = None) -> "KvbmRuntime":
@@ -72,6 +84,9 @@ class KvbmRuntime:
         self.messenger.register_peer(instance_id, address)
 
     def shutdown(self) -> None:
+        if self._registration is not None:
+            self._registration.close()
+            self._registration = None
         self.messenger.close()
 
 

@@ -261,3 +261,25 @@ def test_hub_control_port_and_cli_settings():
         assert requests.post(ctl + "/v1/indexer/query", json={"hashes": []}, timeout=5).status_code == 404
     finally:
         h.stop()
+
+
+def test_runtime_registers_with_hub_and_static_peers():
+    import json as _json
+
+    import kvbm._core as kc
+
+    h = HubServer(max_seq_len=1024).start()
+    try:
+        cfg = {"hub": {"url": h.url, "heartbeat_secs": 0.2},
+               "messenger": {"peers": {"77": "tcp://127.0.0.1:5999"}}}
+        rt = kc.KvbmRuntime.build_leader(_json.dumps(cfg))
+        try:
+            assert rt.messenger._peers[77] == "tcp://127.0.0.1:5999"
+            rt.register_with_hub(features=["indexer", "p2p"])
+            got = {int(i["instance_id"]): i for i in HubClient(h.url).instances()}
+            assert rt.messenger.instance_id in got and got[rt.messenger.instance_id]["address"] == rt.messenger.address
+        finally:
+            rt.shutdown()
+        assert rt.messenger.instance_id not in {int(i["instance_id"]) for i in HubClient(h.url).instances()}
+    finally:
+        h.stop()
