@@ -58,8 +58,9 @@ def main(argv=None) -> int:
     p.add_argument("--concurrency", type=int, default=32)
     p.add_argument("--prompt-len", type=int, default=8192)
     p.add_argument("--gen-len", type=int, default=256)
-    p.add_argument("--engine", default="fused", choices=["fused", "tma", "tile"],
-                   help="fused: the RoPE/KV kernel stores into the decode pool; tma/tile: a copy kernel per layer")
+    p.add_argument("--engine", default="fused", choices=["fused", "tma", "tile", "tma_inline", "tile_inline"],
+                   help="fused: the RoPE/KV kernel stores into the decode pool; tma/tile: a copy kernel per layer "
+                        "on a side stream; *_inline: that copy kernel in the prefill stream")
     p.add_argument("--max-ctas", type=int, default=0)
     p.add_argument("--layers", type=int, default=None, help="override layer count (debug only: invalid for the metric)")
     p.add_argument("--no-graphs", action="store_true")

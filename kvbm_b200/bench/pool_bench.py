@@ -5,7 +5,9 @@ lengths uniform in [512, 4096]; half of them start with one of 8 fixed
 1,024-token prefixes. For each request: hash its complete 16-token blocks,
 match the cached prefix, allocate the rest (evicting under pressure),
 register them, release everything. Reports the block hit rate, requests/s
-and blocks/s of the native pool, and checks the KV-event log (Create /
+and blocks/s through the framework's block handles (``BlockManager``) and
+through the native pool's batch calls (``native_batch``), and checks the
+KV-event log (Create /
 Remove per sequence hash, in order) against an independent pure-Python model
 of the same pool semantics (LRU eviction) - the "event-log equality" check.
 
@@ -108,6 +110,31 @@ def run_native(workload, blocks: int, backend: str = "lru"):
     return {"hit_rate": hits / max(1, total), "seconds": dt, "blocks": total, "events": log}
 
 
+def run_batch(workload, blocks: int, backend: str = "lru"):
+    """The same request loop on the native pool's batch calls (block ids, no Python block handles)."""
+    q = core.EventQueue(all_events=True)
+    pool = core.BlockPool(blocks, 16, backend, int(Tier.G2), core.Registry(events=q), "allow")
+    hits = total = 0
+    log = []
+    t0 = time.perf_counter()
+    for hashes in workload:
+        matched = pool.match_prefix(hashes)
+        need = hashes[len(matched):]
+        got = pool.allocate(len(need))
+        if got is None:
+            pool.release_many(matched)
+            continue
+        ids, _evicted = got
+        reg = pool.stage_and_register(ids, need)
+        pool.release_many(matched)
+        pool.release_many([bid for bid, _ in reg])
+        hits += len(matched)
+        total += len(hashes)
+        log.extend(q.drain())
+    dt = time.perf_counter() - t0
+    return {"hit_rate": hits / max(1, total), "seconds": dt, "blocks": total, "events": log}
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--blocks", type=int, default=65536)
@@ -126,6 +153,11 @@ def main(argv=None):
         hits = sum(max(0, model.process(h)) for h in wl)
         out["model_hit_rate"] = round(hits / sum(len(h) for h in wl), 4)
         out["event_log_equal"] = model.events == [(k, h) for k, h in nat["events"]]
+    bat = run_batch(wl, a.blocks, a.backend)
+    out["native_batch"] = {"requests_per_s": round(a.requests / bat["seconds"], 1),
+                           "blocks_per_s": round(bat["blocks"] / bat["seconds"], 1),
+                           "hit_rate": round(bat["hit_rate"], 4),
+                           "event_log_equal_to_handles": bat["events"] == nat["events"]}
     print(json.dumps(out))
     return out
 

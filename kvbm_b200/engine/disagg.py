@@ -43,7 +43,7 @@ class DisaggConfig:
     prompt_len: int = 8192
     gen_len: int = 256
     page_size: int = 16
-    engine: str = "fused"               # fused (RoPE/KV kernel pushes) | tma | tile (copy kernel per layer)
+    engine: str = "fused"  # fused (RoPE/KV kernel pushes) | tma | tile (side-stream copy) | tma_inline | tile_inline
     max_ctas: int = 0
     prefill_buffers: int = 2
     decode_splits: int | None = None
@@ -198,6 +198,11 @@ class PrefillInstance:
                     # the RoPE/KV kernel of every layer stores straight into the decode pool
                     push = KvPush(sender.remote, dst_ids, timers=sender._timers if sender.timing else None)
                     nxt = self.model.prefill(prompts[r], self.pool, src_ids, kv_push=push)
+                elif sender.engine.endswith("_inline"):
+                    # the copy kernel runs in the prefill stream between the layer's KV write and its next GEMM
+                    nxt = self.model.prefill(prompts[r], self.pool, src_ids,
+                                             on_layer_done=lambda l, s=src_ids, d=dst_ids: sender.send_layer(
+                                                 l, s, d, on_stream=stream))
                 else:
                     nxt = self.model.prefill(prompts[r], self.pool, src_ids,
                                              on_layer_done=lambda l, s=src_ids, d=dst_ids: sender.send_layer(

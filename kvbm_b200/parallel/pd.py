@@ -98,20 +98,30 @@ class PdSender:
 
     def send_layer(self, layer: int, src_ids: torch.Tensor, dst_ids: torch.Tensor,
                    after: torch.cuda.Stream | None = None, num_layers: int = 1, src_head_offset: int = 0,
-                   dst_head_offset: int = 0, num_heads: int | None = None) -> None:
-        """Transfer ``num_layers`` layers starting at ``layer`` once ``after``'s queued work is done."""
-        if after is not None:
+                   dst_head_offset: int = 0, num_heads: int | None = None,
+                   on_stream: torch.cuda.Stream | None = None) -> None:
+        """Transfer ``num_layers`` layers starting at ``layer`` once ``after``'s queued work is done.
+
+        By default the copy runs on this sender's high-priority side stream,
+        overlapping whatever ``after`` does next (and competing with it for
+        SMs). With ``on_stream`` it runs in that stream's order instead (the
+        prefill stream, between the layer's KV write and the next GEMM), so
+        it has the GPU to itself.
+        """
+        st = on_stream if on_stream is not None else self.stream
+        if after is not None and on_stream is None:
             self.stream.wait_stream(after)
-        with torch.cuda.stream(self.stream):
+        with torch.cuda.stream(st):
             if self.timing:
                 s = torch.cuda.Event(enable_timing=True)
                 e = torch.cuda.Event(enable_timing=True)
-                s.record(self.stream)
+                s.record(st)
             kv_ops.kv_transfer(self.local, src_ids, self.remote, dst_ids, layer_begin=layer, num_layers=num_layers,
                                src_head_offset=src_head_offset, dst_head_offset=dst_head_offset,
-                               num_heads=num_heads, engine=self.engine, max_ctas=self.max_ctas, stream=self.stream)
+                               num_heads=num_heads, engine=self.engine.removesuffix("_inline"),
+                               max_ctas=self.max_ctas, stream=st)
             if self.timing:
-                e.record(self.stream)
+                e.record(st)
                 nbytes = len(src_ids) * num_layers * self.bytes_per_layer_block
                 self._timers.append((s, e, nbytes))
 

@@ -35,7 +35,7 @@ def test_prefill_decode_matches_reference():
     _check_greedy(model, seq, T)
 
 
-@pytest.mark.parametrize("engine", ["fused", "tma"])
+@pytest.mark.parametrize("engine", ["fused", "tma", "tma_inline"])
 def test_colocated_wave_and_graphs(engine):
     cfg = DisaggConfig(model=LlamaConfig.tiny(layers=2), concurrency=3, prompt_len=80, gen_len=5, engine=engine)
     server = DisaggServer(cfg, "colocated", 0)
