@@ -4,8 +4,9 @@ The leader answers "how much of this sequence is cached below G1?" and
 decides onboards and offloads; its workers move the bytes.
 
 * ``find_matches`` walks the G2 pool (prefix match, references taken), then
-  continues in G3 from where G2 stopped. G3 hits are staged into G2 (disk ->
-  pinned) unless the staging mode says to only hold or prepare them.
+  continues in G3 from where G2 stopped, then in the object store (G4, an
+  ``engine.object_tier.ObjectTier``). G3 and G4 hits are staged into G2
+  unless the staging mode says to only hold or prepare them.
 * ``onboard`` copies matched G2 blocks into framework-owned G1 block ids on
   every worker (whole blocks, or layer by layer).
 * ``offload`` queues G1 blocks for the G1 -> G2 pipeline (and, by chaining,
@@ -104,7 +105,7 @@ class InstanceLeader:
         self.stats["g2_hits"] += len(res.g2_blocks)
         rest = seq_hashes[len(res.g2_blocks):]
         if self.g3 is None or not rest:
-            return res
+            return self._find_g4(res, rest, opts)
         if opts.staging == StagingMode.HOLD:
             n = self.g3.count_prefix(rest)
             self.stats["g3_hits"] += n
@@ -116,13 +117,26 @@ class InstanceLeader:
         g3_hits = self.g3.match_blocks(rest)
         self.stats["g3_hits"] += len(g3_hits)
         if not g3_hits:
-            return res
+            return self._find_g4(res, rest, opts)
         if opts.staging == StagingMode.PREPARE:
             res.g3_held = g3_hits
             res.status = OnboardingStatus.STAGING
             return res
-        res.g2_blocks += self.stage_g3_to_g2(g3_hits)
+        staged = self.stage_g3_to_g2(g3_hits)
+        res.g2_blocks += staged
         res.staged_from_g3 = len(g3_hits)
+        if len(staged) == len(g3_hits):
+            return self._find_g4(res, rest[len(g3_hits):], opts)
+        return res
+
+    def _find_g4(self, res: FindMatchesResult, rest: list[int], opts: FindMatchesOptions) -> FindMatchesResult:
+        """Continue a find in the object store (G4 -> G2) when one is attached and staging is FULL."""
+        if self.object_store is None or not rest or opts.staging != StagingMode.FULL:
+            return res
+        staged = self.object_store.stage(rest, self.g2)
+        self.stats["g4_hits"] = self.stats.get("g4_hits", 0) + len(staged)
+        res.g2_blocks += staged
+        res.staged_from_g4 = len(staged)  # type: ignore[attr-defined]
         return res
 
     def stage_g3_to_g2(self, g3_blocks: list[ImmutableBlock]) -> list[ImmutableBlock]:

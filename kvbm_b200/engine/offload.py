@@ -231,8 +231,15 @@ class OffloadPipeline:
                 if h.state == OffloadState.CANCELLED:
                     self.stats["cancelled"] += len(h.items)
                 else:
-                    with nvtx_range(f"kvbm.offload.{self.name}.policy"):
-                        kept = self.policy.filter(h.items)
+                    try:
+                        with nvtx_range(f"kvbm.offload.{self.name}.policy"):
+                            kept = self.policy.filter(h.items)
+                    except Exception as e:  # noqa: BLE001 - a broken policy fails the handle, not the thread
+                        h.error = e
+                        with h._lock:
+                            h._finish(OffloadState.FAILED)
+                        self.stats["failed"] += len(h.items)
+                        continue
                     h.skipped = [i.seq_hash for i in h.items if i not in kept]
                     self.stats["filtered"] += len(h.items) - len(kept)
                     if not self._await_precondition(h):
