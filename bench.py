@@ -62,6 +62,7 @@ def main(argv=None) -> int:
                    help="fused: the RoPE/KV kernel stores into the decode pool; tma/tile: a copy kernel per layer "
                         "on a side stream; *_inline: that copy kernel in the prefill stream")
     p.add_argument("--max-ctas", type=int, default=0)
+    p.add_argument("--layer-batch", type=int, default=1, help="copy engines: layers per transfer launch")
     p.add_argument("--layers", type=int, default=None, help="override layer count (debug only: invalid for the metric)")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--out", default=None)
@@ -95,7 +96,8 @@ def main(argv=None) -> int:
     if args.layers:
         mcfg = LlamaConfig(layers=args.layers)
     cfg = DisaggConfig(model=mcfg, concurrency=args.concurrency, prompt_len=args.prompt_len, gen_len=args.gen_len,
-                       engine=args.engine, max_ctas=args.max_ctas, use_graphs=not args.no_graphs)
+                       engine=args.engine, max_ctas=args.max_ctas, layer_batch=args.layer_batch,
+                       use_graphs=not args.no_graphs)
     half = world // 2
     if world == 1:
         role, peer = "colocated", None
@@ -197,6 +199,7 @@ def main(argv=None) -> int:
                 "gen_len": cfg.gen_len,
                 "parallelism": "colocated" if world == 1 else f"{pairs}P{pairs}D tp1",
                 "engine": cfg.engine,
+                "layer_batch": cfg.layer_batch if cfg.engine != "fused" else 1,
                 "prefill_attention": server.model.attention_backend,
                 "l2": "inputs larger than L2 (1 GiB KV per request, 16 GB weights)",
             },

@@ -45,6 +45,7 @@ class DisaggConfig:
     page_size: int = 16
     engine: str = "fused"  # fused (RoPE/KV kernel pushes) | tma | tile (side-stream copy) | tma_inline | tile_inline
     max_ctas: int = 0
+    layer_batch: int = 1   # copy engines: layers moved per transfer launch (fused pushes every layer)
     prefill_buffers: int = 2
     decode_splits: int | None = None
     use_graphs: bool = True
@@ -198,15 +199,22 @@ class PrefillInstance:
                     # the RoPE/KV kernel of every layer stores straight into the decode pool
                     push = KvPush(sender.remote, dst_ids, timers=sender._timers if sender.timing else None)
                     nxt = self.model.prefill(prompts[r], self.pool, src_ids, kv_push=push)
-                elif sender.engine.endswith("_inline"):
-                    # the copy kernel runs in the prefill stream between the layer's KV write and its next GEMM
-                    nxt = self.model.prefill(prompts[r], self.pool, src_ids,
-                                             on_layer_done=lambda l, s=src_ids, d=dst_ids: sender.send_layer(
-                                                 l, s, d, on_stream=stream))
                 else:
-                    nxt = self.model.prefill(prompts[r], self.pool, src_ids,
-                                             on_layer_done=lambda l, s=src_ids, d=dst_ids: sender.send_layer(
-                                                 l, s, d, after=stream))
+                    inline = sender.engine.endswith("_inline")
+                    nl, lb = self.model.cfg.layers, max(1, cfg.layer_batch)
+
+                    def done_layer(l, s=src_ids, d=dst_ids, inline=inline, nl=nl, lb=lb):
+                        # one copy launch per batch of lb layers, issued when its last layer is written;
+                        # inline: in the prefill stream (alone on the GPU), else on the side stream
+                        if (l + 1) % lb and l != nl - 1:
+                            return
+                        first = l - (l % lb)
+                        if inline:
+                            sender.send_layer(first, s, d, num_layers=l + 1 - first, on_stream=stream)
+                        else:
+                            sender.send_layer(first, s, d, num_layers=l + 1 - first, after=stream)
+
+                    nxt = self.model.prefill(prompts[r], self.pool, src_ids, on_layer_done=done_layer)
                 self.first_tok[r: r + 1].copy_(nxt)
                 sender.stream.wait_stream(stream)
                 done.append(sender.complete(slot_base + r, seq, payload=self.first_tok[r: r + 1]))
