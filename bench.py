@@ -4,10 +4,10 @@
     python bench.py --impl reference --gpus N ...          # the reference arm
 
 N=1 runs prefill and decode colocated on one GPU (two instances, two KV
-pools, KV moved by the same fused kernel into the local pool); N=2,4,8 run
-N/2 prefill:decode pairs (1P1D, 2P2D, 4P4D), one process per GPU, ranks
-[0, N/2) prefill and [N/2, N) decode, KV streamed layer by layer over NVLink
-by the fused P2P kernel. A step is one wave: ``concurrency`` requests of
+pools, KV moved by the same transfer kernel into the local pool); N=2,4,8
+run N/2 prefill:decode pairs (1P1D, 2P2D, 4P4D), one process per GPU, ranks
+[0, N/2) prefill and [N/2, N) decode, KV streamed in layer batches over
+NVLink by the P2P transfer kernel. A step is one wave: ``concurrency`` requests of
 ``prompt_len`` uniform-random tokens per pair, prefilled one after another,
 then decoded together for ``gen_len`` tokens. Weights are random-init bf16.
 
@@ -15,11 +15,15 @@ Reported (rank 0, one JSON line):
   value   aggregate P->D KV transfer GB/s: KV bytes moved by all pairs over
           the summed device time of the kernels that move them (max over
           prefill ranks), CUDA events around each kernel. With the default
-          ``--engine fused`` that kernel is the per-layer RoPE + KV launch
-          over the K/V heads, which rotates K and stores the layer's K/V
-          straight into the decode pool (the query heads are rotated by a
-          second launch, outside the timed kernel); with ``tma``/``tile`` it
-          is a separate copy kernel per layer on a side stream.
+          ``--engine tma_inline --layer-batch 8`` that kernel is the TMA
+          transfer kernel, launched in the prefill stream after every 8th
+          layer's KV write: bulk-async loads of the prefill pool's blocks
+          into shared memory, stores straight into the decode pool's blocks
+          over NVLink (layout transform / head slice / fp8 fused). With
+          ``fused`` it is the RoPE + KV launch over the K/V heads, which
+          stores each layer's K/V into the decode pool as it produces them;
+          ``tma``/``tile`` run the copy kernel on a side stream, concurrent
+          with the next GEMMs.
   ttft_p50_ms  p50 over requests of the device time from the wave start to
           the request's KV + first token landing in the decode pool.
   e2e     the same KV bytes over the whole step, timed per rank from before
@@ -58,11 +62,11 @@ def main(argv=None) -> int:
     p.add_argument("--concurrency", type=int, default=32)
     p.add_argument("--prompt-len", type=int, default=8192)
     p.add_argument("--gen-len", type=int, default=256)
-    p.add_argument("--engine", default="fused", choices=["fused", "tma", "tile", "tma_inline", "tile_inline"],
+    p.add_argument("--engine", default="tma_inline", choices=["fused", "tma", "tile", "tma_inline", "tile_inline"],
                    help="fused: the RoPE/KV kernel stores into the decode pool; tma/tile: a copy kernel per layer "
                         "on a side stream; *_inline: that copy kernel in the prefill stream")
     p.add_argument("--max-ctas", type=int, default=0)
-    p.add_argument("--layer-batch", type=int, default=1, help="copy engines: layers per transfer launch")
+    p.add_argument("--layer-batch", type=int, default=8, help="copy engines: layers per transfer launch")
     p.add_argument("--layers", type=int, default=None, help="override layer count (debug only: invalid for the metric)")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--out", default=None)
