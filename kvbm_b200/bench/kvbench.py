@@ -107,10 +107,14 @@ def run(args) -> list[dict]:
     n = nmax
     s_ids = torch.tensor(rng.sample(range(pool_blocks), n), dtype=torch.int32, device="cuda")
     d_ids = torch.tensor(rng.sample(range(pool_blocks), n), dtype=torch.int32, device="cuda")
+    cfg8 = LayoutConfig.for_model(pool_blocks, args.layers, args.heads, args.head_dim, args.page, torch.float8_e4m3fn)
     dsts = {
         "g1_to_g1_nhd_to_hnd": KvLayout.allocate(cfg, "layer_separate", KvBlockLayout.OPERATIONAL_HND),
         "g1_to_g1_copy": KvLayout.allocate(cfg, "fully_contiguous", nhd),
         "g1_to_g1_universal": KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.UNIVERSAL),
+        # bf16 -> fp8 e4m3 with one fp32 scale per (block, layer, K/V, head), NHD -> HND
+        "g1_to_g1_fp8_quant": KvLayout.allocate(cfg8, "fully_contiguous", KvBlockLayout.OPERATIONAL_HND,
+                                                fp8_scales=True),
     }
     for name, b in dsts.items():
         if args.d2d and name not in args.d2d.split(","):
@@ -119,10 +123,22 @@ def run(args) -> list[dict]:
             ms = _time(lambda: kv_ops.kv_transfer(a, s_ids, b, d_ids, engine=engine), args.iters, args.warmup,
                        flush)
             nbytes = n * cfg.bytes_per_block
+            moved = nbytes + n * b.config.bytes_per_block  # read + write (fp8 writes half)
             r = {"direction": name, "blocks": n, "bytes": nbytes, "engine": engine,
-                 "ms": round(ms, 4), "gbps_rw": round(2 * nbytes / ms / 1e6, 2)}
+                 "ms": round(ms, 4), "gbps_rw": round(moved / ms / 1e6, 2)}
             results.append(r)
             print(json.dumps(r), flush=True)
+        if name == "g1_to_g1_fp8_quant":
+            back = KvLayout.allocate(cfg, "fully_contiguous", nhd)
+            for engine in [e for e in ("tile", "tma") if e in args.engines.split(",")]:
+                ms = _time(lambda: kv_ops.kv_transfer(b, d_ids, back, s_ids, engine=engine), args.iters,
+                           args.warmup, flush)
+                nbytes = n * cfg.bytes_per_block
+                moved = nbytes + n * b.config.bytes_per_block
+                r = {"direction": "g1_to_g1_fp8_dequant", "blocks": n, "bytes": nbytes, "engine": engine,
+                     "ms": round(ms, 4), "gbps_rw": round(moved / ms / 1e6, 2)}
+                results.append(r)
+                print(json.dumps(r), flush=True)
         if name == "g1_to_g1_copy" and "ce" in args.engines.split(","):
             src_p = [a.layer_base(0) + int(x) * a.block_stride for x in s_ids.tolist()]
             dst_p = [b.layer_base(0) + int(x) * b.block_stride for x in d_ids.tolist()]
