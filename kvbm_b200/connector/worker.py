@@ -29,7 +29,6 @@ from __future__ import annotations
 import torch
 
 from ..engine.worker import Worker
-from ..logical.manager import Tier
 from ..physical.layout import KvLayout
 from ..physical.transfer import TransferOptions
 from ..utils.config import KvbmConfig

@@ -32,8 +32,8 @@ from .. import _core_native as core
 from ..models.llama import KvPush, LlamaConfig, LlamaModel
 from ..ops import llama_ops
 from ..ops import kv_ops
-from ..parallel.pd import WAIT_TIMEOUT_NS, Mailbox, MailboxDescriptor, PdSender
-from ..physical.layout import KvLayout, LayoutDescriptor
+from ..parallel.pd import WAIT_TIMEOUT_NS, Mailbox, PdSender
+from ..physical.layout import LayoutDescriptor
 
 
 @dataclass

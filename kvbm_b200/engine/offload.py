@@ -30,7 +30,7 @@ import enum
 import queue
 import threading
 import time
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import Callable, Sequence
 
 from ..logical.manager import BlockManager, ImmutableBlock, Tier

@@ -28,7 +28,7 @@ import torch
 
 from ..logical.manager import Tier
 from ..physical.layout import KvBlockLayout, KvLayout, LayoutConfig
-from ..physical.transfer import (DiskLayout, PhysicalLayout, SerializedLayouts, TransferCapabilities,
+from ..physical.transfer import (DiskLayout, SerializedLayouts, TransferCapabilities,
                                  TransferCompleteNotification, TransferManager, TransferOptions)
 
 
