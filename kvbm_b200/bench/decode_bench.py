@@ -72,13 +72,15 @@ def main(argv=None):
     # attention alone, all layers, same inputs
     q = torch.randn(B, cfg.heads, cfg.head_dim, device="cuda", dtype=torch.bfloat16)
     scratch = model.decode_scratch(B, splits)
+    counters = model.decode_counters(B)
     out = torch.empty_like(q)
 
     def attn():
         for l in range(cfg.layers):
             kb, vb = model.kv_bases(pool, l)
             llama_ops.paged_decode_attn(q, kb, vb, pool.block_stride, pool.token_stride, pool.head_stride, page,
-                                        table, seq, cfg.kv_heads, model.scale, splits, scratch=scratch, out=out)
+                                        table, seq, cfg.kv_heads, model.scale, splits, scratch=scratch, out=out,
+                                        counters=counters)
     for _ in range(2):
         attn()
     torch.cuda.synchronize()

@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_mma_kernel(
     const __nv_bfloat16* __restrict__ q, const uint8_t* __restrict__ k_base, const uint8_t* __restrict__ v_base,
     int64_t block_stride, int64_t token_stride, int64_t head_stride, int page, const int32_t* __restrict__ block_table,
     int max_blocks, const int32_t* __restrict__ seq_lens, float qscale, int splits, float* __restrict__ part_acc,
-    float* __restrict__ part_ml) {
+    float* __restrict__ part_ml, unsigned int* __restrict__ counters, __nv_bfloat16* __restrict__ out) {
   static_assert(GROUP == 1 || GROUP == 2 || GROUP == 4 || GROUP == 8, "GROUP must be 1, 2, 4 or 8");
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red_m[kWarps][8];
@@ -258,6 +258,35 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_mma_kernel(
       part_ml[row * 2 + 1] = L;
     }
   }
+  if (counters == nullptr) return;  // a separate combine kernel merges the splits
+
+  // ---- split combine in the last CTA of this (request, KV head) ----
+  // Every CTA publishes its partials (fence, then a ticket); the CTA that draws
+  // the last ticket merges all splits of its GROUP query heads and re-arms the
+  // counter for the next launch.
+  __shared__ unsigned int ticket;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) ticket = atomicAdd(&counters[static_cast<int64_t>(b) * Hkv + kvh], 1u);
+  __syncthreads();
+  if (ticket != static_cast<unsigned int>(splits - 1)) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < GROUP * kHD; i += blockDim.x) {
+    const int g = i / kHD, d = i - g * kHD;
+    const int64_t bh = static_cast<int64_t>(b) * Hq + kvh * GROUP + g;
+    float M = -INFINITY;
+    for (int sp = 0; sp < splits; ++sp) M = fmaxf(M, __ldcg(&part_ml[(bh * splits + sp) * 2]));
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+      for (int sp = 0; sp < splits; ++sp) {
+        const float f = exp2f(__ldcg(&part_ml[(bh * splits + sp) * 2]) - M);
+        L += __ldcg(&part_ml[(bh * splits + sp) * 2 + 1]) * f;
+        A += __ldcg(&part_acc[(bh * splits + sp) * kHD + d]) * f;
+      }
+    }
+    out[bh * kHD + d] = __float2bfloat16(L > 0.f ? A / L : 0.f);
+  }
+  if (threadIdx.x == 0) counters[static_cast<int64_t>(b) * Hkv + kvh] = 0u;
 }
 
 constexpr size_t kSmemBytes = static_cast<size_t>(kWarps) * kStages * kStageBytes;  // 96 KiB

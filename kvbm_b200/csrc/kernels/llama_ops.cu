@@ -801,13 +801,46 @@ extern "C" int kvbm_paged_decode_attn_simt(const void* q, const void* k_base, co
   return cudaGetLastError();
 }
 
+namespace {
+int decode_attn_mma(const void* q, const void* k_base, const void* v_base, int64_t block_stride,
+                    int64_t token_stride, int64_t head_stride, int page, const int32_t* block_table, int max_blocks,
+                    const int32_t* seq_lens, int batch, int hq, int hkv, int hd, float softmax_scale, int splits,
+                    float* part_acc, float* part_ml, unsigned int* counters, void* out, cudaStream_t stream);
+}  // namespace
+
 // Tensor-core paged decode attention (mma.sync + cp.async staging); falls
 // back to the SIMT kernel for shapes it does not cover. Same scratch layout.
+// Two launches: the split-KV kernel, then the combine kernel.
 extern "C" int kvbm_paged_decode_attn(const void* q, const void* k_base, const void* v_base, int64_t block_stride,
                                       int64_t token_stride, int64_t head_stride, int page, const int32_t* block_table,
                                       int max_blocks, const int32_t* seq_lens, int batch, int hq, int hkv, int hd,
                                       float softmax_scale, int splits, float* part_acc, float* part_ml, void* out,
                                       cudaStream_t stream) {
+  return decode_attn_mma(q, k_base, v_base, block_stride, token_stride, head_stride, page, block_table, max_blocks,
+                         seq_lens, batch, hq, hkv, hd, softmax_scale, splits, part_acc, part_ml, nullptr, out, stream);
+}
+
+// One launch: the split-KV kernel's last CTA per (request, KV head) merges the
+// splits itself. `counters` holds batch * hkv zero-initialised words; every
+// launch leaves them zero again, so one buffer serves every layer and every
+// replay of a captured graph. Shapes the tensor-core kernel does not cover
+// take the two-launch SIMT path.
+extern "C" int kvbm_paged_decode_attn_fused(const void* q, const void* k_base, const void* v_base,
+                                            int64_t block_stride, int64_t token_stride, int64_t head_stride, int page,
+                                            const int32_t* block_table, int max_blocks, const int32_t* seq_lens,
+                                            int batch, int hq, int hkv, int hd, float softmax_scale, int splits,
+                                            float* part_acc, float* part_ml, unsigned int* counters, void* out,
+                                            cudaStream_t stream) {
+  if (!counters) return cudaErrorInvalidValue;
+  return decode_attn_mma(q, k_base, v_base, block_stride, token_stride, head_stride, page, block_table, max_blocks,
+                         seq_lens, batch, hq, hkv, hd, softmax_scale, splits, part_acc, part_ml, counters, out, stream);
+}
+
+namespace {
+int decode_attn_mma(const void* q, const void* k_base, const void* v_base, int64_t block_stride,
+                    int64_t token_stride, int64_t head_stride, int page, const int32_t* block_table, int max_blocks,
+                    const int32_t* seq_lens, int batch, int hq, int hkv, int hd, float softmax_scale, int splits,
+                    float* part_acc, float* part_ml, unsigned int* counters, void* out, cudaStream_t stream) {
   const int group = hkv > 0 ? hq / hkv : 0;
   const bool mma_ok = hd == kvbm::attn::kHD && hkv > 0 && hq % hkv == 0 &&
                       (group == 1 || group == 2 || group == 4 || group == 8) && page % 16 == 0 &&
@@ -833,7 +866,7 @@ extern "C" int kvbm_paged_decode_attn(const void* q, const void* k_base, const v
   if (e != cudaSuccess) return e;                                                                                \
   kvbm::attn::paged_decode_mma_kernel<G><<<grid, kvbm::attn::kWarps * 32, smem, stream>>>(                      \
       qq, kb, vb, block_stride, token_stride, head_stride, page, block_table, max_blocks, seq_lens, qscale, splits, \
-      part_acc, part_ml);
+      part_acc, part_ml, counters, static_cast<__nv_bfloat16*>(out));
   switch (group) {
     case 1: KVBM_LAUNCH_MMA(1) break;
     case 2: KVBM_LAUNCH_MMA(2) break;
@@ -842,11 +875,12 @@ extern "C" int kvbm_paged_decode_attn(const void* q, const void* k_base, const v
   }
 #undef KVBM_LAUNCH_MMA
   e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || counters != nullptr) return e;
   attn_combine_kernel<<<static_cast<unsigned>(batch) * hq, kHD, 0, stream>>>(part_acc, part_ml, splits,
                                                                             static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }
+}  // namespace
 
 // ===========================================================================
 // Allocation-free paged decode attention.

@@ -151,6 +151,7 @@ class LlamaModel:
         self.cos_sin = torch.cat([f.cos(), f.sin()], dim=-1).float().to(self.device)
         self.scale = 1.0 / math.sqrt(c.head_dim)
         self._decode_scratch: torch.Tensor | None = None
+        self._decode_counters: torch.Tensor | None = None
         self._attn_backends: dict[bool, list] = {}
 
     # ------------------------------------------------------------ helpers
@@ -272,6 +273,13 @@ class LlamaModel:
             self._decode_scratch = torch.empty(need, dtype=torch.float32, device=self.device)
         return self._decode_scratch
 
+    def decode_counters(self, batch: int) -> torch.Tensor:
+        """Zeroed split-merge tickets for the attention kernel (it leaves them zero after every launch)."""
+        need = batch * self.cfg.kv_heads
+        if self._decode_counters is None or self._decode_counters.numel() < need:
+            self._decode_counters = torch.zeros(need, dtype=torch.int32, device=self.device)
+        return self._decode_counters
+
     @torch.inference_mode()
     def decode_step(self, tokens: torch.Tensor, positions: torch.Tensor, pool: KvLayout, block_table: torch.Tensor,
                     seq_lens: torch.Tensor, splits: int) -> torch.Tensor:
@@ -288,6 +296,7 @@ class LlamaModel:
         residual = x
         h = torch.empty_like(x)
         scratch = self.decode_scratch(B, splits)
+        counters = self.decode_counters(B)
         attn = torch.empty(B, c.heads, c.head_dim, device=self.device, dtype=self.dtype)
         q = torch.empty(B, c.heads, c.head_dim, device=self.device, dtype=self.dtype)
         for li, L in enumerate(self.layers):
@@ -306,7 +315,7 @@ class LlamaModel:
                 q.copy_(qkv[:, : c.heads])
             llama_ops.paged_decode_attn(q, kb, vb, pool.block_stride, pool.token_stride, pool.head_stride, page,
                                         block_table, seq_lens, c.kv_heads, self.scale, splits, scratch=scratch,
-                                        out=attn)
+                                        out=attn, counters=counters)
             x = F.linear(attn.view(B, c.q_size), L["wo"])
             llama_ops.rmsnorm(x, L["n2"], c.eps, residual=residual, out=h)
             x = F.linear(llama_ops.silu_mul(F.linear(h, L["wgu"])), L["wd"])

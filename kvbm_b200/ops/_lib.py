@@ -106,6 +106,11 @@ _SIGS = {
         [_VP, _VP, _VP, _I64, _I64, _I64, _INT, _VP, _INT, _VP, _INT, _INT, _INT, _INT, _F32, _INT, _VP, _VP, _VP,
          _VP],
     ),
+    "kvbm_paged_decode_attn_fused": (
+        _INT,
+        [_VP, _VP, _VP, _I64, _I64, _I64, _INT, _VP, _INT, _VP, _INT, _INT, _INT, _INT, _F32, _INT, _VP, _VP, _VP,
+         _VP, _VP],
+    ),
     "kvbm_paged_decode_attn_simt": (
         _INT,
         [_VP, _VP, _VP, _I64, _I64, _I64, _INT, _VP, _INT, _VP, _INT, _INT, _INT, _INT, _F32, _INT, _VP, _VP, _VP,
@@ -144,7 +149,7 @@ _KERNELS_PER_CALL = {
     "kvbm_block_from_universal": 1, "kvbm_nhd_hnd_transpose": 1, "kvbm_signal_flag": 1, "kvbm_wait_flag": 1,
     "kvbm_signal_flag_payload": 1, "kvbm_wait_flags_all": 1, "kvbm_rmsnorm": 1, "kvbm_rope_kv_write": 1,
     "kvbm_rope_kv_push": 1, "kvbm_rope_kv_write_qout": 1, "kvbm_rope_kv_push_heads": 1,
-    "kvbm_silu_mul": 1, "kvbm_paged_decode_attn": 2, "kvbm_paged_decode_attn_simt": 2,
+    "kvbm_silu_mul": 1, "kvbm_paged_decode_attn": 2, "kvbm_paged_decode_attn_fused": 1, "kvbm_paged_decode_attn_simt": 2,
 }
 _launches = 0
 

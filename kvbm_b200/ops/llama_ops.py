@@ -115,11 +115,14 @@ def decode_splits(batch: int, hkv: int, max_seq: int, page: int, sm_count: int =
 def paged_decode_attn(q: torch.Tensor, k_base: int, v_base: int, block_stride: int, token_stride: int,
                       head_stride: int, page: int, block_table: torch.Tensor, seq_lens: torch.Tensor, hkv: int,
                       softmax_scale: float, splits: int, scratch: torch.Tensor | None = None,
-                      out: torch.Tensor | None = None, stream=None, impl: str = "mma") -> torch.Tensor:
+                      out: torch.Tensor | None = None, stream=None, impl: str = "mma",
+                      counters: torch.Tensor | None = None) -> torch.Tensor:
     """Split-KV paged decode attention. q: [B, Hq, 128] bf16; returns [B, Hq, 128].
 
     ``impl="mma"``: tensor-core kernel (mma.sync, cp.async-staged K/V);
-    ``impl="simt"``: CUDA-core kernel (kept as the reference point)."""
+    ``impl="simt"``: CUDA-core kernel (kept as the reference point).
+    ``counters`` (int32, B * hkv zeros, reusable): the tensor-core kernel merges
+    the splits in its last CTA per (request, KV head) instead of a second launch."""
     B, Hq, hd = q.shape
     if out is None:
         out = torch.empty_like(q)
@@ -129,7 +132,13 @@ def paged_decode_attn(q: torch.Tensor, k_base: int, v_base: int, block_stride: i
         scratch = torch.empty(need, dtype=torch.float32, device=q.device)
     part_acc = scratch.data_ptr()
     part_ml = scratch.data_ptr() + rows * hd * 4
-    _lib.call("kvbm_paged_decode_attn" if impl == "mma" else "kvbm_paged_decode_attn_simt", q.data_ptr(), k_base, v_base, block_stride, token_stride, head_stride, page,
-              block_table.data_ptr(), block_table.shape[1], seq_lens.data_ptr(), B, Hq, hkv, hd,
-              float(softmax_scale), splits, part_acc, part_ml, out.data_ptr(), _stream(stream))
+    args = (q.data_ptr(), k_base, v_base, block_stride, token_stride, head_stride, page, block_table.data_ptr(),
+            block_table.shape[1], seq_lens.data_ptr(), B, Hq, hkv, hd, float(softmax_scale), splits, part_acc, part_ml)
+    if impl == "mma" and counters is not None:
+        if counters.dtype != torch.int32 or counters.numel() < B * hkv:
+            raise ValueError("counters must be int32 with at least batch * hkv entries")
+        _lib.call("kvbm_paged_decode_attn_fused", *args, counters.data_ptr(), out.data_ptr(), _stream(stream))
+    else:
+        _lib.call("kvbm_paged_decode_attn" if impl == "mma" else "kvbm_paged_decode_attn_simt", *args,
+                  out.data_ptr(), _stream(stream))
     return out

@@ -162,7 +162,7 @@ def test_silu_mul():
     torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
 
 
-@pytest.mark.parametrize("impl", ["mma", "simt"])
+@pytest.mark.parametrize("impl", ["mma", "simt", "mma_fused"])
 @pytest.mark.parametrize("group", [1, 4, 8])
 @pytest.mark.parametrize("splits", [1, 3, 8])
 def test_paged_decode_attention(group, splits, impl):
@@ -179,8 +179,18 @@ def test_paged_decode_attention(group, splits, impl):
     q = torch.randn(B, hq, hd, device="cuda", dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(hd)
     kb = pool.layer_base(0)
+    counters = torch.zeros(B * hkv, dtype=torch.int32, device="cuda") if impl == "mma_fused" else None
+    kind = "mma" if impl == "mma_fused" else impl
     out = llama_ops.paged_decode_attn(q, kb, kb + pool.outer_stride, pool.block_stride, pool.token_stride,
-                                      pool.head_stride, page, perm, seq, hkv, scale, splits, impl=impl)
+                                      pool.head_stride, page, perm, seq, hkv, scale, splits, impl=kind,
+                                      counters=counters)
+    if counters is not None:
+        # the tickets are re-armed: a second launch on the same buffer gives the same answer
+        again = llama_ops.paged_decode_attn(q, kb, kb + pool.outer_stride, pool.block_stride, pool.token_stride,
+                                            pool.head_stride, page, perm, seq, hkv, scale, splits, impl=kind,
+                                            counters=counters)
+        torch.cuda.synchronize()
+        assert not counters.any() and torch.equal(again, out)
     torch.cuda.synchronize()
     view = pool.layer_view(0)
     for b in range(B):
