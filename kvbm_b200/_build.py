@@ -34,6 +34,7 @@ CUDA_SOURCES = [
     CSRC / "kernels" / "kv_xfer.cu",
     CSRC / "kernels" / "llama_ops.cu",
     CSRC / "kernels" / "kvbm_mem.cu",
+    CSRC / "kernels" / "skinny_gemm_tc.cu",
 ]
 CUDA_HEADERS = [CSRC / "kernels" / "common.cuh", CSRC / "kernels" / "kvbm_kernels.h",
                 CSRC / "kernels" / "decode_attn_mma.cuh"]

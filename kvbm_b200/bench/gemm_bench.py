@@ -1,0 +1,79 @@
+"""Decode-projection GEMM microbenchmark: the tcgen05 skinny GEMM against
+cuBLAS (``torch.matmul``) on Llama-3-8B's weight shapes for a few batch rows.
+
+Each iteration writes a 256 MiB buffer first (L2 flush: the weights of one
+projection fit in the 126 MB L2), then times one GEMM with CUDA events. The
+GEMMs stream their weight once, so the figure of merit is the weight bytes
+per second against the measured copy bandwidth.
+
+    python -m kvbm_b200.bench.gemm_bench --batch 1,8,32,64,128
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from ..ops import llama_ops
+
+# (name, N, K) of Llama-3-8B: fused q/k/v, o, fused gate/up, down, lm_head
+SHAPES = [("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336),
+          ("lm_head", 128256, 4096)]
+
+
+def _time(fn, iters: int, flush: torch.Tensor) -> float:
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = []
+    for _ in range(iters):
+        flush.add_(1)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        best.append(s.elapsed_time(e))
+    best.sort()
+    return best[len(best) // 2]  # median
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--batch", default="1,8,32,64,128")
+    p.add_argument("--shapes", default=",".join(n for n, _, _ in SHAPES))
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--splits", default="0", help="comma list of split-K counts to try (0 = launcher's choice)")
+    args = p.parse_args(argv)
+    torch.cuda.set_device(0)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    want = set(args.shapes.split(","))
+    for name, N, K in SHAPES:
+        if name not in want:
+            continue
+        w = (torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / K ** 0.5).to(torch.bfloat16)
+        for M in (int(b) for b in args.batch.split(",")):
+            x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            ref = x @ w.t()
+            for _ in range(args.warmup):
+                torch.matmul(x, w.t(), out=out)
+            t_cublas = _time(lambda: torch.matmul(x, w.t(), out=out), args.iters, flush)
+            wbytes = N * K * 2
+            row = {"shape": name, "M": M, "N": N, "K": K, "cublas_us": round(t_cublas * 1e3, 2),
+                   "cublas_gbs": round(wbytes / t_cublas / 1e6, 1)}
+            for sp in (int(v) for v in args.splits.split(",")):
+                for _ in range(args.warmup):
+                    llama_ops.skinny_gemm(x, w, out=out, splits=sp)
+                t = _time(lambda: llama_ops.skinny_gemm(x, w, out=out, splits=sp), args.iters, flush)
+                err = (out.float() - ref.float()).abs().max().item()
+                key = f"tc{sp or llama_ops.skinny_gemm_splits(N, K)}"
+                row[key + "_us"] = round(t * 1e3, 2)
+                row[key + "_gbs"] = round(wbytes / t / 1e6, 1)
+                row[key + "_maxerr"] = round(err, 4)
+            row["status"] = llama_ops.skinny_gemm_status()
+            print(json.dumps(row), flush=True)
+
+
+if __name__ == "__main__":
+    main()

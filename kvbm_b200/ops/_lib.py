@@ -116,6 +116,9 @@ _SIGS = {
         [_VP, _VP, _VP, _I64, _I64, _I64, _INT, _VP, _INT, _VP, _INT, _INT, _INT, _INT, _F32, _INT, _VP, _VP, _VP,
          _VP],
     ),
+    "kvbm_skinny_gemm": (_INT, [_VP, _INT, _VP, _INT, _VP, _INT, _INT, _INT, _INT, _INT, _VP, _VP, _VP]),
+    "kvbm_skinny_gemm_splits": (_INT, [_INT, _INT]),
+    "kvbm_skinny_gemm_status": (_INT, [_INT]),
     "kvbm_device_alloc": (_INT, [_U64, C.POINTER(_VP)]),
     "kvbm_device_free": (_INT, [_VP]),
     "kvbm_memset_async": (_INT, [_VP, _INT, _U64, _VP]),
@@ -150,6 +153,7 @@ _KERNELS_PER_CALL = {
     "kvbm_signal_flag_payload": 1, "kvbm_wait_flags_all": 1, "kvbm_rmsnorm": 1, "kvbm_rope_kv_write": 1,
     "kvbm_rope_kv_push": 1, "kvbm_rope_kv_write_qout": 1, "kvbm_rope_kv_push_heads": 1,
     "kvbm_silu_mul": 1, "kvbm_paged_decode_attn": 2, "kvbm_paged_decode_attn_fused": 1, "kvbm_paged_decode_attn_simt": 2,
+    "kvbm_skinny_gemm": 1,
 }
 _launches = 0
 

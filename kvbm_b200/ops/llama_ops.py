@@ -142,3 +142,69 @@ def paged_decode_attn(q: torch.Tensor, k_base: int, v_base: int, block_stride: i
         _lib.call("kvbm_paged_decode_attn" if impl == "mma" else "kvbm_paged_decode_attn_simt", *args,
                   out.data_ptr(), _stream(stream))
     return out
+
+
+class GemmWorkspace:
+    """Split-K scratch of :func:`skinny_gemm`: an fp32 [M, N] sum and one ticket per
+    128-column tile, both zero between launches (the kernel re-zeroes what it used).
+
+    One workspace serves launches that run one after another; GEMMs that may run
+    at the same time (different streams) need one each."""
+
+    def __init__(self, device, elems: int = 0, tiles: int = 0):
+        self.device = torch.device(device)
+        self.ws = torch.zeros(max(elems, 1), dtype=torch.float32, device=self.device)
+        self.tickets = torch.zeros(max(tiles, 1), dtype=torch.int32, device=self.device)
+
+    def reserve(self, elems: int, tiles: int) -> None:
+        if self.ws.numel() < elems:
+            self.ws = torch.zeros(elems, dtype=torch.float32, device=self.device)
+        if self.tickets.numel() < tiles:
+            self.tickets = torch.zeros(tiles, dtype=torch.int32, device=self.device)
+
+
+_workspaces: dict[int, GemmWorkspace] = {}
+
+
+def skinny_gemm_splits(n: int, k: int) -> int:
+    """The split-K count :func:`skinny_gemm` uses by default for an [n, k] weight."""
+    return int(_lib.load().kvbm_skinny_gemm_splits(n, k))
+
+
+def skinny_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, splits: int = 0,
+                workspace: GemmWorkspace | None = None, stream=None) -> torch.Tensor:
+    """``out = x @ w.T`` for a few rows of x on the tcgen05 tensor cores (TMA-fed, TMEM accumulators).
+
+    x: [M, K] bf16 with M <= 128 (a decode batch), w: [N, K] bf16; both with unit
+    inner stride and 16-byte aligned rows. ``splits`` = split-K count (0: the
+    launcher's choice, which fills the SMs). Without ``workspace`` a per-device
+    one is used, so concurrent launches on several streams must pass their own."""
+    if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1]:
+        raise ValueError(f"skinny_gemm shapes {tuple(x.shape)} x {tuple(w.shape)}^T")
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("skinny_gemm takes bf16 operands")
+    if x.stride(1) != 1 or w.stride(1) != 1:
+        raise ValueError("skinny_gemm operands need unit inner stride")
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    elif out.shape != (M, N) or out.stride(1) != 1 or out.dtype != torch.bfloat16:
+        raise ValueError("skinny_gemm out must be bf16 [M, N] with unit inner stride")
+    if splits <= 0:
+        splits = skinny_gemm_splits(N, K)
+    if workspace is None:
+        dev = x.device.index if x.device.index is not None else torch.cuda.current_device()
+        workspace = _workspaces.get(dev)
+        if workspace is None:
+            workspace = _workspaces[dev] = GemmWorkspace(x.device)
+    if splits > 1:
+        workspace.reserve(M * N, -(-N // 128))
+    _lib.call("kvbm_skinny_gemm", x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
+              out.stride(0), M, N, K, splits, workspace.ws.data_ptr(), workspace.tickets.data_ptr(), _stream(stream))
+    return out
+
+
+def skinny_gemm_status(reset: bool = True) -> int:
+    """0, or the error a :func:`skinny_gemm` launch recorded (3: a pipeline wait timed out). Synchronizes."""
+    return int(_lib.load().kvbm_skinny_gemm_status(1 if reset else 0))

@@ -1,0 +1,63 @@
+"""GPU numerics of the tcgen05 skinny GEMM (y = x w^T) against a PyTorch fp32 matmul."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from kvbm_b200.ops import llama_ops
+
+
+def _check(M, N, K, splits, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16, generator=g)
+    w = (torch.randn(N, K, device="cuda", dtype=torch.bfloat16, generator=g) / K ** 0.5).to(torch.bfloat16)
+    ref = x.float() @ w.float().t()
+    y = llama_ops.skinny_gemm(x, w, splits=splits)
+    torch.cuda.synchronize()
+    assert llama_ops.skinny_gemm_status() == 0
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)
+    return x, w, ref
+
+
+@pytest.mark.parametrize("M,N,K,splits", [
+    (1, 128, 64, 1),        # one tile, one K chunk, BN = 16
+    (16, 256, 1024, 1),
+    (7, 384, 4096, 1),      # rows of x past M read as zeros
+    (32, 512, 4096, 4),     # split-K through the workspace, BN = 32
+    (33, 1000, 520, 1),     # N and K not multiples of the tile (BN = 64)
+    (33, 1000, 520, 3),
+    (128, 256, 2048, 2),    # BN = 128 (6-stage ring)
+])
+def test_skinny_gemm_matches_fp32(M, N, K, splits):
+    _check(M, N, K, splits)
+
+
+def test_skinny_gemm_default_splits_and_rearm():
+    # repeated split-K launches: the kernel leaves workspace and tickets zeroed
+    M, N, K = 32, 4096, 14336
+    s = llama_ops.skinny_gemm_splits(N, K)
+    assert s >= 1
+    x, w, ref = _check(M, N, K, 0, seed=1)
+    for _ in range(3):
+        y = llama_ops.skinny_gemm(x, w)
+    torch.cuda.synchronize()
+    assert llama_ops.skinny_gemm_status() == 0
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)
+    ws = llama_ops._workspaces[torch.cuda.current_device()]
+    assert int(ws.tickets.abs().sum()) == 0
+    assert float(ws.ws.abs().sum()) == 0.0
+
+
+def test_skinny_gemm_strided_operands():
+    # x rows taken from a wider buffer, output into a column slice of a wider buffer
+    M, N, K = 8, 640, 768
+    buf = torch.randn(M, K + 64, device="cuda", dtype=torch.bfloat16)
+    x = buf[:, 32:32 + K]
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / K ** 0.5
+    out = torch.zeros(M, N + 128, device="cuda", dtype=torch.bfloat16)
+    llama_ops.skinny_gemm(x, w.to(torch.bfloat16), out=out[:, 64:64 + N])
+    torch.cuda.synchronize()
+    ref = x.float() @ w.to(torch.bfloat16).float().t()
+    torch.testing.assert_close(out[:, 64:64 + N].float(), ref, rtol=2e-2, atol=2e-2)
+    assert float(out[:, :64].abs().sum()) == 0.0 and float(out[:, 64 + N:].abs().sum()) == 0.0
