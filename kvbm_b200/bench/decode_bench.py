@@ -27,12 +27,15 @@ def main(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--eager", action="store_true")
     p.add_argument("--splits", type=int, default=0)
+    p.add_argument("--gemm", default="cublas", choices=["cublas", "tc"],
+                   help="decode projections: cuBLAS or the tcgen05 skinny GEMM")
     p.add_argument("--profile", action="store_true",
                    help="bracket one extra eager step with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     args = p.parse_args(argv)
     torch.cuda.set_device(0)
     cfg = LlamaConfig(layers=args.layers)
     model = LlamaModel(cfg, "cuda")
+    model.decode_gemm = args.gemm
     page = 16
     bpr = math.ceil((args.ctx + 1) / page)
     pool = model.allocate_pool(args.batch * bpr + 1, page)
@@ -91,7 +94,7 @@ def main(argv=None):
     torch.cuda.synchronize()
     attn_ms = s.elapsed_time(e) / args.steps
     kv_bytes = cfg.layers * B * (args.ctx + 1) * 2 * cfg.kv_heads * cfg.head_dim * 2
-    print(json.dumps({"batch": B, "ctx": args.ctx, "splits": splits, "ms_per_step": round(ms, 3),
+    print(json.dumps({"batch": B, "ctx": args.ctx, "splits": splits, "gemm": args.gemm, "ms_per_step": round(ms, 3),
                       "attn_ms": round(attn_ms, 3), "attn_gbps": round(kv_bytes / attn_ms / 1e6, 1),
                       "weights_gb": round(cfg.num_params() * 2 / 1e9, 2)}))
 

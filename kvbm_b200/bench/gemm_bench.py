@@ -43,7 +43,7 @@ def main(argv=None):
     p.add_argument("--shapes", default=",".join(n for n, _, _ in SHAPES))
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--splits", default="0", help="comma list of split-K counts to try (0 = launcher's choice)")
+    p.add_argument("--ctas", default="0", help="comma list of persistent CTA counts to try (0 = one per SM)")
     args = p.parse_args(argv)
     torch.cuda.set_device(0)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
@@ -62,12 +62,12 @@ def main(argv=None):
             wbytes = N * K * 2
             row = {"shape": name, "M": M, "N": N, "K": K, "cublas_us": round(t_cublas * 1e3, 2),
                    "cublas_gbs": round(wbytes / t_cublas / 1e6, 1)}
-            for sp in (int(v) for v in args.splits.split(",")):
+            for nc in (int(v) for v in args.ctas.split(",")):
                 for _ in range(args.warmup):
-                    llama_ops.skinny_gemm(x, w, out=out, splits=sp)
-                t = _time(lambda: llama_ops.skinny_gemm(x, w, out=out, splits=sp), args.iters, flush)
+                    llama_ops.skinny_gemm(x, w, out=out, ctas=nc)
+                t = _time(lambda: llama_ops.skinny_gemm(x, w, out=out, ctas=nc), args.iters, flush)
                 err = (out.float() - ref.float()).abs().max().item()
-                key = f"tc{sp or llama_ops.skinny_gemm_splits(N, K)}"
+                key = f"tc{nc or 'sm'}"
                 row[key + "_us"] = round(t * 1e3, 2)
                 row[key + "_gbs"] = round(wbytes / t / 1e6, 1)
                 row[key + "_maxerr"] = round(err, 4)

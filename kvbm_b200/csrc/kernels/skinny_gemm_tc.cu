@@ -4,26 +4,36 @@
 // [N, K] - the projections of a decode step, which are bound by streaming W
 // once from HBM.
 //
-// Roles are swapped so the big operand fills the 128-row MMA: each CTA
-// computes D = W_tile X^T for 128 consecutive weight rows (UMMA M = 128)
-// against all tokens (UMMA N = BN, the token count rounded up to 16), with D
-// accumulating in TMEM (128 lanes x BN fp32 columns).
+// Roles are swapped so the big operand fills the 128-row MMA: a work unit is
+// one K chunk (64 elements) of one 128-row weight tile, and the MMA computes
+// D = W_tile X^T (UMMA M = 128, N = BN = the token count rounded up to 16)
+// into a TMEM accumulator of 128 lanes x BN fp32 columns.
 //
-// * TMA: per K chunk of 64 elements (128 bytes), one tiled 2-D bulk tensor
-//   load of the 128 x 64 weight tile and one of the BN x 64 activation tile,
-//   128-byte swizzled, into a ring of kStages shared-memory stages. Both are
-//   this GPU's own memory; no cluster multicast.
-// * MMA: one thread issues 4 tcgen05.mma (K = 16 each, the descriptor start
-//   advanced 32 bytes within the 128-byte swizzle atom) per stage and
-//   tcgen05.commit's the stage's "empty" mbarrier, so the producer refills a
-//   stage as soon as the tensor cores are done reading it.
-// * Split-K: grid = (N / 128) x splits. A single split writes bf16 directly;
-//   otherwise each split adds its fp32 tile into a workspace with red.add and
-//   the last split of a tile (ticket counter) converts the tile to bf16 and
-//   re-zeroes the workspace and counter for the next launch.
-// * Every mbarrier wait is bounded (%globaltimer); a CTA that gives up records
-//   kStatusPipelineTimeout in g_gemm_status, waits (bounded) for its own copies
-//   and MMAs, frees its TMEM and returns.
+// Persistent stream-K schedule: one CTA per SM; the tiles x chunks units are
+// cut into equal contiguous ranges, one per CTA, so every SM streams the same
+// number of weight bytes whatever N and K are (no wave quantisation, no split
+// count to tune). A CTA walks its range as segments (the part of one tile
+// inside the range). A segment that covers a whole tile stores bf16 directly;
+// partial segments add fp32 into a workspace with red.add, and the last
+// contributor of the tile (ticket counter) converts it to bf16 and re-zeroes
+// workspace and ticket for the next launch.
+//
+// Warp roles (192 threads):
+// * warp 0, one lane: TMA producer - per unit, a tiled 2-D bulk tensor load of
+//   the 128 x 64 weight tile and one of the BN x 64 activation tile (128-byte
+//   swizzle) into a ring of shared-memory stages. This GPU's own memory only;
+//   no cluster multicast.
+// * warp 1, one lane: MMA issuer - 4 tcgen05.mma (K = 16 each, descriptor
+//   start advanced 32 bytes inside the 128-byte swizzle atom) per unit, then
+//   tcgen05.commit to the stage's "empty" barrier; tcgen05.commit to the
+//   accumulator's "full" barrier after a segment's last unit. Two TMEM
+//   accumulators alternate between segments, so the next segment's MMAs run
+//   while the epilogue drains the previous one.
+// * warps 2-5: epilogue - tcgen05.ld (warp w reads TMEM lanes 32 (w % 4) ..
+//   +31), stores or red.add, ticket, conversion.
+// Every wait is bounded (%globaltimer) and also gives up when another role has
+// given up; the CTA then records kStatusPipelineTimeout in g_gemm_status, lets
+// its copies and MMAs drain (bounded), frees its TMEM and returns.
 #include "common.cuh"
 
 #include <cuda.h>
@@ -37,9 +47,10 @@ using namespace kvbm;
 
 namespace {
 
-constexpr int kThreads = 128;         // 4 warps: warp w reads TMEM lanes [32w, 32w + 32)
-constexpr int kTileN = 128;           // weight rows per CTA (UMMA M)
-constexpr int kChunkK = 64;           // K elements per stage (128 bytes of bf16: one swizzle atom row)
+constexpr int kThreads = 192;         // producer warp, MMA warp, 4 epilogue warps
+constexpr int kEpiThreads = 128;
+constexpr int kTileN = 128;           // weight rows per tile (UMMA M)
+constexpr int kChunkK = 64;           // K elements per unit (128 bytes of bf16: one swizzle atom row)
 constexpr uint64_t kWaitNs = 2000000000ull;
 
 // Ring depth: as many stages of (128 + BN) x 128 bytes as fit in ~200 KiB, at most 8.
@@ -111,14 +122,48 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | ((128u >> 4) << 24);
 }
 
+// Bounded mbarrier wait that also gives up once another role of the CTA has.
+KVBM_DEVICE bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      atomicExch(&g_gemm_status, kStatusPipelineTimeout);
+      return false;
+    }
+  }
+}
+
+KVBM_DEVICE void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
+
 struct GemmParams {
   int M, N, K;
-  int chunks_per_split;  // K chunks handled by one split
-  int splits;
-  __nv_bfloat16* y;      // [M, N] row stride ldy
+  int chunks;             // K chunks per tile
+  int tiles;              // 128-row weight tiles
+  int per;                // units per CTA
+  __nv_bfloat16* y;       // [M, N] row stride ldy
   int ldy;
-  float* ws;             // [M, N] fp32 zeros (splits > 1)
-  unsigned int* tickets;  // [N / 128] zeros (splits > 1)
+  float* ws;              // [M, N] fp32 zeros
+  unsigned int* tickets;  // [tiles] zeros
+};
+
+// The segments of CTA b's unit range, in order: tile, first and end chunk.
+struct SegIter {
+  int u, u1, chunks;
+  KVBM_DEVICE SegIter(const GemmParams& P, int b) : u(b * P.per), u1(min((b + 1) * P.per, P.tiles * P.chunks)),
+                                                    chunks(P.chunks) {}
+  KVBM_DEVICE bool next(int& tile, int& c0, int& c1) {
+    if (u >= u1) return false;
+    tile = u / chunks;
+    c0 = u - tile * chunks;
+    const int end = min(u1, (tile + 1) * chunks);
+    c1 = end - tile * chunks;
+    u = end;
+    return true;
+  }
 };
 
 template <int BN>
@@ -128,30 +173,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kBytesW = kTileN * kChunkK * 2;  // 16 KiB
   constexpr uint32_t kStageBytes = Ring<BN>::kStageBytes;
   constexpr int kStages = Ring<BN>::kStages;
-  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+  constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;  // two accumulators
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t full[kStages], empty[kStages], done;
+  __shared__ uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t tmem_base;
-  __shared__ int failed;
+  __shared__ volatile int abort_flag;
   __shared__ unsigned int ticket;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, split = blockIdx.y;
-  const int n0 = tile * kTileN;
-  const int kc0 = split * P.chunks_per_split;
-  const int total_chunks = (P.K + kChunkK - 1) / kChunkK;
-  const int nchunks = max(0, min(P.chunks_per_split, total_chunks - kc0));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(&done, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(&mma_done, 1);
     fence_mbar_init();
-    failed = 0;
+    abort_flag = 0;
   }
   if (warp == 0) {
     tmem_alloc(&tmem_base, kTmemCols);
@@ -162,104 +206,123 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_d = tmem_base;
 
-  // ---- producer + MMA issuer: one thread -----------------------------------
-  int issued = 0, consumed = 0;
-  if (threadIdx.x == 0 && nchunks > 0) {
-    bool ok = true;
-    auto produce = [&](int c) {
-      const int s = c % kStages;
-      uint8_t* st = smem + s * kStageBytes;
-      mbar_arrive_expect_tx(&full[s], kStageBytes);
-      tma_load_2d(st, &map_w, (kc0 + c) * kChunkK, n0, &full[s]);
-      tma_load_2d(st + kBytesW, &map_x, (kc0 + c) * kChunkK, 0, &full[s]);
-    };
-    for (; issued < min(kStages, nchunks); ++issued) produce(issued);
-    for (int c = 0; c < nchunks && ok; ++c) {
-      const int s = c % kStages;
-      if (!mbar_wait_bounded(&full[s], (c / kStages) & 1, kWaitNs)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint8_t* st = smem + s * kStageBytes;
-      const uint64_t da = smem_desc_k128(st), db = smem_desc_k128(st + kBytesW);
-#pragma unroll
-      for (int k = 0; k < kChunkK / 16; ++k)  // +32 bytes per K=16 step: +2 in 16-byte units
-        umma_bf16(tmem_d, da + 2 * k, db + 2 * k, idesc_bf16(BN), (c > 0 || k > 0) ? 1u : 0u);
-      umma_commit(&empty[s]);
-      consumed = c + 1;
-      if (issued < nchunks) {
-        // refill this stage once the MMAs above have read it
-        if (!mbar_wait_bounded(&empty[s], (c / kStages) & 1, kWaitNs)) {
-          ok = false;
-          break;
+  if (warp == 0) {
+    // ---- TMA producer ------------------------------------------------------
+    if (lane == 0) {
+      SegIter segs(P, blockIdx.x);
+      int tile, c0, c1, it = 0;
+      bool ok = true;
+      while (ok && segs.next(tile, c0, c1)) {
+        for (int c = c0; c < c1; ++c, ++it) {
+          const int s = it % kStages;
+          if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          tma_load_2d(st, &map_w, c * kChunkK, tile * kTileN, &full[s]);
+          tma_load_2d(st + kBytesW, &map_x, c * kChunkK, 0, &full[s]);
         }
-        produce(issued++);
       }
+      // every copy issued into this CTA's shared memory lands before the CTA leaves
+      for (int i = max(0, it - kStages); i < it; ++i)
+        mbar_wait_bounded(&full[i % kStages], (i / kStages) & 1, kWaitNs);
     }
-    if (ok) {
-      umma_commit(&done);
-    } else {
-      failed = 1;
-      atomicExch(&g_gemm_status, kStatusPipelineTimeout);
-      // let every copy issued into this CTA's shared memory land before leaving
-      for (int c = consumed; c < issued; ++c) mbar_wait_bounded(&full[c % kStages], (c / kStages) & 1, kWaitNs);
-      umma_commit(&done);
+  } else if (warp == 1) {
+    // ---- MMA issuer --------------------------------------------------------
+    if (lane == 0) {
+      SegIter segs(P, blockIdx.x);
+      int tile, c0, c1, it = 0, j = 0;
+      bool ok = true;
+      while (ok && segs.next(tile, c0, c1)) {
+        const int a = j & 1;
+        if (j >= 2 && !wait_or_abort(&acc_empty[a], ((j >> 1) - 1) & 1, &abort_flag)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem_d + a * BN;
+        for (int c = c0; c < c1; ++c, ++it) {
+          const int s = it % kStages;
+          if (!wait_or_abort(&full[s], (it / kStages) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* st = smem + s * kStageBytes;
+          const uint64_t da = smem_desc_k128(st), db = smem_desc_k128(st + kBytesW);
+#pragma unroll
+          for (int k = 0; k < kChunkK / 16; ++k)  // +32 bytes per K=16 step: +2 in 16-byte units
+            umma_bf16(acc, da + 2 * k, db + 2 * k, idesc_bf16(BN), (c > c0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[a]);
+        ++j;
+      }
+      // all MMAs complete before TMEM is freed
+      umma_commit(&mma_done);
+      mbar_wait_bounded(&mma_done, 0, kWaitNs);
     }
-  }
-  __syncthreads();
-
-  // ---- epilogue: TMEM -> registers -> Y (or the split-K workspace) ----------
-  bool mine = nchunks > 0 && !failed;
-  if (nchunks > 0 && !mbar_wait_bounded(&done, 0, kWaitNs)) {
-    mine = false;
-    atomicExch(&g_gemm_status, kStatusPipelineTimeout);
-  }
-  // tcgen05.ld is warp-collective: every thread takes the same branch
-  const bool have = __syncthreads_and(mine) != 0;
-  tc_fence_after();
-  const int row = n0 + warp * 32 + lane;  // weight row = output column of Y
-  if (have) {
+  } else {
+    // ---- epilogue: TMEM -> registers -> Y, or the workspace -----------------
+    const int lane_grp = warp & 3;  // TMEM lanes this warp may read
+    const int et = threadIdx.x - 64;
+    SegIter segs(P, blockIdx.x);
+    int tile, c0, c1, j = 0;
+    // every epilogue warp runs the same sequence of named barriers, aborted or not
+    while (segs.next(tile, c0, c1)) {
+      const int a = j & 1;
+      const bool ok = __all_sync(0xffffffffu, wait_or_abort(&acc_full[a], (j >> 1) & 1, &abort_flag));
+      const bool whole = c0 == 0 && c1 == P.chunks;
+      const int row = tile * kTileN + lane_grp * 32 + lane;  // weight row = output column of Y
+      if (ok) {  // warp-uniform: tcgen05.ld is warp-collective
+        tc_fence_after();
 #pragma unroll
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      float v[16];
-      tmem_ld16(tmem_d + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
-      if (row < P.N) {
+        for (int m0 = 0; m0 < BN; m0 += 16) {
+          float v[16];
+          tmem_ld16(tmem_d + (static_cast<uint32_t>(lane_grp * 32) << 16) + a * BN + m0, v);
+          if (row < P.N) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = c0 + j;
-          if (m < P.M) {
-            if (P.splits == 1)
-              P.y[static_cast<int64_t>(m) * P.ldy + row] = __float2bfloat16(v[j]);
-            else
-              atomicAdd(&P.ws[static_cast<int64_t>(m) * P.N + row], v[j]);
+            for (int i = 0; i < 16; ++i) {
+              const int m = m0 + i;
+              if (m < P.M) {
+                if (whole)
+                  P.y[static_cast<int64_t>(m) * P.ldy + row] = __float2bfloat16(v[i]);
+                else
+                  atomicAdd(&P.ws[static_cast<int64_t>(m) * P.N + row], v[i]);
+              }
+            }
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[a]);  // the MMA warp may reuse this accumulator
       }
+      if (!whole) {
+        // the tile's last contributor turns the fp32 sum into bf16 and re-arms the workspace
+        const int first = (tile * P.chunks) / P.per;
+        const int last = ((tile + 1) * P.chunks - 1) / P.per;
+        __threadfence();
+        epi_bar();
+        if (et == 0) ticket = abort_flag ? ~0u : atomicAdd(&P.tickets[tile], 1u);
+        epi_bar();
+        if (ticket == static_cast<unsigned int>(last - first)) {
+          __threadfence();
+          for (int idx = et; idx < P.M * kTileN; idx += kEpiThreads) {
+            const int m = idx / kTileN, r = tile * kTileN + idx % kTileN;
+            if (r < P.N) {
+              float* w = &P.ws[static_cast<int64_t>(m) * P.N + r];
+              P.y[static_cast<int64_t>(m) * P.ldy + r] = __float2bfloat16(__ldcg(w));
+              __stcg(w, 0.f);
+            }
+          }
+          if (et == 0) P.tickets[tile] = 0u;
+        }
+      }
+      ++j;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_d, kTmemCols);
-
-  if (P.splits > 1) {
-    // the last split of this tile turns the fp32 sum into bf16 and re-arms the workspace
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) ticket = atomicAdd(&P.tickets[tile], 1u);
-    __syncthreads();
-    if (ticket == static_cast<unsigned int>(P.splits - 1)) {
-      __threadfence();
-      if (row < P.N) {
-        for (int m = 0; m < P.M; ++m) {
-          float* w = &P.ws[static_cast<int64_t>(m) * P.N + row];
-          P.y[static_cast<int64_t>(m) * P.ldy + row] = __float2bfloat16(__ldcg(w));
-          *w = 0.f;
-        }
-      }
-      if (threadIdx.x == 0) P.tickets[tile] = 0u;
-    }
-  }
 }
 
 // ---- host side ------------------------------------------------------------------
@@ -301,7 +364,7 @@ int sm_count_cached() {
 }
 
 template <int BN>
-int launch(const CUtensorMap& mw, const CUtensorMap& mx, const GemmParams& P, int tiles, cudaStream_t stream) {
+int launch(const CUtensorMap& mw, const CUtensorMap& mx, const GemmParams& P, int grid, cudaStream_t stream) {
   constexpr size_t smem = 1024 + static_cast<size_t>(Ring<BN>::kStages) * Ring<BN>::kStageBytes;
   static int configured = -1;
   int dev = 0;
@@ -312,43 +375,27 @@ int launch(const CUtensorMap& mw, const CUtensorMap& mx, const GemmParams& P, in
     if (e != cudaSuccess) return e;
     configured = dev;
   }
-  skinny_gemm_tc_kernel<BN><<<dim3(tiles, P.splits), kThreads, smem, stream>>>(mw, mx, P);
+  skinny_gemm_tc_kernel<BN><<<grid, kThreads, smem, stream>>>(mw, mx, P);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-// Split count the launcher would use for an (N, K) weight on this GPU.
-extern "C" int kvbm_skinny_gemm_splits(int n, int k) {
-  const int tiles = (n + kTileN - 1) / kTileN;
-  const int chunks = (k + kChunkK - 1) / kChunkK;
-  const int sms = sm_count_cached();  // one CTA per SM is resident (the ring takes most of shared memory)
-  // time ~ waves of CTAs x K chunks per CTA; the fewest splits that minimise it, >= 4 chunks each
-  int best = 1;
-  long best_cost = -1;
-  for (int s = 1; s <= 16 && (chunks + s - 1) / s >= 4; ++s) {
-    const long waves = (static_cast<long>(tiles) * s + sms - 1) / sms;
-    const long cost = waves * ((chunks + s - 1) / s);
-    if (best_cost < 0 || cost < best_cost) {
-      best = s;
-      best_cost = cost;
-    }
-  }
-  return best;
-}
+// Number of persistent CTAs a launch uses by default (one per SM).
+extern "C" int kvbm_skinny_gemm_ctas() { return sm_count_cached(); }
 
 // Y[M, N] (row stride ldy) = X[M, K] (row stride ldx) * W[N, K]^T (row stride ldw).
-// bf16, M <= 128, K % 8 == 0, all base pointers and row strides 16-byte aligned.
-// With splits > 1, `ws` is an fp32 [M, N] buffer of zeros and `tickets`
-// (N / 128 rounded up) 32-bit zeros; the kernel leaves both zeroed again.
+// bf16, M <= 128, K % 8 == 0, x and w 16-byte aligned, ldx and ldw multiples
+// of 8. `ctas` persistent CTAs (<= 0: one per SM). `ws` is an fp32 [M, N]
+// buffer of zeros and `tickets` (N / 128 rounded up) 32-bit zeros; the kernel
+// leaves both zeroed again.
 extern "C" int kvbm_skinny_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy, int M, int N, int K,
-                                int splits, float* ws, unsigned int* tickets, cudaStream_t stream) {
+                                int ctas, float* ws, unsigned int* tickets, cudaStream_t stream) {
   if (M == 0 || N == 0) return cudaSuccess;
-  if (!x || !w || !y || M < 0 || M > 128 || N < 0 || K <= 0 || K % 8 != 0) return cudaErrorInvalidValue;
+  if (!x || !w || !y || !ws || !tickets || M < 0 || M > 128 || N < 0 || K <= 0 || K % 8 != 0)
+    return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) return cudaErrorInvalidValue;
   if ((ldx % 8) || (ldw % 8) || ldx < K || ldw < K || ldy < N) return cudaErrorInvalidValue;
-  if (splits <= 0) splits = kvbm_skinny_gemm_splits(N, K);
-  if (splits > 1 && (!ws || !tickets)) return cudaErrorInvalidValue;
   const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
   CUtensorMap mw, mx;
   if (!make_map(&mw, w, static_cast<uint64_t>(N), static_cast<uint64_t>(K), static_cast<uint64_t>(ldw), kTileN))
@@ -356,24 +403,27 @@ extern "C" int kvbm_skinny_gemm(const void* x, int ldx, const void* w, int ldw, 
   if (!make_map(&mx, x, static_cast<uint64_t>(M), static_cast<uint64_t>(K), static_cast<uint64_t>(ldx),
                 static_cast<uint32_t>(bn)))
     return cudaErrorInvalidValue;
-  const int tiles = (N + kTileN - 1) / kTileN;
-  const int chunks = (K + kChunkK - 1) / kChunkK;
   GemmParams P;
   P.M = M;
   P.N = N;
   P.K = K;
-  P.splits = std::min(splits, chunks);
-  P.chunks_per_split = (chunks + P.splits - 1) / P.splits;
-  P.splits = (chunks + P.chunks_per_split - 1) / P.chunks_per_split;  // no empty splits
+  P.tiles = (N + kTileN - 1) / kTileN;
+  P.chunks = (K + kChunkK - 1) / kChunkK;
+  const long total = static_cast<long>(P.tiles) * P.chunks;
+  if (total > (1l << 30)) return cudaErrorInvalidValue;
+  long grid = ctas > 0 ? ctas : sm_count_cached();
+  grid = std::min(grid, total);
+  P.per = static_cast<int>((total + grid - 1) / grid);
+  grid = (total + P.per - 1) / P.per;  // no empty CTAs
   P.y = static_cast<__nv_bfloat16*>(y);
   P.ldy = ldy;
   P.ws = ws;
   P.tickets = tickets;
   switch (bn) {
-    case 16: return launch<16>(mw, mx, P, tiles, stream);
-    case 32: return launch<32>(mw, mx, P, tiles, stream);
-    case 64: return launch<64>(mw, mx, P, tiles, stream);
-    default: return launch<128>(mw, mx, P, tiles, stream);
+    case 16: return launch<16>(mw, mx, P, static_cast<int>(grid), stream);
+    case 32: return launch<32>(mw, mx, P, static_cast<int>(grid), stream);
+    case 64: return launch<64>(mw, mx, P, static_cast<int>(grid), stream);
+    default: return launch<128>(mw, mx, P, static_cast<int>(grid), stream);
   }
 }
 

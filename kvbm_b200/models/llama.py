@@ -152,6 +152,8 @@ class LlamaModel:
         self.scale = 1.0 / math.sqrt(c.head_dim)
         self._decode_scratch: torch.Tensor | None = None
         self._decode_counters: torch.Tensor | None = None
+        self.decode_gemm = "cublas"  # "tc": decode projections on the tcgen05 skinny GEMM
+        self._gemm_ws: llama_ops.GemmWorkspace | None = None
         self._attn_backends: dict[bool, list] = {}
 
     # ------------------------------------------------------------ helpers
@@ -273,6 +275,15 @@ class LlamaModel:
             self._decode_scratch = torch.empty(need, dtype=torch.float32, device=self.device)
         return self._decode_scratch
 
+    def dlinear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """A decode-step projection ``x @ w.T``: the tcgen05 skinny GEMM for up to 128 rows
+        (``decode_gemm == "tc"``), cuBLAS otherwise."""
+        if self.decode_gemm == "tc" and x.shape[0] <= 128:
+            if self._gemm_ws is None:
+                self._gemm_ws = llama_ops.GemmWorkspace(self.device)
+            return llama_ops.skinny_gemm(x, w, workspace=self._gemm_ws)
+        return F.linear(x, w)
+
     def decode_counters(self, batch: int) -> torch.Tensor:
         """Zeroed split-merge tickets for the attention kernel (it leaves them zero after every launch)."""
         need = batch * self.cfg.kv_heads
@@ -304,7 +315,7 @@ class LlamaModel:
                 llama_ops.rmsnorm(x, L["n1"], c.eps, out=h)
             else:
                 llama_ops.rmsnorm(x, L["n1"], c.eps, residual=residual, out=h)
-            qkv = F.linear(h, L["wqkv"]).view(B, c.heads + 2 * c.kv_heads, c.head_dim)
+            qkv = self.dlinear(h, L["wqkv"]).view(B, c.heads + 2 * c.kv_heads, c.head_dim)
             kb, vb = self.kv_bases(pool, li)
             if c.head_dim == 128:
                 llama_ops.rope_kv_write_qout(qkv, positions, self.cos_sin, c.heads, c.kv_heads, kb, vb,
@@ -316,12 +327,12 @@ class LlamaModel:
             llama_ops.paged_decode_attn(q, kb, vb, pool.block_stride, pool.token_stride, pool.head_stride, page,
                                         block_table, seq_lens, c.kv_heads, self.scale, splits, scratch=scratch,
                                         out=attn, counters=counters)
-            x = F.linear(attn.view(B, c.q_size), L["wo"])
+            x = self.dlinear(attn.view(B, c.q_size), L["wo"])
             llama_ops.rmsnorm(x, L["n2"], c.eps, residual=residual, out=h)
-            x = F.linear(llama_ops.silu_mul(F.linear(h, L["wgu"])), L["wd"])
+            x = self.dlinear(llama_ops.silu_mul(self.dlinear(h, L["wgu"])), L["wd"])
         out = torch.empty_like(h)
         llama_ops.rmsnorm(x, self.norm, c.eps, residual=residual, out=out)
-        return F.linear(out, self.lm_head).argmax(dim=-1)
+        return self.dlinear(out, self.lm_head).argmax(dim=-1)
 
     # ---------------------------------------------------- torch reference
     @torch.inference_mode()

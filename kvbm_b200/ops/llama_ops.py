@@ -145,8 +145,9 @@ def paged_decode_attn(q: torch.Tensor, k_base: int, v_base: int, block_stride: i
 
 
 class GemmWorkspace:
-    """Split-K scratch of :func:`skinny_gemm`: an fp32 [M, N] sum and one ticket per
-    128-column tile, both zero between launches (the kernel re-zeroes what it used).
+    """Scratch of :func:`skinny_gemm`: an fp32 [M, N] sum for tiles that several CTAs
+    share and one ticket per 128-column tile, both zero between launches (the
+    kernel re-zeroes what it used).
 
     One workspace serves launches that run one after another; GEMMs that may run
     at the same time (different streams) need one each."""
@@ -166,19 +167,15 @@ class GemmWorkspace:
 _workspaces: dict[int, GemmWorkspace] = {}
 
 
-def skinny_gemm_splits(n: int, k: int) -> int:
-    """The split-K count :func:`skinny_gemm` uses by default for an [n, k] weight."""
-    return int(_lib.load().kvbm_skinny_gemm_splits(n, k))
-
-
-def skinny_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, splits: int = 0,
+def skinny_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, ctas: int = 0,
                 workspace: GemmWorkspace | None = None, stream=None) -> torch.Tensor:
     """``out = x @ w.T`` for a few rows of x on the tcgen05 tensor cores (TMA-fed, TMEM accumulators).
 
     x: [M, K] bf16 with M <= 128 (a decode batch), w: [N, K] bf16; both with unit
-    inner stride and 16-byte aligned rows. ``splits`` = split-K count (0: the
-    launcher's choice, which fills the SMs). Without ``workspace`` a per-device
-    one is used, so concurrent launches on several streams must pass their own."""
+    inner stride and 16-byte aligned rows. A persistent launch of ``ctas`` CTAs
+    (0: one per SM) splits the weight's 128-row x 64-column chunks evenly among
+    them (stream-K). Without ``workspace`` a per-device one is used, so
+    concurrent launches on several streams must pass their own."""
     if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1]:
         raise ValueError(f"skinny_gemm shapes {tuple(x.shape)} x {tuple(w.shape)}^T")
     if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
@@ -191,17 +188,15 @@ def skinny_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
         out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
     elif out.shape != (M, N) or out.stride(1) != 1 or out.dtype != torch.bfloat16:
         raise ValueError("skinny_gemm out must be bf16 [M, N] with unit inner stride")
-    if splits <= 0:
-        splits = skinny_gemm_splits(N, K)
     if workspace is None:
         dev = x.device.index if x.device.index is not None else torch.cuda.current_device()
         workspace = _workspaces.get(dev)
         if workspace is None:
             workspace = _workspaces[dev] = GemmWorkspace(x.device)
-    if splits > 1:
-        workspace.reserve(M * N, -(-N // 128))
+    workspace.reserve(M * N, -(-N // 128))
     _lib.call("kvbm_skinny_gemm", x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
-              out.stride(0), M, N, K, splits, workspace.ws.data_ptr(), workspace.tickets.data_ptr(), _stream(stream))
+              out.stride(0), M, N, K, int(ctas), workspace.ws.data_ptr(), workspace.tickets.data_ptr(),
+              _stream(stream))
     return out
 
 

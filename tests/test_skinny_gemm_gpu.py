@@ -8,36 +8,36 @@ pytestmark = pytest.mark.gpu
 from kvbm_b200.ops import llama_ops
 
 
-def _check(M, N, K, splits, seed=0):
+def _check(M, N, K, ctas, seed=0):
     g = torch.Generator(device="cuda").manual_seed(seed)
     x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16, generator=g)
     w = (torch.randn(N, K, device="cuda", dtype=torch.bfloat16, generator=g) / K ** 0.5).to(torch.bfloat16)
     ref = x.float() @ w.float().t()
-    y = llama_ops.skinny_gemm(x, w, splits=splits)
+    y = llama_ops.skinny_gemm(x, w, ctas=ctas)
     torch.cuda.synchronize()
     assert llama_ops.skinny_gemm_status() == 0
     torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)
     return x, w, ref
 
 
-@pytest.mark.parametrize("M,N,K,splits", [
-    (1, 128, 64, 1),        # one tile, one K chunk, BN = 16
-    (16, 256, 1024, 1),
-    (7, 384, 4096, 1),      # rows of x past M read as zeros
-    (32, 512, 4096, 4),     # split-K through the workspace, BN = 32
+@pytest.mark.parametrize("M,N,K,ctas", [
+    (1, 128, 64, 0),        # one tile, one K chunk, BN = 16
+    (16, 256, 1024, 1),     # one CTA walks both tiles whole
+    (16, 256, 1024, 3),     # 32 chunks over 3 CTAs: tiles shared through the workspace
+    (7, 384, 4096, 0),      # rows of x past M read as zeros
+    (32, 512, 4096, 5),     # BN = 32
     (33, 1000, 520, 1),     # N and K not multiples of the tile (BN = 64)
-    (33, 1000, 520, 3),
-    (128, 256, 2048, 2),    # BN = 128 (6-stage ring)
+    (33, 1000, 520, 7),
+    (128, 256, 2048, 0),    # BN = 128 (6-stage ring), 2-chunk ranges
+    (128, 1024, 4096, 11),
 ])
-def test_skinny_gemm_matches_fp32(M, N, K, splits):
-    _check(M, N, K, splits)
+def test_skinny_gemm_matches_fp32(M, N, K, ctas):
+    _check(M, N, K, ctas)
 
 
-def test_skinny_gemm_default_splits_and_rearm():
-    # repeated split-K launches: the kernel leaves workspace and tickets zeroed
+def test_skinny_gemm_default_ctas_and_rearm():
+    # repeated launches with shared tiles: the kernel leaves workspace and tickets zeroed
     M, N, K = 32, 4096, 14336
-    s = llama_ops.skinny_gemm_splits(N, K)
-    assert s >= 1
     x, w, ref = _check(M, N, K, 0, seed=1)
     for _ in range(3):
         y = llama_ops.skinny_gemm(x, w)
