@@ -17,10 +17,12 @@ def _check_greedy(model, seq, first_gen_pos, tol=0.05):
         assert float(row[seq[pos + 1]]) >= float(row.max()) - tol * float(row.abs().max()), pos
 
 
-def test_prefill_decode_matches_reference():
+@pytest.mark.parametrize("gemm", ["cublas", "tc"])
+def test_prefill_decode_matches_reference(gemm):
     torch.manual_seed(0)
     cfg = LlamaConfig.tiny(layers=2)
     model = LlamaModel(cfg, "cuda", seed=1)
+    model.decode_gemm = gemm
     pool = model.allocate_pool(16)
     T = 45
     prompt = torch.randint(0, cfg.vocab, (T,), device="cuda", dtype=torch.int32)
