@@ -21,8 +21,8 @@
 // Warp roles (192 threads):
 // * warp 0, one lane: TMA producer - per unit, a tiled 2-D bulk tensor load of
 //   the 128 x 64 weight tile and one of the BN x 64 activation tile (128-byte
-//   swizzle) into a ring of shared-memory stages. This GPU's own memory only;
-//   no cluster multicast.
+//   swizzle) into a ring of shared-memory stages. Both operands are in this
+//   GPU's own memory; every CTA loads its own tiles.
 // * warp 1, one lane: MMA issuer - 4 tcgen05.mma (K = 16 each, descriptor
 //   start advanced 32 bytes inside the 128-byte swizzle atom) per unit, then
 //   tcgen05.commit to the stage's "empty" barrier; tcgen05.commit to the
