@@ -1,8 +1,9 @@
 """Decode-projection GEMM microbenchmark: the tcgen05 skinny GEMM against
 cuBLAS (``torch.matmul``) on Llama-3-8B's weight shapes for a few batch rows.
 
-Each iteration writes a 256 MiB buffer first (L2 flush: the weights of one
-projection fit in the 126 MB L2), then times one GEMM with CUDA events. The
+Each iteration first reads a 256 MiB buffer (L2 flush: the weights of one
+projection fit in the 126 MB L2; a read leaves no dirty lines whose write-back
+would compete with the timed GEMM), then times one GEMM with CUDA events. The
 GEMMs stream their weight once, so the figure of merit is the weight bytes
 per second against the measured copy bandwidth.
 
@@ -25,9 +26,10 @@ SHAPES = [("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096), ("do
 
 def _time(fn, iters: int, flush: torch.Tensor) -> float:
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sink = torch.empty((), dtype=flush.dtype, device=flush.device)
     best = []
     for _ in range(iters):
-        flush.add_(1)
+        torch.sum(flush, out=sink)
         s.record()
         fn()
         e.record()
@@ -46,7 +48,7 @@ def main(argv=None):
     p.add_argument("--ctas", default="0", help="comma list of persistent CTA counts to try (0 = one per SM)")
     args = p.parse_args(argv)
     torch.cuda.set_device(0)
-    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    flush = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
     want = set(args.shapes.split(","))
     for name, N, K in SHAPES:
         if name not in want:

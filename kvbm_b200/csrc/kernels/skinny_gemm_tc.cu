@@ -143,25 +143,40 @@ struct GemmParams {
   int M, N, K;
   int chunks;             // K chunks per tile
   int tiles;              // 128-row weight tiles
-  int per;                // units per CTA
+  int rounds;             // whole tiles per CTA before the stream-K part
+  int per;                // stream-K units per CTA
   __nv_bfloat16* y;       // [M, N] row stride ldy
   int ldy;
   float* ws;              // [M, N] fp32 zeros
   unsigned int* tickets;  // [tiles] zeros
 };
 
-// The segments of CTA b's unit range, in order: tile, first and end chunk.
+// The segments of CTA b, in order. First `rounds` whole tiles (b, b + grid,
+// ...), written straight to Y; then the CTA's equal share of the remaining
+// tiles' units (stream-K), whose tiles several CTAs may share.
 struct SegIter {
-  int u, u1, chunks;
-  KVBM_DEVICE SegIter(const GemmParams& P, int b) : u(b * P.per), u1(min((b + 1) * P.per, P.tiles * P.chunks)),
-                                                    chunks(P.chunks) {}
+  int r, rounds, grid, b, u, u1, chunks, tile0;
+  KVBM_DEVICE SegIter(const GemmParams& P, int b_, int grid_)
+      : r(0), rounds(P.rounds), grid(grid_), b(b_), chunks(P.chunks), tile0(P.rounds * grid_) {
+    const int total = (P.tiles - tile0) * P.chunks;
+    u = min(b * P.per, total);
+    u1 = min((b + 1) * P.per, total);
+  }
   KVBM_DEVICE bool next(int& tile, int& c0, int& c1) {
+    if (r < rounds) {
+      tile = r * grid + b;
+      c0 = 0;
+      c1 = chunks;
+      ++r;
+      return true;
+    }
     if (u >= u1) return false;
-    tile = u / chunks;
-    c0 = u - tile * chunks;
-    const int end = min(u1, (tile + 1) * chunks);
-    c1 = end - tile * chunks;
+    const int t = u / chunks;
+    c0 = u - t * chunks;
+    const int end = min(u1, (t + 1) * chunks);
+    c1 = end - t * chunks;
     u = end;
+    tile = tile0 + t;
     return true;
   }
 };
@@ -209,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---- TMA producer ------------------------------------------------------
     if (lane == 0) {
-      SegIter segs(P, blockIdx.x);
+      SegIter segs(P, blockIdx.x, gridDim.x);
       int tile, c0, c1, it = 0;
       bool ok = true;
       while (ok && segs.next(tile, c0, c1)) {
@@ -232,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---- MMA issuer --------------------------------------------------------
     if (lane == 0) {
-      SegIter segs(P, blockIdx.x);
+      SegIter segs(P, blockIdx.x, gridDim.x);
       int tile, c0, c1, it = 0, j = 0;
       bool ok = true;
       while (ok && segs.next(tile, c0, c1)) {
@@ -265,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- epilogue: TMEM -> registers -> Y, or the workspace -----------------
     const int lane_grp = warp & 3;  // TMEM lanes this warp may read
     const int et = threadIdx.x - 64;
-    SegIter segs(P, blockIdx.x);
+    SegIter segs(P, blockIdx.x, gridDim.x);
     int tile, c0, c1, j = 0;
     // every epilogue warp runs the same sequence of named barriers, aborted or not
     while (segs.next(tile, c0, c1)) {
@@ -298,20 +313,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!whole) {
         // the tile's last contributor turns the fp32 sum into bf16 and re-arms the workspace
-        const int first = (tile * P.chunks) / P.per;
-        const int last = ((tile + 1) * P.chunks - 1) / P.per;
+        const int t = tile - P.rounds * static_cast<int>(gridDim.x);  // a stream-K tile
+        const int first = (t * P.chunks) / P.per;
+        const int last = ((t + 1) * P.chunks - 1) / P.per;
         __threadfence();
         epi_bar();
         if (et == 0) ticket = abort_flag ? ~0u : atomicAdd(&P.tickets[tile], 1u);
         epi_bar();
         if (ticket == static_cast<unsigned int>(last - first)) {
           __threadfence();
-          for (int idx = et; idx < P.M * kTileN; idx += kEpiThreads) {
-            const int m = idx / kTileN, r = tile * kTileN + idx % kTileN;
-            if (r < P.N) {
-              float* w = &P.ws[static_cast<int64_t>(m) * P.N + r];
-              P.y[static_cast<int64_t>(m) * P.ldy + r] = __float2bfloat16(__ldcg(w));
-              __stcg(w, 0.f);
+          const int r = tile * kTileN + et;  // thread et converts row r of this tile
+          if (r < P.N) {
+            for (int m0 = 0; m0 < P.M; m0 += 16) {
+              float v[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i)  // all loads in flight before the first store
+                v[i] = m0 + i < P.M ? __ldcg(&P.ws[static_cast<int64_t>(m0 + i) * P.N + r]) : 0.f;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                if (m0 + i < P.M) {
+                  P.y[static_cast<int64_t>(m0 + i) * P.ldy + r] = __float2bfloat16(v[i]);
+                  __stcg(&P.ws[static_cast<int64_t>(m0 + i) * P.N + r], 0.f);
+                }
+              }
             }
           }
           if (et == 0) P.tickets[tile] = 0u;
@@ -409,12 +433,12 @@ extern "C" int kvbm_skinny_gemm(const void* x, int ldx, const void* w, int ldw, 
   P.K = K;
   P.tiles = (N + kTileN - 1) / kTileN;
   P.chunks = (K + kChunkK - 1) / kChunkK;
-  const long total = static_cast<long>(P.tiles) * P.chunks;
-  if (total > (1l << 30)) return cudaErrorInvalidValue;
+  if (static_cast<long>(P.tiles) * P.chunks > (1l << 30)) return cudaErrorInvalidValue;
   long grid = ctas > 0 ? ctas : sm_count_cached();
-  grid = std::min(grid, total);
-  P.per = static_cast<int>((total + grid - 1) / grid);
-  grid = (total + P.per - 1) / P.per;  // no empty CTAs
+  P.rounds = static_cast<int>(P.tiles / grid);  // whole tiles every CTA takes first
+  const long rest = (P.tiles - P.rounds * grid) * static_cast<long>(P.chunks);
+  P.per = rest > 0 ? static_cast<int>((rest + grid - 1) / grid) : 1;
+  if (P.rounds == 0) grid = (rest + P.per - 1) / P.per;  // no CTA without work
   P.y = static_cast<__nv_bfloat16*>(y);
   P.ldy = ldy;
   P.ws = ws;
