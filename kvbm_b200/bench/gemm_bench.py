@@ -29,7 +29,7 @@ def _time(fn, iters: int, flush: torch.Tensor) -> float:
     sink = torch.empty((), dtype=flush.dtype, device=flush.device)
     best = []
     for _ in range(iters):
-        torch.sum(flush, out=sink)
+        torch.sum(flush, dim=0, out=sink)
         s.record()
         fn()
         e.record()
