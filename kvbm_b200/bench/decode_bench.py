@@ -29,6 +29,7 @@ def main(argv=None):
     p.add_argument("--splits", type=int, default=0)
     p.add_argument("--gemm", default="cublas", choices=["cublas", "tc"],
                    help="decode projections: cuBLAS or the tcgen05 skinny GEMM")
+    p.add_argument("--no-pdl", action="store_true", help="launch the skinny GEMM without programmatic dependent launch")
     p.add_argument("--profile", action="store_true",
                    help="bracket one extra eager step with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     args = p.parse_args(argv)
@@ -36,6 +37,7 @@ def main(argv=None):
     cfg = LlamaConfig(layers=args.layers)
     model = LlamaModel(cfg, "cuda")
     model.decode_gemm = args.gemm
+    llama_ops.set_skinny_gemm_pdl(not args.no_pdl)
     page = 16
     bpr = math.ceil((args.ctx + 1) / page)
     pool = model.allocate_pool(args.batch * bpr + 1, page)
@@ -94,7 +96,7 @@ def main(argv=None):
     torch.cuda.synchronize()
     attn_ms = s.elapsed_time(e) / args.steps
     kv_bytes = cfg.layers * B * (args.ctx + 1) * 2 * cfg.kv_heads * cfg.head_dim * 2
-    print(json.dumps({"batch": B, "ctx": args.ctx, "splits": splits, "gemm": args.gemm, "ms_per_step": round(ms, 3),
+    print(json.dumps({"batch": B, "ctx": args.ctx, "splits": splits, "gemm": args.gemm, "pdl": not args.no_pdl, "ms_per_step": round(ms, 3),
                       "attn_ms": round(attn_ms, 3), "attn_gbps": round(kv_bytes / attn_ms / 1e6, 1),
                       "weights_gb": round(cfg.num_params() * 2 / 1e9, 2)}))
 

@@ -6,7 +6,8 @@
 // The reference (crates/kvbm-kernels) ships no model kernels; vLLM computes
 // attention there. These exist so the block manager can be exercised end to
 // end on a PyTorch Llama model whose KV cache lives in the block manager's
-// paged layout, with GEMMs left to cuBLAS.
+// paged layout. The decode projections run on the tcgen05 skinny GEMM
+// (skinny_gemm_tc.cu) or cuBLAS; prefill GEMMs on cuBLAS.
 #include "common.cuh"
 #include "decode_attn_mma.cuh"
 
@@ -46,6 +47,9 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
                                                       __nv_bfloat16* __restrict__ residual,
                                                       const __nv_bfloat16* __restrict__ w,
                                                       __nv_bfloat16* __restrict__ out, int D, float eps) {
+  // a GEMM launched after this kernel with programmatic dependent launch may
+  // start streaming its weights now (it waits for this grid before reading `out`)
+  asm volatile("griddepcontrol.launch_dependents;");
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int nvec = D / 8;
@@ -323,6 +327,7 @@ __device__ __forceinline__ int4 silu_mul_vec(const int4 g, const int4 u) {
 // a batch are issued before any math, so a thread has 8 x 16 B outstanding.
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu,
                                                        __nv_bfloat16* __restrict__ out, int64_t T, int I) {
+  asm volatile("griddepcontrol.launch_dependents;");  // as in rmsnorm_kernel
   const int nv = I / 8;
   const int64_t total = T * nv;
   const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;

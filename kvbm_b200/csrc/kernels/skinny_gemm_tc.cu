@@ -137,6 +137,13 @@ KVBM_DEVICE bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abo
   }
 }
 
+// Programmatic dependent launch: wait until the preceding kernel in the stream
+// has completed and its writes are visible (a no-op without the launch attribute).
+KVBM_DEVICE void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+KVBM_DEVICE void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 KVBM_DEVICE void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
 
 struct GemmParams {
@@ -199,6 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  if (threadIdx.x == 32) {
+    prefetch_tmap(&map_w);
+    prefetch_tmap(&map_x);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -224,19 +235,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---- TMA producer ------------------------------------------------------
     if (lane == 0) {
-      SegIter segs(P, blockIdx.x, gridDim.x);
+      // The weight tiles of the first ring's worth of units do not depend on
+      // the preceding kernel: start streaming them before waiting for it.
       int tile, c0, c1, it = 0;
+      {
+        SegIter segs(P, blockIdx.x, gridDim.x);
+        while (it < kStages && segs.next(tile, c0, c1)) {
+          for (int c = c0; c < c1 && it < kStages; ++c, ++it) {
+            mbar_arrive_expect_tx(&full[it], kStageBytes);
+            tma_load_2d(smem + it * kStageBytes, &map_w, c * kChunkK, tile * kTileN, &full[it]);
+          }
+        }
+      }
+      const int early = it;
+      grid_dep_wait();  // the activations are the preceding kernel's output
+      SegIter segs(P, blockIdx.x, gridDim.x);
+      it = 0;
       bool ok = true;
       while (ok && segs.next(tile, c0, c1)) {
         for (int c = c0; c < c1; ++c, ++it) {
           const int s = it % kStages;
-          if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
-          }
           uint8_t* st = smem + s * kStageBytes;
-          mbar_arrive_expect_tx(&full[s], kStageBytes);
-          tma_load_2d(st, &map_w, c * kChunkK, tile * kTileN, &full[s]);
+          if (it >= early) {
+            if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], kStageBytes);
+            tma_load_2d(st, &map_w, c * kChunkK, tile * kTileN, &full[s]);
+          }
           tma_load_2d(st + kBytesW, &map_x, c * kChunkK, 0, &full[s]);
         }
       }
@@ -280,6 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- epilogue: TMEM -> registers -> Y, or the workspace -----------------
     const int lane_grp = warp & 3;  // TMEM lanes this warp may read
     const int et = threadIdx.x - 64;
+    grid_dep_wait();  // Y and the workspace may still be in use by the preceding kernel
     SegIter segs(P, blockIdx.x, gridDim.x);
     int tile, c0, c1, j = 0;
     // every epilogue warp runs the same sequence of named barriers, aborted or not
@@ -387,6 +415,8 @@ int sm_count_cached() {
   return n;
 }
 
+int g_pdl = 1;  // launch with programmatic stream serialization
+
 template <int BN>
 int launch(const CUtensorMap& mw, const CUtensorMap& mx, const GemmParams& P, int grid, cudaStream_t stream) {
   constexpr size_t smem = 1024 + static_cast<size_t>(Ring<BN>::kStages) * Ring<BN>::kStageBytes;
@@ -399,11 +429,30 @@ int launch(const CUtensorMap& mw, const CUtensorMap& mx, const GemmParams& P, in
     if (e != cudaSuccess) return e;
     configured = dev;
   }
-  skinny_gemm_tc_kernel<BN><<<grid, kThreads, smem, stream>>>(mw, mx, P);
-  return cudaGetLastError();
+  // With programmatic dependent launch the CTAs may start while the previous
+  // kernel in the stream drains: they allocate TMEM and stream their first
+  // weight tiles, then wait (griddepcontrol.wait) before reading activations.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = g_pdl;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, skinny_gemm_tc_kernel<BN>, mw, mx, P);
 }
 
 }  // namespace
+
+// Programmatic dependent launch on (1, the default) or off (0); returns the previous setting.
+extern "C" int kvbm_skinny_gemm_set_pdl(int on) {
+  const int prev = g_pdl;
+  g_pdl = on ? 1 : 0;
+  return prev;
+}
 
 // Number of persistent CTAs a launch uses by default (one per SM).
 extern "C" int kvbm_skinny_gemm_ctas() { return sm_count_cached(); }

@@ -203,3 +203,9 @@ def skinny_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
 def skinny_gemm_status(reset: bool = True) -> int:
     """0, or the error a :func:`skinny_gemm` launch recorded (3: a pipeline wait timed out). Synchronizes."""
     return int(_lib.load().kvbm_skinny_gemm_status(1 if reset else 0))
+
+
+def set_skinny_gemm_pdl(on: bool) -> bool:
+    """Launch :func:`skinny_gemm` with programmatic dependent launch (default on): its CTAs
+    start streaming weights while the preceding kernel drains. Returns the previous setting."""
+    return bool(_lib.load().kvbm_skinny_gemm_set_pdl(1 if on else 0))

@@ -61,3 +61,38 @@ def test_skinny_gemm_strided_operands():
     ref = x.float() @ w.to(torch.bfloat16).float().t()
     torch.testing.assert_close(out[:, 64:64 + N].float(), ref, rtol=2e-2, atol=2e-2)
     assert float(out[:, :64].abs().sum()) == 0.0 and float(out[:, 64 + N:].abs().sum()) == 0.0
+
+
+@pytest.mark.parametrize("pdl", [True, False])
+def test_skinny_gemm_after_rmsnorm_in_graph(pdl):
+    # the GEMM reads the norm's output: with programmatic dependent launch it may start
+    # early but must still see that output, eagerly and inside a captured graph
+    prev = llama_ops.set_skinny_gemm_pdl(pdl)
+    try:
+        M, K, N = 32, 4096, 6144
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        g = torch.rand(K, device="cuda", dtype=torch.bfloat16) + 0.5
+        w = (torch.randn(N, K, device="cuda", dtype=torch.bfloat16) / K ** 0.5).to(torch.bfloat16)
+        h = torch.empty_like(x)
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+
+        def step():
+            llama_ops.rmsnorm(x, g, 1e-5, out=h)
+            llama_ops.skinny_gemm(h, w, out=y)
+
+        step()
+        torch.cuda.synchronize()
+        torch.testing.assert_close(y.float(), h.float() @ w.float().t(), rtol=2e-2, atol=2e-2)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(3):
+            x.copy_(torch.randn_like(x))
+            graph.replay()
+            torch.cuda.synchronize()
+            ref_h = llama_ops.rmsnorm(x, g, 1e-5)
+            torch.testing.assert_close(h, ref_h)
+            torch.testing.assert_close(y.float(), ref_h.float() @ w.float().t(), rtol=2e-2, atol=2e-2)
+        assert llama_ops.skinny_gemm_status() == 0
+    finally:
+        llama_ops.set_skinny_gemm_pdl(prev)
