@@ -19,8 +19,9 @@ import torch
 
 from ..ops import llama_ops
 
-# (name, N, K) of Llama-3-8B: fused q/k/v, o, fused gate/up, down, lm_head
-SHAPES = [("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336),
+# (name, N, K): one tile (launch overhead), a 8 MiB weight, then Llama-3-8B's fused q/k/v, o,
+# fused gate/up, down, lm_head
+SHAPES = [("tiny", 128, 64), ("small", 1024, 4096), ("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336),
           ("lm_head", 128256, 4096)]
 
 
@@ -42,7 +43,7 @@ def _time(fn, iters: int, flush: torch.Tensor) -> float:
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--batch", default="1,8,32,64,128")
-    p.add_argument("--shapes", default=",".join(n for n, _, _ in SHAPES))
+    p.add_argument("--shapes", default=",".join(n for n, _, _ in SHAPES[2:]))
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--ctas", default="0", help="comma list of persistent CTA counts to try (0 = one per SM)")

@@ -542,6 +542,19 @@ __global__ void __launch_bounds__(kHD) attn_combine_kernel(const float* __restri
   out[bh * kHD + d] = __float2bfloat16(L > 0.f ? A / L : 0.f);
 }
 
+// The decode GEMM that follows rmsnorm / silu_mul (programmatic dependent
+// launch) needs most of the SM's unified L1 / shared memory; with the same
+// carve-out its CTAs can become resident beside these small kernels' CTAs
+// instead of waiting for the SM to drain and be reconfigured.
+template <typename K>
+void prefer_max_shared(K kernel) {
+  static bool done = false;
+  if (!done) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    done = true;
+  }
+}
+
 }  // namespace
 
 extern "C" int kvbm_rmsnorm(const void* x, void* residual, const void* weight, void* out, int64_t rows, int dim,
@@ -549,6 +562,7 @@ extern "C" int kvbm_rmsnorm(const void* x, void* residual, const void* weight, v
   if (rows == 0) return cudaSuccess;
   if (!x || !weight || !out || dim % 8 != 0 || dim / 8 > 256 * kNormMaxVec) return cudaErrorInvalidValue;
   const int threads = std::min(256, std::max(32, (dim / 8 + 31) / 32 * 32));
+  prefer_max_shared(rmsnorm_kernel);
   rmsnorm_kernel<<<static_cast<unsigned>(rows), threads, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(residual),
       static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out), dim, eps);
@@ -752,6 +766,7 @@ extern "C" int kvbm_silu_mul(const void* gate_up, void* out, int64_t tokens, int
   const unsigned grid = static_cast<unsigned>(
       std::max<int64_t>(1, std::min<int64_t>((work + 256 * kSiluUnroll - 1) / (256 * kSiluUnroll),
                                              static_cast<int64_t>(sms) * 8)));
+  prefer_max_shared(silu_mul_kernel);
   silu_mul_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(gate_up),
                                             static_cast<__nv_bfloat16*>(out), tokens, inter);
   return cudaGetLastError();

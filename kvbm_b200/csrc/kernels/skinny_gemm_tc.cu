@@ -344,21 +344,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = tile - P.rounds * static_cast<int>(gridDim.x);  // a stream-K tile
         const int first = (t * P.chunks) / P.per;
         const int last = ((t + 1) * P.chunks - 1) / P.per;
-        __threadfence();
+        // The barrier orders every epilogue thread's red.add before thread 0's
+        // gpu-scope fence (cumulative), which orders them before the ticket.
         epi_bar();
-        if (et == 0) ticket = abort_flag ? ~0u : atomicAdd(&P.tickets[tile], 1u);
+        if (et == 0) {
+          __threadfence();
+          ticket = abort_flag ? ~0u : atomicAdd(&P.tickets[tile], 1u);
+        }
         epi_bar();
         if (ticket == static_cast<unsigned int>(last - first)) {
           __threadfence();
           const int r = tile * kTileN + et;  // thread et converts row r of this tile
           if (r < P.N) {
-            for (int m0 = 0; m0 < P.M; m0 += 16) {
-              float v[16];
+            for (int m0 = 0; m0 < P.M; m0 += 32) {
+              float v[32];
 #pragma unroll
-              for (int i = 0; i < 16; ++i)  // all loads in flight before the first store
+              for (int i = 0; i < 32; ++i)  // all loads in flight before the first store
                 v[i] = m0 + i < P.M ? __ldcg(&P.ws[static_cast<int64_t>(m0 + i) * P.N + r]) : 0.f;
 #pragma unroll
-              for (int i = 0; i < 16; ++i) {
+              for (int i = 0; i < 32; ++i) {
                 if (m0 + i < P.M) {
                   P.y[static_cast<int64_t>(m0 + i) * P.ldy + r] = __float2bfloat16(v[i]);
                   __stcg(&P.ws[static_cast<int64_t>(m0 + i) * P.N + r], 0.f);
