@@ -47,6 +47,7 @@ def main(argv=None):
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--ctas", default="0", help="comma list of persistent CTA counts to try (0 = one per SM)")
+    p.add_argument("--modes", default="auto", help="comma list of skinny-GEMM modes: auto, streamk, cluster")
     args = p.parse_args(argv)
     torch.cuda.set_device(0)
     flush = torch.ones(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
@@ -65,15 +66,19 @@ def main(argv=None):
             wbytes = N * K * 2
             row = {"shape": name, "M": M, "N": N, "K": K, "cublas_us": round(t_cublas * 1e3, 2),
                    "cublas_gbs": round(wbytes / t_cublas / 1e6, 1)}
-            for nc in (int(v) for v in args.ctas.split(",")):
+            runs = [(m, nc) for m in args.modes.split(",") for nc in (int(v) for v in args.ctas.split(","))
+                    if nc == 0 or m == "streamk"]
+            for mode, nc in runs:
+                llama_ops.set_skinny_gemm_mode(mode)
                 for _ in range(args.warmup):
                     llama_ops.skinny_gemm(x, w, out=out, ctas=nc)
                 t = _time(lambda: llama_ops.skinny_gemm(x, w, out=out, ctas=nc), args.iters, flush)
                 err = (out.float() - ref.float()).abs().max().item()
-                key = f"tc{nc or 'sm'}"
+                key = f"{mode}{nc or ''}"
                 row[key + "_us"] = round(t * 1e3, 2)
                 row[key + "_gbs"] = round(wbytes / t / 1e6, 1)
                 row[key + "_maxerr"] = round(err, 4)
+            llama_ops.set_skinny_gemm_mode("auto")
             row["status"] = llama_ops.skinny_gemm_status()
             print(json.dumps(row), flush=True)
 

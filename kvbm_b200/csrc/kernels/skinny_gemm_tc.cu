@@ -381,6 +381,274 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tmem_dealloc(tmem_d, kTmemCols);
 }
 
+// ---- cluster split-K variant ------------------------------------------------------
+// For weights with fewer 128-row tiles than SMs: a cluster of S CTAs (S <= 8)
+// shares each tile, CTA rank r streaming K chunks [r C / S, (r + 1) C / S).
+// Each CTA leaves its fp32 partial tile in its own shared memory and the S
+// partials are summed through distributed shared memory (ld.shared::cluster),
+// each rank converting an equal slice of the tile to bf16: no workspace, no
+// global atomics, no last-arrival round trip through L2. Clusters walk tiles
+// c, c + clusters, ...
+//
+// Per-tile handshake, one mbarrier pair in every CTA, S arrivals per phase
+// (one per rank, release/acquire at cluster scope):
+//   red_ready - "my partial of this tile is in my shared memory"
+//   red_done  - "I have finished reading your partial of this tile"
+// A rank overwrites its partial (next tile) or exits only after its own
+// red_done phase for the previous tile completed, so no peer reads shared
+// memory that has been reused or released.
+
+template <int BN>
+struct ClusterRing {
+  static constexpr uint32_t kPartialBytes = kTileN * BN * 4;
+  static constexpr uint32_t kStageBytes = (kTileN + BN) * kChunkK * 2;
+  static constexpr int kFit = static_cast<int>((200 * 1024 - kPartialBytes) / kStageBytes);
+  static constexpr int kStages = kFit < 8 ? kFit : 8;
+  static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + kPartialBytes;
+};
+
+KVBM_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// address of this CTA's shared variable `p` in the shared memory of cluster rank `rank`
+KVBM_DEVICE uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+KVBM_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+KVBM_DEVICE bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+KVBM_DEVICE float ld_dsmem_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+// every thread of every CTA in the cluster; used once, right after barrier initialisation
+KVBM_DEVICE void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+KVBM_DEVICE bool wait_cluster_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      atomicExch(&g_gemm_status, kStatusPipelineTimeout);
+      return false;
+    }
+  }
+}
+
+struct ClusterParams {
+  int M, N, K;
+  int chunks;  // K chunks per tile
+  int tiles;   // 128-row weight tiles
+  int S;       // cluster size = CTAs per tile
+  __nv_bfloat16* y;
+  int ldy;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    skinny_gemm_cluster_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                               const __grid_constant__ ClusterParams P) {
+  constexpr uint32_t kBytesW = kTileN * kChunkK * 2;
+  constexpr uint32_t kStageBytes = ClusterRing<BN>::kStageBytes;
+  constexpr int kStages = ClusterRing<BN>::kStages;
+  constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* partial = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [M][128] fp32
+  __shared__ uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], mma_done, red_ready, red_done;
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = P.S;
+  const uint32_t rank = cluster_rank();
+  const int c_lo = static_cast<int>(rank) * P.chunks / S, c_hi = (static_cast<int>(rank) + 1) * P.chunks / S;
+  const int clusters = gridDim.y;
+
+  if (threadIdx.x == 32) {
+    prefetch_tmap(&map_w);
+    prefetch_tmap(&map_x);
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(&mma_done, 1);
+    mbar_init(&red_ready, S);
+    mbar_init(&red_done, S);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  cluster_sync_all();  // every rank's barriers exist before the first remote arrival
+  const uint32_t tmem_d = tmem_base;
+
+  if (warp == 0) {
+    // ---- TMA producer (weight stages before the grid dependency, as above) --
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.y; tile < P.tiles && it < kStages; tile += clusters)
+        for (int c = c_lo; c < c_hi && it < kStages; ++c, ++it) {
+          mbar_arrive_expect_tx(&full[it], kStageBytes);
+          tma_load_2d(smem + it * kStageBytes, &map_w, c * kChunkK, tile * kTileN, &full[it]);
+        }
+      const int early = it;
+      grid_dep_wait();
+      it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.y; ok && tile < P.tiles; tile += clusters) {
+        for (int c = c_lo; c < c_hi; ++c, ++it) {
+          const int s = it % kStages;
+          uint8_t* st = smem + s * kStageBytes;
+          if (it >= early) {
+            if (it >= kStages && !wait_or_abort(&empty[s], ((it / kStages) - 1) & 1, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], kStageBytes);
+            tma_load_2d(st, &map_w, c * kChunkK, tile * kTileN, &full[s]);
+          }
+          tma_load_2d(st + kBytesW, &map_x, c * kChunkK, 0, &full[s]);
+        }
+      }
+      for (int i = max(0, it - kStages); i < it; ++i)
+        mbar_wait_bounded(&full[i % kStages], (i / kStages) & 1, kWaitNs);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----------------------------------------------------------
+    if (lane == 0) {
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int tile = blockIdx.y; ok && tile < P.tiles; tile += clusters, ++j) {
+        const int a = j & 1;
+        if (j >= 2 && !wait_or_abort(&acc_empty[a], ((j >> 1) - 1) & 1, &abort_flag)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem_d + a * BN;
+        for (int c = c_lo; c < c_hi; ++c, ++it) {
+          const int s = it % kStages;
+          if (!wait_or_abort(&full[s], (it / kStages) & 1, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* st = smem + s * kStageBytes;
+          const uint64_t da = smem_desc_k128(st), db = smem_desc_k128(st + kBytesW);
+#pragma unroll
+          for (int k = 0; k < kChunkK / 16; ++k)
+            umma_bf16(acc, da + 2 * k, db + 2 * k, idesc_bf16(BN), (c > c_lo || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[a]);
+      }
+      umma_commit(&mma_done);
+      mbar_wait_bounded(&mma_done, 0, kWaitNs);
+    }
+  } else {
+    // ---- epilogue: TMEM -> own partial -> cluster sum of a slice -> Y ---------
+    const int lane_grp = warp & 3;
+    const int et = threadIdx.x - 64;
+    const int rowl = lane_grp * 32 + lane;  // tile row this thread reads from TMEM
+    grid_dep_wait();
+    const int E = P.M * kTileN;  // partial elements that matter, e = m * 128 + row
+    const int e0 = static_cast<int>(rank) * E / S, e1 = (static_cast<int>(rank) + 1) * E / S;
+    int j = 0;
+    for (int tile = blockIdx.y; tile < P.tiles; tile += clusters, ++j) {
+      const int a = j & 1;
+      const bool ok = __all_sync(0xffffffffu, wait_or_abort(&acc_full[a], (j >> 1) & 1, &abort_flag));
+      // the partial buffer is free once every rank has read the previous tile's
+      if (j > 0) wait_cluster_or_abort(&red_done, (j - 1) & 1, &abort_flag);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int m0 = 0; m0 < BN; m0 += 16) {
+          if (m0 < P.M) {  // uniform across the warp
+            float v[16];
+            tmem_ld16(tmem_d + (static_cast<uint32_t>(lane_grp * 32) << 16) + a * BN + m0, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (m0 + i < P.M) partial[(m0 + i) * kTileN + rowl] = v[i];
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[a]);
+      }
+      // bar.sync orders all 128 writes before thread 0's cluster-scope release
+      epi_bar();
+      if (et == 0)
+        for (int q = 0; q < S; ++q) mbar_arrive_cluster(map_to_rank(&red_ready, q));
+      wait_cluster_or_abort(&red_ready, j & 1, &abort_flag);
+      // this rank's slice of the tile: sum the S partials, convert, store
+      const uint32_t base = smem_u32(partial);
+      for (int e = e0 + et; e < e1; e += 4 * kEpiThreads) {
+        float acc4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int ee = e + u * kEpiThreads;
+          if (ee < e1) {
+            float v[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (q < S) {
+                uint32_t ra;
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(base + ee * 4u), "r"(q));
+                v[q] = ld_dsmem_f32(ra);
+              }
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (q < S) acc4[u] += v[q];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int ee = e + u * kEpiThreads;
+          const int r = tile * kTileN + (ee & (kTileN - 1));
+          if (ee < e1 && r < P.N) P.y[static_cast<int64_t>(ee / kTileN) * P.ldy + r] = __float2bfloat16(acc4[u]);
+        }
+      }
+      epi_bar();
+      if (et == 0)
+        for (int q = 0; q < S; ++q) mbar_arrive_cluster(map_to_rank(&red_done, q));
+    }
+    // leave only when no rank still reads this CTA's partial
+    if (j > 0) wait_cluster_or_abort(&red_done, (j - 1) & 1, &abort_flag);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_d, kTmemCols);
+}
+
 // ---- host side ------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -449,7 +717,138 @@ int launch(const CUtensorMap& mw, const CUtensorMap& mx, const GemmParams& P, in
   return cudaLaunchKernelEx(&cfg, skinny_gemm_tc_kernel<BN>, mw, mx, P);
 }
 
+template <int BN>
+int set_cluster_smem() {
+  static int configured = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured != dev) {
+    cudaError_t e = cudaFuncSetAttribute(skinny_gemm_cluster_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(ClusterRing<BN>::kSmem));
+    if (e != cudaSuccess) return e;
+    configured = dev;
+  }
+  return cudaSuccess;
+}
+
+// Clusters of S CTAs that can be resident at once (0 if none).
+template <int BN>
+int cluster_capacity(int S) {
+  static int cap[9] = {-1, -1, -1, -1, -1, -1, -1, -1, -1};
+  static int cap_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cap_dev != dev) {
+    for (int& c : cap) c = -1;
+    cap_dev = dev;
+  }
+  if (cap[S] < 0) {
+    cap[S] = 0;
+    if (set_cluster_smem<BN>() == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(S);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = ClusterRing<BN>::kSmem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = S;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, skinny_gemm_cluster_kernel<BN>, &cfg) == cudaSuccess) cap[S] = n;
+      else cudaGetLastError();
+    }
+  }
+  return cap[S];
+}
+
+template <int BN>
+int launch_cluster(const CUtensorMap& mw, const CUtensorMap& mx, const ClusterParams& P, int clusters,
+                   cudaStream_t stream) {
+  if (int e = set_cluster_smem<BN>()) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(P.S, clusters);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = ClusterRing<BN>::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = P.S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = g_pdl;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, skinny_gemm_cluster_kernel<BN>, mw, mx, P);
+}
+
+int g_mode = 0;  // 0: pick by estimated time, 1: stream-K only, 2: cluster split-K only
+
+struct ClusterChoice {
+  int S = 0, clusters = 0;
+  long cost = -1;
+};
+
+// Estimated time, in K-chunk loads per CTA, of the best cluster split-K launch.
+template <int BN>
+ClusterChoice best_cluster(int tiles, int chunks) {
+  ClusterChoice best;
+  for (int S = 1; S <= 8 && S <= chunks; ++S) {
+    const int cap = cluster_capacity<BN>(S);
+    if (cap <= 0) continue;
+    const int clusters = std::min(tiles, cap);
+    const long rounds = (tiles + clusters - 1) / clusters;
+    const long cost = rounds * ((chunks + S - 1) / S + (S > 1 ? 3 : 0));  // + the cluster reduction
+    if (best.cost < 0 || cost < best.cost) {
+      best.S = S;
+      best.clusters = clusters;
+      best.cost = cost;
+    }
+  }
+  return best;
+}
+
+template <int BN>
+int run(const CUtensorMap& mw, const CUtensorMap& mx, GemmParams& P, int ctas, cudaStream_t stream) {
+  long grid = ctas > 0 ? ctas : sm_count_cached();
+  P.rounds = static_cast<int>(P.tiles / grid);  // whole tiles every CTA takes first
+  const long rest = (P.tiles - P.rounds * grid) * static_cast<long>(P.chunks);
+  P.per = rest > 0 ? static_cast<int>((rest + grid - 1) / grid) : 1;
+  if (P.rounds == 0) grid = (rest + P.per - 1) / P.per;  // no CTA without work
+  if (g_mode == 2 || (g_mode == 0 && ctas <= 0)) {
+    // stream-K: the largest share, plus the fix-up tail when some tile is split
+    const bool split = rest > 0 && P.per % P.chunks != 0;
+    const long sk_cost = static_cast<long>(P.rounds) * P.chunks + P.per + (split ? 10 + P.M / 8 : 0);
+    const ClusterChoice c = best_cluster<BN>(P.tiles, P.chunks);
+    if (c.cost >= 0 && (g_mode == 2 || c.cost < sk_cost)) {
+      ClusterParams C;
+      C.M = P.M;
+      C.N = P.N;
+      C.K = P.K;
+      C.chunks = P.chunks;
+      C.tiles = P.tiles;
+      C.S = c.S;
+      C.y = P.y;
+      C.ldy = P.ldy;
+      return launch_cluster<BN>(mw, mx, C, c.clusters, stream);
+    }
+    if (g_mode == 2) return cudaErrorLaunchOutOfResources;
+  }
+  return launch<BN>(mw, mx, P, static_cast<int>(grid), stream);
+}
+
 }  // namespace
+
+// 0: choose stream-K or cluster split-K by estimated time (default); 1: stream-K
+// only; 2: cluster split-K only. Returns the previous mode.
+extern "C" int kvbm_skinny_gemm_set_mode(int mode) {
+  const int prev = g_mode;
+  g_mode = (mode >= 0 && mode <= 2) ? mode : 0;
+  return prev;
+}
 
 // Programmatic dependent launch on (1, the default) or off (0); returns the previous setting.
 extern "C" int kvbm_skinny_gemm_set_pdl(int on) {
@@ -463,9 +862,10 @@ extern "C" int kvbm_skinny_gemm_ctas() { return sm_count_cached(); }
 
 // Y[M, N] (row stride ldy) = X[M, K] (row stride ldx) * W[N, K]^T (row stride ldw).
 // bf16, M <= 128, K % 8 == 0, x and w 16-byte aligned, ldx and ldw multiples
-// of 8. `ctas` persistent CTAs (<= 0: one per SM). `ws` is an fp32 [M, N]
-// buffer of zeros and `tickets` (N / 128 rounded up) 32-bit zeros; the kernel
-// leaves both zeroed again.
+// of 8. `ctas` > 0 forces a stream-K launch of that many persistent CTAs
+// (unless the mode is cluster-only); otherwise the launcher picks stream-K
+// over all SMs or cluster split-K. `ws` is an fp32 [M, N] buffer of zeros and
+// `tickets` (N / 128 rounded up) 32-bit zeros; the kernel leaves both zeroed.
 extern "C" int kvbm_skinny_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy, int M, int N, int K,
                                 int ctas, float* ws, unsigned int* tickets, cudaStream_t stream) {
   if (M == 0 || N == 0) return cudaSuccess;
@@ -487,20 +887,15 @@ extern "C" int kvbm_skinny_gemm(const void* x, int ldx, const void* w, int ldw, 
   P.tiles = (N + kTileN - 1) / kTileN;
   P.chunks = (K + kChunkK - 1) / kChunkK;
   if (static_cast<long>(P.tiles) * P.chunks > (1l << 30)) return cudaErrorInvalidValue;
-  long grid = ctas > 0 ? ctas : sm_count_cached();
-  P.rounds = static_cast<int>(P.tiles / grid);  // whole tiles every CTA takes first
-  const long rest = (P.tiles - P.rounds * grid) * static_cast<long>(P.chunks);
-  P.per = rest > 0 ? static_cast<int>((rest + grid - 1) / grid) : 1;
-  if (P.rounds == 0) grid = (rest + P.per - 1) / P.per;  // no CTA without work
   P.y = static_cast<__nv_bfloat16*>(y);
   P.ldy = ldy;
   P.ws = ws;
   P.tickets = tickets;
   switch (bn) {
-    case 16: return launch<16>(mw, mx, P, static_cast<int>(grid), stream);
-    case 32: return launch<32>(mw, mx, P, static_cast<int>(grid), stream);
-    case 64: return launch<64>(mw, mx, P, static_cast<int>(grid), stream);
-    default: return launch<128>(mw, mx, P, static_cast<int>(grid), stream);
+    case 16: return run<16>(mw, mx, P, ctas, stream);
+    case 32: return run<32>(mw, mx, P, ctas, stream);
+    case 64: return run<64>(mw, mx, P, ctas, stream);
+    default: return run<128>(mw, mx, P, ctas, stream);
   }
 }
 

@@ -209,3 +209,15 @@ def set_skinny_gemm_pdl(on: bool) -> bool:
     """Launch :func:`skinny_gemm` with programmatic dependent launch (default on): its CTAs
     start streaming weights while the preceding kernel drains. Returns the previous setting."""
     return bool(_lib.load().kvbm_skinny_gemm_set_pdl(1 if on else 0))
+
+
+_GEMM_MODES = {"auto": 0, "streamk": 1, "cluster": 2}
+
+
+def set_skinny_gemm_mode(mode: str) -> str:
+    """How :func:`skinny_gemm` splits the work: ``"auto"`` (estimated fastest, default),
+    ``"streamk"`` (persistent CTAs, fp32 workspace fix-up) or ``"cluster"`` (thread-block
+    clusters share a tile, partials summed through distributed shared memory).
+    Returns the previous mode."""
+    prev = int(_lib.load().kvbm_skinny_gemm_set_mode(_GEMM_MODES[mode]))
+    return {v: k for k, v in _GEMM_MODES.items()}[prev]

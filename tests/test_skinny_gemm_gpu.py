@@ -35,6 +35,25 @@ def test_skinny_gemm_matches_fp32(M, N, K, ctas):
     _check(M, N, K, ctas)
 
 
+@pytest.mark.parametrize("M,N,K", [
+    (1, 128, 64),        # one tile, one chunk: a cluster of one
+    (16, 256, 1024),
+    (7, 384, 4096),
+    (32, 512, 4096),
+    (33, 1000, 520),     # ragged N and K, BN = 64
+    (128, 1024, 4096),   # BN = 128 (4-stage ring)
+    (32, 6144, 4096),    # Llama-3-8B qkv
+    (32, 4096, 14336),   # Llama-3-8B down
+])
+def test_skinny_gemm_cluster_matches_fp32(M, N, K):
+    prev = llama_ops.set_skinny_gemm_mode("cluster")
+    try:
+        for _ in range(2):  # the second launch reuses nothing from the first
+            _check(M, N, K, 0, seed=M + N)
+    finally:
+        llama_ops.set_skinny_gemm_mode(prev)
+
+
 def test_skinny_gemm_default_ctas_and_rearm():
     # repeated launches with shared tiles: the kernel leaves workspace and tickets zeroed
     M, N, K = 32, 4096, 14336
