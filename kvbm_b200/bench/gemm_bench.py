@@ -55,6 +55,8 @@ def main(argv=None):
     p.add_argument("--replays", type=int, default=5)
     p.add_argument("--ctas", default="0", help="comma list of persistent CTA counts to try (0 = one per SM)")
     p.add_argument("--modes", default="auto", help="comma list of skinny-GEMM modes: auto, streamk, cluster")
+    p.add_argument("--timeline", action="store_true",
+                   help="also print per-phase %%globaltimer stamps of one stream-K launch (after one on another copy)")
     args = p.parse_args(argv)
     torch.cuda.set_device(0)
     want = set(args.shapes.split(","))
@@ -96,6 +98,18 @@ def main(argv=None):
                 row[key + "_gbs"] = round(wbytes / t / 1e6, 1)
                 row[key + "_maxerr"] = round(err, 4)
             llama_ops.set_skinny_gemm_mode("auto")
+            if args.timeline:
+                llama_ops.set_skinny_gemm_mode("streamk")
+
+                def two():
+                    llama_ops.skinny_gemm(x, ws[0], out=out)
+                    llama_ops.skinny_gemm(x, ws[1], out=out)
+
+                two()
+                torch.cuda.synchronize()
+                llama_ops.skinny_gemm(x, ws[0], out=out)  # the stamped launch follows this one
+                row["timeline_us"] = llama_ops.skinny_gemm_timeline(lambda: llama_ops.skinny_gemm(x, ws[1], out=out))
+                llama_ops.set_skinny_gemm_mode("auto")
             row["status"] = llama_ops.skinny_gemm_status()
             print(json.dumps(row), flush=True)
         del ws

@@ -156,7 +156,12 @@ struct GemmParams {
   int ldy;
   float* ws;              // [M, N] fp32 zeros
   unsigned int* tickets;  // [tiles] zeros
+  unsigned long long* timeline;  // optional: 8 %globaltimer stamps per CTA (see kvbm_skinny_gemm_set_timeline)
 };
+
+KVBM_DEVICE void stamp(unsigned long long* tl, int slot) {
+  if (tl) tl[blockIdx.x * 8 + slot] = globaltimer_ns();
+}
 
 // The segments of CTA b, in order. First `rounds` whole tiles (b, b + grid,
 // ...), written straight to Y; then the CTA's equal share of the remaining
@@ -205,12 +210,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ unsigned int ticket;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned long long* tl = P.timeline;
 
   if (threadIdx.x == 32) {
     prefetch_tmap(&map_w);
     prefetch_tmap(&map_x);
   }
   if (threadIdx.x == 0) {
+    stamp(tl, 0);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -231,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = tmem_base;
+  if (threadIdx.x == 0) stamp(tl, 1);
 
   if (warp == 0) {
     // ---- TMA producer ------------------------------------------------------
@@ -249,6 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int early = it;
       grid_dep_wait();  // the activations are the preceding kernel's output
+      stamp(tl, 2);
       SegIter segs(P, blockIdx.x, gridDim.x);
       it = 0;
       bool ok = true;
@@ -288,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          if (it == 0) stamp(tl, 3);
           tc_fence_after();
           const uint8_t* st = smem + s * kStageBytes;
           const uint64_t da = smem_desc_k128(st), db = smem_desc_k128(st + kBytesW);
@@ -299,6 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) umma_commit(&acc_full[a]);
         ++j;
       }
+      stamp(tl, 4);
       // all MMAs complete before TMEM is freed
       umma_commit(&mma_done);
       mbar_wait_bounded(&mma_done, 0, kWaitNs);
@@ -339,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[a]);  // the MMA warp may reuse this accumulator
       }
+      if (et == 0) stamp(tl, 5);  // last accumulator of this CTA drained (overwritten per segment)
       if (!whole) {
         // the tile's last contributor turns the fp32 sum into bf16 and re-arms the workspace
         const int t = tile - P.rounds * static_cast<int>(gridDim.x);  // a stream-K tile
@@ -375,9 +387,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ++j;
     }
+    if (et == 0) stamp(tl, 6);
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) stamp(tl, 7);
   if (warp == 0) tmem_dealloc(tmem_d, kTmemCols);
 }
 
@@ -431,11 +445,6 @@ KVBM_DEVICE bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
-}
-KVBM_DEVICE float ld_dsmem_f32(uint32_t cluster_addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
-  return v;
 }
 // every thread of every CTA in the cluster; used once, right after barrier initialisation
 KVBM_DEVICE void cluster_sync_all() {
@@ -612,23 +621,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this rank's slice of the tile: sum the S partials, convert, store
       const uint32_t base = smem_u32(partial);
       for (int e = e0 + et; e < e1; e += 4 * kEpiThreads) {
-        float acc4[4] = {0.f, 0.f, 0.f, 0.f};
+        // issue every load (4 elements x the other ranks) before the first add
+        float v[4][8];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int ee = e + u * kEpiThreads;
-          if (ee < e1) {
-            float v[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              if (q < S) {
+          for (int q = 0; q < 8; ++q) {
+            v[u][q] = 0.f;
+            if (q < S && ee < e1) {
+              if (q == static_cast<int>(rank)) {
+                v[u][q] = partial[ee];
+              } else {
                 uint32_t ra;
-                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(base + ee * 4u), "r"(q));
-                v[q] = ld_dsmem_f32(ra);
+                asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(base + ee * 4u), "r"(q));
+                asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v[u][q]) : "r"(ra));
               }
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              if (q < S) acc4[u] += v[q];
+            }
           }
+        }
+        float acc4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          acc4[u] = 0.f;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc4[u] += v[u][q];
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -786,6 +803,7 @@ int launch_cluster(const CUtensorMap& mw, const CUtensorMap& mx, const ClusterPa
 }
 
 int g_mode = 0;  // 0: pick by estimated time, 1: stream-K only, 2: cluster split-K only
+unsigned long long* g_timeline = nullptr;  // stream-K launches stamp phases here when set
 
 struct ClusterChoice {
   int S = 0, clusters = 0;
@@ -842,6 +860,15 @@ int run(const CUtensorMap& mw, const CUtensorMap& mx, GemmParams& P, int ctas, c
 
 }  // namespace
 
+// Device buffer of 8 x 64-bit words per CTA (one per SM is enough) that the
+// stream-K kernel fills with %globaltimer stamps: entry, prologue done, grid
+// dependency resolved, first stage landed, last MMA issued, last accumulator
+// drained, fix-ups done, exit. nullptr turns it off (the default).
+extern "C" int kvbm_skinny_gemm_set_timeline(void* buf) {
+  g_timeline = static_cast<unsigned long long*>(buf);
+  return 0;
+}
+
 // 0: choose stream-K or cluster split-K by estimated time (default); 1: stream-K
 // only; 2: cluster split-K only. Returns the previous mode.
 extern "C" int kvbm_skinny_gemm_set_mode(int mode) {
@@ -891,6 +918,7 @@ extern "C" int kvbm_skinny_gemm(const void* x, int ldx, const void* w, int ldw, 
   P.ldy = ldy;
   P.ws = ws;
   P.tickets = tickets;
+  P.timeline = g_timeline;
   switch (bn) {
     case 16: return run<16>(mw, mx, P, ctas, stream);
     case 32: return run<32>(mw, mx, P, ctas, stream);

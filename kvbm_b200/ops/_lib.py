@@ -120,6 +120,7 @@ _SIGS = {
     "kvbm_skinny_gemm_ctas": (_INT, []),
     "kvbm_skinny_gemm_set_pdl": (_INT, [_INT]),
     "kvbm_skinny_gemm_set_mode": (_INT, [_INT]),
+    "kvbm_skinny_gemm_set_timeline": (_INT, [_VP]),
     "kvbm_skinny_gemm_status": (_INT, [_INT]),
     "kvbm_device_alloc": (_INT, [_U64, C.POINTER(_VP)]),
     "kvbm_device_free": (_INT, [_VP]),

@@ -221,3 +221,34 @@ def set_skinny_gemm_mode(mode: str) -> str:
     Returns the previous mode."""
     prev = int(_lib.load().kvbm_skinny_gemm_set_mode(_GEMM_MODES[mode]))
     return {v: k for k, v in _GEMM_MODES.items()}[prev]
+
+
+_TIMELINE_SLOTS = ("entry", "prologue", "grid_dep", "first_stage", "last_mma", "last_drain", "fixup_done", "exit")
+
+
+def skinny_gemm_timeline(run, device=None) -> dict:
+    """Run ``run()`` (which should launch one stream-K :func:`skinny_gemm`) with per-CTA
+    %globaltimer stamps on, and return per-phase statistics in microseconds since the
+    earliest CTA entry: {phase: (median over CTAs, max over CTAs)}."""
+    n_sm = torch.cuda.get_device_properties(device or torch.cuda.current_device()).multi_processor_count
+    buf = torch.zeros(n_sm * 8, dtype=torch.int64, device=device or "cuda")
+    lib = _lib.load()
+    lib.kvbm_skinny_gemm_set_timeline(buf.data_ptr())
+    try:
+        run()
+        torch.cuda.synchronize()
+    finally:
+        lib.kvbm_skinny_gemm_set_timeline(None)
+    t = buf.view(n_sm, 8).cpu()
+    used = t[:, 0] > 0
+    t = t[used]
+    t0 = int(t[:, 0].min())
+    out = {}
+    for i, name in enumerate(_TIMELINE_SLOTS):
+        col = t[:, i]
+        col = col[col > 0]
+        if col.numel():
+            rel = (col - t0).double() / 1e3
+            out[name] = (round(float(rel.median()), 2), round(float(rel.max()), 2))
+    out["ctas"] = int(used.sum())
+    return out
