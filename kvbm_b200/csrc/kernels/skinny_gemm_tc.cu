@@ -144,7 +144,12 @@ KVBM_DEVICE void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-KVBM_DEVICE void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
+// Named barrier of the 4 epilogue warps. bar.sync is warp-aligned: reconverge the
+// warp first (code before it may have run on one lane only).
+KVBM_DEVICE void epi_bar() {
+  __syncwarp();
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+}
 
 struct GemmParams {
   int M, N, K;
@@ -389,6 +394,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (et == 0) stamp(tl, 6);
   }
+  // Lane 0 of warps 0 and 1 ran the producer / MMA loops alone: reconverge each
+  // warp first, so that __syncthreads (an aligned barrier) counts whole warps
+  // only once every thread has arrived - otherwise it can release early and
+  // TMEM would be freed under the epilogue.
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) stamp(tl, 7);
@@ -661,6 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // leave only when no rank still reads this CTA's partial
     if (j > 0) wait_cluster_or_abort(&red_done, (j - 1) & 1, &abort_flag);
   }
+  __syncwarp();  // reconverge the producer and MMA warps (see the stream-K kernel)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_d, kTmemCols);
