@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], mma_done;
+  __shared__ uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], mma_done, teardown;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
   __shared__ unsigned int ticket;
@@ -232,6 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
     }
     mbar_init(&mma_done, 1);
+    mbar_init(&teardown, 5);  // the MMA thread and the 4 epilogue warps, once done with TMEM
     fence_mbar_init();
     abort_flag = 0;
   }
@@ -318,6 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // all MMAs complete before TMEM is freed
       umma_commit(&mma_done);
       mbar_wait_bounded(&mma_done, 0, kWaitNs);
+      tc_fence_before();
+      mbar_arrive(&teardown);
     }
   } else {
     // ---- epilogue: TMEM -> registers -> Y, or the workspace -----------------
@@ -393,16 +396,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++j;
     }
     if (et == 0) stamp(tl, 6);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&teardown);
   }
-  // Lane 0 of warps 0 and 1 ran the producer / MMA loops alone: reconverge each
-  // warp first, so that __syncthreads (an aligned barrier) counts whole warps
-  // only once every thread has arrived - otherwise it can release early and
-  // TMEM would be freed under the epilogue.
+  // TMEM is freed once the MMA thread and every epilogue warp said they are done
+  // with it (an explicit count, independent of how the role warps reconverge).
   __syncwarp();
-  tc_fence_before();
-  __syncthreads();
-  if (threadIdx.x == 0) stamp(tl, 7);
-  if (warp == 0) tmem_dealloc(tmem_d, kTmemCols);
+  if (warp == 0) {
+    mbar_wait_bounded(&teardown, 0, kWaitNs);
+    tc_fence_after();
+    if (lane == 0) stamp(tl, 7);
+    tmem_dealloc(tmem_d, kTmemCols);
+  }
 }
 
 // ---- cluster split-K variant ------------------------------------------------------
@@ -494,7 +500,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* partial = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [M][128] fp32
-  __shared__ uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], mma_done, red_ready, red_done;
+  __shared__ uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], mma_done, red_ready, red_done,
+      teardown;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
 
@@ -520,6 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&mma_done, 1);
     mbar_init(&red_ready, S);
     mbar_init(&red_done, S);
+    mbar_init(&teardown, 5);
     fence_mbar_init();
     abort_flag = 0;
   }
@@ -592,6 +600,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       umma_commit(&mma_done);
       mbar_wait_bounded(&mma_done, 0, kWaitNs);
+      tc_fence_before();
+      mbar_arrive(&teardown);
     }
   } else {
     // ---- epilogue: TMEM -> own partial -> cluster sum of a slice -> Y ---------
@@ -670,11 +680,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // leave only when no rank still reads this CTA's partial
     if (j > 0) wait_cluster_or_abort(&red_done, (j - 1) & 1, &abort_flag);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&teardown);
   }
-  __syncwarp();  // reconverge the producer and MMA warps (see the stream-K kernel)
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem_d, kTmemCols);
+  __syncwarp();
+  if (warp == 0) {  // as in the stream-K kernel
+    mbar_wait_bounded(&teardown, 0, kWaitNs);
+    tc_fence_after();
+    tmem_dealloc(tmem_d, kTmemCols);
+  }
 }
 
 // ---- host side ------------------------------------------------------------------
