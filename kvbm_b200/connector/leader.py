@@ -68,6 +68,8 @@ class SchedulerOutputLite:
     # req_id -> (new token ids appended, new G1 block ids appended, num_computed_tokens after this step)
     scheduled: dict[str, tuple[list[int], list[int], int]] = field(default_factory=dict)
     finished_req_ids: list[str] = field(default_factory=list)
+    # requests the scheduler preempted this step: their G1 blocks return to the framework
+    preempted_req_ids: list[str] = field(default_factory=list)
 
 
 class ConnectorLeader:
@@ -170,6 +172,18 @@ class ConnectorLeader:
         self.iteration += 1
         meta = ConnectorMetadata(step=out.step or self.iteration, onboard=self._onboard_ops)
         self._onboard_ops = []
+        for req_id in out.preempted_req_ids:
+            # The workers fence in-flight offloads of these requests before their G1 blocks are
+            # reused (evict list). The request resumes from its token sequence with new G1 blocks;
+            # what was saved stays in G2 (present blocks are skipped when it is saved again).
+            slot = self.slots.get(req_id)
+            if slot is None:
+                continue
+            meta.evict.append(req_id)
+            slot.g1_block_ids = []
+            slot.save_cursor = 0
+            slot.num_computed_tokens = 0
+            self.leader.stats["preempted"] = self.leader.stats.get("preempted", 0) + 1
         for req_id, (new_tokens, new_blocks, num_computed) in out.scheduled.items():
             slot = self.slots.get(req_id)
             if slot is None:

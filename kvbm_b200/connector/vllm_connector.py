@@ -20,6 +20,7 @@ from typing import Any
 
 from .config import extract_vllm_config_for_kvbm, kv_block_bytes
 from .leader import ConnectorLeader, KvbmRequest, SchedulerOutputLite
+from .protocol import ConnectorMetadata
 
 
 def process_scheduler_output(step: int, so, slots: dict) -> SchedulerOutputLite:
@@ -45,6 +46,7 @@ def process_scheduler_output(step: int, so, slots: dict) -> SchedulerOutputLite:
                     toks = list(cached.new_token_ids[i])
             out.scheduled[rid] = (toks, new_blocks, cached.num_computed_tokens[i] + sched.get(rid, 0))
     out.finished_req_ids = list(getattr(so, "finished_req_ids", []) or [])
+    out.preempted_req_ids = sorted(getattr(so, "preempted_req_ids", None) or [])
     return out
 
 
@@ -159,7 +161,10 @@ def _define():
             self._worker.clear_connector_metadata()
 
         def handle_preemptions(self, kv_connector_metadata):
-            pass
+            # before the preempted requests' G1 blocks are overwritten: wait for their offloads
+            raw = getattr(kv_connector_metadata, "metadata", None)
+            if raw:
+                self._worker.handle_preemptions(ConnectorMetadata.decode(raw).evict)
 
         def start_load_kv(self, forward_context, **kwargs: Any) -> None:
             self._worker.start_load_kv()

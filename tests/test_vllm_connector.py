@@ -74,3 +74,31 @@ def test_scheduler_role_offloads_then_matches():
                                                                           {"b": 3})).metadata)
     assert len(m2.onboard) == 1 and m2.onboard[0].g1_ids == [20, 21, 22, 23, 24]
     assert conn.build_kv_connector_stats() is None
+
+
+def test_preempted_request_is_fenced_and_resumes():
+    from kvbm_b200.connector import vllm_connector as vc
+
+    Role = vllm_base.KVConnectorRole
+    conn = vc.KvbmConnector(_vllm_config({"leader": {"cache": {"host": {"num_blocks": 64}}}}), Role.SCHEDULER)
+    tokens = list(range(5 * 16 + 3))
+    r = _request("p", tokens)
+    assert conn.get_num_new_matched_tokens(r, 0) == (0, False)
+    conn.update_state_after_alloc(r, SimpleNamespace(get_block_ids=lambda: ([10, 11, 12, 13, 14, 15],)), 0)
+    # first chunk: 32 tokens computed -> two full blocks saved
+    m1 = ConnectorMetadata.decode(conn.build_connector_meta(
+        _sched_output([("p", [10, 11, 12, 13, 14, 15])], {"p": 32})).metadata)
+    assert [op.g1_ids for op in m1.offload] == [[10, 11]]
+    assert m1.evict == []
+    # the scheduler preempts it: the workers are told to fence its offloads
+    so = SimpleNamespace(scheduled_new_reqs=[], scheduled_cached_reqs=None, num_scheduled_tokens={},
+                         finished_req_ids=set(), preempted_req_ids={"p"})
+    m2 = ConnectorMetadata.decode(conn.build_connector_meta(so).metadata)
+    assert m2.evict == ["p"] and m2.offload == []
+    # resumed with new G1 blocks and recomputed in full: only the blocks not yet in G2 are saved
+    cached = SimpleNamespace(req_ids=["p"], new_block_ids=[([30, 31, 32, 33, 34, 35],)], num_computed_tokens=[0],
+                             new_token_ids=[[]], all_token_ids={})
+    so3 = SimpleNamespace(scheduled_new_reqs=[], scheduled_cached_reqs=cached, num_scheduled_tokens={"p": 83},
+                          finished_req_ids=set(), preempted_req_ids=None)
+    m3 = ConnectorMetadata.decode(conn.build_connector_meta(so3).metadata)
+    assert [op.g1_ids for op in m3.offload] == [[32, 33, 34]]
