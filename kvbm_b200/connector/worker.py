@@ -106,7 +106,8 @@ class ConnectorWorker:
         if g3 and c.cache.disk.dir:
             path = f"{c.cache.disk.dir}/kvbm_g3_rank{self.rank}.bin"
         self.worker = Worker(self.rank, self.g1, g2_blocks=g2, g3_blocks=g3, g3_path=path, device=self.device,
-                             engine=c.transfer.engine, disk_direct=c.cache.disk.use_direct_io)
+                             engine=c.transfer.engine, disk_direct=c.cache.disk.use_direct_io,
+                             g2_numa_node=c.cache.host.numa_node, g2_hugepages=bool(c.cache.host.hugepages))
 
     def handshake_metadata(self) -> dict:
         """Layout facts the leader needs to size its logical pools."""

@@ -29,7 +29,8 @@ from dataclasses import asdict, dataclass, field
 import torch
 
 from ..ops import _lib
-from .memory import DeviceBuffer, PeerBuffer, PinnedBuffer, SharedHostBuffer, SharedPinnedBuffer
+from .memory import (DeviceBuffer, NumaHostBuffer, PeerBuffer, PinnedBuffer, SharedHostBuffer, SharedPinnedBuffer,
+                     gpu_numa_node)
 
 DTYPE_CODE = {
     torch.float16: _lib.F16,
@@ -222,10 +223,15 @@ class KvLayout:
     def allocate(cls, config: LayoutConfig, kind: str = "fully_contiguous",
                  block_layout: KvBlockLayout = KvBlockLayout.OPERATIONAL_NHD, location: str = "device",
                  block_first: bool = True, fp8_scales: bool = False, device: int | None = None,
-                 zero: bool = False, shm_name: str | None = None) -> "KvLayout":
+                 zero: bool = False, shm_name: str | None = None, numa_node: int | str | None = None,
+                 hugepages: bool = False) -> "KvLayout":
         """Allocate a pool. ``location``: ``device`` (HBM), ``pinned`` (page-locked
         host memory mapped for the GPU) or ``shared`` (a named ``/dev/shm`` file
-        other processes on the node can map; page-locked when CUDA is present)."""
+        other processes on the node can map; page-locked when CUDA is present).
+
+        For ``pinned`` pools, ``numa_node`` places the memory on a NUMA node
+        (``"gpu"``: the node nearest to the current GPU), optionally on 2 MiB
+        ``hugepages``; by default ``cudaHostAlloc`` places it."""
         layer_off, bs, os_, ts, hs, data_bytes = cls._strides(config, kind, block_layout, block_first)
         scales_offset = None
         total = data_bytes
@@ -236,6 +242,11 @@ class KvLayout:
             buf = DeviceBuffer(total, device=device, zero=zero)
             base = buf.ptr
             dev = buf.device
+        elif location == "pinned" and (numa_node is not None or hugepages):
+            node = gpu_numa_node(device) if numa_node in (None, "gpu") else int(numa_node)
+            buf = NumaHostBuffer(total, node=node, hugepages=hugepages)  # zero-filled by first touch
+            base = buf.device_ptr or buf.ptr
+            dev = None
         elif location == "pinned":
             buf = PinnedBuffer(total)
             if zero:

@@ -138,6 +138,115 @@ class PinnedBuffer:
             pass
 
 
+# ---- NUMA placement of host pools ---------------------------------------------
+# Linux x86-64 system call numbers and mempolicy constants (uapi/linux/mempolicy.h).
+_SYS_MBIND, _SYS_GET_MEMPOLICY = 237, 239
+_MPOL_PREFERRED, _MPOL_BIND = 1, 2
+_MPOL_MF_MOVE = 1 << 1
+_MPOL_F_NODE, _MPOL_F_ADDR = 1 << 0, 1 << 1
+
+
+def gpu_numa_node(device: int | None = None) -> int:
+    """NUMA node of the CPU socket nearest to a GPU (from its PCI device in sysfs), or -1."""
+    try:
+        props = torch.cuda.get_device_properties(torch.cuda.current_device() if device is None else device)
+        path = f"/sys/bus/pci/devices/{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0/numa_node"
+        with open(path) as f:
+            return int(f.read().strip())
+    except Exception:
+        return -1
+
+
+def bind_to_numa(ptr: int, nbytes: int, node: int, strict: bool = False) -> bool:
+    """Set the memory policy of the page-aligned range [ptr, ptr + nbytes) to ``node``
+    (MPOL_BIND when ``strict``, else MPOL_PREFERRED), moving pages already touched.
+    Returns False when the kernel refuses (no such node, or a container without
+    CAP_SYS_NICE); the range keeps the default first-touch policy then."""
+    if node < 0 or nbytes <= 0:
+        return False
+    libc = C.CDLL(None, use_errno=True)
+    mask = (C.c_ulong * 16)()
+    if node >= 16 * 64:
+        return False
+    mask[node // 64] = 1 << (node % 64)
+    rc = libc.syscall(_SYS_MBIND, C.c_void_p(ptr), C.c_ulong(nbytes), C.c_int(_MPOL_BIND if strict else _MPOL_PREFERRED),
+                      mask, C.c_ulong(16 * 64 + 1), C.c_uint(_MPOL_MF_MOVE))
+    return rc == 0
+
+
+def numa_node_of(ptr: int) -> int:
+    """NUMA node backing the (touched) page at ``ptr``, or -1."""
+    libc = C.CDLL(None, use_errno=True)
+    node = C.c_int(-1)
+    rc = libc.syscall(_SYS_GET_MEMPOLICY, C.byref(node), None, C.c_ulong(0), C.c_void_p(ptr),
+                      C.c_ulong(_MPOL_F_NODE | _MPOL_F_ADDR))
+    return node.value if rc == 0 else -1
+
+
+class NumaHostBuffer:
+    """Anonymous host memory placed on one NUMA node (the per-NUMA pinned slab of a
+    G2 pool): ``mmap`` (2 MiB huge pages when ``hugepages`` and the system has them),
+    ``mbind`` to ``node`` (default: the node nearest to the current GPU), first touch,
+    then - with CUDA present - page-locked and mapped for the GPU.
+
+    ``numa_bound`` tells whether the policy was applied (containers often refuse
+    ``mbind``; the memory is then placed by first touch from this thread)."""
+
+    def __init__(self, nbytes: int, node: int | None = None, hugepages: bool = False, pin: bool | None = None):
+        import mmap
+
+        self.nbytes = int(nbytes)
+        self.node = gpu_numa_node() if node is None and torch.cuda.is_available() else (-1 if node is None else node)
+        flags = mmap.MAP_PRIVATE | mmap.MAP_ANONYMOUS
+        self.hugepages = False
+        mm = None
+        if hugepages and hasattr(mmap, "MAP_HUGETLB"):
+            try:
+                size = (self.nbytes + (2 << 20) - 1) // (2 << 20) * (2 << 20)
+                mm = mmap.mmap(-1, size, flags | mmap.MAP_HUGETLB, mmap.PROT_READ | mmap.PROT_WRITE)
+                self.hugepages = True
+            except OSError:
+                mm = None
+        if mm is None:
+            mm = mmap.mmap(-1, self.nbytes, flags, mmap.PROT_READ | mmap.PROT_WRITE)
+        self._mm = mm
+        buf = (C.c_uint8 * self.nbytes).from_buffer(mm)
+        self.ptr = C.addressof(buf)
+        del buf
+        self.numa_bound = bind_to_numa(self.ptr, len(mm), self.node) if self.node >= 0 else False
+        C.memset(self.ptr, 0, self.nbytes)  # first touch: pages are allocated under the policy
+        self.pinned = torch.cuda.is_available() if pin is None else pin
+        self.device_ptr = 0
+        if self.pinned:
+            _lib.check(_lib.load().kvbm_host_register(self.ptr, self.nbytes), "cudaHostRegister")
+            d = C.c_void_p()
+            _lib.check(_lib.load().kvbm_host_device_pointer(self.ptr, C.byref(d)), "cudaHostGetDevicePointer")
+            self.device_ptr = int(d.value or 0)
+
+    def tensor(self, dtype: torch.dtype = torch.uint8, shape: tuple | None = None) -> torch.Tensor:
+        arr = (C.c_uint8 * self.nbytes).from_address(self.ptr)
+        t = torch.frombuffer(arr, dtype=torch.uint8)
+        if dtype != torch.uint8:
+            t = t.view(dtype)
+        return t.view(shape) if shape is not None else t
+
+    def close(self) -> None:
+        if self.ptr:
+            if self.pinned:
+                _lib.load().kvbm_host_unregister(self.ptr)
+            self.ptr = 0
+            try:
+                self._mm.close()
+            except BufferError:
+                pass
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 @dataclass
 class ExportedPool:
     """Everything a peer needs to map a pool: IPC handle, size, owner device."""

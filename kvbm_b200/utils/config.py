@@ -35,6 +35,10 @@ SYSTEM_TOML = "/opt/dynamo/etc/kvbm.toml"
 class HostCacheConfig:
     cache_size_gb: float | None = None
     num_blocks: int | None = None
+    # NUMA placement of the G2 pool: None (cudaHostAlloc decides), "gpu" (the node nearest
+    # to the worker's GPU) or a node number; optionally on 2 MiB huge pages
+    numa_node: int | str | None = None
+    hugepages: bool = False
 
 
 @dataclass
@@ -240,6 +244,8 @@ V1_ENV = {
 SHORT_ENV = {
     "KVBM_CACHE_HOST_SIZE_GB": "cache.host.cache_size_gb",
     "KVBM_CACHE_HOST_NUM_BLOCKS": "cache.host.num_blocks",
+    "KVBM_CACHE_HOST_NUMA_NODE": "cache.host.numa_node",
+    "KVBM_CACHE_HOST_HUGEPAGES": "cache.host.hugepages",
     "KVBM_CACHE_DISK_SIZE_GB": "cache.disk.cache_size_gb",
     "KVBM_CACHE_DISK_NUM_BLOCKS": "cache.disk.num_blocks",
     "KVBM_CACHE_DISK_DIR": "cache.disk.dir",

@@ -156,6 +156,22 @@ def test_transfer_to_pinned_host_and_back():
     assert torch.equal(g1b.gather_blocks(s_ids), g1.gather_blocks(s_ids))
 
 
+@pytest.mark.parametrize("hugepages", [False, True])
+def test_transfer_through_numa_placed_pool(hugepages):
+    # G2 on the GPU's NUMA node (huge pages when the host has them), page-locked and mapped
+    cfg = _cfg()
+    g1 = KvLayout.allocate(cfg, "fully_contiguous", NHD)
+    g2 = KvLayout.allocate(cfg, "fully_contiguous", NHD, location="pinned", numa_node="gpu", hugepages=hugepages)
+    assert g2.backing.pinned and g2.backing.device_ptr
+    g1b = KvLayout.allocate(cfg, "fully_contiguous", NHD)
+    _fill(g1, 4)
+    s_ids, d_ids = _pairs(12, 24, 10)
+    kv_ops.kv_transfer(g1, s_ids, g2, d_ids)
+    kv_ops.kv_transfer(g2, d_ids, g1b, s_ids)
+    torch.cuda.synchronize()
+    assert torch.equal(g1b.gather_blocks(s_ids), g1.gather_blocks(s_ids))
+
+
 @pytest.mark.parametrize("nbytes", [1, 7, 16, 4096, 65536 + 48, 2 << 20])
 def test_copy_pairs(nbytes):
     n = 6
