@@ -35,6 +35,7 @@ CUDA_SOURCES = [
     CSRC / "kernels" / "llama_ops.cu",
     CSRC / "kernels" / "kvbm_mem.cu",
     CSRC / "kernels" / "skinny_gemm_tc.cu",
+    CSRC / "kernels" / "gds.cpp",
 ]
 CUDA_HEADERS = [CSRC / "kernels" / "common.cuh", CSRC / "kernels" / "kvbm_kernels.h",
                 CSRC / "kernels" / "decode_attn_mma.cuh"]
@@ -63,7 +64,7 @@ def _run(cmd: list[str]) -> None:
 
 
 def build_cuda(verbose: bool = False) -> Path:
-    """Compile every .cu for sm_100a and link libkvbm_cuda.so."""
+    """Compile every CUDA source for sm_100a (and the cuFile host wrapper) and link libkvbm_cuda.so."""
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     BUILD_DIR.mkdir(parents=True, exist_ok=True)
     nvcc = _nvcc()
@@ -82,7 +83,7 @@ def build_cuda(verbose: bool = False) -> Path:
         with _cf.ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 4)) as ex:
             list(ex.map(_run, jobs))
     if _stale(CUDA_LIB, objs):
-        _run([nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(CUDA_LIB), *map(str, objs)])
+        _run([nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(CUDA_LIB), *map(str, objs), "-ldl"])
     return CUDA_LIB
 
 

@@ -30,7 +30,7 @@ import torch
 
 from ..engine.worker import Worker
 from ..physical.layout import KvLayout
-from ..physical.transfer import TransferOptions
+from ..physical.transfer import TransferCapabilities, TransferOptions
 from ..utils.config import KvbmConfig
 from .dim_probe import (KvDim, infer_from_shape, layout_from_cross_layer_tensor, layout_from_layer_tensors)
 from .protocol import ConnectorMetadata
@@ -105,8 +105,11 @@ class ConnectorWorker:
         path = None
         if g3 and c.cache.disk.dir:
             path = f"{c.cache.disk.dir}/kvbm_g3_rank{self.rank}.bin"
+        caps = TransferCapabilities(allow_gds=c.transfer.allow_gds, allow_gpu_rdma=c.transfer.allow_gpu_rdma,
+                                    cuda_graph_replay=c.transfer.cuda_graph_replay,
+                                    startup_benchmark=c.transfer.startup_benchmark)
         self.worker = Worker(self.rank, self.g1, g2_blocks=g2, g3_blocks=g3, g3_path=path, device=self.device,
-                             engine=c.transfer.engine, disk_direct=c.cache.disk.use_direct_io,
+                             capabilities=caps, engine=c.transfer.engine, disk_direct=c.cache.disk.use_direct_io,
                              g2_numa_node=c.cache.host.numa_node, g2_hugepages=bool(c.cache.host.hugepages))
 
     def handshake_metadata(self) -> dict:

@@ -345,6 +345,8 @@ PYBIND11_MODULE(_kvbm_core, m) {
       .def("read", &DiskPool::read, py::call_guard<py::gil_scoped_release>())
       .def_property_readonly("num_blocks", &DiskPool::num_blocks)
       .def_property_readonly("block_bytes", &DiskPool::block_bytes)
+      .def_property_readonly("fd", &DiskPool::fd)
+      .def_property_readonly("fd_direct", &DiskPool::fd_direct)
       .def_property_readonly("direct", &DiskPool::direct)
       .def_property_readonly("persistent", &DiskPool::persistent)
       .def_property_readonly("path", &DiskPool::path)

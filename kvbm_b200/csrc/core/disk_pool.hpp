@@ -72,6 +72,9 @@ class DiskPool {
   uint64_t block_bytes() const { return block_bytes_; }
   bool direct() const { return direct_; }
   bool persistent() const { return persistent_; }
+  // descriptors of the (possibly already unlinked) file, for other I/O paths such as cuFile
+  int fd() const { return fd_; }
+  int fd_direct() const { return fd_direct_; }
   const std::string& path() const { return path_; }
   uint64_t bytes_written() const { return written_.load(); }
   uint64_t bytes_read() const { return read_.load(); }

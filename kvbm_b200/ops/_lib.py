@@ -122,6 +122,13 @@ _SIGS = {
     "kvbm_skinny_gemm_set_mode": (_INT, [_INT]),
     "kvbm_skinny_gemm_set_timeline": (_INT, [_VP]),
     "kvbm_skinny_gemm_status": (_INT, [_INT]),
+    "kvbm_gds_status": (_INT, []),
+    "kvbm_gds_open": (_INT, [C.c_char_p, _INT, C.POINTER(_VP)]),
+    "kvbm_gds_open_fd": (_INT, [_INT, C.POINTER(_VP)]),
+    "kvbm_gds_close": (_INT, [_VP]),
+    "kvbm_gds_register_buffer": (_INT, [_VP, _U64]),
+    "kvbm_gds_deregister_buffer": (_INT, [_VP]),
+    "kvbm_gds_io": (_I64, [_VP, _INT, _VP, _I64, _I64, _I64]),
     "kvbm_device_alloc": (_INT, [_U64, C.POINTER(_VP)]),
     "kvbm_device_free": (_INT, [_VP]),
     "kvbm_memset_async": (_INT, [_VP, _INT, _U64, _VP]),

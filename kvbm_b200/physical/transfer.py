@@ -26,8 +26,10 @@ transfer/context.rs:333-342 (4+4 streams), notifications/* (completion).
 from __future__ import annotations
 
 import concurrent.futures as cf
+import dataclasses
 import enum
 import itertools
+import logging
 import threading
 import time
 from dataclasses import dataclass, field
@@ -37,6 +39,8 @@ import torch
 from .. import _core_native as core
 from ..ops import kv_ops
 from .layout import KvBlockLayout, KvLayout, LayoutConfig, LayoutDescriptor
+
+log = logging.getLogger(__name__)
 
 
 class StorageKind(str, enum.Enum):
@@ -180,7 +184,18 @@ class DiskLayout:
                  threads: int = 4, block_layout: KvBlockLayout = KvBlockLayout.OPERATIONAL_NHD):
         self.config = config
         self.block_layout = block_layout
+        self.path, self.direct = path, direct
         self.pool = core.DiskPool(path, config.num_blocks, config.bytes_per_block, direct, persistent, threads)
+        self._gds = None
+
+    def gds_file(self):
+        """The file opened for cuFile I/O (GPUDirect Storage), on first use."""
+        if self._gds is None:
+            from .gds import GdsFile
+
+            fd = self.pool.fd_direct if self.pool.fd_direct >= 0 else self.pool.fd  # the file may be unlinked
+            self._gds = GdsFile(self.path, self.config.bytes_per_block, direct=self.direct, fd=fd)
+        return self._gds
 
 
 @dataclass
@@ -214,6 +229,14 @@ class TransferManager:
         self.worker_id = worker_id
         self.device = device
         self.caps = capabilities or TransferCapabilities()
+        if self.caps.allow_gds:
+            from .gds import gds_available, gds_status
+
+            if not gds_available():
+                # cuFile cannot run here: device <-> disk goes through the pinned bounce instead
+                log.warning("GDS requested but cuFile is unavailable (status %d); using the two-hop path",
+                            gds_status())
+                self.caps = dataclasses.replace(self.caps, allow_gds=False)
         self._layouts: dict[int, PhysicalLayout] = {}
         self._ids = itertools.count(1)
         self._lock = threading.Lock()
@@ -416,9 +439,22 @@ class TransferManager:
         else:
             host, disk, h_ids, k_ids = dst.layout, src.layout, d_ids, s_ids
         if not isinstance(host, KvLayout) or host.kind != "fully_contiguous":
-            raise ValueError("disk transfers need a fully contiguous pinned layout")
+            raise ValueError("disk transfers need a fully contiguous layout on the other side")
         if host.block_stride != disk.config.bytes_per_block:
-            raise ValueError("pinned and disk block sizes differ")
+            raise ValueError("memory and disk block sizes differ")
+        if host.location == "device":
+            # GPUDirect Storage: cuFile moves the blocks between HBM and the file
+            if not self.caps.allow_gds:
+                raise ValueError("device <-> disk needs allow_gds (or the two-hop plan)")
+            gds = disk.gds_file()
+            write = strat == TransferStrategy.DISK_WRITE
+            base = host.layer_base(0)
+            if self.device is not None:
+                torch.cuda.current_stream(self.device).synchronize()  # the blocks' producers are done
+            else:
+                torch.cuda.current_stream().synchronize()
+            return TransferCompleteNotification(future=self._io.submit(
+                gds.transfer, write, base, host.block_stride, list(h_ids), list(k_ids)))
         ptrs = [host.layer_base(0) + i * host.block_stride for i in h_ids]
         fn = disk.pool.write if strat == TransferStrategy.DISK_WRITE else disk.pool.read
         return TransferCompleteNotification(future=self._io.submit(fn, list(k_ids), ptrs))

@@ -1,0 +1,52 @@
+"""GPUDirect Storage (cuFile) path of the G3 tier.
+
+CPU: run coalescing, and the transfer manager falling back to the two-hop path
+when cuFile cannot run. GPU: device -> disk -> device through cuFile (its
+compatibility mode where the nvidia-fs driver is absent)."""
+
+import pytest
+import torch
+
+from kvbm_b200.physical.gds import _runs
+
+
+def test_runs_coalesce_consecutive_blocks():
+    assert _runs([(3, 10), (4, 11), (5, 12), (9, 13), (10, 20)]) == [(3, 10, 3), (9, 13, 1), (10, 20, 1)]
+    assert _runs([]) == []
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the fallback where cuFile cannot run")
+def test_manager_falls_back_without_cufile():
+    from kvbm_b200.physical.gds import gds_available
+    from kvbm_b200.physical.transfer import TransferCapabilities, TransferManager
+
+    assert not gds_available()
+    tm = TransferManager(capabilities=TransferCapabilities(allow_gds=True))
+    assert tm.caps.allow_gds is False
+    tm.close()
+
+
+@pytest.mark.gpu
+def test_device_disk_roundtrip_through_cufile(tmp_path):
+    from kvbm_b200.physical.gds import gds_available, gds_status
+    from kvbm_b200.physical.layout import KvBlockLayout, KvLayout, LayoutConfig
+    from kvbm_b200.physical.transfer import DiskLayout, TransferCapabilities, TransferManager
+
+    if not gds_available():
+        pytest.skip(f"cuFile unavailable on this host (status {gds_status()})")
+    cfg = LayoutConfig.for_model(24, 4, 8, 128, 16, torch.bfloat16)  # 256 KiB blocks: O_DIRECT-aligned
+    nhd = KvBlockLayout.OPERATIONAL_NHD
+    g1 = KvLayout.allocate(cfg, "fully_contiguous", nhd)
+    g1b = KvLayout.allocate(cfg, "fully_contiguous", nhd, zero=True)
+    g3 = DiskLayout(cfg, str(tmp_path / "g3.bin"), block_layout=nhd)
+    for l in range(cfg.num_layers):
+        g1.layer_view(l).normal_()
+    tm = TransferManager(device=0, capabilities=TransferCapabilities(allow_gds=True))
+    assert tm.caps.allow_gds
+    h1, h3, h1b = tm.register_layout(g1), tm.register_layout(g3), tm.register_layout(g1b)
+    src, slots, dst = [5, 6, 7, 1, 20], [0, 1, 2, 9, 3], [2, 3, 4, 10, 11]
+    tm.execute_transfer(h1, src, h3, slots).wait()    # device -> disk, no host bounce
+    tm.execute_transfer(h3, slots, h1b, dst).wait()   # disk -> device
+    torch.cuda.synchronize()
+    assert torch.equal(g1b.gather_blocks(dst), g1.gather_blocks(src))
+    tm.close()
