@@ -198,15 +198,21 @@ class NumaHostBuffer:
         self.nbytes = int(nbytes)
         self.node = gpu_numa_node() if node is None and torch.cuda.is_available() else (-1 if node is None else node)
         flags = mmap.MAP_PRIVATE | mmap.MAP_ANONYMOUS
-        self.hugepages = False
+        self.hugepages: str | bool = False  # "hugetlb" (reserved 2 MiB pages), "thp" (transparent) or False
         mm = None
-        if hugepages and hasattr(mmap, "MAP_HUGETLB"):
-            try:
-                size = (self.nbytes + (2 << 20) - 1) // (2 << 20) * (2 << 20)
-                mm = mmap.mmap(-1, size, flags | mmap.MAP_HUGETLB, mmap.PROT_READ | mmap.PROT_WRITE)
-                self.hugepages = True
+        if hugepages:
+            size = (self.nbytes + (2 << 20) - 1) // (2 << 20) * (2 << 20)
+            try:  # reserved huge pages (MAP_HUGETLB, Linux 0x40000)
+                mm = mmap.mmap(-1, size, flags | getattr(mmap, "MAP_HUGETLB", 0x40000), mmap.PROT_READ | mmap.PROT_WRITE)
+                self.hugepages = "hugetlb"
             except OSError:
-                mm = None
+                mm = mmap.mmap(-1, size, flags, mmap.PROT_READ | mmap.PROT_WRITE)
+                if hasattr(mmap, "MADV_HUGEPAGE"):
+                    try:  # transparent huge pages, before the first touch
+                        mm.madvise(mmap.MADV_HUGEPAGE)
+                        self.hugepages = "thp"
+                    except OSError:
+                        pass
         if mm is None:
             mm = mmap.mmap(-1, self.nbytes, flags, mmap.PROT_READ | mmap.PROT_WRITE)
         self._mm = mm

@@ -43,3 +43,11 @@ def test_config_carries_g2_numa_placement():
     assert cfg.cache.host.numa_node == "gpu" and cfg.cache.host.hugepages is True
     cfg = KvbmConfig.load(env={"KVBM_CACHE_HOST_NUMA_NODE": "1"})
     assert cfg.cache.host.numa_node == 1 and cfg.cache.host.hugepages is False
+
+
+def test_hugepage_buffer_falls_back_cleanly():
+    b = NumaHostBuffer(5 << 20, node=0, hugepages=True, pin=False)
+    assert b.hugepages in ("hugetlb", "thp", False)
+    b.tensor()[:10] = 1
+    assert int(b.tensor().sum()) == 10
+    b.close()
