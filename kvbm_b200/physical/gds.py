@@ -19,13 +19,23 @@ import os
 from ..ops import _lib
 
 _status: int | None = None
+PROBE_TIMEOUT_S = 15.0   # cuFile's driver open has been seen not to return in some containers
+IO_TIMEOUT_S = 120.0     # per transfer call
 
 
 def gds_status() -> int:
-    """0 when cuFile is usable, else a reason code (1 no library, 2 missing symbols, >= 1000 driver error)."""
+    """0 when cuFile is usable, else a reason code (1 no library, 2 missing symbols, 3 the
+    driver open did not return within PROBE_TIMEOUT_S, >= 1000 driver error)."""
     global _status
     if _status is None:
-        _status = int(_lib.load().kvbm_gds_status())
+        import threading
+
+        box: list[int] = []
+        t = threading.Thread(target=lambda: box.append(int(_lib.load().kvbm_gds_status())), daemon=True,
+                             name="kvbm-gds-probe")
+        t.start()
+        t.join(PROBE_TIMEOUT_S)
+        _status = box[0] if box else 3
     return _status
 
 
@@ -79,11 +89,11 @@ class GdsFile:
                 raise OSError(f"cuFile {'write' if write else 'read'} of {nbytes} bytes at block {f}: {got}")
 
         for fut in [self._pool.submit(one, r) for r in _runs(list(zip(dev_ids, file_ids)))]:
-            fut.result()
+            fut.result(timeout=IO_TIMEOUT_S)  # a cuFile call that never returns becomes an error here
 
     def close(self) -> None:
         if self._h:
-            self._pool.shutdown(wait=True)
+            self._pool.shutdown(wait=False, cancel_futures=True)
             _lib.load().kvbm_gds_close(self._h)
             self._h = None
 
