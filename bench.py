@@ -38,7 +38,6 @@ import json
 import os
 import statistics
 import sys
-import time
 from datetime import timedelta
 
 import torch

@@ -16,9 +16,7 @@ src/torch/mod.rs:140, src/vllm/config.rs:246, src/hub/prefill_router.rs.
 
 from __future__ import annotations
 
-import json
 import types
-import uuid
 from dataclasses import dataclass, field
 
 from . import __version__

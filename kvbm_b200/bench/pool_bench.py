@@ -19,7 +19,6 @@ from __future__ import annotations
 import argparse
 import collections
 import json
-import random
 import time
 
 import numpy as np

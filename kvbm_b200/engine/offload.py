@@ -33,7 +33,7 @@ import time
 from dataclasses import dataclass
 from typing import Callable, Sequence
 
-from ..logical.manager import BlockManager, ImmutableBlock, Tier
+from ..logical.manager import BlockManager, ImmutableBlock
 from ..utils.config import PipelineConfig
 from ..utils.tracing import audit, nvtx_range
 

@@ -15,7 +15,6 @@ protocol.rs:56 (KvbmCacheEvents{events, instance_id})}.
 from __future__ import annotations
 
 import threading
-import time
 from typing import Callable
 
 import msgpack

@@ -1,7 +1,6 @@
 """Connector leader logic on CPU (no GPU): matching, onboard planning,
 save-cursor offloads, delayed frees; and the step-metadata wire format."""
 
-import pytest
 
 from kvbm_b200.connector.leader import ConnectorLeader, KvbmRequest, SchedulerOutputLite
 from kvbm_b200.connector.protocol import ConnectorMetadata, OffloadOp, OnboardOp

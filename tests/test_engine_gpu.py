@@ -1,8 +1,6 @@
 """Tier transfers through the TransferManager, offload pipelines and the
 InstanceLeader on one GPU (G1 device, G2 pinned host, G3 local disk)."""
 
-import os
-import tempfile
 
 import pytest
 import torch
@@ -16,7 +14,6 @@ from kvbm_b200.engine.worker import Worker
 from kvbm_b200.logical.manager import BlockManager, Tier
 from kvbm_b200.logical.sequence import sequence_hashes
 from kvbm_b200.physical.layout import KvBlockLayout, KvLayout, LayoutConfig
-from kvbm_b200.physical.transfer import TransferOptions
 
 NHD = KvBlockLayout.OPERATIONAL_NHD
 

@@ -2,7 +2,6 @@
 policies, duplicates, registry presence and KV events (after the
 reference's crates/kvbm-logical/src/manager/tests.rs and events/tests.rs)."""
 
-import random
 
 import pytest
 from hypothesis import given, settings

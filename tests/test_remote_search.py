@@ -2,10 +2,8 @@
 indexer, pulls it from A's shared-memory G2 pool (or over the messenger),
 and the connector stalls the request until the blocks are local."""
 
-import time
 
 import pytest
-import torch
 
 from kvbm_b200.connector.leader import ConnectorLeader, KvbmRequest
 from kvbm_b200.engine.leader import InstanceLeader, ParallelWorkers

@@ -7,7 +7,7 @@ import time
 import pytest
 
 from kvbm_b200 import _core_native as core
-from kvbm_b200.engine.offload import (AllOf, AnyOf, OffloadEngine, OffloadItem, OffloadPipeline, OffloadState,
+from kvbm_b200.engine.offload import (AllOf, AnyOf, OffloadItem, OffloadPipeline, OffloadState,
                                       PassAll, PresenceAndLFUFilter, PresenceFilter)
 from kvbm_b200.hub.client import CompletionEvent, HubClient, HubRegistration, PrefillRouterHandler
 from kvbm_b200.hub.kvbmctl import main as kvbmctl

@@ -1,7 +1,6 @@
 """Checksums, fill patterns and the startup-benchmark cache (CPU parts)."""
 
 import numpy as np
-import pytest
 import torch
 
 from kvbm_b200.physical.layout import KvBlockLayout, KvLayout, LayoutConfig
