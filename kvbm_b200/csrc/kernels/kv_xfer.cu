@@ -268,7 +268,6 @@ template <int KIND, int U>
 __device__ __forceinline__ void run_tile(const XferParams& P, const uint8_t* s, int64_t s_rs, uint8_t* d,
                                          int64_t d_rs, int64_t p, int64_t i, int64_t o, int h, int lane) {
   const int rows = P.shape.page_size;
-  const int hd = P.shape.head_dim;
   if constexpr (KIND == kCopy) {
     tile_copy<U>(s, s_rs, d, d_rs, rows, P.fd_upr, lane);
     // fp8 -> fp8 copies carry their scales along.
