@@ -401,7 +401,7 @@ class KvLayout:
             if self.location == "device":
                 t = torch.as_tensor(_RawDev(self.base_ptr, self.nbytes), device=f"cuda:{self.device}")
             elif self.location == "pinned":
-                if isinstance(self.backing, (PinnedBuffer, SharedHostBuffer)):
+                if isinstance(self.backing, (PinnedBuffer, SharedHostBuffer, NumaHostBuffer)):
                     t = self.backing.tensor()
                 else:
                     t = self.backing.view(torch.uint8).reshape(-1)

@@ -39,6 +39,7 @@ import torch
 from .. import _core_native as core
 from ..ops import kv_ops
 from .layout import KvBlockLayout, KvLayout, LayoutConfig, LayoutDescriptor
+from .plan import PreparedPlanCache, lower, plan_copy
 
 log = logging.getLogger(__name__)
 
@@ -247,7 +248,7 @@ class TransferManager:
         self._rr = itertools.count()
         self._io = cf.ThreadPoolExecutor(max_workers=io_threads, thread_name_prefix="kvbm-io")
         self._bounce: PhysicalLayout | None = None
-        self._plan_cache: dict[tuple, str] = {}
+        self._plans = PreparedPlanCache()
         self._bench = None  # StartupBenchmark, created by calibrate() when caps.startup_benchmark is on
         self.stats = {"transfers": 0, "bytes": 0, "failures": 0}
 
@@ -344,29 +345,22 @@ class TransferManager:
         opts.head_range = head_range or opts.head_range
         return self.execute_transfer(src_handle, src_ids, dst_handle, dst_ids, opts)
 
-    def _pick_engine(self, src: KvLayout, dst: KvLayout, opts: TransferOptions) -> str:
-        if opts.engine != "auto":
-            return opts.engine
-        if self.caps.prefer_copy_engine:
-            return "ce"
-        a, b = src.config, dst.config
-        same_geometry = (a.num_layers, a.outer_dim, a.page_size, a.inner_dim, a.dtype_width_bytes) == (
-            b.num_layers, b.outer_dim, b.page_size, b.inner_dim, b.dtype_width_bytes)
-        same = (src.kind == dst.kind == "fully_contiguous" and src.block_layout == dst.block_layout
-                and src.dtype == dst.dtype and opts.layer_range is None and opts.head_range is None
-                and same_geometry and src.block_stride == a.bytes_per_block and dst.block_stride == b.bytes_per_block)
-        if same:
-            return "pairs"
+    def _pick_engine(self, src: KvLayout, dst: KvLayout, opts: TransferOptions, s_ids=(), d_ids=()) -> str:
+        """Plan (``plan.plan_copy``) and lower (``plan.lower``) the transfer; the choice is
+        memoised per layout pair and ranges (it does not depend on the block ids)."""
+        key = PreparedPlanCache.key(src, dst, opts.layer_range, opts.head_range, opts.engine)
+        hit = self._plans.get(key)
+        if hit is not None:
+            return hit.engine
+        plan = plan_copy(src, s_ids, dst, d_ids, opts.layer_range, opts.head_range)
+        bench = None
         if self.caps.startup_benchmark and self._bench is not None:
-            best = self._bench.lookup(src, dst)
-            if best is not None:
-                return best
-        if src.dtype != dst.dtype:
-            # fp8 casts are issue-bound, not copy-bound: the tile kernel's 8 resident CTAs per SM
-            # beat the TMA pipe's one producer + 8 consumer warps (3.8 vs 3.1 TB/s quantising,
-            # 4.2 vs 3.3 TB/s dequantising, 128 Llama-3-8B blocks on B200)
-            return "tile"
-        return "tma"
+            bench = self._bench.lookup(src, dst)
+        low = lower(plan, src, dst, prefer_copy_engine=self.caps.prefer_copy_engine, engine=opts.engine,
+                    bench_choice=bench)
+        if bench is not None or not self.caps.startup_benchmark:
+            self._plans.put(key, low)  # a pair not yet calibrated may get a benchmark result later
+        return low.engine
 
     def calibrate(self, src_handle: int, dst_handle: int) -> str:
         """Run (or load from the cache) the startup benchmark for a layout pair; returns the chosen engine."""
@@ -386,7 +380,7 @@ class TransferManager:
             "d2h" if strat in (TransferStrategy.KERNEL_D2H, TransferStrategy.CUDA_ASYNC_D2H) else "d2d")
         stream = opts.stream or self._stream(kind)
         a, b = src.layout, dst.layout
-        engine = "ce" if strat.value.startswith("cuda_async") else self._pick_engine(a, b, opts)
+        engine = "ce" if strat.value.startswith("cuda_async") else self._pick_engine(a, b, opts, s_ids, d_ids)
         lb, le = opts.layer_range or (0, a.config.num_layers)
         with torch.cuda.stream(stream):
             if engine == "ce":
