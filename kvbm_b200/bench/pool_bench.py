@@ -12,6 +12,9 @@ Remove per sequence hash, in order) against an independent pure-Python model
 of the same pool semantics (LRU eviction) - the "event-log equality" check.
 
     python -m kvbm_b200.bench.pool_bench --blocks 65536 --requests 4096
+    python -m kvbm_b200.bench.pool_bench --micro     # per-block match (active / inactive) and drop
+
+Parity: benches/block_manager.rs (match active hit, inactive hit, bulk drop).
 """
 
 from __future__ import annotations
@@ -134,6 +137,64 @@ def run_batch(workload, blocks: int, backend: str = "lru"):
     return {"hit_rate": hits / max(1, total), "seconds": dt, "blocks": total, "events": log}
 
 
+def micro(n: int = 4096, reps: int = 20, backend: str = "lru") -> dict:
+    """Per-block cost of the pool's three hot calls, as the reference's block-manager
+    micro-benchmarks time them: a prefix match that hits blocks still held by another
+    request (active), one that hits released blocks (inactive: reactivated from the
+    eviction index), and dropping a batch of registered blocks. Native batch calls and
+    Python block handles, ns per block (median of ``reps``)."""
+    hashes = sequence_hashes(list(range(n * 16)), 16)
+    out = {}
+
+    def med(xs):
+        return round(sorted(xs)[len(xs) // 2] * 1e9 / n, 1)
+
+    # native batch API
+    pool = core.BlockPool(n + 8, 16, backend, int(Tier.G2), core.Registry(), "allow")
+    ids, _ = pool.allocate(n)
+    held = [bid for bid, _ in pool.stage_and_register(ids, hashes)]
+    t_act, t_inact, t_drop = [], [], []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        m = pool.match_prefix(hashes)
+        t_act.append(time.perf_counter() - t0)
+        pool.release_many(m)
+    pool.release_many(held)  # every block inactive now
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        m = pool.match_prefix(hashes)
+        t_inact.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        pool.release_many(m)
+        t_drop.append(time.perf_counter() - t0)
+    out["native_batch_ns_per_block"] = {"match_active": med(t_act), "match_inactive": med(t_inact),
+                                        "drop": med(t_drop)}
+    # Python block handles
+    mgr = BlockManager(n + 8, 16, inactive=backend, tier=Tier.G2)
+    got = mgr.allocate_blocks(n)
+    owner = mgr.register_mutable(got, hashes)
+    t_act, t_inact, t_drop = [], [], []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        m = mgr.match_blocks(hashes)
+        t_act.append(time.perf_counter() - t0)
+        for b in m:
+            b.release()
+    for b in owner:
+        b.release()
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        m = mgr.match_blocks(hashes)
+        t_inact.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        for b in m:
+            b.release()
+        t_drop.append(time.perf_counter() - t0)
+    out["handles_ns_per_block"] = {"match_active": med(t_act), "match_inactive": med(t_inact), "drop": med(t_drop)}
+    out["blocks"] = n
+    return out
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--blocks", type=int, default=65536)
@@ -141,7 +202,12 @@ def main(argv=None):
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--backend", default="lru")
     p.add_argument("--check", action="store_true", default=True)
+    p.add_argument("--micro", action="store_true", help="only the per-block match / drop micro-benchmarks")
     a = p.parse_args(argv)
+    if a.micro:
+        out = micro(backend=a.backend)
+        print(json.dumps(out))
+        return out
     wl = make_workload(a.requests, a.seed)
     nat = run_native(wl, a.blocks, a.backend)
     out = {"requests": a.requests, "blocks": a.blocks, "backend": a.backend,

@@ -313,3 +313,12 @@ def test_lock_hierarchy_is_checked():
     blocks = mgr.allocate_blocks(2)
     imm = mgr.register_mutable(blocks, sequence_hashes(list(range(32)), 16))
     assert len(mgr.match_blocks([b.sequence_hash for b in imm])) == 2
+
+
+def test_pool_micro_benchmark_runs():
+    from kvbm_b200.bench.pool_bench import micro
+
+    out = micro(n=64, reps=3)
+    for api in ("native_batch_ns_per_block", "handles_ns_per_block"):
+        assert set(out[api]) == {"match_active", "match_inactive", "drop"}
+        assert all(v > 0 for v in out[api].values())
