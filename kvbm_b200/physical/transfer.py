@@ -25,6 +25,7 @@ transfer/context.rs:333-342 (4+4 streams), notifications/* (completion).
 
 from __future__ import annotations
 
+import collections
 import concurrent.futures as cf
 import dataclasses
 import enum
@@ -249,6 +250,7 @@ class TransferManager:
         self._io = cf.ThreadPoolExecutor(max_workers=io_threads, thread_name_prefix="kvbm-io")
         self._bounce: PhysicalLayout | None = None
         self._plans = PreparedPlanCache()
+        self._ce_graphs: collections.OrderedDict[tuple, torch.cuda.CUDAGraph] = collections.OrderedDict()
         self._bench = None  # StartupBenchmark, created by calibrate() when caps.startup_benchmark is on
         self.stats = {"transfers": 0, "bytes": 0, "failures": 0}
 
@@ -385,7 +387,10 @@ class TransferManager:
         with torch.cuda.stream(stream):
             if engine == "ce":
                 sp, dp, size = self._regions(a, s_ids, b, d_ids, lb, le)
-                kv_ops.memcpy_pairs_ce(sp, dp, size, stream=stream)
+                if self.caps.cuda_graph_replay:
+                    self._replay_ce(sp, dp, size, stream)
+                else:
+                    kv_ops.memcpy_pairs_ce(sp, dp, size, stream=stream)
             elif engine == "pairs":
                 sp = [a.layer_base(0) + i * a.block_stride for i in s_ids]
                 dp = [b.layer_base(0) + i * b.block_stride for i in d_ids]
@@ -403,6 +408,25 @@ class TransferManager:
             ev = torch.cuda.Event()
             ev.record(stream)
         return TransferCompleteNotification(event=ev)
+
+    def _replay_ce(self, sp: list[int], dp: list[int], size: int, stream: torch.cuda.Stream) -> None:
+        """Copy-engine regions as a replayed CUDA graph of memcpy nodes: captured the first
+        time a region list is seen, replayed on ``stream`` afterwards (LRU of 64 graphs)."""
+        key = (tuple(sp), tuple(dp), size)
+        g = self._ce_graphs.get(key)
+        if g is None:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                kv_ops.memcpy_pairs_ce(sp, dp, size, stream=torch.cuda.current_stream())
+            self._ce_graphs[key] = g
+            self.stats["graph_captures"] = self.stats.get("graph_captures", 0) + 1
+            while len(self._ce_graphs) > 64:
+                self._ce_graphs.popitem(last=False)
+        else:
+            self._ce_graphs.move_to_end(key)
+        with torch.cuda.stream(stream):
+            g.replay()
+        self.stats["graph_replays"] = self.stats.get("graph_replays", 0) + 1
 
     @staticmethod
     def _regions(a: KvLayout, s_ids, b: KvLayout, d_ids, lb: int, le: int):
