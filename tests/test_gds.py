@@ -55,3 +55,47 @@ def test_device_disk_roundtrip_through_cufile(tmp_path):
     torch.cuda.synchronize()
     assert torch.equal(g1b.gather_blocks(dst), g1.gather_blocks(src))
     tm.close()
+
+
+class _FakeCuFile:
+    """Stands in for the library's cuFile entry points: records every I/O call."""
+
+    def __init__(self, short_at=None):
+        self.calls, self.short_at = [], short_at
+
+    def kvbm_gds_open_fd(self, fd, out):
+        out._obj.value = 42
+        return 0
+
+    def kvbm_gds_io(self, h, write, dev, dev_off, file_off, nbytes):
+        self.calls.append((write, dev, dev_off, file_off, nbytes))
+        return nbytes // 2 if self.short_at == file_off else nbytes
+
+    def kvbm_gds_close(self, h):
+        return 0
+
+
+def test_gds_file_issues_one_call_per_run(monkeypatch):
+    from kvbm_b200.ops import _lib
+    from kvbm_b200.physical import gds
+
+    fake = _FakeCuFile()
+    monkeypatch.setattr(_lib, "load", lambda *a, **k: fake)
+    f = gds.GdsFile(None, 4096, fd=3)
+    f.transfer(True, 0x1000, 4096, [0, 1, 2, 7], [10, 11, 12, 3])
+    assert sorted(fake.calls) == sorted([(1, 0x1000, 0, 10 * 4096, 3 * 4096), (1, 0x1000, 7 * 4096, 3 * 4096, 4096)])
+    with pytest.raises(ValueError):
+        f.transfer(False, 0x1000, 8192, [0], [0])  # device stride must equal the block size
+    f.close()
+
+
+def test_gds_short_transfer_is_an_error(monkeypatch):
+    from kvbm_b200.ops import _lib
+    from kvbm_b200.physical import gds
+
+    fake = _FakeCuFile(short_at=5 * 4096)
+    monkeypatch.setattr(_lib, "load", lambda *a, **k: fake)
+    f = gds.GdsFile(None, 4096, fd=3)
+    with pytest.raises(OSError):
+        f.transfer(False, 0x2000, 4096, [1], [5])
+    f.close()
