@@ -481,13 +481,17 @@ class TransferManager:
         bounce = opts.bounce or self._bounce
         if bounce is None:
             raise ValueError("two-hop transfer needs a bounce layout (TransferManager.set_bounce)")
-        n = len(s_ids)
-        if n > bounce.config.num_blocks:
-            raise ValueError("transfer larger than the bounce layout")
-        b_ids = list(range(n))
-        first = self._direct(src, s_ids, bounce, b_ids, plan.first, TransferOptions(engine=opts.engine))
-        first.wait()
-        return self._direct(bounce, b_ids, dst, d_ids, plan.second, TransferOptions(engine=opts.engine))
+        cap = bounce.config.num_blocks
+        note = None
+        for i in range(0, len(s_ids), cap):  # transfers larger than the bounce go through it in chunks
+            cs, cd = s_ids[i:i + cap], d_ids[i:i + cap]
+            b_ids = list(range(len(cs)))
+            if note is not None:
+                note.wait()  # the previous chunk's second hop has drained the bounce
+            first = self._direct(src, cs, bounce, b_ids, plan.first, TransferOptions(engine=opts.engine))
+            first.wait()
+            note = self._direct(bounce, b_ids, dst, cd, plan.second, TransferOptions(engine=opts.engine))
+        return note
 
     def close(self) -> None:
         self._io.shutdown(wait=True)

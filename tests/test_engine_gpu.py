@@ -51,6 +51,19 @@ def test_tier_roundtrip_g1_g2_g3(engine, tmp_path):
     w.close()
 
 
+def test_two_hop_larger_than_the_bounce(tmp_path):
+    # 10 blocks through a 4-block bounce: three chunks each way
+    g1 = _g1(kind="fully_contiguous")
+    w = Worker(0, g1, g2_blocks=4, g3_blocks=16, g3_path=str(tmp_path / "g3.bin"), bounce_blocks=4)
+    src, slots, dst = list(range(2, 12)), list(range(3, 13)), list(range(20, 30))
+    ref = g1.gather_blocks(src).clone()
+    w.execute_local_transfer(Tier.G1, src, Tier.G3, slots).wait()
+    w.execute_local_transfer(Tier.G3, slots, Tier.G1, dst).wait()
+    torch.cuda.synchronize()
+    assert torch.equal(_bits(g1.gather_blocks(dst)), _bits(ref))
+    w.close()
+
+
 def test_layer_selection_and_layerwise_onboard():
     g1 = _g1()
     w = Worker(0, g1, g2_blocks=8)
