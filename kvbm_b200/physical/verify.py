@@ -32,7 +32,7 @@ import numpy as np
 import torch
 
 from .layout import KvLayout
-from .memory import PinnedBuffer, SharedPinnedBuffer
+from .memory import NumaHostBuffer, PinnedBuffer, SharedPinnedBuffer
 
 _M1 = np.uint64(0xBF58476D1CE4E5B9)
 _M2 = np.uint64(0x94D049BB133111EB)
@@ -71,6 +71,8 @@ def _device_readable(layout: KvLayout) -> bool:
     b = layout.backing
     if isinstance(b, torch.Tensor):
         return b.is_pinned()
+    if isinstance(b, NumaHostBuffer):
+        return b.pinned
     return isinstance(b, (PinnedBuffer, SharedPinnedBuffer))
 
 
