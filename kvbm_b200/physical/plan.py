@@ -169,7 +169,9 @@ class PreparedPlanCache:
 
     @staticmethod
     def key(src: KvLayout, dst: KvLayout, layer_range, head_range, engine: str) -> tuple:
-        return (layout_signature(src), layout_signature(dst), layer_range, head_range, engine)
+        lr = tuple(layer_range) if layer_range is not None else None  # callers may pass lists
+        hr = tuple(head_range) if head_range is not None else None
+        return (layout_signature(src), layout_signature(dst), lr, hr, engine)
 
     def get(self, key: tuple) -> Lowered | None:
         v = self._d.get(key)
