@@ -35,7 +35,7 @@ class _Bar:
         return self.phase > phase
 
 
-def _run(S, T, seed):
+def _run(S, T, seed, wait_before_overwrite=True):
     rng = random.Random(seed)
     ready = [_Bar(S) for _ in range(S)]
     done = [_Bar(S) for _ in range(S)]
@@ -44,7 +44,7 @@ def _run(S, T, seed):
 
     def rank(r):
         for j in range(T):
-            if j > 0:
+            if j > 0 and wait_before_overwrite:
                 while not done[r].done(j - 1):
                     yield
             partial[r] = j                 # overwrite own partial
@@ -78,15 +78,11 @@ def _run(S, T, seed):
 
 
 def test_model_catches_an_early_overwrite():
-    # the same protocol without the red_done wait before a rank reuses its partial must fail
-    src = open(__file__).read().replace(
-        "            if j > 0:\n                while not done[r].done(j - 1):\n                    yield\n", "")
-    ns: dict = {}
-    exec(compile(src.split("@pytest.mark.parametrize")[0], "broken", "exec"), ns)
+    # without the red_done wait before a rank reuses its partial, some schedule must fail
     failures = 0
     for seed in range(100):
         try:
-            ns["_run"](3, 3, seed)
+            _run(3, 3, seed, wait_before_overwrite=False)
         except AssertionError:
             failures += 1
     assert failures > 0
