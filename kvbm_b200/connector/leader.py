@@ -3,35 +3,54 @@
 Hooks (called by the serving framework's scheduler, one process):
 
 * ``get_num_new_matched_tokens(req_id, num_computed_tokens)`` - how many
-  tokens beyond the framework's own G1 prefix hit can be loaded from G2/G3;
-  matched G2 blocks are held by the slot;
+  tokens beyond the framework's own G1 prefix hit can be loaded from
+  outside: G2/G3 prefix matches (held by the slot), and - with conditional
+  disaggregation on a decode instance - the rest of the prompt when the
+  policy sends its prefill to a prefill instance (an asynchronous load);
 * ``update_state_after_alloc(req_id, block_ids, num_external_tokens)`` -
-  records the G1 destinations and queues the G2 -> G1 onboard;
+  records the G1 destinations, queues the G2 -> G1 onboard and, for a
+  remote prefill, dispatches the request (tokens, ``RemotePrefillParams``,
+  destination block ids, mailbox slot) to the prefill instance and tells the
+  workers to watch for it;
 * ``build_connector_meta(scheduler_output)`` - advances every scheduled
-  request's save cursor: blocks that became complete this step get G2 slots
-  (skipping hashes G2 already holds), are registered in G2 and queued as
-  G1 -> G2 offloads; returns the step's serialized ops for the workers;
-* ``update_connector_output(finished_sending, finished_recving)`` - releases
-  onboarded G2 references and acknowledges finished offloads;
+  request's save cursor (blocks that became complete get G2 slots and are
+  queued as G1 -> G2 offloads; they are registered in G2 only once every
+  worker reports the copy done) and, on a prefill instance, every remote
+  request's push cursor (blocks computed this step are pushed into the
+  decode instance's G1 pool during the pass); returns the step's ops;
+* ``update_connector_output(finished_sending, finished_recving, worker_meta)``
+  - releases onboarded G2 references, registers G2 blocks whose copies
+  landed, closes finished remote prefills (budget, mailbox slot);
 * ``request_finished(req_id)`` - asks the framework to delay freeing G1
-  blocks while an offload still reads them.
+  blocks while an offload or a push still reads them.
 
 Parity: crates/kvbm-connector/src/connector/leader/mod.rs:139-723 (Leader:
 gnmt :449, usaa :462, build_connector_meta :493, request_finished :570,
-update_connector_output :559), python/kvbm/vllm/connector/leader.py:50-347.
+update_connector_output :559), python/kvbm/vllm/connector/leader.py:50-347;
+conditional disaggregation: crates/kvbm-engine/src/remote/cd/decode.rs:118
+(decode-side plan in GNMT), budget.rs:16, tiering/engine/prefill.rs:97
+(prefill accept), remote/cd/output.rs:85 (blocks made available as the
+prefill produces them). Registration after the copy: tiering/offload/
+engine.rs:123 (TransferExecutor -> register_blocks).
 """
 
 from __future__ import annotations
 
+import itertools
 import threading
+from collections import deque
 from dataclasses import dataclass, field
 
+from ..engine.cd import ConditionalDisagg, Decision, RemotePrefillParams
 from ..engine.leader import FindMatchesOptions, InstanceLeader
-from ..logical.manager import ImmutableBlock
+from ..logical.manager import ImmutableBlock, MutableBlock
 from ..logical.sequence import TokenBlockSequence
 from ..utils.metrics import CacheStatsTracker
 from ..utils.tracing import audit
-from .protocol import ConnectorMetadata, OffloadOp, OnboardOp
+from .protocol import ConnectorMetadata, OffloadOp, OnboardOp, PushOp, RecvOp
+
+# kv_transfer_params key a decode instance puts on the requests it sends to a prefill instance
+REMOTE_DECODE_KEY = "kvbm_remote_decode"
 
 
 @dataclass
@@ -42,6 +61,31 @@ class KvbmRequest:
     salt: str | None = None
     max_tokens: int | None = None
     kv_transfer_params: dict | None = None
+
+
+@dataclass
+class RemotePrefill:
+    """Decode side: a request whose prefill runs on a prefill instance."""
+
+    params: RemotePrefillParams
+    target: int
+    slot: int
+    seq: int = 0
+    provided_blocks: int = 0
+    dispatched: bool = False
+
+
+@dataclass
+class PushState:
+    """Prefill side: where a remote request's blocks go and how far they went."""
+
+    peer: int
+    dst_ids: list[int]        # decode G1 blocks of blocks [provided_blocks, prompt_blocks)
+    provided_blocks: int
+    slot: int
+    seq: int
+    cursor: int               # next block index to push
+    in_flight: bool = False   # the final push was issued and has not been reported done
 
 
 @dataclass
@@ -58,6 +102,9 @@ class RequestSlot:
     finished: bool = False
     remote_future: object = None              # in-flight remote search + pull (concurrent.futures.Future)
     remote_done: bool = False
+    cd_decided: bool = False
+    remote_prefill: RemotePrefill | None = None
+    push: PushState | None = None
 
 
 @dataclass
@@ -73,8 +120,22 @@ class SchedulerOutputLite:
 
 
 class ConnectorLeader:
+    """Scheduler-side connector.
+
+    ``cd`` / ``plane`` / ``prefill_target`` turn on conditional
+    disaggregation on a decode instance: ``cd`` decides per request,
+    ``plane`` (``engine.cd_plane.PrefillPlane``) carries the dispatch to the
+    prefill instance ``prefill_target`` (an instance id, or a callable
+    returning one per request), ``mailbox_slots`` bounds the remote prefills
+    in flight (one completion word each). Any instance accepts remote
+    prefills: a request whose ``kv_transfer_params`` carry
+    ``REMOTE_DECODE_KEY`` is pushed to the decode instance named there.
+    """
+
     def __init__(self, leader: InstanceLeader, block_size: int, offload_enabled: bool = True,
-                 decode_offload: bool = False, stats: CacheStatsTracker | None = None, remote_search=None):
+                 decode_offload: bool = False, stats: CacheStatsTracker | None = None, remote_search=None,
+                 cd: ConditionalDisagg | None = None, plane=None, prefill_target=None, instance_id: int = 0,
+                 mailbox_slots: int = 0, recv_timeout_s: float = 120.0, num_workers: int = 1):
         self.leader = leader
         self.remote = remote_search  # engine.remote_search.RemoteSearch, or None
         self.block_size = block_size
@@ -83,8 +144,18 @@ class ConnectorLeader:
         self.slots: dict[str, RequestSlot] = {}
         self.iteration = 0
         self._onboard_ops: list[OnboardOp] = []
+        self._recv_ops: list[RecvOp] = []
         self._lock = threading.Lock()
         self.stats = stats or CacheStatsTracker()
+        self.cd, self.plane, self.prefill_target = cd, plane, prefill_target
+        self.instance_id = instance_id
+        self.recv_timeout_s = recv_timeout_s
+        self._mailbox_free = deque(range(mailbox_slots))
+        self._seq = itertools.count(1)
+        self.num_workers = num_workers
+        # step -> (G2 mutables awaiting their copies, their hashes, worker reports so far)
+        self._pending_g2: dict[int, tuple[list[MutableBlock], list[int], int]] = {}
+        self.cd_stats = {"remote": 0, "local": 0, "dispatched": 0, "received": 0, "failed": 0, "pushed_blocks": 0}
 
     # ---------------------------------------------------------------- slots
     def create_slot(self, request: KvbmRequest) -> RequestSlot:
@@ -93,6 +164,14 @@ class ConnectorLeader:
             salt = request.salt or request.lora_name
             slot = RequestSlot(request, TokenBlockSequence(request.tokens, self.block_size, salt))
             self.slots[request.request_id] = slot
+            remote = (request.kv_transfer_params or {}).get(REMOTE_DECODE_KEY)
+            if remote is not None:
+                # prefill accept: this instance computes the prompt and pushes it to the decode instance
+                pb = int(remote["provided_blocks"])
+                slot.push = PushState(int(remote["instance"]), list(remote["dst_ids"]), pb, int(remote["slot"]),
+                                      int(remote["seq"]), pb)
+                audit("cd_prefill_accept", request=request.request_id, peer=slot.push.peer,
+                      blocks=len(slot.push.dst_ids))
         return slot
 
     def has_slot(self, req_id: str) -> bool:
@@ -101,15 +180,19 @@ class ConnectorLeader:
     # ----------------------------------------------------------------- GNMT
     def get_num_new_matched_tokens(self, req_id: str, num_computed_tokens: int) -> tuple[int | None, bool]:
         slot = self.slots[req_id]
+        if slot.remote_prefill is not None:
+            return len(slot.request.tokens) - num_computed_tokens, True
         for b in slot.matched:
             b.release()
         slot.matched = []
         hashes = slot.seq.sequence_hashes
         start = num_computed_tokens // self.block_size
-        if num_computed_tokens % self.block_size or start >= len(hashes):
+        if num_computed_tokens % self.block_size or start > len(hashes):
             return 0, False
-        res = self.leader.find_matches(hashes[start:], FindMatchesOptions())
-        blocks = res.g2_blocks
+        blocks: list[ImmutableBlock] = []
+        if start < len(hashes):
+            res = self.leader.find_matches(hashes[start:], FindMatchesOptions())
+            blocks = res.g2_blocks
         # the framework must compute at least the last prompt token itself
         max_blocks = (len(slot.request.tokens) - 1 - num_computed_tokens) // self.block_size
         if self.remote is not None and not slot.remote_done and len(blocks) < max_blocks:
@@ -136,13 +219,38 @@ class ConnectorLeader:
             b.release()
         blocks = blocks[: max(0, max_blocks)]
         self.stats.record("host", len(hashes) - start, len(blocks), self.block_size)
-        if not blocks:
-            return 0, False
         slot.matched = blocks
         slot.matched_start_block = start
+        local_tokens = len(blocks) * self.block_size
+        if self._decide_remote(slot, num_computed_tokens, local_tokens):
+            # the held G2 prefix plus everything the prefill instance computes arrive asynchronously
+            return len(slot.request.tokens) - num_computed_tokens, True
+        if not blocks:
+            return 0, False
         if slot.remote_done:
-            audit("gnmt_matched", request=req_id, matched_tokens=len(blocks) * self.block_size)
-        return len(blocks) * self.block_size, True
+            audit("gnmt_matched", request=req_id, matched_tokens=local_tokens)
+        return local_tokens, True
+
+    def _decide_remote(self, slot: RequestSlot, computed: int, local_tokens: int) -> bool:
+        """Decode-side CD decision (policy, breaker tier, in-flight budget, a free mailbox slot)."""
+        if self.cd is None or self.plane is None or slot.push is not None or slot.cd_decided:
+            return False
+        slot.cd_decided = True
+        total = len(slot.request.tokens)
+        if self.cd.decide(total, computed, local_tokens) != Decision.REMOTE:
+            self.cd_stats["local"] += 1
+            return False
+        if not self._mailbox_free:
+            self.cd.finish_remote()  # no completion word free: prefill locally
+            self.cd_stats["local"] += 1
+            return False
+        target = self.prefill_target(slot.request) if callable(self.prefill_target) else self.prefill_target
+        params = RemotePrefillParams(initiator_instance_id=str(self.instance_id),
+                                     decode_endpoint=str(self.instance_id))
+        slot.remote_prefill = RemotePrefill(params, int(target), self._mailbox_free.popleft())
+        self.cd_stats["remote"] += 1
+        audit("cd_decision", request=slot.request.request_id, decision="remote", target=int(target))
+        return True
 
     # ----------------------------------------------------------------- USAA
     def update_state_after_alloc(self, req_id: str, block_ids: list[int], num_external_tokens: int) -> None:
@@ -153,25 +261,57 @@ class ConnectorLeader:
                 b.release()
             slot.matched = []
             return
-        n = num_external_tokens // self.block_size
-        take, rest = slot.matched[:n], slot.matched[n:]
-        for b in rest:
-            b.release()
+        bs = self.block_size
         start = slot.matched_start_block
+        if slot.remote_prefill is not None:
+            take = slot.matched
+        else:
+            n = num_external_tokens // bs
+            take, rest = slot.matched[:n], slot.matched[n:]
+            for b in rest:
+                b.release()
+        n = len(take)
         g1 = slot.g1_block_ids[start: start + n]
         if len(g1) != n:
             raise ValueError(f"{req_id}: {n} onboard blocks but only {len(g1)} G1 destinations")
-        self._onboard_ops.append(OnboardOp(req_id, [b.block_id for b in take], g1))
+        if n:
+            self._onboard_ops.append(OnboardOp(req_id, [b.block_id for b in take], g1))
         slot.onboarding = take
         slot.matched = []
         # onboarded blocks are already in G2: the save cursor skips past them
         slot.save_cursor = max(slot.save_cursor, start + n)
+        if slot.remote_prefill is not None:
+            self._dispatch_remote(slot, start + n)
+
+    def _dispatch_remote(self, slot: RequestSlot, provided_blocks: int) -> None:
+        """Send the request to its prefill instance; the workers watch its mailbox slot."""
+        from ..engine.cd_plane import encode_dispatch
+
+        rp = slot.remote_prefill
+        req = slot.request
+        bs = self.block_size
+        prompt_blocks = (len(req.tokens) + bs - 1) // bs
+        if len(slot.g1_block_ids) < prompt_blocks:
+            raise ValueError(f"{req.request_id}: {len(slot.g1_block_ids)} G1 blocks for a {prompt_blocks}-block prompt")
+        rp.provided_blocks = provided_blocks
+        rp.seq = next(self._seq)
+        rp.params.num_provided_tokens = provided_blocks * bs
+        dst = slot.g1_block_ids[provided_blocks:prompt_blocks]
+        decode = {"instance": self.instance_id, "dst_ids": dst, "slot": rp.slot, "seq": rp.seq,
+                  "provided_blocks": provided_blocks}
+        self.plane.dispatch(rp.target, encode_dispatch(req.request_id, slot.seq.tokens, rp.params.to_dict(), decode,
+                                                      salt=req.salt, lora=req.lora_name))
+        rp.dispatched = True
+        self.cd_stats["dispatched"] += 1
+        self._recv_ops.append(RecvOp(req.request_id, rp.slot, rp.seq, dst, self.recv_timeout_s))
+        audit("cd_dispatch", request=req.request_id, target=rp.target, provided_blocks=provided_blocks,
+              blocks=len(dst), seq=rp.seq)
 
     # ------------------------------------------------------ metadata build
     def build_connector_meta(self, out: SchedulerOutputLite) -> bytes:
         self.iteration += 1
-        meta = ConnectorMetadata(step=out.step or self.iteration, onboard=self._onboard_ops)
-        self._onboard_ops = []
+        meta = ConnectorMetadata(step=out.step or self.iteration, onboard=self._onboard_ops, recv=self._recv_ops)
+        self._onboard_ops, self._recv_ops = [], []
         for req_id in out.preempted_req_ids:
             # The workers fence in-flight offloads of these requests before their G1 blocks are
             # reused (evict list). The request resumes from its token sequence with new G1 blocks;
@@ -184,6 +324,8 @@ class ConnectorLeader:
             slot.save_cursor = 0
             slot.num_computed_tokens = 0
             self.leader.stats["preempted"] = self.leader.stats.get("preempted", 0) + 1
+        g2_pending: list[MutableBlock] = []
+        g2_hashes: list[int] = []
         for req_id, (new_tokens, new_blocks, num_computed) in out.scheduled.items():
             slot = self.slots.get(req_id)
             if slot is None:
@@ -192,6 +334,8 @@ class ConnectorLeader:
                 slot.seq.append(new_tokens)
             slot.g1_block_ids.extend(new_blocks)
             slot.num_computed_tokens = num_computed
+            if slot.push is not None:
+                self._advance_push(slot, num_computed, meta)
             if not self.offload_enabled:
                 continue
             complete = min(num_computed // self.block_size, slot.seq.num_complete_blocks, len(slot.g1_block_ids))
@@ -203,7 +347,8 @@ class ConnectorLeader:
             g1 = slot.g1_block_ids[slot.save_cursor: complete]
             reg = self.leader.g2.registry
             tier = int(self.leader.g2.tier)
-            todo = [(h, b) for h, b in zip(hashes, g1) if not reg.is_present(h, tier)]
+            pending = set(g2_hashes) | self._pending_hashes()
+            todo = [(h, b) for h, b in zip(hashes, g1) if not reg.is_present(h, tier) and h not in pending]
             slot.save_cursor = complete
             if not todo:
                 continue
@@ -211,29 +356,89 @@ class ConnectorLeader:
             if got is None:
                 continue  # G2 full of active blocks: skip this offload
             dst, _ = got
-            imm = self.leader.g2.register_mutable(dst, [h for h, _ in todo])
-            meta.offload.append(OffloadOp(req_id, [b for _, b in todo], [d.block_id for d in imm]))
+            meta.offload.append(OffloadOp(req_id, [b for _, b in todo], [d.block_id for d in dst]))
             slot.pending_offload_steps.add(meta.step)
-            for b in imm:
-                b.release()  # cached in G2 (inactive) once the worker's copy lands
+            g2_pending.extend(dst)
+            g2_hashes.extend(h for h, _ in todo)
             self.leader.stats["offloaded_blocks"] += len(todo)
+        if g2_pending:
+            # registered (and so matchable) only once every worker reports these copies done
+            self._pending_g2[meta.step] = (g2_pending, g2_hashes, 0)
         return meta.encode()
+
+    def _pending_hashes(self) -> set[int]:
+        return {h for _, hs, _ in self._pending_g2.values() for h in hs}
+
+    def _advance_push(self, slot: RequestSlot, num_computed: int, meta: ConnectorMetadata) -> None:
+        """Prefill side: push the blocks whose KV this step computes (the last, partial one with the last chunk)."""
+        ps = slot.push
+        bs = self.block_size
+        prompt_blocks = ps.provided_blocks + len(ps.dst_ids)
+        upto = prompt_blocks if num_computed >= len(slot.request.tokens) else num_computed // bs
+        upto = min(upto, prompt_blocks, len(slot.g1_block_ids))
+        if upto <= ps.cursor:
+            return
+        src = slot.g1_block_ids[ps.cursor: upto]
+        dst = ps.dst_ids[ps.cursor - ps.provided_blocks: upto - ps.provided_blocks]
+        final = upto >= prompt_blocks
+        meta.push.append(PushOp(slot.request.request_id, ps.peer, src, dst, ps.slot, ps.seq, final))
+        ps.cursor = upto
+        ps.in_flight = ps.in_flight or final
+        self.cd_stats["pushed_blocks"] += len(src)
 
     # ------------------------------------------------------ worker output
     def update_connector_output(self, finished_sending: set[str] | None = None,
-                                finished_recving: set[str] | None = None) -> None:
+                                finished_recving: set[str] | None = None, worker_meta: dict | None = None,
+                                invalid_block_ids: set[int] | None = None) -> None:
+        if worker_meta:
+            self._register_landed(worker_meta.get("offloaded", {}))
+        bad = set(invalid_block_ids or ())
         for req_id in finished_recving or ():
             slot = self.slots.get(req_id)
-            if slot is not None:
-                for b in slot.onboarding:
-                    b.release()
-                slot.onboarding = []
+            if slot is None:
+                continue
+            for b in slot.onboarding:
+                b.release()
+            slot.onboarding = []
+            rp = slot.remote_prefill
+            if rp is not None:
+                failed = bool(bad.intersection(slot.g1_block_ids))
+                self._close_remote(slot, failed)
+            if slot.finished and not slot.pending_offload_steps:
+                self._drop(req_id)
         for req_id in finished_sending or ():
             slot = self.slots.get(req_id)
             if slot is not None:
                 slot.pending_offload_steps.clear()
+                if slot.push is not None:
+                    slot.push.in_flight = False
                 if slot.finished:
                     self._drop(req_id)
+
+    def _close_remote(self, slot: RequestSlot, failed: bool) -> None:
+        rp = slot.remote_prefill
+        slot.remote_prefill = None
+        self._mailbox_free.append(rp.slot)
+        if self.cd is not None:
+            self.cd.finish_remote()
+        self.cd_stats["failed" if failed else "received"] += 1
+        audit("cd_received", request=slot.request.request_id, seq=rp.seq, failed=failed)
+
+    def _register_landed(self, offloaded: dict) -> None:
+        """Register the G2 blocks of steps whose offload copies every worker reported done."""
+        for step, n in offloaded.items():
+            step = int(step)
+            entry = self._pending_g2.get(step)
+            if entry is None:
+                continue
+            blocks, hashes, seen = entry
+            seen += int(n)
+            if seen < self.num_workers:
+                self._pending_g2[step] = (blocks, hashes, seen)
+                continue
+            del self._pending_g2[step]
+            for b in self.leader.g2.register_mutable(blocks, hashes):
+                b.release()  # cached in G2 (inactive, matchable)
 
     def request_finished(self, req_id: str, block_ids: list[int] | None = None) -> tuple[bool, dict | None]:
         slot = self.slots.get(req_id)
@@ -243,7 +448,10 @@ class ConnectorLeader:
         for b in slot.matched + slot.onboarding:
             b.release()
         slot.matched, slot.onboarding = [], []
-        if slot.pending_offload_steps:
+        if slot.remote_prefill is not None and slot.remote_prefill.dispatched:
+            # finished (e.g. aborted) before its KV arrived: the workers still watch the slot
+            return True, None
+        if slot.pending_offload_steps or (slot.push is not None and slot.push.in_flight):
             return True, None  # the worker reports it in finished_sending when its copies are done
         self._drop(req_id)
         return False, None

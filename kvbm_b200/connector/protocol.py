@@ -1,11 +1,27 @@
 """Wire format of the per-step connector metadata (leader -> workers).
 
-One msgpack map per scheduler step:
-``{"step": n, "onboard": [[req_id, g2_ids, g1_ids], ...],
-  "offload": [[req_id, g1_ids, g2_ids], ...], "evict": [...]}``.
+One msgpack map per scheduler step::
+
+    {"step": n,
+     "onboard": [[req_id, g2_ids, g1_ids], ...],      # G2 -> G1 before the pass
+     "offload": [[req_id, g1_ids, g2_ids], ...],      # G1 -> G2 after the pass
+     "stage":   [[req_id, g3_ids, g2_ids], ...],      # G3 -> G2 before the onboards
+     "spill":   [[g2_ids, g3_ids], ...],              # G2 -> G3 after the offloads
+     "push":    [[req_id, peer, src, dst, slot, seq, final], ...],
+     "recv":    [[req_id, slot, seq, g1_ids, timeout_s], ...],
+     "evict":   [req_id, ...]}
+
+``push`` / ``recv`` carry conditional disaggregation: a prefill worker
+pushes the listed G1 blocks of a request into the decode instance ``peer``
+(its G1 pool mapped over NVLink) layer batch by layer batch while the
+forward pass runs, and after the pass publishes ``seq`` in mailbox ``slot``
+of that instance (``final``); the decode worker watches that mailbox slot
+and reports the request as received once the value lands.
 
 Parity: crates/kvbm-connector/src/connector/leader/mod.rs:551
 (serialize_metadata, JSON WireMetadata{plan, control}); msgpack here.
+crates/kvbm-protocols/src/disagg.rs:167 (RemotePrefillParams) for what a
+remote prefill carries.
 """
 
 from __future__ import annotations
@@ -30,11 +46,56 @@ class OffloadOp:
 
 
 @dataclass
+class StageOp:
+    """G3 -> G2 for blocks a later onboard of the same step reads."""
+
+    req_id: str
+    g3_ids: list[int]
+    g2_ids: list[int]
+
+
+@dataclass
+class SpillOp:
+    """G2 -> G3 copy of blocks the leader registered in G3 (the G2 -> G3 chain)."""
+
+    g2_ids: list[int]
+    g3_ids: list[int]
+
+
+@dataclass
+class PushOp:
+    """Prefill side: store ``src_ids`` (local G1) into ``dst_ids`` of instance ``peer``'s G1 pool."""
+
+    req_id: str
+    peer: int
+    src_ids: list[int]
+    dst_ids: list[int]
+    slot: int
+    seq: int
+    final: bool
+
+
+@dataclass
+class RecvOp:
+    """Decode side: ``g1_ids`` of ``req_id`` arrive from a remote prefill; done when mailbox ``slot`` reads ``seq``."""
+
+    req_id: str
+    slot: int
+    seq: int
+    g1_ids: list[int]
+    timeout_s: float = 60.0
+
+
+@dataclass
 class ConnectorMetadata:
     step: int = 0
     onboard: list[OnboardOp] = field(default_factory=list)
     offload: list[OffloadOp] = field(default_factory=list)
     evict: list[str] = field(default_factory=list)
+    stage: list[StageOp] = field(default_factory=list)
+    spill: list[SpillOp] = field(default_factory=list)
+    push: list[PushOp] = field(default_factory=list)
+    recv: list[RecvOp] = field(default_factory=list)
 
     def encode(self) -> bytes:
         return msgpack.packb({
@@ -42,10 +103,19 @@ class ConnectorMetadata:
             "onboard": [[o.req_id, o.g2_ids, o.g1_ids] for o in self.onboard],
             "offload": [[o.req_id, o.g1_ids, o.g2_ids] for o in self.offload],
             "evict": self.evict,
+            "stage": [[o.req_id, o.g3_ids, o.g2_ids] for o in self.stage],
+            "spill": [[o.g2_ids, o.g3_ids] for o in self.spill],
+            "push": [[o.req_id, o.peer, o.src_ids, o.dst_ids, o.slot, o.seq, o.final] for o in self.push],
+            "recv": [[o.req_id, o.slot, o.seq, o.g1_ids, o.timeout_s] for o in self.recv],
         }, use_bin_type=True)
 
     @classmethod
     def decode(cls, raw: bytes) -> "ConnectorMetadata":
         d = msgpack.unpackb(raw, raw=False)
         return cls(step=d["step"], onboard=[OnboardOp(*o) for o in d["onboard"]],
-                   offload=[OffloadOp(*o) for o in d["offload"]], evict=list(d.get("evict", [])))
+                   offload=[OffloadOp(*o) for o in d["offload"]], evict=list(d.get("evict", [])),
+                   stage=[StageOp(*o) for o in d.get("stage", [])], spill=[SpillOp(*o) for o in d.get("spill", [])],
+                   push=[PushOp(*o) for o in d.get("push", [])], recv=[RecvOp(*o) for o in d.get("recv", [])])
+
+    def empty(self) -> bool:
+        return not (self.onboard or self.offload or self.evict or self.stage or self.spill or self.push or self.recv)

@@ -29,6 +29,9 @@ def process_scheduler_output(step: int, so, slots: dict) -> SchedulerOutputLite:
     sched = dict(getattr(so, "num_scheduled_tokens", {}) or {})
     for nr in getattr(so, "scheduled_new_reqs", []) or []:
         blocks = list(nr.block_ids[0]) if nr.block_ids else []
+        slot = slots.get(nr.req_id)
+        if slot is not None and slot.g1_block_ids and blocks[: len(slot.g1_block_ids)] == slot.g1_block_ids:
+            blocks = blocks[len(slot.g1_block_ids):]  # update_state_after_alloc already recorded these
         out.scheduled[nr.req_id] = ([], blocks, nr.num_computed_tokens + sched.get(nr.req_id, 0))
     cached = getattr(so, "scheduled_cached_reqs", None)
     if cached is not None:
@@ -57,7 +60,7 @@ def _base():
 
 
 def __getattr__(name):  # lazily build the vLLM subclasses on first access
-    if name in ("KvbmConnector", "KvbmConnectorMetadata"):
+    if name in ("KvbmConnector", "KvbmConnectorMetadata", "KvbmConnectorWorkerMetadata"):
         _define()
         return globals()[name]
     raise AttributeError(name)
@@ -72,6 +75,23 @@ def _define():
         def __init__(self, metadata: bytes):
             assert isinstance(metadata, bytes)
             self.metadata = metadata
+
+    try:
+        from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorWorkerMetadata as WorkerMetaBase
+    except ImportError:  # older vLLM: no worker -> scheduler channel
+        WorkerMetaBase = object
+
+    class KvbmConnectorWorkerMetadata(WorkerMetaBase):
+        """Worker -> scheduler report: steps whose G1 -> G2 copies a worker finished (summed over workers)."""
+
+        def __init__(self, data: dict):
+            self.data = data
+
+        def aggregate(self, other):
+            merged = {int(k): int(v) for k, v in self.data.get("offloaded", {}).items()}
+            for k, v in other.data.get("offloaded", {}).items():
+                merged[int(k)] = merged.get(int(k), 0) + int(v)
+            return KvbmConnectorWorkerMetadata({"offloaded": merged})
 
     class KvbmConnector(Base):
         """KV Block Manager connector for vLLM (scheduler and worker roles)."""
@@ -136,8 +156,11 @@ def _define():
             return KvbmConnectorMetadata(self._leader.build_connector_meta(lite))
 
         def update_connector_output(self, connector_output):
+            wm = getattr(connector_output, "kv_connector_worker_meta", None)
             self._leader.update_connector_output(getattr(connector_output, "finished_sending", None),
-                                                 getattr(connector_output, "finished_recving", None))
+                                                 getattr(connector_output, "finished_recving", None),
+                                                 getattr(wm, "data", None),
+                                                 getattr(connector_output, "invalid_block_ids", None))
 
         def request_finished(self, request, block_ids):
             return self._leader.request_finished(request.request_id, list(block_ids))
@@ -185,9 +208,14 @@ def _define():
         def get_block_ids_with_load_errors(self):
             return self._worker.get_block_ids_with_load_errors()
 
+        def build_connector_worker_meta(self):
+            data = self._worker.build_connector_worker_meta()
+            return KvbmConnectorWorkerMetadata(data) if data else None
+
         def shutdown(self):
             if self._worker is not None:
                 self._worker.shutdown()
 
     globals()["KvbmConnector"] = KvbmConnector
     globals()["KvbmConnectorMetadata"] = KvbmConnectorMetadata
+    globals()["KvbmConnectorWorkerMetadata"] = KvbmConnectorWorkerMetadata

@@ -3,37 +3,53 @@
 Hooks (called by the serving framework's model runner):
 
 * ``register_kv_caches(tensors)`` / ``register_cross_layers_kv_cache(tensor)``
-  - describe the framework's G1 KV tensors as a layout (axis labels from the
-  dimension probe) and build the worker's G2 (pinned) / G3 (disk) pools;
-* ``bind_connector_metadata(raw)`` - the step's onboard/offload ops;
-* ``start_load_kv()`` - G2 -> G1 onboards on the H2D stream (whole blocks,
-  or one transfer per layer with per-layer events in intra mode); the H2D
-  stream first waits for earlier offloads so G2 slots are never read before
-  they are written;
+  / ``register_layout(layout)`` - describe the framework's G1 KV tensors as
+  a layout (axis labels from the dimension probe) and build the worker's G2
+  (pinned) / G3 (disk) pools;
+* ``bind_connector_metadata(raw)`` - the step's ops;
+* ``start_load_kv()`` - G3 -> G2 stages and G2 -> G1 onboards on the H2D
+  stream (whole blocks, or one transfer per layer with per-layer events in
+  intra mode); the H2D stream first waits for earlier offloads so G2 slots
+  are never read before they are written. Remote prefills the leader
+  dispatched start being watched here;
 * ``wait_for_layer_load(layer)`` - intra mode: the compute stream waits on
   that layer's onboard event;
-* ``save_kv_layer(layer)`` - records the layer's compute event;
+* ``save_kv_layer(layer)`` - on a prefill instance, pushes the blocks of
+  remote requests into their decode instance's G1 pool once every
+  ``layer_batch`` layers (one fused transfer launch per batch, in the
+  compute stream right behind the layer's KV write, NVLink stores into the
+  peer's pool);
 * ``wait_for_save()`` - G1 -> G2 offloads on the D2H stream behind the
-  forward pass;
-* ``get_finished(finished_req_ids)`` - requests whose onboards completed
-  (``finished_recving``) and finished requests whose offloads completed
-  (``finished_sending``).
+  forward pass, then G2 -> G3 spills; publishes finished pushes (a
+  system-scope release store of the request's sequence number into the
+  decode instance's host mailbox, behind the last push);
+* ``get_finished(finished_req_ids)`` - requests whose onboards completed or
+  whose remote prefill's mailbox word landed (``finished_recving``; a word
+  that does not land within the timeout reports the request's blocks as
+  load errors) and finished requests whose offloads / pushes completed
+  (``finished_sending``);
+* ``build_connector_worker_meta()`` - the steps whose offload copies this
+  worker completed, so the leader registers those G2 blocks only then.
 
 Parity: python/kvbm/vllm/connector/worker.py:74-602 (KvbmConnectorWorker),
 crates/kvbm-connector/src/connector/worker/mod.rs:57-275,
-crates/kvbm-engine/src/tiering/engine/worker.rs:215-387.
+crates/kvbm-engine/src/tiering/engine/worker.rs:215-387; the push replaces
+the decode side's NIXL pull of the prefill's G2 blocks
+(crates/kvbm-engine/src/leader/instance.rs:1394).
 """
 
 from __future__ import annotations
 
+import time
+
 import torch
 
 from ..engine.worker import Worker
-from ..physical.layout import KvLayout
+from ..physical.layout import KvLayout, LayoutDescriptor
 from ..physical.transfer import TransferCapabilities, TransferOptions
 from ..utils.config import KvbmConfig
 from .dim_probe import (KvDim, infer_from_shape, layout_from_cross_layer_tensor, layout_from_layer_tensors)
-from .protocol import ConnectorMetadata
+from .protocol import ConnectorMetadata, PushOp
 
 
 def blocks_for_bytes(size_gb: float | None, num_blocks: int | None, bytes_per_block: int) -> int:
@@ -42,6 +58,23 @@ def blocks_for_bytes(size_gb: float | None, num_blocks: int | None, bytes_per_bl
     if size_gb:
         return int(size_gb * (1 << 30)) // bytes_per_block
     return 0
+
+
+class PeerConnection:
+    """A decode instance as a prefill worker writes to it: its G1 pool and mailbox."""
+
+    def __init__(self, info: dict, device: int):
+        from ..parallel.pd import MailboxWriter
+
+        if "pool_obj" in info:  # same process (e.g. colocated): the live objects
+            self.pool = info["pool_obj"]
+            self.mailbox = MailboxWriter(info["mailbox"], local=info["mailbox_obj"])
+        else:
+            self.pool = KvLayout.from_descriptor(LayoutDescriptor.from_dict(info["pool"]), device=device)
+            self.mailbox = MailboxWriter(info["mailbox"])
+
+    def close(self) -> None:
+        self.mailbox.close()
 
 
 class ConnectorWorker:
@@ -60,10 +93,22 @@ class ConnectorWorker:
         self._h2d = self._d2h = None
         self._last_offload: torch.cuda.Event | None = None
         self._recv_events: dict[str, torch.cuda.Event] = {}
-        self._send_events: dict[str, torch.cuda.Event] = {}
+        self._send_events: dict[str, list[torch.cuda.Event]] = {}
         self._layer_events: list[torch.cuda.Event] = []
         self._load_errors: set[int] = set()
         self._pending_finished: set[str] = set()
+        self._offload_steps: list[tuple[int, torch.cuda.Event]] = []
+        # conditional disaggregation
+        self.layer_batch = max(1, int(self.config.transfer.layer_batch))
+        self.push_engine = self.config.transfer.push_engine
+        self.instance_id = 0
+        self.directory = None
+        self.mailbox = None
+        self._peers: dict[int, PeerConnection] = {}
+        self._pushes: list[tuple[PushOp, PeerConnection, torch.Tensor, torch.Tensor]] = []
+        self._recvs: dict[str, tuple] = {}
+        self.push_timing = False
+        self._push_timers: list[tuple[torch.cuda.Event, torch.cuda.Event, int]] = []
 
     # --------------------------------------------------------- registration
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor], num_blocks: int | None = None,
@@ -92,6 +137,12 @@ class ConnectorWorker:
         self.g1 = layout_from_cross_layer_tensor(tensor, labels, self.block_size, heads, hd)
         self._build_worker()
         return self.g1
+
+    def register_layout(self, layout: KvLayout) -> KvLayout:
+        """Use an already described G1 pool (a serving engine that allocates its KV through the block manager)."""
+        self.g1 = layout
+        self._build_worker()
+        return layout
 
     def _guess_blocks(self, shape) -> int:
         dims = [d for d in shape[:-1] if d not in (2, self.block_size, self.num_kv_heads)]
@@ -122,6 +173,47 @@ class ConnectorWorker:
                 "g3_blocks": self.worker.g3_layout.config.num_blocks if self.worker.handles.g3 else 0,
                 "block_layout": self.g1.block_layout.value, "kind": self.g1.kind}
 
+    # ------------------------------------------- conditional disaggregation
+    def enable_disagg(self, instance_id: int, directory, mailbox_slots: int = 0, shared: bool = False,
+                      timing: bool = False) -> None:
+        """Join the node's P/D deployment as instance ``instance_id``.
+
+        With ``mailbox_slots`` this worker can receive remote prefills: it
+        allocates the host mailbox (a named shared-memory file when
+        ``shared``, so prefill workers in other processes map it) and
+        publishes its G1 pool and mailbox in ``directory``. Every worker can
+        push (prefill side). ``timing`` brackets each push launch with CUDA
+        events (``take_push_timings``).
+        """
+        from ..parallel.pd import HostMailbox
+
+        self.instance_id, self.directory, self.push_timing = int(instance_id), directory, timing
+        if mailbox_slots:
+            name = f"kvbm_mb_{self.instance_id:x}_{self.rank}" if shared else None
+            self.mailbox = HostMailbox(mailbox_slots, name=name)
+            info = {"mailbox": self.mailbox.descriptor(), "device": self.device, "rank": self.rank}
+            if shared:
+                info["pool"] = self.g1.descriptor().to_dict()
+            else:
+                info.update(pool_obj=self.g1, mailbox_obj=self.mailbox)
+            directory.publish(self.instance_id, info)
+
+    def _peer(self, instance: int) -> PeerConnection:
+        conn = self._peers.get(instance)
+        if conn is None:
+            conn = self._peers[instance] = PeerConnection(self.directory.lookup(instance), self.device)
+        return conn
+
+    def take_push_timings(self) -> tuple[float, int]:
+        """(summed device ms of the push launches, bytes pushed) since the last call; waits for them."""
+        ms = nb = 0
+        for s, e, b in self._push_timers:
+            e.synchronize()
+            ms += s.elapsed_time(e)
+            nb += b
+        self._push_timers.clear()
+        return ms, nb
+
     # ----------------------------------------------------------- per step
     def _streams(self):
         if self._h2d is None:
@@ -131,12 +223,24 @@ class ConnectorWorker:
 
     def bind_connector_metadata(self, raw: bytes) -> None:
         self._meta = ConnectorMetadata.decode(raw)
+        self._pushes = []
+        if self._meta.push:
+            dev = torch.device("cuda", self.device)
+            for op in self._meta.push:
+                ids = torch.tensor(op.src_ids + op.dst_ids, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+                n = len(op.src_ids)
+                self._pushes.append((op, self._peer(op.peer), ids[:n], ids[n:]))
 
     def clear_connector_metadata(self) -> None:
         self._meta = None
+        self._pushes = []
 
     def start_load_kv(self) -> None:
-        if self._meta is None or not self._meta.onboard:
+        meta = self._meta
+        now = time.monotonic()
+        for op in (meta.recv if meta is not None else ()):
+            self._recvs[op.req_id] = (op, now + op.timeout_s)
+        if meta is None or not (meta.onboard or meta.stage):
             self._layer_events = []
             return
         h2d, _ = self._streams()
@@ -144,20 +248,25 @@ class ConnectorWorker:
             h2d.wait_event(self._last_offload)
         intra = self.config.onboard.mode == "intra"
         w = self.worker
+        for op in meta.stage:  # G3 -> G2 ahead of the onboards that read them
+            w.tm.execute_transfer(w.handles.g3, op.g3_ids, w.handles.g2, op.g2_ids,
+                                  TransferOptions(stream=h2d, engine=w.engine)).wait()
         self._layer_events = []
+        if not meta.onboard:
+            return
         if intra:
-            g2 = [i for op in self._meta.onboard for i in op.g2_ids]
-            g1 = [i for op in self._meta.onboard for i in op.g1_ids]
+            g2 = [i for op in meta.onboard for i in op.g2_ids]
+            g1 = [i for op in meta.onboard for i in op.g1_ids]
             for l in range(self.g1.config.num_layers):
                 w.tm.execute_transfer(w.handles.g2, g2, w.handles.g1, g1,
                                       TransferOptions(layer_range=(l, l + 1), stream=h2d, engine=w.engine))
                 ev = torch.cuda.Event()
                 ev.record(h2d)
                 self._layer_events.append(ev)
-            for op in self._meta.onboard:
+            for op in meta.onboard:
                 self._recv_events[op.req_id] = self._layer_events[-1]
         else:
-            for op in self._meta.onboard:
+            for op in meta.onboard:
                 w.tm.execute_transfer(w.handles.g2, op.g2_ids, w.handles.g1, op.g1_ids,
                                       TransferOptions(stream=h2d, engine=w.engine))
                 ev = torch.cuda.Event()
@@ -172,38 +281,107 @@ class ConnectorWorker:
         if layer < len(self._layer_events):
             torch.cuda.current_stream(self.device).wait_event(self._layer_events[layer])
 
-    def save_kv_layer(self, layer: int | str) -> None:
-        # whole-pass offload (wait_for_save) needs no per-layer event; intra-pass
-        # offload would record one here
-        return None
+    def save_kv_layer(self, layer: int | str, requests=None) -> None:
+        """Push the remote requests' layers once a batch of ``layer_batch`` layers is written.
+
+        ``requests`` limits the pushes to those requests (a runner that runs
+        its requests' forward passes one at a time calls this per request);
+        None pushes every remote request of the step.
+        """
+        if not self._pushes:
+            return
+        if isinstance(layer, str):
+            layer = self.layer_names.index(layer)
+        nl = self.g1.config.num_layers
+        lb = self.layer_batch
+        if (layer + 1) % lb and layer != nl - 1:
+            return
+        first = layer - (layer % lb)
+        st = torch.cuda.current_stream(self.device)
+        from ..ops import kv_ops
+
+        for op, conn, src, dst in self._pushes:
+            if requests is not None and op.req_id not in requests:
+                continue
+            if self.push_timing:
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(st)
+            kv_ops.kv_transfer(self.g1, src, conn.pool, dst, layer_begin=first, num_layers=layer + 1 - first,
+                               engine=self.push_engine, stream=st)
+            if self.push_timing:
+                e.record(st)
+                self._push_timers.append((s, e, len(op.src_ids) * (layer + 1 - first) * self.g1.config.outer_dim
+                                          * self.g1.config.bytes_per_chunk))
 
     def wait_for_save(self) -> None:
-        if self._meta is None or not self._meta.offload:
+        meta = self._meta
+        if meta is None:
+            return
+        from ..ops import kv_ops
+
+        st = torch.cuda.current_stream(self.device)
+        for op, conn, _, _ in self._pushes:
+            if op.final:
+                # behind the request's last push in stream order: the decode side may read its blocks
+                kv_ops.signal_flag(conn.mailbox.flag_ptr(op.slot), op.seq, stream=st)
+                ev = torch.cuda.Event()
+                ev.record(st)
+                self._send_events.setdefault(op.req_id, []).append(ev)
+        if not (meta.offload or meta.spill):
             return
         _, d2h = self._streams()
-        d2h.wait_stream(torch.cuda.current_stream(self.device))
+        d2h.wait_stream(st)
         w = self.worker
-        for op in self._meta.offload:
+        for op in meta.offload:
             w.tm.execute_transfer(w.handles.g1, op.g1_ids, w.handles.g2, op.g2_ids,
                                   TransferOptions(stream=d2h, engine=w.engine))
             ev = torch.cuda.Event()
             ev.record(d2h)
-            self._send_events[op.req_id] = ev
+            self._send_events.setdefault(op.req_id, []).append(ev)
             self._last_offload = ev
+        if meta.offload:
+            self._offload_steps.append((meta.step, self._last_offload))
+        for op in meta.spill:  # G2 -> G3 behind this step's offloads
+            if self._last_offload is not None:
+                self._last_offload.synchronize()
+            w.tm.execute_transfer(w.handles.g2, op.g2_ids, w.handles.g3, op.g3_ids,
+                                  TransferOptions(stream=d2h, engine=w.engine)).wait()
 
     def get_finished(self, finished_req_ids: set[str] | None = None) -> tuple[set[str], set[str]]:
         recving = {r for r, ev in self._recv_events.items() if ev.query()}
         for r in recving:
             del self._recv_events[r]
+        if self._recvs:
+            now = time.monotonic()
+            for r, (op, deadline) in list(self._recvs.items()):
+                if r in self._recv_events:
+                    continue  # its local onboard part is still running
+                if self.mailbox is not None and self.mailbox.value(op.slot) == op.seq:
+                    recving.add(r)
+                    del self._recvs[r]
+                elif now > deadline:
+                    # the prefill never published: report the blocks so the framework recomputes them
+                    self._load_errors.update(op.g1_ids)
+                    recving.add(r)
+                    del self._recvs[r]
+        recving -= set(self._recvs)
         self._pending_finished |= set(finished_req_ids or ())
         sending = set()
         for r in list(self._pending_finished):
-            ev = self._send_events.get(r)
-            if ev is None or ev.query():
+            evs = self._send_events.get(r)
+            if not evs or all(ev.query() for ev in evs):
                 sending.add(r)
                 self._pending_finished.discard(r)
                 self._send_events.pop(r, None)
         return sending, recving
+
+    def build_connector_worker_meta(self) -> dict | None:
+        """Steps whose G1 -> G2 copies this worker finished (the leader registers their G2 blocks then)."""
+        done = {}
+        while self._offload_steps and self._offload_steps[0][1].query():
+            step, _ = self._offload_steps.pop(0)
+            done[step] = 1
+        return {"offloaded": done} if done else None
 
     def get_block_ids_with_load_errors(self) -> set[int]:
         out, self._load_errors = self._load_errors, set()
@@ -212,10 +390,15 @@ class ConnectorWorker:
     def handle_preemptions(self, preempted_req_ids) -> None:
         """Fence: wait for in-flight offloads of preempted requests before their G1 blocks are reused."""
         for r in preempted_req_ids or ():
-            ev = self._send_events.pop(r, None)
-            if ev is not None:
+            for ev in self._send_events.pop(r, []):
                 ev.synchronize()
 
     def shutdown(self) -> None:
+        for c in self._peers.values():
+            c.close()
+        self._peers.clear()
+        if self.mailbox is not None:
+            self.mailbox.close()
+            self.mailbox = None
         if self.worker is not None:
             self.worker.close()

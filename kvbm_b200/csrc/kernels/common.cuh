@@ -112,6 +112,35 @@ KVBM_DEVICE void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, 
       : "memory");
 }
 
+// 1-D bulk copy this CTA's shared memory -> global (TMA store), tracked in
+// bulk async-groups. `gmem_dst` 16-byte aligned; `bytes` a multiple of 16.
+KVBM_DEVICE void bulk_s2g(void* gmem_dst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gmem_dst),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+KVBM_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups still read shared memory.
+template <int N>
+KVBM_DEVICE void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until at most N committed bulk groups are incomplete (writes done).
+template <int N>
+KVBM_DEVICE void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// A status word a kernel may write from any thread: plain stores (the word
+// can live in mapped host memory, where device atomics are not available on
+// every host link), made visible at system scope.
+KVBM_DEVICE void report_status(int* status, int code) {
+  if (status != nullptr) {
+    *reinterpret_cast<volatile int*>(status) = code;
+    __threadfence_system();
+  }
+}
+
 // ---- division by a run-time invariant ------------------------------------
 //
 // Granlund & Montgomery, "Division by Invariant Integers using

@@ -554,7 +554,8 @@ struct PipeParams {
   int32_t src_nhd;          // 1: smem rows ordered [token][head], 0: [head][token]
   int64_t run_stride;       // global-memory stride between runs
   int64_t total_chunks;
-  int* status;              // device status word (may be null)
+  int* status;              // status word in mapped host memory (may be null)
+  uint64_t wait_ns;         // limit of every pipeline wait
 };
 
 template <int KIND>
@@ -591,7 +592,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __
       for (int64_t c = blockIdx.x; c < Q.total_chunks && ok; c += gridDim.x, ++k) {
         const int s = static_cast<int>(k % Q.stages);
         const uint32_t phase = static_cast<uint32_t>((k / Q.stages) & 1);
-        if (k >= Q.stages && !mbar_wait_bounded(&empty_bar[s], phase ^ 1u, kPipeWaitNs)) {
+        if (k >= Q.stages && !mbar_wait_bounded(&empty_bar[s], phase ^ 1u, Q.wait_ns)) {
           ok = false;
           break;
         }
@@ -605,7 +606,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __
                                          : static_cast<int64_t>(P.src.head_offset) * P.src.head_stride);
         if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) {
           // Never issue a misaligned bulk copy: record it and stop.
-          if (Q.status) atomicExch(Q.status, kStatusBadIndex);
+          report_status(Q.status, kStatusBadIndex);
           ok = false;
           break;
         }
@@ -616,9 +617,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __
                    static_cast<uint32_t>(Q.run_bytes), &full_bar[s]);
       }
       if (!ok) {
-        if (Q.status) atomicCAS(Q.status, kStatusOk, kStatusPipelineTimeout);
-        // Drain: wait (bounded) for the copies already issued so none are in
-        // flight when the CTA exits.
+        report_status(Q.status, kStatusPipelineTimeout);
+        // Drain: wait (bounded by the full 2 s, whatever the pipeline's own
+        // limit) for the copies already issued so none are in flight when
+        // the CTA exits.
         const int64_t issued = k;
         const int64_t first = issued > Q.stages ? issued - Q.stages : 0;
         for (int64_t kk = first; kk < issued; ++kk) {
@@ -638,8 +640,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __
        c += static_cast<int64_t>(groups) * gridDim.x, k += groups) {
     const int s = static_cast<int>(k % Q.stages);
     const uint32_t phase = static_cast<uint32_t>((k / Q.stages) & 1);
-    if (!mbar_wait_bounded(&full_bar[s], phase, kPipeWaitNs)) {
-      if (Q.status && lane == 0) atomicCAS(Q.status, kStatusOk, kStatusPipelineTimeout);
+    if (!mbar_wait_bounded(&full_bar[s], phase, Q.wait_ns)) {
+      if (lane == 0) report_status(Q.status, kStatusPipelineTimeout);
       break;
     }
     int64_t r = c;
@@ -672,20 +674,131 @@ cudaError_t launch_pipe(PipeParams& Q, int max_ctas, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-}  // namespace
+// ---------------------------------------------------------------------------
+// Bulk copy engine: same-layout, same-dtype chunks moved entirely by the TMA
+// unit. One thread per CTA keeps stages-1 bulk loads (global -> shared) in
+// flight ahead of the bulk stores (shared -> global) that drain them; no SM
+// load/store instruction touches the data, so the copy rate does not follow
+// the SM clock down when the GPU runs at its power cap.
+// ---------------------------------------------------------------------------
 
-extern "C" int kvbm_kv_chunk_xfer_tma(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape,
-                                      int max_ctas, cudaStream_t stream) {
-  PipeParams Q;
+__device__ __forceinline__ const uint8_t* src_chunk(const XferParams& P, int64_t c) {
+  const int O = P.shape.num_outer, L = P.shape.num_layers;
+  int64_t r = c;
+  const int64_t o = r % O;
+  r /= O;
+  const int64_t i = r % L;
+  return chunk_addr(P.src, r / L, i, o);
+}
+
+__device__ __forceinline__ uint8_t* dst_chunk(const XferParams& P, int64_t c) {
+  const int O = P.shape.num_outer, L = P.shape.num_layers;
+  int64_t r = c;
+  const int64_t o = r % O;
+  r /= O;
+  const int64_t i = r % L;
+  return const_cast<uint8_t*>(chunk_addr(P.dst, r / L, i, o));
+}
+
+__global__ void __launch_bounds__(32, 1) kv_bulk_copy_kernel(const __grid_constant__ PipeParams Q) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  if (threadIdx.x != 0) return;
+  const XferParams& P = Q.x;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  uint8_t* stage0 = smem_raw + 1024;
+  const int S = Q.stages;
+  for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+  fence_mbar_init();
+  const int64_t G = gridDim.x;
+  const int64_t n = Q.total_chunks > blockIdx.x ? (Q.total_chunks - blockIdx.x + G - 1) / G : 0;
+  const uint32_t bytes = static_cast<uint32_t>(Q.chunk_bytes);
+  int64_t issued = 0;  // loads issued so far (chunk j of this CTA = blockIdx.x + j * G)
+  bool ok = true;
+  auto load = [&](int64_t j) -> bool {
+    const uint8_t* src = src_chunk(P, blockIdx.x + j * G);
+    if ((reinterpret_cast<uintptr_t>(src) & 15) != 0) return false;
+    const int s = static_cast<int>(j % S);
+    mbar_arrive_expect_tx(&full[s], bytes);
+    bulk_g2s(stage0 + static_cast<int64_t>(s) * Q.stage_bytes, src, bytes, &full[s]);
+    return true;
+  };
+  for (; issued < n && issued < S; ++issued) {
+    if (!load(issued)) {
+      report_status(Q.status, kStatusBadIndex);
+      ok = false;
+      break;
+    }
+  }
+  int64_t j = 0;
+  for (; ok && j < n; ++j) {
+    const int s = static_cast<int>(j % S);
+    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((j / S) & 1), Q.wait_ns)) {
+      report_status(Q.status, kStatusPipelineTimeout);
+      ok = false;
+      break;
+    }
+    uint8_t* dst = dst_chunk(P, blockIdx.x + j * G);
+    if ((reinterpret_cast<uintptr_t>(dst) & 15) != 0) {
+      report_status(Q.status, kStatusBadIndex);
+      ok = false;
+      break;
+    }
+    fence_proxy_async_smem();
+    bulk_s2g(dst, stage0 + static_cast<int64_t>(s) * Q.stage_bytes, bytes);
+    bulk_commit();
+    // refill the previous chunk's stage: its store had this iteration to read shared memory
+    if (j >= 1 && issued < n) {
+      bulk_wait_read<1>();
+      if (!load(issued)) {
+        report_status(Q.status, kStatusBadIndex);
+        ok = false;
+        break;
+      }
+      ++issued;
+    }
+  }
+  if (!ok) {
+    // loads issued but not consumed: wait (bounded) so none lands after the CTA exits
+    for (int64_t k = j; k < issued; ++k)
+      mbar_wait_bounded(&full[k % S], static_cast<uint32_t>((k / S) & 1), kPipeWaitNs);
+  }
+  bulk_wait_all<0>();  // every store complete before the kernel ends
+}
+
+int* g_status_host = nullptr;  // one status word per device, in mapped pinned memory
+uint64_t g_wait_ns_override = 0;
+constexpr int kMaxDevices = 64;
+
+int* status_word() {
+  if (g_status_host == nullptr) {
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, sizeof(int) * kMaxDevices, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess)
+      return nullptr;
+    std::memset(p, 0, sizeof(int) * kMaxDevices);
+    g_status_host = static_cast<int*>(p);
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, g_status_host + dev, 0) != cudaSuccess) return nullptr;
+  return static_cast<int*>(d);
+}
+
+enum XferEngine { kEngineAuto = 0, kEngineTile = 1, kEngineTma = 2 };
+enum XferRan { kRanNone = 0, kRanTile = 1, kRanTmaPipe = 2, kRanTmaBulk = 3 };
+
+// Fills Q for the TMA engines; returns the tile kind, or -1 when the source
+// chunks are not contiguous / aligned (the TMA engines cannot take them).
+int tma_setup(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape, PipeParams& Q) {
   std::memset(&Q, 0, sizeof(Q));
   int unit = 16;
   const int kind = prepare(src, dst, shape, Q.x, &unit);
-  if (kind < 0) return cudaErrorInvalidValue;
-  if (Q.x.total_tiles == 0) return cudaSuccess;
+  if (kind < 0) return -1;
   const KvbmTileShape& S = Q.x.shape;
   const int64_t row = Q.x.src_row_bytes;
   const KvbmSide& s = Q.x.src;
-  if (row % 16 != 0 || (kind == kCopy && Q.x.dst_row_bytes % 16 != 0)) return cudaErrorInvalidValue;
+  if (row % 16 != 0 || (kind == kCopy && Q.x.dst_row_bytes % 16 != 0)) return -1;
   // Find the contiguous runs of one chunk on the source side.
   if (s.head_stride == row) {
     // NHD-like: each token holds its heads back to back.
@@ -710,16 +823,42 @@ extern "C" int kvbm_kv_chunk_xfer_tma(const KvbmSide* src, const KvbmSide* dst, 
       Q.run_stride = s.head_stride;
     }
   } else {
-    return cudaErrorInvalidValue;
+    return -1;
   }
-  if (Q.run_bytes % 16 != 0 || Q.run_stride % 16 != 0) return cudaErrorInvalidValue;
+  if (Q.run_bytes % 16 != 0 || Q.run_stride % 16 != 0) return -1;
   Q.chunk_bytes = Q.run_bytes * Q.num_runs;
   Q.stage_bytes = (Q.chunk_bytes + 127) / 128 * 128;
   const int budget = 200 * 1024;
   Q.stages = std::min(16, budget / Q.stage_bytes);
-  if (Q.stages < 2) return cudaErrorInvalidValue;
+  if (Q.stages < 2) return -1;
   Q.total_chunks = static_cast<int64_t>(S.num_pairs) * S.num_layers * S.num_outer;
-  Q.status = nullptr;
+  Q.status = status_word();
+  Q.wait_ns = g_wait_ns_override ? g_wait_ns_override : kPipeWaitNs;
+  return kind;
+}
+
+// Whether the destination chunk is the source chunk's exact byte image (a
+// whole contiguous chunk in the same layout and dtype).
+bool bulk_eligible(const PipeParams& Q, int kind) {
+  const KvbmSide& s = Q.x.src;
+  const KvbmSide& d = Q.x.dst;
+  return kind == kCopy && Q.num_runs == 1 && s.head_offset == 0 && d.head_offset == 0 &&
+         d.token_stride == s.token_stride && d.head_stride == s.head_stride && Q.x.dst_row_bytes == Q.x.src_row_bytes &&
+         s.scales == nullptr && d.scales == nullptr;
+}
+
+cudaError_t launch_bulk(PipeParams& Q, int max_ctas, cudaStream_t stream) {
+  const size_t smem = 1024 + static_cast<size_t>(Q.stages) * Q.stage_bytes;
+  cudaError_t e =
+      cudaFuncSetAttribute(kv_bulk_copy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const int64_t cap = max_ctas > 0 ? max_ctas : sm_count();
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(Q.total_chunks, cap)));
+  kv_bulk_copy_kernel<<<grid, 32, smem, stream>>>(Q);
+  return cudaGetLastError();
+}
+
+cudaError_t dispatch_pipe(PipeParams& Q, int kind, int max_ctas, cudaStream_t stream) {
   switch (kind) {
     case kCopy: return launch_pipe<kCopy>(Q, max_ctas, stream);
     case kQuantBf16: return launch_pipe<kQuantBf16>(Q, max_ctas, stream);
@@ -731,6 +870,53 @@ extern "C" int kvbm_kv_chunk_xfer_tma(const KvbmSide* src, const KvbmSide* dst, 
     default: return cudaErrorInvalidValue;
   }
 }
+
+}  // namespace
+
+extern "C" int kvbm_kv_chunk_xfer_tma(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape,
+                                      int max_ctas, cudaStream_t stream) {
+  PipeParams Q;
+  const int kind = tma_setup(src, dst, shape, Q);
+  if (kind < 0) return cudaErrorInvalidValue;
+  if (Q.x.total_tiles == 0) return cudaSuccess;
+  return dispatch_pipe(Q, kind, max_ctas, stream);
+}
+
+extern "C" int kvbm_kv_xfer(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape, int engine,
+                            int max_ctas, int flags, int* ran, cudaStream_t stream) {
+  if (ran) *ran = kRanNone;
+  if (engine != kEngineTile) {
+    PipeParams Q;
+    const int kind = tma_setup(src, dst, shape, Q);
+    if (kind >= 0) {
+      if (Q.x.total_tiles == 0) return cudaSuccess;
+      const bool dst_bulk_ok = (flags & KVBM_XFER_DST_LOCAL) || (flags & KVBM_XFER_BULK_PEER);
+      if (dst_bulk_ok && !(flags & KVBM_XFER_NO_BULK) && bulk_eligible(Q, kind)) {
+        if (ran) *ran = kRanTmaBulk;
+        return launch_bulk(Q, max_ctas, stream);
+      }
+      if (ran) *ran = kRanTmaPipe;
+      return dispatch_pipe(Q, kind, max_ctas, stream);
+    }
+    if (engine == kEngineTma) return cudaErrorInvalidValue;  // asked for the TMA engine: never a silent fallback
+  }
+  XferParams P;
+  int unit = 16;
+  const int kind = prepare(src, dst, shape, P, &unit);
+  if (kind < 0) return cudaErrorInvalidValue;
+  if (P.total_tiles == 0) return cudaSuccess;
+  if (ran) *ran = kRanTile;
+  return dispatch_tile(P, kind, unit, max_ctas, stream);
+}
+
+extern "C" int kvbm_xfer_status(int device, int reset) {
+  if (g_status_host == nullptr || device < 0 || device >= kMaxDevices) return 0;
+  const int v = *reinterpret_cast<volatile int*>(g_status_host + device);
+  if (reset) *reinterpret_cast<volatile int*>(g_status_host + device) = 0;
+  return v;
+}
+
+extern "C" void kvbm_xfer_set_wait_limit_ns(uint64_t ns) { g_wait_ns_override = ns; }
 
 // ---------------------------------------------------------------------------
 // Reference-compatible permutes (pointer-table API), expressed as tile

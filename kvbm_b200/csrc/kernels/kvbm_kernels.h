@@ -82,6 +82,33 @@ int kvbm_kv_tile_xfer(const KvbmSide* src, const KvbmSide* dst, const KvbmTileSh
 int kvbm_kv_chunk_xfer_tma(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape, int max_ctas,
                            cudaStream_t stream);
 
+// One entry point for both engines. `engine`: 0 auto (a TMA engine when the
+// source chunks allow it, else the tile kernel), 1 tile, 2 TMA (returns
+// cudaErrorInvalidValue instead of falling back when the TMA engines cannot
+// take the transfer). Among the TMA engines, the bulk copy (TMA loads and TMA
+// stores only, no SM data path) runs when the destination chunk is the
+// source chunk's byte image and `flags` allows TMA stores to the destination
+// (KVBM_XFER_DST_LOCAL: this GPU's memory; KVBM_XFER_BULK_PEER: a peer GPU's
+// memory); otherwise the staged pipeline with consumer warps. `*ran` (may be
+// null) receives which kernel was launched: 1 tile, 2 TMA pipeline, 3 TMA
+// bulk copy.
+#define KVBM_XFER_DST_LOCAL 1
+#define KVBM_XFER_BULK_PEER 2
+#define KVBM_XFER_NO_BULK 4
+int kvbm_kv_xfer(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* shape, int engine, int max_ctas,
+                 int flags, int* ran, cudaStream_t stream);
+
+// Status word the TMA engines write when a bounded wait gives up (3) or a
+// chunk address is misaligned (2); 0 = no error since the last reset. It
+// lives in mapped host memory, so reading it needs no device synchronization
+// (read it after the transfer's stream has passed the launch).
+int kvbm_xfer_status(int device, int reset);
+
+// Test hook: the limit of the TMA engines' pipeline waits for launches made
+// after the call (0 restores the default of 2 s). Waits that drain copies
+// already issued keep the full limit.
+void kvbm_xfer_set_wait_limit_ns(uint64_t ns);
+
 // Split-by-bytes batched copy of num_pairs (src, dst) regions of equal size.
 // `align` is the alignment (16, 8, 4, 2 or 1) that every pointer and
 // `bytes_per_pair` is guaranteed to have.

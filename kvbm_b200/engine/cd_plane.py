@@ -1,0 +1,186 @@
+"""Control plane of conditional disaggregation on one node.
+
+Two small services the decode and prefill instances share:
+
+* a **prefill plane** carries remote-prefill dispatches from a decode
+  leader to a prefill instance's engine: the request's token ids, its
+  ``RemotePrefillParams`` and where its KV goes (the decode instance id,
+  the destination G1 block ids, the mailbox slot and sequence number);
+* a **peer directory** publishes what a prefill worker needs to write into
+  a decode instance: its G1 pool descriptor (a CUDA IPC handle of the pool
+  and its strides) and its mailbox descriptor.
+
+Both come as an in-process version (prefill and decode in one process, e.g.
+sharing a GPU) and as a version over a key-value store (the
+``torch.distributed`` TCPStore of the serving group), and the plane also
+over the hub's disaggregation queue. Messages are msgpack maps; token ids
+travel as raw int32 bytes.
+
+Parity: crates/kvbm-engine/src/remote/cd/wire.rs (PrefillPlane,
+PrefillDispatch), leader/cd/plane.rs (enqueue on the hub CD queue),
+crates/kvbm-physical/src/manager/mod.rs:119-138 (export_metadata /
+import_metadata: here the pool descriptor), crates/kvbm-protocols/src/
+disagg.rs:167 (RemotePrefillParams).
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+from collections import deque
+
+import msgpack
+import numpy as np
+
+
+def encode_dispatch(request_id: str, tokens, params: dict, decode: dict, salt=None, lora=None) -> bytes:
+    toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+    return msgpack.packb({"request_id": request_id, "tokens": toks.tobytes(), "params": params, "decode": decode,
+                          "salt": salt, "lora": lora}, use_bin_type=True)
+
+
+def decode_dispatch(raw: bytes) -> dict:
+    d = msgpack.unpackb(raw, raw=False)
+    d["tokens"] = np.frombuffer(d["tokens"], dtype=np.int32)
+    return d
+
+
+class PrefillPlane:
+    """Dispatch queue of remote prefills, one queue per prefill instance."""
+
+    def dispatch(self, target: int, raw: bytes) -> None:
+        raise NotImplementedError
+
+    def poll(self, instance: int, limit: int | None = None) -> list[dict]:
+        """Dispatches for ``instance`` that have arrived (non-blocking)."""
+        raise NotImplementedError
+
+    def wait(self, instance: int, timeout_s: float, limit: int | None = None) -> list[dict]:
+        """Like :meth:`poll`, but waits up to ``timeout_s`` for at least one."""
+        deadline = time.monotonic() + timeout_s
+        while True:
+            got = self.poll(instance, limit)
+            if got or time.monotonic() >= deadline:
+                return got
+            time.sleep(0.0005)
+
+
+class LocalPrefillPlane(PrefillPlane):
+    def __init__(self):
+        self._q: dict[int, deque] = {}
+        self._cv = threading.Condition()
+
+    def dispatch(self, target, raw):
+        with self._cv:
+            self._q.setdefault(int(target), deque()).append(raw)
+            self._cv.notify_all()
+
+    def poll(self, instance, limit=None):
+        out = []
+        with self._cv:
+            q = self._q.get(int(instance))
+            while q and (limit is None or len(out) < limit):
+                out.append(decode_dispatch(q.popleft()))
+        return out
+
+    def wait(self, instance, timeout_s, limit=None):
+        with self._cv:
+            self._cv.wait_for(lambda: bool(self._q.get(int(instance))), timeout=timeout_s)
+        return self.poll(instance, limit)
+
+
+class StorePrefillPlane(PrefillPlane):
+    """Over a ``torch.distributed`` store: ``{prefix}/{target}/n`` counts the
+    dispatches to ``target`` (an atomic add hands out the slot), message ``i``
+    sits under ``{prefix}/{target}/{i}`` until the consumer takes it."""
+
+    def __init__(self, store, prefix: str = "kvbm/cd/plane"):
+        self.store, self.prefix = store, prefix
+        self._next: dict[int, int] = {}
+
+    def dispatch(self, target, raw):
+        i = int(self.store.add(f"{self.prefix}/{int(target)}/n", 1))
+        self.store.set(f"{self.prefix}/{int(target)}/{i}", raw)
+
+    def poll(self, instance, limit=None):
+        out = []
+        inst = int(instance)
+        while limit is None or len(out) < limit:
+            i = self._next.get(inst, 1)
+            key = f"{self.prefix}/{inst}/{i}"
+            if not self.store.check([key]):
+                break
+            raw = self.store.get(key)
+            self.store.delete_key(key)
+            self._next[inst] = i + 1
+            out.append(decode_dispatch(raw))
+        return out
+
+
+class HubPrefillPlane(PrefillPlane):
+    """Over the hub's disaggregation queue (``/v1/disagg/enqueue`` / ``dequeue``).
+
+    One queue for all prefill instances: whichever polls first serves the
+    request, which is the hub's load-spreading policy for CD dispatches.
+    """
+
+    def __init__(self, client):
+        self.client = client
+
+    def dispatch(self, target, raw):
+        self.client.cd_enqueue({"target": int(target), "payload": raw.hex()})
+
+    def poll(self, instance, limit=None):
+        out = []
+        while limit is None or len(out) < limit:
+            r = self.client.cd_dequeue()
+            if not r:
+                break
+            out.append(decode_dispatch(bytes.fromhex(r["payload"])))
+        return out
+
+
+class PeerDirectory:
+    """Where each decode instance's G1 pool and mailbox can be found."""
+
+    def publish(self, instance: int, info: dict) -> None:
+        raise NotImplementedError
+
+    def lookup(self, instance: int, timeout_s: float = 60.0) -> dict:
+        raise NotImplementedError
+
+
+class LocalPeerDirectory(PeerDirectory):
+    """In-process: ``info`` may hold the live objects (``pool_obj``, ``mailbox_obj``)."""
+
+    def __init__(self):
+        self._d: dict[int, dict] = {}
+        self._cv = threading.Condition()
+
+    def publish(self, instance, info):
+        with self._cv:
+            self._d[int(instance)] = info
+            self._cv.notify_all()
+
+    def lookup(self, instance, timeout_s=60.0):
+        with self._cv:
+            if not self._cv.wait_for(lambda: int(instance) in self._d, timeout=timeout_s):
+                raise TimeoutError(f"instance {instance} never published its pool")
+            return self._d[int(instance)]
+
+
+class StorePeerDirectory(PeerDirectory):
+    def __init__(self, store, prefix: str = "kvbm/cd/peer"):
+        self.store, self.prefix = store, prefix
+
+    def publish(self, instance, info):
+        self.store.set(f"{self.prefix}/{int(instance)}", msgpack.packb(info, use_bin_type=True))
+
+    def lookup(self, instance, timeout_s=60.0):
+        key = f"{self.prefix}/{int(instance)}"
+        deadline = time.monotonic() + timeout_s
+        while not self.store.check([key]):
+            if time.monotonic() >= deadline:
+                raise TimeoutError(f"instance {instance} never published its pool")
+            time.sleep(0.005)
+        return msgpack.unpackb(self.store.get(key), raw=False)

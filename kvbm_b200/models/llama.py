@@ -170,13 +170,15 @@ class LlamaModel:
     # ------------------------------------------------------------ prefill
     @torch.inference_mode()
     def prefill(self, tokens: torch.Tensor, pool: KvLayout, block_ids: torch.Tensor, start_pos: int = 0,
-                on_layer_done=None, kv_push: "KvPush | None" = None) -> torch.Tensor:
+                on_layer_done=None, kv_push: "KvPush | None" = None, on_layer_start=None) -> torch.Tensor:
         """Prefill ``tokens`` [T] at positions [start_pos, start_pos+T).
 
         K/V land in ``pool`` blocks ``block_ids`` (int32, device; block j holds
         positions [16j, 16j+16) of the sequence). ``on_layer_done(layer)`` is
         called on the host right after layer ``layer``'s K/V writes are enqueued
-        on the current stream. With ``kv_push`` the kernel that rotates and
+        on the current stream, ``on_layer_start(layer)`` before the layer reads
+        the pool (a layer-wise onboard makes the stream wait for that layer
+        there). With ``kv_push`` the kernel that rotates and
         writes each layer's K/V also stores it into ``kv_push.remote`` (a
         decode pool, possibly a peer GPU's), and the local pool write is
         skipped unless ``kv_push.local_write``. Returns the greedy next token
@@ -192,6 +194,8 @@ class LlamaModel:
         h = torch.empty_like(x)
         first = True
         for li, L in enumerate(self.layers):
+            if on_layer_start is not None:
+                on_layer_start(li)
             if first:
                 llama_ops.rmsnorm(x, L["n1"], c.eps, out=h)
                 first = False

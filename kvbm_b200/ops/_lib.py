@@ -70,6 +70,10 @@ _SZ = C.c_size_t
 _SIGS = {
     "kvbm_kv_tile_xfer": (_INT, [C.POINTER(KvbmSide), C.POINTER(KvbmSide), C.POINTER(KvbmTileShape), _INT, _VP]),
     "kvbm_kv_chunk_xfer_tma": (_INT, [C.POINTER(KvbmSide), C.POINTER(KvbmSide), C.POINTER(KvbmTileShape), _INT, _VP]),
+    "kvbm_kv_xfer": (_INT, [C.POINTER(KvbmSide), C.POINTER(KvbmSide), C.POINTER(KvbmTileShape), _INT, _INT, _INT,
+                            C.POINTER(_INT), _VP]),
+    "kvbm_xfer_status": (_INT, [_INT, _INT]),
+    "kvbm_xfer_set_wait_limit_ns": (None, [_U64]),
     "kvbm_copy_pairs": (_INT, [_VP, _VP, _U64, _U64, _INT, _INT, _VP]),
     "kvbm_universal_from_block": (_INT, [_VP, _VP, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _INT, _INT, _VP]),
     "kvbm_block_from_universal": (_INT, [_VP, _VP, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _INT, _INT, _VP]),
@@ -158,7 +162,7 @@ class KvbmCudaError(RuntimeError):
 # Kernels launched per successful call of each entry point. The benchmark
 # reports how many of this library's kernels ran inside its timed region.
 _KERNELS_PER_CALL = {
-    "kvbm_kv_tile_xfer": 1, "kvbm_kv_chunk_xfer_tma": 1, "kvbm_copy_pairs": 1, "kvbm_universal_from_block": 1,
+    "kvbm_kv_tile_xfer": 1, "kvbm_kv_chunk_xfer_tma": 1, "kvbm_kv_xfer": 1, "kvbm_copy_pairs": 1, "kvbm_universal_from_block": 1,
     "kvbm_block_from_universal": 1, "kvbm_nhd_hnd_transpose": 1, "kvbm_signal_flag": 1, "kvbm_wait_flag": 1,
     "kvbm_signal_flag_payload": 1, "kvbm_wait_flags_all": 1, "kvbm_rmsnorm": 1, "kvbm_rope_kv_write": 1,
     "kvbm_rope_kv_push": 1, "kvbm_rope_kv_write_qout": 1, "kvbm_rope_kv_push_heads": 1,

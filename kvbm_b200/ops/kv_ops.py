@@ -54,10 +54,16 @@ def _ids(ids, device, stream=None) -> torch.Tensor:
     return upload(t, device, stream) if device is not None else t
 
 
+ENGINE_CODES = {"auto": 0, "tile": 1, "tma": 2}
+RAN_NAMES = {1: "tile", 2: "tma", 3: "tma_bulk"}
+XFER_DST_LOCAL, XFER_BULK_PEER, XFER_NO_BULK = 1, 2, 4
+
+
 def kv_transfer(src, src_ids, dst, dst_ids, *, layer_begin: int = 0, num_layers: int | None = None,
                 dst_layer_begin: int | None = None, src_head_offset: int = 0, dst_head_offset: int = 0,
-                num_heads: int | None = None, engine: str = "tile", max_ctas: int = 0, stream=None) -> None:
-    """Copy blocks ``src_ids`` of ``src`` into blocks ``dst_ids`` of ``dst``.
+                num_heads: int | None = None, engine: str = "tile", max_ctas: int = 0, stream=None,
+                bulk: bool | None = None) -> str:
+    """Copy blocks ``src_ids`` of ``src`` into blocks ``dst_ids`` of ``dst``; returns the kernel that ran.
 
     Fuses, in one launch: the layout transform between the two pools (FC/LW,
     NHD/HND/universal), a KV-head slice (``num_heads`` heads starting at
@@ -66,15 +72,22 @@ def kv_transfer(src, src_ids, dst, dst_ids, *, layer_begin: int = 0, num_layers:
     the pool dtypes differ. ``dst`` may be a peer GPU's pool mapped over
     NVLink (``KvLayout.from_descriptor``) or a pinned host pool (G2).
 
-    ``engine``: ``"tile"`` (warp per head tile, direct 16-byte loads) or
-    ``"tma"`` (bulk async copies staged through shared memory; falls back to
-    ``"tile"`` when the source chunk is not contiguous).
+    ``engine``: ``"tile"`` (warp per head tile, direct 16-byte loads),
+    ``"tma"`` (bulk async copies staged through shared memory; raises when
+    the source chunks are not contiguous / aligned, never falls back) or
+    ``"auto"`` (``"tma"`` when it can, else ``"tile"``). Among the TMA
+    kernels, same-layout whole-chunk copies run as the bulk copy (TMA loads
+    and TMA stores only) when the destination is this GPU's memory, or any
+    memory when ``bulk`` is True (``bulk=False`` never uses it). Returns
+    ``"tile"``, ``"tma"`` or ``"tma_bulk"``.
     """
     n_pairs = len(src_ids)
     if n_pairs != len(dst_ids):
         raise ValueError("src_ids and dst_ids differ in length")
+    if engine not in ENGINE_CODES:
+        raise ValueError(f"unknown transfer engine {engine!r}")
     if n_pairs == 0:
-        return
+        return "none"
     sc, dc = src.config, dst.config
     nl = sc.num_layers - layer_begin if num_layers is None else num_layers
     dlb = layer_begin if dst_layer_begin is None else dst_layer_begin
@@ -97,14 +110,44 @@ def kv_transfer(src, src_ids, dst, dst_ids, *, layer_begin: int = 0, num_layers:
         for t in (sid, did):
             if t.is_cuda:
                 t.record_stream(stream)
-    if engine == "tma":
-        # falls through to the tile engine when the source chunks are not
-        # contiguous / aligned (the TMA entry point rejects before launching)
-        if lib.kvbm_kv_chunk_xfer_tma(C.byref(s), C.byref(d), C.byref(shape), max_ctas, st) == 0:
-            _lib.count_launches(1)
-            return
-    _lib.check(lib.kvbm_kv_tile_xfer(C.byref(s), C.byref(d), C.byref(shape), max_ctas, st), "kvbm_kv_tile_xfer")
-    _lib.count_launches(1)
+    flags = 0
+    if bulk is False:
+        flags |= XFER_NO_BULK
+    elif bulk:
+        flags |= XFER_BULK_PEER
+    elif getattr(dst, "location", None) == "device" and (dst.device is None or dst.device == dev.index):
+        flags |= XFER_DST_LOCAL
+    ran = C.c_int(0)
+    rc = lib.kvbm_kv_xfer(C.byref(s), C.byref(d), C.byref(shape), ENGINE_CODES[engine], max_ctas, flags,
+                          C.byref(ran), st)
+    if rc != 0 and engine == "tma":
+        raise _lib.KvbmCudaError("kvbm_kv_xfer: the TMA engine cannot take this transfer (source chunks not "
+                                 "contiguous or not 16-byte aligned); use engine='auto' or 'tile'")
+    _lib.check(rc, "kvbm_kv_xfer")
+    _lib.count_launches(1 if ran.value else 0)
+    return RAN_NAMES.get(ran.value, "none")
+
+
+def transfer_status(reset: bool = False, device: int | None = None) -> int:
+    """The TMA engines' status word for ``device`` (0: no error since the last reset;
+    2: a misaligned chunk was refused; 3: a pipeline wait gave up). A host read of
+    mapped memory: no device synchronization, so read it after the transfer's
+    stream has passed the launch."""
+    dev = torch.cuda.current_device() if device is None else device
+    return int(_lib.load().kvbm_xfer_status(dev, 1 if reset else 0))
+
+
+def check_transfer_status(device: int | None = None) -> None:
+    """Raise (and clear the word) if a TMA transfer on ``device`` reported an error."""
+    st = transfer_status(reset=True, device=device)
+    if st:
+        what = {2: "a chunk address was misaligned", 3: "a pipeline wait gave up (bulk copy did not land)"}
+        raise _lib.KvbmCudaError(f"KV transfer failed on the device: status {st} ({what.get(st, 'unknown')})")
+
+
+def set_pipeline_wait_limit_ns(ns: int) -> None:
+    """Test hook: the TMA engines' pipeline wait limit for later launches (0: the default 2 s)."""
+    _lib.load().kvbm_xfer_set_wait_limit_ns(int(ns))
 
 
 def kv_checksum(layout, ids, *, layer_begin: int = 0, num_layers: int | None = None, head_offset: int = 0,
@@ -132,15 +175,15 @@ def kv_checksum(layout, ids, *, layer_begin: int = 0, num_layers: int | None = N
     return out
 
 
-def kv_transfer_sides(src_side, dst_side, shape, *, engine: str = "tile", max_ctas: int = 0, stream=None) -> None:
-    """Low-level launch with prebuilt ``KvbmSide`` / ``KvbmTileShape`` structs."""
+def kv_transfer_sides(src_side, dst_side, shape, *, engine: str = "tile", max_ctas: int = 0, stream=None,
+                      flags: int = 0) -> str:
+    """Low-level launch with prebuilt ``KvbmSide`` / ``KvbmTileShape`` structs; returns the kernel that ran."""
     lib = _lib.load()
-    st = _stream(stream)
-    if engine == "tma":
-        if lib.kvbm_kv_chunk_xfer_tma(C.byref(src_side), C.byref(dst_side), C.byref(shape), max_ctas, st) == 0:
-            return
-    _lib.check(lib.kvbm_kv_tile_xfer(C.byref(src_side), C.byref(dst_side), C.byref(shape), max_ctas, st),
-               "kvbm_kv_tile_xfer")
+    ran = C.c_int(0)
+    _lib.check(lib.kvbm_kv_xfer(C.byref(src_side), C.byref(dst_side), C.byref(shape), ENGINE_CODES[engine], max_ctas,
+                                flags, C.byref(ran), _stream(stream)), "kvbm_kv_xfer")
+    _lib.count_launches(1 if ran.value else 0)
+    return RAN_NAMES.get(ran.value, "none")
 
 
 def _ptr_align(ptrs: list[int], nbytes: int) -> int:

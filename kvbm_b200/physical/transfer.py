@@ -399,10 +399,13 @@ class TransferManager:
                 hr = opts.head_range
                 sid = kv_ops.upload(torch.tensor(s_ids, dtype=torch.int32), stream.device, stream)
                 did = kv_ops.upload(torch.tensor(d_ids, dtype=torch.int32), stream.device, stream)
-                kv_ops.kv_transfer(a, sid, b, did, layer_begin=lb, num_layers=le - lb,
-                                   src_head_offset=hr[0] if hr else 0, dst_head_offset=hr[1] if hr else 0,
-                                   num_heads=hr[2] if hr else None, engine=engine, max_ctas=opts.max_ctas,
-                                   stream=stream)
+                # an engine the manager chose itself may fall back; one the caller forced may not
+                run = "auto" if (engine == "tma" and opts.engine == "auto") else engine
+                self.last_engine = kv_ops.kv_transfer(a, sid, b, did, layer_begin=lb, num_layers=le - lb,
+                                                      src_head_offset=hr[0] if hr else 0,
+                                                      dst_head_offset=hr[1] if hr else 0,
+                                                      num_heads=hr[2] if hr else None, engine=run,
+                                                      max_ctas=opts.max_ctas, stream=stream)
             if opts.stream is not None:
                 return TransferCompleteNotification.ready()
             ev = torch.cuda.Event()

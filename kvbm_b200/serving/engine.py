@@ -1,0 +1,460 @@
+"""A small serving engine that drives the block manager through its connector.
+
+It plays the part a serving framework (vLLM) plays for the reference: a
+scheduler with waiting / waiting-for-remote-KV / running requests, a G1
+block allocator over one KV pool, prefill chunks under a token budget, a
+static decode batch replayed as one CUDA graph per step - and, around every
+step, the connector hooks in the order vLLM's v1 engine calls them:
+
+scheduler side
+    ``get_num_new_matched_tokens`` and ``update_state_after_alloc`` when a
+    request is admitted, ``build_connector_meta`` once per step,
+    ``update_connector_output`` with the workers' reports, and
+    ``request_finished`` when a request ends (blocks stay allocated while the
+    connector reports a transfer still reading them);
+worker side
+    ``bind_connector_metadata``, ``start_load_kv``, ``wait_for_layer_load`` /
+    ``save_kv_layer`` around every layer, ``wait_for_save``,
+    ``get_finished``, ``build_connector_worker_meta``,
+    ``get_block_ids_with_load_errors``.
+
+Requests whose prompt arrives from outside (a G2/G3 onboard or a remote
+prefill) wait until the connector reports them received; on a full-prompt
+hit the last prompt token is recomputed to sample the first output token
+(vLLM's rule, v1/core/sched/scheduler.py ``_update_waiting_for_remote_kv``),
+which the decode batch does as its first step for that request. Blocks
+reported as failed to load are recomputed by a local prefill.
+
+The model is ``models.llama.LlamaModel`` (random-init weights); inference
+only, no sampling beyond greedy argmax, no stop tokens (requests end after
+``max_tokens``).
+"""
+
+from __future__ import annotations
+
+import enum
+import math
+from collections import deque
+from dataclasses import dataclass, field
+
+import torch
+
+from ..connector.leader import ConnectorLeader, KvbmRequest, SchedulerOutputLite
+from ..connector.worker import ConnectorWorker
+from ..models.llama import LlamaModel
+from ..ops import llama_ops
+from ..physical.layout import KvLayout
+
+
+class RequestStatus(str, enum.Enum):
+    WAITING = "waiting"
+    WAITING_FOR_REMOTE_KVS = "waiting_for_remote_kvs"
+    PREFILL = "prefill"
+    DECODE = "decode"
+    FINISHED = "finished"
+
+
+@dataclass
+class Request:
+    request_id: str
+    prompt: torch.Tensor                 # int32 [S] on the host (pinned for an asynchronous upload)
+    max_tokens: int = 1
+    kv_transfer_params: dict | None = None
+    salt: str | None = None
+    status: RequestStatus = RequestStatus.WAITING
+    num_computed_tokens: int = 0
+    num_external_tokens: int = 0
+    block_ids: list[int] = field(default_factory=list)
+    num_output: int = 0
+    slot: int = -1
+    output: torch.Tensor | None = None   # pinned int64 [max_tokens]; valid once the engine's stream passed the step
+    arrival_event: torch.cuda.Event | None = None
+    first_token_event: torch.cuda.Event | None = None
+    finish_event: torch.cuda.Event | None = None
+    load_failed: bool = False
+    _dev_prompt: torch.Tensor | None = None
+    _dev_ids: torch.Tensor | None = None
+    _first_tok: torch.Tensor | None = None
+
+    @property
+    def num_prompt_tokens(self) -> int:
+        return int(self.prompt.numel())
+
+
+@dataclass
+class EngineConfig:
+    num_gpu_blocks: int
+    block_size: int = 16
+    max_num_seqs: int = 32               # decode batch slots
+    max_num_batched_tokens: int = 8192   # prefill tokens per step
+    max_model_len: int = 16384
+    max_tokens: int = 256                # largest max_tokens a request may ask for (sizes the output buffer)
+    use_graphs: bool = True
+    decode_splits: int | None = None
+    record_events: bool = True           # arrival / first-token CUDA events per request
+    max_inflight_steps: int = 2          # the host runs at most this many steps ahead of the GPU
+
+
+class DecodeBatch:
+    """``slots`` decode sequences with static shapes; one step is one CUDA graph replay.
+
+    Idle slots point at block 0 (reserved by the engine) at position 0 and
+    compute a throw-away token; a slot's position, length and output index
+    advance only while it is active.
+    """
+
+    def __init__(self, model: LlamaModel, pool: KvLayout, slots: int, max_blocks: int, max_out: int, splits: int,
+                 use_graphs: bool = True):
+        self.model, self.pool, self.slots = model, pool, slots
+        self.max_blocks, self.max_out, self.splits = max_blocks, max_out, splits
+        dev = model.device
+        self.tok = torch.zeros(slots, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(slots, dtype=torch.int32, device=dev)
+        self.seq_lens = torch.ones(slots, dtype=torch.int32, device=dev)
+        self.block_table = torch.zeros(slots, max_blocks, dtype=torch.int32, device=dev)
+        self.active = torch.zeros(slots, dtype=torch.int32, device=dev)
+        self.out_idx = torch.zeros(slots, 1, dtype=torch.int64, device=dev)
+        self.out = torch.zeros(slots, max_out, dtype=torch.int64, device=dev)
+        self.use_graphs = use_graphs
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.graph_launches = 0
+
+    def _step(self) -> None:
+        nxt = self.model.decode_step(self.tok, self.pos, self.pool, self.block_table, self.seq_lens, self.splits)
+        self.out.scatter_(1, self.out_idx, nxt.unsqueeze(1))
+        self.tok.copy_(nxt)
+        self.pos.add_(self.active)
+        self.seq_lens.add_(self.active)
+        self.out_idx.add_(self.active.unsqueeze(1))
+        self.out_idx.clamp_(max=self.max_out - 1)
+
+    def _reset(self) -> None:
+        self.tok.zero_()
+        self.pos.zero_()
+        self.seq_lens.fill_(1)
+        self.block_table.zero_()
+        self.active.zero_()
+        self.out_idx.zero_()
+
+    def capture(self) -> None:
+        if not self.use_graphs or self.graph is not None:
+            return
+        from ..ops import _lib
+
+        s = torch.cuda.Stream(device=self.model.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._step()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        before = _lib.launch_count()
+        with torch.cuda.graph(g):
+            self._step()
+        self.graph_launches = _lib.launch_count() - before
+        self.graph = g
+        self._reset()
+
+    def enter(self, entries: list[tuple[int, list[int], int, int, int]]) -> None:
+        """Activate slots: ``(slot, block_ids, input_token, position, first_output_index)`` each.
+        ``input_token < 0`` keeps the token already in the slot (written by the caller)."""
+        if not entries:
+            return
+        n = len(entries)
+        dev = self.tok.device
+        slots = torch.tensor([e[0] for e in entries], dtype=torch.int64)
+        rows = torch.zeros(n, self.max_blocks, dtype=torch.int32)
+        for i, e in enumerate(entries):
+            if len(e[1]) > self.max_blocks:
+                raise ValueError(f"{len(e[1])} blocks exceed the decode batch's {self.max_blocks}")
+            rows[i, : len(e[1])] = torch.tensor(e[1], dtype=torch.int32)
+        scal = torch.tensor([[e[2], e[3], e[3] + 1, e[4]] for e in entries], dtype=torch.int64)
+        slots_d = slots.pin_memory().to(dev, non_blocking=True)
+        rows_d = rows.pin_memory().to(dev, non_blocking=True)
+        scal_d = scal.pin_memory().to(dev, non_blocking=True)
+        self.block_table.index_copy_(0, slots_d, rows_d)
+        keep = scal_d[:, 0] < 0
+        self.tok.index_copy_(0, slots_d, torch.where(keep, self.tok.index_select(0, slots_d), scal_d[:, 0]))
+        self.pos.index_copy_(0, slots_d, scal_d[:, 1].to(torch.int32))
+        self.seq_lens.index_copy_(0, slots_d, scal_d[:, 2].to(torch.int32))
+        self.out_idx.index_copy_(0, slots_d, scal_d[:, 3:4])
+        self.active.index_fill_(0, slots_d, 1)
+
+    def leave(self, slots: list[int]) -> None:
+        if not slots:
+            return
+        idx = torch.tensor(slots, dtype=torch.int64).pin_memory().to(self.tok.device, non_blocking=True)
+        self.active.index_fill_(0, idx, 0)
+        self.pos.index_fill_(0, idx, 0)
+        self.seq_lens.index_fill_(0, idx, 1)
+        self.out_idx.index_fill_(0, idx, 0)
+        self.block_table.index_fill_(0, idx, 0)
+
+    def step(self) -> None:
+        if self.graph is not None:
+            from ..ops import _lib
+
+            self.graph.replay()
+            _lib.count_launches(self.graph_launches)
+        else:
+            self._step()
+
+
+class LLMEngine:
+    """One serving instance (one GPU, TP = 1) with an optional block-manager connector."""
+
+    def __init__(self, model: LlamaModel, cfg: EngineConfig, leader: ConnectorLeader | None = None,
+                 worker: ConnectorWorker | None = None, pool: KvLayout | None = None):
+        self.model, self.cfg = model, cfg
+        self.device = model.device
+        self.pool = pool if pool is not None else model.allocate_pool(cfg.num_gpu_blocks, cfg.block_size)
+        self.leader, self.worker = leader, worker
+        self.free_blocks = deque(range(1, cfg.num_gpu_blocks))  # block 0: target of idle decode slots
+        self.requests: dict[str, Request] = {}
+        self.waiting: deque[Request] = deque()
+        self.remote: dict[str, Request] = {}
+        self.prefilling: deque[Request] = deque()
+        self.ready: deque[Request] = deque()
+        self.decoding: dict[int, Request] = {}
+        self.free_slots = deque(range(cfg.max_num_seqs))
+        self._delayed: dict[str, Request] = {}
+        self.step_id = 0
+        self._mark = torch.cuda.Stream(device=self.device) if cfg.record_events else None
+        max_blocks = math.ceil(cfg.max_model_len / cfg.block_size)
+        splits = cfg.decode_splits or llama_ops.decode_splits(cfg.max_num_seqs, model.cfg.kv_heads,
+                                                              cfg.max_model_len, cfg.block_size)
+        self.batch = DecodeBatch(model, self.pool, cfg.max_num_seqs, max_blocks, cfg.max_tokens, splits,
+                                 cfg.use_graphs)
+        self.stats = {"steps": 0, "prefill_tokens": 0, "decode_steps": 0, "finished": 0, "recomputed": 0}
+        self._inflight: deque[torch.cuda.Event] = deque()
+
+    # ------------------------------------------------------------- public
+    def warmup(self) -> None:
+        """Capture the decode step's CUDA graph (before the first timed step)."""
+        self.batch.capture()
+        torch.cuda.synchronize(self.device)
+
+    def add_request(self, req: Request) -> None:
+        if req.max_tokens > self.cfg.max_tokens:
+            raise ValueError(f"max_tokens {req.max_tokens} > engine limit {self.cfg.max_tokens}")
+        if req.num_prompt_tokens + req.max_tokens > self.cfg.max_model_len:
+            raise ValueError("prompt + max_tokens exceeds max_model_len")
+        self.requests[req.request_id] = req
+        if self._mark is not None:
+            req.arrival_event = torch.cuda.Event(enable_timing=True)
+            req.arrival_event.record(self._mark)
+        if self.leader is not None:
+            self.leader.create_slot(KvbmRequest(req.request_id, req.prompt.tolist(), salt=req.salt,
+                                                max_tokens=req.max_tokens,
+                                                kv_transfer_params=req.kv_transfer_params))
+        self.waiting.append(req)
+
+    def has_unfinished(self) -> bool:
+        return bool(self.requests)
+
+    @property
+    def num_waiting_for_remote(self) -> int:
+        return len(self.remote)
+
+    def step(self) -> list[Request]:
+        """One engine step; returns the requests that finished in it."""
+        self.step_id += 1
+        self.stats["steps"] += 1
+        self._finished_now: list[Request] = []
+        so = SchedulerOutputLite(step=self.step_id)
+        self._admit(so)
+        prefills = self._schedule_prefill(so)
+        self._enter_decode(so)
+        for req in self.decoding.values():
+            if req.request_id not in so.scheduled:
+                so.scheduled[req.request_id] = ([], [], req.num_prompt_tokens + req.num_output)
+        w = self.worker
+        if self.leader is not None:
+            raw = self.leader.build_connector_meta(so)
+            w.bind_connector_metadata(raw)
+            w.start_load_kv()
+        for req, start, end in prefills:
+            self._run_prefill(req, start, end)
+        if self.decoding:
+            self._run_decode()
+        if w is not None:
+            w.wait_for_save()
+        finished = self._finished_now
+        if w is not None:
+            sending, recving = w.get_finished({r.request_id for r in finished})
+            wmeta = w.build_connector_worker_meta()
+            errs = w.get_block_ids_with_load_errors()
+            self.leader.update_connector_output(sending, recving, wmeta, errs)
+            self._on_received(recving, errs)
+            self._on_sent(sending)
+            w.clear_connector_metadata()
+        # bounded lookahead: what the connector polls reflects the GPU's progress, as in an engine that
+        # reads its sampled tokens every step
+        ev = torch.cuda.Event()
+        ev.record()
+        self._inflight.append(ev)
+        while len(self._inflight) > max(1, self.cfg.max_inflight_steps):
+            self._inflight.popleft().synchronize()
+        return finished
+
+    # ----------------------------------------------------------- schedule
+    def _blocks_needed(self, req: Request) -> int:
+        return math.ceil((req.num_prompt_tokens + max(0, req.max_tokens - 1)) / self.cfg.block_size)
+
+    def _admit(self, so: SchedulerOutputLite) -> None:
+        for _ in range(len(self.waiting)):
+            req = self.waiting[0]
+            need = self._blocks_needed(req)
+            if len(self.free_blocks) < need:
+                break
+            n_ext, is_async = 0, False
+            if self.leader is not None:
+                n_ext, is_async = self.leader.get_num_new_matched_tokens(req.request_id, 0)
+                if n_ext is None:  # the connector is still searching: try again next step
+                    self.waiting.rotate(-1)
+                    continue
+            self.waiting.popleft()
+            req.block_ids = [self.free_blocks.popleft() for _ in range(need)]
+            if self.leader is not None:
+                self.leader.update_state_after_alloc(req.request_id, req.block_ids, n_ext)
+            req.num_external_tokens = n_ext
+            if n_ext and is_async:
+                req.status = RequestStatus.WAITING_FOR_REMOTE_KVS
+                self.remote[req.request_id] = req
+            else:
+                req.num_computed_tokens = n_ext
+                req.status = RequestStatus.PREFILL
+                self.prefilling.append(req)
+
+    def _schedule_prefill(self, so: SchedulerOutputLite) -> list[tuple[Request, int, int]]:
+        budget = self.cfg.max_num_batched_tokens
+        out = []
+        for req in self.prefilling:
+            if budget <= 0:
+                break
+            start = req.num_computed_tokens
+            end = min(req.num_prompt_tokens, start + budget)
+            out.append((req, start, end))
+            budget -= end - start
+            so.scheduled[req.request_id] = ([], [], end)
+        return out
+
+    def _enter_decode(self, so: SchedulerOutputLite) -> None:
+        entries = []
+        while self.ready and self.free_slots:
+            req = self.ready.popleft()
+            slot = self.free_slots.popleft()
+            req.slot, req.status = slot, RequestStatus.DECODE
+            S = req.num_prompt_tokens
+            if req._first_tok is not None:
+                # prefilled here: the sampled token is on the device, output 0 already written
+                self.batch.tok[slot: slot + 1].copy_(req._first_tok)
+                self.batch.out[slot, 0:1].copy_(req._first_tok)
+                entries.append((slot, req.block_ids, -1, S, 1))
+                req._first_tok = None
+            else:
+                # every prompt token's KV arrived: the first step recomputes the last one
+                entries.append((slot, req.block_ids, int(req.prompt[S - 1]), S - 1, 0))
+                so.scheduled[req.request_id] = ([], [], S)
+            self.decoding[slot] = req
+        self.batch.enter(entries)
+
+    # ------------------------------------------------------------ execute
+    def _run_prefill(self, req: Request, start: int, end: int) -> None:
+        dev = self.device
+        if req._dev_prompt is None:
+            p = req.prompt if req.prompt.is_pinned() else req.prompt.pin_memory()
+            req._dev_prompt = p.to(dev, non_blocking=True)
+            req._dev_ids = torch.tensor(req.block_ids, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        w = self.worker
+        rid = {req.request_id}
+        nxt = self.model.prefill(req._dev_prompt[start:end], self.pool, req._dev_ids, start_pos=start,
+                                 on_layer_done=(lambda l: w.save_kv_layer(l, requests=rid)) if w else None,
+                                 on_layer_start=w.wait_for_layer_load if w else None)
+        self.stats["prefill_tokens"] += end - start
+        req.num_computed_tokens = end
+        if end < req.num_prompt_tokens:
+            return
+        self.prefilling.remove(req)
+        req.num_output = 1
+        if self._mark is not None:
+            req.first_token_event = torch.cuda.Event(enable_timing=True)
+            req.first_token_event.record()
+        if req.max_tokens <= 1:
+            req.output = torch.empty(1, dtype=torch.int64, pin_memory=True)
+            req.output.copy_(nxt, non_blocking=True)
+            self._finish(req)
+        else:
+            req._first_tok = nxt
+            self.ready.append(req)
+
+    def _run_decode(self) -> None:
+        self.batch.step()
+        self.stats["decode_steps"] += 1
+        ev = None
+        leave = []
+        for slot, req in list(self.decoding.items()):
+            req.num_output += 1
+            if self._mark is not None and (req.num_output == 1 or req.num_output >= req.max_tokens):
+                if ev is None:
+                    ev = torch.cuda.Event(enable_timing=True)
+                    ev.record()
+                if req.num_output == 1:
+                    req.first_token_event = ev
+                if req.num_output >= req.max_tokens:
+                    req.finish_event = ev
+            if req.num_output >= req.max_tokens:
+                req.output = torch.empty(req.max_tokens, dtype=torch.int64, pin_memory=True)
+                req.output.copy_(self.batch.out[slot, : req.max_tokens], non_blocking=True)
+                leave.append(slot)
+                del self.decoding[slot]
+                self.free_slots.append(slot)
+                self._finish(req)
+        self.batch.leave(leave)
+
+    # -------------------------------------------------------- completion
+    def _finish(self, req: Request) -> None:
+        self._finished_now.append(req)
+        req.status = RequestStatus.FINISHED
+        self.requests.pop(req.request_id, None)
+        self.stats["finished"] += 1
+        delay = False
+        if self.leader is not None:
+            delay, _ = self.leader.request_finished(req.request_id, req.block_ids)
+        if delay:
+            self._delayed[req.request_id] = req
+        else:
+            self._free(req)
+
+    def _free(self, req: Request) -> None:
+        # the request keeps the list of the blocks it held (for inspection); the blocks return to the pool
+        self.free_blocks.extend(req.block_ids)
+
+    def _on_sent(self, sending: set[str]) -> None:
+        for rid in sending:
+            req = self._delayed.pop(rid, None)
+            if req is not None:
+                self._free(req)
+
+    def _on_received(self, recving: set[str], errs: set[int]) -> None:
+        for rid in recving:
+            req = self.remote.pop(rid, None)
+            if req is None:
+                continue
+            S = req.num_prompt_tokens
+            if errs and errs.intersection(req.block_ids):
+                # the external KV never arrived: recompute the prompt here
+                req.load_failed = True
+                req.num_computed_tokens = 0
+                req.status = RequestStatus.PREFILL
+                self.prefilling.append(req)
+                self.stats["recomputed"] += 1
+                continue
+            req.num_computed_tokens = req.num_external_tokens
+            if req.num_computed_tokens >= S and req.max_tokens > 1:
+                req.num_computed_tokens = S - 1
+                self.ready.append(req)
+            else:
+                req.num_computed_tokens = min(req.num_computed_tokens, S - 1)
+                req.status = RequestStatus.PREFILL
+                self.prefilling.append(req)

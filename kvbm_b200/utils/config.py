@@ -160,6 +160,8 @@ class TransferConfig:
     allow_gpu_rdma: bool = False
     cuda_graph_replay: bool = False
     startup_benchmark: bool = False
+    layer_batch: int = 8               # P->D push: layers per transfer launch during the prefill pass
+    push_engine: str = "tma"           # P->D push kernel: tma (bulk-copy pipeline) | tile
 
 
 @dataclass

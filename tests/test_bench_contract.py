@@ -22,5 +22,5 @@ def test_bench_defaults_and_engine_choices():
     import bench  # noqa: F401 - module imports without touching CUDA
 
     src = open(os.path.join(ROOT, "bench.py")).read()
-    assert '"--engine", default="tma_inline"' in src and '"--layer-batch", type=int, default=8' in src
+    assert '"--engine", default="tma"' in src and '"--layer-batch", type=int, default=8' in src
     assert '"--steps", type=int, default=3' in src and '"--warmup", type=int, default=3' in src

@@ -1,0 +1,156 @@
+"""Conditional disaggregation through the connector, on CPU: the decode
+leader's decision, dispatch and receive bookkeeping; the prefill leader's
+push cursor over prefill chunks; the prefill plane and peer directory."""
+
+import threading
+
+import torch.distributed as dist
+
+from kvbm_b200.connector.leader import REMOTE_DECODE_KEY, ConnectorLeader, KvbmRequest, SchedulerOutputLite
+from kvbm_b200.connector.protocol import ConnectorMetadata
+from kvbm_b200.engine.cd import ConditionalDisagg, InflightBudget, SelectionPolicy
+from kvbm_b200.engine.cd_plane import (LocalPeerDirectory, LocalPrefillPlane, StorePeerDirectory, StorePrefillPlane,
+                                       decode_dispatch, encode_dispatch)
+from kvbm_b200.engine.leader import InstanceLeader, ParallelWorkers
+from kvbm_b200.logical.manager import BlockManager, Tier
+
+BS = 16
+
+
+def decode_leader(plane, slots=4, policy="always", budget=None, g2_blocks=64):
+    g2 = BlockManager(g2_blocks, BS, "lineage", Tier.G2)
+    cd = ConditionalDisagg(SelectionPolicy(policy, 64), InflightBudget(budget))
+    return ConnectorLeader(InstanceLeader(g2, ParallelWorkers([])), BS, cd=cd, plane=plane, prefill_target=7,
+                           instance_id=3, mailbox_slots=slots, recv_timeout_s=5.0)
+
+
+def meta(leader, step, sched):
+    return ConnectorMetadata.decode(leader.build_connector_meta(SchedulerOutputLite(step, sched)))
+
+
+def test_decode_dispatches_and_receives():
+    plane = LocalPrefillPlane()
+    L = decode_leader(plane)
+    prompt = list(range(100))  # 7 blocks (last one partial)
+    L.create_slot(KvbmRequest("a", prompt))
+    assert L.get_num_new_matched_tokens("a", 0) == (100, True)
+    L.update_state_after_alloc("a", list(range(10, 18)), 100)
+    [d] = plane.poll(7)
+    assert d["request_id"] == "a" and list(d["tokens"]) == prompt
+    dec = d["decode"]
+    assert dec["instance"] == 3 and dec["dst_ids"] == list(range(10, 17)) and dec["provided_blocks"] == 0
+    assert d["params"]["decode_endpoint"] == "3" and d["params"]["num_provided_tokens"] == 0
+    m = meta(L, 1, {})
+    assert len(m.recv) == 1 and m.recv[0].slot == dec["slot"] and m.recv[0].seq == dec["seq"]
+    assert m.recv[0].g1_ids == list(range(10, 17))
+    assert L.cd.budget.inflight == 1 and len(L._mailbox_free) == 3
+    # vLLM asks again while the request waits: same answer, no second dispatch
+    assert L.get_num_new_matched_tokens("a", 0) == (100, True)
+    assert plane.poll(7) == []
+    L.update_connector_output(finished_recving={"a"})
+    assert L.cd.budget.inflight == 0 and len(L._mailbox_free) == 4
+    assert L.cd_stats["received"] == 1
+    assert L.request_finished("a") == (False, None)
+
+
+def test_budget_and_mailbox_bound_remote_prefills():
+    plane = LocalPrefillPlane()
+    L = decode_leader(plane, slots=1)
+    for rid in ("a", "b"):
+        L.create_slot(KvbmRequest(rid, list(range(64))))
+    assert L.get_num_new_matched_tokens("a", 0) == (64, True)
+    assert L.get_num_new_matched_tokens("b", 0) == (0, False)  # no free mailbox slot: local prefill
+    assert L.cd_stats == {**L.cd_stats, "remote": 1, "local": 1}
+    assert L.cd.budget.inflight == 1
+
+
+def test_threshold_policy_counts_connector_tokens():
+    plane = LocalPrefillPlane()
+    L = decode_leader(plane, policy="threshold")  # remote when >= 64 tokens still need prefill
+    L.create_slot(KvbmRequest("short", list(range(40))))
+    assert L.get_num_new_matched_tokens("short", 0) == (0, False)
+    L.create_slot(KvbmRequest("long", list(range(1000, 1100))))
+    assert L.get_num_new_matched_tokens("long", 0) == (100, True)
+
+
+def test_g2_prefix_is_onboarded_and_rest_comes_remote():
+    plane = LocalPrefillPlane()
+    L = decode_leader(plane)
+    L.cd = None  # warm G2 first with a local request
+    prompt = list(range(100))
+    L.create_slot(KvbmRequest("warm", prompt[:64] + [5]))
+    L.update_state_after_alloc("warm", [0, 1, 2, 3, 4], 0)
+    meta(L, 1, {"warm": ([], [], 65)})
+    L.update_connector_output(worker_meta={"offloaded": {1: 1}})
+    L.cd = ConditionalDisagg(SelectionPolicy("always"))
+    L.create_slot(KvbmRequest("a", prompt))
+    assert L.get_num_new_matched_tokens("a", 0) == (100, True)
+    L.update_state_after_alloc("a", list(range(20, 28)), 100)
+    m = meta(L, 2, {})
+    assert [o.g1_ids for o in m.onboard] == [[20, 21, 22, 23]]
+    [d] = plane.poll(7)
+    assert d["decode"]["provided_blocks"] == 4 and d["decode"]["dst_ids"] == [24, 25, 26]
+    assert d["params"]["num_provided_tokens"] == 64
+    assert m.recv[0].g1_ids == [24, 25, 26]
+
+
+def test_prefill_pushes_chunks_and_delays_free():
+    g2 = BlockManager(8, BS, "lineage", Tier.G2)
+    P = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([])), BS, offload_enabled=False)
+    prompt = list(range(100))
+    remote = {"instance": 3, "dst_ids": list(range(40, 47)), "slot": 2, "seq": 11, "provided_blocks": 0}
+    P.create_slot(KvbmRequest("a", prompt, kv_transfer_params={REMOTE_DECODE_KEY: remote}))
+    assert P.get_num_new_matched_tokens("a", 0) == (0, False)
+    P.update_state_after_alloc("a", list(range(7)), 0)
+    m1 = meta(P, 1, {"a": ([], [], 48)})  # chunk 1: three complete blocks
+    assert [(o.src_ids, o.dst_ids, o.final) for o in m1.push] == [([0, 1, 2], [40, 41, 42], False)]
+    m2 = meta(P, 2, {"a": ([], [], 100)})  # last chunk: the rest, with the partial block
+    [op] = m2.push
+    assert op.src_ids == [3, 4, 5, 6] and op.dst_ids == [43, 44, 45, 46] and op.final
+    assert (op.peer, op.slot, op.seq) == (3, 2, 11)
+    assert P.request_finished("a") == (True, None)  # the push still reads its blocks
+    P.update_connector_output(finished_sending={"a"})
+    assert P.num_slots() == 0
+
+
+def test_prefill_skips_blocks_the_decode_side_provides():
+    g2 = BlockManager(8, BS, "lineage", Tier.G2)
+    P = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([])), BS, offload_enabled=False)
+    remote = {"instance": 3, "dst_ids": [50, 51], "slot": 0, "seq": 1, "provided_blocks": 2}
+    P.create_slot(KvbmRequest("a", list(range(64)), kv_transfer_params={REMOTE_DECODE_KEY: remote}))
+    P.update_state_after_alloc("a", [0, 1, 2, 3], 0)
+    [op] = meta(P, 1, {"a": ([], [], 64)}).push
+    assert op.src_ids == [2, 3] and op.dst_ids == [50, 51] and op.final
+
+
+def test_dispatch_wire_roundtrip():
+    raw = encode_dispatch("r", [1, 2, 3], {"session_id": "s"}, {"instance": 1, "dst_ids": [4]}, salt="x")
+    d = decode_dispatch(raw)
+    assert d["request_id"] == "r" and d["tokens"].tolist() == [1, 2, 3] and d["decode"]["dst_ids"] == [4]
+    assert d["salt"] == "x"
+
+
+def test_store_plane_and_directory_in_order():
+    store = dist.HashStore()
+    plane = StorePrefillPlane(store)
+    for i in range(3):
+        plane.dispatch(5, encode_dispatch(f"r{i}", [i], {}, {}))
+    plane.dispatch(6, encode_dispatch("other", [9], {}, {}))
+    got = plane.poll(5, limit=2) + plane.poll(5)
+    assert [d["request_id"] for d in got] == ["r0", "r1", "r2"]
+    assert plane.poll(5) == []
+    assert [d["request_id"] for d in plane.poll(6)] == ["other"]
+    dirs = StorePeerDirectory(store)
+    dirs.publish(5, {"mailbox": {"name": "m", "nbytes": 4096, "slots": 8}, "pool": {"x": b"\x01\x02"}})
+    assert dirs.lookup(5, timeout_s=1)["pool"]["x"] == b"\x01\x02"
+
+
+def test_local_plane_wait_wakes_on_dispatch():
+    plane = LocalPrefillPlane()
+    t = threading.Timer(0.05, lambda: plane.dispatch(1, encode_dispatch("late", [1], {}, {})))
+    t.start()
+    got = plane.wait(1, timeout_s=5.0)
+    assert [d["request_id"] for d in got] == ["late"]
+    d = LocalPeerDirectory()
+    d.publish(1, {"a": 1})
+    assert d.lookup(1)["a"] == 1

@@ -3,7 +3,8 @@ save-cursor offloads, delayed frees; and the step-metadata wire format."""
 
 
 from kvbm_b200.connector.leader import ConnectorLeader, KvbmRequest, SchedulerOutputLite
-from kvbm_b200.connector.protocol import ConnectorMetadata, OffloadOp, OnboardOp
+from kvbm_b200.connector.protocol import (ConnectorMetadata, OffloadOp, OnboardOp, PushOp, RecvOp, SpillOp,
+                                          StageOp)
 from kvbm_b200.engine.leader import InstanceLeader, ParallelWorkers
 from kvbm_b200.logical.manager import BlockManager, Tier
 
@@ -40,7 +41,7 @@ def test_warm_request_onboards_and_skips_present_blocks():
     L.get_num_new_matched_tokens("a", 0)
     L.update_state_after_alloc("a", list(range(7)), 0)
     step(L, 1, {"a": ([], [], 100)})
-    L.update_connector_output(finished_sending={"a"})
+    L.update_connector_output(finished_sending={"a"}, worker_meta={"offloaded": {1: 1}})
     L.request_finished("a")
     # same prompt again: 6 cached blocks, but the last prompt token must be computed -> 6 blocks (96 < 99)
     L.create_slot(KvbmRequest("b", prompt))
@@ -60,6 +61,7 @@ def test_framework_prefix_hit_is_skipped():
     L.create_slot(KvbmRequest("a", prompt))
     L.update_state_after_alloc("a", list(range(4)), 0)
     step(L, 1, {"a": ([], [], 64)})
+    L.update_connector_output(worker_meta={"offloaded": {1: 1}})
     L.create_slot(KvbmRequest("b", prompt + list(range(1000, 1040))))
     # the framework already has 32 tokens in G1: KVBM contributes blocks 2..3
     n, _ = L.get_num_new_matched_tokens("b", 32)
@@ -87,8 +89,34 @@ def test_decode_tokens_extend_sequence_when_enabled():
     assert [o.g1_ids for o in m.offload] == [[1]]
 
 
+def test_offloaded_blocks_match_only_after_every_worker_reports_the_copy():
+    g2 = BlockManager(64, 16, "lineage", Tier.G2)
+    L = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([])), 16, num_workers=2)
+    prompt = list(range(64))
+    L.create_slot(KvbmRequest("a", prompt))
+    L.update_state_after_alloc("a", list(range(4)), 0)
+    m = step(L, 1, {"a": ([], [], 64)})
+    assert [o.g1_ids for o in m.offload] == [[0, 1, 2, 3]]
+    probe = prompt + [7]
+    # copies still in flight: another request must not match the G2 destinations
+    L.create_slot(KvbmRequest("b", probe))
+    assert L.get_num_new_matched_tokens("b", 0) == (0, False)
+    # the same blocks are not offloaded twice while the first copy is pending
+    L.create_slot(KvbmRequest("c", prompt))
+    L.update_state_after_alloc("c", list(range(10, 14)), 0)
+    assert step(L, 2, {"c": ([], [], 64)}).offload == []
+    L.update_connector_output(worker_meta={"offloaded": {1: 1}})  # one of two workers
+    L.create_slot(KvbmRequest("d", probe))
+    assert L.get_num_new_matched_tokens("d", 0) == (0, False)
+    L.update_connector_output(worker_meta={"offloaded": {1: 1}})  # the second one
+    L.create_slot(KvbmRequest("e", probe))
+    assert L.get_num_new_matched_tokens("e", 0) == (64, True)
+
+
 def test_metadata_roundtrip():
-    m = ConnectorMetadata(3, [OnboardOp("r", [1, 2], [5, 6])], [OffloadOp("q", [7], [9])], ["z"])
+    m = ConnectorMetadata(3, [OnboardOp("r", [1, 2], [5, 6])], [OffloadOp("q", [7], [9])], ["z"],
+                          stage=[StageOp("r", [4], [8])], spill=[SpillOp([3], [11])],
+                          push=[PushOp("p", 7, [1, 2], [3, 4], 5, 9, True)], recv=[RecvOp("q", 2, 9, [3, 4], 1.5)])
     d = ConnectorMetadata.decode(m.encode())
     assert d == m
 

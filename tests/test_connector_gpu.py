@@ -45,7 +45,9 @@ def test_offload_wipe_onboard_same_tokens(mode):
     torch.cuda.synchronize()
     sending, recving = worker.get_finished({"a"})
     assert sending == {"a"}
-    leader.update_connector_output(sending, recving)
+    wmeta = worker.build_connector_worker_meta()
+    assert wmeta == {"offloaded": {1: 1}}  # step 1's copies landed: the leader may register them now
+    leader.update_connector_output(sending, recving, wmeta)
     leader.request_finished("a")
     ref_blocks = g1.gather_blocks(ids_a[:4]).clone()
 

@@ -5,7 +5,6 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-from kvbm_b200.engine.disagg import DisaggConfig, DisaggServer
 from kvbm_b200.models.llama import LlamaConfig, LlamaModel
 
 
@@ -37,23 +36,42 @@ def test_prefill_decode_matches_reference(gemm):
     _check_greedy(model, seq, T)
 
 
-@pytest.mark.parametrize("engine", ["fused", "tma", "tma_inline"])
-def test_colocated_wave_and_graphs(engine):
-    cfg = DisaggConfig(model=LlamaConfig.tiny(layers=2), concurrency=3, prompt_len=80, gen_len=5, engine=engine)
-    server = DisaggServer(cfg, "colocated", 0)
-    server.warmup_graphs()
-    prompts = torch.randint(0, cfg.model.vocab, (3, 80), dtype=torch.int32).pin_memory()
-    res = server.serve_wave(prompts)
-    assert res.tokens.shape == (3, 5)
-    assert res.kv_bytes == 3 * cfg.kv_bytes_per_request()
-    assert len(res.ttft_ms) == 3 and all(t > 0 for t in res.ttft_ms)
-    # the decode pool holds exactly the prefill KV: check every request's greedy tokens
+@pytest.mark.parametrize("engine", ["tma", "tile"])
+def test_serving_waves_with_graphs(engine):
+    """Two waves through the disaggregated serving path (colocated), decode steps as CUDA graphs."""
+    from kvbm_b200.engine.cd_plane import LocalPeerDirectory, LocalPrefillPlane
+    from kvbm_b200.serving.engine import Request
+    from kvbm_b200.serving.pd import PdConfig, PdInstance
+
+    mcfg = LlamaConfig.tiny(layers=2)
+    model = LlamaModel(mcfg, "cuda", seed=2)
+    cfg = PdConfig(model=mcfg, concurrency=3, prompt_len=80, gen_len=5, push_engine=engine, layer_batch=2)
+    plane, directory = LocalPrefillPlane(), LocalPeerDirectory()
+    dec = PdInstance("decode", model, cfg, 1, plane, directory, prefill_target=2)
+    pre = PdInstance("prefill", model, cfg, 2, plane, directory)
+    dec.warmup()
+    assert dec.engine.batch.graph is not None
+    prompts = torch.randint(0, mcfg.vocab, (3, 80), dtype=torch.int32).pin_memory()
+    outs = []
+    for wave in range(2):
+        reqs = [Request(f"w{wave}r{i}", prompts[i], max_tokens=5) for i in range(3)]
+        for r in reqs:
+            dec.engine.add_request(r)
+        while dec.engine.has_unfinished():
+            pre.pull()
+            while pre.engine.has_unfinished():
+                pre.step()
+            dec.step()
+        torch.cuda.synchronize()
+        outs.append(torch.stack([r.output for r in reqs]))
+        assert all(r.arrival_event.elapsed_time(r.first_token_event) > 0 for r in reqs)
     for r in range(3):
-        seq = prompts[r].tolist() + res.tokens[r].tolist()
-        _check_greedy(server.model, seq, 80)
-    # a second wave reuses the graph and the pools
-    res2 = server.serve_wave(prompts)
-    assert torch.equal(res2.tokens, res.tokens)
+        _check_greedy(model, prompts[r].tolist() + outs[0][r].tolist(), 80)
+    # the second wave reuses the graph, the pools and the mailbox slots
+    assert torch.equal(outs[0], outs[1])
+    assert pre.worker.take_push_timings()[1] == 6 * cfg.kv_bytes_per_request()
+    dec.shutdown()
+    pre.shutdown()
 
 
 def test_smoke_entry():

@@ -1,0 +1,198 @@
+"""The serving engine driving the connector on a B200: conditional
+disaggregation end to end (decode GNMT -> dispatch -> prefill push in layer
+batches -> host mailbox -> finished_recving -> decode), the engine's
+asynchronous G2 onboard, and (2 GPUs) the same P->D flow across two
+processes whose decode tokens must equal the colocated run's."""
+
+import os
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+
+from kvbm_b200.engine.cd_plane import LocalPeerDirectory, LocalPrefillPlane
+from kvbm_b200.models.llama import LlamaConfig, LlamaModel
+from kvbm_b200.serving.engine import EngineConfig, LLMEngine, Request
+from kvbm_b200.serving.pd import PdConfig, PdInstance
+
+pytestmark = pytest.mark.gpu
+
+
+def _prompts(n, lens, vocab, seed=11):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randint(0, vocab, (lens[i % len(lens)],), generator=g, dtype=torch.int32).pin_memory()
+            for i in range(n)]
+
+
+def run_colocated(model, cfg, prompts, layer_batch=1):
+    cfg.layer_batch = layer_batch
+    plane, directory = LocalPrefillPlane(), LocalPeerDirectory()
+    dec = PdInstance("decode", model, cfg, 1, plane, directory, prefill_target=2)
+    pre = PdInstance("prefill", model, cfg, 2, plane, directory)
+    dec.warmup()
+    reqs = [Request(f"r{i}", p, max_tokens=cfg.gen_len) for i, p in enumerate(prompts)]
+    for r in reqs:
+        dec.engine.add_request(r)
+    for _ in range(100000):
+        pre.pull()
+        while pre.engine.has_unfinished():
+            pre.step()
+        dec.step()
+        if not dec.engine.has_unfinished():
+            break
+    torch.cuda.synchronize()
+    return dec, pre, reqs
+
+
+def _check_against_reference(model, prompt, out, n_check=3, tol=0.05):
+    seq = torch.cat([prompt.cuda().long(), out[:n_check].cuda()])
+    logits = model.reference_forward(seq)
+    S = prompt.numel()
+    for j in range(n_check):
+        row = logits[S - 1 + j]
+        assert float(row[int(out[j])]) >= float(row.max()) - tol * float(row.abs().max()), (j, int(out[j]))
+
+
+def test_colocated_cd_pushes_prompt_and_decodes():
+    cfg_m = LlamaConfig.tiny(layers=3)
+    model = LlamaModel(cfg_m, "cuda", seed=5)
+    cfg = PdConfig(model=cfg_m, concurrency=4, prompt_len=72, gen_len=6)
+    prompts = _prompts(4, [72, 50, 33, 16], cfg_m.vocab)
+    dec, pre, reqs = run_colocated(model, cfg, prompts, layer_batch=2)
+    assert dec.leader.cd_stats["dispatched"] == 4 and dec.leader.cd_stats["received"] == 4
+    assert pre.leader.cd_stats["pushed_blocks"] == sum((p.numel() + 15) // 16 for p in prompts)
+    for r, p in zip(reqs, prompts):
+        assert r.output is not None and r.output.numel() == cfg.gen_len
+        _check_against_reference(model, p, r.output)
+    # the decode pool holds the prefill's K/V bit for bit (the last prompt position is recomputed by decode)
+    scratch = model.allocate_pool(16, 16)
+    for r, p in zip(reqs, prompts):
+        S = p.numel()
+        nb = (S + 15) // 16
+        ids = torch.arange(1, nb + 1, dtype=torch.int32, device="cuda")
+        model.prefill(p.cuda(), scratch, ids)
+        torch.cuda.synchronize()
+        for li in range(cfg_m.layers):
+            ref = scratch.layer_view(li)[ids.long()].reshape(nb, 2, -1, cfg_m.kv_heads, cfg_m.head_dim)
+            got = dec.engine.pool.layer_view(li)[torch.tensor(r.block_ids[:nb], device="cuda").long()]
+            got = got.reshape(nb, 2, -1, cfg_m.kv_heads, cfg_m.head_dim)
+            ref = ref.permute(1, 0, 2, 3, 4).reshape(2, nb * 16, -1)[:, : S - 1]
+            got = got.permute(1, 0, 2, 3, 4).reshape(2, nb * 16, -1)[:, : S - 1]
+            assert torch.equal(ref, got), (r.request_id, li)
+    for inst in (dec, pre):
+        inst.shutdown()
+
+
+def test_engine_onboards_g2_prefix_asynchronously():
+    from kvbm_b200.connector.leader import ConnectorLeader
+    from kvbm_b200.connector.worker import ConnectorWorker
+    from kvbm_b200.engine.leader import InstanceLeader, ParallelWorkers
+    from kvbm_b200.logical.manager import BlockManager, Tier
+    from kvbm_b200.utils.config import KvbmConfig
+
+    cfg_m = LlamaConfig.tiny(layers=2)
+    model = LlamaModel(cfg_m, "cuda", seed=3)
+    kcfg = KvbmConfig.load({"cache": {"host": {"num_blocks": 32}}}, env={}, system_toml=None)
+    leader = ConnectorLeader(InstanceLeader(BlockManager(32, 16, "lineage", Tier.G2), ParallelWorkers([])), 16)
+    worker = ConnectorWorker(kcfg, block_size=16)
+    eng = LLMEngine(model, EngineConfig(num_gpu_blocks=40, max_num_seqs=2, max_model_len=256, max_tokens=4,
+                                        use_graphs=False), leader, worker)
+    worker.register_layout(eng.pool)
+    prompt = _prompts(1, [80], cfg_m.vocab)[0]
+    a = Request("a", prompt, max_tokens=4)
+    eng.add_request(a)
+    while eng.has_unfinished() or eng._delayed:
+        eng.step()
+    torch.cuda.synchronize()
+    for _ in range(10):  # the worker reports the offload; the leader registers the G2 blocks
+        eng.step()
+    b = Request("b", prompt, max_tokens=4)
+    eng.add_request(b)
+    eng.step()
+    assert b.num_external_tokens == 64  # 4 blocks from G2; the rest is prefilled
+    while eng.has_unfinished() or eng._delayed:
+        eng.step()
+    torch.cuda.synchronize()
+    assert torch.equal(a.output, b.output)
+    worker.shutdown()
+
+
+# ------------------------------------------------------------------ 2 GPUs
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _pd_rank(rank, port, q):
+    import torch.distributed as dist
+
+    from kvbm_b200.engine.cd_plane import StorePeerDirectory, StorePrefillPlane
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                            timeout=timedelta(seconds=60))
+    try:
+        store = dist.distributed_c10d._get_default_store()
+        cfg_m = LlamaConfig.tiny(layers=3)
+        model = LlamaModel(cfg_m, torch.device("cuda", rank), seed=9)
+        cfg = PdConfig(model=cfg_m, concurrency=4, prompt_len=72, gen_len=6, layer_batch=2, recv_timeout_s=60)
+        prompts = _prompts(4, [72, 40, 65, 17], cfg_m.vocab, seed=21)
+        plane, directory = StorePrefillPlane(store), StorePeerDirectory(store)
+        if rank == 0:
+            pre = PdInstance("prefill", model, cfg, 100, plane, directory, shared=True)
+            served = 0
+            while served < len(prompts):
+                pre.pull(wait_s=0.0 if pre.engine.has_unfinished() else 0.01)
+                if pre.engine.has_unfinished() or pre.engine._delayed:
+                    served += len(pre.step())
+            torch.cuda.synchronize()
+            dist.barrier()
+            pre.shutdown()
+            q.put(("prefill", served))
+        else:
+            dec = PdInstance("decode", model, cfg, 101, plane, directory, shared=True, prefill_target=100)
+            dec.warmup()
+            reqs = [Request(f"q{i}", p, max_tokens=cfg.gen_len) for i, p in enumerate(prompts)]
+            for r in reqs:
+                dec.engine.add_request(r)
+            while dec.engine.has_unfinished():
+                dec.step()
+            torch.cuda.synchronize()
+            dist.barrier()
+            got = [r.output.tolist() for r in reqs]
+            stats = dict(dec.leader.cd_stats)
+            dec.shutdown()
+            _, _, ref = run_colocated(model, PdConfig(model=cfg_m, concurrency=4, prompt_len=72, gen_len=6),
+                                      prompts, layer_batch=2)
+            q.put(("decode", got, [r.output.tolist() for r in ref], stats))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.multigpu
+def test_two_gpu_pd_tokens_equal_colocated():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pd_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            item = q.get(timeout=240)
+            results[item[0]] = item
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert results["prefill"][1] == 4
+    _, got, ref, stats = results["decode"]
+    assert stats["received"] == 4 and stats["failed"] == 0
+    assert got == ref

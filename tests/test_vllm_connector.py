@@ -63,7 +63,10 @@ def test_scheduler_role_offloads_then_matches():
     assert isinstance(meta, vc.KvbmConnectorMetadata)
     m = ConnectorMetadata.decode(meta.metadata)
     assert [op.g1_ids for op in m.offload] == [[10, 11, 12, 13, 14]]  # the five full prompt blocks
-    conn.update_connector_output(SimpleNamespace(finished_sending={"a"}, finished_recving=None))
+    # the worker reports step 1's copies done: only now are the G2 blocks registered
+    wm = vc.KvbmConnectorWorkerMetadata({"offloaded": {1: 1}})
+    conn.update_connector_output(SimpleNamespace(finished_sending={"a"}, finished_recving=None,
+                                                 kv_connector_worker_meta=wm, invalid_block_ids=set()))
     assert conn.request_finished(r1, [10, 11, 12, 13, 14, 15]) == (False, None)
 
     # the same prompt again: five blocks come from G2 (the last token is always computed)
