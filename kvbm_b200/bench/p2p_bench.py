@@ -12,8 +12,11 @@ the same bytes:
   side (gather/scatter done with the same SM kernel).
 
 Device time with CUDA events (max over the two ranks), L2 flushed before
-every timed iteration. Roofline: the measured peer copy bandwidth of this
-pool (770 GB/s per direction).
+every timed iteration. Roofline: the peer copy bandwidth measured first in
+the same run (``peer_copy`` rows: a 1 GiB ``cudaMemcpyAsync`` from this
+GPU's memory into the peer's, the copy engines' path, and the same bytes by
+the SM copy kernel; median of ``--peer-iters``); fractions are reported
+against the best of those and against the 900 GB/s nominal NVLink 5 rate.
 
     torchrun --nproc-per-node 2 -m kvbm_b200.bench.p2p_bench
 """
@@ -32,7 +35,48 @@ import torch.distributed as dist
 from ..ops import kv_ops
 from ..physical.layout import KvBlockLayout, KvLayout, LayoutConfig, LayoutDescriptor
 
-PEER_COPY_GBPS = 770.0
+NVLINK_NOMINAL_GBPS = 900.0
+PEER_COPY_GBPS = 770.0  # replaced by the run's own measurement in main()
+
+
+def measure_peer_copy(rank, remote_ptr, nbytes, iters, gloo) -> list[dict]:
+    """1 GiB from this GPU into the peer's memory: copy engine (cudaMemcpyAsync over UVA) and the SM copy
+    kernel; device time with CUDA events, median of ``iters`` after warm-up."""
+    dev = torch.device("cuda", rank)
+    src = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    src.random_(0, 256)
+    out = []
+    for path in ("cudaMemcpyAsync_peer", "sm_copy_kernel_peer"):
+        def fn(path=path):
+            if rank != 0:
+                return
+            if path.startswith("cudaMemcpy"):
+                from ..ops import _lib
+                _lib.check(_lib.load().kvbm_memcpy_async(remote_ptr, src.data_ptr(), nbytes, None), "memcpy")
+            else:
+                kv_ops.copy_pairs([src.data_ptr()], [remote_ptr], nbytes)
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            dist.barrier(group=gloo)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            ts.append(s.elapsed_time(e))
+        ms = sorted(ts)[len(ts) // 2]
+        both = [None, None]
+        dist.all_gather_object(both, ms, group=gloo)
+        r = {"path": "peer_copy", "how": path, "bytes": nbytes, "ms": round(both[0], 4),
+             "gbps": round(nbytes / both[0] / 1e6, 1), "iters": iters,
+             "frac_of_nominal": round(nbytes / both[0] / 1e6 / NVLINK_NOMINAL_GBPS, 3)}
+        out.append(r)
+        if rank == 0:
+            print(json.dumps(r), flush=True)
+    return out
 
 
 def gloo_of(args):
@@ -148,6 +192,9 @@ def main(argv=None):
                    help="also time the fused RoPE + KV push kernel (the bench's prefill path), with the decode "
                         "GPU idle and with it streaming HBM (a stand-in for decode)")
     p.add_argument("--rope-unrolls", default="2,8", help="extra RoPE/KV kernel unroll depths to time")
+    p.add_argument("--peer-iters", type=int, default=10)
+    p.add_argument("--bulk-peer", action="store_true",
+                   help="also time the TMA bulk copy storing into the peer's pool (TMA stores to NVLink memory)")
     p.add_argument("--out", default=None)
     args = p.parse_args(argv)
     args.rope_unrolls = [int(x) for x in args.rope_unrolls.split(",") if x]
@@ -173,6 +220,10 @@ def main(argv=None):
     remote = KvLayout.from_descriptor(LayoutDescriptor.from_dict(descs[1])) if rank == 0 else None
     rng = random.Random(7)
     results = []
+    global PEER_COPY_GBPS
+    pc = measure_peer_copy(rank, remote.base_ptr if rank == 0 else 0, 1 << 30, args.peer_iters, gloo)
+    results += pc
+    PEER_COPY_GBPS = max(r["gbps"] for r in pc)
 
     def timed(fn) -> float:
         for _ in range(args.warmup):
@@ -201,15 +252,23 @@ def main(argv=None):
         s_ids = torch.tensor(rng.sample(range(pool_blocks), n), dtype=torch.int32, device="cuda")
         d_ids = torch.tensor(rng.sample(range(pool_blocks), n), dtype=torch.int32, device="cuda")
         nbytes = n * cfg.bytes_per_block
-        for engine in args.engines.split(","):
+        engines = args.engines.split(",") + (["tma_bulk_peer"] if args.bulk_peer else [])
+        for engine in engines:
             for ctas in [int(c) for c in args.ctas.split(",")]:
+                ran = [None]
+
                 def fn(engine=engine, ctas=ctas):
                     if rank == 0:
-                        kv_ops.kv_transfer(local, s_ids, remote, d_ids, engine=engine, max_ctas=ctas)
+                        if engine == "tma_bulk_peer":
+                            ran[0] = kv_ops.kv_transfer(local, s_ids, remote, d_ids, engine="tma", max_ctas=ctas,
+                                                        bulk=True)
+                        else:
+                            ran[0] = kv_ops.kv_transfer(local, s_ids, remote, d_ids, engine=engine, max_ctas=ctas)
                 ms = timed(fn)
-                r = {"path": f"fused_{engine}", "max_ctas": ctas, "requests": nreq, "bytes": nbytes,
-                     "ms": round(ms, 4), "gbps": round(nbytes / ms / 1e6, 1),
-                     "frac_of_peer_copy": round(nbytes / ms / 1e6 / PEER_COPY_GBPS, 3)}
+                r = {"path": f"fused_{engine}", "kernel": ran[0], "max_ctas": ctas, "requests": nreq,
+                     "bytes": nbytes, "ms": round(ms, 4), "gbps": round(nbytes / ms / 1e6, 1),
+                     "frac_of_peer_copy": round(nbytes / ms / 1e6 / PEER_COPY_GBPS, 3),
+                     "frac_of_nominal": round(nbytes / ms / 1e6 / NVLINK_NOMINAL_GBPS, 3)}
                 results.append(r)
                 if rank == 0:
                     print(json.dumps(r), flush=True)

@@ -42,12 +42,13 @@ from collections import deque
 from dataclasses import dataclass, field
 
 from ..engine.cd import ConditionalDisagg, Decision, RemotePrefillParams
-from ..engine.leader import FindMatchesOptions, InstanceLeader
-from ..logical.manager import ImmutableBlock, MutableBlock
+from ..engine.leader import FindMatchesOptions, InstanceLeader, StagingMode
+from ..engine.offload import OffloadItem, OffloadPolicy, PresenceFilter
+from ..logical.manager import ImmutableBlock, MutableBlock, Tier
 from ..logical.sequence import TokenBlockSequence
 from ..utils.metrics import CacheStatsTracker
 from ..utils.tracing import audit
-from .protocol import ConnectorMetadata, OffloadOp, OnboardOp, PushOp, RecvOp
+from .protocol import ConnectorMetadata, OffloadOp, OnboardOp, PushOp, RecvOp, SpillOp, StageOp
 
 # kv_transfer_params key a decode instance puts on the requests it sends to a prefill instance
 REMOTE_DECODE_KEY = "kvbm_remote_decode"
@@ -105,6 +106,9 @@ class RequestSlot:
     cd_decided: bool = False
     remote_prefill: RemotePrefill | None = None
     push: PushState | None = None
+    # G3 hits being staged into G2 for this request's onboard: (G3 refs, G2 destinations, hashes)
+    staging: tuple[list[ImmutableBlock], list[MutableBlock], list[int]] | None = None
+    onboard_pending: bool = False             # an onboard (or stage) was queued and not reported received
 
 
 @dataclass
@@ -135,7 +139,8 @@ class ConnectorLeader:
     def __init__(self, leader: InstanceLeader, block_size: int, offload_enabled: bool = True,
                  decode_offload: bool = False, stats: CacheStatsTracker | None = None, remote_search=None,
                  cd: ConditionalDisagg | None = None, plane=None, prefill_target=None, instance_id: int = 0,
-                 mailbox_slots: int = 0, recv_timeout_s: float = 120.0, num_workers: int = 1):
+                 mailbox_slots: int = 0, recv_timeout_s: float = 120.0, num_workers: int = 1,
+                 g2_policy: OffloadPolicy | None = None, g3_policy: OffloadPolicy | None = None):
         self.leader = leader
         self.remote = remote_search  # engine.remote_search.RemoteSearch, or None
         self.block_size = block_size
@@ -155,6 +160,14 @@ class ConnectorLeader:
         self.num_workers = num_workers
         # step -> (G2 mutables awaiting their copies, their hashes, worker reports so far)
         self._pending_g2: dict[int, tuple[list[MutableBlock], list[int], int]] = {}
+        # G1 -> G2 and G2 -> G3 admission policies (the offload pipelines' filters)
+        self.g2_policy = g2_policy or PresenceFilter(leader.g2)
+        self.g3_policy = g3_policy or (PresenceFilter(leader.g3) if leader.g3 is not None else None)
+        self._spill_queue: list[tuple[list[ImmutableBlock], list[MutableBlock], list[int]]] = []
+        # step -> (G3 mutables awaiting the spill copies, hashes, G2 sources held, worker reports so far)
+        self._pending_g3: dict[int, tuple[list[MutableBlock], list[int], list[ImmutableBlock], int]] = {}
+        self._stage_ops: list[StageOp] = []
+        self.tier_stats = {"staged_from_g3": 0, "spilled_to_g3": 0}
         self.cd_stats = {"remote": 0, "local": 0, "dispatched": 0, "received": 0, "failed": 0, "pushed_blocks": 0}
 
     # ---------------------------------------------------------------- slots
@@ -190,9 +203,10 @@ class ConnectorLeader:
         if num_computed_tokens % self.block_size or start > len(hashes):
             return 0, False
         blocks: list[ImmutableBlock] = []
+        if slot.staging is not None:
+            self._release_staging(slot)
         if start < len(hashes):
-            res = self.leader.find_matches(hashes[start:], FindMatchesOptions())
-            blocks = res.g2_blocks
+            blocks = self._find(hashes[start:])
         # the framework must compute at least the last prompt token itself
         max_blocks = (len(slot.request.tokens) - 1 - num_computed_tokens) // self.block_size
         if self.remote is not None and not slot.remote_done and len(blocks) < max_blocks:
@@ -214,10 +228,11 @@ class ConnectorLeader:
             if pulled:
                 for b in blocks:
                     b.release()
-                blocks = self.leader.find_matches(hashes[start:], FindMatchesOptions()).g2_blocks
+                blocks = self._find(hashes[start:])
         for b in blocks[max(0, max_blocks):]:
             b.release()
         blocks = blocks[: max(0, max_blocks)]
+        blocks = self._prepare_staging(slot, blocks)
         self.stats.record("host", len(hashes) - start, len(blocks), self.block_size)
         slot.matched = blocks
         slot.matched_start_block = start
@@ -230,6 +245,33 @@ class ConnectorLeader:
         if slot.remote_done:
             audit("gnmt_matched", request=req_id, matched_tokens=local_tokens)
         return local_tokens, True
+
+    def _find(self, hashes: list[int]) -> list[ImmutableBlock]:
+        """G2 prefix, continued in G3 (held, not staged: the workers stage them with the onboard)."""
+        res = self.leader.find_matches(hashes, FindMatchesOptions(staging=StagingMode.PREPARE))
+        return res.g2_blocks + res.g3_held
+
+    def _prepare_staging(self, slot: RequestSlot, blocks: list[ImmutableBlock]) -> list[ImmutableBlock]:
+        """Give every G3 block of the match a G2 destination; without room in G2 the match stops before G3."""
+        g3 = [b for b in blocks if b.tier == Tier.G3]
+        if not g3:
+            return blocks
+        g2 = blocks[: len(blocks) - len(g3)]
+        got = self.leader.g2.allocate_blocks_with_evictions(len(g3))
+        if got is None:
+            for b in g3:
+                b.release()
+            return g2
+        slot.staging = (g3, got[0], [b.sequence_hash for b in g3])
+        return blocks
+
+    def _release_staging(self, slot: RequestSlot) -> None:
+        g3, dst, _ = slot.staging
+        slot.staging = None
+        for b in g3:
+            b.release()
+        for m in dst:
+            m.release()
 
     def _decide_remote(self, slot: RequestSlot, computed: int, local_tokens: int) -> bool:
         """Decode-side CD decision (policy, breaker tier, in-flight budget, a free mailbox slot)."""
@@ -274,8 +316,23 @@ class ConnectorLeader:
         g1 = slot.g1_block_ids[start: start + n]
         if len(g1) != n:
             raise ValueError(f"{req_id}: {n} onboard blocks but only {len(g1)} G1 destinations")
+        src_ids = [b.block_id for b in take if b.tier == Tier.G2]
+        if slot.staging is not None:
+            g3, dst, hashes = slot.staging
+            k = n - len(src_ids)  # G3 blocks actually onboarded
+            for b in g3[k:]:
+                b.release()
+            for m in dst[k:]:
+                m.release()
+            slot.staging = (g3[:k], dst[:k], hashes[:k]) if k else None
+            if k:
+                self._stage_ops.append(StageOp(req_id, [b.block_id for b in g3[:k]], [m.block_id for m in dst[:k]]))
+                src_ids += [m.block_id for m in dst[:k]]
+                self.tier_stats["staged_from_g3"] += k
+            take = [b for b in take if b.tier == Tier.G2]
         if n:
-            self._onboard_ops.append(OnboardOp(req_id, [b.block_id for b in take], g1))
+            self._onboard_ops.append(OnboardOp(req_id, src_ids, g1))
+            slot.onboard_pending = True
         slot.onboarding = take
         slot.matched = []
         # onboarded blocks are already in G2: the save cursor skips past them
@@ -310,8 +367,18 @@ class ConnectorLeader:
     # ------------------------------------------------------ metadata build
     def build_connector_meta(self, out: SchedulerOutputLite) -> bytes:
         self.iteration += 1
-        meta = ConnectorMetadata(step=out.step or self.iteration, onboard=self._onboard_ops, recv=self._recv_ops)
-        self._onboard_ops, self._recv_ops = [], []
+        meta = ConnectorMetadata(step=out.step or self.iteration, onboard=self._onboard_ops, recv=self._recv_ops,
+                                 stage=self._stage_ops)
+        self._onboard_ops, self._recv_ops, self._stage_ops = [], [], []
+        if self._spill_queue:
+            srcs, dsts, hs = [], [], []
+            for g2_refs, g3_dst, hashes in self._spill_queue:
+                meta.spill.append(SpillOp([b.block_id for b in g2_refs], [m.block_id for m in g3_dst]))
+                srcs += g2_refs
+                dsts += g3_dst
+                hs += hashes
+            self._spill_queue = []
+            self._pending_g3[meta.step] = (dsts, hs, srcs, 0)
         for req_id in out.preempted_req_ids:
             # The workers fence in-flight offloads of these requests before their G1 blocks are
             # reused (evict list). The request resumes from its token sequence with new G1 blocks;
@@ -348,7 +415,8 @@ class ConnectorLeader:
             reg = self.leader.g2.registry
             tier = int(self.leader.g2.tier)
             pending = set(g2_hashes) | self._pending_hashes()
-            todo = [(h, b) for h, b in zip(hashes, g1) if not reg.is_present(h, tier) and h not in pending]
+            todo = [(h, b) for h, b in zip(hashes, g1)
+                    if h not in pending and self.g2_policy.keep(OffloadItem(h, b)) and not reg.is_present(h, tier)]
             slot.save_cursor = complete
             if not todo:
                 continue
@@ -392,6 +460,7 @@ class ConnectorLeader:
                                 invalid_block_ids: set[int] | None = None) -> None:
         if worker_meta:
             self._register_landed(worker_meta.get("offloaded", {}))
+            self._register_spilled(worker_meta.get("spilled", {}))
         bad = set(invalid_block_ids or ())
         for req_id in finished_recving or ():
             slot = self.slots.get(req_id)
@@ -400,6 +469,15 @@ class ConnectorLeader:
             for b in slot.onboarding:
                 b.release()
             slot.onboarding = []
+            slot.onboard_pending = False
+            if slot.staging is not None:
+                # the stage ran before the onboard that finished: the G2 copies hold the data now
+                g3, dst, hashes = slot.staging
+                slot.staging = None
+                for b in self.leader.g2.register_mutable(dst, hashes):
+                    b.release()
+                for b in g3:
+                    b.release()
             rp = slot.remote_prefill
             if rp is not None:
                 failed = bool(bad.intersection(slot.g1_block_ids))
@@ -437,14 +515,52 @@ class ConnectorLeader:
                 self._pending_g2[step] = (blocks, hashes, seen)
                 continue
             del self._pending_g2[step]
-            for b in self.leader.g2.register_mutable(blocks, hashes):
+            imm = self.leader.g2.register_mutable(blocks, hashes)
+            self._chain_to_g3(imm)
+            for b in imm:
                 b.release()  # cached in G2 (inactive, matchable)
+
+    def _chain_to_g3(self, imm: list[ImmutableBlock]) -> None:
+        """G2 -> G3: blocks the G3 policy admits get G3 destinations; the next step's workers copy them."""
+        g3 = self.leader.g3
+        if g3 is None or not imm:
+            return
+        pending = {h for _, hs, _, _ in self._pending_g3.values() for h in hs}
+        pending |= {h for _, _, hs in self._spill_queue for h in hs}
+        keep = [b for b in imm if b.sequence_hash not in pending
+                and self.g3_policy.keep(OffloadItem(b.sequence_hash, b.block_id))]
+        if not keep:
+            return
+        got = g3.allocate_blocks_with_evictions(len(keep))
+        if got is None:
+            return
+        self._spill_queue.append(([b.clone() for b in keep], got[0], [b.sequence_hash for b in keep]))
+
+    def _register_spilled(self, spilled: dict) -> None:
+        for step, n in spilled.items():
+            step = int(step)
+            entry = self._pending_g3.get(step)
+            if entry is None:
+                continue
+            dst, hashes, srcs, seen = entry
+            seen += int(n)
+            if seen < self.num_workers:
+                self._pending_g3[step] = (dst, hashes, srcs, seen)
+                continue
+            del self._pending_g3[step]
+            for b in self.leader.g3.register_mutable(dst, hashes):
+                b.release()
+            for b in srcs:
+                b.release()
+            self.tier_stats["spilled_to_g3"] += len(dst)
 
     def request_finished(self, req_id: str, block_ids: list[int] | None = None) -> tuple[bool, dict | None]:
         slot = self.slots.get(req_id)
         if slot is None:
             return False, None
         slot.finished = True
+        if slot.staging is not None and not slot.onboard_pending:
+            self._release_staging(slot)
         for b in slot.matched + slot.onboarding:
             b.release()
         slot.matched, slot.onboarding = [], []

@@ -98,6 +98,7 @@ class ConnectorWorker:
         self._load_errors: set[int] = set()
         self._pending_finished: set[str] = set()
         self._offload_steps: list[tuple[int, torch.cuda.Event]] = []
+        self._spill_steps: list[int] = []
         # conditional disaggregation
         self.layer_batch = max(1, int(self.config.transfer.layer_batch))
         self.push_engine = self.config.transfer.push_engine
@@ -109,6 +110,8 @@ class ConnectorWorker:
         self._recvs: dict[str, tuple] = {}
         self.push_timing = False
         self._push_timers: list[tuple[torch.cuda.Event, torch.cuda.Event, int]] = []
+        self.onboard_timing = False   # bracket each step's onboards with CUDA events (take_onboard_timings)
+        self._onboard_timers: list[tuple[torch.cuda.Event, torch.cuda.Event, int]] = []
 
     # --------------------------------------------------------- registration
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor], num_blocks: int | None = None,
@@ -204,6 +207,16 @@ class ConnectorWorker:
             conn = self._peers[instance] = PeerConnection(self.directory.lookup(instance), self.device)
         return conn
 
+    def take_onboard_timings(self) -> tuple[float, int]:
+        """(summed device ms of the steps' G2 -> G1 onboards, bytes onboarded) since the last call; waits."""
+        ms = nb = 0
+        for s, e, b in self._onboard_timers:
+            e.synchronize()
+            ms += s.elapsed_time(e)
+            nb += b
+        self._onboard_timers.clear()
+        return ms, nb
+
     def take_push_timings(self) -> tuple[float, int]:
         """(summed device ms of the push launches, bytes pushed) since the last call; waits for them."""
         ms = nb = 0
@@ -254,6 +267,10 @@ class ConnectorWorker:
         self._layer_events = []
         if not meta.onboard:
             return
+        t0 = None
+        if self.onboard_timing:
+            t0 = torch.cuda.Event(enable_timing=True)
+            t0.record(h2d)
         if intra:
             g2 = [i for op in meta.onboard for i in op.g2_ids]
             g1 = [i for op in meta.onboard for i in op.g1_ids]
@@ -274,6 +291,11 @@ class ConnectorWorker:
                 self._recv_events[op.req_id] = ev
             # inter mode: the whole onboard completes before the forward pass
             torch.cuda.current_stream(self.device).wait_stream(h2d)
+        if t0 is not None:
+            t1 = torch.cuda.Event(enable_timing=True)
+            t1.record(h2d)
+            nblk = sum(len(op.g1_ids) for op in meta.onboard)
+            self._onboard_timers.append((t0, t1, nblk * self.g1.config.bytes_per_block))
 
     def wait_for_layer_load(self, layer: int | str) -> None:
         if isinstance(layer, str):
@@ -341,11 +363,11 @@ class ConnectorWorker:
             self._last_offload = ev
         if meta.offload:
             self._offload_steps.append((meta.step, self._last_offload))
-        for op in meta.spill:  # G2 -> G3 behind this step's offloads
-            if self._last_offload is not None:
-                self._last_offload.synchronize()
+        for op in meta.spill:  # G2 -> G3 (the sources were registered after their offload landed)
             w.tm.execute_transfer(w.handles.g2, op.g2_ids, w.handles.g3, op.g3_ids,
-                                  TransferOptions(stream=d2h, engine=w.engine)).wait()
+                                  TransferOptions(engine=w.engine)).wait()
+        if meta.spill:
+            self._spill_steps.append(meta.step)
 
     def get_finished(self, finished_req_ids: set[str] | None = None) -> tuple[set[str], set[str]]:
         recving = {r for r, ev in self._recv_events.items() if ev.query()}
@@ -381,7 +403,14 @@ class ConnectorWorker:
         while self._offload_steps and self._offload_steps[0][1].query():
             step, _ = self._offload_steps.pop(0)
             done[step] = 1
-        return {"offloaded": done} if done else None
+        spilled = {s: 1 for s in self._spill_steps}
+        self._spill_steps = []
+        out = {}
+        if done:
+            out["offloaded"] = done
+        if spilled:
+            out["spilled"] = spilled
+        return out or None
 
     def get_block_ids_with_load_errors(self) -> set[int]:
         out, self._load_errors = self._load_errors, set()

@@ -144,6 +144,43 @@ int kvbm_kv_checksum(const KvbmSide* side, const KvbmTileShape* shape, uint64_t*
 // Number of SMs of the current device (cached).
 int kvbm_sm_count(void);
 
+// ---- Llama driver harness: paged decode attention (llama_ops.cu) ----------
+//
+// Split-KV paged decode attention over a block table, grouped-query heads
+// (hq = group * hkv), head_dim 128, bf16 q / K / V / out. The caller provides
+// the split partials: part_acc (batch * hq * splits * 128 floats) and
+// part_ml (batch * hq * splits * 2 floats). Two launches (split kernel, then
+// combine).
+int kvbm_paged_decode_attn(const void* q, const void* k_base, const void* v_base, int64_t block_stride,
+                           int64_t token_stride, int64_t head_stride, int page, const int32_t* block_table,
+                           int max_blocks, const int32_t* seq_lens, int batch, int hq, int hkv, int hd,
+                           float softmax_scale, int splits, float* part_acc, float* part_ml, void* out,
+                           cudaStream_t stream);
+
+// The same attention for callers that cannot allocate device memory when they
+// call in (an application that owns all device memory in its own arena, code
+// running inside an allocator callback, a path that cannot absorb the device
+// synchronization cudaMalloc / cudaFree may cause). No counterpart in the
+// reference block manager: an addition of this library.
+//
+// The split partials live in a fixed array of device memory inside this
+// library (kvbm_paged_decode_attn_noalloc_max_rows() rows of 130 floats,
+// about 4.3 MB, held by every GPU that loads the library until the process
+// exits). The first call on a device, with that device current, looks the
+// array's address up once (cudaGetSymbolAddress) and caches it: make that
+// first call before any stream capture. batch * hq * splits above the
+// capacity is rejected with cudaErrorInvalidValue. All calls on a device share
+// the array: calls whose kernels can overlap on the GPU race on it, so order
+// them on one stream or with events. After cudaDeviceReset the cached address
+// is stale: do not call this entry point on a device after resetting it.
+// On failure kvbm_last_error_message() says why (per calling thread).
+int kvbm_paged_decode_attn_noalloc(const void* q, const void* k_base, const void* v_base, int64_t block_stride,
+                                   int64_t token_stride, int64_t head_stride, int page, const int32_t* block_table,
+                                   int max_blocks, const int32_t* seq_lens, int batch, int hq, int hkv, int hd,
+                                   float softmax_scale, int splits, void* out, cudaStream_t stream);
+int kvbm_paged_decode_attn_noalloc_max_rows(void);
+const char* kvbm_last_error_message(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -10,6 +10,7 @@
 // (skinny_gemm_tc.cu) or cuBLAS; prefill GEMMs on cuBLAS.
 #include "common.cuh"
 #include "decode_attn_mma.cuh"
+#include "kvbm_kernels.h"
 
 #include <algorithm>
 
@@ -933,6 +934,9 @@ int decode_attn_mma(const void* q, const void* k_base, const void* v_base, int64
 // is rejected with cudaErrorInvalidValue, and kvbm_last_error_message() says
 // why.
 //
+// Reset: after cudaDeviceReset the address cached for that device is stale;
+// the entry point must not be called on a device after resetting it.
+//
 // Sharing: all calls on one device use the same array, which still holds the
 // previous call's partials. Nothing has to be cleared first, because each
 // call's split kernel writes every partial row its combine kernel reads. Two
@@ -1005,7 +1009,11 @@ extern "C" int kvbm_paged_decode_attn_noalloc(const void* q, const void* k_base,
   }
   float* part_acc = base;
   float* part_ml = base + rows * kHD;
-  return kvbm_paged_decode_attn(q, k_base, v_base, block_stride, token_stride, head_stride, page, block_table,
-                                max_blocks, seq_lens, batch, hq, hkv, hd, softmax_scale, splits, part_acc, part_ml,
-                                out, stream);
+  e = static_cast<cudaError_t>(kvbm_paged_decode_attn(q, k_base, v_base, block_stride, token_stride, head_stride,
+                                                      page, block_table, max_blocks, seq_lens, batch, hq, hkv, hd,
+                                                      softmax_scale, splits, part_acc, part_ml, out, stream));
+  if (e != cudaSuccess)
+    std::snprintf(g_last_error, sizeof(g_last_error), "kvbm_paged_decode_attn_noalloc: attention launch failed (%s)",
+                  cudaGetErrorString(e));
+  return e;
 }

@@ -33,7 +33,14 @@
 //   +31), stores or red.add, ticket, conversion.
 // Every wait is bounded (%globaltimer) and also gives up when another role has
 // given up; the CTA then records kStatusPipelineTimeout in g_gemm_status, lets
-// its copies and MMAs drain (bounded), frees its TMEM and returns.
+// its copies and MMAs drain (bounded), frees its TMEM and returns. Such a
+// launch leaves the workspace and tickets dirty; the host zeroes them
+// (ops/llama_ops.py skinny_gemm_status).
+//
+// The stream-K schedule (SegIter, the rounds / per-CTA split and the grid
+// shrink in the host launcher, the ticket rule) is restated as a Python model
+// in tests/test_gemm_cluster_protocol.py and model-checked there: change both
+// together.
 #include "common.cuh"
 
 #include <cuda.h>

@@ -140,7 +140,17 @@ class InstanceLeader:
         return res
 
     def stage_g3_to_g2(self, g3_blocks: list[ImmutableBlock]) -> list[ImmutableBlock]:
-        """Disk -> pinned for the given G3 blocks; returns the registered G2 blocks."""
+        """Disk -> pinned for the given G3 blocks; returns the registered G2 blocks.
+
+        The copy runs on this leader's workers; a leader without workers (the
+        scheduler side of a connector, whose workers live in other processes)
+        cannot stage and raises: it finds with ``StagingMode.PREPARE`` and has
+        the connector's workers stage the held blocks with the onboard."""
+        if not len(self.workers):
+            for b in g3_blocks:
+                b.release()
+            raise RuntimeError("no workers to stage G3 -> G2 here; find with StagingMode.PREPARE and let the "
+                               "connector's workers stage the held G3 blocks")
         got = self.g2.allocate_blocks_with_evictions(len(g3_blocks))
         if got is None:
             for b in g3_blocks:

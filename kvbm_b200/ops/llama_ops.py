@@ -163,6 +163,12 @@ class GemmWorkspace:
         if self.tickets.numel() < tiles:
             self.tickets = torch.zeros(tiles, dtype=torch.int32, device=self.device)
 
+    def clear(self) -> None:
+        """Zero the partial sums and tickets (after a launch that gave up: an aborted CTA
+        leaves its tile's ticket short and its partial sums in place)."""
+        self.ws.zero_()
+        self.tickets.zero_()
+
 
 _workspaces: dict[int, GemmWorkspace] = {}
 
@@ -201,8 +207,19 @@ def skinny_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
 
 
 def skinny_gemm_status(reset: bool = True) -> int:
-    """0, or the error a :func:`skinny_gemm` launch recorded (3: a pipeline wait timed out). Synchronizes."""
-    return int(_lib.load().kvbm_skinny_gemm_status(1 if reset else 0))
+    """0, or the error a :func:`skinny_gemm` launch recorded (3: a pipeline wait timed out). Synchronizes.
+
+    A launch that gave up leaves its workspace dirty (partial sums, a ticket
+    count that never reached the last CTA). With ``reset`` and a nonzero
+    status, the per-device workspaces used when no ``workspace`` is passed are
+    zeroed here; callers that pass their own workspace must call its
+    :meth:`GemmWorkspace.clear` before the next launch."""
+    st = int(_lib.load().kvbm_skinny_gemm_status(1 if reset else 0))
+    if st and reset:
+        for ws in _workspaces.values():
+            ws.clear()
+        torch.cuda.synchronize()
+    return st
 
 
 def set_skinny_gemm_pdl(on: bool) -> bool:

@@ -41,6 +41,8 @@ import torch
 
 from ..connector.leader import ConnectorLeader, KvbmRequest, SchedulerOutputLite
 from ..connector.worker import ConnectorWorker
+from ..logical.manager import BlockManager, MutableBlock, Tier
+from ..logical.sequence import sequence_hashes
 from ..models.llama import LlamaModel
 from ..ops import llama_ops
 from ..physical.layout import KvLayout
@@ -63,7 +65,8 @@ class Request:
     salt: str | None = None
     status: RequestStatus = RequestStatus.WAITING
     num_computed_tokens: int = 0
-    num_external_tokens: int = 0
+    num_cached_tokens: int = 0           # prompt tokens found in this engine's own G1 prefix cache
+    num_external_tokens: int = 0         # prompt tokens the connector loads (G2/G3 onboard or a remote prefill)
     block_ids: list[int] = field(default_factory=list)
     num_output: int = 0
     slot: int = -1
@@ -75,6 +78,8 @@ class Request:
     _dev_prompt: torch.Tensor | None = None
     _dev_ids: torch.Tensor | None = None
     _first_tok: torch.Tensor | None = None
+    _handles: list = field(default_factory=list)   # prefix-cache mode: G1 block handles held
+    _hashes: list[int] | None = None
 
     @property
     def num_prompt_tokens(self) -> int:
@@ -93,6 +98,7 @@ class EngineConfig:
     decode_splits: int | None = None
     record_events: bool = True           # arrival / first-token CUDA events per request
     max_inflight_steps: int = 2          # the host runs at most this many steps ahead of the GPU
+    prefix_caching: bool = False         # keep finished prompts' full blocks in G1 (LRU) and match them first
 
 
 class DecodeBatch:
@@ -104,14 +110,15 @@ class DecodeBatch:
     """
 
     def __init__(self, model: LlamaModel, pool: KvLayout, slots: int, max_blocks: int, max_out: int, splits: int,
-                 use_graphs: bool = True):
+                 use_graphs: bool = True, dummy_block: int = 0):
         self.model, self.pool, self.slots = model, pool, slots
+        self.dummy = int(dummy_block)
         self.max_blocks, self.max_out, self.splits = max_blocks, max_out, splits
         dev = model.device
         self.tok = torch.zeros(slots, dtype=torch.int64, device=dev)
         self.pos = torch.zeros(slots, dtype=torch.int32, device=dev)
         self.seq_lens = torch.ones(slots, dtype=torch.int32, device=dev)
-        self.block_table = torch.zeros(slots, max_blocks, dtype=torch.int32, device=dev)
+        self.block_table = torch.full((slots, max_blocks), self.dummy, dtype=torch.int32, device=dev)
         self.active = torch.zeros(slots, dtype=torch.int32, device=dev)
         self.out_idx = torch.zeros(slots, 1, dtype=torch.int64, device=dev)
         self.out = torch.zeros(slots, max_out, dtype=torch.int64, device=dev)
@@ -132,7 +139,7 @@ class DecodeBatch:
         self.tok.zero_()
         self.pos.zero_()
         self.seq_lens.fill_(1)
-        self.block_table.zero_()
+        self.block_table.fill_(self.dummy)
         self.active.zero_()
         self.out_idx.zero_()
 
@@ -163,7 +170,7 @@ class DecodeBatch:
         n = len(entries)
         dev = self.tok.device
         slots = torch.tensor([e[0] for e in entries], dtype=torch.int64)
-        rows = torch.zeros(n, self.max_blocks, dtype=torch.int32)
+        rows = torch.full((n, self.max_blocks), self.dummy, dtype=torch.int32)
         for i, e in enumerate(entries):
             if len(e[1]) > self.max_blocks:
                 raise ValueError(f"{len(e[1])} blocks exceed the decode batch's {self.max_blocks}")
@@ -188,7 +195,7 @@ class DecodeBatch:
         self.pos.index_fill_(0, idx, 0)
         self.seq_lens.index_fill_(0, idx, 1)
         self.out_idx.index_fill_(0, idx, 0)
-        self.block_table.index_fill_(0, idx, 0)
+        self.block_table.index_fill_(0, idx, self.dummy)
 
     def step(self) -> None:
         if self.graph is not None:
@@ -209,7 +216,17 @@ class LLMEngine:
         self.device = model.device
         self.pool = pool if pool is not None else model.allocate_pool(cfg.num_gpu_blocks, cfg.block_size)
         self.leader, self.worker = leader, worker
-        self.free_blocks = deque(range(1, cfg.num_gpu_blocks))  # block 0: target of idle decode slots
+        self.g1: BlockManager | None = None
+        if cfg.prefix_caching:
+            # G1 blocks through the logical block manager: finished prompts' full blocks stay
+            # registered (inactive, LRU-evicted) and later prompts match them before asking the connector
+            self.g1 = BlockManager(cfg.num_gpu_blocks, cfg.block_size, "lru", Tier.G1)
+            self._dummy_handle = self.g1.allocate_blocks(1)[0]  # target of idle decode slots, never freed
+            dummy = self._dummy_handle.block_id
+            self.free_blocks = deque()
+        else:
+            self.free_blocks = deque(range(1, cfg.num_gpu_blocks))  # block 0: target of idle decode slots
+            dummy = 0
         self.requests: dict[str, Request] = {}
         self.waiting: deque[Request] = deque()
         self.remote: dict[str, Request] = {}
@@ -224,8 +241,9 @@ class LLMEngine:
         splits = cfg.decode_splits or llama_ops.decode_splits(cfg.max_num_seqs, model.cfg.kv_heads,
                                                               cfg.max_model_len, cfg.block_size)
         self.batch = DecodeBatch(model, self.pool, cfg.max_num_seqs, max_blocks, cfg.max_tokens, splits,
-                                 cfg.use_graphs)
-        self.stats = {"steps": 0, "prefill_tokens": 0, "decode_steps": 0, "finished": 0, "recomputed": 0}
+                                 cfg.use_graphs, dummy_block=dummy)
+        self.stats = {"steps": 0, "prefill_tokens": 0, "decode_steps": 0, "finished": 0, "recomputed": 0,
+                      "prompt_tokens": 0, "g1_hit_tokens": 0, "external_tokens": 0}
         self._inflight: deque[torch.cuda.Event] = deque()
 
     # ------------------------------------------------------------- public
@@ -301,28 +319,66 @@ class LLMEngine:
     def _blocks_needed(self, req: Request) -> int:
         return math.ceil((req.num_prompt_tokens + max(0, req.max_tokens - 1)) / self.cfg.block_size)
 
+    def _allocate(self, req: Request, need: int) -> bool:
+        """G1 blocks for ``req`` (its cached prefix first in prefix-cache mode); False if G1 is full."""
+        if self.g1 is None:
+            if len(self.free_blocks) < need:
+                return False
+            req.block_ids = [self.free_blocks.popleft() for _ in range(need)]
+            req.num_cached_tokens = 0
+            return True
+        bs = self.cfg.block_size
+        if req._hashes is None:
+            req._hashes = sequence_hashes(req.prompt.numpy(), bs, req.salt)
+        hits = self.g1.match_blocks(req._hashes[: (req.num_prompt_tokens - 1) // bs])
+        fresh = self.g1.allocate_blocks(need - len(hits))
+        if fresh is None:
+            for b in hits:
+                b.release()
+            return False
+        req._handles = hits + fresh
+        req.block_ids = [b.block_id for b in req._handles]
+        req.num_cached_tokens = len(hits) * bs
+        return True
+
+    def _register_prompt(self, req: Request) -> None:
+        """Prefix-cache mode: the prompt's full blocks hold their final K/V now; make them matchable."""
+        if self.g1 is None or not req._handles:
+            return
+        nfull = req.num_prompt_tokens // self.cfg.block_size
+        first = req.num_cached_tokens // self.cfg.block_size
+        fresh = [b for b in req._handles[first:nfull] if isinstance(b, MutableBlock)]
+        if len(fresh) != nfull - first:
+            return  # already registered
+        reg = self.g1.register_mutable(fresh, req._hashes[first:nfull])
+        req._handles = req._handles[:first] + reg + req._handles[nfull:]
+
     def _admit(self, so: SchedulerOutputLite) -> None:
         for _ in range(len(self.waiting)):
             req = self.waiting[0]
             need = self._blocks_needed(req)
-            if len(self.free_blocks) < need:
+            if not self._allocate(req, need):
                 break
             n_ext, is_async = 0, False
             if self.leader is not None:
-                n_ext, is_async = self.leader.get_num_new_matched_tokens(req.request_id, 0)
+                n_ext, is_async = self.leader.get_num_new_matched_tokens(req.request_id, req.num_cached_tokens)
                 if n_ext is None:  # the connector is still searching: try again next step
+                    self._release_blocks(req)
                     self.waiting.rotate(-1)
                     continue
             self.waiting.popleft()
-            req.block_ids = [self.free_blocks.popleft() for _ in range(need)]
             if self.leader is not None:
                 self.leader.update_state_after_alloc(req.request_id, req.block_ids, n_ext)
             req.num_external_tokens = n_ext
+            self.stats["prompt_tokens"] += req.num_prompt_tokens
+            self.stats["g1_hit_tokens"] += req.num_cached_tokens
+            self.stats["external_tokens"] += n_ext
             if n_ext and is_async:
                 req.status = RequestStatus.WAITING_FOR_REMOTE_KVS
+                req.num_computed_tokens = req.num_cached_tokens
                 self.remote[req.request_id] = req
             else:
-                req.num_computed_tokens = n_ext
+                req.num_computed_tokens = req.num_cached_tokens + n_ext
                 req.status = RequestStatus.PREFILL
                 self.prefilling.append(req)
 
@@ -376,6 +432,7 @@ class LLMEngine:
         if end < req.num_prompt_tokens:
             return
         self.prefilling.remove(req)
+        self._register_prompt(req)
         req.num_output = 1
         if self._mark is not None:
             req.first_token_event = torch.cuda.Event(enable_timing=True)
@@ -428,7 +485,15 @@ class LLMEngine:
 
     def _free(self, req: Request) -> None:
         # the request keeps the list of the blocks it held (for inspection); the blocks return to the pool
-        self.free_blocks.extend(req.block_ids)
+        self._release_blocks(req)
+
+    def _release_blocks(self, req: Request) -> None:
+        if self.g1 is None:
+            self.free_blocks.extend(req.block_ids)
+            return
+        for b in req._handles:
+            b.release()  # registered blocks stay cached (inactive) until G1 evicts them
+        req._handles = []
 
     def _on_sent(self, sending: set[str]) -> None:
         for rid in sending:
@@ -445,14 +510,15 @@ class LLMEngine:
             if errs and errs.intersection(req.block_ids):
                 # the external KV never arrived: recompute the prompt here
                 req.load_failed = True
-                req.num_computed_tokens = 0
+                req.num_computed_tokens = req.num_cached_tokens
                 req.status = RequestStatus.PREFILL
                 self.prefilling.append(req)
                 self.stats["recomputed"] += 1
                 continue
-            req.num_computed_tokens = req.num_external_tokens
+            req.num_computed_tokens = req.num_cached_tokens + req.num_external_tokens
             if req.num_computed_tokens >= S and req.max_tokens > 1:
                 req.num_computed_tokens = S - 1
+                self._register_prompt(req)
                 self.ready.append(req)
             else:
                 req.num_computed_tokens = min(req.num_computed_tokens, S - 1)

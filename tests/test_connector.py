@@ -129,3 +129,43 @@ def test_lazy_import_does_not_pull_vllm():
             "print('vllm' in sys.modules)")
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True)
     assert out.stdout.strip() == "False"
+
+
+def test_g2_spills_to_g3_and_g3_hits_are_staged_by_the_workers():
+    """G2 capped at 4 blocks: registered G2 blocks chain to G3 (a spill op the workers run),
+    evicted G2 blocks come back from G3 (a stage op before the onboard) and are registered
+    in G2 only once the onboard is reported received."""
+    g2 = BlockManager(4, 16, "lru", Tier.G2)
+    g3 = BlockManager(32, 16, "lru", Tier.G3, registry=g2.registry)
+    L = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([]), g3=g3), 16)
+    prompt = list(range(64))
+    L.create_slot(KvbmRequest("a", prompt))
+    L.update_state_after_alloc("a", [0, 1, 2, 3, 4], 0)
+    m1 = step(L, 1, {"a": ([], [], 65)})
+    assert [o.g1_ids for o in m1.offload] == [[0, 1, 2, 3]] and m1.spill == []
+    L.update_connector_output(worker_meta={"offloaded": {1: 1}})
+    m2 = step(L, 2, {})
+    assert len(m2.spill) == 1 and len(m2.spill[0].g2_ids) == 4
+    L.update_connector_output(worker_meta={"spilled": {2: 1}})
+    assert L.tier_stats["spilled_to_g3"] == 4
+    # a different prompt fills G2 and evicts a's blocks there
+    other = list(range(1000, 1064))
+    L.create_slot(KvbmRequest("b", other))
+    L.update_state_after_alloc("b", [10, 11, 12, 13, 14], 0)
+    step(L, 3, {"b": ([], [], 65)})
+    L.update_connector_output(worker_meta={"offloaded": {3: 1}})
+    assert g2.count_prefix(L.slots["a"].seq.sequence_hashes) == 0
+    assert len(step(L, 4, {}).spill) == 1  # b's blocks chain to G3 too; G2 holds them until the copy lands
+    L.update_connector_output(worker_meta={"spilled": {4: 1}})
+    # a's prompt again: all four blocks come from G3, staged into G2 by the workers
+    L.create_slot(KvbmRequest("c", prompt + [5]))
+    assert L.get_num_new_matched_tokens("c", 0) == (64, True)
+    L.update_state_after_alloc("c", [20, 21, 22, 23, 24], 64)
+    m4 = step(L, 5, {})
+    [st] = m4.stage
+    [ob] = m4.onboard
+    assert ob.g2_ids == st.g2_ids and ob.g1_ids == [20, 21, 22, 23]
+    assert g2.count_prefix(L.slots["c"].seq.sequence_hashes) == 0  # not matchable before the data lands
+    L.update_connector_output(finished_recving={"c"})
+    assert g2.count_prefix(L.slots["c"].seq.sequence_hashes) == 4
+    assert L.tier_stats["staged_from_g3"] == 4

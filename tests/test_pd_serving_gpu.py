@@ -196,3 +196,47 @@ def test_two_gpu_pd_tokens_equal_colocated():
     _, got, ref, stats = results["decode"]
     assert stats["received"] == 4 and stats["failed"] == 0
     assert got == ref
+
+
+def test_engine_g2_spill_to_g3_and_onboard_back(tmp_path):
+    """G2 capped below the working set: offloaded blocks chain to G3 on disk, G2 evicts
+    them, and the same prompt later comes back G3 -> G2 -> G1 (staged by the worker),
+    producing the same tokens."""
+    from kvbm_b200.connector.leader import ConnectorLeader
+    from kvbm_b200.connector.worker import ConnectorWorker
+    from kvbm_b200.engine.leader import InstanceLeader, ParallelWorkers
+    from kvbm_b200.logical.manager import BlockManager, Tier
+    from kvbm_b200.utils.config import KvbmConfig
+
+    cfg_m = LlamaConfig.tiny(layers=2)
+    model = LlamaModel(cfg_m, "cuda", seed=4)
+    kcfg = KvbmConfig.load({"cache": {"host": {"num_blocks": 5}, "disk": {"num_blocks": 32, "dir": str(tmp_path)}}},
+                           env={}, system_toml=None)
+    g2 = BlockManager(5, 16, "lru", Tier.G2)
+    g3 = BlockManager(32, 16, "lru", Tier.G3, registry=g2.registry)
+    leader = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([]), g3=g3), 16)
+    worker = ConnectorWorker(kcfg, block_size=16)
+    eng = LLMEngine(model, EngineConfig(num_gpu_blocks=40, max_num_seqs=2, max_model_len=256, max_tokens=4,
+                                        use_graphs=False), leader, worker)
+    worker.register_layout(eng.pool)
+    pa, px = _prompts(2, [88, 88], cfg_m.vocab, seed=3)
+
+    def run(req, idle=12):
+        eng.add_request(req)
+        while eng.has_unfinished() or eng._delayed:
+            eng.step()
+        torch.cuda.synchronize()
+        for _ in range(idle):  # offload reports, G3 chain, spill reports
+            eng.step()
+            torch.cuda.synchronize()
+
+    a = Request("a", pa, max_tokens=4)
+    run(a)
+    assert leader.tier_stats["spilled_to_g3"] == 5
+    run(Request("x", px, max_tokens=4))  # evicts a's blocks from G2
+    b = Request("b", pa, max_tokens=4)
+    run(b)
+    assert b.num_external_tokens == 80  # 5 blocks: staged from G3, onboarded to G1
+    assert leader.tier_stats["staged_from_g3"] == 5
+    assert torch.equal(a.output, b.output)
+    worker.shutdown()

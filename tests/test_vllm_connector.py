@@ -105,3 +105,22 @@ def test_preempted_request_is_fenced_and_resumes():
                           finished_req_ids=set(), preempted_req_ids=None)
     m3 = ConnectorMetadata.decode(conn.build_connector_meta(so3).metadata)
     assert [op.g1_ids for op in m3.offload] == [[32, 33, 34]]
+
+
+def test_pd_connector_validates_children_and_routes_handshakes():
+    from kvbm_b200.connector import pd
+    from kvbm_b200.connector import vllm_connector as vc
+
+    Role = vllm_base.KVConnectorRole
+    kvbm = vc.KvbmConnector(_vllm_config({"leader": {"cache": {"host": {"num_blocks": 8}}}}), Role.SCHEDULER)
+    with pytest.raises(ValueError, match="exactly two"):
+        pd.validate_children([kvbm])
+    with pytest.raises(TypeError, match="first connector"):
+        pd.validate_children([object(), kvbm])
+    with pytest.raises(TypeError, match="second connector to be NixlConnector"):
+        pd.validate_children([kvbm, object()])
+    H = pd.PdHandshakeMetadata
+    a, b, legacy = object(), object(), object()
+    kv, nx = pd.route_handshake({0: H(kvbm_metadata=a, nixl_metadata=b), 1: H(kvbm_metadata=None, nixl_metadata=b),
+                                 2: legacy}, H)
+    assert kv == {0: a} and nx == {0: b, 1: b, 2: legacy}

@@ -82,3 +82,34 @@ def test_noalloc_rejects_requests_beyond_its_capacity():
             torch.cuda.current_stream().cuda_stream)
     assert rc != 0
     assert b"exceeds the static scratch capacity" in msg()
+
+
+def test_noalloc_at_exactly_its_capacity():
+    """batch * hq * splits equal to the capacity: the partials fill the array to its last row."""
+    fn, cap, msg = _noalloc_symbol()
+    B, hkv, group, page = 2, 2, 4, 16
+    hq = hkv * group
+    splits = cap // (B * hq)
+    assert B * hq * splits == cap
+    seq_len = splits * page  # one block per split
+    g = torch.Generator(device="cuda").manual_seed(17)
+    nb = B * splits + 1
+    pool = KvLayout.allocate(LayoutConfig.for_model(nb, 1, hkv, 128, page), "fully_contiguous",
+                             KvBlockLayout.OPERATIONAL_NHD)
+    view = pool.layer_view(0)
+    view.copy_(torch.randn(view.shape, generator=g, device="cuda").to(torch.bfloat16))
+    table = torch.randperm(nb - 1, generator=g, device="cuda")[: B * splits].view(B, splits).to(torch.int32)
+    seq = torch.full((B,), seq_len, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, hq, 128, generator=g, device="cuda").to(torch.bfloat16)
+    kb = pool.layer_base(0)
+    vb = kb + pool.outer_stride
+    scale = 1.0 / math.sqrt(128)
+    ref = llama_ops.paged_decode_attn(q, kb, vb, pool.block_stride, pool.token_stride, pool.head_stride, page,
+                                      table, seq, hkv, scale, splits)
+    out = torch.full_like(q, float("nan"))
+    rc = fn(q.data_ptr(), kb, vb, pool.block_stride, pool.token_stride, pool.head_stride, page, table.data_ptr(),
+            table.shape[1], seq.data_ptr(), B, hq, hkv, 128, scale, splits, out.data_ptr(),
+            torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == 0, msg()
+    torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
