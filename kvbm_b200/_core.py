@@ -185,8 +185,15 @@ class ConnectorLeader:
                           duplicate_policy=cfg.cache.duplicate_policy)
         g3 = BlockManager(g3n, self.block_size, cfg.cache.inactive_backend, Tier.G3,
                           registry=g2.registry) if g3n else None
-        self._impl = _Leader(InstanceLeader(g2, ParallelWorkers([]), g3=g3), self.block_size,
-                             offload_enabled=layout.get("g2_blocks", 0) > 0)
+        # the registered workers (one per TP rank, each serving its shard) carry out the leader's own
+        # block operations; per-step ops reach them through the connector metadata
+        workers = ParallelWorkers([])
+        if self._workers:
+            from .engine.spmd import SpmdParallelWorkers
+
+            workers = SpmdParallelWorkers(self.runtime.messenger, [self._workers[r][0] for r in sorted(self._workers)])
+        self._impl = _Leader(InstanceLeader(g2, workers, g3=g3), self.block_size,
+                             offload_enabled=layout.get("g2_blocks", 0) > 0, num_workers=max(1, len(self._workers)))
 
     def _need(self) -> _Leader:
         if self._impl is None:
@@ -223,10 +230,33 @@ class ConnectorWorker:
                  head_size: int | None = None, rank: int = 0):
         from .connector.worker import ConnectorWorker as _Worker
 
-        self.runtime = runtime
+        self.runtime, self.rank = runtime, rank
         self._impl = _Worker(runtime.config, rank=rank, block_size=block_size, num_kv_heads=num_kv_heads,
                              head_size=head_size)
+        self._service = None
         runtime.messenger.register_handler(LAYOUT_HANDLER, lambda _p: self._impl.handshake_metadata())
+
+    def _serve(self):
+        """Once the KV caches are registered, serve this rank's block operations to the leader."""
+        from .engine.spmd import WorkerService
+
+        if self._service is None and self._impl.worker is not None:
+            self._service = WorkerService(self.runtime.messenger, self._impl.worker, self.rank)
+
+    def register_kv_caches(self, *a, **kw):
+        out = self._impl.register_kv_caches(*a, **kw)
+        self._serve()
+        return out
+
+    def register_cross_layers_kv_cache(self, *a, **kw):
+        out = self._impl.register_cross_layers_kv_cache(*a, **kw)
+        self._serve()
+        return out
+
+    def register_layout(self, layout):
+        out = self._impl.register_layout(layout)
+        self._serve()
+        return out
 
     def __getattr__(self, name):
         return getattr(self._impl, name)

@@ -127,6 +127,14 @@ class ConnectorWorker:
         nb = t.shape[labels.index(KvDim.BLOCK)]
         heads = t.shape[labels.index(KvDim.HEAD)]
         hd = t.shape[labels.index(KvDim.HEAD_SIZE)]
+        # backends may hand out a permuted view of a buffer allocated in another dimension order
+        # (a KV stride order): describe the memory in its physical order
+        perm = sorted(range(t.dim()), key=lambda i: (-t.stride(i), i))
+        if perm != list(range(t.dim())):
+            tensors = [x.permute(perm) for x in tensors]
+            labels = [labels[i] for i in perm]
+        if not all(x.is_contiguous() for x in tensors):
+            raise ValueError("KV tensors must be dense (in some dimension order)")
         self.g1 = layout_from_layer_tensors(tensors, labels, nb, self.block_size, heads, hd)
         self._build_worker()
         return self.g1

@@ -144,122 +144,209 @@ __device__ __forceinline__ float2 unpack_fp8x2(uint16_t x) {
   return __half22float2(h);
 }
 
-// Quantise a tile of 16-bit or f32 values to e4m3 with one fp32 scale per
-// tile (per block, layer, outer, head): scale = amax / 448, q = sat(x / scale).
-template <int KIND>
-__device__ __forceinline__ float unit_amax(const int4& v) {
-  if (KIND == kQuantF32) {
-    return fmaxf(fmaxf(fabsf(__int_as_float(v.x)), fabsf(__int_as_float(v.y))),
-                 fmaxf(fabsf(__int_as_float(v.z)), fabsf(__int_as_float(v.w))));
+// ---- fp8 e4m3 block scaling ------------------------------------------------
+//
+// One fp32 scale per tile (per block, layer, outer, head): scale = amax / 448,
+// q = satfinite_rn(x * (448 / amax)); x = q * scale on the way back. The
+// tile is read once: every lane keeps its share of the tile in registers
+// (8 x 16 bytes for a [16 x 128] 16-bit head tile), the warp reduces amax,
+// then each lane converts and stores. amax of 16-bit data is taken on the
+// raw bits: with the sign bit cleared, non-negative IEEE / bfloat16 values
+// order like unsigned integers, so a SIMD unsigned max over the packed
+// halves finds the largest magnitude without unpacking (NaN inputs are not
+// filtered). Unit index -> (row, column) uses shifts when the units per row
+// are a power of two (every head_dim the block manager uses).
+
+struct UnitMap {
+  FastDiv upr;
+  int shift;  // log2(units per row), or -1
+  __device__ __forceinline__ void rc(int u, int& r, int& c) const {
+    if (shift >= 0) {
+      r = u >> shift;
+      c = u & ((1 << shift) - 1);
+    } else {
+      r = static_cast<int>(upr.div(static_cast<uint32_t>(u)));
+      c = static_cast<int>(upr.mod(static_cast<uint32_t>(u), static_cast<uint32_t>(r)));
+    }
   }
-  float f[8];
-  unpack8_16bit(v, f, KIND == kQuantBf16);
-  float m = 0.f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(f[j]));
+};
+
+__device__ __forceinline__ UnitMap unit_map(const FastDiv& upr) {
+  UnitMap m{upr, -1};
+  if ((upr.d & (upr.d - 1)) == 0) m.shift = __ffs(static_cast<int>(upr.d)) - 1;
   return m;
 }
 
 template <int KIND>
-__device__ __forceinline__ void unit_quant_store(const int4& v, float inv, uint8_t* d) {
+__device__ __forceinline__ uint32_t unit_amax_bits(const int4& v) {
   if (KIND == kQuantF32) {
-    const uint16_t a = pack_fp8x2(__int_as_float(v.x) * inv, __int_as_float(v.y) * inv);
-    const uint16_t b = pack_fp8x2(__int_as_float(v.z) * inv, __int_as_float(v.w) * inv);
-    *reinterpret_cast<uint32_t*>(d) = (uint32_t)a | ((uint32_t)b << 16);
-  } else {
-    float f[8];
-    unpack8_16bit(v, f, KIND == kQuantBf16);
-    const uint32_t w0 =
-        (uint32_t)pack_fp8x2(f[0] * inv, f[1] * inv) | ((uint32_t)pack_fp8x2(f[2] * inv, f[3] * inv) << 16);
-    const uint32_t w1 =
-        (uint32_t)pack_fp8x2(f[4] * inv, f[5] * inv) | ((uint32_t)pack_fp8x2(f[6] * inv, f[7] * inv) << 16);
-    *reinterpret_cast<uint2*>(d) = make_uint2(w0, w1);
+    const uint32_t a = static_cast<uint32_t>(v.x) & 0x7fffffffu, b = static_cast<uint32_t>(v.y) & 0x7fffffffu;
+    const uint32_t c = static_cast<uint32_t>(v.z) & 0x7fffffffu, d = static_cast<uint32_t>(v.w) & 0x7fffffffu;
+    return max(max(a, b), max(c, d));
   }
+  const uint32_t m = 0x7fff7fffu;
+  const uint32_t a = __vmaxu2(static_cast<uint32_t>(v.x) & m, static_cast<uint32_t>(v.y) & m);
+  const uint32_t b = __vmaxu2(static_cast<uint32_t>(v.z) & m, static_cast<uint32_t>(v.w) & m);
+  return __vmaxu2(a, b);
 }
 
-// Quantise a tile of 16-bit or f32 values to e4m3 with one fp32 scale per
-// tile (per block, layer, outer, head): scale = amax / 448, q = sat(x / scale).
-// The first 8 units of each lane stay in registers; larger tiles re-read the
-// remainder (an L1/L2 hit) in the second pass.
+template <int KIND>
+__device__ __forceinline__ float amax_bits_to_float(uint32_t bits) {
+  if (KIND == kQuantF32) return __uint_as_float(bits);
+  const uint32_t h = max(bits & 0xffffu, bits >> 16);
+  if (KIND == kQuantBf16) return __uint_as_float(h << 16);
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+}
+
+// 16-byte source unit -> its fp8 bytes (8 for 16-bit sources, 4 for f32), as 32-bit words.
+template <int KIND>
+__device__ __forceinline__ void unit_to_fp8(const int4& v, float inv, uint32_t* out) {
+  const uint32_t w[4] = {(uint32_t)v.x, (uint32_t)v.y, (uint32_t)v.z, (uint32_t)v.w};
+  if (KIND == kQuantF32) {
+    const uint16_t a = pack_fp8x2(__uint_as_float(w[0]) * inv, __uint_as_float(w[1]) * inv);
+    const uint16_t b = pack_fp8x2(__uint_as_float(w[2]) * inv, __uint_as_float(w[3]) * inv);
+    out[0] = (uint32_t)a | ((uint32_t)b << 16);
+    return;
+  }
+  float f[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (KIND == kQuantBf16) {
+      f[2 * j] = __uint_as_float(w[j] << 16);
+      f[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    } else {
+      const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      f[2 * j] = p.x;
+      f[2 * j + 1] = p.y;
+    }
+  }
+  out[0] = (uint32_t)pack_fp8x2(f[0] * inv, f[1] * inv) | ((uint32_t)pack_fp8x2(f[2] * inv, f[3] * inv) << 16);
+  out[1] = (uint32_t)pack_fp8x2(f[4] * inv, f[5] * inv) | ((uint32_t)pack_fp8x2(f[6] * inv, f[7] * inv) << 16);
+}
+
+// Quantise one head tile. Lanes take pairs of adjacent 16-byte source units
+// (units per row are even for every head_dim that is a multiple of 16), so
+// 16-bit sources store 16 fp8 bytes per lane and pair.
 template <int KIND>
 __device__ __forceinline__ void tile_quant(const uint8_t* src, int64_t src_rs, uint8_t* dst, int64_t dst_rs,
                                            int rows, const FastDiv& upr, float* scale_out, int lane) {
-  constexpr int kElems = (KIND == kQuantF32) ? 4 : 8;  // elements per 16-byte source unit
-  constexpr int kOut = kElems;                          // fp8 bytes written per unit
-  constexpr int kCache = 8;
-  const int n = rows * static_cast<int>(upr.d);
-  int4 cache[kCache];
-  float amax = 0.f;
+  constexpr int kOut = (KIND == kQuantF32) ? 4 : 8;  // fp8 bytes per source unit
+  constexpr int kCache = 4;                           // pairs per lane kept in registers
+  const UnitMap um = unit_map(upr);
+  const int pairs = rows * static_cast<int>(upr.d) / 2;
+  int4 va[kCache], vb[kCache];
+  uint32_t mx = 0;
 #pragma unroll
   for (int k = 0; k < kCache; ++k) {
-    const int u = k * 32 + lane;
-    if (u < n) {
-      const int r = upr.div(u), c = upr.mod(u, r);
-      cache[k] = *reinterpret_cast<const int4*>(src + r * src_rs + c * 16);
-      amax = fmaxf(amax, unit_amax<KIND>(cache[k]));
+    const int q = k * 32 + lane;
+    if (q < pairs) {
+      int r, c;
+      um.rc(2 * q, r, c);
+      const int4* p = reinterpret_cast<const int4*>(src + r * src_rs + c * 16);
+      va[k] = p[0];
+      vb[k] = p[1];
     }
   }
-  for (int u = kCache * 32 + lane; u < n; u += 32) {
-    const int r = upr.div(u), c = upr.mod(u, r);
-    amax = fmaxf(amax, unit_amax<KIND>(*reinterpret_cast<const int4*>(src + r * src_rs + c * 16)));
+#pragma unroll
+  for (int k = 0; k < kCache; ++k) {
+    if (k * 32 + lane < pairs) mx = max(mx, max(unit_amax_bits<KIND>(va[k]), unit_amax_bits<KIND>(vb[k])));
   }
-  amax = warp_max(amax);
+  for (int q = kCache * 32 + lane; q < pairs; q += 32) {  // tiles larger than the register share
+    int r, c;
+    um.rc(2 * q, r, c);
+    const int4* p = reinterpret_cast<const int4*>(src + r * src_rs + c * 16);
+    mx = max(mx, max(unit_amax_bits<KIND>(p[0]), unit_amax_bits<KIND>(p[1])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float amax = amax_bits_to_float<KIND>(mx);
   const float scale = amax > 0.f ? amax / kE4M3Max : 1.0f;
   const float inv = amax > 0.f ? kE4M3Max / amax : 1.0f;
+  auto store_pair = [&](const int4& a, const int4& b, int q) {
+    int r, c;
+    um.rc(2 * q, r, c);
+    uint8_t* d = dst + r * dst_rs + c * kOut;
+    uint32_t w[4];
+    unit_to_fp8<KIND>(a, inv, w);
+    unit_to_fp8<KIND>(b, inv, w + kOut / 4);
+    if (KIND == kQuantF32) {
+      *reinterpret_cast<uint2*>(d) = make_uint2(w[0], w[1]);
+    } else {
+      *reinterpret_cast<int4*>(d) = make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]);
+    }
+  };
 #pragma unroll
   for (int k = 0; k < kCache; ++k) {
-    const int u = k * 32 + lane;
-    if (u < n) {
-      const int r = upr.div(u), c = upr.mod(u, r);
-      unit_quant_store<KIND>(cache[k], inv, dst + r * dst_rs + c * kOut);
-    }
+    const int q = k * 32 + lane;
+    if (q < pairs) store_pair(va[k], vb[k], q);
   }
-  for (int u = kCache * 32 + lane; u < n; u += 32) {
-    const int r = upr.div(u), c = upr.mod(u, r);
-    unit_quant_store<KIND>(*reinterpret_cast<const int4*>(src + r * src_rs + c * 16), inv, dst + r * dst_rs + c * kOut);
+  for (int q = kCache * 32 + lane; q < pairs; q += 32) {
+    int r, c;
+    um.rc(2 * q, r, c);
+    const int4* p = reinterpret_cast<const int4*>(src + r * src_rs + c * 16);
+    store_pair(p[0], p[1], q);
   }
   if (lane == 0 && scale_out != nullptr) *scale_out = scale;
 }
 
-// Dequantise an e4m3 tile into 16-bit or f32 values: x = q * scale.
+// Dequantise an e4m3 tile into 16-bit or f32 values: x = q * scale. All of a
+// lane's loads are issued before its first conversion.
 template <int KIND>
 __device__ __forceinline__ void tile_dequant(const uint8_t* src, int64_t src_rs, uint8_t* dst, int64_t dst_rs,
                                              int rows, const FastDiv& upr, const float* scale_in, int lane) {
   const float scale = scale_in ? *scale_in : 1.0f;
+  const UnitMap um = unit_map(upr);
   const int n = rows * static_cast<int>(upr.d);  // 16 fp8 per source unit
-  for (int u = lane; u < n; u += 32) {
-    const int r = upr.div(u), c = upr.mod(u, r);
-    const int4 v = *reinterpret_cast<const int4*>(src + r * src_rs + c * 16);
-    const uint32_t w[4] = {(uint32_t)v.x, (uint32_t)v.y, (uint32_t)v.z, (uint32_t)v.w};
-    float f[16];
+  constexpr int kBatch = 4;
+  for (int base = 0; base < n; base += 32 * kBatch) {
+    int4 v[kBatch];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 a = unpack_fp8x2(static_cast<uint16_t>(w[j] & 0xffffu));
-      const float2 b = unpack_fp8x2(static_cast<uint16_t>(w[j] >> 16));
-      f[4 * j + 0] = a.x * scale;
-      f[4 * j + 1] = a.y * scale;
-      f[4 * j + 2] = b.x * scale;
-      f[4 * j + 3] = b.y * scale;
-    }
-    uint8_t* d = dst + r * dst_rs;
-    if (KIND == kDequantF32) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        *reinterpret_cast<float4*>(d + c * 64 + q * 16) = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
-    } else {
-      uint32_t o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (KIND == kDequantBf16) {
-          __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
-          o[j] = *reinterpret_cast<uint32_t*>(&b);
-        } else {
-          __half2 h = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
-          o[j] = *reinterpret_cast<uint32_t*>(&h);
-        }
+    for (int k = 0; k < kBatch; ++k) {
+      const int u = base + k * 32 + lane;
+      if (u < n) {
+        int r, c;
+        um.rc(u, r, c);
+        v[k] = *reinterpret_cast<const int4*>(src + r * src_rs + c * 16);
       }
-      *reinterpret_cast<int4*>(d + c * 32) = make_int4(o[0], o[1], o[2], o[3]);
-      *reinterpret_cast<int4*>(d + c * 32 + 16) = make_int4(o[4], o[5], o[6], o[7]);
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int u = base + k * 32 + lane;
+      if (u >= n) continue;
+      int r, c;
+      um.rc(u, r, c);
+      const uint32_t w[4] = {(uint32_t)v[k].x, (uint32_t)v[k].y, (uint32_t)v[k].z, (uint32_t)v[k].w};
+      float f[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = unpack_fp8x2(static_cast<uint16_t>(w[j] & 0xffffu));
+        const float2 b = unpack_fp8x2(static_cast<uint16_t>(w[j] >> 16));
+        f[4 * j + 0] = a.x * scale;
+        f[4 * j + 1] = a.y * scale;
+        f[4 * j + 2] = b.x * scale;
+        f[4 * j + 3] = b.y * scale;
+      }
+      uint8_t* d = dst + r * dst_rs;
+      if (KIND == kDequantF32) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<float4*>(d + c * 64 + q * 16) =
+              make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+      } else {
+        uint32_t o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (KIND == kDequantBf16) {
+            __nv_bfloat162 bb = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+            o[j] = *reinterpret_cast<uint32_t*>(&bb);
+          } else {
+            __half2 hh = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+            o[j] = *reinterpret_cast<uint32_t*>(&hh);
+          }
+        }
+        *reinterpret_cast<int4*>(d + c * 32) = make_int4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<int4*>(d + c * 32 + 16) = make_int4(o[4], o[5], o[6], o[7]);
+      }
     }
   }
 }
@@ -284,7 +371,7 @@ __device__ __forceinline__ void run_tile(const XferParams& P, const uint8_t* s, 
 // Warp-per-tile kernel. Tiles are ordered (pair, layer, outer, head) with
 // head fastest so the warps of one CTA sweep one contiguous chunk together.
 template <int KIND, int U>
-__global__ void __launch_bounds__(kThreads) kv_tile_xfer_kernel(const __grid_constant__ XferParams P) {
+__global__ void __launch_bounds__(kThreads, KIND == kCopy ? 1 : 4) kv_tile_xfer_kernel(const __grid_constant__ XferParams P) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerCta;
