@@ -18,9 +18,10 @@ host mailbox; the decode connector reports the request received and the
 engine decodes it (first step: the last prompt token, recomputed).
 
 A step is one wave: ``concurrency`` requests of ``prompt_len`` uniform-random
-tokens per pair, each generating ``gen_len`` tokens. The next wave is
-submitted once the current one has been received (prefill of k+1 overlaps
-decode of k). Weights are random-init bf16.
+tokens per pair, each generating ``gen_len`` tokens. With separate prefill
+and decode GPUs the next wave is submitted once the current one has been
+received (prefill of k+1 overlaps decode of k); colocated, waves run one
+after another. Weights are random-init bf16.
 
 Reported (rank 0, one JSON line):
   value   aggregate P->D KV transfer GB/s: KV bytes pushed by all prefill
@@ -210,8 +211,11 @@ def main(argv=None) -> int:
                 while pre.engine.has_unfinished():
                     pre.step()
             dec.step()
-            if k + 1 < total and k + 1 != args.warmup and k + 1 not in submitted and wave_received(k):
-                submit(k + 1)  # the next wave's prefill overlaps this wave's decode (not across the timed edge)
+            if (role == "decode" and k + 1 < total and k + 1 != args.warmup and k + 1 not in submitted
+                    and wave_received(k)):
+                # the next wave's prefill (on the prefill GPU) overlaps this wave's decode; not across the
+                # timed edge, and not when both share one GPU (colocated: waves run one after another)
+                submit(k + 1)
 
     timed: list[Request] = []
     for k in range(args.warmup):

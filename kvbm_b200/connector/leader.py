@@ -87,6 +87,7 @@ class PushState:
     seq: int
     cursor: int               # next block index to push
     in_flight: bool = False   # the final push was issued and has not been reported done
+    peer_tp: int = 1          # the decode instance's TP degree
 
 
 @dataclass
@@ -140,7 +141,8 @@ class ConnectorLeader:
                  decode_offload: bool = False, stats: CacheStatsTracker | None = None, remote_search=None,
                  cd: ConditionalDisagg | None = None, plane=None, prefill_target=None, instance_id: int = 0,
                  mailbox_slots: int = 0, recv_timeout_s: float = 120.0, num_workers: int = 1,
-                 g2_policy: OffloadPolicy | None = None, g3_policy: OffloadPolicy | None = None):
+                 g2_policy: OffloadPolicy | None = None, g3_policy: OffloadPolicy | None = None,
+                 tp_size: int = 1, directory=None):
         self.leader = leader
         self.remote = remote_search  # engine.remote_search.RemoteSearch, or None
         self.block_size = block_size
@@ -158,6 +160,8 @@ class ConnectorLeader:
         self._mailbox_free = deque(range(mailbox_slots))
         self._seq = itertools.count(1)
         self.num_workers = num_workers
+        self.tp_size = tp_size          # this instance's TP degree (decode side: its ranks' head shards)
+        self.directory = directory      # where prefill instances publish their TP degree
         # step -> (G2 mutables awaiting their copies, their hashes, worker reports so far)
         self._pending_g2: dict[int, tuple[list[MutableBlock], list[int], int]] = {}
         # G1 -> G2 and G2 -> G3 admission policies (the offload pipelines' filters)
@@ -182,7 +186,7 @@ class ConnectorLeader:
                 # prefill accept: this instance computes the prompt and pushes it to the decode instance
                 pb = int(remote["provided_blocks"])
                 slot.push = PushState(int(remote["instance"]), list(remote["dst_ids"]), pb, int(remote["slot"]),
-                                      int(remote["seq"]), pb)
+                                      int(remote["seq"]), pb, peer_tp=int(remote.get("tp", 1)))
                 audit("cd_prefill_accept", request=request.request_id, peer=slot.push.peer,
                       blocks=len(slot.push.dst_ids))
         return slot
@@ -355,14 +359,22 @@ class ConnectorLeader:
         rp.params.num_provided_tokens = provided_blocks * bs
         dst = slot.g1_block_ids[provided_blocks:prompt_blocks]
         decode = {"instance": self.instance_id, "dst_ids": dst, "slot": rp.slot, "seq": rp.seq,
-                  "provided_blocks": provided_blocks}
+                  "provided_blocks": provided_blocks, "tp": self.tp_size}
         self.plane.dispatch(rp.target, encode_dispatch(req.request_id, slot.seq.tokens, rp.params.to_dict(), decode,
                                                       salt=req.salt, lora=req.lora_name))
         rp.dispatched = True
         self.cd_stats["dispatched"] += 1
-        self._recv_ops.append(RecvOp(req.request_id, rp.slot, rp.seq, dst, self.recv_timeout_s))
+        self._recv_ops.append(RecvOp(req.request_id, rp.slot, rp.seq, dst, self.recv_timeout_s,
+                                     self._contributors(rp.target)))
         audit("cd_dispatch", request=req.request_id, target=rp.target, provided_blocks=provided_blocks,
               blocks=len(dst), seq=rp.seq)
+
+    def _contributors(self, prefill_instance: int) -> int:
+        """Prefill ranks whose pushes fill one of this instance's rank shards."""
+        if self.directory is None:
+            return 1
+        ptp = int(self.directory.lookup(prefill_instance).get("tp", 1))
+        return max(1, ptp // self.tp_size)
 
     # ------------------------------------------------------ metadata build
     def build_connector_meta(self, out: SchedulerOutputLite) -> bytes:
@@ -449,7 +461,7 @@ class ConnectorLeader:
         src = slot.g1_block_ids[ps.cursor: upto]
         dst = ps.dst_ids[ps.cursor - ps.provided_blocks: upto - ps.provided_blocks]
         final = upto >= prompt_blocks
-        meta.push.append(PushOp(slot.request.request_id, ps.peer, src, dst, ps.slot, ps.seq, final))
+        meta.push.append(PushOp(slot.request.request_id, ps.peer, src, dst, ps.slot, ps.seq, final, ps.peer_tp))
         ps.cursor = upto
         ps.in_flight = ps.in_flight or final
         self.cd_stats["pushed_blocks"] += len(src)

@@ -7,8 +7,8 @@ One msgpack map per scheduler step::
      "offload": [[req_id, g1_ids, g2_ids], ...],      # G1 -> G2 after the pass
      "stage":   [[req_id, g3_ids, g2_ids], ...],      # G3 -> G2 before the onboards
      "spill":   [[g2_ids, g3_ids], ...],              # G2 -> G3 after the offloads
-     "push":    [[req_id, peer, src, dst, slot, seq, final], ...],
-     "recv":    [[req_id, slot, seq, g1_ids, timeout_s], ...],
+     "push":    [[req_id, peer, src, dst, slot, seq, final, peer_tp], ...],
+     "recv":    [[req_id, slot, seq, g1_ids, timeout_s, contributors], ...],
      "evict":   [req_id, ...]}
 
 ``push`` / ``recv`` carry conditional disaggregation: a prefill worker
@@ -73,6 +73,7 @@ class PushOp:
     slot: int
     seq: int
     final: bool
+    peer_tp: int = 1          # TP degree of the decode instance (its ranks hold head shards)
 
 
 @dataclass
@@ -84,6 +85,7 @@ class RecvOp:
     seq: int
     g1_ids: list[int]
     timeout_s: float = 60.0
+    contributors: int = 1     # prefill ranks whose pushes fill one decode rank's shard
 
 
 @dataclass
@@ -105,8 +107,9 @@ class ConnectorMetadata:
             "evict": self.evict,
             "stage": [[o.req_id, o.g3_ids, o.g2_ids] for o in self.stage],
             "spill": [[o.g2_ids, o.g3_ids] for o in self.spill],
-            "push": [[o.req_id, o.peer, o.src_ids, o.dst_ids, o.slot, o.seq, o.final] for o in self.push],
-            "recv": [[o.req_id, o.slot, o.seq, o.g1_ids, o.timeout_s] for o in self.recv],
+            "push": [[o.req_id, o.peer, o.src_ids, o.dst_ids, o.slot, o.seq, o.final, o.peer_tp]
+                     for o in self.push],
+            "recv": [[o.req_id, o.slot, o.seq, o.g1_ids, o.timeout_s, o.contributors] for o in self.recv],
         }, use_bin_type=True)
 
     @classmethod

@@ -106,7 +106,8 @@ class ConnectorWorker:
         self.directory = None
         self.mailbox = None
         self._peers: dict[int, PeerConnection] = {}
-        self._pushes: list[tuple[PushOp, PeerConnection, torch.Tensor, torch.Tensor]] = []
+        self._pushes: list[tuple[PushOp, list, torch.Tensor, torch.Tensor]] = []
+        self.tp_rank, self.tp_size = 0, 1
         self._recvs: dict[str, tuple] = {}
         self.push_timing = False
         self._push_timers: list[tuple[torch.cuda.Event, torch.cuda.Event, int]] = []
@@ -186,34 +187,59 @@ class ConnectorWorker:
 
     # ------------------------------------------- conditional disaggregation
     def enable_disagg(self, instance_id: int, directory, mailbox_slots: int = 0, shared: bool = False,
-                      timing: bool = False) -> None:
-        """Join the node's P/D deployment as instance ``instance_id``.
+                      timing: bool = False, tp_rank: int = 0, tp_size: int = 1) -> None:
+        """Join the node's P/D deployment as rank ``tp_rank`` of instance ``instance_id``.
 
         With ``mailbox_slots`` this worker can receive remote prefills: it
         allocates the host mailbox (a named shared-memory file when
-        ``shared``, so prefill workers in other processes map it) and
-        publishes its G1 pool and mailbox in ``directory``. Every worker can
-        push (prefill side). ``timing`` brackets each push launch with CUDA
-        events (``take_push_timings``).
+        ``shared``, so prefill workers in other processes map it). Every
+        worker publishes its G1 pool (its KV-head shard with tensor
+        parallelism), its mailbox and its instance's TP degree in
+        ``directory`` and can push (prefill side). ``timing`` brackets each
+        push launch with CUDA events (``take_push_timings``).
         """
         from ..parallel.pd import HostMailbox
 
         self.instance_id, self.directory, self.push_timing = int(instance_id), directory, timing
+        self.tp_rank, self.tp_size = int(tp_rank), int(tp_size)
+        info = {"device": self.device, "rank": self.tp_rank, "tp": self.tp_size,
+                "heads": self.g1.config.num_heads * self.tp_size}
         if mailbox_slots:
-            name = f"kvbm_mb_{self.instance_id:x}_{self.rank}" if shared else None
+            name = f"kvbm_mb_{self.instance_id:x}_{self.tp_rank}" if shared else None
             self.mailbox = HostMailbox(mailbox_slots, name=name)
-            info = {"mailbox": self.mailbox.descriptor(), "device": self.device, "rank": self.rank}
+            info["mailbox"] = self.mailbox.descriptor()
             if shared:
                 info["pool"] = self.g1.descriptor().to_dict()
             else:
                 info.update(pool_obj=self.g1, mailbox_obj=self.mailbox)
-            directory.publish(self.instance_id, info)
+        directory.publish(self.instance_id, info, rank=self.tp_rank)
 
-    def _peer(self, instance: int) -> PeerConnection:
-        conn = self._peers.get(instance)
+    def _peer(self, instance: int, rank: int = 0) -> PeerConnection:
+        conn = self._peers.get((instance, rank))
         if conn is None:
-            conn = self._peers[instance] = PeerConnection(self.directory.lookup(instance), self.device)
+            conn = self._peers[(instance, rank)] = PeerConnection(self.directory.lookup(instance, rank=rank),
+                                                                  self.device)
         return conn
+
+    def _targets(self, peer_tp: int):
+        """(decode rank, src head offset, dst head offset, heads, contributor index) for this rank's shard."""
+        from ..parallel.tp import ParallelismTemplate, plan_pull, plan_push
+
+        key = (self.tp_size, peer_tp)
+        got = getattr(self, "_target_cache", {}).get(key)
+        if got is not None:
+            return got
+        c = self.g1.config
+        G = c.num_heads * self.tp_size
+        src = ParallelismTemplate(self.tp_size, G, c.num_layers, c.head_dim, c.page_size)
+        dst = ParallelismTemplate(peer_tp, G, c.num_layers, c.head_dim, c.page_size)
+        pulls = plan_pull(dst, src)
+        out = []
+        for t in plan_push(src, dst)[self.tp_rank]:
+            contrib = [sh.remote_rank for sh in pulls[t.dst_rank].shards].index(self.tp_rank)
+            out.append((t.dst_rank, t.src_head_offset, t.dst_head_offset, t.num_heads, contrib))
+        self.__dict__.setdefault("_target_cache", {})[key] = out
+        return out
 
     def take_onboard_timings(self) -> tuple[float, int]:
         """(summed device ms of the steps' G2 -> G1 onboards, bytes onboarded) since the last call; waits."""
@@ -250,7 +276,8 @@ class ConnectorWorker:
             for op in self._meta.push:
                 ids = torch.tensor(op.src_ids + op.dst_ids, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
                 n = len(op.src_ids)
-                self._pushes.append((op, self._peer(op.peer), ids[:n], ids[n:]))
+                targets = [(self._peer(op.peer, d), so, do, nh, cb) for d, so, do, nh, cb in self._targets(op.peer_tp)]
+                self._pushes.append((op, targets, ids[:n], ids[n:]))
 
     def clear_connector_metadata(self) -> None:
         self._meta = None
@@ -330,18 +357,21 @@ class ConnectorWorker:
         st = torch.cuda.current_stream(self.device)
         from ..ops import kv_ops
 
-        for op, conn, src, dst in self._pushes:
+        for op, targets, src, dst in self._pushes:
             if requests is not None and op.req_id not in requests:
                 continue
-            if self.push_timing:
-                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                s.record(st)
-            kv_ops.kv_transfer(self.g1, src, conn.pool, dst, layer_begin=first, num_layers=layer + 1 - first,
-                               engine=self.push_engine, stream=st)
-            if self.push_timing:
-                e.record(st)
-                self._push_timers.append((s, e, len(op.src_ids) * (layer + 1 - first) * self.g1.config.outer_dim
-                                          * self.g1.config.bytes_per_chunk))
+            for conn, so, do, nh, _ in targets:
+                if self.push_timing:
+                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s.record(st)
+                kv_ops.kv_transfer(self.g1, src, conn.pool, dst, layer_begin=first, num_layers=layer + 1 - first,
+                                   src_head_offset=so, dst_head_offset=do, num_heads=nh, engine=self.push_engine,
+                                   stream=st)
+                if self.push_timing:
+                    e.record(st)
+                    c = self.g1.config
+                    self._push_timers.append((s, e, len(op.src_ids) * (layer + 1 - first) * c.outer_dim
+                                              * c.bytes_per_chunk * nh // c.num_heads))
 
     def wait_for_save(self) -> None:
         meta = self._meta
@@ -350,10 +380,11 @@ class ConnectorWorker:
         from ..ops import kv_ops
 
         st = torch.cuda.current_stream(self.device)
-        for op, conn, _, _ in self._pushes:
+        for op, targets, _, _ in self._pushes:
             if op.final:
                 # behind the request's last push in stream order: the decode side may read its blocks
-                kv_ops.signal_flag(conn.mailbox.flag_ptr(op.slot), op.seq, stream=st)
+                for conn, _, _, _, cb in targets:
+                    kv_ops.signal_flag(conn.mailbox.flag_ptr(op.slot, cb), op.seq, stream=st)
                 ev = torch.cuda.Event()
                 ev.record(st)
                 self._send_events.setdefault(op.req_id, []).append(ev)
@@ -386,7 +417,7 @@ class ConnectorWorker:
             for r, (op, deadline) in list(self._recvs.items()):
                 if r in self._recv_events:
                     continue  # its local onboard part is still running
-                if self.mailbox is not None and self.mailbox.value(op.slot) == op.seq:
+                if self.mailbox is not None and self.mailbox.landed(op.slot, op.seq, op.contributors):
                     recving.add(r)
                     del self._recvs[r]
                 elif now > deadline:

@@ -117,23 +117,6 @@ __device__ __forceinline__ void tile_copy(const uint8_t* src, int64_t src_rs, ui
   }
 }
 
-__device__ __forceinline__ void unpack8_16bit(const int4& v, float* f, bool bf16) {
-  const uint32_t w[4] = {(uint32_t)v.x, (uint32_t)v.y, (uint32_t)v.z, (uint32_t)v.w};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float2 p;
-    if (bf16) {
-      __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
-      p = __bfloat1622float2(b);
-    } else {
-      __half2 h = *reinterpret_cast<const __half2*>(&w[j]);
-      p = __half22float2(h);
-    }
-    f[2 * j] = p.x;
-    f[2 * j + 1] = p.y;
-  }
-}
-
 __device__ __forceinline__ uint16_t pack_fp8x2(float a, float b) {
   return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
 }
@@ -188,6 +171,13 @@ __device__ __forceinline__ uint32_t unit_amax_bits(const int4& v) {
   const uint32_t a = __vmaxu2(static_cast<uint32_t>(v.x) & m, static_cast<uint32_t>(v.y) & m);
   const uint32_t b = __vmaxu2(static_cast<uint32_t>(v.z) & m, static_cast<uint32_t>(v.w) & m);
   return __vmaxu2(a, b);
+}
+
+// Combine two amax words: per 16-bit half for 16-bit data (the halves are
+// independent maxima until the very end), as one value for f32.
+template <int KIND>
+__device__ __forceinline__ uint32_t amax_combine(uint32_t a, uint32_t b) {
+  return KIND == kQuantF32 ? max(a, b) : __vmaxu2(a, b);
 }
 
 template <int KIND>
@@ -249,16 +239,17 @@ __device__ __forceinline__ void tile_quant(const uint8_t* src, int64_t src_rs, u
   }
 #pragma unroll
   for (int k = 0; k < kCache; ++k) {
-    if (k * 32 + lane < pairs) mx = max(mx, max(unit_amax_bits<KIND>(va[k]), unit_amax_bits<KIND>(vb[k])));
+    if (k * 32 + lane < pairs)
+      mx = amax_combine<KIND>(mx, amax_combine<KIND>(unit_amax_bits<KIND>(va[k]), unit_amax_bits<KIND>(vb[k])));
   }
   for (int q = kCache * 32 + lane; q < pairs; q += 32) {  // tiles larger than the register share
     int r, c;
     um.rc(2 * q, r, c);
     const int4* p = reinterpret_cast<const int4*>(src + r * src_rs + c * 16);
-    mx = max(mx, max(unit_amax_bits<KIND>(p[0]), unit_amax_bits<KIND>(p[1])));
+    mx = amax_combine<KIND>(mx, amax_combine<KIND>(unit_amax_bits<KIND>(p[0]), unit_amax_bits<KIND>(p[1])));
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  for (int o = 16; o > 0; o >>= 1) mx = amax_combine<KIND>(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   const float amax = amax_bits_to_float<KIND>(mx);
   const float scale = amax > 0.f ? amax / kE4M3Max : 1.0f;
   const float inv = amax > 0.f ? kE4M3Max / amax : 1.0f;
@@ -645,6 +636,27 @@ struct PipeParams {
   uint64_t wait_ns;         // limit of every pipeline wait
 };
 
+// This CTA's contiguous range of chunks. Chunks are ordered (pair, layer,
+// outer), so a contiguous range walks one block's layers before the next
+// block's: each CTA touches a few memory pages at a time on both sides
+// (fewer address-translation misses than a grid-strided walk over pools
+// that span tens of GiB).
+__device__ __forceinline__ void cta_chunks(int64_t total, int64_t& begin, int64_t& count) {
+  const int64_t G = gridDim.x, b = blockIdx.x;
+  const int64_t per = total / G, rem = total % G;
+  count = per + (b < rem ? 1 : 0);
+  begin = b * per + (b < rem ? b : rem);
+}
+
+// A pipeline wait bounded by `limit_ns`. A limit of 1 ns or less gives up at
+// once, before the first try (mbarrier.try_wait may itself block for a while,
+// so a tiny limit alone would not make the give-up path run reliably): the
+// test hook that exercises the timeout path without any fault.
+__device__ __forceinline__ bool pipe_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (limit_ns <= 1) return false;
+  return mbar_wait_bounded(bar, parity, limit_ns);
+}
+
 template <int KIND>
 __global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __grid_constant__ PipeParams Q) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -676,10 +688,13 @@ __global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __
     if (lane == 0) {
       int64_t k = 0;
       bool ok = true;
-      for (int64_t c = blockIdx.x; c < Q.total_chunks && ok; c += gridDim.x, ++k) {
+      int64_t begin, count;
+      cta_chunks(Q.total_chunks, begin, count);
+      for (; k < count && ok; ++k) {
+        const int64_t c = begin + k;
         const int s = static_cast<int>(k % Q.stages);
         const uint32_t phase = static_cast<uint32_t>((k / Q.stages) & 1);
-        if (k >= Q.stages && !mbar_wait_bounded(&empty_bar[s], phase ^ 1u, Q.wait_ns)) {
+        if (k >= Q.stages && !pipe_wait(&empty_bar[s], phase ^ 1u, Q.wait_ns)) {
           ok = false;
           break;
         }
@@ -722,12 +737,13 @@ __global__ void __launch_bounds__(kPipeThreads, 1) kv_chunk_pipe_kernel(const __
   // ---------------- consumers ----------------
   const int group = warp / wc, gw = warp - group * wc;
   if (group >= groups) return;  // H does not divide the consumer warps: the remainder idles
-  int64_t k = group;
-  for (int64_t c = blockIdx.x + static_cast<int64_t>(group) * gridDim.x; c < Q.total_chunks;
-       c += static_cast<int64_t>(groups) * gridDim.x, k += groups) {
+  int64_t begin, count;
+  cta_chunks(Q.total_chunks, begin, count);
+  for (int64_t k = group; k < count; k += groups) {
+    const int64_t c = begin + k;
     const int s = static_cast<int>(k % Q.stages);
     const uint32_t phase = static_cast<uint32_t>((k / Q.stages) & 1);
-    if (!mbar_wait_bounded(&full_bar[s], phase, Q.wait_ns)) {
+    if (!pipe_wait(&full_bar[s], phase, Q.wait_ns)) {
       if (lane == 0) report_status(Q.status, kStatusPipelineTimeout);
       break;
     }
@@ -796,13 +812,13 @@ __global__ void __launch_bounds__(32, 1) kv_bulk_copy_kernel(const __grid_consta
   const int S = Q.stages;
   for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
   fence_mbar_init();
-  const int64_t G = gridDim.x;
-  const int64_t n = Q.total_chunks > blockIdx.x ? (Q.total_chunks - blockIdx.x + G - 1) / G : 0;
+  int64_t begin, n;
+  cta_chunks(Q.total_chunks, begin, n);
   const uint32_t bytes = static_cast<uint32_t>(Q.chunk_bytes);
-  int64_t issued = 0;  // loads issued so far (chunk j of this CTA = blockIdx.x + j * G)
+  int64_t issued = 0;  // loads issued so far (chunk j of this CTA = begin + j)
   bool ok = true;
   auto load = [&](int64_t j) -> bool {
-    const uint8_t* src = src_chunk(P, blockIdx.x + j * G);
+    const uint8_t* src = src_chunk(P, begin + j);
     if ((reinterpret_cast<uintptr_t>(src) & 15) != 0) return false;
     const int s = static_cast<int>(j % S);
     mbar_arrive_expect_tx(&full[s], bytes);
@@ -819,12 +835,12 @@ __global__ void __launch_bounds__(32, 1) kv_bulk_copy_kernel(const __grid_consta
   int64_t j = 0;
   for (; ok && j < n; ++j) {
     const int s = static_cast<int>(j % S);
-    if (!mbar_wait_bounded(&full[s], static_cast<uint32_t>((j / S) & 1), Q.wait_ns)) {
+    if (!pipe_wait(&full[s], static_cast<uint32_t>((j / S) & 1), Q.wait_ns)) {
       report_status(Q.status, kStatusPipelineTimeout);
       ok = false;
       break;
     }
-    uint8_t* dst = dst_chunk(P, blockIdx.x + j * G);
+    uint8_t* dst = dst_chunk(P, begin + j);
     if ((reinterpret_cast<uintptr_t>(dst) & 15) != 0) {
       report_status(Q.status, kStatusBadIndex);
       ok = false;

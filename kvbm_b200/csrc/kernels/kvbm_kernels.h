@@ -105,8 +105,9 @@ int kvbm_kv_xfer(const KvbmSide* src, const KvbmSide* dst, const KvbmTileShape* 
 int kvbm_xfer_status(int device, int reset);
 
 // Test hook: the limit of the TMA engines' pipeline waits for launches made
-// after the call (0 restores the default of 2 s). Waits that drain copies
-// already issued keep the full limit.
+// after the call (0 restores the default of 2 s; 1 makes every pipeline wait
+// give up at once). Waits that drain copies already issued keep the full
+// limit, so no copy is in flight when a CTA exits.
 void kvbm_xfer_set_wait_limit_ns(uint64_t ns);
 
 // Split-by-bytes batched copy of num_pairs (src, dst) regions of equal size.

@@ -141,12 +141,13 @@ class HubPrefillPlane(PrefillPlane):
 
 
 class PeerDirectory:
-    """Where each decode instance's G1 pool and mailbox can be found."""
+    """Where each instance's G1 pool and mailbox can be found, per TP rank (a
+    tensor-parallel instance publishes one entry per rank: its KV shard)."""
 
-    def publish(self, instance: int, info: dict) -> None:
+    def publish(self, instance: int, info: dict, rank: int = 0) -> None:
         raise NotImplementedError
 
-    def lookup(self, instance: int, timeout_s: float = 60.0) -> dict:
+    def lookup(self, instance: int, timeout_s: float = 60.0, rank: int = 0) -> dict:
         raise NotImplementedError
 
 
@@ -154,30 +155,31 @@ class LocalPeerDirectory(PeerDirectory):
     """In-process: ``info`` may hold the live objects (``pool_obj``, ``mailbox_obj``)."""
 
     def __init__(self):
-        self._d: dict[int, dict] = {}
+        self._d: dict[tuple[int, int], dict] = {}
         self._cv = threading.Condition()
 
-    def publish(self, instance, info):
+    def publish(self, instance, info, rank=0):
         with self._cv:
-            self._d[int(instance)] = info
+            self._d[(int(instance), int(rank))] = info
             self._cv.notify_all()
 
-    def lookup(self, instance, timeout_s=60.0):
+    def lookup(self, instance, timeout_s=60.0, rank=0):
+        key = (int(instance), int(rank))
         with self._cv:
-            if not self._cv.wait_for(lambda: int(instance) in self._d, timeout=timeout_s):
-                raise TimeoutError(f"instance {instance} never published its pool")
-            return self._d[int(instance)]
+            if not self._cv.wait_for(lambda: key in self._d, timeout=timeout_s):
+                raise TimeoutError(f"instance {instance} rank {rank} never published its pool")
+            return self._d[key]
 
 
 class StorePeerDirectory(PeerDirectory):
     def __init__(self, store, prefix: str = "kvbm/cd/peer"):
         self.store, self.prefix = store, prefix
 
-    def publish(self, instance, info):
-        self.store.set(f"{self.prefix}/{int(instance)}", msgpack.packb(info, use_bin_type=True))
+    def publish(self, instance, info, rank=0):
+        self.store.set(f"{self.prefix}/{int(instance)}/{int(rank)}", msgpack.packb(info, use_bin_type=True))
 
-    def lookup(self, instance, timeout_s=60.0):
-        key = f"{self.prefix}/{int(instance)}"
+    def lookup(self, instance, timeout_s=60.0, rank=0):
+        key = f"{self.prefix}/{int(instance)}/{int(rank)}"
         deadline = time.monotonic() + timeout_s
         while not self.store.check([key]):
             if time.monotonic() >= deadline:

@@ -117,14 +117,32 @@ class KvPush:
 
 
 class LlamaModel:
-    """Weights + forward passes. Not an nn.Module: no autograd, inference only."""
+    """Weights + forward passes. Not an nn.Module: no autograd, inference only.
+
+    With ``tp_size`` > 1 the model is this rank's tensor-parallel shard:
+    ``heads / tp`` query heads and ``kv_heads / tp`` KV heads (the rank's KV
+    pool holds only those), ``intermediate / tp`` FFN columns; the attention
+    output and FFN down projections are row-parallel and summed over
+    ``tp_group`` with an all-reduce (NCCL). ``self.cfg`` is the shard's
+    geometry, ``self.full_cfg`` the model's. Weights are random per shard
+    (seeded by ``seed`` and the rank).
+    """
 
     def __init__(self, cfg: LlamaConfig, device: torch.device | str = "cuda", seed: int = 0,
-                 dtype: torch.dtype = torch.bfloat16):
+                 dtype: torch.dtype = torch.bfloat16, tp_rank: int = 0, tp_size: int = 1, tp_group=None):
+        if cfg.heads % tp_size or cfg.kv_heads % tp_size or cfg.intermediate % tp_size:
+            raise ValueError(f"tp_size {tp_size} must divide heads, kv_heads and intermediate")
+        self.full_cfg = cfg
+        self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
+        if tp_size > 1:
+            from dataclasses import replace
+
+            cfg = replace(cfg, heads=cfg.heads // tp_size, kv_heads=cfg.kv_heads // tp_size,
+                          intermediate=cfg.intermediate // tp_size)
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype
-        g = torch.Generator(device=self.device).manual_seed(seed)
+        g = torch.Generator(device=self.device).manual_seed(seed + 7919 * tp_rank)
         std = 0.02
 
         def w(*shape, scale=std):
@@ -133,7 +151,12 @@ class LlamaModel:
             return t
 
         c = cfg
-        self.embed = w(c.vocab, c.hidden)
+        if tp_size > 1:  # replicated tensors are identical on every rank
+            g_rep = torch.Generator(device=self.device).manual_seed(seed)
+            self.embed = torch.empty(c.vocab, c.hidden, device=self.device, dtype=dtype).normal_(0.0, std,
+                                                                                              generator=g_rep)
+        else:
+            self.embed = w(c.vocab, c.hidden)
         self.layers = []
         for _ in range(c.layers):
             self.layers.append({
@@ -145,7 +168,11 @@ class LlamaModel:
                 "n2": torch.ones(c.hidden, device=self.device, dtype=dtype),
             })
         self.norm = torch.ones(c.hidden, device=self.device, dtype=dtype)
-        self.lm_head = w(c.vocab, c.hidden)
+        if tp_size > 1:
+            self.lm_head = torch.empty(c.vocab, c.hidden, device=self.device, dtype=dtype).normal_(0.0, std,
+                                                                                                generator=g_rep)
+        else:
+            self.lm_head = w(c.vocab, c.hidden)
         inv = 1.0 / (c.rope_theta ** (torch.arange(0, c.head_dim, 2, dtype=torch.float64) / c.head_dim))
         f = torch.outer(torch.arange(c.max_position, dtype=torch.float64), inv)
         self.cos_sin = torch.cat([f.cos(), f.sin()], dim=-1).float().to(self.device)
@@ -157,6 +184,14 @@ class LlamaModel:
         self._attn_backends: dict[bool, list] = {}
 
     # ------------------------------------------------------------ helpers
+    def _reduce(self, x: torch.Tensor) -> torch.Tensor:
+        """Sum a row-parallel projection's partial output over the tensor-parallel ranks."""
+        if self.tp_size > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(x, group=self.tp_group)
+        return x
+
     @staticmethod
     def kv_bases(pool: KvLayout, layer: int) -> tuple[int, int]:
         k = pool.layer_base(layer)
@@ -224,10 +259,10 @@ class LlamaModel:
                 v = torch.cat([pv, v], dim=1)
             a = self._attention(q, k.unsqueeze(0), v.unsqueeze(0), start_pos)
             a = a.squeeze(0).transpose(0, 1).reshape(T, c.q_size)
-            x = F.linear(a, L["wo"])
+            x = self._reduce(F.linear(a, L["wo"]))
             llama_ops.rmsnorm(x, L["n2"], c.eps, residual=residual, out=h)
             gu = F.linear(h, L["wgu"])
-            x = F.linear(llama_ops.silu_mul(gu), L["wd"])
+            x = self._reduce(F.linear(llama_ops.silu_mul(gu), L["wd"]))
         last = torch.empty(1, c.hidden, device=self.device, dtype=self.dtype)
         res_last = residual[-1:].contiguous()
         llama_ops.rmsnorm(x[-1:].contiguous(), self.norm, c.eps, residual=res_last, out=last)
@@ -331,9 +366,9 @@ class LlamaModel:
             llama_ops.paged_decode_attn(q, kb, vb, pool.block_stride, pool.token_stride, pool.head_stride, page,
                                         block_table, seq_lens, c.kv_heads, self.scale, splits, scratch=scratch,
                                         out=attn, counters=counters)
-            x = self.dlinear(attn.view(B, c.q_size), L["wo"])
+            x = self._reduce(self.dlinear(attn.view(B, c.q_size), L["wo"]))
             llama_ops.rmsnorm(x, L["n2"], c.eps, residual=residual, out=h)
-            x = self.dlinear(llama_ops.silu_mul(self.dlinear(h, L["wgu"])), L["wd"])
+            x = self._reduce(self.dlinear(llama_ops.silu_mul(self.dlinear(h, L["wgu"])), L["wd"]))
         out = torch.empty_like(h)
         llama_ops.rmsnorm(x, self.norm, c.eps, residual=residual, out=out)
         return self.dlinear(out, self.lm_head).argmax(dim=-1)

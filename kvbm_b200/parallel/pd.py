@@ -40,9 +40,13 @@ class HostMailbox:
 
     Sequence numbers only grow, so a slot can be reused as soon as its
     request is reported: a stale value can never equal a newer number.
+
+    With tensor parallelism several prefill ranks fill one decode rank's
+    shard: each slot has ``words`` words, one per contributing prefill rank,
+    and the request has landed once all of them read its sequence number.
     """
 
-    def __init__(self, slots: int, name: str | None = None):
+    def __init__(self, slots: int, name: str | None = None, words: int = 8):
         import ctypes as C
         from collections import deque
 
@@ -50,16 +54,16 @@ class HostMailbox:
 
         from ..physical.memory import PinnedBuffer, SharedPinnedBuffer
 
-        self.slots, self.name = int(slots), name
-        self.nbytes = max(4096, (self.slots * 8 + 4095) // 4096 * 4096)
+        self.slots, self.name, self.words = int(slots), name, int(words)
+        self.nbytes = max(4096, (self.slots * self.words * 8 + 4095) // 4096 * 4096)
         self.buf = SharedPinnedBuffer(name, self.nbytes) if name else PinnedBuffer(self.nbytes)
         arr = (C.c_uint8 * self.nbytes).from_address(self.buf.ptr)
-        self._words = np.frombuffer(arr, dtype=np.uint64, count=self.slots)
+        self._words = np.frombuffer(arr, dtype=np.uint64, count=self.slots * self.words)
         self._words[:] = 0
         self._free = deque(range(self.slots))
 
     def descriptor(self) -> dict:
-        return {"name": self.name, "nbytes": self.nbytes, "slots": self.slots}
+        return {"name": self.name, "nbytes": self.nbytes, "slots": self.slots, "words": self.words}
 
     def alloc(self) -> int | None:
         return self._free.popleft() if self._free else None
@@ -71,11 +75,15 @@ class HostMailbox:
     def num_free(self) -> int:
         return len(self._free)
 
-    def value(self, slot: int) -> int:
-        return int(self._words[slot])
+    def value(self, slot: int, contributor: int = 0) -> int:
+        return int(self._words[slot * self.words + contributor])
 
-    def device_ptr(self, slot: int = 0) -> int:
-        return self.buf.device_ptr + 8 * int(slot)
+    def landed(self, slot: int, seq: int, contributors: int = 1) -> bool:
+        base = slot * self.words
+        return all(int(self._words[base + c]) == seq for c in range(contributors))
+
+    def device_ptr(self, slot: int = 0, contributor: int = 0) -> int:
+        return self.buf.device_ptr + 8 * (int(slot) * self.words + int(contributor))
 
     def close(self) -> None:
         self._words = None
@@ -89,6 +97,7 @@ class MailboxWriter:
         from ..physical.memory import SharedPinnedBuffer
 
         self.slots = int(desc["slots"])
+        self.words = int(desc.get("words", 1))
         self._buf = None
         if local is not None:
             self._base = local.buf.device_ptr
@@ -98,10 +107,10 @@ class MailboxWriter:
             self._buf = SharedPinnedBuffer(desc["name"], int(desc["nbytes"]), create=False)
             self._base = self._buf.device_ptr
 
-    def flag_ptr(self, slot: int) -> int:
-        if not 0 <= slot < self.slots:
-            raise IndexError(f"mailbox slot {slot} out of range [0, {self.slots})")
-        return self._base + 8 * int(slot)
+    def flag_ptr(self, slot: int, contributor: int = 0) -> int:
+        if not 0 <= slot < self.slots or not 0 <= contributor < self.words:
+            raise IndexError(f"mailbox word ({slot}, {contributor}) out of range ({self.slots}, {self.words})")
+        return self._base + 8 * (int(slot) * self.words + int(contributor))
 
     def close(self) -> None:
         if self._buf is not None:

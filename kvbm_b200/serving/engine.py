@@ -207,15 +207,45 @@ class DecodeBatch:
             self._step()
 
 
+@dataclass
+class StepPlan:
+    """Everything a model runner needs to execute one engine step.
+
+    The scheduling rank builds it; with tensor parallelism it is broadcast so
+    every rank runs the same prefill chunks and decode step on its shard (the
+    collectives inside the forward pass line up) and the same connector ops on
+    its KV shard."""
+
+    step: int
+    meta: bytes | None = None
+    new: list[tuple] = field(default_factory=list)        # (req_id, prompt int32 bytes, block_ids, max_tokens)
+    enter: list[tuple] = field(default_factory=list)      # (slot, req_id, input token or -1, position, output index)
+    prefills: list[tuple] = field(default_factory=list)   # (req_id, start, end)
+    decode: bool = False
+    finish: list[tuple] = field(default_factory=list)     # (req_id, slot, n tokens): decode ends after this step
+    done: list[str] = field(default_factory=list)         # every request that ends in this step
+
+
 class LLMEngine:
-    """One serving instance (one GPU, TP = 1) with an optional block-manager connector."""
+    """One serving instance with an optional block-manager connector.
+
+    Single GPU by default. With ``tp`` (a :class:`~kvbm_b200.serving.tp.TpComm`)
+    the instance spans ``tp.size`` processes: rank 0 schedules (it holds the
+    connector leader and the G1 block allocator) and broadcasts each step's
+    plan; every rank runs the plan on its model shard and its connector
+    worker, and rank 0 aggregates the workers' reports (a request counts as
+    received / sent when every rank reported it, the way vLLM aggregates its
+    workers' outputs).
+    """
 
     def __init__(self, model: LlamaModel, cfg: EngineConfig, leader: ConnectorLeader | None = None,
-                 worker: ConnectorWorker | None = None, pool: KvLayout | None = None):
+                 worker: ConnectorWorker | None = None, pool: KvLayout | None = None, tp=None):
         self.model, self.cfg = model, cfg
         self.device = model.device
         self.pool = pool if pool is not None else model.allocate_pool(cfg.num_gpu_blocks, cfg.block_size)
-        self.leader, self.worker = leader, worker
+        self.tp = tp
+        self.is_scheduler = tp is None or tp.rank == 0
+        self.leader, self.worker = (leader if self.is_scheduler else None), worker
         self.g1: BlockManager | None = None
         if cfg.prefix_caching:
             # G1 blocks through the logical block manager: finished prompts' full blocks stay
@@ -228,6 +258,7 @@ class LLMEngine:
             self.free_blocks = deque(range(1, cfg.num_gpu_blocks))  # block 0: target of idle decode slots
             dummy = 0
         self.requests: dict[str, Request] = {}
+        self._mirror: dict[str, Request] = {}   # TP ranks > 0: the requests the plans named
         self.waiting: deque[Request] = deque()
         self.remote: dict[str, Request] = {}
         self.prefilling: deque[Request] = deque()
@@ -235,6 +266,9 @@ class LLMEngine:
         self.decoding: dict[int, Request] = {}
         self.free_slots = deque(range(cfg.max_num_seqs))
         self._delayed: dict[str, Request] = {}
+        self._announced: set[str] = set()
+        self._recv_count: dict[str, int] = {}
+        self._send_count: dict[str, int] = {}
         self.step_id = 0
         self._mark = torch.cuda.Stream(device=self.device) if cfg.record_events else None
         max_blocks = math.ceil(cfg.max_model_len / cfg.block_size)
@@ -253,6 +287,8 @@ class LLMEngine:
         torch.cuda.synchronize(self.device)
 
     def add_request(self, req: Request) -> None:
+        if not self.is_scheduler:
+            raise RuntimeError("requests enter a tensor-parallel instance on its rank 0")
         if req.max_tokens > self.cfg.max_tokens:
             raise ValueError(f"max_tokens {req.max_tokens} > engine limit {self.cfg.max_tokens}")
         if req.num_prompt_tokens + req.max_tokens > self.cfg.max_model_len:
@@ -275,37 +311,21 @@ class LLMEngine:
         return len(self.remote)
 
     def step(self) -> list[Request]:
-        """One engine step; returns the requests that finished in it."""
+        """One engine step; returns the requests that finished in it (on the scheduling rank)."""
         self.step_id += 1
         self.stats["steps"] += 1
         self._finished_now: list[Request] = []
-        so = SchedulerOutputLite(step=self.step_id)
-        self._admit(so)
-        prefills = self._schedule_prefill(so)
-        self._enter_decode(so)
-        for req in self.decoding.values():
-            if req.request_id not in so.scheduled:
-                so.scheduled[req.request_id] = ([], [], req.num_prompt_tokens + req.num_output)
-        w = self.worker
-        if self.leader is not None:
-            raw = self.leader.build_connector_meta(so)
-            w.bind_connector_metadata(raw)
-            w.start_load_kv()
-        for req, start, end in prefills:
-            self._run_prefill(req, start, end)
-        if self.decoding:
-            self._run_decode()
-        if w is not None:
-            w.wait_for_save()
-        finished = self._finished_now
-        if w is not None:
-            sending, recving = w.get_finished({r.request_id for r in finished})
-            wmeta = w.build_connector_worker_meta()
-            errs = w.get_block_ids_with_load_errors()
-            self.leader.update_connector_output(sending, recving, wmeta, errs)
-            self._on_received(recving, errs)
-            self._on_sent(sending)
-            w.clear_connector_metadata()
+        plan = self._schedule() if self.is_scheduler else None
+        if self.tp is not None:
+            plan = self.tp.broadcast_plan(plan)
+        self._execute(plan)
+        report = self._report(plan)
+        if self.tp is not None:
+            reports = self.tp.gather_reports(report)
+        else:
+            reports = [report]
+        if self.is_scheduler:
+            self._update(reports)
         # bounded lookahead: what the connector polls reflects the GPU's progress, as in an engine that
         # reads its sampled tokens every step
         ev = torch.cuda.Event()
@@ -313,9 +333,37 @@ class LLMEngine:
         self._inflight.append(ev)
         while len(self._inflight) > max(1, self.cfg.max_inflight_steps):
             self._inflight.popleft().synchronize()
-        return finished
+        return self._finished_now
 
     # ----------------------------------------------------------- schedule
+    def _schedule(self) -> StepPlan:
+        plan = StepPlan(step=self.step_id)
+        so = SchedulerOutputLite(step=self.step_id)
+        self._admit(so)
+        for req in self.prefilling:
+            if req.request_id not in self._announced:
+                self._announce(req, plan)
+        self._plan_prefill(so, plan)
+        self._plan_enter(so, plan)
+        for slot, req in self.decoding.items():
+            if req.request_id not in so.scheduled:
+                so.scheduled[req.request_id] = ([], [], req.num_prompt_tokens + req.num_output)
+            if req.num_output + 1 >= req.max_tokens:
+                plan.finish.append((req.request_id, slot, req.max_tokens))
+        plan.decode = bool(self.decoding)
+        plan.done = [rid for rid, _, _ in plan.finish]
+        plan.done += [rid for rid, _, end in plan.prefills
+                      if end >= self.requests[rid].num_prompt_tokens and self.requests[rid].max_tokens <= 1]
+        if self.leader is not None:
+            plan.meta = self.leader.build_connector_meta(so)
+        return plan
+
+    def _announce(self, req: Request, plan: StepPlan) -> None:
+        """Tell the other TP ranks about a request the first time a plan uses it."""
+        self._announced.add(req.request_id)
+        if self.tp is not None:
+            plan.new.append((req.request_id, req.prompt.numpy().tobytes(), list(req.block_ids), req.max_tokens))
+
     def _blocks_needed(self, req: Request) -> int:
         return math.ceil((req.num_prompt_tokens + max(0, req.max_tokens - 1)) / self.cfg.block_size)
 
@@ -382,40 +430,81 @@ class LLMEngine:
                 req.status = RequestStatus.PREFILL
                 self.prefilling.append(req)
 
-    def _schedule_prefill(self, so: SchedulerOutputLite) -> list[tuple[Request, int, int]]:
+    def _plan_prefill(self, so: SchedulerOutputLite, plan: StepPlan) -> None:
         budget = self.cfg.max_num_batched_tokens
-        out = []
         for req in self.prefilling:
             if budget <= 0:
                 break
             start = req.num_computed_tokens
             end = min(req.num_prompt_tokens, start + budget)
-            out.append((req, start, end))
+            plan.prefills.append((req.request_id, start, end))
             budget -= end - start
             so.scheduled[req.request_id] = ([], [], end)
-        return out
 
-    def _enter_decode(self, so: SchedulerOutputLite) -> None:
-        entries = []
+    def _plan_enter(self, so: SchedulerOutputLite, plan: StepPlan) -> None:
         while self.ready and self.free_slots:
             req = self.ready.popleft()
             slot = self.free_slots.popleft()
             req.slot, req.status = slot, RequestStatus.DECODE
             S = req.num_prompt_tokens
-            if req._first_tok is not None:
-                # prefilled here: the sampled token is on the device, output 0 already written
-                self.batch.tok[slot: slot + 1].copy_(req._first_tok)
-                self.batch.out[slot, 0:1].copy_(req._first_tok)
-                entries.append((slot, req.block_ids, -1, S, 1))
-                req._first_tok = None
+            if req.request_id not in self._announced:
+                self._announce(req, plan)
+            if req.num_output >= 1:
+                # prefilled here: the sampled token is on the device (every rank has it), output 0 written
+                plan.enter.append((slot, req.request_id, -1, S, 1))
             else:
                 # every prompt token's KV arrived: the first step recomputes the last one
-                entries.append((slot, req.block_ids, int(req.prompt[S - 1]), S - 1, 0))
+                plan.enter.append((slot, req.request_id, int(req.prompt[S - 1]), S - 1, 0))
                 so.scheduled[req.request_id] = ([], [], S)
             self.decoding[slot] = req
-        self.batch.enter(entries)
 
     # ------------------------------------------------------------ execute
+    def _req(self, rid: str) -> Request:
+        req = self.requests.get(rid) or self._mirror.get(rid) or self._delayed.get(rid)
+        if req is None:
+            raise KeyError(f"plan names unknown request {rid}")
+        return req
+
+    def _execute(self, plan: StepPlan) -> None:
+        for rid, prompt, block_ids, max_tokens in plan.new:
+            if not self.is_scheduler and rid not in self._mirror:
+                t = torch.frombuffer(bytearray(prompt), dtype=torch.int32)
+                m = Request(rid, t, max_tokens=max_tokens)
+                m.block_ids = list(block_ids)
+                self._mirror[rid] = m
+        w = self.worker
+        if w is not None and plan.meta is not None:
+            w.bind_connector_metadata(plan.meta)
+            w.start_load_kv()
+        entries = []
+        for slot, rid, tok, pos, oi in plan.enter:
+            req = self._req(rid)
+            if tok < 0:
+                self.batch.tok[slot: slot + 1].copy_(req._first_tok)
+                self.batch.out[slot, 0:1].copy_(req._first_tok)
+                req._first_tok = None
+            entries.append((slot, req.block_ids, tok, pos, oi))
+        self.batch.enter(entries)
+        for rid, start, end in plan.prefills:
+            self._run_prefill(self._req(rid), start, end)
+        if plan.decode:
+            self.batch.step()
+            self.stats["decode_steps"] += 1
+            if self.is_scheduler:
+                self._advance_decode(plan)
+            leave = []
+            for rid, slot, n in plan.finish:
+                if self.is_scheduler:
+                    req = self._req(rid)
+                    req.output = torch.empty(n, dtype=torch.int64, pin_memory=True)
+                    req.output.copy_(self.batch.out[slot, :n], non_blocking=True)
+                else:
+                    self._mirror.pop(rid, None)
+                leave.append(slot)
+            self.batch.leave(leave)
+        if w is not None and plan.meta is not None:
+            w.wait_for_save()
+
     def _run_prefill(self, req: Request, start: int, end: int) -> None:
         dev = self.device
         if req._dev_prompt is None:
@@ -428,9 +517,17 @@ class LLMEngine:
                                  on_layer_done=(lambda l: w.save_kv_layer(l, requests=rid)) if w else None,
                                  on_layer_start=w.wait_for_layer_load if w else None)
         self.stats["prefill_tokens"] += end - start
-        req.num_computed_tokens = end
         if end < req.num_prompt_tokens:
+            if self.is_scheduler:
+                req.num_computed_tokens = end
             return
+        if not self.is_scheduler:
+            if req.max_tokens > 1:
+                req._first_tok = nxt
+            else:
+                self._mirror.pop(req.request_id, None)
+            return
+        req.num_computed_tokens = end
         self.prefilling.remove(req)
         self._register_prompt(req)
         req.num_output = 1
@@ -445,29 +542,62 @@ class LLMEngine:
             req._first_tok = nxt
             self.ready.append(req)
 
-    def _run_decode(self) -> None:
-        self.batch.step()
-        self.stats["decode_steps"] += 1
+    def _advance_decode(self, plan: StepPlan) -> None:
         ev = None
-        leave = []
+        ending = {rid for rid, _, _ in plan.finish}
         for slot, req in list(self.decoding.items()):
             req.num_output += 1
-            if self._mark is not None and (req.num_output == 1 or req.num_output >= req.max_tokens):
+            if self._mark is not None and (req.num_output == 1 or req.request_id in ending):
                 if ev is None:
                     ev = torch.cuda.Event(enable_timing=True)
                     ev.record()
                 if req.num_output == 1:
                     req.first_token_event = ev
-                if req.num_output >= req.max_tokens:
+                if req.request_id in ending:
                     req.finish_event = ev
-            if req.num_output >= req.max_tokens:
-                req.output = torch.empty(req.max_tokens, dtype=torch.int64, pin_memory=True)
-                req.output.copy_(self.batch.out[slot, : req.max_tokens], non_blocking=True)
-                leave.append(slot)
+            if req.request_id in ending:
                 del self.decoding[slot]
                 self.free_slots.append(slot)
                 self._finish(req)
-        self.batch.leave(leave)
+
+    # ------------------------------------------------------------- report
+    def _report(self, plan: StepPlan) -> dict:
+        """This rank's connector-worker outputs for the step."""
+        w = self.worker
+        if w is None:
+            return {}
+        sending, recving = w.get_finished(set(plan.done))
+        out = {"sending": sending, "recving": recving, "meta": w.build_connector_worker_meta(),
+               "errors": w.get_block_ids_with_load_errors()}
+        w.clear_connector_metadata()
+        return out
+
+    def _update(self, reports: list[dict]) -> None:
+        if self.leader is None:
+            return
+        n = len(reports)
+        sending, recving, errs, meta = set(), set(), set(), {}
+        for rep in reports:
+            for r in rep.get("sending", ()):
+                self._send_count[r] = self._send_count.get(r, 0) + 1
+            for r in rep.get("recving", ()):
+                self._recv_count[r] = self._recv_count.get(r, 0) + 1
+            errs |= set(rep.get("errors", ()))
+            for kind, steps in (rep.get("meta") or {}).items():
+                d = meta.setdefault(kind, {})
+                for st, c in steps.items():
+                    d[st] = d.get(st, 0) + c
+        for r, c in list(self._send_count.items()):
+            if c >= n:
+                sending.add(r)
+                del self._send_count[r]
+        for r, c in list(self._recv_count.items()):
+            if c >= n:
+                recving.add(r)
+                del self._recv_count[r]
+        self.leader.update_connector_output(sending, recving, meta or None, errs)
+        self._on_received(recving, errs)
+        self._on_sent(sending)
 
     # -------------------------------------------------------- completion
     def _finish(self, req: Request) -> None:
@@ -486,6 +616,7 @@ class LLMEngine:
     def _free(self, req: Request) -> None:
         # the request keeps the list of the blocks it held (for inspection); the blocks return to the pool
         self._release_blocks(req)
+        self._announced.discard(req.request_id)
 
     def _release_blocks(self, req: Request) -> None:
         if self.g1 is None:

@@ -83,11 +83,13 @@ class PdInstance:
     """One serving instance of a P/D deployment."""
 
     def __init__(self, role: str, model: LlamaModel, cfg: PdConfig, instance_id: int, plane, directory,
-                 shared: bool = False, prefill_target: int | None = None, timing: bool = True):
+                 shared: bool = False, prefill_target: int | None = None, timing: bool = True, tp=None):
         if role not in ("prefill", "decode"):
             raise ValueError(role)
         self.role, self.model, self.cfg, self.instance_id = role, model, cfg, int(instance_id)
         self.plane = plane
+        self.tp = tp
+        tp_rank, tp_size = (tp.rank, tp.size) if tp is not None else (0, 1)
         bs = cfg.page_size
         kcfg = KvbmConfig.load({"transfer": {"layer_batch": cfg.layer_batch, "push_engine": cfg.push_engine}},
                                env={}, system_toml=None)
@@ -103,19 +105,22 @@ class PdInstance:
             nblocks = cfg.prefill_requests * cfg.prompt_blocks + 1
             max_seqs = 1
         g2 = BlockManager(1, bs, "lru", Tier.G2)
-        self.leader = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([])), bs, offload_enabled=False, cd=cd,
-                                      plane=plane if role == "decode" else None, prefill_target=prefill_target,
-                                      instance_id=self.instance_id, mailbox_slots=slots,
-                                      recv_timeout_s=cfg.recv_timeout_s)
-        self.worker = ConnectorWorker(kcfg, rank=0, device=model.device.index, block_size=bs)
+        self.leader = None
+        if tp_rank == 0:
+            self.leader = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([])), bs, offload_enabled=False, cd=cd,
+                                          plane=plane if role == "decode" else None, prefill_target=prefill_target,
+                                          instance_id=self.instance_id, mailbox_slots=slots,
+                                          recv_timeout_s=cfg.recv_timeout_s, num_workers=tp_size, tp_size=tp_size,
+                                          directory=directory)
+        self.worker = ConnectorWorker(kcfg, rank=tp_rank, device=model.device.index, block_size=bs)
         ecfg = EngineConfig(num_gpu_blocks=nblocks, block_size=bs, max_num_seqs=max_seqs,
                             max_num_batched_tokens=max(cfg.prompt_len, 2048),
                             max_model_len=cfg.prompt_len + cfg.gen_len, max_tokens=cfg.gen_len,
                             use_graphs=cfg.use_graphs and role == "decode")
-        self.engine = LLMEngine(model, ecfg, self.leader, self.worker)
+        self.engine = LLMEngine(model, ecfg, self.leader, self.worker, tp=tp)
         self.worker.register_layout(self.engine.pool)
         self.worker.enable_disagg(self.instance_id, directory, mailbox_slots=slots, shared=shared,
-                                  timing=timing and role == "prefill")
+                                  timing=timing and role == "prefill", tp_rank=tp_rank, tp_size=tp_size)
         self.served = 0
 
     def warmup(self) -> None:
@@ -123,7 +128,10 @@ class PdInstance:
 
     # ----------------------------------------------------------- prefill
     def pull(self, wait_s: float = 0.0) -> int:
-        """Prefill role: turn dispatches waiting on the plane into requests (waits up to ``wait_s`` for one)."""
+        """Prefill role: turn dispatches waiting on the plane into requests (waits up to ``wait_s`` for one).
+        With tensor parallelism only the instance's rank 0 takes dispatches (it schedules)."""
+        if self.tp is not None and self.tp.rank != 0:
+            return 0
         got = self.plane.wait(self.instance_id, wait_s) if wait_s > 0 else self.plane.poll(self.instance_id)
         for d in got:
             prompt = torch.from_numpy(d["tokens"].copy()).pin_memory()
