@@ -60,15 +60,27 @@ def blocks_for_bytes(size_gb: float | None, num_blocks: int | None, bytes_per_bl
     return 0
 
 
+# Instances whose workers live in this process, by (instance, rank): a peer in the same
+# process is written through its live pool and mailbox (a CUDA IPC handle cannot be opened by
+# the process that exported it).
+_LOCAL_SHARDS: dict[tuple[int, int], tuple] = {}
+
+
 class PeerConnection:
     """A decode instance as a prefill worker writes to it: its G1 pool and mailbox."""
 
     def __init__(self, info: dict, device: int):
+        import os
+
         from ..parallel.pd import MailboxWriter
 
+        local = _LOCAL_SHARDS.get((info.get("instance"), info.get("rank"))) if info.get("pid") == os.getpid() else None
         if "pool_obj" in info:  # same process (e.g. colocated): the live objects
             self.pool = info["pool_obj"]
             self.mailbox = MailboxWriter(info["mailbox"], local=info["mailbox_obj"])
+        elif local is not None:
+            self.pool = local[0]
+            self.mailbox = MailboxWriter(info["mailbox"], local=local[1])
         else:
             self.pool = KvLayout.from_descriptor(LayoutDescriptor.from_dict(info["pool"]), device=device)
             self.mailbox = MailboxWriter(info["mailbox"])
@@ -202,14 +214,17 @@ class ConnectorWorker:
 
         self.instance_id, self.directory, self.push_timing = int(instance_id), directory, timing
         self.tp_rank, self.tp_size = int(tp_rank), int(tp_size)
+        import os
+
         info = {"device": self.device, "rank": self.tp_rank, "tp": self.tp_size,
-                "heads": self.g1.config.num_heads * self.tp_size}
+                "heads": self.g1.config.num_heads * self.tp_size, "instance": self.instance_id, "pid": os.getpid()}
         if mailbox_slots:
             name = f"kvbm_mb_{self.instance_id:x}_{self.tp_rank}" if shared else None
             self.mailbox = HostMailbox(mailbox_slots, name=name)
             info["mailbox"] = self.mailbox.descriptor()
             if shared:
                 info["pool"] = self.g1.descriptor().to_dict()
+                _LOCAL_SHARDS[(self.instance_id, self.tp_rank)] = (self.g1, self.mailbox)
             else:
                 info.update(pool_obj=self.g1, mailbox_obj=self.mailbox)
         directory.publish(self.instance_id, info, rank=self.tp_rank)
@@ -466,6 +481,7 @@ class ConnectorWorker:
             c.close()
         self._peers.clear()
         if self.mailbox is not None:
+            _LOCAL_SHARDS.pop((self.instance_id, self.tp_rank), None)
             self.mailbox.close()
             self.mailbox = None
         if self.worker is not None:

@@ -84,9 +84,13 @@ class LocalPrefillPlane(PrefillPlane):
         return out
 
     def wait(self, instance, timeout_s, limit=None):
-        with self._cv:
-            self._cv.wait_for(lambda: bool(self._q.get(int(instance))), timeout=timeout_s)
+        self.wait_nonempty(instance, timeout_s)
         return self.poll(instance, limit)
+
+    def wait_nonempty(self, instance, timeout_s) -> bool:
+        """Wait up to ``timeout_s`` until a dispatch for ``instance`` is queued (does not take it)."""
+        with self._cv:
+            return self._cv.wait_for(lambda: bool(self._q.get(int(instance))), timeout=timeout_s)
 
 
 class StorePrefillPlane(PrefillPlane):
@@ -138,6 +142,33 @@ class HubPrefillPlane(PrefillPlane):
                 break
             out.append(decode_dispatch(bytes.fromhex(r["payload"])))
         return out
+
+
+class HubRouterPlane(PrefillPlane):
+    """Dispatch through the hub's prefill router (``/v1/prefill-router/dispatch``): the router
+    picks the prefill worker (lowest net-new load, breaker tier) and calls its
+    ``PrefillRouterHandler`` over the messenger. The call returns when that prefill is done, so
+    it runs on a small thread pool: the decode scheduler never waits for it (completion reaches
+    the decode side through the mailbox). The dispatch's ``target`` is only a hint."""
+
+    def __init__(self, client, workers: int = 8, timeout: float = 300.0):
+        import concurrent.futures as cf
+
+        self.client, self.timeout = client, timeout
+        self._pool = cf.ThreadPoolExecutor(max_workers=workers, thread_name_prefix="kvbm-cd-route")
+        self.futures = []
+
+    def dispatch(self, target, raw):
+        d = decode_dispatch(raw)
+        provided = int(d["decode"].get("provided_blocks", 0)) * 16
+        self.futures.append(self._pool.submit(self.client.dispatch, int(d["tokens"].size), provided,
+                                              {"payload": raw.hex(), "hint": int(target)}, self.timeout))
+
+    def poll(self, instance, limit=None):
+        raise RuntimeError("a hub-routed plane is consumed by PrefillRouterHandler, not polled")
+
+    def close(self) -> None:
+        self._pool.shutdown(wait=False)
 
 
 class PeerDirectory:

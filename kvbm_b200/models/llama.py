@@ -124,12 +124,16 @@ class LlamaModel:
     pool holds only those), ``intermediate / tp`` FFN columns; the attention
     output and FFN down projections are row-parallel and summed over
     ``tp_group`` with an all-reduce (NCCL). ``self.cfg`` is the shard's
-    geometry, ``self.full_cfg`` the model's. Weights are random per shard
-    (seeded by ``seed`` and the rank).
+    geometry, ``self.full_cfg`` the model's. ``shard_init="slice"`` draws
+    every weight at full size from ``seed`` and keeps this rank's slice, so
+    any TP degree computes the same model as TP = 1 (up to the order of the
+    all-reduce sums); ``"independent"`` draws only the shard (models too
+    large to materialise whole on one GPU).
     """
 
     def __init__(self, cfg: LlamaConfig, device: torch.device | str = "cuda", seed: int = 0,
-                 dtype: torch.dtype = torch.bfloat16, tp_rank: int = 0, tp_size: int = 1, tp_group=None):
+                 dtype: torch.dtype = torch.bfloat16, tp_rank: int = 0, tp_size: int = 1, tp_group=None,
+                 shard_init: str = "slice"):
         if cfg.heads % tp_size or cfg.kv_heads % tp_size or cfg.intermediate % tp_size:
             raise ValueError(f"tp_size {tp_size} must divide heads, kv_heads and intermediate")
         self.full_cfg = cfg
@@ -142,7 +146,8 @@ class LlamaModel:
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype
-        g = torch.Generator(device=self.device).manual_seed(seed + 7919 * tp_rank)
+        sliced = tp_size == 1 or shard_init == "slice"
+        g = torch.Generator(device=self.device).manual_seed(seed if sliced else seed + 7919 * tp_rank)
         std = 0.02
 
         def w(*shape, scale=std):
@@ -150,29 +155,46 @@ class LlamaModel:
             t.normal_(0.0, scale, generator=g)
             return t
 
-        c = cfg
-        if tp_size > 1:  # replicated tensors are identical on every rank
-            g_rep = torch.Generator(device=self.device).manual_seed(seed)
-            self.embed = torch.empty(c.vocab, c.hidden, device=self.device, dtype=dtype).normal_(0.0, std,
-                                                                                              generator=g_rep)
-        else:
-            self.embed = w(c.vocab, c.hidden)
+        c, F_ = cfg, self.full_cfg
+        T, r = tp_size, tp_rank
+
+        def rows(t, parts):
+            """This rank's slice of each of ``parts`` consecutive row blocks of t."""
+            out, o = [], 0
+            for n in parts:
+                k = n // T
+                out.append(t[o + r * k: o + (r + 1) * k])
+                o += n
+            return torch.cat(out).contiguous()
+
+        def layer_weights():
+            if sliced:
+                wqkv = w(F_.q_size + 2 * F_.kv_size, F_.hidden)
+                wo = w(F_.hidden, F_.q_size, scale=std / math.sqrt(2 * F_.layers))
+                wgu = w(2 * F_.intermediate, F_.hidden)
+                wd = w(F_.hidden, F_.intermediate, scale=std / math.sqrt(2 * F_.layers))
+                if T > 1:
+                    wqkv = rows(wqkv, [F_.q_size, F_.kv_size, F_.kv_size])
+                    wo = wo[:, r * c.q_size:(r + 1) * c.q_size].contiguous()
+                    wgu = rows(wgu, [F_.intermediate, F_.intermediate])
+                    wd = wd[:, r * c.intermediate:(r + 1) * c.intermediate].contiguous()
+                return wqkv, wo, wgu, wd
+            return (w(c.q_size + 2 * c.kv_size, c.hidden), w(c.hidden, c.q_size, scale=std / math.sqrt(2 * c.layers)),
+                    w(2 * c.intermediate, c.hidden), w(c.hidden, c.intermediate, scale=std / math.sqrt(2 * c.layers)))
+
+        g_rep = torch.Generator(device=self.device).manual_seed(seed)  # replicated tensors: same on every rank
+        self.embed = torch.empty(c.vocab, c.hidden, device=self.device, dtype=dtype).normal_(0.0, std, generator=g_rep)
         self.layers = []
         for _ in range(c.layers):
+            wqkv, wo, wgu, wd = layer_weights()
             self.layers.append({
-                "wqkv": w(c.q_size + 2 * c.kv_size, c.hidden),
-                "wo": w(c.hidden, c.q_size, scale=std / math.sqrt(2 * c.layers)),
-                "wgu": w(2 * c.intermediate, c.hidden),
-                "wd": w(c.hidden, c.intermediate, scale=std / math.sqrt(2 * c.layers)),
+                "wqkv": wqkv, "wo": wo, "wgu": wgu, "wd": wd,
                 "n1": torch.ones(c.hidden, device=self.device, dtype=dtype),
                 "n2": torch.ones(c.hidden, device=self.device, dtype=dtype),
             })
         self.norm = torch.ones(c.hidden, device=self.device, dtype=dtype)
-        if tp_size > 1:
-            self.lm_head = torch.empty(c.vocab, c.hidden, device=self.device, dtype=dtype).normal_(0.0, std,
-                                                                                                generator=g_rep)
-        else:
-            self.lm_head = w(c.vocab, c.hidden)
+        self.lm_head = torch.empty(c.vocab, c.hidden, device=self.device, dtype=dtype).normal_(0.0, std,
+                                                                                            generator=g_rep)
         inv = 1.0 / (c.rope_theta ** (torch.arange(0, c.head_dim, 2, dtype=torch.float64) / c.head_dim))
         f = torch.outer(torch.arange(c.max_position, dtype=torch.float64), inv)
         self.cos_sin = torch.cat([f.cos(), f.sin()], dim=-1).float().to(self.device)

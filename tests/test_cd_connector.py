@@ -154,3 +154,60 @@ def test_local_plane_wait_wakes_on_dispatch():
     d = LocalPeerDirectory()
     d.publish(1, {"a": 1})
     assert d.lookup(1)["a"] == 1
+
+
+def test_decode_dispatch_routed_through_the_hub_to_a_prefill_server():
+    """Decode leader -> hub prefill router -> PrefillRouterHandler -> prefill server's local plane;
+    the router's call completes once the prefill engine finished the request."""
+    from types import SimpleNamespace
+
+    from kvbm_b200.engine.cd_plane import HubRouterPlane
+    from kvbm_b200.hub.client import HubClient
+    from kvbm_b200.hub.server import HubServer
+    from kvbm_b200.runtime.messenger import wait_until
+    from kvbm_b200.serving.prefill_server import PrefillServer
+
+    class FakePrefill:
+        role, instance_id = "prefill", 7
+
+        def __init__(self):
+            self.plane = LocalPrefillPlane()
+            self.queue, self.seen = [], []
+            self.engine = SimpleNamespace(has_unfinished=lambda: bool(self.queue), _delayed={})
+
+        def pull(self, wait_s=0.0):
+            got = self.plane.poll(self.instance_id)
+            self.queue += got
+            self.seen += got
+            return len(got)
+
+        def step(self):
+            out = [SimpleNamespace(request_id=d["request_id"], num_prompt_tokens=int(d["tokens"].size))
+                   for d in self.queue]
+            self.queue = []
+            return out
+
+    hub = HubServer(max_seq_len=4096, ttl=5.0).start()
+    fake = FakePrefill()
+    server = PrefillServer(fake, hub.url)
+    stop = threading.Event()
+    t = threading.Thread(target=server.serve_forever, args=(stop,), daemon=True)
+    t.start()
+    client = HubClient(hub.url)
+    plane = HubRouterPlane(client, timeout=10.0)
+    try:
+        assert wait_until(lambda: len(client.targets()) == 1, 5.0)
+        L = decode_leader(plane)
+        L.create_slot(KvbmRequest("routed", list(range(80))))
+        assert L.get_num_new_matched_tokens("routed", 0) == (80, True)
+        L.update_state_after_alloc("routed", list(range(30, 35)), 80)
+        res = plane.futures[0].result(timeout=10)
+        assert res["forwarded"] and res["result"]["result"]["request_id"] == "routed"
+        [d] = fake.seen
+        assert d["decode"]["dst_ids"] == list(range(30, 35)) and d["decode"]["instance"] == 3
+    finally:
+        stop.set()
+        t.join(timeout=5)
+        server.close()
+        plane.close()
+        hub.stop()

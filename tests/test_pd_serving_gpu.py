@@ -240,3 +240,104 @@ def test_engine_g2_spill_to_g3_and_onboard_back(tmp_path):
     assert leader.tier_stats["staged_from_g3"] == 5
     assert torch.equal(a.output, b.output)
     worker.shutdown()
+
+
+def _hetero_rank(rank, port, q):
+    """Rank 0: prefill TP rank 0 and the TP=1 decode instance; rank 1: prefill TP rank 1."""
+    import torch.distributed as dist
+
+    from kvbm_b200.engine.cd_plane import StorePeerDirectory, StorePrefillPlane
+    from kvbm_b200.serving.tp import TpComm
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                            timeout=timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    try:
+        tp = TpComm.create([0, 1], timeout=timedelta(seconds=120))
+        store = dist.distributed_c10d._get_default_store()
+        plane, directory = StorePrefillPlane(store), StorePeerDirectory(store)
+        cfg_m = LlamaConfig.tiny(layers=3)
+        cfg = PdConfig(model=cfg_m, concurrency=4, prompt_len=72, gen_len=5, layer_batch=2, recv_timeout_s=60)
+        pre = PdInstance("prefill", LlamaModel(cfg_m, torch.device("cuda", rank), seed=13, tp_rank=rank, tp_size=2,
+                                               tp_group=tp.nccl), cfg, 100, plane, directory, shared=True, tp=tp)
+        dec, reqs, full = None, [], None
+        prompts = _prompts(4, [72, 45, 64, 30], cfg_m.vocab, seed=8)
+        if rank == 0:
+            full = LlamaModel(cfg_m, torch.device("cuda", 0), seed=13)  # the same weights as the two shards
+            dec = PdInstance("decode", full, cfg, 200, plane, directory, shared=True, prefill_target=100)
+            dec.warmup()
+            reqs = [Request(f"h{i}", p, max_tokens=cfg.gen_len) for i, p in enumerate(prompts)]
+            for r in reqs:
+                dec.engine.add_request(r)
+        while True:
+            if rank == 0:
+                dec.step()
+                pre.pull()
+            state = tp.broadcast((dec.engine.has_unfinished(), pre.engine.has_unfinished() or bool(pre.engine._delayed))
+                                 if rank == 0 else None)
+            if not state[0] and not state[1]:
+                break
+            if state[1]:
+                pre.step()
+        torch.cuda.synchronize()
+        if rank == 0:
+            scratch = full.allocate_pool(8, 16)
+            worst = 0.0
+            layer0_exact = True
+            for r, p in zip(reqs, prompts):
+                S = p.numel()
+                nb = (S + 15) // 16
+                ids = torch.arange(1, nb + 1, dtype=torch.int32, device="cuda")
+                full.prefill(p.cuda(), scratch, ids)
+                torch.cuda.synchronize()
+                for li in range(cfg_m.layers):
+                    ref = scratch.layer_view(li)[ids.long()].float()
+                    got = dec.engine.pool.layer_view(li)[torch.tensor(r.block_ids[:nb], device="cuda").long()].float()
+                    ref = ref.permute(1, 0, 2, 3, 4).reshape(2, nb * 16, -1)[:, : S - 1]
+                    got = got.permute(1, 0, 2, 3, 4).reshape(2, nb * 16, -1)[:, : S - 1]
+                    if li == 0:
+                        layer0_exact &= bool(torch.equal(ref, got))
+                    worst = max(worst, float((ref - got).abs().max()) / max(1e-6, float(ref.abs().max())))
+            outs = [r.output.tolist() for r in reqs]
+            stats = dict(dec.leader.cd_stats)
+            q.put(("decode", layer0_exact, worst, outs, stats))
+            dec.shutdown()
+        else:
+            q.put(("prefill", pre.worker.take_push_timings()[1]))
+        pre.shutdown()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.multigpu
+def test_two_gpu_prefill_tp2_pushes_head_shards_into_decode_tp1():
+    """Prefill with TP=2 (one KV head per rank) pushes into a TP=1 decode instance: each prefill
+    rank's shard lands at its head offset (layer 0's K/V bit for bit; later layers within bf16
+    tolerance of a TP=1 prefill, which sums its projections in another order), both ranks'
+    completion words are awaited, and every request decodes."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_hetero_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            item = q.get(timeout=300)
+            results[item[0]] = item
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    _, layer0_exact, worst, outs, stats = results["decode"]
+    assert stats["received"] == 4 and stats["failed"] == 0
+    assert layer0_exact
+    assert worst < 0.05, worst
+    assert all(len(o) == 5 for o in outs)
+    assert results["prefill"][1] > 0  # rank 1 pushed its shard across NVLink
