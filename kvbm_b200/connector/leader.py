@@ -171,7 +171,7 @@ class ConnectorLeader:
         # step -> (G3 mutables awaiting the spill copies, hashes, G2 sources held, worker reports so far)
         self._pending_g3: dict[int, tuple[list[MutableBlock], list[int], list[ImmutableBlock], int]] = {}
         self._stage_ops: list[StageOp] = []
-        self.tier_stats = {"staged_from_g3": 0, "spilled_to_g3": 0}
+        self.tier_stats = {"staged_from_g3": 0, "spilled_to_g3": 0, "onboarded_blocks": 0, "offload_ops": 0}
         self.cd_stats = {"remote": 0, "local": 0, "dispatched": 0, "received": 0, "failed": 0, "pushed_blocks": 0}
 
     # ---------------------------------------------------------------- slots
@@ -336,6 +336,7 @@ class ConnectorLeader:
             take = [b for b in take if b.tier == Tier.G2]
         if n:
             self._onboard_ops.append(OnboardOp(req_id, src_ids, g1))
+            self.tier_stats["onboarded_blocks"] += n
             slot.onboard_pending = True
         slot.onboarding = take
         slot.matched = []
@@ -437,6 +438,7 @@ class ConnectorLeader:
                 continue  # G2 full of active blocks: skip this offload
             dst, _ = got
             meta.offload.append(OffloadOp(req_id, [b for _, b in todo], [d.block_id for d in dst]))
+            self.tier_stats["offload_ops"] += 1
             slot.pending_offload_steps.add(meta.step)
             g2_pending.extend(dst)
             g2_hashes.extend(h for h, _ in todo)

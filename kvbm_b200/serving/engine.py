@@ -490,18 +490,18 @@ class LLMEngine:
         if plan.decode:
             self.batch.step()
             self.stats["decode_steps"] += 1
-            if self.is_scheduler:
-                self._advance_decode(plan)
             leave = []
             for rid, slot, n in plan.finish:
                 if self.is_scheduler:
                     req = self._req(rid)
-                    req.output = torch.empty(n, dtype=torch.int64, pin_memory=True)
+                    req.output = torch.empty(n, dtype=torch.int64, pin_memory=self.device.type == "cuda")
                     req.output.copy_(self.batch.out[slot, :n], non_blocking=True)
                 else:
                     self._mirror.pop(rid, None)
                 leave.append(slot)
             self.batch.leave(leave)
+            if self.is_scheduler:
+                self._advance_decode(plan)
         if w is not None and plan.meta is not None:
             w.wait_for_save()
 
@@ -535,7 +535,7 @@ class LLMEngine:
             req.first_token_event = torch.cuda.Event(enable_timing=True)
             req.first_token_event.record()
         if req.max_tokens <= 1:
-            req.output = torch.empty(1, dtype=torch.int64, pin_memory=True)
+            req.output = torch.empty(1, dtype=torch.int64, pin_memory=self.device.type == "cuda")
             req.output.copy_(nxt, non_blocking=True)
             self._finish(req)
         else:

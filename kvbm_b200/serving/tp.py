@@ -35,13 +35,14 @@ class TpComm:
         self.gloo, self.nccl = gloo_group, nccl_group
 
     @classmethod
-    def create(cls, ranks: list[int], timeout=None) -> "TpComm":
+    def create(cls, ranks: list[int], timeout=None, nccl: bool = True) -> "TpComm":
         """Collective over the whole world: every process must call it with the same ``ranks``
-        sequence of every instance, in the same order (process groups are created collectively)."""
+        sequence of every instance, in the same order (process groups are created collectively).
+        ``nccl=False`` skips the NCCL group (control-plane tests without GPUs)."""
         kw = {"timeout": timeout} if timeout is not None else {}
         gloo = dist.new_group(ranks, backend="gloo", **kw)
-        nccl = dist.new_group(ranks, backend="nccl", **kw) if dist.is_nccl_available() else None
-        return cls(ranks, gloo, nccl)
+        ng = dist.new_group(ranks, backend="nccl", **kw) if nccl else None
+        return cls(ranks, gloo, ng)
 
     def broadcast_plan(self, plan):
         box = [plan]

@@ -96,8 +96,11 @@ def _ref_quant(x: torch.Tensor):
     """x: [..., page, heads, hd] per (block, layer, outer) -> per-head scales over (page, hd)."""
     xf = x.float()
     amax = xf.abs().amax(dim=(-3, -1))  # [..., heads]
-    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
-    inv = torch.where(amax > 0, 448.0 / amax, torch.ones_like(amax))
+    # tensor / tensor divisions round correctly (torch computes a division by a scalar, or of a scalar, as a
+    # multiplication by a reciprocal, which can differ in the last bit from the kernel's fp32 division)
+    c448 = torch.full_like(amax, 448.0)
+    scale = torch.where(amax > 0, amax / c448, torch.ones_like(amax))
+    inv = torch.where(amax > 0, c448 / amax, torch.ones_like(amax))
     q = (xf * inv.unsqueeze(-2).unsqueeze(-1)).clamp(-448, 448).to(torch.float8_e4m3fn)
     return q, scale
 
@@ -119,7 +122,7 @@ def test_fp8_quant_dequant(engine, src_dtype):
     qref, sref = _ref_quant(x)
     got_q = q8.gather_blocks(d_ids).view(torch.float8_e4m3fn)
     got_s = q8.scales_view()[torch.tensor(d_ids, device="cuda")]
-    torch.testing.assert_close(got_s, sref, rtol=1e-6, atol=0)
+    assert torch.equal(got_s, sref)
     # same fp32 scale, same fp32 product, both round to nearest even with saturation: byte-exact
     mism = (got_q.view(torch.uint8) != qref.view(torch.uint8))
     assert int(mism.sum()) == 0, (int(mism.sum()), x[mism].flatten()[:8].tolist())

@@ -74,4 +74,6 @@ def test_vllm_engine_outputs_identical_after_prefix_cache_reset(tmp_path, monkey
         lead = conn._leader
         # the second pass found the prompts' full blocks in G2 (all but the last prompt token's block)
         assert lead.leader.stats["g2_hits"] >= sum((len(p["prompt_token_ids"]) - 1) // 16 for p in prompts)
-        assert lead.leader.stats["onboarded_blocks"] if "onboarded_blocks" in lead.leader.stats else True
+        # ... and its workers onboarded them into vLLM's G1 blocks
+        assert lead.tier_stats["onboarded_blocks"] >= sum((len(p["prompt_token_ids"]) - 1) // 16 for p in prompts)
+        assert lead.tier_stats["offload_ops"] > 0
