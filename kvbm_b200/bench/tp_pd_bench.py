@@ -58,6 +58,8 @@ def main(argv=None):
     p.add_argument("--warmup", type=int, default=1)
     p.add_argument("--layers", type=int, default=80)
     p.add_argument("--layer-batch", type=int, default=8)
+    p.add_argument("--wire", default="bf16", choices=["bf16", "fp8"],
+                   help="fp8: the push quantises to e4m3 (per block/layer/K-V/head scales), decode dequantises")
     p.add_argument("--out", default=None)
     a = p.parse_args(argv)
     world = int(os.environ["WORLD_SIZE"])
@@ -79,10 +81,11 @@ def main(argv=None):
     role = "prefill" if inst_idx == 0 else "decode"
     iid = 1000 + 100 * inst_idx
     mcfg = llama3_70b(a.layers)
-    model = LlamaModel(mcfg, torch.device("cuda", local), seed=11 + inst_idx, tp_rank=tp.rank, tp_size=tp.size,
+    # one model (same seed, every TP degree slices the same full weights) on both sides of the push
+    model = LlamaModel(mcfg, torch.device("cuda", local), seed=11, tp_rank=tp.rank, tp_size=tp.size,
                        tp_group=tp.nccl)
     cfg = PdConfig(model=mcfg, concurrency=a.requests, prompt_len=a.max_len, gen_len=a.gen,
-                   layer_batch=a.layer_batch, decode_waves=2, prefill_requests=2)
+                   layer_batch=a.layer_batch, decode_waves=2, prefill_requests=2, wire_dtype=a.wire)
     store = dist.distributed_c10d._get_default_store()
     plane, directory = StorePrefillPlane(store), StorePeerDirectory(store)
     inst = PdInstance(role, model, cfg, iid, plane, directory, shared=True,
@@ -155,6 +158,7 @@ def main(argv=None):
         tt = sorted(t for r in allr for t in r["ttft"])
         line = {"bench": "tp_pd", "prefill_tp": a.prefill_tp, "decode_tp": a.decode_tp,
                 "decode_instances": a.decode_instances, "layers": a.layers, "kv_dtype": "bf16",
+                "wire_dtype": a.wire, "note": "push GB/s counts bf16 KV bytes; with fp8 on the wire half cross NVLink",
                 "push_gbps_total": round(kb / max(kms, 1e-9) / 1e6, 1),
                 "push_gbps_per_prefill_rank": [round(r["push_bytes"] / max(r["push_ms"], 1e-9) / 1e6, 1) for r in pre],
                 "push_bytes": kb, "waves": a.waves, "requests_per_wave": a.requests * a.decode_instances,

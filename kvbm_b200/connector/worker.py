@@ -120,6 +120,7 @@ class ConnectorWorker:
         self._peers: dict[int, PeerConnection] = {}
         self._pushes: list[tuple[PushOp, list, torch.Tensor, torch.Tensor]] = []
         self.tp_rank, self.tp_size = 0, 1
+        self.landing: KvLayout | None = None   # fp8 landing pool of pushes (wire_dtype="fp8")
         self._recvs: dict[str, tuple] = {}
         self.push_timing = False
         self._push_timers: list[tuple[torch.cuda.Event, torch.cuda.Event, int]] = []
@@ -199,7 +200,7 @@ class ConnectorWorker:
 
     # ------------------------------------------- conditional disaggregation
     def enable_disagg(self, instance_id: int, directory, mailbox_slots: int = 0, shared: bool = False,
-                      timing: bool = False, tp_rank: int = 0, tp_size: int = 1) -> None:
+                      timing: bool = False, tp_rank: int = 0, tp_size: int = 1, wire_dtype: str | None = None) -> None:
         """Join the node's P/D deployment as rank ``tp_rank`` of instance ``instance_id``.
 
         With ``mailbox_slots`` this worker can receive remote prefills: it
@@ -222,11 +223,22 @@ class ConnectorWorker:
             name = f"kvbm_mb_{self.instance_id:x}_{self.tp_rank}" if shared else None
             self.mailbox = HostMailbox(mailbox_slots, name=name)
             info["mailbox"] = self.mailbox.descriptor()
+            target = self.g1
+            if wire_dtype == "fp8":
+                from ..physical.layout import LayoutConfig
+
+                c = self.g1.config
+                cfg8 = LayoutConfig.for_model(c.num_blocks, c.num_layers, c.num_heads, c.head_dim, c.page_size,
+                                              torch.float8_e4m3fn, outer_dim=c.outer_dim)
+                self.landing = KvLayout.allocate(cfg8, "fully_contiguous", self.g1.block_layout, fp8_scales=True,
+                                                 device=self.device)
+                target = self.landing
+            info["wire"] = wire_dtype or "native"
             if shared:
-                info["pool"] = self.g1.descriptor().to_dict()
-                _LOCAL_SHARDS[(self.instance_id, self.tp_rank)] = (self.g1, self.mailbox)
+                info["pool"] = target.descriptor().to_dict()
+                _LOCAL_SHARDS[(self.instance_id, self.tp_rank)] = (target, self.mailbox)
             else:
-                info.update(pool_obj=self.g1, mailbox_obj=self.mailbox)
+                info.update(pool_obj=target, mailbox_obj=self.mailbox)
         directory.publish(self.instance_id, info, rank=self.tp_rank)
 
     def _peer(self, instance: int, rank: int = 0) -> PeerConnection:
@@ -433,8 +445,18 @@ class ConnectorWorker:
                 if r in self._recv_events:
                     continue  # its local onboard part is still running
                 if self.mailbox is not None and self.mailbox.landed(op.slot, op.seq, op.contributors):
-                    recving.add(r)
                     del self._recvs[r]
+                    if self.landing is not None:
+                        # fp8 on the wire: dequantise into G1, report once that copy is done
+                        from ..ops import kv_ops
+
+                        h2d, _ = self._streams()
+                        kv_ops.kv_transfer(self.landing, op.g1_ids, self.g1, op.g1_ids, engine="tile", stream=h2d)
+                        ev = torch.cuda.Event()
+                        ev.record(h2d)
+                        self._recv_events[r] = ev
+                    else:
+                        recving.add(r)
                 elif now > deadline:
                     # the prefill never published: report the blocks so the framework recomputes them
                     self._load_errors.update(op.g1_ids)

@@ -65,6 +65,7 @@ class PdConfig:
     use_graphs: bool = True
     seed: int = 0
     recv_timeout_s: float = 300.0
+    wire_dtype: str = "bf16"         # bf16 | fp8 (block-scaled e4m3 over NVLink, dequantised on arrival)
 
     @property
     def request_blocks(self) -> int:
@@ -120,7 +121,8 @@ class PdInstance:
         self.engine = LLMEngine(model, ecfg, self.leader, self.worker, tp=tp)
         self.worker.register_layout(self.engine.pool)
         self.worker.enable_disagg(self.instance_id, directory, mailbox_slots=slots, shared=shared,
-                                  timing=timing and role == "prefill", tp_rank=tp_rank, tp_size=tp_size)
+                                  timing=timing and role == "prefill", tp_rank=tp_rank, tp_size=tp_size,
+                                  wire_dtype="fp8" if cfg.wire_dtype == "fp8" and role == "decode" else None)
         self.served = 0
 
     def warmup(self) -> None:
