@@ -252,3 +252,201 @@ class LocalConnectorEngine(LeaderEngine):
             return
         s.close("released")
         self.sessions.remove(session_id)
+
+
+class WorkerTierEngine(LocalConnectorEngine):
+    """``LeaderEngine`` of a connector whose workers live in other processes.
+
+    The leader cannot move bytes itself: every copy becomes an op in the
+    step metadata that the workers run (onboard, offload, stage, spill), and
+    the tier state follows the workers' reports:
+
+    * :meth:`match` - G2 prefix continued in G3; G3 hits are held, not
+      staged (``StagingMode.PREPARE``);
+    * :meth:`prepare_staging` / :meth:`finish_staging` - G2 destinations for
+      held G3 hits, registered in G2 once the onboard that follows the stage
+      is reported received;
+    * :meth:`offload` (buffer) / :meth:`take_offload_drain` (flush, once per
+      step, after the pass that wrote the blocks): the G1 -> G2 policy,
+      skipping hashes G2 holds or has in flight, G2 destinations allocated
+      (evicting inactive blocks), returned as offload ops;
+    * :meth:`on_worker_report` - G2 destinations registered when every
+      worker reported the step's copies; registered G2 blocks pass the G3
+      policy and are queued as spill ops (:meth:`take_spill_ops`), the G3
+      copies registered when the spill is reported.
+
+    Parity: crates/kvbm-engine/src/tiering/engine/{local.rs, find.rs,
+    offload.rs} (buffer, flush at finish_forward_pass), tiering/offload/
+    engine.rs:123 (register after the transfer), the G2 -> G3 auto-chain.
+    """
+
+    def __init__(self, leader: InstanceLeader, num_workers: int = 1, g2_policy=None, g3_policy=None,
+                 remote_search=None, sessions=None):
+        from ..engine.offload import PresenceFilter
+
+        super().__init__(leader, remote_search, sessions)
+        self.num_workers = num_workers
+        self.g2_policy = g2_policy or PresenceFilter(leader.g2)
+        self.g3_policy = g3_policy or (PresenceFilter(leader.g3) if leader.g3 is not None else None)
+        self._buffer: list[tuple[str, list[int], list[int]]] = []
+        # step -> (G2 mutables awaiting their copies, their hashes, worker reports so far)
+        self._pending_g2: dict[int, tuple[list, list[int], int]] = {}
+        self._spill_queue: list[tuple[list[ImmutableBlock], list, list[int]]] = []
+        # step -> (G3 mutables awaiting the spill copies, hashes, G2 sources held, worker reports so far)
+        self._pending_g3: dict[int, tuple[list, list[int], list[ImmutableBlock], int]] = {}
+        self.stats = {"offloaded_blocks": 0, "staged_from_g3": 0, "spilled_to_g3": 0, "offload_ops": 0}
+
+    # ------------------------------------------------------------- find
+    def match(self, hashes: list[int]) -> list[ImmutableBlock]:
+        from ..engine.leader import StagingMode
+
+        res = self.leader.find_matches(list(hashes), FindMatchesOptions(staging=StagingMode.PREPARE))
+        return res.g2_blocks + res.g3_held
+
+    def prepare_staging(self, blocks: list[ImmutableBlock]):
+        """(blocks the onboard can use, staging) - G3 hits get G2 destinations; without room in G2 the
+        match stops before G3. ``staging`` is (G3 refs, G2 destinations, hashes) or None."""
+        from ..logical.manager import Tier
+
+        g3 = [b for b in blocks if b.tier == Tier.G3]
+        if not g3:
+            return blocks, None
+        got = self.leader.g2.allocate_blocks_with_evictions(len(g3))
+        if got is None:
+            for b in g3:
+                b.release()
+            return blocks[: len(blocks) - len(g3)], None
+        return blocks, (g3, got[0], [b.sequence_hash for b in g3])
+
+    @staticmethod
+    def release_staging(staging) -> None:
+        g3, dst, _ = staging
+        for b in g3:
+            b.release()
+        for m in dst:
+            m.release()
+
+    def finish_staging(self, staging) -> None:
+        """The stage ran before the onboard that was reported: the G2 copies hold the data now."""
+        g3, dst, hashes = staging
+        for b in self.leader.g2.register_mutable(dst, hashes):
+            b.release()
+        for b in g3:
+            b.release()
+        self.stats["staged_from_g3"] += len(dst)
+
+    # ---------------------------------------------------------- offload
+    def offload(self, request_id, hashes, g1_ids):
+        if len(hashes) != len(g1_ids):
+            raise ValueError("one G1 block per hash")
+        self._buffer.append((request_id, list(hashes), list(g1_ids)))
+
+    def evict(self, request_id):
+        before = len(self._buffer)
+        self._buffer = [e for e in self._buffer if e[0] != request_id]
+        return before - len(self._buffer)
+
+    def take_offload_drain(self, step: int = 0) -> list:
+        """Flush the buffered offloads into this step's ops: ``[(request_id, g1_ids, g2_ids)]``."""
+        from ..engine.offload import OffloadItem
+
+        buf, self._buffer = self._buffer, []
+        g2 = self.leader.g2
+        reg, tier = g2.registry, int(g2.tier)
+        pending = self._pending_hashes()
+        ops, dsts, hashes_all = [], [], []
+        for rid, hashes, g1_ids in buf:
+            todo = [(h, b) for h, b in zip(hashes, g1_ids)
+                    if h not in pending and self.g2_policy.keep(OffloadItem(h, b)) and not reg.is_present(h, tier)]
+            if not todo:
+                continue
+            got = g2.allocate_blocks_with_evictions(len(todo))
+            if got is None:
+                continue  # G2 full of active blocks: skip this offload
+            dst, _ = got
+            pending |= {h for h, _ in todo}
+            ops.append((rid, [b for _, b in todo], [d.block_id for d in dst]))
+            dsts.extend(dst)
+            hashes_all.extend(h for h, _ in todo)
+            self.stats["offloaded_blocks"] += len(todo)
+            self.stats["offload_ops"] += 1
+        if dsts:
+            # registered (and so matchable) only once every worker reports these copies done
+            self._pending_g2[step] = (dsts, hashes_all, 0)
+        return ops
+
+    def _pending_hashes(self) -> set[int]:
+        return {h for _, hs, _ in self._pending_g2.values() for h in hs}
+
+    def take_spill_ops(self, step: int) -> list[tuple[list[int], list[int]]]:
+        """G2 -> G3 copies for this step's metadata: ``[(g2_ids, g3_ids)]``."""
+        if not self._spill_queue:
+            return []
+        ops, srcs, dsts, hs = [], [], [], []
+        for g2_refs, g3_dst, hashes in self._spill_queue:
+            ops.append(([b.block_id for b in g2_refs], [m.block_id for m in g3_dst]))
+            srcs += g2_refs
+            dsts += g3_dst
+            hs += hashes
+        self._spill_queue = []
+        self._pending_g3[step] = (dsts, hs, srcs, 0)
+        return ops
+
+    # --------------------------------------------------- worker reports
+    def on_worker_report(self, meta: dict | None) -> None:
+        if not meta:
+            return
+        self._register_landed(meta.get("offloaded", {}))
+        self._register_spilled(meta.get("spilled", {}))
+
+    def _register_landed(self, offloaded: dict) -> None:
+        for step, n in offloaded.items():
+            step = int(step)
+            entry = self._pending_g2.get(step)
+            if entry is None:
+                continue
+            blocks, hashes, seen = entry
+            seen += int(n)
+            if seen < self.num_workers:
+                self._pending_g2[step] = (blocks, hashes, seen)
+                continue
+            del self._pending_g2[step]
+            imm = self.leader.g2.register_mutable(blocks, hashes)
+            self._chain_to_g3(imm)
+            for b in imm:
+                b.release()  # cached in G2 (inactive, matchable)
+
+    def _chain_to_g3(self, imm: list[ImmutableBlock]) -> None:
+        from ..engine.offload import OffloadItem
+
+        g3 = self.leader.g3
+        if g3 is None or not imm:
+            return
+        pending = {h for _, hs, _, _ in self._pending_g3.values() for h in hs}
+        pending |= {h for _, _, hs in self._spill_queue for h in hs}
+        keep = [b for b in imm if b.sequence_hash not in pending
+                and self.g3_policy.keep(OffloadItem(b.sequence_hash, b.block_id))]
+        if not keep:
+            return
+        got = g3.allocate_blocks_with_evictions(len(keep))
+        if got is None:
+            return
+        self._spill_queue.append(([b.clone() for b in keep], got[0], [b.sequence_hash for b in keep]))
+
+    def _register_spilled(self, spilled: dict) -> None:
+        for step, n in spilled.items():
+            step = int(step)
+            entry = self._pending_g3.get(step)
+            if entry is None:
+                continue
+            dst, hashes, srcs, seen = entry
+            seen += int(n)
+            if seen < self.num_workers:
+                self._pending_g3[step] = (dst, hashes, srcs, seen)
+                continue
+            del self._pending_g3[step]
+            for b in self.leader.g3.register_mutable(dst, hashes):
+                b.release()
+            for b in srcs:
+                b.release()
+            self.stats["spilled_to_g3"] += len(dst)

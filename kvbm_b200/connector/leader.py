@@ -42,12 +42,13 @@ from collections import deque
 from dataclasses import dataclass, field
 
 from ..engine.cd import ConditionalDisagg, Decision, RemotePrefillParams
-from ..engine.leader import FindMatchesOptions, InstanceLeader, StagingMode
-from ..engine.offload import OffloadItem, OffloadPolicy, PresenceFilter
+from ..engine.leader import InstanceLeader
+from ..engine.offload import OffloadPolicy
 from ..logical.manager import ImmutableBlock, MutableBlock, Tier
 from ..logical.sequence import TokenBlockSequence
 from ..utils.metrics import CacheStatsTracker
 from ..utils.tracing import audit
+from .engine import WorkerTierEngine
 from .protocol import ConnectorMetadata, OffloadOp, OnboardOp, PushOp, RecvOp, SpillOp, StageOp
 
 # kv_transfer_params key a decode instance puts on the requests it sends to a prefill instance
@@ -162,16 +163,10 @@ class ConnectorLeader:
         self.num_workers = num_workers
         self.tp_size = tp_size          # this instance's TP degree (decode side: its ranks' head shards)
         self.directory = directory      # where prefill instances publish their TP degree
-        # step -> (G2 mutables awaiting their copies, their hashes, worker reports so far)
-        self._pending_g2: dict[int, tuple[list[MutableBlock], list[int], int]] = {}
-        # G1 -> G2 and G2 -> G3 admission policies (the offload pipelines' filters)
-        self.g2_policy = g2_policy or PresenceFilter(leader.g2)
-        self.g3_policy = g3_policy or (PresenceFilter(leader.g3) if leader.g3 is not None else None)
-        self._spill_queue: list[tuple[list[ImmutableBlock], list[MutableBlock], list[int]]] = []
-        # step -> (G3 mutables awaiting the spill copies, hashes, G2 sources held, worker reports so far)
-        self._pending_g3: dict[int, tuple[list[MutableBlock], list[int], list[ImmutableBlock], int]] = {}
+        # the tier engine behind the LeaderEngine seam: G2/G3 state driven by the workers' reports
+        self.engine = WorkerTierEngine(leader, num_workers=num_workers, g2_policy=g2_policy, g3_policy=g3_policy)
         self._stage_ops: list[StageOp] = []
-        self.tier_stats = {"staged_from_g3": 0, "spilled_to_g3": 0, "onboarded_blocks": 0, "offload_ops": 0}
+        self._counts = {"onboarded_blocks": 0, "offload_ops": 0}
         self.cd_stats = {"remote": 0, "local": 0, "dispatched": 0, "received": 0, "failed": 0, "pushed_blocks": 0}
 
     # ---------------------------------------------------------------- slots
@@ -250,32 +245,24 @@ class ConnectorLeader:
             audit("gnmt_matched", request=req_id, matched_tokens=local_tokens)
         return local_tokens, True
 
+    @property
+    def tier_stats(self) -> dict:
+        """Blocks onboarded, offload ops issued, G3 blocks staged into G2 and G2 blocks spilled to G3."""
+        e = self.engine.stats
+        return {**self._counts, "staged_from_g3": e["staged_from_g3"], "spilled_to_g3": e["spilled_to_g3"]}
+
     def _find(self, hashes: list[int]) -> list[ImmutableBlock]:
         """G2 prefix, continued in G3 (held, not staged: the workers stage them with the onboard)."""
-        res = self.leader.find_matches(hashes, FindMatchesOptions(staging=StagingMode.PREPARE))
-        return res.g2_blocks + res.g3_held
+        return self.engine.match(hashes)
 
     def _prepare_staging(self, slot: RequestSlot, blocks: list[ImmutableBlock]) -> list[ImmutableBlock]:
         """Give every G3 block of the match a G2 destination; without room in G2 the match stops before G3."""
-        g3 = [b for b in blocks if b.tier == Tier.G3]
-        if not g3:
-            return blocks
-        g2 = blocks[: len(blocks) - len(g3)]
-        got = self.leader.g2.allocate_blocks_with_evictions(len(g3))
-        if got is None:
-            for b in g3:
-                b.release()
-            return g2
-        slot.staging = (g3, got[0], [b.sequence_hash for b in g3])
+        blocks, slot.staging = self.engine.prepare_staging(blocks)
         return blocks
 
     def _release_staging(self, slot: RequestSlot) -> None:
-        g3, dst, _ = slot.staging
-        slot.staging = None
-        for b in g3:
-            b.release()
-        for m in dst:
-            m.release()
+        staging, slot.staging = slot.staging, None
+        self.engine.release_staging(staging)
 
     def _decide_remote(self, slot: RequestSlot, computed: int, local_tokens: int) -> bool:
         """Decode-side CD decision (policy, breaker tier, in-flight budget, a free mailbox slot)."""
@@ -332,11 +319,11 @@ class ConnectorLeader:
             if k:
                 self._stage_ops.append(StageOp(req_id, [b.block_id for b in g3[:k]], [m.block_id for m in dst[:k]]))
                 src_ids += [m.block_id for m in dst[:k]]
-                self.tier_stats["staged_from_g3"] += k
+                pass
             take = [b for b in take if b.tier == Tier.G2]
         if n:
             self._onboard_ops.append(OnboardOp(req_id, src_ids, g1))
-            self.tier_stats["onboarded_blocks"] += n
+            self._counts["onboarded_blocks"] += n
             slot.onboard_pending = True
         slot.onboarding = take
         slot.matched = []
@@ -383,15 +370,7 @@ class ConnectorLeader:
         meta = ConnectorMetadata(step=out.step or self.iteration, onboard=self._onboard_ops, recv=self._recv_ops,
                                  stage=self._stage_ops)
         self._onboard_ops, self._recv_ops, self._stage_ops = [], [], []
-        if self._spill_queue:
-            srcs, dsts, hs = [], [], []
-            for g2_refs, g3_dst, hashes in self._spill_queue:
-                meta.spill.append(SpillOp([b.block_id for b in g2_refs], [m.block_id for m in g3_dst]))
-                srcs += g2_refs
-                dsts += g3_dst
-                hs += hashes
-            self._spill_queue = []
-            self._pending_g3[meta.step] = (dsts, hs, srcs, 0)
+        meta.spill = [SpillOp(g2, g3) for g2, g3 in self.engine.take_spill_ops(meta.step)]
         for req_id in out.preempted_req_ids:
             # The workers fence in-flight offloads of these requests before their G1 blocks are
             # reused (evict list). The request resumes from its token sequence with new G1 blocks;
@@ -400,12 +379,12 @@ class ConnectorLeader:
             if slot is None:
                 continue
             meta.evict.append(req_id)
+            self.engine.evict(req_id)
             slot.g1_block_ids = []
             slot.save_cursor = 0
             slot.num_computed_tokens = 0
             self.leader.stats["preempted"] = self.leader.stats.get("preempted", 0) + 1
-        g2_pending: list[MutableBlock] = []
-        g2_hashes: list[int] = []
+        offloading: dict[str, RequestSlot] = {}
         for req_id, (new_tokens, new_blocks, num_computed) in out.scheduled.items():
             slot = self.slots.get(req_id)
             if slot is None:
@@ -423,33 +402,17 @@ class ConnectorLeader:
                 complete = min(complete, len(slot.request.tokens) // self.block_size)
             if complete <= slot.save_cursor:
                 continue
-            hashes = slot.seq.sequence_hashes[slot.save_cursor: complete]
-            g1 = slot.g1_block_ids[slot.save_cursor: complete]
-            reg = self.leader.g2.registry
-            tier = int(self.leader.g2.tier)
-            pending = set(g2_hashes) | self._pending_hashes()
-            todo = [(h, b) for h, b in zip(hashes, g1)
-                    if h not in pending and self.g2_policy.keep(OffloadItem(h, b)) and not reg.is_present(h, tier)]
+            self.engine.offload(req_id, slot.seq.sequence_hashes[slot.save_cursor: complete],
+                                slot.g1_block_ids[slot.save_cursor: complete])
             slot.save_cursor = complete
-            if not todo:
-                continue
-            got = self.leader.g2.allocate_blocks_with_evictions(len(todo))
-            if got is None:
-                continue  # G2 full of active blocks: skip this offload
-            dst, _ = got
-            meta.offload.append(OffloadOp(req_id, [b for _, b in todo], [d.block_id for d in dst]))
-            self.tier_stats["offload_ops"] += 1
-            slot.pending_offload_steps.add(meta.step)
-            g2_pending.extend(dst)
-            g2_hashes.extend(h for h, _ in todo)
-            self.leader.stats["offloaded_blocks"] += len(todo)
-        if g2_pending:
-            # registered (and so matchable) only once every worker reports these copies done
-            self._pending_g2[meta.step] = (g2_pending, g2_hashes, 0)
+            offloading[req_id] = slot
+        # flush: the copies run after this step's forward pass (wait_for_save), never mid-pass
+        for req_id, g1_ids, g2_ids in self.engine.take_offload_drain(meta.step):
+            meta.offload.append(OffloadOp(req_id, g1_ids, g2_ids))
+            offloading[req_id].pending_offload_steps.add(meta.step)
+            self.leader.stats["offloaded_blocks"] += len(g1_ids)
+            self._counts["offload_ops"] += 1
         return meta.encode()
-
-    def _pending_hashes(self) -> set[int]:
-        return {h for _, hs, _ in self._pending_g2.values() for h in hs}
 
     def _advance_push(self, slot: RequestSlot, num_computed: int, meta: ConnectorMetadata) -> None:
         """Prefill side: push the blocks whose KV this step computes (the last, partial one with the last chunk)."""
@@ -472,9 +435,7 @@ class ConnectorLeader:
     def update_connector_output(self, finished_sending: set[str] | None = None,
                                 finished_recving: set[str] | None = None, worker_meta: dict | None = None,
                                 invalid_block_ids: set[int] | None = None) -> None:
-        if worker_meta:
-            self._register_landed(worker_meta.get("offloaded", {}))
-            self._register_spilled(worker_meta.get("spilled", {}))
+        self.engine.on_worker_report(worker_meta)
         bad = set(invalid_block_ids or ())
         for req_id in finished_recving or ():
             slot = self.slots.get(req_id)
@@ -486,12 +447,8 @@ class ConnectorLeader:
             slot.onboard_pending = False
             if slot.staging is not None:
                 # the stage ran before the onboard that finished: the G2 copies hold the data now
-                g3, dst, hashes = slot.staging
-                slot.staging = None
-                for b in self.leader.g2.register_mutable(dst, hashes):
-                    b.release()
-                for b in g3:
-                    b.release()
+                staging, slot.staging = slot.staging, None
+                self.engine.finish_staging(staging)
             rp = slot.remote_prefill
             if rp is not None:
                 failed = bool(bad.intersection(slot.g1_block_ids))
@@ -515,58 +472,6 @@ class ConnectorLeader:
             self.cd.finish_remote()
         self.cd_stats["failed" if failed else "received"] += 1
         audit("cd_received", request=slot.request.request_id, seq=rp.seq, failed=failed)
-
-    def _register_landed(self, offloaded: dict) -> None:
-        """Register the G2 blocks of steps whose offload copies every worker reported done."""
-        for step, n in offloaded.items():
-            step = int(step)
-            entry = self._pending_g2.get(step)
-            if entry is None:
-                continue
-            blocks, hashes, seen = entry
-            seen += int(n)
-            if seen < self.num_workers:
-                self._pending_g2[step] = (blocks, hashes, seen)
-                continue
-            del self._pending_g2[step]
-            imm = self.leader.g2.register_mutable(blocks, hashes)
-            self._chain_to_g3(imm)
-            for b in imm:
-                b.release()  # cached in G2 (inactive, matchable)
-
-    def _chain_to_g3(self, imm: list[ImmutableBlock]) -> None:
-        """G2 -> G3: blocks the G3 policy admits get G3 destinations; the next step's workers copy them."""
-        g3 = self.leader.g3
-        if g3 is None or not imm:
-            return
-        pending = {h for _, hs, _, _ in self._pending_g3.values() for h in hs}
-        pending |= {h for _, _, hs in self._spill_queue for h in hs}
-        keep = [b for b in imm if b.sequence_hash not in pending
-                and self.g3_policy.keep(OffloadItem(b.sequence_hash, b.block_id))]
-        if not keep:
-            return
-        got = g3.allocate_blocks_with_evictions(len(keep))
-        if got is None:
-            return
-        self._spill_queue.append(([b.clone() for b in keep], got[0], [b.sequence_hash for b in keep]))
-
-    def _register_spilled(self, spilled: dict) -> None:
-        for step, n in spilled.items():
-            step = int(step)
-            entry = self._pending_g3.get(step)
-            if entry is None:
-                continue
-            dst, hashes, srcs, seen = entry
-            seen += int(n)
-            if seen < self.num_workers:
-                self._pending_g3[step] = (dst, hashes, srcs, seen)
-                continue
-            del self._pending_g3[step]
-            for b in self.leader.g3.register_mutable(dst, hashes):
-                b.release()
-            for b in srcs:
-                b.release()
-            self.tier_stats["spilled_to_g3"] += len(dst)
 
     def request_finished(self, req_id: str, block_ids: list[int] | None = None) -> tuple[bool, dict | None]:
         slot = self.slots.get(req_id)
