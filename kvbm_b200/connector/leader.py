@@ -44,6 +44,7 @@ from dataclasses import dataclass, field
 from ..engine.cd import ConditionalDisagg, Decision, RemotePrefillParams
 from ..engine.leader import InstanceLeader
 from ..engine.offload import OffloadPolicy
+from ..logical.assignments import ExternalBlockAssignments
 from ..logical.manager import ImmutableBlock, MutableBlock, Tier
 from ..logical.sequence import TokenBlockSequence
 from ..utils.metrics import CacheStatsTracker
@@ -95,7 +96,8 @@ class PushState:
 class RequestSlot:
     request: KvbmRequest
     seq: TokenBlockSequence
-    g1_block_ids: list[int] = field(default_factory=list)
+    # the request's G1 block ids, paired with sequence hashes as blocks complete (assigned)
+    g1: ExternalBlockAssignments = field(default_factory=ExternalBlockAssignments)
     num_computed_tokens: int = 0
     matched: list[ImmutableBlock] = field(default_factory=list)
     matched_start_block: int = 0
@@ -111,6 +113,10 @@ class RequestSlot:
     # G3 hits being staged into G2 for this request's onboard: (G3 refs, G2 destinations, hashes)
     staging: tuple[list[ImmutableBlock], list[MutableBlock], list[int]] | None = None
     onboard_pending: bool = False             # an onboard (or stage) was queued and not reported received
+
+    @property
+    def g1_block_ids(self) -> list[int]:
+        return self.g1.block_ids()
 
 
 @dataclass
@@ -288,7 +294,8 @@ class ConnectorLeader:
     # ----------------------------------------------------------------- USAA
     def update_state_after_alloc(self, req_id: str, block_ids: list[int], num_external_tokens: int) -> None:
         slot = self.slots[req_id]
-        slot.g1_block_ids = list(block_ids)
+        slot.g1.clear()
+        slot.g1.extend_block_ids(block_ids)
         if num_external_tokens <= 0:
             for b in slot.matched:
                 b.release()
@@ -380,7 +387,7 @@ class ConnectorLeader:
                 continue
             meta.evict.append(req_id)
             self.engine.evict(req_id)
-            slot.g1_block_ids = []
+            slot.g1.clear()
             slot.save_cursor = 0
             slot.num_computed_tokens = 0
             self.leader.stats["preempted"] = self.leader.stats.get("preempted", 0) + 1
@@ -391,19 +398,23 @@ class ConnectorLeader:
                 continue
             if new_tokens:
                 slot.seq.append(new_tokens)
-            slot.g1_block_ids.extend(new_blocks)
+            if new_blocks:
+                slot.g1.extend_block_ids(new_blocks)
             slot.num_computed_tokens = num_computed
+            # computed complete blocks take their sequence hashes (assigned, in position order)
+            hashes = slot.seq.sequence_hashes
+            slot.g1.assign_pending(hashes[: num_computed // self.block_size])
             if slot.push is not None:
                 self._advance_push(slot, num_computed, meta)
             if not self.offload_enabled:
                 continue
-            complete = min(num_computed // self.block_size, slot.seq.num_complete_blocks, len(slot.g1_block_ids))
+            complete = slot.g1.assigned_count()
             if not self.decode_offload and num_computed > len(slot.request.tokens):
                 complete = min(complete, len(slot.request.tokens) // self.block_size)
             if complete <= slot.save_cursor:
                 continue
-            self.engine.offload(req_id, slot.seq.sequence_hashes[slot.save_cursor: complete],
-                                slot.g1_block_ids[slot.save_cursor: complete])
+            self.engine.offload(req_id, hashes[slot.save_cursor: complete],
+                                slot.g1.assigned_ids(slot.save_cursor, complete))
             slot.save_cursor = complete
             offloading[req_id] = slot
         # flush: the copies run after this step's forward pass (wait_for_save), never mid-pass

@@ -8,6 +8,7 @@
 #include <pybind11/stl.h>
 
 #include "block_pool.hpp"
+#include "branch_tracker.hpp"
 #include "disk_pool.hpp"
 #include "hash.hpp"
 #include "registry.hpp"
@@ -129,11 +130,45 @@ PYBIND11_MODULE(_kvbm_core, m) {
         return out;
       }, py::arg("max_batch") = 1024);
 
+  auto record = [](const BranchRecord& r) {
+    py::dict d;
+    d["position"] = r.position;
+    d["fragment"] = r.fragment;
+    d["current_fanout"] = r.current_fanout;
+    d["max_fanout"] = r.max_fanout;
+    d["observation_count"] = r.observations;
+    d["last_updated_tick"] = r.last_tick;
+    return d;
+  };
+  py::class_<BranchTracker, std::shared_ptr<BranchTracker>>(m, "BranchTracker")
+      .def(py::init<size_t>(), py::arg("history_capacity") = 1024)
+      .def("on_block_registered", [](BranchTracker& t, py::handle h) { t.on_registered(from_py(h)); })
+      .def("is_branch_point", &BranchTracker::is_branch_point, py::arg("position"), py::arg("fragment"))
+      .def("current_fanout", &BranchTracker::current_fanout, py::arg("position"), py::arg("fragment"))
+      .def("current_branch_points", &BranchTracker::current_branch_points)
+      .def("hot_branch_points", [record](const BranchTracker& t, size_t limit) {
+        py::list out;
+        for (auto& r : t.hot_branch_points(limit)) out.append(record(r));
+        return out;
+      }, py::arg("limit"))
+      .def("branch_points_on_prefix", [record](const BranchTracker& t, py::iterable hs) {
+        auto v = from_py_list(hs);
+        py::list out;
+        for (auto& r : t.on_prefix(v)) out.append(record(r));
+        return out;
+      })
+      .def("branch_point_count", &BranchTracker::branch_point_count)
+      .def("tracked_parent_count", &BranchTracker::tracked_parent_count)
+      .def("history_len", &BranchTracker::history_len)
+      .def_property_readonly("tick", &BranchTracker::tick);
+
   py::class_<Registry, std::shared_ptr<Registry>>(m, "Registry")
-      .def(py::init([](std::shared_ptr<EventQueue> ev, std::shared_ptr<TinyLfu> f) {
-             return std::make_shared<Registry>(ev, f);
+      .def(py::init([](std::shared_ptr<EventQueue> ev, std::shared_ptr<TinyLfu> f, std::shared_ptr<BranchTracker> b) {
+             auto r = std::make_shared<Registry>(ev, f);
+             if (b) r->set_branch_tracker(std::move(b));
+             return r;
            }),
-           py::arg("events") = nullptr, py::arg("frequency") = nullptr)
+           py::arg("events") = nullptr, py::arg("frequency") = nullptr, py::arg("branch_tracker") = nullptr)
       .def("mark_present", [](Registry& r, py::handle h, int t) { r.mark_present(from_py(h), t); })
       .def("mark_absent", [](Registry& r, py::handle h, int t) { r.mark_absent(from_py(h), t); })
       .def("is_present", [](Registry& r, py::handle h, int t) { return r.is_present(from_py(h), t); },
@@ -147,7 +182,8 @@ PYBIND11_MODULE(_kvbm_core, m) {
       .def("touch", [](Registry& r, py::handle h) { r.touch(from_py(h)); })
       .def("frequency", [](Registry& r, py::handle h) { return r.frequency(from_py(h)); })
       .def("size", &Registry::size)
-      .def_property_readonly("events", &Registry::events);
+      .def_property_readonly("events", &Registry::events)
+      .def_property_readonly("branch_tracker", &Registry::branch_tracker);
 
   py::enum_<SlotState>(m, "SlotState")
       .value("Reset", SlotState::Reset)

@@ -4,7 +4,7 @@
 // whose rank is strictly greater than the rank of every mutex it already
 // holds. The hierarchy:
 //
-//   Registry (10) -> BlockPool (20) -> EventQueue (30), TinyLfu (40)
+//   Registry (10) -> BlockPool (20) -> EventQueue (30), TinyLfu (40), BranchTracker (45)
 //   ConsolidatorTracker (50), PositionalIndex (60): independent leaves
 //
 // (a BlockPool releases its mutex before it calls into the registry; the
@@ -33,6 +33,7 @@ enum LockRank : int {
   kRankBlockPool = 20,
   kRankEventQueue = 30,
   kRankTinyLfu = 40,
+  kRankBranchTracker = 45,
   kRankTracker = 50,
   kRankPositionalIndex = 60,
 };

@@ -28,6 +28,7 @@
 #include <unordered_set>
 #include <vector>
 
+#include "branch_tracker.hpp"
 #include "hash.hpp"
 #include "tinylfu.hpp"
 
@@ -129,6 +130,7 @@ class Registry {
       ++e.total;
     }
     if (first && events_) events_->on_present(h);
+    if (first && branches_) branches_->on_registered(h);
   }
   void mark_absent(const SeqHash& h, int tier) {
     bool last = false;
@@ -169,6 +171,9 @@ class Registry {
   }
   std::shared_ptr<EventQueue> events() const { return events_; }
   std::shared_ptr<TinyLfu> freq() const { return freq_; }
+  // Set before the first registration; not synchronised with mark_present.
+  void set_branch_tracker(std::shared_ptr<BranchTracker> b) { branches_ = std::move(b); }
+  std::shared_ptr<BranchTracker> branch_tracker() const { return branches_; }
 
  private:
   struct Entry {
@@ -179,6 +184,7 @@ class Registry {
   std::unordered_map<SeqHash, Entry, SeqHashHasher> map_;
   std::shared_ptr<EventQueue> events_;
   std::shared_ptr<TinyLfu> freq_;
+  std::shared_ptr<BranchTracker> branches_;
 };
 
 }  // namespace kvbm

@@ -126,6 +126,9 @@ class ImmutableBlock(_Handle):
         self._mgr._pool.add_ref(self.block_id)
         return ImmutableBlock(self._mgr, self.block_id, self.sequence_hash, self.kind)
 
+    def registration_handle(self):
+        return self._mgr.registration_handle(self.sequence_hash)
+
     def downgrade(self) -> "WeakBlock":
         return WeakBlock(self._mgr, self.sequence_hash)
 
@@ -176,6 +179,9 @@ class BlockManager:
             if frequency is None and inactive == "multi_lru":
                 frequency = core.TinyLfu()
             registry = core.Registry(events=events, frequency=frequency)
+        # a logical.registry.BlockRegistry (handles, attachments) or a bare native registry
+        self.handles = registry if hasattr(registry, "native") else None
+        registry = getattr(registry, "native", registry)
         self.tier = Tier(tier)
         self.registry = registry
         self._pool = core.BlockPool(num_blocks, block_size, inactive, int(self.tier), registry, duplicate_policy)
@@ -229,6 +235,13 @@ class BlockManager:
 
     def contains(self, seq_hash: int) -> bool:
         return self._pool.contains(seq_hash)
+
+    def registration_handle(self, seq_hash: int):
+        """The shared registration handle of a registered hash (managers built over a
+        ``BlockRegistry``); None when the hash is not registered in any tier."""
+        if self.handles is None:
+            raise RuntimeError("this manager was built without a BlockRegistry")
+        return self.handles.handle(seq_hash)
 
     # ---------------------------------------------------------------- admin
     def reset_inactive_pool(self) -> None:
