@@ -32,6 +32,7 @@ BUILD_DIR = PKG.parent / "_build"
 
 CUDA_SOURCES = [
     CSRC / "kernels" / "kv_xfer.cu",
+    CSRC / "kernels" / "kv_multicast.cu",
     CSRC / "kernels" / "llama_ops.cu",
     CSRC / "kernels" / "kvbm_mem.cu",
     CSRC / "kernels" / "skinny_gemm_tc.cu",

@@ -134,6 +134,19 @@ int kvbm_nhd_hnd_transpose(const void* const* src_chunks, void* const* dst_chunk
 int kvbm_signal_flag(uint64_t* flag, uint64_t value, cudaStream_t stream);
 int kvbm_wait_flag(const uint64_t* flag, uint64_t expected, uint64_t timeout_ns, int* status, cudaStream_t stream);
 
+// Fan-out of (block, layer, K/V) chunks from this rank's pool into every
+// member of an NVLink multicast group (multimem stores through `mc_base`, the
+// multicast address of the pool base); the last CTA adds 1 to the group's
+// u64 counter at multicast address `flag_mc`. `cta_done` is a zeroed device
+// u32 of this rank. Geometry must match on every rank; ids outside
+// [0, pool_blocks) are skipped and reported in `status` (kStatusBadIndex).
+int kvbm_kv_multicast(const uint64_t* src_layer_base, const uint64_t* dst_layer_off, int num_layers,
+                      uint64_t mc_base, int64_t block_stride, int64_t outer_stride, int64_t chunk_bytes, int outer,
+                      const int32_t* src_ids, const int32_t* dst_ids, int num_blocks, int pool_blocks,
+                      uint64_t flag_mc, unsigned int* cta_done, int* status, int max_ctas, cudaStream_t stream);
+// Add 1 (release, system scope) to the u64 counter at multicast address `flag_mc`.
+int kvbm_signal_multicast(uint64_t flag_mc, cudaStream_t stream);
+
 // Layout-independent 64-bit checksum per block: the wrapping sum over every
 // 4-byte word w of the block's selected layers/heads of mix64(w, i), with i
 // the word's index in canonical [layer, outer, token, head, word] order.

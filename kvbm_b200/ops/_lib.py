@@ -82,6 +82,9 @@ _SIGS = {
     "kvbm_wait_flag": (_INT, [_VP, _U64, _U64, _VP, _VP]),
     "kvbm_signal_flag_payload": (_INT, [_VP, _U64, _VP, _VP, _INT, _VP]),
     "kvbm_wait_flags_all": (_INT, [_VP, _INT, _U64, _U64, _VP, _VP]),
+    "kvbm_signal_multicast": (_INT, [_U64, _VP]),
+    "kvbm_kv_multicast": (_INT, [_VP, _VP, _INT, _U64, _I64, _I64, _I64, _INT, _VP, _VP, _INT, _INT, _U64, _VP, _VP,
+                                 _INT, _VP]),
     "kvbm_sm_count": (_INT, []),
     "kvbm_kv_checksum": (_INT, [_VP, _VP, _VP, _VP]),
     "kvbm_rmsnorm": (_INT, [_VP, _VP, _VP, _VP, _I64, _INT, _F32, _VP]),
@@ -167,7 +170,7 @@ _KERNELS_PER_CALL = {
     "kvbm_signal_flag_payload": 1, "kvbm_wait_flags_all": 1, "kvbm_rmsnorm": 1, "kvbm_rope_kv_write": 1,
     "kvbm_rope_kv_push": 1, "kvbm_rope_kv_write_qout": 1, "kvbm_rope_kv_push_heads": 1,
     "kvbm_silu_mul": 1, "kvbm_paged_decode_attn": 2, "kvbm_paged_decode_attn_fused": 1, "kvbm_paged_decode_attn_simt": 2,
-    "kvbm_skinny_gemm": 1,
+    "kvbm_skinny_gemm": 1, "kvbm_kv_multicast": 1, "kvbm_signal_multicast": 1,
 }
 _launches = 0
 

@@ -262,6 +262,11 @@ def signal_flag(flag_ptr: int, value: int, stream=None) -> None:
     _lib.call("kvbm_signal_flag", flag_ptr, value, _stream(stream))
 
 
+def signal_flag_multicast(flag_mc: int, stream=None) -> None:
+    """Add 1 to a u64 counter through its NVLink multicast address (every member's copy)."""
+    _lib.call("kvbm_signal_multicast", flag_mc, _stream(stream))
+
+
 def wait_flag(flag_ptr: int, expected: int, timeout_ns: int, status_ptr: int, stream=None) -> None:
     _lib.call("kvbm_wait_flag", flag_ptr, expected, timeout_ns, status_ptr, _stream(stream))
 

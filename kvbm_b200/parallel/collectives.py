@@ -10,6 +10,12 @@ the other ranks' G1.
   peer's paged slots with the fused transfer kernel (one launch per peer,
   NVLink stores), then publishes a per-peer completion flag; peers make
   their compute stream wait on the flag with a bounded-spin kernel.
+* :class:`NvlsFanoutCollectives` - the one-to-many path through NVSwitch
+  multicast: every rank's G1 pool lives in one symmetric-memory allocation
+  bound to an NVLink multicast object, and rank 0 writes each chunk once with
+  ``multimem.st`` (the switch replicates it to every member), then bumps the
+  group's completion counter through the same multicast address. Rank 0
+  sends the bytes over NVLink once instead of ``world_size - 1`` times.
 * :class:`NcclCollectives` - the baseline: gather the blocks into a
   contiguous staging buffer, ``torch.distributed.broadcast`` it over NCCL,
   scatter on every rank.
@@ -27,7 +33,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops import kv_ops
-from ..physical.layout import KvLayout, LayoutConfig, LayoutDescriptor
+from ..physical.layout import KvBlockLayout, KvLayout, LayoutConfig, LayoutDescriptor
 from ..physical.memory import DeviceBuffer, PeerBuffer
 
 WAIT_NS = 30_000_000_000
@@ -114,6 +120,94 @@ class P2PFanoutCollectives(CollectiveOps):
         st = int(self.flags.tensor(torch.int32)[2].item())
         if st != 0:
             raise TimeoutError("replicated-data broadcast wait timed out")
+
+
+class NvlsUnavailable(RuntimeError):
+    """The GPUs or the driver offer no NVLink multicast object for this group."""
+
+
+class NvlsFanoutCollectives(CollectiveOps):
+    """Rank 0 fans blocks out to every rank with one multicast store per 16 bytes."""
+
+    FLAG_BYTES = 4096
+
+    @staticmethod
+    def allocate_pool(config: LayoutConfig, group=None, kind: str = "fully_contiguous",
+                      block_layout: KvBlockLayout = KvBlockLayout.OPERATIONAL_NHD):
+        """Collective: allocate this rank's replicated G1 pool (plus a completion-counter page) in
+        symmetric memory and bind it to the group's multicast object. Returns ``(layout, handle,
+        flag_offset)``; ``handle.multicast_ptr`` is 0 when the platform has no multicast."""
+        import torch.distributed._symmetric_memory as symm
+
+        if block_layout == KvBlockLayout.UNIVERSAL:
+            raise ValueError("the multicast fan-out copies contiguous (block, layer, K/V) chunks")
+        *_, data = KvLayout._strides(config, kind, block_layout, True)
+        flag_off = (data + 4095) // 4096 * 4096
+        dev = torch.device("cuda", torch.cuda.current_device())
+        t = symm.empty(flag_off + NvlsFanoutCollectives.FLAG_BYTES, dtype=torch.uint8, device=dev)
+        t.zero_()
+        handle = symm.rendezvous(t, group if group is not None else dist.group.WORLD)
+        layout = KvLayout.over_tensor(config, t, kind, block_layout)
+        layout._symm = (t, handle)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        return layout, handle, flag_off
+
+    def __init__(self, g1: KvLayout, handle, flag_offset: int, group=None, max_ctas: int = 0,
+                 wait_ns: int = WAIT_NS):
+        self.g1, self.group = g1, group
+        self.rank = dist.get_rank(group)
+        self.world_size = dist.get_world_size(group)
+        self.mc = int(getattr(handle, "multicast_ptr", 0) or 0)
+        if not self.mc:
+            raise NvlsUnavailable("no NVLink multicast object for this group")
+        self.handle = handle
+        self.flag_ptr = g1.base_ptr + flag_offset
+        self.flag_mc = self.mc + flag_offset
+        self.max_ctas, self.wait_ns = max_ctas, wait_ns
+        self.cta_done = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", g1.device))
+        self.status = torch.zeros(2, dtype=torch.int32, device=self.cta_done.device)
+        self.seq = 0
+
+    def broadcast(self, src_ids, dst_ids, layer_range=None, stream=None) -> None:
+        """Asynchronous on ``stream``: every rank's stream (rank 0's included) waits for the
+        group counter to reach this call's sequence number."""
+        import ctypes
+
+        from ..ops import _lib
+
+        self.seq += 1
+        cfg = self.g1.config
+        lb, le = layer_range or (0, cfg.num_layers)
+        st = stream or torch.cuda.current_stream()
+        if len(src_ids) != len(dst_ids):
+            raise ValueError("src_ids and dst_ids differ in length")
+        nb = cfg.num_blocks
+        if any(not 0 <= int(i) < nb for i in list(src_ids) + list(dst_ids)):
+            raise IndexError(f"block id outside [0, {nb})")
+        if self.rank == 0 and len(dst_ids):
+            dev = self.cta_done.device
+            sid = torch.as_tensor(src_ids, dtype=torch.int32).to(dev, non_blocking=True)
+            did = torch.as_tensor(dst_ids, dtype=torch.int32).to(dev, non_blocking=True)
+            n = le - lb
+            src_base = (ctypes.c_uint64 * n)(*[self.g1.layer_base(l) for l in range(lb, le)])
+            dst_off = (ctypes.c_uint64 * n)(*[self.g1.layer_offsets[l] for l in range(lb, le)])
+            _lib.call("kvbm_kv_multicast", src_base, dst_off, n, self.mc, self.g1.block_stride,
+                      self.g1.outer_stride, cfg.bytes_per_chunk, cfg.outer_dim, sid.data_ptr(), did.data_ptr(),
+                      len(dst_ids), nb, self.flag_mc, self.cta_done.data_ptr(), self.status.data_ptr() + 4,
+                      self.max_ctas, kv_ops._stream(st))
+            self._keep = (sid, did)
+        elif self.rank == 0:
+            # nothing to copy: still advance every member's counter so the sequence stays aligned
+            kv_ops.signal_flag_multicast(self.flag_mc, stream=st)
+        kv_ops.wait_flag(self.flag_ptr, self.seq, self.wait_ns, self.status.data_ptr(), stream=st)
+
+    def check(self) -> None:
+        st = self.status.tolist()
+        if st[0] != 0:
+            raise TimeoutError("multicast fan-out wait timed out")
+        if st[1] != 0:
+            raise IndexError("multicast fan-out skipped out-of-range block ids")
 
 
 class ReplicatedDataWorker:
