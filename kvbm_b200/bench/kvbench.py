@@ -119,8 +119,11 @@ def run(args) -> list[dict]:
     for name, b in dsts.items():
         if args.d2d and name not in args.d2d.split(","):
             continue
-        for engine in [e for e in ("tile", "tma") if e in args.engines.split(",")]:
-            ms = _time(lambda: kv_ops.kv_transfer(a, s_ids, b, d_ids, engine=engine), args.iters, args.warmup,
+        for engine in [e for e in ("tile", "tile1", "tma") if e in args.engines.split(",")]:
+            # tile1: the fp8 casts on the one-tile-at-a-time kernel (tile: the pipelined one)
+            kv_ops.set_cast_pipeline(engine != "tile1")
+            eng = "tile" if engine == "tile1" else engine
+            ms = _time(lambda: kv_ops.kv_transfer(a, s_ids, b, d_ids, engine=eng), args.iters, args.warmup,
                        flush)
             nbytes = n * cfg.bytes_per_block
             moved = nbytes + n * b.config.bytes_per_block  # read + write (fp8 writes half)
@@ -130,8 +133,10 @@ def run(args) -> list[dict]:
             print(json.dumps(r), flush=True)
         if name == "g1_to_g1_fp8_quant":
             back = KvLayout.allocate(cfg, "fully_contiguous", nhd)
-            for engine in [e for e in ("tile", "tma") if e in args.engines.split(",")]:
-                ms = _time(lambda: kv_ops.kv_transfer(b, d_ids, back, s_ids, engine=engine), args.iters,
+            for engine in [e for e in ("tile", "tile1", "tma") if e in args.engines.split(",")]:
+                kv_ops.set_cast_pipeline(engine != "tile1")
+                eng = "tile" if engine == "tile1" else engine
+                ms = _time(lambda: kv_ops.kv_transfer(b, d_ids, back, s_ids, engine=eng), args.iters,
                            args.warmup, flush)
                 nbytes = n * cfg.bytes_per_block
                 moved = nbytes + n * b.config.bytes_per_block
@@ -139,6 +144,7 @@ def run(args) -> list[dict]:
                      "ms": round(ms, 4), "gbps_rw": round(moved / ms / 1e6, 2)}
                 results.append(r)
                 print(json.dumps(r), flush=True)
+        kv_ops.set_cast_pipeline(True)
         if name == "g1_to_g1_copy" and "ce" in args.engines.split(","):
             src_p = [a.layer_base(0) + int(x) * a.block_stride for x in s_ids.tolist()]
             dst_p = [b.layer_base(0) + int(x) * b.block_stride for x in d_ids.tolist()]

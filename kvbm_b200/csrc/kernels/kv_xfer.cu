@@ -342,6 +342,195 @@ __device__ __forceinline__ void tile_dequant(const uint8_t* src, int64_t src_rs,
   }
 }
 
+// ---- software-pipelined fp8 tiles ------------------------------------------
+//
+// When a head tile fits in one load batch per lane (16 x 16-byte source
+// units for a quantise, 4 fp8 units for a dequantise: every [16 x 128]
+// head tile), a persistent warp issues the loads of its next tile before it
+// reduces, converts and stores the current one, so DRAM reads stay in flight
+// while the cast math runs. Larger tiles take the one-tile-at-a-time path.
+
+constexpr int kQPairs = 4;   // source unit pairs per lane held per tile
+constexpr int kDqUnits = 4;  // fp8 source units per lane held per tile
+
+template <int KIND>
+__device__ __forceinline__ void quant_load(const uint8_t* src, int64_t rs, int pairs, const UnitMap& um, int lane,
+                                           int4 (&va)[kQPairs], int4 (&vb)[kQPairs]) {
+#pragma unroll
+  for (int k = 0; k < kQPairs; ++k) {
+    const int q = k * 32 + lane;
+    if (q < pairs) {
+      int r, c;
+      um.rc(2 * q, r, c);
+      const int4* p = reinterpret_cast<const int4*>(src + r * rs + c * 16);
+      va[k] = p[0];
+      vb[k] = p[1];
+    }
+  }
+}
+
+template <int KIND>
+__device__ __forceinline__ void quant_store(const int4 (&va)[kQPairs], const int4 (&vb)[kQPairs], uint8_t* dst,
+                                            int64_t rs, int pairs, const UnitMap& um, float* scale_out, int lane) {
+  constexpr int kOut = (KIND == kQuantF32) ? 4 : 8;
+  uint32_t mx = 0;
+#pragma unroll
+  for (int k = 0; k < kQPairs; ++k)
+    if (k * 32 + lane < pairs)
+      mx = amax_combine<KIND>(mx, amax_combine<KIND>(unit_amax_bits<KIND>(va[k]), unit_amax_bits<KIND>(vb[k])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = amax_combine<KIND>(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float amax = amax_bits_to_float<KIND>(mx);
+  const float inv = amax > 0.f ? kE4M3Max / amax : 1.0f;
+#pragma unroll
+  for (int k = 0; k < kQPairs; ++k) {
+    const int q = k * 32 + lane;
+    if (q >= pairs) continue;
+    int r, c;
+    um.rc(2 * q, r, c);
+    uint8_t* d = dst + r * rs + c * kOut;
+    uint32_t w[4];
+    unit_to_fp8<KIND>(va[k], inv, w);
+    unit_to_fp8<KIND>(vb[k], inv, w + kOut / 4);
+    if (KIND == kQuantF32) {
+      *reinterpret_cast<uint2*>(d) = make_uint2(w[0], w[1]);
+    } else {
+      *reinterpret_cast<int4*>(d) = make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]);
+    }
+  }
+  if (lane == 0 && scale_out != nullptr) *scale_out = amax > 0.f ? amax / kE4M3Max : 1.0f;
+}
+
+__device__ __forceinline__ void dequant_load(const uint8_t* src, int64_t rs, int n, const UnitMap& um, int lane,
+                                             int4 (&v)[kDqUnits]) {
+#pragma unroll
+  for (int k = 0; k < kDqUnits; ++k) {
+    const int u = k * 32 + lane;
+    if (u < n) {
+      int r, c;
+      um.rc(u, r, c);
+      v[k] = *reinterpret_cast<const int4*>(src + r * rs + c * 16);
+    }
+  }
+}
+
+template <int KIND>
+__device__ __forceinline__ void dequant_store(const int4 (&v)[kDqUnits], uint8_t* dst, int64_t rs, int n,
+                                              const UnitMap& um, float scale, int lane) {
+#pragma unroll
+  for (int k = 0; k < kDqUnits; ++k) {
+    const int u = k * 32 + lane;
+    if (u >= n) continue;
+    int r, c;
+    um.rc(u, r, c);
+    const uint32_t w[4] = {(uint32_t)v[k].x, (uint32_t)v[k].y, (uint32_t)v[k].z, (uint32_t)v[k].w};
+    float f[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 a = unpack_fp8x2(static_cast<uint16_t>(w[j] & 0xffffu));
+      const float2 b = unpack_fp8x2(static_cast<uint16_t>(w[j] >> 16));
+      f[4 * j + 0] = a.x * scale;
+      f[4 * j + 1] = a.y * scale;
+      f[4 * j + 2] = b.x * scale;
+      f[4 * j + 3] = b.y * scale;
+    }
+    uint8_t* d = dst + r * rs;
+    if (KIND == kDequantF32) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<float4*>(d + c * 64 + q * 16) = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+    } else {
+      uint32_t o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (KIND == kDequantBf16) {
+          __nv_bfloat162 bb = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+          o[j] = *reinterpret_cast<uint32_t*>(&bb);
+        } else {
+          __half2 hh = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+          o[j] = *reinterpret_cast<uint32_t*>(&hh);
+        }
+      }
+      *reinterpret_cast<int4*>(d + c * 32) = make_int4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<int4*>(d + c * 32 + 16) = make_int4(o[4], o[5], o[6], o[7]);
+    }
+  }
+}
+
+struct TilePtrs {
+  const uint8_t* s;
+  uint8_t* d;
+  float* scale;
+};
+
+template <int KIND>
+__device__ __forceinline__ TilePtrs tile_ptrs(const XferParams& P, int64_t t) {
+  const uint32_t t32 = static_cast<uint32_t>(t);
+  const uint32_t q1 = P.fd_heads.div(t32);
+  const int h = static_cast<int>(P.fd_heads.mod(t32, q1));
+  const uint32_t q2 = P.fd_outer.div(q1);
+  const int64_t o = P.fd_outer.mod(q1, q2);
+  const uint32_t q3 = P.fd_layers.div(q2);
+  const int64_t i = P.fd_layers.mod(q2, q3);
+  const int64_t p = q3;
+  TilePtrs r;
+  r.s = chunk_addr(P.src, p, i, o) + static_cast<int64_t>(h + P.src.head_offset) * P.src.head_stride;
+  r.d = const_cast<uint8_t*>(chunk_addr(P.dst, p, i, o)) + static_cast<int64_t>(h + P.dst.head_offset) * P.dst.head_stride;
+  r.scale = (KIND <= kQuantF32) ? scale_addr(P.dst, p, i, o, h + P.dst.head_offset)
+                                : scale_addr(P.src, p, i, o, h + P.src.head_offset);
+  return r;
+}
+
+template <int KIND>
+__device__ __forceinline__ void cast_tiles_pipelined(const XferParams& P, int64_t warp, int64_t nwarps, int lane) {
+  const UnitMap um = unit_map(P.fd_upr);
+  const int units = P.shape.page_size * static_cast<int>(P.fd_upr.d);
+  const int64_t srs = P.src.token_stride, drs = P.dst.token_stride;
+  int64_t t = warp;
+  if (t >= P.total_tiles) return;
+  TilePtrs cur = tile_ptrs<KIND>(P, t);
+  if constexpr (KIND <= kQuantF32) {
+    const int pairs = units / 2;
+    int4 a[kQPairs], b[kQPairs];
+    quant_load<KIND>(cur.s, srs, pairs, um, lane, a, b);
+    while (true) {
+      const int64_t tn = t + nwarps;
+      const bool more = tn < P.total_tiles;
+      TilePtrs nxt{};
+      int4 an[kQPairs], bn[kQPairs];
+      if (more) {
+        nxt = tile_ptrs<KIND>(P, tn);
+        quant_load<KIND>(nxt.s, srs, pairs, um, lane, an, bn);
+      }
+      quant_store<KIND>(a, b, cur.d, drs, pairs, um, cur.scale, lane);
+      if (!more) break;
+#pragma unroll
+      for (int k = 0; k < kQPairs; ++k) a[k] = an[k], b[k] = bn[k];
+      cur = nxt;
+      t = tn;
+    }
+  } else {
+    int4 v[kDqUnits];
+    dequant_load(cur.s, srs, units, um, lane, v);
+    while (true) {
+      const int64_t tn = t + nwarps;
+      const bool more = tn < P.total_tiles;
+      TilePtrs nxt{};
+      int4 vn[kDqUnits];
+      if (more) {
+        nxt = tile_ptrs<KIND>(P, tn);
+        dequant_load(nxt.s, srs, units, um, lane, vn);
+      }
+      dequant_store<KIND>(v, cur.d, drs, units, um, cur.scale ? *cur.scale : 1.0f, lane);
+      if (!more) break;
+#pragma unroll
+      for (int k = 0; k < kDqUnits; ++k) v[k] = vn[k];
+      cur = nxt;
+      t = tn;
+    }
+  }
+}
+
 template <int KIND, int U>
 __device__ __forceinline__ void run_tile(const XferParams& P, const uint8_t* s, int64_t s_rs, uint8_t* d,
                                          int64_t d_rs, int64_t p, int64_t i, int64_t o, int h, int lane) {
@@ -361,6 +550,17 @@ __device__ __forceinline__ void run_tile(const XferParams& P, const uint8_t* s, 
 
 // Warp-per-tile kernel. Tiles are ordered (pair, layer, outer, head) with
 // head fastest so the warps of one CTA sweep one contiguous chunk together.
+// Resident CTAs per SM the pipelined cast kernels are built for (their register budget).
+constexpr int pipe_ctas_per_sm(int kind) { return kind <= kQuantF32 ? 2 : 3; }
+
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, pipe_ctas_per_sm(KIND))
+    kv_cast_pipe_kernel(const __grid_constant__ XferParams P) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
+  cast_tiles_pipelined<KIND>(P, warp, static_cast<int64_t>(gridDim.x) * kWarpsPerCta, lane);
+}
+
 template <int KIND, int U>
 __global__ void __launch_bounds__(kThreads, KIND == kCopy ? 1 : 4) kv_tile_xfer_kernel(const __grid_constant__ XferParams P) {
   const int lane = threadIdx.x & 31;
@@ -447,9 +647,22 @@ int common_align(std::initializer_list<int64_t> xs) {
   return a;
 }
 
+bool g_cast_pipe = true;
+
 template <int KIND, int U>
 cudaError_t launch_tile(const XferParams& P, int max_ctas, cudaStream_t stream) {
   const int64_t ctas_needed = (P.total_tiles + kWarpsPerCta - 1) / kWarpsPerCta;
+  if constexpr (KIND != kCopy) {
+    const int units = P.shape.page_size * static_cast<int>(P.fd_upr.d);
+    const bool fits = (KIND <= kQuantF32) ? units / 2 <= kQPairs * 32 : units <= kDqUnits * 32;
+    if (g_cast_pipe && fits) {
+      // persistent: every warp walks many tiles, so the next tile's loads overlap this one's math
+      const int64_t pcap = max_ctas > 0 ? max_ctas : static_cast<int64_t>(sm_count()) * pipe_ctas_per_sm(KIND);
+      const int pgrid = static_cast<int>(std::max<int64_t>(1, std::min(ctas_needed, pcap)));
+      kv_cast_pipe_kernel<KIND><<<pgrid, kThreads, 0, stream>>>(P);
+      return cudaGetLastError();
+    }
+  }
   int64_t cap = max_ctas > 0 ? max_ctas : static_cast<int64_t>(sm_count()) * 8;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min(ctas_needed, cap)));
   kv_tile_xfer_kernel<KIND, U><<<grid, kThreads, 0, stream>>>(P);
@@ -1018,6 +1231,10 @@ extern "C" int kvbm_xfer_status(int device, int reset) {
   if (reset) *reinterpret_cast<volatile int*>(g_status_host + device) = 0;
   return v;
 }
+
+// 1 (default): fp8 casts whose head tile fits one register batch run the
+// software-pipelined persistent kernel; 0: the one-tile-at-a-time kernel.
+extern "C" void kvbm_xfer_set_cast_pipeline(int on) { g_cast_pipe = on != 0; }
 
 extern "C" void kvbm_xfer_set_wait_limit_ns(uint64_t ns) { g_wait_ns_override = ns; }
 

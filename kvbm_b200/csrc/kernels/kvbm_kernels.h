@@ -109,6 +109,9 @@ int kvbm_xfer_status(int device, int reset);
 // give up at once). Waits that drain copies already issued keep the full
 // limit, so no copy is in flight when a CTA exits.
 void kvbm_xfer_set_wait_limit_ns(uint64_t ns);
+// 1 (default): fp8 casts whose head tile fits one register batch per lane run
+// the software-pipelined persistent cast kernel; 0: the one-tile-at-a-time kernel.
+void kvbm_xfer_set_cast_pipeline(int on);
 
 // Split-by-bytes batched copy of num_pairs (src, dst) regions of equal size.
 // `align` is the alignment (16, 8, 4, 2 or 1) that every pointer and

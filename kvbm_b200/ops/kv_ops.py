@@ -150,6 +150,11 @@ def set_pipeline_wait_limit_ns(ns: int) -> None:
     _lib.load().kvbm_xfer_set_wait_limit_ns(int(ns))
 
 
+def set_cast_pipeline(on: bool) -> None:
+    """fp8 casts: the software-pipelined persistent kernel (default) or the one-tile-at-a-time kernel."""
+    _lib.load().kvbm_xfer_set_cast_pipeline(1 if on else 0)
+
+
 def kv_checksum(layout, ids, *, layer_begin: int = 0, num_layers: int | None = None, head_offset: int = 0,
                 num_heads: int | None = None, stream=None) -> torch.Tensor:
     """Layout-independent 64-bit checksum of each block in ``ids`` (int64 tensor on the device).

@@ -105,9 +105,18 @@ def _ref_quant(x: torch.Tensor):
     return q, scale
 
 
-@pytest.mark.parametrize("engine", ["tile", "tma"])
+@pytest.mark.parametrize("engine", ["tile", "tile1", "tma"])
 @pytest.mark.parametrize("src_dtype", [torch.bfloat16, torch.float16])
 def test_fp8_quant_dequant(engine, src_dtype):
+    # tile: the software-pipelined cast kernel; tile1: the one-tile-at-a-time kernel
+    kv_ops.set_cast_pipeline(engine != "tile1")
+    try:
+        _fp8_roundtrip("tile" if engine == "tile1" else engine, src_dtype)
+    finally:
+        kv_ops.set_cast_pipeline(True)
+
+
+def _fp8_roundtrip(engine, src_dtype):
     cfg = _cfg(dtype=src_dtype)
     cfg8 = _cfg(dtype=torch.float8_e4m3fn)
     src = KvLayout.allocate(cfg, "fully_contiguous", NHD)
