@@ -91,8 +91,12 @@ class OnboardConfig:
 @dataclass
 class ObjectConfig:
     bucket: str = "kvbm"
+    kind: str = "fs"             # fs (a directory standing in for a bucket) | s3 (S3 REST API, SigV4)
     root: str | None = None      # filesystem-backed store root
-    endpoint: str | None = None
+    endpoint: str | None = None  # S3 endpoint URL (MinIO, RGW); None: AWS for `region`
+    region: str = "us-east-1"
+    force_path_style: bool = True
+    max_concurrent_requests: int = 16
     lock: bool = True
 
 
