@@ -13,6 +13,12 @@ kvbm_disk_cache_hit_rate, kvbm_object_cache_hit_rate,
 kvbm_inactive_pool_size, kvbm_reset_pool_size, kvbm_inflight_mutable,
 kvbm_inflight_immutable, kvbm_transfer_duration_seconds,
 kvbm_transfer_inflight, kvbm_transfer_failures_total, kvbm_cd_*.
+
+``StatsCollector`` turns one pool's cumulative counters into a rolling window
+of derived figures (allocation and eviction rates per second and their
+change per second, match and scan hit ratios over the interval, pool
+occupancy), sampled on demand or by a daemon thread (parity:
+crates/kvbm-observability/src/stats.rs:18-200).
 """
 
 from __future__ import annotations
@@ -20,6 +26,7 @@ from __future__ import annotations
 import threading
 import time
 from collections import deque
+from dataclasses import dataclass
 
 from prometheus_client import CollectorRegistry, start_http_server
 from prometheus_client.core import CounterMetricFamily, GaugeMetricFamily, HistogramMetricFamily
@@ -158,6 +165,98 @@ class KvbmCollector:
         bt = GaugeMetricFamily("kvbm_cd_breaker_tier", "prefill-router breaker tier (0 calm, 1 warm, 2 hot)")
         bt.add_metric([], self.cd.breaker_tier)
         yield bt
+
+
+@dataclass(frozen=True)
+class StatsSnapshot:
+    allocation_rate: float = 0.0      # blocks allocated per second over the last interval
+    eviction_rate: float = 0.0
+    match_hit_rate: float = 0.0       # blocks returned / hashes requested by prefix matches in the interval
+    scan_hit_rate: float = 0.0
+    allocation_gradient: float = 0.0  # change of allocation_rate per second
+    eviction_gradient: float = 0.0
+    inflight_mutable: int = 0
+    inflight_immutable: int = 0
+    reset_pool_size: int = 0
+    inactive_pool_size: int = 0
+
+
+class StatsCollector:
+    """Rolling window of derived pool statistics. Disabled until ``set_enabled(True)``; ``sample``
+    is then cheap (one counter read) and may be called from any thread."""
+
+    def __init__(self, manager, window_size: int = 60, sample_interval_s: float = 1.0, clock=time.monotonic):
+        self.mgr = manager
+        self.window_size, self.interval = int(window_size), float(sample_interval_s)
+        self._clock = clock
+        self._enabled = False
+        self._entries: deque = deque(maxlen=self.window_size)
+        self._lock = threading.Lock()
+        self._thread: threading.Thread | None = None
+        self._stop = threading.Event()
+
+    def set_enabled(self, on: bool) -> None:
+        self._enabled = bool(on)
+
+    def is_enabled(self) -> bool:
+        return self._enabled
+
+    def _raw(self) -> dict:
+        m = dict(self.mgr.metrics())
+        m["inflight_immutable"] = self.mgr.active_len()
+        m["reset_pool_size"] = self.mgr.reset_len()
+        m["inactive_pool_size"] = self.mgr.inactive_len()
+        m["inflight_mutable"] = max(0, self.mgr.total_blocks() - m["inflight_immutable"] - m["reset_pool_size"]
+                                    - m["inactive_pool_size"])
+        return m
+
+    def sample(self) -> StatsSnapshot | None:
+        if not self._enabled:
+            return None
+        now, raw = self._clock(), self._raw()
+        occ = {k: raw[k] for k in ("inflight_mutable", "inflight_immutable", "reset_pool_size", "inactive_pool_size")}
+        with self._lock:
+            prev = self._entries[-1] if self._entries else None
+            dt = now - prev[0] if prev else 0.0
+            if prev is None or dt <= 0:
+                st = StatsSnapshot(**occ)
+            else:
+                p, ps = prev[1], prev[2]
+
+                def ratio(req, ret):
+                    dq = raw[req] - p[req]
+                    return (raw[ret] - p[ret]) / dq if dq > 0 else 0.0
+
+                ar = (raw["allocations"] - p["allocations"]) / dt
+                er = (raw["evictions"] - p["evictions"]) / dt
+                st = StatsSnapshot(ar, er, ratio("match_hashes_requested", "match_blocks_returned"),
+                                   ratio("scan_hashes_requested", "scan_blocks_returned"),
+                                   (ar - ps.allocation_rate) / dt, (er - ps.eviction_rate) / dt, **occ)
+            self._entries.append((now, raw, st))
+        return st
+
+    def latest(self) -> StatsSnapshot | None:
+        with self._lock:
+            return self._entries[-1][2] if self._entries else None
+
+    def window(self, n: int) -> list[StatsSnapshot]:
+        """The last ``n`` snapshots, oldest first."""
+        with self._lock:
+            return [e[2] for e in list(self._entries)[-n:]] if n > 0 else []
+
+    def spawn(self) -> threading.Thread:
+        """Sample every ``sample_interval_s`` on a daemon thread until ``stop``."""
+        def loop():
+            while not self._stop.wait(self.interval):
+                self.sample()
+        self._thread = threading.Thread(target=loop, name="kvbm-stats", daemon=True)
+        self._thread.start()
+        return self._thread
+
+    def stop(self) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
 
 
 def make_registry(collector: KvbmCollector) -> CollectorRegistry:
