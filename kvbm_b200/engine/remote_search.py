@@ -20,6 +20,9 @@ Holder side (:class:`RemoteHolder`) handlers on the instance messenger:
 * ``kvbm.remote.read``  {sid, worker, first, count} -> canonical bytes
 * ``kvbm.remote.close`` {sid}
 
+Initiator side handler: ``kvbm.remote.pull_from`` {holder, hashes, session?}
+(an operator's ``kvbmctl p2p pull`` / ``xfer``).
+
 Initiator side (:class:`RemoteSearch`): ``search`` (hub query, self
 filtered, decimated for long prompts), ``pull`` (session + copy + register)
 and ``start`` (the same on a background thread, one future per request).
@@ -49,6 +52,7 @@ from ..physical.layout import KvBlockLayout, KvLayout, LayoutConfig, LayoutDescr
 from ..utils.tracing import audit
 
 OPEN, READ, CLOSE = "kvbm.remote.open", "kvbm.remote.read", "kvbm.remote.close"
+PULL = "kvbm.remote.pull_from"
 
 
 @dataclass
@@ -167,6 +171,7 @@ class RemoteSearch:
         self._pool = cf.ThreadPoolExecutor(max_workers=2, thread_name_prefix="kvbm-remote")
         self._mapped: dict[str, KvLayout] = {}
         self.stats = {"searches": 0, "hits": 0, "pulled_blocks": 0, "bytes": 0, "rpc_reads": 0}
+        messenger.register_handler(PULL, self._pull_rpc)
 
     # -------------------------------------------------------------- search
     def _query_set(self, hashes: list[int]) -> list[int]:
@@ -198,54 +203,74 @@ class RemoteSearch:
 
     # ---------------------------------------------------------------- pull
     def pull(self, holder: int, hashes: list[int]) -> int:
-        """Copy the holder's blocks for ``hashes`` (a prefix of them) into local G2; returns blocks registered."""
-        peer = self.hub.peer(holder)
-        addr = peer["address"]
+        """Copy the holder's blocks for ``hashes`` (a prefix of them) into local G2; returns blocks registered.
+        Opens a session on the holder (it pins the blocks), copies, and closes it."""
+        addr = self.hub.peer(holder)["address"]
         resp = self.messenger.call(addr, OPEN, {"initiator": str(self.leader.instance_id),
                                                 "hashes": [str(h) for h in hashes]},
                                    timeout=self.config.timeout)
         sid = resp.get("sid")
         if sid is None:
             return 0
-        audit("transfer_pull_started", session=sid, source=str(holder), blocks=len(resp["block_ids"]))
         try:
-            n = len(resp["block_ids"])
-            got = self.leader.g2.allocate_blocks_with_evictions(n)
-            if got is None:
-                return 0
-            dst, _ = got
-            dst_ids = [b.block_id for b in dst]
-            pools = resp["pools"]
-            if len(pools) != len(self.layouts):
-                raise ValueError(f"holder has {len(pools)} workers, this instance {len(self.layouts)}")
-            for w, (pd, mine) in enumerate(zip(pools, self.layouts)):
-                src = self._mapped.get(pd["extra"].get("shm_path") or "")
-                if src is None:
-                    src = _map_pool(pd)
-                    if src is not None:
-                        self._mapped[pd["extra"]["shm_path"]] = src
-                if src is not None:
-                    mine.scatter_blocks(dst_ids, src.gather_blocks(resp["block_ids"]))
-                else:
-                    raw = self.messenger.call(addr, READ, {"sid": sid, "worker": w, "first": 0, "count": n},
-                                              timeout=self.config.timeout)
-                    self.stats["rpc_reads"] += 1
-                    c = mine.config
-                    shape = (n, c.num_layers, c.outer_dim, c.page_size, c.num_heads, c.head_dim)
-                    buf = torch.frombuffer(bytearray(raw), dtype=torch.uint8)
-                    data = buf.view(torch.uint8 if mine.dtype in (torch.uint8, torch.float8_e4m3fn)
-                                    else mine.dtype).view(shape)
-                    mine.scatter_blocks(dst_ids, data)
-                self.stats["bytes"] += n * mine.config.bytes_per_block
-            registered = self.leader.g2.register_mutable(dst, hashes[:n])
-            for b in registered:
-                b.release()  # now an inactive (matchable) G2 block
-            self.stats["pulled_blocks"] += n
-            self.stats["hits"] += 1
-            audit("transfer_pull_completed", session=sid, pulled=n)
-            return n
+            return self.pull_from_session(holder, resp, hashes, addr=addr)
         finally:
             self.messenger.call(addr, CLOSE, {"sid": sid}, timeout=self.config.timeout)
+
+    def _pull_rpc(self, req: dict) -> dict:
+        """``kvbm.remote.pull_from`` {holder, hashes, session?}: with ``session`` (the holder's open
+        response) copy from that pinned session and leave it open, else pin + copy + unpin."""
+        hashes = [int(h) for h in req["hashes"]]
+        holder = int(req["holder"])
+        if req.get("session"):
+            n = self.pull_from_session(holder, req["session"], hashes)
+        else:
+            n = self.pull(holder, hashes)
+        return {"pulled": n}
+
+    def pull_from_session(self, holder: int, resp: dict, hashes: list[int], addr: str | None = None) -> int:
+        """Copy the blocks of an open session (the holder's open response) into local G2 and register
+        them under ``hashes``; the session stays open."""
+        sid = resp.get("sid")
+        if sid is None:
+            return 0
+        addr = addr or self.hub.peer(holder)["address"]
+        audit("transfer_pull_started", session=sid, source=str(holder), blocks=len(resp["block_ids"]))
+        n = len(resp["block_ids"])
+        got = self.leader.g2.allocate_blocks_with_evictions(n)
+        if got is None:
+            return 0
+        dst, _ = got
+        dst_ids = [b.block_id for b in dst]
+        pools = resp["pools"]
+        if len(pools) != len(self.layouts):
+            raise ValueError(f"holder has {len(pools)} workers, this instance {len(self.layouts)}")
+        for w, (pd, mine) in enumerate(zip(pools, self.layouts)):
+            src = self._mapped.get(pd["extra"].get("shm_path") or "")
+            if src is None:
+                src = _map_pool(pd)
+                if src is not None:
+                    self._mapped[pd["extra"]["shm_path"]] = src
+            if src is not None:
+                mine.scatter_blocks(dst_ids, src.gather_blocks(resp["block_ids"]))
+            else:
+                raw = self.messenger.call(addr, READ, {"sid": sid, "worker": w, "first": 0, "count": n},
+                                          timeout=self.config.timeout)
+                self.stats["rpc_reads"] += 1
+                c = mine.config
+                shape = (n, c.num_layers, c.outer_dim, c.page_size, c.num_heads, c.head_dim)
+                buf = torch.frombuffer(bytearray(raw), dtype=torch.uint8)
+                data = buf.view(torch.uint8 if mine.dtype in (torch.uint8, torch.float8_e4m3fn)
+                                else mine.dtype).view(shape)
+                mine.scatter_blocks(dst_ids, data)
+            self.stats["bytes"] += n * mine.config.bytes_per_block
+        registered = self.leader.g2.register_mutable(dst, hashes[:n])
+        for b in registered:
+            b.release()  # now an inactive (matchable) G2 block
+        self.stats["pulled_blocks"] += n
+        self.stats["hits"] += 1
+        audit("transfer_pull_completed", session=sid, pulled=n)
+        return n
 
     def find_and_pull(self, hashes: list[int]) -> int:
         found = self.search(hashes)

@@ -128,6 +128,7 @@ class DebugConfig:
 class HubConfig:
     url: str | None = None
     heartbeat_secs: float = 5.0
+    features: list[str] = field(default_factory=list)  # hub features this connector takes part in
 
 
 @dataclass

@@ -102,3 +102,44 @@ def test_warm_and_unknown_prefixes_skip_or_miss(hub):
         rs.close()
     finally:
         a.close()
+
+
+def test_kvbmctl_p2p_pin_pull_unpin_and_xfer(hub, capsys):
+    import json
+
+    from kvbm_b200.hub.kvbmctl import main as kvbmctl
+
+    c = HubClient(hub.url)
+    a = _Instance(401, c, KvBlockLayout.OPERATIONAL_NHD)
+    b = _Instance(402, c, KvBlockLayout.OPERATIONAL_HND)
+    try:
+        hashes = sequence_hashes(list(range(500, 500 + 4 * BS)), BS)
+        blocks = a.g2.allocate_blocks(4)
+        fill_blocks(a.layout, [x.block_id for x in blocks], FillPattern.RANDOM, seed=3)
+        imm = a.g2.register_mutable(blocks, hashes)
+        want = checksum_blocks(a.layout, [x.block_id for x in imm])
+        for x in imm:
+            x.release()
+        rs = RemoteSearch(b.leader, [b.layout], b.msg, c, BS, RemoteSearchConfig(enabled=True))
+        hs = ",".join(hex(h) for h in hashes[:2])
+        assert kvbmctl(["--hub", hub.url, "--json", "p2p", "pin", "--instance-id", "401", "--hashes", hs]) == 0
+        pin = json.loads(capsys.readouterr().out)
+        assert pin["sid"] is not None and len(pin["block_ids"]) == 2 and a.holder.open_sessions() == 1
+        assert kvbmctl(["--hub", hub.url, "--json", "p2p", "pull", "--from", "401", "--to", "402",
+                        "--session", json.dumps(pin)]) == 0
+        assert json.loads(capsys.readouterr().out) == {"pulled": 2}
+        assert a.holder.open_sessions() == 1  # pull leaves the session pinned
+        assert kvbmctl(["--hub", hub.url, "--json", "p2p", "unpin", "--instance-id", "401",
+                        "--session", pin["sid"]]) == 0
+        capsys.readouterr()
+        assert a.holder.open_sessions() == 0
+        assert kvbmctl(["--hub", hub.url, "--json", "p2p", "xfer", "--from", "401", "--to", "402",
+                        "--hashes", ",".join(hex(h) for h in hashes)]) == 0
+        assert json.loads(capsys.readouterr().out) == {"pulled": 4}
+        got = b.g2.match_blocks(hashes)
+        assert checksum_blocks(b.layout, [x.block_id for x in got]) == want
+        assert a.holder.open_sessions() == 0
+        rs.close()
+    finally:
+        a.close()
+        b.close()

@@ -87,6 +87,35 @@ def test_kvbmctl_renders(hub, capsys):
     assert "INSTANCE_ID" in capsys.readouterr().out
 
 
+def test_kvbmctl_renders_the_vllm_flags(hub, capsys):
+    import json
+    import shlex
+
+    from kvbm_b200.hub.kvbmctl import render_vllm_cli
+
+    assert kvbmctl(["--hub", hub.url, "config", "vllm", "--features", "disagg", "--role", "decode",
+                    "--kvbm", "cache.host.cache_size_gb=4", "--kvbm-config", '{"disagg": {"role": "prefill"}}']) == 0
+    line = capsys.readouterr().out.strip()
+    toks = shlex.split(line)
+    assert toks[:4] == ["--block-size", "16", "--max-model-len", "4096"]
+    ktc = json.loads(toks[toks.index("--kv-transfer-config") + 1])
+    extra = ktc["kv_connector_extra_config"]
+    assert ktc["kv_connector"] == "KvbmConnector" and ktc["kv_load_failure_policy"] == "recompute"
+    assert extra["hub"] == {"url": hub.url, "features": ["p2p", "disagg"]}  # dependency pulled in, no router
+    assert extra["disagg"]["role"] == "decode"  # the hub-owned role wins over --kvbm-config
+    assert extra["cache"]["host"]["cache_size_gb"] == 4
+    cfg = {"features": ["indexer", "p2p", "disagg", "prefill_router"], "block_size": 16}
+    pre = render_vllm_cli(cfg, "http://h'x", ["disagg"], "prefill")
+    assert "prefill_router" in pre and "'\\''" in pre  # router for a prefill role; quote escaped
+    with pytest.raises(ValueError):
+        render_vllm_cli(cfg, "u", ["disagg"], None)      # disagg needs a role
+    with pytest.raises(ValueError):
+        render_vllm_cli({"features": ["indexer"]}, "u", ["p2p"])  # not enabled on the hub
+    with pytest.raises(ValueError):
+        render_vllm_cli(cfg, "u", [], None, ["cache.nope=1"])  # the config loader rejects unknown keys
+    assert kvbmctl(["--hub", hub.url, "config", "vllm", "--features", "bogus"]) == 2
+
+
 def test_selector_and_breaker():
     s = Selector(max_inflight=1)
     s.add_worker(1)
