@@ -194,6 +194,17 @@ class ConnectorLeader:
             workers = SpmdParallelWorkers(self.runtime.messenger, [self._workers[r][0] for r in sorted(self._workers)])
         self._impl = _Leader(InstanceLeader(g2, workers, g3=g3), self.block_size,
                              offload_enabled=layout.get("g2_blocks", 0) > 0, num_workers=max(1, len(self._workers)))
+        # operator / peer control plane on the runtime's messenger (describe, reset, metrics)
+        import dataclasses
+        import json
+
+        from .engine.control import LeaderControl
+
+        plain = json.loads(json.dumps(dataclasses.asdict(cfg), default=str))
+        self.control = LeaderControl(self._impl.leader, self.runtime.messenger, self.block_size,
+                                     role=(plain.get("disagg") or {}).get("role"), config=plain,
+                                     parallelism={"workers": max(1, len(self._workers))},
+                                     cd_stats=lambda: self._impl.cd_stats)
 
     def _need(self) -> _Leader:
         if self._impl is None:

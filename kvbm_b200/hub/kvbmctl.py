@@ -9,6 +9,7 @@
     kvbmctl --hub URL p2p pull  --from H --to P --session JSON [--hashes ...]
     kvbmctl --hub URL p2p unpin --instance-id H --session SID
     kvbmctl --hub URL p2p xfer  --from H --to P --hashes h1,h2,...
+    kvbmctl --hub URL control --instance-id I modules | describe | metrics | reset [--tiers g2,g3]
 
 ``config vllm`` renders the vLLM flags that connect an engine to this hub:
 the hub's block size and maximum sequence length, and a
@@ -21,6 +22,10 @@ each ``--kvbm path=value``; the hub-owned fields (hub URL and features,
 disaggregation role) are applied last and always win. The result is checked
 by loading it as a block-manager configuration.
 
+``control`` calls an instance leader's control plane (its messenger
+address comes from the hub): the modules it serves, its description, a
+metrics snapshot, or a reset of its cached (inactive) G2/G3 blocks.
+
 ``p2p`` drives the remote-search transfer sessions by hand: ``pin`` opens a
 session on a holder (its blocks stay pinned), ``pull`` makes another
 instance copy a pinned session's blocks into its G2, ``unpin`` closes the
@@ -28,7 +33,8 @@ session, ``xfer`` does all three.
 
 Parity: crates/kvbm-hub/src/bin/kvbmctl.rs, render.rs:82-300
 (resolve_features, render_vllm_cli, shell quoting), features/p2p/cli.rs
-(pin / pull / unpin / xfer).
+(pin / pull / unpin / xfer), kvbm-protocols/src/control/client.rs (the
+leader control client).
 """
 
 from __future__ import annotations
@@ -180,6 +186,24 @@ def run_p2p(a, client: HubClient) -> dict:
         m.close()
 
 
+def run_control(a, client: HubClient):
+    from ..engine.control import LeaderControlClient
+    from ..runtime.messenger import Messenger
+
+    m = Messenger(instance_id=0)
+    try:
+        ctl = LeaderControlClient(m, client.peer(a.instance_id)["address"], timeout=a.timeout)
+        if a.action == "modules":
+            return {"modules": ctl.list_modules()}
+        if a.action == "describe":
+            return ctl.describe()
+        if a.action == "metrics":
+            return ctl.metrics()
+        return ctl.reset([t for t in a.tiers.split(",") if t] if a.tiers else None)
+    finally:
+        m.close()
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(prog="kvbmctl")
     p.add_argument("--hub", default="http://127.0.0.1:1337")
@@ -215,6 +239,11 @@ def main(argv=None) -> int:
         if name in ("pull", "unpin"):
             s.add_argument("--session", required=True, help="unpin: the session id; pull: pin's JSON output")
         s.add_argument("--hashes", default=None, required=name in ("pin", "xfer"))
+    ct = sub.add_parser("control")
+    ct.add_argument("--instance-id", type=int, required=True)
+    ct.add_argument("--timeout", type=float, default=10.0)
+    ct.add_argument("action", choices=["modules", "describe", "metrics", "reset"])
+    ct.add_argument("--tiers", default=None, help="reset: comma list of g2,g3 (default: every configured tier)")
     a = p.parse_args(argv)
     client = HubClient(a.hub)
     if a.cmd == "health":
@@ -239,6 +268,14 @@ def main(argv=None) -> int:
         out = rows
     elif a.cmd == "query":
         out = client.query([int(h, 0) for h in a.hashes])
+    elif a.cmd == "control":
+        from ..engine.control import ControlError
+
+        try:
+            out = run_control(a, client)
+        except ControlError as e:
+            print(f"kvbmctl: {e}", file=sys.stderr)
+            return 2
     elif a.cmd == "p2p":
         out = run_p2p(a, client)
         if a.p2p == "pin" and out.get("sid") is not None:

@@ -122,6 +122,20 @@ def test_core_surface_leader_from_layout():
         meta = ConnectorMetadata.decode(leader.build_connector_metadata(so))
         assert meta.offload[0].g1_ids == [4, 5, 6]
         assert kc.hub.CompletionEvent is not None
+        # the leader's control plane answers on the runtime's messenger
+        from kvbm_b200.engine.control import LeaderControlClient
+        from kvbm_b200.runtime.messenger import Messenger
+
+        m = Messenger()
+        try:
+            ctl = LeaderControlClient(m, addr)
+            assert ctl.list_modules() == ["core", "dev", "metrics"]
+            d = ctl.describe()
+            assert d["block_size"] == 16 and d["tier_capacity"] == [{"tier": "g2", "total_blocks": 32}]
+            assert d["config"]["cache"]["host"]["num_blocks"] == 32
+            assert ctl.metrics()["pools"][0]["total_blocks"] == 32
+        finally:
+            m.close()
     finally:
         rt.shutdown()
 

@@ -143,3 +143,64 @@ def test_kvbmctl_p2p_pin_pull_unpin_and_xfer(hub, capsys):
     finally:
         a.close()
         b.close()
+
+
+def test_leader_control_plane_modules(hub):
+    from kvbm_b200.engine.control import ControlError, LeaderControl, LeaderControlClient, plan_reset
+
+    assert plan_reset(None, {"g2"}) == (["g2"], ["g3"])
+    assert plan_reset(["g2", "g2"], {"g2", "g3"}) == (["g2"], [])
+    with pytest.raises(ControlError) as e:
+        plan_reset(["g2", "g3"], {"g2"})
+    assert e.value.kind == "tier_not_configured"
+    c = HubClient(hub.url)
+    a = _Instance(501, c, KvBlockLayout.OPERATIONAL_NHD)
+    b = _Instance(502, c, KvBlockLayout.OPERATIONAL_NHD)
+    try:
+        rs = RemoteSearch(b.leader, [b.layout], b.msg, c, BS, RemoteSearchConfig(enabled=True))
+        LeaderControl(a.leader, a.msg, BS, [{"g2": a.layout}], holder=a.holder, search=None, role="decode",
+                      parallelism={"tp": 1})
+        ctl_b = LeaderControl(b.leader, b.msg, BS, [{"g2": b.layout}], holder=b.holder, search=rs)
+        cli_a, cli_b = LeaderControlClient(b.msg, a.msg.address), LeaderControlClient(a.msg, b.msg.address)
+        assert cli_a.list_modules() == ["core", "dev", "metrics"]
+        assert cli_b.list_modules() == ["core", "dev", "metrics", "transfer"] == ctl_b.modules
+        d = cli_a.describe()
+        assert d["instance_id"] == "501" and d["block_size"] == BS and d["role"] == "decode"
+        assert d["tier_capacity"] == [{"tier": "g2", "total_blocks": 32}]
+        assert d["workers"][0]["layouts"][0]["config"]["num_blocks"] == 32
+        hashes = sequence_hashes(list(range(700, 700 + 3 * BS)), BS)
+        imm = a.g2.register_mutable(a.g2.allocate_blocks(3), hashes)
+        for x in imm:
+            x.release()
+        c.publish_events(a.iid, [("create", hashes)])
+        m = cli_a.metrics()
+        assert m["pools"][0]["inactive_blocks"] == 3 and m["sessions_inflight"] == 0
+        assert cli_b.search_prefix(hashes) == {"local_g2_blocks": 0, "remote": {"holder": 501, "blocks": 3}}
+        # transfer module under its control-plane names: pin on A, pull into B, unpin
+        with pytest.raises(ControlError) as e:
+            cli_a.open_session(hashes)  # A offers no transfer module
+        assert e.value.kind == "module_not_offered"
+        opened = LeaderControlClient(a.msg, b.msg.address)  # B's own holder has nothing to pin
+        assert opened.open_session(hashes)["sid"] is None
+        assert cli_b.pull_from_session(501, {}, hashes) == {"pulled": 3}  # no session: pin + pull + unpin
+        assert b.g2.count_prefix(hashes) == 3
+        import json
+
+        from kvbm_b200.hub.kvbmctl import main as kvbmctl
+
+        assert kvbmctl(["--hub", hub.url, "--json", "control", "--instance-id", "501", "modules"]) == 0
+        assert kvbmctl(["--hub", hub.url, "control", "--instance-id", "501", "reset", "--tiers", "g3"]) == 2
+        assert kvbmctl(["--hub", hub.url, "--json", "control", "--instance-id", "501", "reset"]) == 0
+        assert a.g2.inactive_len() == 0
+        imm = a.g2.register_mutable(a.g2.allocate_blocks(1), hashes[:1])
+        imm[0].release()
+        r = cli_a.reset()
+        assert r == {"reset": ["g2"], "failed": [], "skipped_unconfigured": ["g3"]}
+        assert a.g2.inactive_len() == 0
+        with pytest.raises(ControlError) as e:
+            cli_a.reset(["g3"])
+        assert e.value.kind == "tier_not_configured"
+        rs.close()
+    finally:
+        a.close()
+        b.close()
