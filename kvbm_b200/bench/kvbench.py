@@ -90,6 +90,13 @@ def run(args) -> list[dict]:
                     if engine == "ce":
                         sp, dp, sz = _ce_regions(a, ai.tolist(), b, bi.tolist())
                         fn = lambda sp=sp, dp=dp, sz=sz: kv_ops.memcpy_pairs_ce(sp, dp, sz)
+                    elif engine == "ce_graph":
+                        # the same copy-engine regions captured once as a graph of memcpy nodes, replayed
+                        sp, dp, sz = _ce_regions(a, ai.tolist(), b, bi.tolist())
+                        g = torch.cuda.CUDAGraph()
+                        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                            kv_ops.memcpy_pairs_ce(sp, dp, sz, stream=torch.cuda.current_stream())
+                        fn = g.replay
                     else:
                         fn = lambda a=a, ai=ai, b=b, bi=bi, engine=engine: kv_ops.kv_transfer(
                             a, ai, b, bi, engine=engine, max_ctas=args.max_ctas)
@@ -171,7 +178,7 @@ def main(argv=None):
     p.add_argument("--page", type=int, default=16)
     p.add_argument("--batches", default="1,8,64,512")
     p.add_argument("--layouts", default="fc,lw")
-    p.add_argument("--engines", default="tile,tma,ce")
+    p.add_argument("--engines", default="tile,tma,ce", help="tile, tile1, tma, ce, ce_graph")
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--max-ctas", type=int, default=0)
