@@ -24,6 +24,7 @@ from __future__ import annotations
 import asyncio
 import collections
 import json
+import os
 import threading
 import time
 
@@ -38,15 +39,9 @@ DEFAULT_DISCOVERY_PORT = 1337
 DEFAULT_CONTROL_PORT = 8337
 DISPATCH_HANDLER = "kvbm.prefill_router.dispatch"
 
-STATUS_PAGE = """<!doctype html><html><head><title>kvbm hub</title>
-<style>body{font-family:sans-serif;margin:2em}td,th{padding:4px 10px;border-bottom:1px solid #ddd}</style></head>
-<body><h2>kvbm hub</h2><div id=s></div><table id=t><tr><th>instance</th><th>role</th><th>features</th>
-<th>address</th></tr></table><script>
-fetch('/v1/instances').then(r=>r.json()).then(d=>{const t=document.getElementById('t');
-for(const i of d.instances){const r=t.insertRow();[i.instance_id,i.role,i.features.join(','),i.address]
-.forEach(v=>r.insertCell().textContent=v)}});
-fetch('/v1/config').then(r=>r.json()).then(c=>document.getElementById('s').textContent=JSON.stringify(c));
-</script></body></html>"""
+WEB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "web")
+WEB_ASSETS = {"/": ("index.html", "text/html"), "/app.js": ("app.js", "application/javascript"),
+              "/style.css": ("style.css", "text/css")}
 
 
 def _h(x) -> int:
@@ -90,7 +85,8 @@ class HubServer:
     def app(self) -> web.Application:
         a = web.Application()
         r = a.router
-        r.add_get("/", self._index_page)
+        for path in WEB_ASSETS:
+            r.add_get(path, self._asset)
         r.add_get("/health", self._health)
         r.add_get("/v1/config", self._config)
         r.add_post("/v1/instances", self._register)
@@ -121,8 +117,10 @@ class HubServer:
     async def _targets(self, req):
         return web.json_response({"targets": self.selector.targets()})
 
-    async def _index_page(self, req):
-        return web.Response(text=STATUS_PAGE, content_type="text/html")
+    async def _asset(self, req):
+        name, ctype = WEB_ASSETS[req.path]
+        with open(os.path.join(WEB_DIR, name), encoding="utf-8") as f:
+            return web.Response(text=f.read(), content_type=ctype)
 
     async def _config(self, req):
         return web.json_response({"block_size": self.block_size, "max_seq_len": self.max_seq_len,
@@ -133,7 +131,8 @@ class HubServer:
 
     def control_app(self) -> web.Application:
         a = web.Application()
-        a.router.add_get("/", self._index_page)
+        for path in WEB_ASSETS:
+            a.router.add_get(path, self._asset)
         a.router.add_get("/health", self._health)
         a.router.add_get("/v1/config", self._config)
         a.router.add_get("/v1/metrics", self._metrics)

@@ -312,3 +312,14 @@ def test_runtime_registers_with_hub_and_static_peers():
         assert rt.messenger.instance_id not in {int(i["instance_id"]) for i in HubClient(h.url).instances()}
     finally:
         h.stop()
+
+
+def test_hub_serves_its_web_ui(hub):
+    import requests
+
+    page = requests.get(hub.url + "/", timeout=5)
+    assert page.status_code == 200 and "text/html" in page.headers["content-type"]
+    assert '<script src="/app.js">' in page.text
+    js = requests.get(hub.url + "/app.js", timeout=5)
+    assert js.status_code == 200 and "/v1/instances" in js.text and "javascript" in js.headers["content-type"]
+    assert requests.get(hub.url + "/style.css", timeout=5).headers["content-type"].startswith("text/css")
