@@ -255,3 +255,51 @@ def test_tensor_parallel_ranks_run_the_scheduling_rank_plans():
     assert res[0][1] == res[1][1] > 0
     assert sorted(res[0][2]) == [[7, 1020, 1021], [7, 1021, 1022], [7, 1022, 1023]]
     assert res[1][2] == []
+
+
+class TimeoutWorker(FakeWorker):
+    """A decode worker whose mailbox word never lands: after ``polls`` get_finished calls it reports
+    the receive done with the request's blocks as load errors (what the real worker does when the
+    receive timeout expires)."""
+
+    def __init__(self, instance, polls=3):
+        super().__init__(instance)
+        self.polls, self.seen, self.errors = polls, {}, set()
+
+    def get_finished(self, finished):
+        recving = set()
+        for r, op in list(self.pending_recv.items()):
+            self.seen[r] = self.seen.get(r, 0) + 1
+            if self.seen[r] >= self.polls:
+                recving.add(r)
+                self.errors.update(op.g1_ids)
+                del self.pending_recv[r]
+        return set(finished), recving
+
+    def get_block_ids_with_load_errors(self):
+        out, self.errors = self.errors, set()
+        return out
+
+
+def test_dropped_remote_prefill_times_out_and_is_recomputed_locally():
+    """The prefill instance never serves the dispatch (the message is dropped): the decode worker's
+    receive gives up, reports the blocks as load errors, the engine prefills the prompt itself and the
+    leader frees the in-flight budget and the mailbox slot."""
+    plane = LocalPrefillPlane()
+    dl = ConnectorLeader(InstanceLeader(BlockManager(1, 16, "lru", Tier.G2), ParallelWorkers([])), 16,
+                         offload_enabled=False, cd=ConditionalDisagg(SelectionPolicy("always"), InflightBudget(2)),
+                         plane=plane, prefill_target=2, instance_id=1, mailbox_slots=2)
+    model = FakeModel()
+    dec = E.LLMEngine(model, E.EngineConfig(num_gpu_blocks=64, max_num_seqs=2, max_model_len=256, max_tokens=3,
+                                            use_graphs=False), dl, TimeoutWorker(1))
+    r = E.Request("lost", torch.arange(40, dtype=torch.int32), max_tokens=3)
+    dec.add_request(r)
+    for _ in range(50):
+        dec.step()
+        if not dec.has_unfinished():
+            break
+    assert len(plane.poll(2)) == 1  # it was dispatched, and nobody served it
+    assert r.status == E.RequestStatus.FINISHED and r.load_failed
+    assert model.prefills == [(40, 0)] and dec.stats["recomputed"] == 1
+    assert r.output.tolist() == [7, 1040, 1041]
+    assert dl.cd.budget.inflight == 0 and len(dl._mailbox_free) == 2 and dl.cd_stats["failed"] == 1
