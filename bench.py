@@ -111,6 +111,8 @@ def main(argv=None) -> int:
     p.add_argument("--layer-batch", type=int, default=8, help="layers per push launch")
     p.add_argument("--layers", type=int, default=None, help="override layer count (debug only: invalid for the metric)")
     p.add_argument("--no-graphs", action="store_true")
+    p.add_argument("--no-bulk-peer", action="store_true",
+                   help="peer pushes with consumer-warp stores instead of TMA bulk stores")
     p.add_argument("--out", default=None)
     args = p.parse_args(argv)
     if args.impl == "reference":
@@ -143,7 +145,8 @@ def main(argv=None) -> int:
         gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=600))
     mcfg = LlamaConfig.llama3_8b() if not args.layers else LlamaConfig(layers=args.layers)
     cfg = PdConfig(model=mcfg, concurrency=args.concurrency, prompt_len=args.prompt_len, gen_len=args.gen_len,
-                   layer_batch=args.layer_batch, push_engine=args.engine, use_graphs=not args.no_graphs)
+                   layer_batch=args.layer_batch, push_engine=args.engine, use_graphs=not args.no_graphs,
+                   push_bulk_peer=not args.no_bulk_peer)
     C = cfg.concurrency
     half = world // 2
     model = LlamaModel(mcfg, torch.device("cuda", local), seed=cfg.seed)
@@ -206,9 +209,11 @@ def main(argv=None) -> int:
         if k not in submitted:
             submit(k)
         while not wave_done(k):
-            if pre is not None:  # colocated: serve the local plane first
+            if pre is not None:
+                # colocated: one prefill step (one request's prompt, pushed layer batch by layer batch),
+                # then one decode step, so a request starts decoding as soon as its KV has landed
                 pre.pull()
-                while pre.engine.has_unfinished():
+                if pre.engine.has_unfinished() or pre.engine._delayed:
                     pre.step()
             dec.step()
             if (role == "decode" and k + 1 < total and k + 1 != args.warmup and k + 1 not in submitted
@@ -297,7 +302,7 @@ def main(argv=None) -> int:
                 "seq_len": cfg.prompt_len,
                 "gen_len": cfg.gen_len,
                 "parallelism": "colocated" if world == 1 else f"{pairs}P{pairs}D tp1",
-                "push_engine": cfg.push_engine,
+                "push_engine": cfg.push_engine, "push_bulk_peer": cfg.push_bulk_peer,
                 "layer_batch": cfg.layer_batch,
                 "cd_policy": cfg.selection,
                 "prefill_attention": model.attention_backend,

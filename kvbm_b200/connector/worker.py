@@ -114,6 +114,7 @@ class ConnectorWorker:
         # conditional disaggregation
         self.layer_batch = max(1, int(self.config.transfer.layer_batch))
         self.push_engine = self.config.transfer.push_engine
+        self.push_bulk_peer = self.config.transfer.push_bulk_peer
         self.instance_id = 0
         self.directory = None
         self.mailbox = None
@@ -393,7 +394,7 @@ class ConnectorWorker:
                     s.record(st)
                 kv_ops.kv_transfer(self.g1, src, conn.pool, dst, layer_begin=first, num_layers=layer + 1 - first,
                                    src_head_offset=so, dst_head_offset=do, num_heads=nh, engine=self.push_engine,
-                                   stream=st)
+                                   stream=st, bulk=True if self.push_bulk_peer else None)
                 if self.push_timing:
                     e.record(st)
                     c = self.g1.config

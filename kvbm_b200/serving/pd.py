@@ -58,6 +58,7 @@ class PdConfig:
     page_size: int = 16
     layer_batch: int = 8             # layers per push launch
     push_engine: str = "tma"
+    push_bulk_peer: bool = True      # same-layout peer pushes as TMA bulk stores over NVLink
     prefill_requests: int = 4        # prefill G1 capacity, in requests
     decode_waves: int = 2            # decode G1 capacity, in waves
     selection: str = "always"        # CD policy on the decode instance: always | threshold | never
@@ -92,8 +93,8 @@ class PdInstance:
         self.tp = tp
         tp_rank, tp_size = (tp.rank, tp.size) if tp is not None else (0, 1)
         bs = cfg.page_size
-        kcfg = KvbmConfig.load({"transfer": {"layer_batch": cfg.layer_batch, "push_engine": cfg.push_engine}},
-                               env={}, system_toml=None)
+        kcfg = KvbmConfig.load({"transfer": {"layer_batch": cfg.layer_batch, "push_engine": cfg.push_engine,
+                                             "push_bulk_peer": cfg.push_bulk_peer}}, env={}, system_toml=None)
         cd = None
         slots = 0
         if role == "decode":

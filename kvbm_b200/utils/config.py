@@ -167,6 +167,9 @@ class TransferConfig:
     startup_benchmark: bool = False
     layer_batch: int = 8               # P->D push: layers per transfer launch during the prefill pass
     push_engine: str = "tma"           # P->D push kernel: tma (bulk-copy pipeline) | tile
+    # same-layout pushes into a peer GPU's pool: TMA loads and TMA bulk stores over NVLink (no SM
+    # instruction touches the data); false: TMA loads, stores by the consumer warps
+    push_bulk_peer: bool = True
 
 
 @dataclass
