@@ -195,6 +195,10 @@ def main(argv=None):
     p.add_argument("--peer-iters", type=int, default=10)
     p.add_argument("--bulk-peer", action="store_true",
                    help="also time the TMA bulk copy storing into the peer's pool (TMA stores to NVLink memory)")
+    p.add_argument("--src-heads", type=int, default=0,
+                   help="heterogeneous-TP shape: the pushing pool holds this many KV heads and stores them at "
+                        "--head-offset of the decode pool's --heads heads (0: same heads on both sides)")
+    p.add_argument("--head-offset", type=int, default=0)
     p.add_argument("--out", default=None)
     args = p.parse_args(argv)
     args.rope_unrolls = [int(x) for x in args.rope_unrolls.split(",") if x]
@@ -208,10 +212,12 @@ def main(argv=None):
     reqs = [int(x) for x in args.requests.split(",")]
     nmax = max(reqs) * args.blocks
     pool_blocks = 2 * nmax + 8
-    cfg = LayoutConfig.for_model(pool_blocks, args.layers, args.heads, 128, 16)
+    sh = args.src_heads or args.heads
+    cfg = LayoutConfig.for_model(pool_blocks, args.layers, sh if rank == 0 else args.heads, 128, 16)
     nhd = KvBlockLayout.OPERATIONAL_NHD
     dst_bl = nhd if args.dst_layout == "nhd" else KvBlockLayout.OPERATIONAL_HND
     local = KvLayout.allocate(cfg, "fully_contiguous", nhd if rank == 0 else dst_bl)
+    hkw = {"dst_head_offset": args.head_offset, "num_heads": sh} if args.src_heads else {}
     local._flat().random_(0, 256)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     # exchange pools
@@ -261,11 +267,13 @@ def main(argv=None):
                     if rank == 0:
                         if engine == "tma_bulk_peer":
                             ran[0] = kv_ops.kv_transfer(local, s_ids, remote, d_ids, engine="tma", max_ctas=ctas,
-                                                        bulk=True)
+                                                        bulk=True, **hkw)
                         else:
-                            ran[0] = kv_ops.kv_transfer(local, s_ids, remote, d_ids, engine=engine, max_ctas=ctas)
+                            ran[0] = kv_ops.kv_transfer(local, s_ids, remote, d_ids, engine=engine, max_ctas=ctas,
+                                                        **hkw)
                 ms = timed(fn)
                 r = {"path": f"fused_{engine}", "kernel": ran[0], "max_ctas": ctas, "requests": nreq,
+                     "heads": f"{sh}->{args.heads}@{args.head_offset}" if args.src_heads else args.heads,
                      "bytes": nbytes, "ms": round(ms, 4), "gbps": round(nbytes / ms / 1e6, 1),
                      "frac_of_peer_copy": round(nbytes / ms / 1e6 / PEER_COPY_GBPS, 3),
                      "frac_of_nominal": round(nbytes / ms / 1e6 / NVLINK_NOMINAL_GBPS, 3)}
@@ -281,10 +289,14 @@ def main(argv=None):
             dist.send(data.view(torch.uint8).reshape(-1), dst=1, group=gloo)
         else:
             got = local.gather_blocks(d_ids[sample].tolist()).cpu()
+            if args.src_heads:  # [n, L, O, T, H, D]: the pushed heads only
+                got = got[..., args.head_offset: args.head_offset + sh, :].contiguous()
             ref = torch.empty_like(got.view(torch.uint8).reshape(-1))
             dist.recv(ref, src=0, group=gloo)
             ok = torch.equal(got.view(torch.uint8).reshape(-1), ref)
             print(json.dumps({"check": "fused_transfer_exact", "requests": nreq, "ok": bool(ok)}), flush=True)
+        if args.src_heads:
+            continue  # the NCCL baselines move whole blocks of one geometry
         # NCCL baselines
         contig = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
 
