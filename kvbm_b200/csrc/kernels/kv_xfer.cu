@@ -359,30 +359,15 @@ __device__ __forceinline__ void tile_dequant(const uint8_t* src, int64_t src_rs,
 
 // ---- software-pipelined fp8 tiles ------------------------------------------
 //
-// When a head tile fits in one load batch per lane (16 x 16-byte source
-// units for a quantise, 4 fp8 units for a dequantise: every [16 x 128]
-// head tile), a persistent warp issues the loads of its next tile before it
-// reduces, converts and stores the current one, so DRAM reads stay in flight
-// while the cast math runs. Larger tiles take the one-tile-at-a-time path.
+// When a head tile fits one batch per lane (16 x 16-byte source units for a
+// quantise, 4 fp8 units for a dequantise: every [16 x 128] head tile), a
+// persistent warp keeps the copies of its next tiles in flight (cp.async
+// into a per-warp shared-memory ring) while it reduces, converts and stores
+// the current one, so DRAM reads overlap the cast math without costing
+// registers. Larger tiles take the one-tile-at-a-time path.
 
 constexpr int kQPairs = 4;   // source unit pairs per lane held per tile
 constexpr int kDqUnits = 4;  // fp8 source units per lane held per tile
-
-template <int KIND>
-__device__ __forceinline__ void quant_load(const uint8_t* src, int64_t rs, int pairs, const UnitMap& um, int lane,
-                                           int4 (&va)[kQPairs], int4 (&vb)[kQPairs]) {
-#pragma unroll
-  for (int k = 0; k < kQPairs; ++k) {
-    const int q = k * 32 + lane;
-    if (q < pairs) {
-      int r, c;
-      um.rc(2 * q, r, c);
-      const int4* p = reinterpret_cast<const int4*>(src + r * rs + c * 16);
-      va[k] = p[0];
-      vb[k] = p[1];
-    }
-  }
-}
 
 template <int KIND>
 __device__ __forceinline__ void quant_store(const int4 (&va)[kQPairs], const int4 (&vb)[kQPairs], uint8_t* dst,
@@ -414,19 +399,6 @@ __device__ __forceinline__ void quant_store(const int4 (&va)[kQPairs], const int
     }
   }
   if (lane == 0 && scale_out != nullptr) *scale_out = amax > 0.f ? amax / kE4M3Max : 1.0f;
-}
-
-__device__ __forceinline__ void dequant_load(const uint8_t* src, int64_t rs, int n, const UnitMap& um, int lane,
-                                             int4 (&v)[kDqUnits]) {
-#pragma unroll
-  for (int k = 0; k < kDqUnits; ++k) {
-    const int u = k * 32 + lane;
-    if (u < n) {
-      int r, c;
-      um.rc(u, r, c);
-      v[k] = *reinterpret_cast<const int4*>(src + r * rs + c * 16);
-    }
-  }
 }
 
 template <int KIND>
@@ -497,54 +469,77 @@ __device__ __forceinline__ TilePtrs tile_ptrs(const XferParams& P, int64_t t) {
   return r;
 }
 
-template <int KIND>
-__device__ __forceinline__ void cast_tiles_pipelined(const XferParams& P, int64_t warp, int64_t nwarps, int lane) {
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Copy one source tile densely into a warp's shared-memory slot (unit u at byte 16 u).
+__device__ __forceinline__ void tile_fetch(const uint8_t* src, int64_t rs, int units, const UnitMap& um, int lane,
+                                           uint8_t* slot) {
+  for (int u = lane; u < units; u += 32) {
+    int r, c;
+    um.rc(u, r, c);
+    cp_async16(slot + u * 16, src + r * rs + c * 16);
+  }
+}
+
+// Each warp walks its tiles (warp, warp + nwarps, ...) through a ring of S
+// shared-memory slots filled by cp.async: the copies of the next S - 1 tiles
+// are in flight while the warp reduces, converts and stores the current one,
+// without holding them in registers.
+template <int KIND, int S>
+__device__ __forceinline__ void cast_tiles_async(const XferParams& P, uint8_t* ring, int tile_bytes, int64_t warp,
+                                                 int64_t nwarps, int lane) {
   const UnitMap um = unit_map(P.fd_upr);
   const int units = P.shape.page_size * static_cast<int>(P.fd_upr.d);
   const int64_t srs = P.src.token_stride, drs = P.dst.token_stride;
-  int64_t t = warp;
-  if (t >= P.total_tiles) return;
-  TilePtrs cur = tile_ptrs<KIND>(P, t);
-  if constexpr (KIND <= kQuantF32) {
-    const int pairs = units / 2;
-    int4 a[kQPairs], b[kQPairs];
-    quant_load<KIND>(cur.s, srs, pairs, um, lane, a, b);
-    while (true) {
-      const int64_t tn = t + nwarps;
-      const bool more = tn < P.total_tiles;
-      TilePtrs nxt{};
-      int4 an[kQPairs], bn[kQPairs];
-      if (more) {
-        nxt = tile_ptrs<KIND>(P, tn);
-        quant_load<KIND>(nxt.s, srs, pairs, um, lane, an, bn);
+  const int64_t total = P.total_tiles;
+#pragma unroll
+  for (int k = 0; k < S - 1; ++k) {
+    const int64_t t = warp + k * nwarps;
+    if (t < total) tile_fetch(tile_ptrs<KIND>(P, t).s, srs, units, um, lane, ring + k * tile_bytes);
+    cp_async_commit();
+  }
+  for (int64_t k = 0;; ++k) {
+    const int64_t t = warp + k * nwarps;
+    if (t >= total) break;
+    const int64_t tn = t + (S - 1) * nwarps;
+    if (tn < total) tile_fetch(tile_ptrs<KIND>(P, tn).s, srs, units, um, lane, ring + ((k + S - 1) % S) * tile_bytes);
+    cp_async_commit();
+    cp_async_wait<S - 1>();  // this tile's group has landed (S - 1 younger groups may still fly)
+    __syncwarp();
+    const uint8_t* slot = ring + (k % S) * tile_bytes;
+    const TilePtrs cur = tile_ptrs<KIND>(P, t);
+    if constexpr (KIND <= kQuantF32) {
+      const int pairs = units / 2;
+      int4 a[kQPairs], b[kQPairs];
+#pragma unroll
+      for (int j = 0; j < kQPairs; ++j) {
+        const int q = j * 32 + lane;
+        if (q < pairs) {
+          a[j] = *reinterpret_cast<const int4*>(slot + 32 * q);
+          b[j] = *reinterpret_cast<const int4*>(slot + 32 * q + 16);
+        }
       }
       quant_store<KIND>(a, b, cur.d, drs, pairs, um, cur.scale, lane);
-      if (!more) break;
+    } else {
+      int4 v[kDqUnits];
 #pragma unroll
-      for (int k = 0; k < kQPairs; ++k) a[k] = an[k], b[k] = bn[k];
-      cur = nxt;
-      t = tn;
-    }
-  } else {
-    int4 v[kDqUnits];
-    dequant_load(cur.s, srs, units, um, lane, v);
-    while (true) {
-      const int64_t tn = t + nwarps;
-      const bool more = tn < P.total_tiles;
-      TilePtrs nxt{};
-      int4 vn[kDqUnits];
-      if (more) {
-        nxt = tile_ptrs<KIND>(P, tn);
-        dequant_load(nxt.s, srs, units, um, lane, vn);
+      for (int j = 0; j < kDqUnits; ++j) {
+        const int u = j * 32 + lane;
+        if (u < units) v[j] = *reinterpret_cast<const int4*>(slot + 16 * u);
       }
       dequant_store<KIND>(v, cur.d, drs, units, um, cur.scale ? *cur.scale : 1.0f, lane);
-      if (!more) break;
-#pragma unroll
-      for (int k = 0; k < kDqUnits; ++k) v[k] = vn[k];
-      cur = nxt;
-      t = tn;
     }
+    __syncwarp();  // every lane is done with the slot before it is refilled
   }
+  cp_async_wait<0>();
 }
 
 template <int KIND, int U>
@@ -566,15 +561,18 @@ __device__ __forceinline__ void run_tile(const XferParams& P, const uint8_t* s, 
 
 // Warp-per-tile kernel. Tiles are ordered (pair, layer, outer, head) with
 // head fastest so the warps of one CTA sweep one contiguous chunk together.
-// Resident CTAs per SM the pipelined cast kernels are built for (their register budget).
-constexpr int pipe_ctas_per_sm(int kind) { return kind <= kQuantF32 ? 2 : 3; }
+// Ring depth of the pipelined cast kernels: 3 x 4 KiB slots per warp for a
+// quantise (two CTAs of 96 KiB per SM), 4 x 2 KiB for a dequantise.
+__host__ __device__ constexpr int cast_stages(int kind) { return kind <= kQuantF32 ? 3 : 4; }
 
 template <int KIND>
-__global__ void __launch_bounds__(kThreads, pipe_ctas_per_sm(KIND))
-    kv_cast_pipe_kernel(const __grid_constant__ XferParams P) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5);
-  cast_tiles_pipelined<KIND>(P, warp, static_cast<int64_t>(gridDim.x) * kWarpsPerCta, lane);
+__global__ void __launch_bounds__(kThreads) kv_cast_pipe_kernel(const __grid_constant__ XferParams P, int tile_bytes) {
+  extern __shared__ __align__(128) uint8_t cast_smem[];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  constexpr int S = cast_stages(KIND);
+  const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + w;
+  cast_tiles_async<KIND, S>(P, cast_smem + static_cast<size_t>(w) * S * tile_bytes, tile_bytes, warp,
+                            static_cast<int64_t>(gridDim.x) * kWarpsPerCta, lane);
 }
 
 template <int KIND, int U>
@@ -672,10 +670,18 @@ cudaError_t launch_tile(const XferParams& P, int max_ctas, cudaStream_t stream) 
     const int units = P.shape.page_size * static_cast<int>(P.fd_upr.d);
     const bool fits = (KIND <= kQuantF32) ? units / 2 <= kQPairs * 32 : units <= kDqUnits * 32;
     if (g_cast_pipe && fits) {
-      // persistent: every warp walks many tiles, so the next tile's loads overlap this one's math
-      const int64_t pcap = max_ctas > 0 ? max_ctas : static_cast<int64_t>(sm_count()) * pipe_ctas_per_sm(KIND);
+      // persistent: every warp walks many tiles, so the next tiles' copies overlap this one's math
+      const int tile_bytes = units * 16;
+      const size_t smem = static_cast<size_t>(kWarpsPerCta) * cast_stages(KIND) * tile_bytes;
+      cudaError_t e = cudaFuncSetAttribute(kv_cast_pipe_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      int per_sm = 1;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kv_cast_pipe_kernel<KIND>, kThreads, smem);
+      if (e != cudaSuccess) return e;
+      const int64_t pcap = max_ctas > 0 ? max_ctas : static_cast<int64_t>(sm_count()) * std::max(1, per_sm);
       const int pgrid = static_cast<int>(std::max<int64_t>(1, std::min(ctas_needed, pcap)));
-      kv_cast_pipe_kernel<KIND><<<pgrid, kThreads, 0, stream>>>(P);
+      kv_cast_pipe_kernel<KIND><<<pgrid, kThreads, smem, stream>>>(P, tile_bytes);
       return cudaGetLastError();
     }
   }
