@@ -126,10 +126,12 @@ def run(args) -> list[dict]:
     for name, b in dsts.items():
         if args.d2d and name not in args.d2d.split(","):
             continue
-        for engine in [e for e in ("tile", "tile1", "tma") if e in args.engines.split(",")]:
-            # tile1: the fp8 casts on the one-tile-at-a-time kernel (tile: the pipelined one)
+        for engine in [e for e in ("tile", "tile_sw", "tile1", "tma") if e in args.engines.split(",")]:
+            # tile1: the fp8 casts on the one-tile-at-a-time kernel (tile: the pipelined one; tile_sw:
+            # the pipelined one converting on the integer / FMA pipes)
             kv_ops.set_cast_pipeline(engine != "tile1")
-            eng = "tile" if engine == "tile1" else engine
+            kv_ops.set_cast_softconv(engine == "tile_sw")
+            eng = "tile" if engine in ("tile1", "tile_sw") else engine
             ms = _time(lambda: kv_ops.kv_transfer(a, s_ids, b, d_ids, engine=eng), args.iters, args.warmup,
                        flush)
             nbytes = n * cfg.bytes_per_block
@@ -140,9 +142,10 @@ def run(args) -> list[dict]:
             print(json.dumps(r), flush=True)
         if name == "g1_to_g1_fp8_quant":
             back = KvLayout.allocate(cfg, "fully_contiguous", nhd)
-            for engine in [e for e in ("tile", "tile1", "tma") if e in args.engines.split(",")]:
+            for engine in [e for e in ("tile", "tile_sw", "tile1", "tma") if e in args.engines.split(",")]:
                 kv_ops.set_cast_pipeline(engine != "tile1")
-                eng = "tile" if engine == "tile1" else engine
+                kv_ops.set_cast_softconv(engine == "tile_sw")
+                eng = "tile" if engine in ("tile1", "tile_sw") else engine
                 ms = _time(lambda: kv_ops.kv_transfer(b, d_ids, back, s_ids, engine=eng), args.iters,
                            args.warmup, flush)
                 nbytes = n * cfg.bytes_per_block
@@ -152,6 +155,7 @@ def run(args) -> list[dict]:
                 results.append(r)
                 print(json.dumps(r), flush=True)
         kv_ops.set_cast_pipeline(True)
+        kv_ops.set_cast_softconv(False)
         if name == "g1_to_g1_copy" and "ce" in args.engines.split(","):
             src_p = [a.layer_base(0) + int(x) * a.block_stride for x in s_ids.tolist()]
             dst_p = [b.layer_base(0) + int(x) * b.block_stride for x in d_ids.tolist()]

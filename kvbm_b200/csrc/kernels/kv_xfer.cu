@@ -200,8 +200,47 @@ __device__ __forceinline__ float amax_bits_to_float(uint32_t bits) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
 }
 
+// ---- fp8 conversions on the integer / FMA pipes ------------------------------
+//
+// The hardware conversions (f32 -> e4m3x2, e4m3x2 -> f16x2, f32 -> bf16x2)
+// issue on the SM's narrow conversion pipe, which the casts saturate; these
+// produce the same bits with integer and FMA instructions, for finite inputs:
+//   f32 -> e4m3 (round to nearest even, saturating to 448): normal results
+//     round the fp32 bits at 3 mantissa bits and rebias the exponent (127 ->
+//     7); results below 2^-6 are multiples of 2^-9, rounded by adding
+//     1.5 * 2^14 (whose ulp is 2^-9) in fp32 and reading the low bits (the
+//     round-by-addition method: an fp32 add rounds to the ulp of the larger
+//     operand, to nearest even).
+//   e4m3 -> f32: normal codes rebias the exponent; subnormal codes m give
+//     m * 2^-9 = (1.5 * 2^14 + m * 2^-9) - 1.5 * 2^14, exact in fp32.
+//   f32 -> bf16 (round to nearest even): add 0x7fff plus the kept lsb, keep
+//     the top 16 bits.
+// The quantiser never writes the e4m3 NaN codes (0x7f / 0xff), so the
+// dequantiser does not special-case them.
+__device__ __forceinline__ uint32_t f32_to_e4m3_sw(float v) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t a = b & 0x7fffffffu;
+  const uint32_t r = a + 0x7ffffu + ((a >> 20) & 1u);
+  const uint32_t normal = min((r >> 20) - (120u << 3), 0x7eu);
+  const uint32_t sub = __float_as_uint(__uint_as_float(a) + 24576.0f) - 0x46c00000u;
+  return ((b >> 24) & 0x80u) | (a >= 0x3c800000u ? normal : sub);
+}
+
+__device__ __forceinline__ float e4m3_to_f32_sw(uint32_t c) {
+  const uint32_t em = c & 0x7fu;
+  const uint32_t normal = (em + (120u << 3)) << 20;
+  const uint32_t sub = __float_as_uint(__uint_as_float(0x46c00000u | em) - 24576.0f);
+  return __uint_as_float(((c & 0x80u) << 24) | (em >= 8u ? normal : sub));
+}
+
+__device__ __forceinline__ uint32_t f32_to_bf16_bits_sw(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u + 0x7fffu + ((u >> 16) & 1u)) >> 16;
+}
+
 // 16-byte source unit -> its fp8 bytes (8 for 16-bit sources, 4 for f32), as 32-bit words.
-template <int KIND>
+// SW: bf16 sources convert on the integer / FMA pipes (same bits as the hardware path).
+template <int KIND, bool SW = false>
 __device__ __forceinline__ void unit_to_fp8(const int4& v, float inv, uint32_t* out) {
   const uint32_t w[4] = {(uint32_t)v.x, (uint32_t)v.y, (uint32_t)v.z, (uint32_t)v.w};
   if (KIND == kQuantF32) {
@@ -225,6 +264,15 @@ __device__ __forceinline__ void unit_to_fp8(const int4& v, float inv, uint32_t* 
   float2 p[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) p[j] = mul2(f[2 * j], f[2 * j + 1], inv);
+  if constexpr (SW && KIND == kQuantBf16) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t c0 = f32_to_e4m3_sw(p[2 * h].x), c1 = f32_to_e4m3_sw(p[2 * h].y);
+      const uint32_t c2 = f32_to_e4m3_sw(p[2 * h + 1].x), c3 = f32_to_e4m3_sw(p[2 * h + 1].y);
+      out[h] = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
+    }
+    return;
+  }
   out[0] = (uint32_t)pack_fp8x2(p[0].x, p[0].y) | ((uint32_t)pack_fp8x2(p[1].x, p[1].y) << 16);
   out[1] = (uint32_t)pack_fp8x2(p[2].x, p[2].y) | ((uint32_t)pack_fp8x2(p[3].x, p[3].y) << 16);
 }
@@ -369,7 +417,7 @@ __device__ __forceinline__ void tile_dequant(const uint8_t* src, int64_t src_rs,
 constexpr int kQPairs = 4;   // source unit pairs per lane held per tile
 constexpr int kDqUnits = 4;  // fp8 source units per lane held per tile
 
-template <int KIND>
+template <int KIND, bool SW = false>
 __device__ __forceinline__ void quant_store(const int4 (&va)[kQPairs], const int4 (&vb)[kQPairs], uint8_t* dst,
                                             int64_t rs, int pairs, const UnitMap& um, float* scale_out, int lane) {
   constexpr int kOut = (KIND == kQuantF32) ? 4 : 8;
@@ -390,8 +438,8 @@ __device__ __forceinline__ void quant_store(const int4 (&va)[kQPairs], const int
     um.rc(2 * q, r, c);
     uint8_t* d = dst + r * rs + c * kOut;
     uint32_t w[4];
-    unit_to_fp8<KIND>(va[k], inv, w);
-    unit_to_fp8<KIND>(vb[k], inv, w + kOut / 4);
+    unit_to_fp8<KIND, SW>(va[k], inv, w);
+    unit_to_fp8<KIND, SW>(vb[k], inv, w + kOut / 4);
     if (KIND == kQuantF32) {
       *reinterpret_cast<uint2*>(d) = make_uint2(w[0], w[1]);
     } else {
@@ -401,7 +449,7 @@ __device__ __forceinline__ void quant_store(const int4 (&va)[kQPairs], const int
   if (lane == 0 && scale_out != nullptr) *scale_out = amax > 0.f ? amax / kE4M3Max : 1.0f;
 }
 
-template <int KIND>
+template <int KIND, bool SW = false>
 __device__ __forceinline__ void dequant_store(const int4 (&v)[kDqUnits], uint8_t* dst, int64_t rs, int n,
                                               const UnitMap& um, float scale, int lane) {
 #pragma unroll
@@ -411,6 +459,20 @@ __device__ __forceinline__ void dequant_store(const int4 (&v)[kDqUnits], uint8_t
     int r, c;
     um.rc(u, r, c);
     const uint32_t w[4] = {(uint32_t)v[k].x, (uint32_t)v[k].y, (uint32_t)v[k].z, (uint32_t)v[k].w};
+    if constexpr (SW && KIND == kDequantBf16) {
+      uint32_t o[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 pa = mul2(e4m3_to_f32_sw(w[j]), e4m3_to_f32_sw(w[j] >> 8), scale);
+        const float2 pb = mul2(e4m3_to_f32_sw(w[j] >> 16), e4m3_to_f32_sw(w[j] >> 24), scale);
+        o[2 * j] = __byte_perm(f32_to_bf16_bits_sw(pa.x), f32_to_bf16_bits_sw(pa.y), 0x5410);
+        o[2 * j + 1] = __byte_perm(f32_to_bf16_bits_sw(pb.x), f32_to_bf16_bits_sw(pb.y), 0x5410);
+      }
+      uint8_t* d = dst + r * rs;
+      *reinterpret_cast<int4*>(d + c * 32) = make_int4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<int4*>(d + c * 32 + 16) = make_int4(o[4], o[5], o[6], o[7]);
+      continue;
+    }
     float f[16];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -493,7 +555,7 @@ __device__ __forceinline__ void tile_fetch(const uint8_t* src, int64_t rs, int u
 // shared-memory slots filled by cp.async: the copies of the next S - 1 tiles
 // are in flight while the warp reduces, converts and stores the current one,
 // without holding them in registers.
-template <int KIND, int S>
+template <int KIND, int S, bool SW>
 __device__ __forceinline__ void cast_tiles_async(const XferParams& P, uint8_t* ring, int tile_bytes, int64_t warp,
                                                  int64_t nwarps, int lane) {
   const UnitMap um = unit_map(P.fd_upr);
@@ -527,7 +589,7 @@ __device__ __forceinline__ void cast_tiles_async(const XferParams& P, uint8_t* r
           b[j] = *reinterpret_cast<const int4*>(slot + 32 * q + 16);
         }
       }
-      quant_store<KIND>(a, b, cur.d, drs, pairs, um, cur.scale, lane);
+      quant_store<KIND, SW>(a, b, cur.d, drs, pairs, um, cur.scale, lane);
     } else {
       int4 v[kDqUnits];
 #pragma unroll
@@ -535,7 +597,7 @@ __device__ __forceinline__ void cast_tiles_async(const XferParams& P, uint8_t* r
         const int u = j * 32 + lane;
         if (u < units) v[j] = *reinterpret_cast<const int4*>(slot + 16 * u);
       }
-      dequant_store<KIND>(v, cur.d, drs, units, um, cur.scale ? *cur.scale : 1.0f, lane);
+      dequant_store<KIND, SW>(v, cur.d, drs, units, um, cur.scale ? *cur.scale : 1.0f, lane);
     }
     __syncwarp();  // every lane is done with the slot before it is refilled
   }
@@ -565,13 +627,13 @@ __device__ __forceinline__ void run_tile(const XferParams& P, const uint8_t* s, 
 // quantise (two CTAs of 96 KiB per SM), 4 x 2 KiB for a dequantise.
 __host__ __device__ constexpr int cast_stages(int kind) { return kind <= kQuantF32 ? 3 : 4; }
 
-template <int KIND>
+template <int KIND, bool SW>
 __global__ void __launch_bounds__(kThreads) kv_cast_pipe_kernel(const __grid_constant__ XferParams P, int tile_bytes) {
   extern __shared__ __align__(128) uint8_t cast_smem[];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   constexpr int S = cast_stages(KIND);
   const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + w;
-  cast_tiles_async<KIND, S>(P, cast_smem + static_cast<size_t>(w) * S * tile_bytes, tile_bytes, warp,
+  cast_tiles_async<KIND, S, SW>(P, cast_smem + static_cast<size_t>(w) * S * tile_bytes, tile_bytes, warp,
                             static_cast<int64_t>(gridDim.x) * kWarpsPerCta, lane);
 }
 
@@ -662,6 +724,7 @@ int common_align(std::initializer_list<int64_t> xs) {
 }
 
 bool g_cast_pipe = true;
+bool g_cast_soft = false;  // bf16 <-> fp8 conversions on the integer / FMA pipes in the pipelined kernel
 
 template <int KIND, int U>
 cudaError_t launch_tile(const XferParams& P, int max_ctas, cudaStream_t stream) {
@@ -673,15 +736,15 @@ cudaError_t launch_tile(const XferParams& P, int max_ctas, cudaStream_t stream) 
       // persistent: every warp walks many tiles, so the next tiles' copies overlap this one's math
       const int tile_bytes = units * 16;
       const size_t smem = static_cast<size_t>(kWarpsPerCta) * cast_stages(KIND) * tile_bytes;
-      cudaError_t e = cudaFuncSetAttribute(kv_cast_pipe_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem));
+      auto kern = g_cast_soft ? kv_cast_pipe_kernel<KIND, true> : kv_cast_pipe_kernel<KIND, false>;
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
       if (e != cudaSuccess) return e;
       int per_sm = 1;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kv_cast_pipe_kernel<KIND>, kThreads, smem);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
       if (e != cudaSuccess) return e;
       const int64_t pcap = max_ctas > 0 ? max_ctas : static_cast<int64_t>(sm_count()) * std::max(1, per_sm);
       const int pgrid = static_cast<int>(std::max<int64_t>(1, std::min(ctas_needed, pcap)));
-      kv_cast_pipe_kernel<KIND><<<pgrid, kThreads, smem, stream>>>(P, tile_bytes);
+      kern<<<pgrid, kThreads, smem, stream>>>(P, tile_bytes);
       return cudaGetLastError();
     }
   }
@@ -1257,6 +1320,10 @@ extern "C" int kvbm_xfer_status(int device, int reset) {
 // 1 (default): fp8 casts whose head tile fits one register batch run the
 // software-pipelined persistent kernel; 0: the one-tile-at-a-time kernel.
 extern "C" void kvbm_xfer_set_cast_pipeline(int on) { g_cast_pipe = on != 0; }
+
+// 1: the pipelined cast kernel converts bf16 <-> fp8 on the integer / FMA
+// pipes (same bits); 0 (default): with the hardware conversion instructions.
+extern "C" void kvbm_xfer_set_cast_softconv(int on) { g_cast_soft = on != 0; }
 
 extern "C" void kvbm_xfer_set_wait_limit_ns(uint64_t ns) { g_wait_ns_override = ns; }
 

@@ -112,6 +112,9 @@ void kvbm_xfer_set_wait_limit_ns(uint64_t ns);
 // 1 (default): fp8 casts whose head tile fits one register batch per lane run
 // the software-pipelined persistent cast kernel; 0: the one-tile-at-a-time kernel.
 void kvbm_xfer_set_cast_pipeline(int on);
+// 1: the pipelined cast kernel converts bf16 <-> fp8 on the integer / FMA pipes
+// (bit-identical for finite values); 0 (default): hardware conversions.
+void kvbm_xfer_set_cast_softconv(int on);
 
 // Split-by-bytes batched copy of num_pairs (src, dst) regions of equal size.
 // `align` is the alignment (16, 8, 4, 2 or 1) that every pointer and

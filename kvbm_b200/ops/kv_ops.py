@@ -155,6 +155,12 @@ def set_cast_pipeline(on: bool) -> None:
     _lib.load().kvbm_xfer_set_cast_pipeline(1 if on else 0)
 
 
+def set_cast_softconv(on: bool) -> None:
+    """Pipelined fp8 casts of bf16 data: conversions on the integer / FMA pipes (True) or with the
+    hardware conversion instructions (False); the bits are the same for finite values."""
+    _lib.load().kvbm_xfer_set_cast_softconv(1 if on else 0)
+
+
 def kv_checksum(layout, ids, *, layer_begin: int = 0, num_layers: int | None = None, head_offset: int = 0,
                 num_heads: int | None = None, stream=None) -> torch.Tensor:
     """Layout-independent 64-bit checksum of each block in ``ids`` (int64 tensor on the device).
