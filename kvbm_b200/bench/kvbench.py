@@ -60,6 +60,11 @@ def _ce_regions(src: KvLayout, s_ids, dst: KvLayout, d_ids):
     return sp, dp, c.bytes_per_chunk
 
 
+# on-device engines: tile (pipelined cast kernel), tile_sw1 / tile_sw2 / tile_sw (a quarter, half or
+# all of its bf16 <-> fp8 conversions on the integer / FMA pipes), tile1 (one tile at a time), tma
+CAST_ENGINES = ("tile", "tile_sw1", "tile_sw2", "tile_sw", "tile1", "tma")
+
+
 def run(args) -> list[dict]:
     torch.cuda.set_device(0)
     rng = random.Random(args.seed)
@@ -126,12 +131,12 @@ def run(args) -> list[dict]:
     for name, b in dsts.items():
         if args.d2d and name not in args.d2d.split(","):
             continue
-        for engine in [e for e in ("tile", "tile_sw", "tile1", "tma") if e in args.engines.split(",")]:
+        for engine in [e for e in CAST_ENGINES if e in args.engines.split(",")]:
             # tile1: the fp8 casts on the one-tile-at-a-time kernel (tile: the pipelined one; tile_sw:
             # the pipelined one converting on the integer / FMA pipes)
             kv_ops.set_cast_pipeline(engine != "tile1")
-            kv_ops.set_cast_softconv(engine == "tile_sw")
-            eng = "tile" if engine in ("tile1", "tile_sw") else engine
+            kv_ops.set_cast_softconv({"tile_sw1": 1, "tile_sw2": 2, "tile_sw": 4}.get(engine, 0))
+            eng = "tile" if engine.startswith("tile") else engine
             ms = _time(lambda: kv_ops.kv_transfer(a, s_ids, b, d_ids, engine=eng), args.iters, args.warmup,
                        flush)
             nbytes = n * cfg.bytes_per_block
@@ -142,10 +147,10 @@ def run(args) -> list[dict]:
             print(json.dumps(r), flush=True)
         if name == "g1_to_g1_fp8_quant":
             back = KvLayout.allocate(cfg, "fully_contiguous", nhd)
-            for engine in [e for e in ("tile", "tile_sw", "tile1", "tma") if e in args.engines.split(",")]:
+            for engine in [e for e in CAST_ENGINES if e in args.engines.split(",")]:
                 kv_ops.set_cast_pipeline(engine != "tile1")
-                kv_ops.set_cast_softconv(engine == "tile_sw")
-                eng = "tile" if engine in ("tile1", "tile_sw") else engine
+                kv_ops.set_cast_softconv({"tile_sw1": 1, "tile_sw2": 2, "tile_sw": 4}.get(engine, 0))
+                eng = "tile" if engine.startswith("tile") else engine
                 ms = _time(lambda: kv_ops.kv_transfer(b, d_ids, back, s_ids, engine=eng), args.iters,
                            args.warmup, flush)
                 nbytes = n * cfg.bytes_per_block
@@ -155,7 +160,7 @@ def run(args) -> list[dict]:
                 results.append(r)
                 print(json.dumps(r), flush=True)
         kv_ops.set_cast_pipeline(True)
-        kv_ops.set_cast_softconv(False)
+        kv_ops.set_cast_softconv(0)
         if name == "g1_to_g1_copy" and "ce" in args.engines.split(","):
             src_p = [a.layer_base(0) + int(x) * a.block_stride for x in s_ids.tolist()]
             dst_p = [b.layer_base(0) + int(x) * b.block_stride for x in d_ids.tolist()]

@@ -239,8 +239,9 @@ __device__ __forceinline__ uint32_t f32_to_bf16_bits_sw(float v) {
 }
 
 // 16-byte source unit -> its fp8 bytes (8 for 16-bit sources, 4 for f32), as 32-bit words.
-// SW: bf16 sources convert on the integer / FMA pipes (same bits as the hardware path).
-template <int KIND, bool SW = false>
+// SWQ: for bf16 sources, this many of every four converted pairs go through the integer / FMA
+// pipes (same bits as the hardware path), the rest through the conversion instructions.
+template <int KIND, int SWQ = 0>
 __device__ __forceinline__ void unit_to_fp8(const int4& v, float inv, uint32_t* out) {
   const uint32_t w[4] = {(uint32_t)v.x, (uint32_t)v.y, (uint32_t)v.z, (uint32_t)v.w};
   if (KIND == kQuantF32) {
@@ -264,17 +265,16 @@ __device__ __forceinline__ void unit_to_fp8(const int4& v, float inv, uint32_t* 
   float2 p[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) p[j] = mul2(f[2 * j], f[2 * j + 1], inv);
-  if constexpr (SW && KIND == kQuantBf16) {
+  uint32_t h16[4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t c0 = f32_to_e4m3_sw(p[2 * h].x), c1 = f32_to_e4m3_sw(p[2 * h].y);
-      const uint32_t c2 = f32_to_e4m3_sw(p[2 * h + 1].x), c3 = f32_to_e4m3_sw(p[2 * h + 1].y);
-      out[h] = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
-    }
-    return;
+  for (int j = 0; j < 4; ++j) {
+    if (KIND == kQuantBf16 && j < SWQ)
+      h16[j] = f32_to_e4m3_sw(p[j].x) | (f32_to_e4m3_sw(p[j].y) << 8);
+    else
+      h16[j] = pack_fp8x2(p[j].x, p[j].y);
   }
-  out[0] = (uint32_t)pack_fp8x2(p[0].x, p[0].y) | ((uint32_t)pack_fp8x2(p[1].x, p[1].y) << 16);
-  out[1] = (uint32_t)pack_fp8x2(p[2].x, p[2].y) | ((uint32_t)pack_fp8x2(p[3].x, p[3].y) << 16);
+  out[0] = h16[0] | (h16[1] << 16);
+  out[1] = h16[2] | (h16[3] << 16);
 }
 
 // Quantise one head tile. Lanes take pairs of adjacent 16-byte source units
@@ -417,7 +417,7 @@ __device__ __forceinline__ void tile_dequant(const uint8_t* src, int64_t src_rs,
 constexpr int kQPairs = 4;   // source unit pairs per lane held per tile
 constexpr int kDqUnits = 4;  // fp8 source units per lane held per tile
 
-template <int KIND, bool SW = false>
+template <int KIND, int SWQ = 0>
 __device__ __forceinline__ void quant_store(const int4 (&va)[kQPairs], const int4 (&vb)[kQPairs], uint8_t* dst,
                                             int64_t rs, int pairs, const UnitMap& um, float* scale_out, int lane) {
   constexpr int kOut = (KIND == kQuantF32) ? 4 : 8;
@@ -438,8 +438,8 @@ __device__ __forceinline__ void quant_store(const int4 (&va)[kQPairs], const int
     um.rc(2 * q, r, c);
     uint8_t* d = dst + r * rs + c * kOut;
     uint32_t w[4];
-    unit_to_fp8<KIND, SW>(va[k], inv, w);
-    unit_to_fp8<KIND, SW>(vb[k], inv, w + kOut / 4);
+    unit_to_fp8<KIND, SWQ>(va[k], inv, w);
+    unit_to_fp8<KIND, SWQ>(vb[k], inv, w + kOut / 4);
     if (KIND == kQuantF32) {
       *reinterpret_cast<uint2*>(d) = make_uint2(w[0], w[1]);
     } else {
@@ -449,7 +449,7 @@ __device__ __forceinline__ void quant_store(const int4 (&va)[kQPairs], const int
   if (lane == 0 && scale_out != nullptr) *scale_out = amax > 0.f ? amax / kE4M3Max : 1.0f;
 }
 
-template <int KIND, bool SW = false>
+template <int KIND, int SWQ = 0>
 __device__ __forceinline__ void dequant_store(const int4 (&v)[kDqUnits], uint8_t* dst, int64_t rs, int n,
                                               const UnitMap& um, float scale, int lane) {
 #pragma unroll
@@ -459,14 +459,24 @@ __device__ __forceinline__ void dequant_store(const int4 (&v)[kDqUnits], uint8_t
     int r, c;
     um.rc(u, r, c);
     const uint32_t w[4] = {(uint32_t)v[k].x, (uint32_t)v[k].y, (uint32_t)v[k].z, (uint32_t)v[k].w};
-    if constexpr (SW && KIND == kDequantBf16) {
+    if constexpr (SWQ > 0 && KIND == kDequantBf16) {
+      // word j (4 fp8 values): the first SWQ words on the integer / FMA pipes, the rest in hardware
       uint32_t o[8];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float2 pa = mul2(e4m3_to_f32_sw(w[j]), e4m3_to_f32_sw(w[j] >> 8), scale);
-        const float2 pb = mul2(e4m3_to_f32_sw(w[j] >> 16), e4m3_to_f32_sw(w[j] >> 24), scale);
-        o[2 * j] = __byte_perm(f32_to_bf16_bits_sw(pa.x), f32_to_bf16_bits_sw(pa.y), 0x5410);
-        o[2 * j + 1] = __byte_perm(f32_to_bf16_bits_sw(pb.x), f32_to_bf16_bits_sw(pb.y), 0x5410);
+        if (j < SWQ) {
+          const float2 pa = mul2(e4m3_to_f32_sw(w[j]), e4m3_to_f32_sw(w[j] >> 8), scale);
+          const float2 pb = mul2(e4m3_to_f32_sw(w[j] >> 16), e4m3_to_f32_sw(w[j] >> 24), scale);
+          o[2 * j] = __byte_perm(f32_to_bf16_bits_sw(pa.x), f32_to_bf16_bits_sw(pa.y), 0x5410);
+          o[2 * j + 1] = __byte_perm(f32_to_bf16_bits_sw(pb.x), f32_to_bf16_bits_sw(pb.y), 0x5410);
+        } else {
+          const float2 a = unpack_fp8x2(static_cast<uint16_t>(w[j] & 0xffffu));
+          const float2 b = unpack_fp8x2(static_cast<uint16_t>(w[j] >> 16));
+          const float2 pa = mul2(a.x, a.y, scale), pb = mul2(b.x, b.y, scale);
+          __nv_bfloat162 ba = __floats2bfloat162_rn(pa.x, pa.y), bb = __floats2bfloat162_rn(pb.x, pb.y);
+          o[2 * j] = *reinterpret_cast<uint32_t*>(&ba);
+          o[2 * j + 1] = *reinterpret_cast<uint32_t*>(&bb);
+        }
       }
       uint8_t* d = dst + r * rs;
       *reinterpret_cast<int4*>(d + c * 32) = make_int4(o[0], o[1], o[2], o[3]);
@@ -555,7 +565,7 @@ __device__ __forceinline__ void tile_fetch(const uint8_t* src, int64_t rs, int u
 // shared-memory slots filled by cp.async: the copies of the next S - 1 tiles
 // are in flight while the warp reduces, converts and stores the current one,
 // without holding them in registers.
-template <int KIND, int S, bool SW>
+template <int KIND, int S, int SWQ>
 __device__ __forceinline__ void cast_tiles_async(const XferParams& P, uint8_t* ring, int tile_bytes, int64_t warp,
                                                  int64_t nwarps, int lane) {
   const UnitMap um = unit_map(P.fd_upr);
@@ -589,7 +599,7 @@ __device__ __forceinline__ void cast_tiles_async(const XferParams& P, uint8_t* r
           b[j] = *reinterpret_cast<const int4*>(slot + 32 * q + 16);
         }
       }
-      quant_store<KIND, SW>(a, b, cur.d, drs, pairs, um, cur.scale, lane);
+      quant_store<KIND, SWQ>(a, b, cur.d, drs, pairs, um, cur.scale, lane);
     } else {
       int4 v[kDqUnits];
 #pragma unroll
@@ -597,7 +607,7 @@ __device__ __forceinline__ void cast_tiles_async(const XferParams& P, uint8_t* r
         const int u = j * 32 + lane;
         if (u < units) v[j] = *reinterpret_cast<const int4*>(slot + 16 * u);
       }
-      dequant_store<KIND, SW>(v, cur.d, drs, units, um, cur.scale ? *cur.scale : 1.0f, lane);
+      dequant_store<KIND, SWQ>(v, cur.d, drs, units, um, cur.scale ? *cur.scale : 1.0f, lane);
     }
     __syncwarp();  // every lane is done with the slot before it is refilled
   }
@@ -627,13 +637,13 @@ __device__ __forceinline__ void run_tile(const XferParams& P, const uint8_t* s, 
 // quantise (two CTAs of 96 KiB per SM), 4 x 2 KiB for a dequantise.
 __host__ __device__ constexpr int cast_stages(int kind) { return kind <= kQuantF32 ? 3 : 4; }
 
-template <int KIND, bool SW>
+template <int KIND, int SWQ>
 __global__ void __launch_bounds__(kThreads) kv_cast_pipe_kernel(const __grid_constant__ XferParams P, int tile_bytes) {
   extern __shared__ __align__(128) uint8_t cast_smem[];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   constexpr int S = cast_stages(KIND);
   const int64_t warp = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + w;
-  cast_tiles_async<KIND, S, SW>(P, cast_smem + static_cast<size_t>(w) * S * tile_bytes, tile_bytes, warp,
+  cast_tiles_async<KIND, S, SWQ>(P, cast_smem + static_cast<size_t>(w) * S * tile_bytes, tile_bytes, warp,
                             static_cast<int64_t>(gridDim.x) * kWarpsPerCta, lane);
 }
 
@@ -724,7 +734,7 @@ int common_align(std::initializer_list<int64_t> xs) {
 }
 
 bool g_cast_pipe = true;
-bool g_cast_soft = false;  // bf16 <-> fp8 conversions on the integer / FMA pipes in the pipelined kernel
+int g_cast_soft = 0;  // quarters of the bf16 <-> fp8 conversions done on the integer / FMA pipes (0, 1, 2, 4)
 
 template <int KIND, int U>
 cudaError_t launch_tile(const XferParams& P, int max_ctas, cudaStream_t stream) {
@@ -736,7 +746,12 @@ cudaError_t launch_tile(const XferParams& P, int max_ctas, cudaStream_t stream) 
       // persistent: every warp walks many tiles, so the next tiles' copies overlap this one's math
       const int tile_bytes = units * 16;
       const size_t smem = static_cast<size_t>(kWarpsPerCta) * cast_stages(KIND) * tile_bytes;
-      auto kern = g_cast_soft ? kv_cast_pipe_kernel<KIND, true> : kv_cast_pipe_kernel<KIND, false>;
+      auto kern = kv_cast_pipe_kernel<KIND, 0>;
+      if constexpr (KIND == kQuantBf16 || KIND == kDequantBf16) {
+        if (g_cast_soft == 1) kern = kv_cast_pipe_kernel<KIND, 1>;
+        if (g_cast_soft == 2) kern = kv_cast_pipe_kernel<KIND, 2>;
+        if (g_cast_soft >= 4) kern = kv_cast_pipe_kernel<KIND, 4>;
+      }
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
       if (e != cudaSuccess) return e;
       int per_sm = 1;
@@ -1321,9 +1336,10 @@ extern "C" int kvbm_xfer_status(int device, int reset) {
 // software-pipelined persistent kernel; 0: the one-tile-at-a-time kernel.
 extern "C" void kvbm_xfer_set_cast_pipeline(int on) { g_cast_pipe = on != 0; }
 
-// 1: the pipelined cast kernel converts bf16 <-> fp8 on the integer / FMA
-// pipes (same bits); 0 (default): with the hardware conversion instructions.
-extern "C" void kvbm_xfer_set_cast_softconv(int on) { g_cast_soft = on != 0; }
+// Quarters (0, 1, 2 or 4) of the pipelined cast kernel's bf16 <-> fp8
+// conversions done on the integer / FMA pipes (same bits) instead of with the
+// conversion instructions, to balance the two pipes; 0 by default.
+extern "C" void kvbm_xfer_set_cast_softconv(int quarters) { g_cast_soft = quarters < 0 ? 0 : quarters; }
 
 extern "C" void kvbm_xfer_set_wait_limit_ns(uint64_t ns) { g_wait_ns_override = ns; }
 

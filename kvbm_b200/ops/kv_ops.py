@@ -155,10 +155,11 @@ def set_cast_pipeline(on: bool) -> None:
     _lib.load().kvbm_xfer_set_cast_pipeline(1 if on else 0)
 
 
-def set_cast_softconv(on: bool) -> None:
-    """Pipelined fp8 casts of bf16 data: conversions on the integer / FMA pipes (True) or with the
-    hardware conversion instructions (False); the bits are the same for finite values."""
-    _lib.load().kvbm_xfer_set_cast_softconv(1 if on else 0)
+def set_cast_softconv(quarters: int) -> None:
+    """Pipelined fp8 casts of bf16 data: how many quarters (0, 1, 2 or 4) of the conversions run on
+    the integer / FMA pipes instead of the conversion instructions; the bits are the same for
+    finite values."""
+    _lib.load().kvbm_xfer_set_cast_softconv(int(quarters))
 
 
 def kv_checksum(layout, ids, *, layer_begin: int = 0, num_layers: int | None = None, head_offset: int = 0,

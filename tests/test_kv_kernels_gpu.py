@@ -105,18 +105,18 @@ def _ref_quant(x: torch.Tensor):
     return q, scale
 
 
-@pytest.mark.parametrize("engine", ["tile", "tile_sw", "tile1", "tma"])
+@pytest.mark.parametrize("engine", ["tile", "tile_sw1", "tile_sw", "tile1", "tma"])
 @pytest.mark.parametrize("src_dtype", [torch.bfloat16, torch.float16])
 def test_fp8_quant_dequant(engine, src_dtype):
     # tile: the software-pipelined cast kernel; tile_sw: the same with the conversions on the
     # integer / FMA pipes; tile1: the one-tile-at-a-time kernel
     kv_ops.set_cast_pipeline(engine != "tile1")
-    kv_ops.set_cast_softconv(engine == "tile_sw")
+    kv_ops.set_cast_softconv({"tile_sw1": 1, "tile_sw": 4}.get(engine, 0))
     try:
-        _fp8_roundtrip("tile" if engine in ("tile1", "tile_sw") else engine, src_dtype)
+        _fp8_roundtrip("tile" if engine.startswith("tile") else engine, src_dtype)
     finally:
         kv_ops.set_cast_pipeline(True)
-        kv_ops.set_cast_softconv(False)
+        kv_ops.set_cast_softconv(0)
 
 
 def _fp8_roundtrip(engine, src_dtype):
