@@ -60,8 +60,9 @@ def _ce_regions(src: KvLayout, s_ids, dst: KvLayout, d_ids):
     return sp, dp, c.bytes_per_chunk
 
 
-# on-device engines: tile (pipelined cast kernel), tile_sw1 / tile_sw2 / tile_sw (a quarter, half or
-# all of its bf16 <-> fp8 conversions on the integer / FMA pipes), tile1 (one tile at a time), tma
+# on-device engines: tile (pipelined cast kernel, every conversion in hardware), tile_sw1 / tile_sw2 /
+# tile_sw (a quarter, half or all of its bf16 <-> fp8 conversions on the integer / FMA pipes; the
+# library default is none for quantise, a quarter for dequantise), tile1 (one tile at a time), tma
 CAST_ENGINES = ("tile", "tile_sw1", "tile_sw2", "tile_sw", "tile1", "tma")
 
 
@@ -135,7 +136,8 @@ def run(args) -> list[dict]:
             # tile1: the fp8 casts on the one-tile-at-a-time kernel (tile: the pipelined one; tile_sw:
             # the pipelined one converting on the integer / FMA pipes)
             kv_ops.set_cast_pipeline(engine != "tile1")
-            kv_ops.set_cast_softconv({"tile_sw1": 1, "tile_sw2": 2, "tile_sw": 4}.get(engine, 0))
+            sq = {"tile_sw1": 1, "tile_sw2": 2, "tile_sw": 4}.get(engine, 0)
+            kv_ops.set_cast_softconv(sq, sq)
             eng = "tile" if engine.startswith("tile") else engine
             ms = _time(lambda: kv_ops.kv_transfer(a, s_ids, b, d_ids, engine=eng), args.iters, args.warmup,
                        flush)
@@ -149,7 +151,8 @@ def run(args) -> list[dict]:
             back = KvLayout.allocate(cfg, "fully_contiguous", nhd)
             for engine in [e for e in CAST_ENGINES if e in args.engines.split(",")]:
                 kv_ops.set_cast_pipeline(engine != "tile1")
-                kv_ops.set_cast_softconv({"tile_sw1": 1, "tile_sw2": 2, "tile_sw": 4}.get(engine, 0))
+                sq = {"tile_sw1": 1, "tile_sw2": 2, "tile_sw": 4}.get(engine, 0)
+            kv_ops.set_cast_softconv(sq, sq)
                 eng = "tile" if engine.startswith("tile") else engine
                 ms = _time(lambda: kv_ops.kv_transfer(b, d_ids, back, s_ids, engine=eng), args.iters,
                            args.warmup, flush)
@@ -160,7 +163,7 @@ def run(args) -> list[dict]:
                 results.append(r)
                 print(json.dumps(r), flush=True)
         kv_ops.set_cast_pipeline(True)
-        kv_ops.set_cast_softconv(0)
+        kv_ops.set_cast_softconv()
         if name == "g1_to_g1_copy" and "ce" in args.engines.split(","):
             src_p = [a.layer_base(0) + int(x) * a.block_stride for x in s_ids.tolist()]
             dst_p = [b.layer_base(0) + int(x) * b.block_stride for x in d_ids.tolist()]

@@ -734,7 +734,12 @@ int common_align(std::initializer_list<int64_t> xs) {
 }
 
 bool g_cast_pipe = true;
-int g_cast_soft = 0;  // quarters of the bf16 <-> fp8 conversions done on the integer / FMA pipes (0, 1, 2, 4)
+// Quarters (0, 1, 2, 4) of the bf16 <-> fp8 conversions done on the integer / FMA pipes. Measured on
+// B200 (128 Llama-3-8B blocks): quantise is fastest all in hardware (software conversion costs more
+// than the conversion pipe saves); dequantise is fastest with one quarter in software (+8 %), which
+// offloads the saturated conversion pipe without saturating the integer pipe.
+int g_cast_soft_quant = 0;
+int g_cast_soft_dequant = 1;
 
 template <int KIND, int U>
 cudaError_t launch_tile(const XferParams& P, int max_ctas, cudaStream_t stream) {
@@ -748,9 +753,10 @@ cudaError_t launch_tile(const XferParams& P, int max_ctas, cudaStream_t stream) 
       const size_t smem = static_cast<size_t>(kWarpsPerCta) * cast_stages(KIND) * tile_bytes;
       auto kern = kv_cast_pipe_kernel<KIND, 0>;
       if constexpr (KIND == kQuantBf16 || KIND == kDequantBf16) {
-        if (g_cast_soft == 1) kern = kv_cast_pipe_kernel<KIND, 1>;
-        if (g_cast_soft == 2) kern = kv_cast_pipe_kernel<KIND, 2>;
-        if (g_cast_soft >= 4) kern = kv_cast_pipe_kernel<KIND, 4>;
+        const int q = KIND == kQuantBf16 ? g_cast_soft_quant : g_cast_soft_dequant;
+        if (q == 1) kern = kv_cast_pipe_kernel<KIND, 1>;
+        if (q == 2) kern = kv_cast_pipe_kernel<KIND, 2>;
+        if (q >= 4) kern = kv_cast_pipe_kernel<KIND, 4>;
       }
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
       if (e != cudaSuccess) return e;
@@ -1336,10 +1342,14 @@ extern "C" int kvbm_xfer_status(int device, int reset) {
 // software-pipelined persistent kernel; 0: the one-tile-at-a-time kernel.
 extern "C" void kvbm_xfer_set_cast_pipeline(int on) { g_cast_pipe = on != 0; }
 
-// Quarters (0, 1, 2 or 4) of the pipelined cast kernel's bf16 <-> fp8
-// conversions done on the integer / FMA pipes (same bits) instead of with the
-// conversion instructions, to balance the two pipes; 0 by default.
-extern "C" void kvbm_xfer_set_cast_softconv(int quarters) { g_cast_soft = quarters < 0 ? 0 : quarters; }
+// Quarters (0, 1, 2 or 4) of the pipelined cast kernel's bf16 -> fp8 and
+// fp8 -> bf16 conversions done on the integer / FMA pipes (same bits) instead
+// of with the conversion instructions, to balance the two pipes. Defaults:
+// 0 for quantise, 1 for dequantise.
+extern "C" void kvbm_xfer_set_cast_softconv(int quant_quarters, int dequant_quarters) {
+  g_cast_soft_quant = quant_quarters < 0 ? 0 : quant_quarters;
+  g_cast_soft_dequant = dequant_quarters < 0 ? 0 : dequant_quarters;
+}
 
 extern "C" void kvbm_xfer_set_wait_limit_ns(uint64_t ns) { g_wait_ns_override = ns; }
 

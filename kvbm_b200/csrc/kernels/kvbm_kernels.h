@@ -112,10 +112,11 @@ void kvbm_xfer_set_wait_limit_ns(uint64_t ns);
 // 1 (default): fp8 casts whose head tile fits one register batch per lane run
 // the software-pipelined persistent cast kernel; 0: the one-tile-at-a-time kernel.
 void kvbm_xfer_set_cast_pipeline(int on);
-// Quarters (0, 1, 2 or 4) of the pipelined cast kernel's bf16 <-> fp8
-// conversions done on the integer / FMA pipes (bit-identical for finite
-// values) instead of with the conversion instructions; 0 by default.
-void kvbm_xfer_set_cast_softconv(int quarters);
+// Quarters (0, 1, 2 or 4) of the pipelined cast kernel's bf16 -> fp8 and
+// fp8 -> bf16 conversions done on the integer / FMA pipes (bit-identical for
+// finite values) instead of with the conversion instructions. Defaults: 0 for
+// quantise, 1 for dequantise.
+void kvbm_xfer_set_cast_softconv(int quant_quarters, int dequant_quarters);
 
 // Split-by-bytes batched copy of num_pairs (src, dst) regions of equal size.
 // `align` is the alignment (16, 8, 4, 2 or 1) that every pointer and

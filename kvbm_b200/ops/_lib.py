@@ -75,7 +75,7 @@ _SIGS = {
     "kvbm_xfer_status": (_INT, [_INT, _INT]),
     "kvbm_xfer_set_wait_limit_ns": (None, [_U64]),
     "kvbm_xfer_set_cast_pipeline": (None, [_INT]),
-    "kvbm_xfer_set_cast_softconv": (None, [_INT]),
+    "kvbm_xfer_set_cast_softconv": (None, [_INT, _INT]),
     "kvbm_copy_pairs": (_INT, [_VP, _VP, _U64, _U64, _INT, _INT, _VP]),
     "kvbm_universal_from_block": (_INT, [_VP, _VP, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _INT, _INT, _VP]),
     "kvbm_block_from_universal": (_INT, [_VP, _VP, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _SZ, _INT, _INT, _VP]),

@@ -155,11 +155,16 @@ def set_cast_pipeline(on: bool) -> None:
     _lib.load().kvbm_xfer_set_cast_pipeline(1 if on else 0)
 
 
-def set_cast_softconv(quarters: int) -> None:
+CAST_SOFTCONV_DEFAULT = (0, 1)  # (quantise, dequantise) quarters, the measured best on B200
+
+
+def set_cast_softconv(quant_quarters: int | None = None, dequant_quarters: int | None = None) -> None:
     """Pipelined fp8 casts of bf16 data: how many quarters (0, 1, 2 or 4) of the conversions run on
-    the integer / FMA pipes instead of the conversion instructions; the bits are the same for
-    finite values."""
-    _lib.load().kvbm_xfer_set_cast_softconv(int(quarters))
+    the integer / FMA pipes instead of the conversion instructions, per direction (None: the
+    default); the bits are the same for finite values."""
+    q = CAST_SOFTCONV_DEFAULT[0] if quant_quarters is None else int(quant_quarters)
+    d = CAST_SOFTCONV_DEFAULT[1] if dequant_quarters is None else int(dequant_quarters)
+    _lib.load().kvbm_xfer_set_cast_softconv(q, d)
 
 
 def kv_checksum(layout, ids, *, layer_begin: int = 0, num_layers: int | None = None, head_offset: int = 0,

@@ -111,12 +111,13 @@ def test_fp8_quant_dequant(engine, src_dtype):
     # tile: the software-pipelined cast kernel; tile_sw: the same with the conversions on the
     # integer / FMA pipes; tile1: the one-tile-at-a-time kernel
     kv_ops.set_cast_pipeline(engine != "tile1")
-    kv_ops.set_cast_softconv({"tile_sw1": 1, "tile_sw": 4}.get(engine, 0))
+    sq = {"tile_sw1": 1, "tile_sw": 4}.get(engine, 0)
+    kv_ops.set_cast_softconv(sq, sq)
     try:
         _fp8_roundtrip("tile" if engine.startswith("tile") else engine, src_dtype)
     finally:
         kv_ops.set_cast_pipeline(True)
-        kv_ops.set_cast_softconv(0)
+        kv_ops.set_cast_softconv()
 
 
 def _fp8_roundtrip(engine, src_dtype):
