@@ -1,0 +1,95 @@
+"""Attach a live vLLM engine to the hub's prefill router.
+
+``try_wrap_engine(vllm_config, engine)`` looks at the engine's connector
+configuration (``kv_transfer_config.kv_connector_extra_config``: the
+block-manager configuration, with its ``default`` / ``leader`` profiles
+applied) and, when it names a hub and the ``prefill`` disaggregation role,
+registers the process as a prefill target: it returns a
+:class:`PrefillRouterHandler` whose dispatch lambda turns every routed
+request into an ``engine.generate`` call (the prompt's token ids, one output
+token, ``kv_transfer_params`` naming the decode instance that waits for the
+KV) on the engine's event loop, and completes the router's call when that
+generation ends. Decode or aggregated engines, and engines with no hub, get
+``None``.
+
+Parity: python/kvbm/hub/detect.py (try_wrap_engine), the dispatch lambda of
+python/kvbm/hub/dispatch_lambda.py, src/hub/prefill_router.rs:133-245.
+"""
+
+from __future__ import annotations
+
+import asyncio
+import logging
+from typing import Any
+
+from ..connector.leader import REMOTE_DECODE_KEY
+from ..engine.cd_plane import decode_dispatch
+from .client import CompletionEvent, PrefillRouterHandler
+
+log = logging.getLogger(__name__)
+
+
+def connector_settings(vllm_config: Any) -> tuple[str | None, str | None]:
+    """(hub url, disaggregation role) from the engine's connector configuration."""
+    ktc = getattr(vllm_config, "kv_transfer_config", None)
+    extra = dict(getattr(ktc, "kv_connector_extra_config", None) or {})
+    merged: dict = {}
+    for layer in ({k: v for k, v in extra.items() if k not in ("default", "leader", "worker")},
+                  extra.get("default") or {}, extra.get("leader") or {}):
+        for k, v in layer.items():
+            if isinstance(v, dict) and isinstance(merged.get(k), dict):
+                merged[k] = {**merged[k], **v}
+            else:
+                merged[k] = v
+    return (merged.get("hub") or {}).get("url"), (merged.get("disagg") or {}).get("role")
+
+
+def _vllm_params(max_tokens: int, kv_transfer_params: dict):
+    from vllm import SamplingParams
+
+    return SamplingParams(max_tokens=max_tokens, extra_args={"kv_transfer_params": kv_transfer_params})
+
+
+def make_dispatch_lambda(engine: Any, loop: asyncio.AbstractEventLoop, max_tokens: int = 1, make_params=None):
+    """A dispatch lambda for :class:`PrefillRouterHandler`: runs each routed prefill as
+    ``engine.generate`` on ``loop`` and completes the router's event when it finishes.
+    ``make_params(max_tokens, kv_transfer_params)`` builds the sampling parameters (vLLM's by
+    default)."""
+    make_params = make_params or _vllm_params
+
+    def dispatch(request: dict, done: CompletionEvent) -> None:
+        d = decode_dispatch(bytes.fromhex(request["payload"]))
+        params = dict(d["params"])
+        params[REMOTE_DECODE_KEY] = d["decode"]
+
+        async def run():
+            sp = make_params(max_tokens, params)
+            prompt = {"prompt_token_ids": [int(t) for t in d["tokens"]]}
+            last = None
+            async for out in engine.generate(prompt, sp, d["request_id"]):
+                last = out
+            return {"request_id": d["request_id"], "finished": bool(getattr(last, "finished", True))}
+
+        fut = asyncio.run_coroutine_threadsafe(run(), loop)
+
+        def finish(f):
+            if f.exception() is not None:
+                done.fail(f"{type(f.exception()).__name__}: {f.exception()}")
+            else:
+                done.complete(f.result())
+
+        fut.add_done_callback(finish)
+
+    return dispatch
+
+
+def try_wrap_engine(vllm_config: Any, engine: Any, loop: asyncio.AbstractEventLoop | None = None,
+                    max_concurrency: int = 4, make_params=None) -> PrefillRouterHandler | None:
+    hub_url, role = connector_settings(vllm_config)
+    if not hub_url or role != "prefill":
+        return None
+    loop = loop or asyncio.get_running_loop()
+    handler = PrefillRouterHandler(hub_url, make_dispatch_lambda(engine, loop, make_params=make_params),
+                                   max_concurrency=max_concurrency)
+    log.info("prefill router attached (instance %s, hub %s)", handler.instance_id, hub_url)
+    return handler

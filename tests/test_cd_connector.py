@@ -211,3 +211,59 @@ def test_decode_dispatch_routed_through_the_hub_to_a_prefill_server():
         server.close()
         plane.close()
         hub.stop()
+
+
+def test_engine_attached_to_the_prefill_router_serves_routed_prefills():
+    """try_wrap_engine on a prefill-role engine config registers with the hub; a decode leader's
+    dispatch routed by the hub becomes an engine.generate call carrying the decode instance in its
+    kv_transfer_params; decode-role configs are not attached."""
+    import asyncio
+    from types import SimpleNamespace
+
+    from kvbm_b200.engine.cd_plane import HubRouterPlane
+    from kvbm_b200.hub.client import HubClient
+    from kvbm_b200.hub.detect import connector_settings, try_wrap_engine
+    from kvbm_b200.hub.server import HubServer
+    from kvbm_b200.runtime.messenger import wait_until
+
+    hub = HubServer(max_seq_len=4096, ttl=5.0).start()
+    calls = []
+
+    class FakeAsyncEngine:
+        async def generate(self, prompt, params, request_id):
+            calls.append((request_id, prompt["prompt_token_ids"], params))
+            await asyncio.sleep(0.01)
+            yield SimpleNamespace(finished=True)
+
+    def cfg(extra):
+        return SimpleNamespace(kv_transfer_config=SimpleNamespace(kv_connector_extra_config=extra))
+
+    assert connector_settings(cfg({"leader": {"hub": {"url": "u"}, "disagg": {"role": "prefill"}}})) == ("u", "prefill")
+    loop = asyncio.new_event_loop()
+    t = threading.Thread(target=loop.run_forever, daemon=True)
+    t.start()
+    client = HubClient(hub.url)
+    plane = HubRouterPlane(client, timeout=10.0)
+    handler = None
+    try:
+        assert try_wrap_engine(cfg({"hub": {"url": hub.url}, "disagg": {"role": "decode"}}), FakeAsyncEngine(),
+                               loop) is None
+        handler = try_wrap_engine(cfg({"hub": {"url": hub.url}, "disagg": {"role": "prefill"}}), FakeAsyncEngine(),
+                                  loop, make_params=lambda n, p: {"max_tokens": n, "kv_transfer_params": p})
+        assert handler is not None and wait_until(lambda: len(client.targets()) == 1, 5.0)
+        L = decode_leader(plane)
+        L.create_slot(KvbmRequest("vllm-routed", list(range(48))))
+        assert L.get_num_new_matched_tokens("vllm-routed", 0) == (48, True)
+        L.update_state_after_alloc("vllm-routed", [8, 9, 10], 48)
+        res = plane.futures[0].result(timeout=10)
+        assert res["forwarded"] and res["result"]["result"] == {"request_id": "vllm-routed", "finished": True}
+        [(rid, toks, params)] = calls
+        assert rid == "vllm-routed" and toks == list(range(48)) and params["max_tokens"] == 1
+        ktp = params["kv_transfer_params"]
+        assert ktp[REMOTE_DECODE_KEY]["dst_ids"] == [8, 9, 10] and ktp[REMOTE_DECODE_KEY]["instance"] == 3
+    finally:
+        if handler is not None:
+            handler.close()
+        plane.close()
+        loop.call_soon_threadsafe(loop.stop)
+        hub.stop()
