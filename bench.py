@@ -41,6 +41,7 @@ Reported (rank 0, one JSON line):
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -111,6 +112,8 @@ def main(argv=None) -> int:
     p.add_argument("--layer-batch", type=int, default=8, help="layers per push launch")
     p.add_argument("--layers", type=int, default=None, help="override layer count (debug only: invalid for the metric)")
     p.add_argument("--no-graphs", action="store_true")
+    p.add_argument("--one-stream", action="store_true",
+                   help="colocated: run the decode instance on the prefill's stream (no overlap)")
     p.add_argument("--no-bulk-peer", action="store_true",
                    help="peer pushes with consumer-warp stores instead of TMA bulk stores")
     p.add_argument("--out", default=None)
@@ -165,9 +168,17 @@ def main(argv=None) -> int:
         else:
             role, pre = "decode", None
             dec = PdInstance("decode", model, cfg, iid, plane, directory, shared=True, prefill_target=1000 + rank - half)
-    for inst in (dec, pre):
-        if inst is not None:
-            inst.warmup()
+    # colocated: the decode instance runs on its own stream, so its memory-bound decode steps overlap
+    # the prefill instance's compute-bound prefill on the same GPU (the mailbox orders a request's
+    # decode after its push, as across GPUs)
+    dec_stream = torch.cuda.Stream() if world == 1 and not args.one_stream else None
+    dec_ctx = (lambda: torch.cuda.stream(dec_stream)) if dec_stream is not None else contextlib.nullcontext
+    if dec is not None:
+        with dec_ctx():
+            dec.warmup()
+    if pre is not None:
+        pre.warmup()
+    torch.cuda.synchronize()
 
     gen = torch.Generator().manual_seed(1234 + rank)
     total = args.warmup + args.steps
@@ -207,7 +218,8 @@ def main(argv=None) -> int:
             prefill_until((k + 1) * C)
             return
         if k not in submitted:
-            submit(k)
+            with dec_ctx():
+                submit(k)
         while not wave_done(k):
             if pre is not None:
                 # colocated: one prefill step (one request's prompt, pushed layer batch by layer batch),
@@ -215,12 +227,14 @@ def main(argv=None) -> int:
                 pre.pull()
                 if pre.engine.has_unfinished() or pre.engine._delayed:
                     pre.step()
-            dec.step()
+            with dec_ctx():
+                dec.step()
             if (role == "decode" and k + 1 < total and k + 1 != args.warmup and k + 1 not in submitted
                     and wave_received(k)):
                 # the next wave's prefill (on the prefill GPU) overlaps this wave's decode; not across the
                 # timed edge, and not when both share one GPU (colocated: waves run one after another)
-                submit(k + 1)
+                with dec_ctx():
+                    submit(k + 1)
 
     timed: list[Request] = []
     for k in range(args.warmup):
@@ -232,11 +246,15 @@ def main(argv=None) -> int:
     launches0 = _lib.launch_count()
     t_begin = torch.cuda.Event(enable_timing=True)
     t_begin.record()
+    if dec_stream is not None:
+        dec_stream.wait_stream(torch.cuda.current_stream())
     for k in range(args.warmup, total):
         run_wave(k)
         if dec is not None:
             timed += submitted[k]
     t_end = torch.cuda.Event(enable_timing=True)
+    if dec_stream is not None:
+        torch.cuda.current_stream().wait_stream(dec_stream)
     t_end.record()
     barrier()
     launches = _lib.launch_count() - launches0
@@ -302,6 +320,8 @@ def main(argv=None) -> int:
                 "seq_len": cfg.prompt_len,
                 "gen_len": cfg.gen_len,
                 "parallelism": "colocated" if world == 1 else f"{pairs}P{pairs}D tp1",
+                "colocated_streams": ("separate decode stream" if dec_stream is not None else "one stream")
+                if world == 1 else None,
                 "push_engine": cfg.push_engine, "push_bulk_peer": cfg.push_bulk_peer,
                 "layer_batch": cfg.layer_batch,
                 "cd_policy": cfg.selection,
