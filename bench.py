@@ -112,8 +112,8 @@ def main(argv=None) -> int:
     p.add_argument("--layer-batch", type=int, default=8, help="layers per push launch")
     p.add_argument("--layers", type=int, default=None, help="override layer count (debug only: invalid for the metric)")
     p.add_argument("--no-graphs", action="store_true")
-    p.add_argument("--one-stream", action="store_true",
-                   help="colocated: run the decode instance on the prefill's stream (no overlap)")
+    p.add_argument("--decode-stream", action="store_true",
+                   help="colocated: run the decode instance on its own stream, overlapping the prefill")
     p.add_argument("--no-bulk-peer", action="store_true",
                    help="peer pushes with consumer-warp stores instead of TMA bulk stores")
     p.add_argument("--out", default=None)
@@ -171,7 +171,7 @@ def main(argv=None) -> int:
     # colocated: the decode instance runs on its own stream, so its memory-bound decode steps overlap
     # the prefill instance's compute-bound prefill on the same GPU (the mailbox orders a request's
     # decode after its push, as across GPUs)
-    dec_stream = torch.cuda.Stream() if world == 1 and not args.one_stream else None
+    dec_stream = torch.cuda.Stream() if world == 1 and args.decode_stream else None
     dec_ctx = (lambda: torch.cuda.stream(dec_stream)) if dec_stream is not None else contextlib.nullcontext
     if dec is not None:
         with dec_ctx():
