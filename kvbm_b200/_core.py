@@ -187,12 +187,14 @@ class ConnectorLeader:
                           registry=g2.registry) if g3n else None
         # the registered workers (one per TP rank, each serving its shard) carry out the leader's own
         # block operations; per-step ops reach them through the connector metadata
-        workers = ParallelWorkers([])
         if self._workers:
             from .engine.spmd import SpmdParallelWorkers
 
-            workers = SpmdParallelWorkers(self.runtime.messenger, [self._workers[r][0] for r in sorted(self._workers)])
-        self._impl = _Leader(InstanceLeader(g2, workers, g3=g3), self.block_size,
+            leader = InstanceLeader(g2, SpmdParallelWorkers(self.runtime.messenger,
+                                                            [self._workers[r][0] for r in sorted(self._workers)]), g3=g3)
+        else:
+            leader = InstanceLeader.scheduler_side(g2, g3)
+        self._impl = _Leader(leader, self.block_size,
                              offload_enabled=layout.get("g2_blocks", 0) > 0, num_workers=max(1, len(self._workers)))
         # operator / peer control plane on the runtime's messenger (describe, reset, metrics)
         import dataclasses

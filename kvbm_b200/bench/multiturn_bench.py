@@ -39,7 +39,7 @@ import torch.distributed as dist
 
 from ..connector.leader import ConnectorLeader
 from ..connector.worker import ConnectorWorker
-from ..engine.leader import InstanceLeader, ParallelWorkers
+from ..engine.leader import InstanceLeader
 from ..logical.manager import BlockManager, Tier
 from ..models.llama import LlamaConfig, LlamaModel
 from ..serving.engine import EngineConfig, LLMEngine, Request
@@ -62,7 +62,7 @@ def run(a, rank: int = 0) -> dict:
     g1_blocks = max(int(live_blocks * a.g1_fraction), 2 * max_req_blocks) + 1
     g2_blocks = int(live_blocks * 1.2) + 64
     kcfg = KvbmConfig.load({"cache": {"host": {"num_blocks": g2_blocks}}}, env={}, system_toml=None)
-    leader = ConnectorLeader(InstanceLeader(BlockManager(g2_blocks, bs, "lineage", Tier.G2), ParallelWorkers([])),
+    leader = ConnectorLeader(InstanceLeader.scheduler_side(BlockManager(g2_blocks, bs, "lineage", Tier.G2)),
                              bs)
     worker = ConnectorWorker(kcfg, device=local, block_size=bs)
     eng = LLMEngine(model, EngineConfig(num_gpu_blocks=g1_blocks, block_size=bs, max_num_seqs=a.batch,

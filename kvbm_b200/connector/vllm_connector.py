@@ -98,7 +98,7 @@ def _define():
 
         def __init__(self, vllm_config, role, kv_cache_config=None):
             super().__init__(vllm_config=vllm_config, role=role, kv_cache_config=kv_cache_config)
-            from ..engine.leader import InstanceLeader, ParallelWorkers
+            from ..engine.leader import InstanceLeader
             from ..logical.manager import BlockManager, Tier
             from ..utils.config import KvbmConfig
             from .worker import ConnectorWorker, blocks_for_bytes
@@ -116,7 +116,7 @@ def _define():
                 g2 = BlockManager(max(1, g2n), bs, cfg.cache.inactive_backend, Tier.G2,
                                   duplicate_policy=cfg.cache.duplicate_policy)
                 g3 = BlockManager(g3n, bs, cfg.cache.inactive_backend, Tier.G3, registry=g2.registry) if g3n else None
-                self._leader = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([]), g3=g3), bs,
+                self._leader = ConnectorLeader(InstanceLeader.scheduler_side(g2, g3), bs,
                                                offload_enabled=g2n > 0,
                                                decode_offload=os.getenv("KVBM_DECODE_OFFLOAD", "false") == "true")
                 self._worker = None

@@ -97,6 +97,16 @@ class InstanceLeader:
         self._lock = threading.Lock()
         self.stats = {"find_calls": 0, "g2_hits": 0, "g3_hits": 0, "onboarded_blocks": 0, "offloaded_blocks": 0}
 
+    @classmethod
+    def scheduler_side(cls, g2: BlockManager, g3: BlockManager | None = None, **kw) -> "InstanceLeader":
+        """The leader a connector's scheduler process holds: it owns the G2/G3 pools'
+        logical state (matching, registration, eviction) while the bytes are moved by
+        the connector's workers in the model-runner processes, which receive their
+        onboard / offload / stage / spill ops in the per-step connector metadata. It
+        has no in-process workers, so a direct ``onboard`` or ``stage_g3_to_g2``
+        raises instead of silently moving nothing."""
+        return cls(g2, ParallelWorkers([]), g3=g3, **kw)
+
     # --------------------------------------------------------------- find
     def find_matches(self, seq_hashes: list[int], options: FindMatchesOptions | None = None) -> FindMatchesResult:
         opts = options or FindMatchesOptions()
@@ -176,6 +186,9 @@ class InstanceLeader:
             raise ValueError("one G1 destination per G2 block")
         if not g2_blocks:
             return TransferCompleteNotification.ready()
+        if not len(self.workers):
+            raise RuntimeError("this leader has no in-process workers; onboards travel to the connector's "
+                               "workers in the step's connector metadata")
         ids = [b.block_id for b in g2_blocks]
         self.stats["onboarded_blocks"] += len(ids)
         if layerwise:

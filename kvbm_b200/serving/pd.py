@@ -42,7 +42,7 @@ import torch
 from ..connector.leader import REMOTE_DECODE_KEY, ConnectorLeader
 from ..connector.worker import ConnectorWorker
 from ..engine.cd import ConditionalDisagg, InflightBudget, SelectionPolicy
-from ..engine.leader import InstanceLeader, ParallelWorkers
+from ..engine.leader import InstanceLeader
 from ..logical.manager import BlockManager, Tier
 from ..models.llama import LlamaConfig, LlamaModel
 from ..utils.config import KvbmConfig
@@ -109,7 +109,7 @@ class PdInstance:
         g2 = BlockManager(1, bs, "lru", Tier.G2)
         self.leader = None
         if tp_rank == 0:
-            self.leader = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([])), bs, offload_enabled=False, cd=cd,
+            self.leader = ConnectorLeader(InstanceLeader.scheduler_side(g2), bs, offload_enabled=False, cd=cd,
                                           plane=plane if role == "decode" else None, prefill_target=prefill_target,
                                           instance_id=self.instance_id, mailbox_slots=slots,
                                           recv_timeout_s=cfg.recv_timeout_s, num_workers=tp_size, tp_size=tp_size,

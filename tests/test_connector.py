@@ -2,16 +2,18 @@
 save-cursor offloads, delayed frees; and the step-metadata wire format."""
 
 
+import pytest
+
 from kvbm_b200.connector.leader import ConnectorLeader, KvbmRequest, SchedulerOutputLite
 from kvbm_b200.connector.protocol import (ConnectorMetadata, OffloadOp, OnboardOp, PushOp, RecvOp, SpillOp,
                                           StageOp)
-from kvbm_b200.engine.leader import InstanceLeader, ParallelWorkers
+from kvbm_b200.engine.leader import InstanceLeader
 from kvbm_b200.logical.manager import BlockManager, Tier
 
 
 def make_leader(g2_blocks=64, bs=16):
     g2 = BlockManager(g2_blocks, bs, "lineage", Tier.G2)
-    return ConnectorLeader(InstanceLeader(g2, ParallelWorkers([])), bs)
+    return ConnectorLeader(InstanceLeader.scheduler_side(g2), bs)
 
 
 def step(leader, n, sched):
@@ -91,7 +93,7 @@ def test_decode_tokens_extend_sequence_when_enabled():
 
 def test_offloaded_blocks_match_only_after_every_worker_reports_the_copy():
     g2 = BlockManager(64, 16, "lineage", Tier.G2)
-    L = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([])), 16, num_workers=2)
+    L = ConnectorLeader(InstanceLeader.scheduler_side(g2), 16, num_workers=2)
     prompt = list(range(64))
     L.create_slot(KvbmRequest("a", prompt))
     L.update_state_after_alloc("a", list(range(4)), 0)
@@ -137,7 +139,7 @@ def test_g2_spills_to_g3_and_g3_hits_are_staged_by_the_workers():
     in G2 only once the onboard is reported received."""
     g2 = BlockManager(4, 16, "lru", Tier.G2)
     g3 = BlockManager(32, 16, "lru", Tier.G3, registry=g2.registry)
-    L = ConnectorLeader(InstanceLeader(g2, ParallelWorkers([]), g3=g3), 16)
+    L = ConnectorLeader(InstanceLeader.scheduler_side(g2, g3), 16)
     prompt = list(range(64))
     L.create_slot(KvbmRequest("a", prompt))
     L.update_state_after_alloc("a", [0, 1, 2, 3, 4], 0)
@@ -169,3 +171,21 @@ def test_g2_spills_to_g3_and_g3_hits_are_staged_by_the_workers():
     L.update_connector_output(finished_recving={"c"})
     assert g2.count_prefix(L.slots["c"].seq.sequence_hashes) == 4
     assert L.tier_stats["staged_from_g3"] == 4
+
+
+def test_scheduler_side_leader_refuses_direct_moves():
+    """The scheduler-side leader owns G2/G3 state only: a direct onboard or G3 stage
+    raises (the bytes move through the connector's workers), it never reports a copy
+    that did not happen."""
+    g2 = BlockManager(8, 16, "lru", Tier.G2)
+    g3 = BlockManager(8, 16, "lru", Tier.G3, registry=g2.registry)
+    leader = InstanceLeader.scheduler_side(g2, g3)
+    blocks = g2.allocate_blocks(1)
+    imm = g2.register_mutable(blocks, [123])
+    with pytest.raises(RuntimeError, match="no in-process workers"):
+        leader.onboard(imm, [0])
+    for b in imm:
+        b.release()
+    g3b = g3.register_mutable(g3.allocate_blocks(1), [456])
+    with pytest.raises(RuntimeError, match="PREPARE"):
+        leader.stage_g3_to_g2(g3b)

@@ -11,7 +11,7 @@ pytestmark = pytest.mark.gpu
 
 from kvbm_b200.connector.leader import ConnectorLeader, KvbmRequest, SchedulerOutputLite
 from kvbm_b200.connector.worker import ConnectorWorker
-from kvbm_b200.engine.leader import InstanceLeader, ParallelWorkers
+from kvbm_b200.engine.leader import InstanceLeader
 from kvbm_b200.logical.manager import BlockManager, Tier
 from kvbm_b200.models.llama import LlamaConfig, LlamaModel
 from kvbm_b200.utils.config import KvbmConfig
@@ -30,7 +30,7 @@ def test_offload_wipe_onboard_same_tokens(mode):
     worker = ConnectorWorker(kcfg, block_size=bs, num_kv_heads=cfg.kv_heads, head_size=cfg.head_dim)
     g1 = worker.register_kv_caches(kv, num_blocks=NB)
     assert g1.kind == "layer_separate" and not g1._block_first
-    leader = ConnectorLeader(InstanceLeader(BlockManager(64, bs, "lineage", Tier.G2), ParallelWorkers([])), bs)
+    leader = ConnectorLeader(InstanceLeader.scheduler_side(BlockManager(64, bs, "lineage", Tier.G2)), bs)
 
     prompt = torch.randint(0, cfg.vocab, (80,), dtype=torch.int32)
     ids_a = list(range(6))

@@ -12,7 +12,7 @@ from kvbm_b200.connector.leader import REMOTE_DECODE_KEY, ConnectorLeader
 from kvbm_b200.connector.protocol import ConnectorMetadata
 from kvbm_b200.engine.cd import ConditionalDisagg, InflightBudget, SelectionPolicy
 from kvbm_b200.engine.cd_plane import LocalPrefillPlane
-from kvbm_b200.engine.leader import InstanceLeader, ParallelWorkers
+from kvbm_b200.engine.leader import InstanceLeader
 from kvbm_b200.logical.manager import BlockManager, Tier
 from kvbm_b200.serving import engine as E
 
@@ -129,10 +129,10 @@ def _no_cuda(monkeypatch):
 
 def make_pair(concurrency=3, gen=4):
     plane = LocalPrefillPlane()
-    dl = ConnectorLeader(InstanceLeader(BlockManager(1, 16, "lru", Tier.G2), ParallelWorkers([])), 16,
+    dl = ConnectorLeader(InstanceLeader.scheduler_side(BlockManager(1, 16, "lru", Tier.G2)), 16,
                          offload_enabled=False, cd=ConditionalDisagg(SelectionPolicy("always"), InflightBudget(8)),
                          plane=plane, prefill_target=2, instance_id=1, mailbox_slots=8)
-    pl = ConnectorLeader(InstanceLeader(BlockManager(1, 16, "lru", Tier.G2), ParallelWorkers([])), 16,
+    pl = ConnectorLeader(InstanceLeader.scheduler_side(BlockManager(1, 16, "lru", Tier.G2)), 16,
                          offload_enabled=False, instance_id=2)
     dec = E.LLMEngine(FakeModel(), E.EngineConfig(num_gpu_blocks=64, max_num_seqs=concurrency, max_model_len=256,
                                                   max_tokens=gen, use_graphs=False), dl, FakeWorker(1))
@@ -215,7 +215,7 @@ def _tp_rank(rank, port, q):
         tp = TpComm.create([0, 1], nccl=False)
         leader = None
         if rank == 0:
-            leader = ConnectorLeader(InstanceLeader(BlockManager(1, 16, "lru", Tier.G2), ParallelWorkers([])), 16,
+            leader = ConnectorLeader(InstanceLeader.scheduler_side(BlockManager(1, 16, "lru", Tier.G2)), 16,
                                      offload_enabled=False, num_workers=2)
         model = T.FakeModel()
         eng = E.LLMEngine(model, E.EngineConfig(num_gpu_blocks=32, max_num_seqs=2, max_model_len=128, max_tokens=3,
@@ -286,7 +286,7 @@ def test_dropped_remote_prefill_times_out_and_is_recomputed_locally():
     receive gives up, reports the blocks as load errors, the engine prefills the prompt itself and the
     leader frees the in-flight budget and the mailbox slot."""
     plane = LocalPrefillPlane()
-    dl = ConnectorLeader(InstanceLeader(BlockManager(1, 16, "lru", Tier.G2), ParallelWorkers([])), 16,
+    dl = ConnectorLeader(InstanceLeader.scheduler_side(BlockManager(1, 16, "lru", Tier.G2)), 16,
                          offload_enabled=False, cd=ConditionalDisagg(SelectionPolicy("always"), InflightBudget(2)),
                          plane=plane, prefill_target=2, instance_id=1, mailbox_slots=2)
     model = FakeModel()
