@@ -139,7 +139,9 @@ def main(argv=None):
                 "ttft_p50_ms": round(ttft[len(ttft) // 2], 2), "ttft_p99_ms": round(ttft[int(len(ttft) * 0.99)], 2),
                 "prefilled_tokens": sum(r["prefilled"] for r in allr), "prompt_tokens": tot,
                 "g1_blocks": allr[0]["g1_blocks"], "g2_blocks": allr[0]["g2_blocks"],
-                "g1_fraction_of_live": round(allr[0]["g1_blocks"] / allr[0]["live_blocks_est"], 3)}
+                "g1_fraction_of_live": round(allr[0]["g1_blocks"] / allr[0]["live_blocks_est"], 3),
+                "ttft_p50_p99_ms_per_rank": [[round(r["ttft"][len(r["ttft"]) // 2], 1),
+                                              round(r["ttft"][int(len(r["ttft"]) * 0.99)], 1)] for r in allr]}
         print(json.dumps(line), flush=True)
         if a.out:
             with open(a.out, "a") as f:

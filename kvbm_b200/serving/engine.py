@@ -286,6 +286,13 @@ class LLMEngine:
         self.batch.capture()
         torch.cuda.synchronize(self.device)
 
+    def release_graphs(self) -> None:
+        """Drop the captured decode graph. A tensor-parallel instance's graph holds NCCL
+        all-reduces, and a process group cannot be destroyed while a graph that calls it
+        is alive, so instances release their graphs before their groups go away."""
+        torch.cuda.synchronize(self.device)
+        self.batch.graph = None
+
     def add_request(self, req: Request) -> None:
         if not self.is_scheduler:
             raise RuntimeError("requests enter a tensor-parallel instance on its rank 0")

@@ -150,4 +150,5 @@ class PdInstance:
         return out
 
     def shutdown(self) -> None:
+        self.engine.release_graphs()
         self.worker.shutdown()
