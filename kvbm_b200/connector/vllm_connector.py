@@ -53,6 +53,59 @@ def process_scheduler_output(step: int, so, slots: dict) -> SchedulerOutputLite:
     return out
 
 
+def disagg_leader_kwargs(cfg) -> dict:
+    """ConnectorLeader arguments for the configured disaggregation role (none when unset).
+
+    Every role joins the node's plane as ``disagg.instance_id``: any instance
+    accepts remote prefills and pushes their KV to the decode instance named in
+    the request's ``kv_transfer_params``. A decode instance also decides per
+    request (``disagg.selection``) and sends remote prefills to
+    ``disagg.prefill_instance`` over the plane at ``disagg.directory``, or,
+    with ``hub.url`` set and no prefill instance named, through the hub's
+    prefill router (which then picks the prefill engine)."""
+    dis = cfg.disagg
+    if dis is None or not dis.role:
+        return {}
+    if dis.instance_id is None:
+        raise ValueError("disagg.role needs disagg.instance_id (the scheduler and its workers share it)")
+    from ..engine.cd import ConditionalDisagg, InflightBudget, SelectionPolicy
+    from ..engine.cd_plane import HubRouterPlane, open_cd_services
+
+    plane, directory = open_cd_services(dis.directory)
+    kw: dict = {"instance_id": int(dis.instance_id), "directory": directory}
+    if dis.role in ("decode", "both") and dis.selection != "never":
+        slots = int(dis.mailbox_slots)
+        kw.update(cd=ConditionalDisagg(SelectionPolicy(dis.selection, dis.min_remote_prefill_tokens),
+                                       InflightBudget(dis.max_inflight or slots), fallback=dis.fallback),
+                  mailbox_slots=slots, recv_timeout_s=float(dis.recv_timeout_s))
+        if dis.prefill_instance is not None:
+            kw.update(plane=plane, prefill_target=int(dis.prefill_instance))
+        elif cfg.hub is not None and cfg.hub.url:
+            from ..hub.client import HubClient
+
+            # the router picks the prefill engine: contributor counts assume its TP degree divides ours
+            kw.update(plane=HubRouterPlane(HubClient(cfg.hub.url)), prefill_target=0, directory=None)
+        else:
+            raise ValueError("disagg decode role needs disagg.prefill_instance or hub.url")
+    return kw
+
+
+def disagg_worker_enable(worker, cfg, tp_rank: int, tp_size: int) -> bool:
+    """Join the plane from a model-runner worker once its KV caches are registered: publish
+    the pool (through CUDA IPC records of the engine's own KV tensors) and, on a decode
+    instance, the mailbox the prefill workers complete into."""
+    dis = cfg.disagg
+    if dis is None or not dis.role:
+        return False
+    from ..engine.cd_plane import open_cd_services
+
+    _, directory = open_cd_services(dis.directory)
+    receives = dis.role in ("decode", "both") and dis.selection != "never"
+    worker.enable_disagg(int(dis.instance_id), directory, mailbox_slots=int(dis.mailbox_slots) if receives else 0,
+                         shared=True, tp_rank=tp_rank, tp_size=tp_size)
+    return True
+
+
 def _base():
     from vllm.distributed.kv_transfer.kv_connector.v1.base import (KVConnectorBase_V1, KVConnectorMetadata,
                                                                   KVConnectorRole)
@@ -118,7 +171,10 @@ def _define():
                 g3 = BlockManager(g3n, bs, cfg.cache.inactive_backend, Tier.G3, registry=g2.registry) if g3n else None
                 self._leader = ConnectorLeader(InstanceLeader.scheduler_side(g2, g3), bs,
                                                offload_enabled=g2n > 0,
-                                               decode_offload=os.getenv("KVBM_DECODE_OFFLOAD", "false") == "true")
+                                               decode_offload=os.getenv("KVBM_DECODE_OFFLOAD", "false") == "true",
+                                               num_workers=max(1, int(self.info.get("tensor_parallel_size", 1))),
+                                               tp_size=max(1, int(self.info.get("tensor_parallel_size", 1))),
+                                               **disagg_leader_kwargs(cfg))
                 self._worker = None
             else:
                 cfg = KvbmConfig.for_worker(json.dumps(extra) if extra else None)
@@ -126,6 +182,7 @@ def _define():
                                                num_kv_heads=self.info["num_kv_heads"],
                                                head_size=self.info["head_size"])
                 self._leader = None
+            self._cfg = cfg
 
         # ------------------------------------------------ scheduler side
         @property
@@ -169,11 +226,17 @@ def _define():
             return None
 
         # --------------------------------------------------- worker side
+        def _join_plane(self):
+            tp = max(1, int(self.info.get("tensor_parallel_size", 1)))
+            disagg_worker_enable(self._worker, self._cfg, int(self.info.get("rank", 0)) % tp, tp)
+
         def register_kv_caches(self, kv_caches):
             self._worker.register_kv_caches(dict(kv_caches))
+            self._join_plane()
 
         def register_cross_layers_kv_cache(self, kv_cache, attn_backend=None):
             self._worker.register_cross_layers_kv_cache(kv_cache)
+            self._join_plane()
 
         def bind_connector_metadata(self, connector_metadata):
             super().bind_connector_metadata(connector_metadata)

@@ -108,6 +108,7 @@ class ConnectorWorker:
         self._send_events: dict[str, list[torch.cuda.Event]] = {}
         self._layer_events: list[torch.cuda.Event] = []
         self._load_errors: set[int] = set()
+        self.transfer_log: list | None = None
         self._pending_finished: set[str] = set()
         self._offload_steps: list[tuple[int, torch.cuda.Event]] = []
         self._spill_steps: list[int] = []
@@ -299,6 +300,10 @@ class ConnectorWorker:
     def bind_connector_metadata(self, raw: bytes) -> None:
         self._meta = ConnectorMetadata.decode(raw)
         self._pushes = []
+        if self.transfer_log is not None:  # which G1 blocks each remote prefill moves (set by tests and tools)
+            self.transfer_log += [("push", op.req_id, op.peer, list(op.src_ids), list(op.dst_ids))
+                                  for op in self._meta.push]
+            self.transfer_log += [("recv", op.req_id, list(op.g1_ids)) for op in self._meta.recv]
         if self._meta.push:
             dev = torch.device("cuda", self.device)
             for op in self._meta.push:

@@ -11,10 +11,13 @@ Two small services the decode and prefill instances share:
   and its strides) and its mailbox descriptor.
 
 Both come as an in-process version (prefill and decode in one process, e.g.
-sharing a GPU) and as a version over a key-value store (the
-``torch.distributed`` TCPStore of the serving group), and the plane also
-over the hub's disaggregation queue. Messages are msgpack maps; token ids
-travel as raw int32 bytes.
+sharing a GPU), as a version over a key-value store (the
+``torch.distributed`` TCPStore of the serving group) and as a version over
+a directory on the node's shared-memory filesystem (engines started
+independently, e.g. two vLLM servers); the plane also runs over the hub's
+disaggregation queue and its prefill router. :func:`open_cd_services`
+builds the pair from a URL. Messages are msgpack maps; token ids travel as
+raw int32 bytes.
 
 Parity: crates/kvbm-engine/src/remote/cd/wire.rs (PrefillPlane,
 PrefillDispatch), leader/cd/plane.rs (enqueue on the hub CD queue),
@@ -25,6 +28,8 @@ disagg.rs:167 (RemotePrefillParams).
 
 from __future__ import annotations
 
+import itertools
+import os
 import threading
 import time
 from collections import deque
@@ -217,3 +222,101 @@ class StorePeerDirectory(PeerDirectory):
                 raise TimeoutError(f"instance {instance} never published its pool")
             time.sleep(0.005)
         return msgpack.unpackb(self.store.get(key), raw=False)
+
+
+def _atomic_write(path: str, data: bytes) -> None:
+    tmp = f"{path}.{os.getpid()}.{threading.get_ident()}.tmp"
+    with open(tmp, "wb") as f:
+        f.write(data)
+    os.replace(tmp, path)
+
+
+class FilePrefillPlane(PrefillPlane):
+    """Over a directory shared by the node's engines (``/dev/shm`` by default).
+
+    A dispatch is one file ``{root}/plane/{target}/{ns}-{pid}-{n}.msg``,
+    written under a temporary name and renamed into place, so a consumer
+    never reads a partial message. A consumer claims a message by renaming
+    it (only one rename of a name succeeds) and then deletes it, so several
+    pollers of one instance never serve the same dispatch twice. Messages
+    are served in name order (their nanosecond timestamps)."""
+
+    def __init__(self, root: str):
+        self.root = os.path.join(root, "plane")
+        self._n = itertools.count()
+
+    def _dir(self, instance: int) -> str:
+        d = os.path.join(self.root, str(int(instance)))
+        os.makedirs(d, exist_ok=True)
+        return d
+
+    def dispatch(self, target, raw):
+        name = f"{time.time_ns():020d}-{os.getpid()}-{next(self._n)}.msg"
+        _atomic_write(os.path.join(self._dir(target), name), raw)
+
+    def poll(self, instance, limit=None):
+        d = self._dir(instance)
+        out = []
+        for name in sorted(n for n in os.listdir(d) if n.endswith(".msg")):
+            if limit is not None and len(out) >= limit:
+                break
+            src = os.path.join(d, name)
+            mine = f"{src}.{os.getpid()}.{threading.get_ident()}.claim"
+            try:
+                os.rename(src, mine)
+            except FileNotFoundError:  # another poller claimed it
+                continue
+            with open(mine, "rb") as f:
+                raw = f.read()
+            os.unlink(mine)
+            out.append(decode_dispatch(raw))
+        return out
+
+
+class FilePeerDirectory(PeerDirectory):
+    """Pool and mailbox descriptors as files ``{root}/peer/{instance}_{rank}.bin``
+    (msgpack, written atomically). ``info`` must be serialisable: an engine in
+    another process maps the pool through the descriptor's IPC handles."""
+
+    def __init__(self, root: str):
+        self.root = os.path.join(root, "peer")
+        os.makedirs(self.root, exist_ok=True)
+
+    def _path(self, instance: int, rank: int) -> str:
+        return os.path.join(self.root, f"{int(instance)}_{int(rank)}.bin")
+
+    def publish(self, instance, info, rank=0):
+        _atomic_write(self._path(instance, rank), msgpack.packb(info, use_bin_type=True))
+
+    def withdraw(self, instance, rank=0) -> None:
+        try:
+            os.unlink(self._path(instance, rank))
+        except FileNotFoundError:
+            pass
+
+    def lookup(self, instance, timeout_s=60.0, rank=0):
+        path = self._path(instance, rank)
+        deadline = time.monotonic() + timeout_s
+        while not os.path.exists(path):
+            if time.monotonic() >= deadline:
+                raise TimeoutError(f"instance {instance} rank {rank} never published its pool")
+            time.sleep(0.005)
+        with open(path, "rb") as f:
+            return msgpack.unpackb(f.read(), raw=False)
+
+
+def open_cd_services(url: str) -> tuple[PrefillPlane, PeerDirectory]:
+    """(plane, directory) for a URL: ``file:///path`` (a directory on this node) or
+    ``store://host:port`` (a ``torch.distributed`` TCPStore that another process hosts)."""
+    if url.startswith("file://"):
+        root = url[len("file://"):]
+        return FilePrefillPlane(root), FilePeerDirectory(root)
+    if url.startswith("store://"):
+        from datetime import timedelta
+
+        import torch.distributed as dist
+
+        host, _, port = url[len("store://"):].rpartition(":")
+        store = dist.TCPStore(host or "127.0.0.1", int(port), is_master=False, timeout=timedelta(seconds=60))
+        return StorePrefillPlane(store), StorePeerDirectory(store)
+    raise ValueError(f"unknown disaggregation directory URL {url!r} (file:///path or store://host:port)")

@@ -308,24 +308,62 @@ class KvLayout:
         return lay
 
     # -------------------------------------------------------------- export
+    def _framework_tensors(self) -> list[torch.Tensor] | None:
+        """The framework-owned CUDA tensors this layout describes (one per layer, or one), else None."""
+        ts = getattr(self, "_layer_tensors", None)
+        if ts is None and isinstance(self.backing, torch.Tensor):
+            ts = [self.backing]
+        if ts and all(isinstance(t, torch.Tensor) and t.is_cuda for t in ts):
+            return list(ts)
+        return None
+
     def descriptor(self, with_ipc: bool = True) -> LayoutDescriptor:
+        """A serialisable description of the pool. With ``with_ipc`` it also carries what
+        another process needs to map the memory: the CUDA IPC handle of a pool this
+        library allocated, or, for a framework-owned KV cache (an inference engine's own
+        tensors, described with ``over_tensor`` / ``over_layer_tensors``), one PyTorch
+        CUDA IPC record per tensor (the allocation's handle, the tensor's offset in it,
+        and PyTorch's cross-process reference count, which keeps the memory alive while a
+        peer holds it)."""
         handle = None
+        extra: dict = {}
         if with_ipc:
-            if not isinstance(self.backing, DeviceBuffer):
-                raise ValueError("only pools allocated by KvLayout.allocate(location='device') can be exported")
-            handle = self.backing.ipc_handle()
+            if isinstance(self.backing, DeviceBuffer):
+                handle = self.backing.ipc_handle()
+            else:
+                ts = self._framework_tensors()
+                if ts is None:
+                    raise ValueError("only device pools (allocated here or framework-owned CUDA tensors) can be "
+                                     "exported")
+                extra["torch_ipc"] = [_torch_ipc_export(t) for t in ts]
         cfg = asdict(self.config)
         return LayoutDescriptor(config=cfg, kind=self.kind, block_layout=self.block_layout.value,
                                 layer_offsets=self.layer_offsets, block_stride=self.block_stride,
                                 outer_stride=self.outer_stride, token_stride=self.token_stride,
                                 head_stride=self.head_stride, nbytes=self.nbytes, scales_offset=self.scales_offset,
-                                ipc_handle=handle, device=self.device or 0)
+                                ipc_handle=handle, device=self.device or 0, extra=extra)
 
     @classmethod
     def from_descriptor(cls, desc: LayoutDescriptor, device: int | None = None) -> "KvLayout":
-        """Map a peer's exported pool into this process (CUDA IPC over NVLink)."""
-        peer = PeerBuffer(desc.ipc_handle, desc.nbytes, device=device)
+        """Map a peer's exported pool into this process (CUDA IPC; over NVLink when the
+        pool is on another GPU)."""
         cfg = LayoutConfig(**desc.config)
+        recs = (desc.extra or {}).get("torch_ipc")
+        if recs:
+            if device is not None:
+                torch.cuda.set_device(device)
+            ts = [_torch_ipc_import(r) for r in recs]
+            if len(ts) == 1:
+                base, offsets = ts[0].data_ptr(), list(desc.layer_offsets)
+            else:  # one tensor per layer, each mapped wherever the driver put it
+                base = min(t.data_ptr() for t in ts)
+                offsets = [t.data_ptr() - base for t in ts]
+            lay = cls(cfg, desc.kind, KvBlockLayout(desc.block_layout), base, offsets, desc.block_stride,
+                      desc.outer_stride, desc.token_stride, desc.head_stride,
+                      max(t.data_ptr() + t.numel() * t.element_size() for t in ts) - base, "peer",
+                      torch.cuda.current_device(), ts, desc.scales_offset)
+            return lay
+        peer = PeerBuffer(desc.ipc_handle, desc.nbytes, device=device)
         lay = cls(cfg, desc.kind, KvBlockLayout(desc.block_layout), peer.ptr, desc.layer_offsets,
                   desc.block_stride, desc.outer_stride, desc.token_stride, desc.head_stride, desc.nbytes,
                   "peer", peer.device, peer, desc.scales_offset)
@@ -460,3 +498,29 @@ class _RawDev:
     def __cuda_array_interface__(self):
         return {"shape": (self.nbytes,), "typestr": "|u1", "data": (self.ptr, False), "version": 3,
                 "strides": None, "stream": None}
+
+
+def _torch_ipc_export(t: torch.Tensor) -> dict:
+    """PyTorch's CUDA IPC record of ``t`` as plain data (no pickle: the record crosses
+    process boundaries through files other local users could write)."""
+    from torch.multiprocessing.reductions import reduce_tensor
+
+    _, a = reduce_tensor(t)
+    (_, size, stride, offset, _, dtype, dev, handle, ssize, soff, _, rc_handle, rc_off, ev_handle, ev_sync) = a
+    return {"size": list(size), "stride": list(stride), "offset": int(offset), "dtype": str(dtype).split(".")[-1],
+            "device": int(dev), "handle": bytes(handle).hex(), "storage_bytes": int(ssize),
+            "storage_offset": int(soff), "rc_handle": bytes(rc_handle).hex(), "rc_offset": int(rc_off),
+            "event": bytes(ev_handle).hex() if ev_handle is not None else None, "event_sync": bool(ev_sync)}
+
+
+def _torch_ipc_import(r: dict) -> torch.Tensor:
+    from torch.multiprocessing.reductions import rebuild_cuda_tensor
+
+    dtype = getattr(torch, r["dtype"])
+    if not isinstance(dtype, torch.dtype):
+        raise ValueError(f"bad dtype {r['dtype']!r} in an IPC record")
+    return rebuild_cuda_tensor(torch.Tensor, torch.Size(r["size"]), tuple(r["stride"]), int(r["offset"]),
+                               torch.storage.TypedStorage, dtype, int(r["device"]), bytes.fromhex(r["handle"]),
+                               int(r["storage_bytes"]), int(r["storage_offset"]), False,
+                               bytes.fromhex(r["rc_handle"]), int(r["rc_offset"]),
+                               bytes.fromhex(r["event"]) if r.get("event") else None, bool(r["event_sync"]))

@@ -140,6 +140,12 @@ class DisaggSettings:
     fallback: str = "local"
     drain_poll_ms: float = 2.0
     watchdog_secs: float = 10.0
+    # the on-node data plane of remote prefills (a vLLM engine's connector reads these):
+    instance_id: int | None = None     # this engine's id on the plane (scheduler and workers agree on it)
+    prefill_instance: int | None = None  # decode: where its remote prefills go (a hub routes when unset)
+    directory: str = "file:///dev/shm/kvbm_pd"  # file:///path | store://host:port (pools, mailboxes, plane)
+    mailbox_slots: int = 64            # decode: remote prefills in flight (one completion word each)
+    recv_timeout_s: float = 120.0      # decode: a remote prefill not landed by then is recomputed
 
 
 @dataclass

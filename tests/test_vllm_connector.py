@@ -124,3 +124,67 @@ def test_pd_connector_validates_children_and_routes_handshakes():
     kv, nx = pd.route_handshake({0: H(kvbm_metadata=a, nixl_metadata=b), 1: H(kvbm_metadata=None, nixl_metadata=b),
                                  2: legacy}, H)
     assert kv == {0: a} and nx == {0: b, 1: b, 2: legacy}
+
+
+def test_disagg_roles_dispatch_over_the_file_plane_and_push(tmp_path):
+    """The adapter's disaggregation settings: a decode-role connector sends a prompt to the
+    prefill instance over the on-node plane, and a prefill-role connector that receives the
+    request (its kv_transfer_params name the decode instance) plans the push of its blocks."""
+    from kvbm_b200.connector import vllm_connector as vc
+    from kvbm_b200.connector.leader import REMOTE_DECODE_KEY
+    from kvbm_b200.engine.cd_plane import FilePeerDirectory, FilePrefillPlane
+
+    Role = vllm_base.KVConnectorRole
+    url = f"file://{tmp_path}"
+    dec = vc.KvbmConnector(_vllm_config({"disagg": {"role": "decode", "instance_id": 11, "prefill_instance": 22,
+                                                    "selection": "always", "directory": url,
+                                                    "mailbox_slots": 4}}), Role.SCHEDULER)
+    pre = vc.KvbmConnector(_vllm_config({"disagg": {"role": "prefill", "instance_id": 22, "directory": url}}),
+                           Role.SCHEDULER)
+    # the prefill engine's worker publishes its TP degree when its KV caches are registered
+    FilePeerDirectory(str(tmp_path)).publish(22, {"tp": 1, "rank": 0, "instance": 22})
+    tokens = list(range(3 * 16 + 5))
+    r = _request("d1", tokens)
+    assert dec.get_num_new_matched_tokens(r, 0) == (len(tokens), True)  # the whole prompt arrives remotely
+    dec.update_state_after_alloc(r, SimpleNamespace(get_block_ids=lambda: ([40, 41, 42, 43],)), len(tokens))
+    m = ConnectorMetadata.decode(dec.build_connector_meta(_sched_output([], {})).metadata)
+    assert [(op.req_id, op.g1_ids) for op in m.recv] == [("d1", [40, 41, 42, 43])]
+    got = FilePrefillPlane(str(tmp_path)).poll(22)
+    assert len(got) == 1 and list(got[0]["tokens"]) == tokens
+    assert got[0]["decode"]["instance"] == 11 and got[0]["decode"]["dst_ids"] == [40, 41, 42, 43]
+
+    # the prefill engine serves it as a one-token request naming the decode instance
+    params = dict(got[0]["params"])
+    params[REMOTE_DECODE_KEY] = got[0]["decode"]
+    rp = SimpleNamespace(request_id="p1", prompt_token_ids=tokens, cache_salt=None, lora_request=None,
+                         kv_transfer_params=params)
+    assert pre.get_num_new_matched_tokens(rp, 0) == (0, False)
+    pre.update_state_after_alloc(rp, SimpleNamespace(get_block_ids=lambda: ([7, 8, 9, 10],)), 0)
+    mp = ConnectorMetadata.decode(pre.build_connector_meta(_sched_output([("p1", [7, 8, 9, 10])],
+                                                                         {"p1": len(tokens)})).metadata)
+    pushed = [(op.peer, op.src_ids, op.dst_ids) for op in mp.push]
+    assert pushed and all(p == 11 for p, _, _ in pushed)
+    assert sum((s for _, s, _ in pushed), []) == [7, 8, 9, 10]
+    assert sum((d for _, _, d in pushed), []) == [40, 41, 42, 43]
+    assert mp.push[-1].final
+    # its blocks stay allocated until the workers report the push done
+    assert pre.request_finished(rp, [7, 8, 9, 10])[0] is True
+
+
+def test_disagg_settings_are_validated(tmp_path):
+    from kvbm_b200.connector import vllm_connector as vc
+    from kvbm_b200.utils.config import KvbmConfig
+
+    def cfg(d):
+        return KvbmConfig.for_leader({"disagg": d}, env={}, system_toml=None)
+
+    assert vc.disagg_leader_kwargs(cfg({})) == {}
+    with pytest.raises(ValueError, match="instance_id"):
+        vc.disagg_leader_kwargs(cfg({"role": "decode"}))
+    with pytest.raises(ValueError, match="prefill_instance or hub.url"):
+        vc.disagg_leader_kwargs(cfg({"role": "decode", "instance_id": 1, "selection": "always",
+                                     "directory": f"file://{tmp_path}"}))
+    kw = vc.disagg_leader_kwargs(cfg({"role": "prefill", "instance_id": 2, "directory": f"file://{tmp_path}"}))
+    assert kw["instance_id"] == 2 and "cd" not in kw and "plane" not in kw
+    with pytest.raises(ValueError, match="directory URL"):
+        vc.disagg_leader_kwargs(cfg({"role": "prefill", "instance_id": 2, "directory": "nats://x"}))
