@@ -87,8 +87,17 @@ class HubClient:
                                "request": request, "timeout": timeout}, timeout=timeout + 5)
 
     def calibrate(self, instance_id: int, ttft=(), itl=()) -> dict:
+        """Post measured (tokens, seconds) samples for a prefill instance's TTFT / ITL models."""
         return self._req("POST", f"/v1/prefill-router/calibrate/{instance_id}",
                          json={"ttft": list(ttft), "itl": list(itl)})
+
+    def run_calibration(self, instance_id: int, request: dict | None = None, force: bool = False,
+                        timeout: float = 1800.0) -> dict:
+        """Ask a prefill worker to run a calibration sweep (``CalibrationRequest`` fields, all
+        optional); returns the fitted model, the resolved knobs and whether it was cached."""
+        return self._req("POST", f"/v1/prefill-router/calibrate/{instance_id}",
+                         params={"force": "true" if force else "false"},
+                         json={"request": request or {}, "timeout": timeout}, timeout=timeout + 10)
 
     def router_counters(self) -> dict:
         return self._req("GET", "/v1/prefill-router/counters")
@@ -171,7 +180,11 @@ class PrefillRouterHandler:
 
     def __init__(self, hub_url: str, dispatch: Callable[[dict, CompletionEvent], None],
                  calibrate: Callable[[], dict] | None = None, instance_id: int | None = None,
-                 max_concurrency: int = 4, timeout: float = 60.0):
+                 max_concurrency: int = 4, timeout: float = 60.0,
+                 calibrate_lambda: Callable[[dict, CompletionEvent], None] | None = None,
+                 calibration_defaults: dict | None = None, calibration_timeout: float = 1800.0):
+        from .calibration import CALIBRATE_HANDLER, CalibrationDefaults
+
         self.instance_id = instance_id if instance_id is not None else uuid.uuid4().int >> 64
         self.messenger = Messenger(self.instance_id)
         self.dispatch_fn, self.calibrate_fn = dispatch, calibrate
@@ -180,7 +193,15 @@ class PrefillRouterHandler:
         self.inflight = 0
         self.completed = 0
         self._lock = threading.Lock()
+        # hub-triggered calibration sweeps: never while a prefill runs, no prefill while one runs
+        self.calibrate_lambda = calibrate_lambda
+        self.calibration_defaults = CalibrationDefaults.from_dict(calibration_defaults)
+        self.calibration_timeout = calibration_timeout
+        self.calibrating = False
+        self._calibration: dict | None = None  # the last analysed sweep (returned again unless forced)
         self.messenger.register_handler(DISPATCH_HANDLER, self._on_dispatch)
+        if calibrate_lambda is not None:
+            self.messenger.register_handler(CALIBRATE_HANDLER, self._on_calibrate)
         self.client = HubClient(hub_url)
         self.registration = HubRegistration(self.client, self.instance_id, role="prefill",
                                             features=["prefill_router"], address=self.messenger.address,
@@ -189,8 +210,39 @@ class PrefillRouterHandler:
             cal = calibrate()
             self.client.calibrate(self.instance_id, cal.get("ttft", ()), cal.get("itl", ()))
 
+    def _on_calibrate(self, payload: dict | None):
+        """Run (or return the cached) calibration sweep: resolve the caller's knobs against the
+        engine's limits, hand them to the calibrate lambda, fit the traces it returns."""
+        from .calibration import CalibrationRequest, analyze
+
+        req = CalibrationRequest.from_dict((payload or {}).get("request"))
+        force = bool((payload or {}).get("force")) or req.force
+        with self._lock:
+            if self._calibration is not None and not force:
+                return {**self._calibration, "from_cache": True}
+            if self.calibrating:
+                raise RuntimeError("already_calibrating")
+            if self.inflight:
+                raise RuntimeError(f"prefill_busy ({self.inflight} in flight)")
+            self.calibrating = True
+        try:
+            resolved = req.resolve(self.calibration_defaults)
+            done = CompletionEvent()
+            self.calibrate_lambda(resolved.to_dict(), done)
+            raw = done.wait(self.calibration_timeout)
+            out = {"results": analyze(list(raw["traces"])), "resolved": resolved.to_dict(),
+                   "defaults": dict(vars(self.calibration_defaults))}
+            with self._lock:
+                self._calibration = out
+            return {**out, "from_cache": False}
+        finally:
+            with self._lock:
+                self.calibrating = False
+
     def _on_dispatch(self, request: dict):
         with self._lock:
+            if self.calibrating:
+                raise RuntimeError("calibration_in_progress")
             if self.inflight >= self.max_concurrency:
                 raise RuntimeError("prefill handler saturated")
             self.inflight += 1

@@ -5,7 +5,8 @@ configuration (``kv_transfer_config.kv_connector_extra_config``: the
 block-manager configuration, with its ``default`` / ``leader`` profiles
 applied) and, when it names a hub and the ``prefill`` disaggregation role,
 registers the process as a prefill target: it returns a
-:class:`PrefillRouterHandler` whose dispatch lambda turns every routed
+:class:`PrefillRouterHandler` (with a calibrate handler when the engine's
+limits can be read) whose dispatch lambda turns every routed
 request into an ``engine.generate`` call (the prompt's token ids, one output
 token, ``kv_transfer_params`` naming the decode instance that waits for the
 KV) on the engine's event loop, and completes the router's call when that
@@ -89,7 +90,19 @@ def try_wrap_engine(vllm_config: Any, engine: Any, loop: asyncio.AbstractEventLo
     if not hub_url or role != "prefill":
         return None
     loop = loop or asyncio.get_running_loop()
+    # the calibrate handler is best effort: an engine whose limits cannot be read still serves prefills
+    cal_lambda = cal_defaults = None
+    try:
+        from .calibrate_lambda import capture_calibration_defaults, make_calibrate_lambda
+
+        mc = getattr(vllm_config, "model_config", None)
+        model_id = str(getattr(mc, "served_model_name", None) or getattr(mc, "model", "") or "")
+        cal_defaults = capture_calibration_defaults(engine, model_id)
+        cal_lambda = make_calibrate_lambda(engine, loop)
+    except Exception as e:  # noqa: BLE001
+        log.info("prefill router: no calibrate handler (%s: %s)", type(e).__name__, e)
     handler = PrefillRouterHandler(hub_url, make_dispatch_lambda(engine, loop, make_params=make_params),
-                                   max_concurrency=max_concurrency)
+                                   max_concurrency=max_concurrency, calibrate_lambda=cal_lambda,
+                                   calibration_defaults=cal_defaults)
     log.info("prefill router attached (instance %s, hub %s)", handler.instance_id, hub_url)
     return handler

@@ -32,6 +32,7 @@ from aiohttp import web
 
 from .. import _core_native as core
 from ..runtime.messenger import Messenger
+from .calibration import CALIBRATE_HANDLER, samples_from_traces
 from .prefill_router import BreakerTicker, Calibration, CircuitBreaker, Selector
 from .registry import InstanceRecord, InstanceRegistry
 
@@ -238,13 +239,42 @@ class HubServer:
                                   "calibration": {str(k): v.to_dict() for k, v in self.calibration.items()}})
 
     async def _calibrate(self, req):
+        """Either measured samples (``ttft`` / ``itl`` lists) for an instance's models, or a
+        calibration request proxied to that prefill worker (``request``, ``?force=true``): the
+        worker runs its sweep and the fitted traces feed the instance's models here too.
+        409 when the worker is busy with prefills or another sweep."""
         d = await req.json()
-        cal = self.calibration[_h(req.match_info["iid"])]
-        for isl, s in d.get("ttft", []):
-            cal.add_ttft(isl, s)
-        for ctx, s in d.get("itl", []):
-            cal.add_itl(ctx, s)
-        return web.json_response(cal.to_dict())
+        iid = _h(req.match_info["iid"])
+        cal = self.calibration[iid]
+        if "ttft" in d or "itl" in d:
+            for isl, s in d.get("ttft", []):
+                cal.add_ttft(isl, s)
+            for ctx, s in d.get("itl", []):
+                cal.add_itl(ctx, s)
+            return web.json_response(cal.to_dict())
+        rec = self.registry.get(iid)
+        if rec is None:
+            return web.json_response({"error": f"unknown instance {iid}"}, status=404)
+        if self.messenger is None:
+            return web.json_response({"error": "this hub has no messenger to reach workers"}, status=503)
+        force = req.query.get("force", "false").lower() in ("1", "true", "yes")
+        timeout = float(d.get("timeout", 1800.0))
+        loop = asyncio.get_running_loop()
+        try:
+            out = await loop.run_in_executor(None, lambda: self.messenger.call(
+                rec.address, CALIBRATE_HANDLER, {"request": d.get("request") or {}, "force": force}, timeout=timeout))
+        except Exception as e:  # noqa: BLE001 - the worker's refusal or failure goes back to the caller
+            msg = str(e)
+            busy = "already_calibrating" in msg or "prefill_busy" in msg
+            return web.json_response({"error": msg}, status=409 if busy else 502)
+        if not out.get("from_cache"):
+            ttft, itl = samples_from_traces(out["results"]["traces"])
+            for isl, s in ttft:
+                cal.add_ttft(isl, s)
+            for ctx, s in itl:
+                cal.add_itl(ctx, s)
+        self.counters["calibrations"] += 1
+        return web.json_response(out)
 
     async def _dispatch(self, req):
         d = await req.json()

@@ -155,8 +155,10 @@ def test_vllm_engines_disaggregated_through_the_connector(tmp_path):
     os.makedirs(root)
     base = int.from_bytes(os.urandom(2), "little") * 16 + 4096
     pre_iid, dec_iid = base + 1, base + 2
+    repo = os.path.dirname(os.path.dirname(HERE))
     env = {**os.environ, "VLLM_ENABLE_V1_MULTIPROCESSING": "0", "CUDA_VISIBLE_DEVICES":
-           os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]}
+           os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0],
+           "PYTHONPATH": os.pathsep.join([repo] + [p for p in [os.environ.get("PYTHONPATH")] if p])}
     pre_out, dec_out = str(tmp_path / "prefill.json"), str(tmp_path / "decode.json")
     pre = subprocess.Popen([sys.executable, HERE, "prefill", model_dir, root, str(pre_iid), pre_out], env=env)
     dec = None
