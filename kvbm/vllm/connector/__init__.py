@@ -3,12 +3,12 @@ when a connector class is accessed."""
 
 
 def __getattr__(name):
-    if name in ("KvbmConnector", "KvbmConnectorMetadata"):
+    if name in ("KvbmConnector", "KvbmConnectorMetadata", "KvbmConnectorWorkerMetadata"):
         from kvbm_b200.connector import vllm_connector
 
         return getattr(vllm_connector, name)
-    if name == "PdConnector":
-        from kvbm_b200.connector.pd import PdConnector
+    if name in ("PdConnector", "PdConnectorMetadata", "PdHandshakeMetadata"):
+        from kvbm_b200.connector import pd
 
-        return PdConnector
+        return getattr(pd, name)
     raise AttributeError(name)

@@ -71,3 +71,17 @@ def check_vllm_version(version: str | None = None) -> None:
     if not (lo <= parts < hi):
         raise RuntimeError(f"vLLM {version} is outside the supported range {lo}..{hi} "
                            "(set KVBM_SKIP_VLLM_VERSION_CHECK=true to override)")
+
+
+def format_config_table(config: dict) -> str:
+    """A fixed-width text table of a connector configuration: either sections of key/value
+    pairs (``{"parallel": {...}, "attention": {...}}``) or one flat mapping (what
+    :func:`extract_vllm_config_for_kvbm` returns)."""
+    rule = "=" * 70
+    lines = [rule, "KV block manager connector configuration", rule]
+    sections = config if config and all(isinstance(v, dict) for v in config.values()) else {"settings": config}
+    for name, items in sections.items():
+        lines += ["", f"{str(name).replace('_', ' ').capitalize()}:", "-" * 70]
+        lines += [f"  {k:30s} : {v}" for k, v in items.items()]
+    lines.append(rule)
+    return "\n".join(lines)

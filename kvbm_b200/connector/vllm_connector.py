@@ -16,11 +16,38 @@ from __future__ import annotations
 
 import json
 import os
-from typing import Any
+from typing import Any, Protocol
 
 from .config import extract_vllm_config_for_kvbm, kv_block_bytes
 from .leader import ConnectorLeader, KvbmRequest, SchedulerOutputLite
 from .protocol import ConnectorMetadata
+
+
+class NewRequestDataProtocol(Protocol):
+    """The fields of vLLM's ``NewRequestData`` the connector reads."""
+
+    req_id: str
+    prompt_token_ids: list[int] | None
+    block_ids: tuple[list[int], ...]
+    num_computed_tokens: int
+
+
+class CachedRequestDataProtocol(Protocol):
+    """The fields of vLLM's ``CachedRequestData`` the connector reads (one list entry per request)."""
+
+    req_ids: list[str]
+    new_token_ids: list[list[int]]
+    new_block_ids: list[tuple[list[int], ...] | None]
+    num_computed_tokens: list[int]
+
+
+class SchedulerOutputProtocol(Protocol):
+    """The fields of vLLM's ``SchedulerOutput`` the connector reads."""
+
+    scheduled_new_reqs: list[NewRequestDataProtocol]
+    scheduled_cached_reqs: CachedRequestDataProtocol
+    num_scheduled_tokens: dict[str, int]
+    finished_req_ids: set[str]
 
 
 def process_scheduler_output(step: int, so, slots: dict) -> SchedulerOutputLite:
@@ -166,8 +193,21 @@ def _define():
                 bpb = kv_block_bytes(self.info)
                 g2n = blocks_for_bytes(cfg.cache.host.cache_size_gb, cfg.cache.host.num_blocks, bpb)
                 g3n = blocks_for_bytes(cfg.cache.disk.cache_size_gb, cfg.cache.disk.num_blocks, bpb)
+                # KV-event consolidator: vLLM's G1 events and the block manager's G2/G3 presence in one stream
+                from .consolidator_config import get_consolidator_endpoints
+
+                self.consolidator = self._events = None
+                eps = get_consolidator_endpoints(vllm_config)
+                if eps is not None:
+                    from ..consolidator.service import start_leader_consolidator
+                    from ..logical.events import EventsManager
+
+                    self._events = EventsManager(int((cfg.disagg.instance_id if cfg.disagg else None) or os.getpid()))
+                    self.consolidator = start_leader_consolidator(eps[0], eps[1], "vllm", bs, self._events)
+                    self._events.start()
                 g2 = BlockManager(max(1, g2n), bs, cfg.cache.inactive_backend, Tier.G2,
-                                  duplicate_policy=cfg.cache.duplicate_policy)
+                                  duplicate_policy=cfg.cache.duplicate_policy,
+                                  events=self._events.queue if self._events is not None else None)
                 g3 = BlockManager(g3n, bs, cfg.cache.inactive_backend, Tier.G3, registry=g2.registry) if g3n else None
                 self._leader = ConnectorLeader(InstanceLeader.scheduler_side(g2, g3), bs,
                                                offload_enabled=g2n > 0,
@@ -278,6 +318,10 @@ def _define():
         def shutdown(self):
             if self._worker is not None:
                 self._worker.shutdown()
+            if getattr(self, "_events", None) is not None:
+                self._events.stop()
+            if getattr(self, "consolidator", None) is not None:
+                self.consolidator.close()
 
     globals()["KvbmConnector"] = KvbmConnector
     globals()["KvbmConnectorMetadata"] = KvbmConnectorMetadata

@@ -175,3 +175,19 @@ def _event_kind(ev):
             return tag, dict(zip(["block_hashes", "medium"], ev[1:]))
         return tag, {}
     return None, {}
+
+
+def start_leader_consolidator(vllm_endpoint: str | None, output_bind: str, source: str = "vllm",
+                              block_size: int = 16, events=None) -> Consolidator:
+    """The consolidator a scheduler-side connector runs: subscribed to the engine's KV-event
+    endpoint, publishing on ``output_bind``, and fed the block manager's own G2/G3 presence
+    events when ``events`` (a ``logical.events.EventsManager``) is given."""
+    c = Consolidator(publish_endpoint=output_bind, block_size=block_size)
+    if vllm_endpoint:
+        c.subscribe(vllm_endpoint, source=source)
+    if events is not None:
+        def sink(_instance_id, batches):
+            c.ingest_kvbm_events([(kind, int(h)) for kind, hashes in batches for h in hashes])
+            c.flush()
+        events.add_sink(sink)
+    return c

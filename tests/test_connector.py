@@ -131,6 +131,15 @@ def test_lazy_import_does_not_pull_vllm():
             "print('vllm' in sys.modules)")
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True)
     assert out.stdout.strip() == "False"
+    # every module of the reference package's import paths, the same way
+    mods = ["kvbm", "kvbm._core", "kvbm.hub", "kvbm.hub.detect", "kvbm.hub.dispatch_lambda",
+            "kvbm.hub.calibrate_lambda", "kvbm.vllm", "kvbm.vllm.config", "kvbm.vllm.consolidator_config",
+            "kvbm.vllm.sched_output", "kvbm.vllm.version_check", "kvbm.vllm.dim_probe", "kvbm.vllm.connector",
+            "kvbm.vllm.connector.base", "kvbm.vllm.connector.leader", "kvbm.vllm.connector.worker",
+            "kvbm.vllm.connector.pd", "kvbm.vllm.connector.protocols"]
+    code = f"import sys, importlib; [importlib.import_module(m) for m in {mods!r}]; print('vllm' in sys.modules)"
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True)
+    assert out.stdout.strip() == "False"
 
 
 def test_g2_spills_to_g3_and_g3_hits_are_staged_by_the_workers():

@@ -188,3 +188,68 @@ def test_disagg_settings_are_validated(tmp_path):
     assert kw["instance_id"] == 2 and "cd" not in kw and "plane" not in kw
     with pytest.raises(ValueError, match="directory URL"):
         vc.disagg_leader_kwargs(cfg({"role": "prefill", "instance_id": 2, "directory": "nats://x"}))
+
+
+def test_scheduler_connector_runs_the_consolidator(monkeypatch):
+    """With prefix caching and vLLM KV events configured, the scheduler-role connector starts the
+    consolidator: it subscribes to vLLM's event endpoint and republishes deduplicated events on the
+    block manager's port + 1000; the enable rules follow the environment and the vLLM config."""
+    import socket
+    import time
+
+    import msgpack
+    import zmq
+
+    from kvbm_b200.connector import consolidator_config as cc
+    from kvbm_b200.connector import vllm_connector as vc
+
+    def free_port():
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            return s.getsockname()[1]
+
+    ctx = zmq.Context.instance()
+    vpub = ctx.socket(zmq.PUB)
+    vport = vpub.bind_to_random_port("tcp://127.0.0.1")
+    out_port = free_port()
+    monkeypatch.setenv("DYN_KVBM_LEADER_ZMQ_PUB_PORT", str(out_port - 1000))
+    cfg = _vllm_config({"leader": {"cache": {"host": {"num_blocks": 64}}}})
+    cfg.cache_config.enable_prefix_caching = True
+    cfg.kv_events_config = SimpleNamespace(endpoint=f"tcp://*:{vport}")
+    cfg.parallel_config.data_parallel_rank = 0
+    assert cc.get_consolidator_endpoints(cfg) == (f"tcp://127.0.0.1:{vport}", f"tcp://0.0.0.0:{out_port}",
+                                                  f"tcp://127.0.0.1:{out_port}")
+    conn = vc.KvbmConnector(cfg, vllm_base.KVConnectorRole.SCHEDULER)
+    sub = ctx.socket(zmq.SUB)
+    sub.setsockopt(zmq.SUBSCRIBE, b"")
+    sub.connect(f"tcp://127.0.0.1:{out_port}")
+    try:
+        assert conn.consolidator is not None
+        stored = {"type": "BlockStored", "block_hashes": [7, 8], "parent_block_hash": None,
+                  "token_ids": list(range(32)), "block_size": 16}
+        got = []
+        deadline = time.monotonic() + 10
+        while not got and time.monotonic() < deadline:  # the SUB sockets join asynchronously
+            vpub.send_multipart([b"kv", msgpack.packb([time.time(), [stored], None], use_bin_type=True)])
+            if sub.poll(200):
+                got = msgpack.unpackb(sub.recv_multipart()[-1], raw=False)[1]
+        assert [e["type"] for e in got] == ["BlockStored", "BlockStored"]
+        assert got[0]["token_ids"] == list(range(16))
+    finally:
+        conn.shutdown()
+        sub.close(0)
+        vpub.close(0)
+    # opt-out and missing prerequisites
+    monkeypatch.setenv("DYN_KVBM_KV_EVENTS_ENABLE_CONSOLIDATOR", "0")
+    assert cc.get_consolidator_endpoints(cfg) is None
+    monkeypatch.delenv("DYN_KVBM_KV_EVENTS_ENABLE_CONSOLIDATOR")
+    cfg.kv_events_config = None
+    assert not cc.should_enable_consolidator(cfg)
+    pd = _vllm_config({"connectors": [{"kv_connector": "KvbmConnector"}, {"kv_connector": "NixlConnector"}]})
+    pd.kv_transfer_config.kv_connector = "PdConnector"
+    pd.cache_config.enable_prefix_caching = True
+    pd.kv_events_config = SimpleNamespace(endpoint="tcp://*:5557")
+    assert cc.should_enable_consolidator(pd)
+    assert cc._offset_port("tcp://*:5557", 2) == "tcp://*:5559" and cc._offset_port("inproc://c", 1) == "inproc://c_dp1"
+    monkeypatch.setenv("DYN_KVBM_KV_EVENTS_CONSOLIDATOR_MODE", "weird")
+    assert cc.get_consolidator_mode() == "dedup"
