@@ -106,6 +106,9 @@ class ConnectorWorker:
         self._last_offload: torch.cuda.Event | None = None
         self._recv_events: dict[str, torch.cuda.Event] = {}
         self._send_events: dict[str, list[torch.cuda.Event]] = {}
+        # requests this worker sent blocks for (offloads, remote-prefill pushes): the only ones whose free
+        # the scheduler delays for a send, so the only ones get_finished may report as sent
+        self._send_seen: set[str] = set()
         self._layer_events: list[torch.cuda.Event] = []
         self._load_errors: set[int] = set()
         self.transfer_log: list | None = None
@@ -421,6 +424,7 @@ class ConnectorWorker:
                 ev = torch.cuda.Event()
                 ev.record(st)
                 self._send_events.setdefault(op.req_id, []).append(ev)
+                self._send_seen.add(op.req_id)
         if not (meta.offload or meta.spill):
             return
         _, d2h = self._streams()
@@ -432,6 +436,7 @@ class ConnectorWorker:
             ev = torch.cuda.Event()
             ev.record(d2h)
             self._send_events.setdefault(op.req_id, []).append(ev)
+            self._send_seen.add(op.req_id)
             self._last_offload = ev
         if meta.offload:
             self._offload_steps.append((meta.step, self._last_offload))
@@ -469,7 +474,9 @@ class ConnectorWorker:
                     recving.add(r)
                     del self._recvs[r]
         recving -= set(self._recvs)
-        self._pending_finished |= set(finished_req_ids or ())
+        # a finished request is reported sent once its copies are done, and only if it sent any: a
+        # request the scheduler freed at once must not come back (vLLM no longer knows it)
+        self._pending_finished |= set(finished_req_ids or ()) & self._send_seen
         sending = set()
         for r in list(self._pending_finished):
             evs = self._send_events.get(r)
@@ -477,6 +484,7 @@ class ConnectorWorker:
                 sending.add(r)
                 self._pending_finished.discard(r)
                 self._send_events.pop(r, None)
+                self._send_seen.discard(r)
         return sending, recving
 
     def build_connector_worker_meta(self) -> dict | None:

@@ -198,3 +198,16 @@ def test_scheduler_side_leader_refuses_direct_moves():
     g3b = g3.register_mutable(g3.allocate_blocks(1), [456])
     with pytest.raises(RuntimeError, match="PREPARE"):
         leader.stage_g3_to_g2(g3b)
+
+
+def test_worker_reports_sent_only_for_requests_that_sent():
+    """vLLM frees a finished request at once unless the scheduler delayed it for a send, and
+    asserts on a finished_sending report of a request it no longer knows: the worker reports
+    only requests it sent blocks for (offloads, pushes)."""
+    from kvbm_b200.connector.worker import ConnectorWorker
+
+    w = ConnectorWorker(device=0)
+    assert w.get_finished({"a", "b"}) == (set(), set())
+    w._send_seen.add("b")  # "b" offloaded; its copies have completed (no events left to wait for)
+    assert w.get_finished({"a", "b"}) == ({"b"}, set())
+    assert w.get_finished({"b"}) == (set(), set())  # reported once
