@@ -4,6 +4,7 @@ push cursor over prefill chunks; the prefill plane and peer directory."""
 
 import threading
 
+import pytest
 import torch.distributed as dist
 
 from kvbm_b200.connector.leader import REMOTE_DECODE_KEY, ConnectorLeader, KvbmRequest, SchedulerOutputLite
@@ -267,3 +268,40 @@ def test_engine_attached_to_the_prefill_router_serves_routed_prefills():
         plane.close()
         loop.call_soon_threadsafe(loop.stop)
         hub.stop()
+
+
+def test_file_plane_serves_each_dispatch_once_across_pollers(tmp_path):
+    """Several pollers of one prefill instance (e.g. threads of a prefill server) share the
+    file plane's spool: every dispatch is served exactly once, in arrival order per poller."""
+    from kvbm_b200.engine.cd_plane import FilePeerDirectory, FilePrefillPlane, encode_dispatch
+
+    plane = FilePrefillPlane(str(tmp_path))
+    for i in range(200):
+        plane.dispatch(9, encode_dispatch(f"r{i}", [i], {}, {"instance": 1}))
+    got: list[list[str]] = [[] for _ in range(4)]
+
+    def poll(k):
+        p = FilePrefillPlane(str(tmp_path))
+        while True:
+            batch = p.poll(9, limit=7)
+            if not batch:
+                return
+            got[k] += [d["request_id"] for d in batch]
+
+    ts = [threading.Thread(target=poll, args=(k,)) for k in range(4)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join(10)
+    served = sum(got, [])
+    assert sorted(served, key=lambda r: int(r[1:])) == [f"r{i}" for i in range(200)]
+    for g in got:
+        assert g == sorted(g, key=lambda r: int(r[1:]))
+    d = FilePeerDirectory(str(tmp_path))
+    with pytest.raises(TimeoutError):
+        d.lookup(5, timeout_s=0.05)
+    d.publish(5, {"tp": 2}, rank=1)
+    assert d.lookup(5, rank=1) == {"tp": 2}
+    d.withdraw(5, rank=1)
+    with pytest.raises(TimeoutError):
+        d.lookup(5, timeout_s=0.05, rank=1)
