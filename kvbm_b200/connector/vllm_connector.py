@@ -14,6 +14,7 @@ Role dispatch and hook set follow python/kvbm/vllm/connector/base.py:55-473
 
 from __future__ import annotations
 
+import dataclasses
 import json
 import os
 from typing import Any, Protocol
@@ -196,14 +197,20 @@ def _define():
                 # KV-event consolidator: vLLM's G1 events and the block manager's G2/G3 presence in one stream
                 from .consolidator_config import get_consolidator_endpoints
 
+                # the G2/G3 presence events: to the configured sink (events.enabled) and/or the consolidator
                 self.consolidator = self._events = None
                 eps = get_consolidator_endpoints(vllm_config)
+                if eps is not None or cfg.events.enabled:
+                    from ..logical.events import events_from_config
+
+                    iid = int((cfg.disagg.instance_id if cfg.disagg else None) or os.getpid())
+                    ev_cfg = cfg.events if cfg.events.enabled else dataclasses.replace(cfg.events, endpoint=None)
+                    self._events = events_from_config(ev_cfg, iid, cfg.hub.url if cfg.hub else None)
                 if eps is not None:
                     from ..consolidator.service import start_leader_consolidator
-                    from ..logical.events import EventsManager
 
-                    self._events = EventsManager(int((cfg.disagg.instance_id if cfg.disagg else None) or os.getpid()))
                     self.consolidator = start_leader_consolidator(eps[0], eps[1], "vllm", bs, self._events)
+                if self._events is not None:
                     self._events.start()
                 g2 = BlockManager(max(1, g2n), bs, cfg.cache.inactive_backend, Tier.G2,
                                   duplicate_policy=cfg.cache.duplicate_policy,

@@ -5,9 +5,9 @@ One interface, three transports:
 * :class:`StubPubSub` - in-process (tests, single-process deployments);
 * :class:`ZmqPubSub` - ZeroMQ PUB/SUB; ``connect`` another endpoint to
   receive its subjects (subjects are ZeroMQ topic prefixes);
-* :class:`NatsPubSub` - a NATS server, when the ``nats`` client package is
-  installed (it is optional and not bundled; constructing one without it
-  raises ``ImportError``).
+* :class:`NatsPubSub` - a NATS server, through a client of the NATS text
+  protocol written here (``PUB`` / ``SUB`` / ``MSG`` / ``PING`` over TCP), so
+  no client package is needed.
 
 ``make_pubsub(url)`` picks the transport from the URL scheme (``stub://``,
 ``tcp://`` / ``ipc://``, ``nats://``). :class:`PubSubEventSink` plugs a
@@ -119,37 +119,138 @@ class ZmqPubSub(PubSub):
         self._pub.close(0)
 
 
-class NatsPubSub(PubSub):  # pragma: no cover - needs the optional nats client and a server
-    def __init__(self, url: str):
-        try:
-            import nats  # noqa: F401
-        except ImportError as e:
-            raise ImportError("NatsPubSub needs the optional 'nats-py' package") from e
-        import asyncio
+class NatsPubSub(PubSub):
+    """A NATS client speaking the NATS client protocol directly over TCP (no client package).
 
-        self._loop = asyncio.new_event_loop()
-        self._t = threading.Thread(target=self._loop.run_forever, daemon=True, name="kvbm-nats")
+    Connects to ``nats://[user:pass@]host[:port]`` (port 4222 by default),
+    reads the server's ``INFO``, sends ``CONNECT`` (and the credentials in
+    the URL) and waits for the ``PONG`` of a ``PING`` before returning, so a
+    refused connection fails here. ``publish`` writes one ``PUB``; a reader
+    thread answers the server's ``PING`` and delivers every ``MSG`` to the
+    handler of its subscription. Subjects get ``prefix.`` in front when a
+    prefix is set. ``subscribe`` follows the other transports' prefix
+    semantics: a subject without wildcards receives itself and every subject
+    below it (``a.b`` and ``a.b.>``); a subject with NATS wildcards (``*``,
+    ``>``) is passed to the server as is. ``flush`` waits until the server
+    has processed everything sent before it (a ``PING`` / ``PONG`` round
+    trip). A server ``-ERR`` is kept in ``last_error`` and raised by the
+    next ``flush``.
+    """
+
+    def __init__(self, url: str, prefix: str | None = None, name: str = "kvbm", timeout: float = 5.0):
+        import json
+        import socket
+        from urllib.parse import urlparse
+
+        u = urlparse(url)
+        if u.scheme != "nats":
+            raise ValueError(f"not a nats:// URL: {url!r}")
+        self.prefix = prefix.rstrip(".") if prefix else None
+        self.timeout = timeout
+        self._sock = socket.create_connection((u.hostname or "127.0.0.1", u.port or 4222), timeout=timeout)
+        self._rfile = self._sock.makefile("rb")
+        line = self._rfile.readline()
+        if not line.startswith(b"INFO "):
+            raise ConnectionError(f"not a NATS server (first line {line[:40]!r})")
+        self.server_info = json.loads(line[5:])
+        opts = {"verbose": False, "pedantic": False, "name": name, "lang": "python", "version": "kvbm-b200",
+                "protocol": 1, "headers": False}
+        if u.username:
+            opts.update(user=u.username, **({"pass": u.password} if u.password is not None else {}))
+        self._wlock = threading.Lock()
+        self._handlers: dict[int, tuple[str, Handler]] = {}
+        self._sid = 0
+        self._pongs = 0
+        self._pings_sent = 0
+        self._cv = threading.Condition()
+        self.last_error: str | None = None
+        self._closed = False
+        self._send(b"CONNECT " + json.dumps(opts).encode() + b"\r\n")
+        self._sock.settimeout(None)
+        self._t = threading.Thread(target=self._read_loop, daemon=True, name="kvbm-nats")
         self._t.start()
-        self._nc = asyncio.run_coroutine_threadsafe(nats.connect(url), self._loop).result(10)
+        self.flush(timeout)
+
+    def _subject(self, subject: str) -> str:
+        return f"{self.prefix}.{subject}" if self.prefix else subject
+
+    def _send(self, data: bytes) -> None:
+        with self._wlock:
+            self._sock.sendall(data)
+
+    def _read_loop(self) -> None:
+        f = self._rfile
+        try:
+            while True:
+                line = f.readline()
+                if not line:
+                    break
+                if line.startswith(b"MSG "):
+                    parts = line[4:].split()
+                    subject, sid, size = parts[0].decode(), int(parts[1]), int(parts[-1])
+                    payload = f.read(size + 2)[:size]
+                    h = self._handlers.get(sid)
+                    if h is not None:
+                        h[1](subject[len(self.prefix) + 1:] if self.prefix and subject.startswith(self.prefix + ".")
+                             else subject, payload)
+                elif line.startswith(b"PING"):
+                    self._send(b"PONG\r\n")
+                elif line.startswith(b"PONG"):
+                    with self._cv:
+                        self._pongs += 1
+                        self._cv.notify_all()
+                elif line.startswith(b"-ERR"):
+                    with self._cv:
+                        self.last_error = line[4:].strip().decode(errors="replace")
+                        self._cv.notify_all()
+                # +OK and INFO updates need no action
+        except (OSError, ValueError):
+            pass
+        finally:
+            with self._cv:
+                self._closed = True
+                self._cv.notify_all()
 
     def publish(self, subject: str, payload: bytes) -> None:
-        import asyncio
-
-        asyncio.run_coroutine_threadsafe(self._nc.publish(subject, payload), self._loop).result(10)
+        subj = self._subject(subject).encode()
+        self._send(b"PUB " + subj + b" " + str(len(payload)).encode() + b"\r\n" + bytes(payload) + b"\r\n")
 
     def subscribe(self, subject: str, handler: Handler) -> None:
-        import asyncio
+        subj = self._subject(subject)
+        patterns = [subj] if ("*" in subj.split(".") or subj.endswith(">")) else [subj, subj + ".>"]
+        for pat in patterns:
+            with self._wlock:
+                self._sid += 1
+                sid = self._sid
+            self._handlers[sid] = (pat, handler)
+            self._send(f"SUB {pat} {sid}\r\n".encode())
 
-        async def cb(msg):
-            handler(msg.subject, msg.data)
-
-        asyncio.run_coroutine_threadsafe(self._nc.subscribe(subject + ">", cb=cb), self._loop).result(10)
+    def flush(self, timeout: float | None = None) -> None:
+        """Wait until the server has processed everything sent so far."""
+        with self._cv:
+            self._pings_sent += 1
+            want = self._pings_sent
+        self._send(b"PING\r\n")
+        with self._cv:
+            ok = self._cv.wait_for(lambda: self._pongs >= want or self.last_error is not None or self._closed,
+                                   timeout=timeout if timeout is not None else self.timeout)
+            if self.last_error is not None:
+                err, self.last_error = self.last_error, None
+                raise ConnectionError(f"NATS server error: {err}")
+            if self._closed:
+                raise ConnectionError("NATS connection closed")
+            if not ok:
+                raise TimeoutError("NATS server did not answer PING")
 
     def close(self) -> None:
-        import asyncio
+        import socket
 
-        asyncio.run_coroutine_threadsafe(self._nc.close(), self._loop).result(10)
-        self._loop.call_soon_threadsafe(self._loop.stop)
+        try:
+            self._sock.shutdown(socket.SHUT_RDWR)
+        except OSError:
+            pass
+        self._sock.close()
+        self._t.join(timeout=2)
 
 
 def make_pubsub(url: str) -> PubSub:
@@ -158,7 +259,7 @@ def make_pubsub(url: str) -> PubSub:
     if url.startswith(("tcp://", "ipc://", "inproc://")):
         return ZmqPubSub(url)
     if url.startswith("nats://"):
-        return NatsPubSub(url)
+        return NatsPubSub(url)  # NATS subjects: '.'-separated tokens
     raise ValueError(f"no pub/sub transport for {url!r}")
 
 

@@ -94,3 +94,34 @@ class HubEventSink:
 
     def __call__(self, instance_id: int, batches) -> None:
         self.client.publish_events(instance_id, batches)
+
+
+def sink_for_endpoint(endpoint: str | None, hub_url: str | None = None):
+    """The event sink an ``events.endpoint`` names: ``tcp://`` / ``ipc://`` binds a ZeroMQ PUB
+    socket, ``nats://`` publishes on ``kvbm.events.<instance>`` through NATS, ``hub`` posts
+    to the hub's indexer (``hub_url``); None names no sink."""
+    if not endpoint:
+        return None
+    if endpoint.startswith(("tcp://", "ipc://", "inproc://")):
+        return ZmqEventSink(endpoint)
+    if endpoint.startswith("nats://"):
+        from ..engine.pubsub import NatsPubSub, PubSubEventSink
+
+        return PubSubEventSink(NatsPubSub(endpoint))
+    if endpoint == "hub":
+        if not hub_url:
+            raise ValueError("events.endpoint = 'hub' needs hub.url")
+        from ..hub.client import HubClient
+
+        return HubEventSink(HubClient(hub_url))
+    raise ValueError(f"unknown events endpoint {endpoint!r} (tcp://, ipc://, nats:// or hub)")
+
+
+def events_from_config(cfg, instance_id: int, hub_url: str | None = None) -> EventsManager:
+    """An EventsManager built from an ``EventsConfig``, its configured sink attached."""
+    em = EventsManager(instance_id, policy=cfg.policy, min_position=cfg.min_position, max_position=cfg.max_position,
+                       window_ms=cfg.window_ms, max_batch=cfg.max_batch)
+    sink = sink_for_endpoint(cfg.endpoint, hub_url)
+    if sink is not None:
+        em.add_sink(sink)
+    return em
