@@ -50,7 +50,7 @@ from ..logical.sequence import TokenBlockSequence
 from ..utils.metrics import CacheStatsTracker
 from ..utils.tracing import audit
 from .engine import WorkerTierEngine
-from .protocol import ConnectorMetadata, OffloadOp, OnboardOp, PushOp, RecvOp, SpillOp, StageOp
+from .protocol import ConnectorMetadata, OffloadOp, OnboardOp, PullOp, PushOp, RecvOp, SpillOp, StageOp
 
 # kv_transfer_params key a decode instance puts on the requests it sends to a prefill instance
 REMOTE_DECODE_KEY = "kvbm_remote_decode"
@@ -171,6 +171,10 @@ class ConnectorLeader:
         self.directory = directory      # where prefill instances publish their TP degree
         # the tier engine behind the LeaderEngine seam: G2/G3 state driven by the workers' reports
         self.engine = WorkerTierEngine(leader, num_workers=num_workers, g2_policy=g2_policy, g3_policy=g3_policy)
+        # remote-search pulls the workers run (queued from the remote-search thread, emitted per step)
+        self._pull_ops: list[PullOp] = []
+        self._pulls: dict[int, list] = {}   # pull id -> [done event, workers reported]
+        self._pull_ids = itertools.count(1)
         self._stage_ops: list[StageOp] = []
         self._counts = {"onboarded_blocks": 0, "offload_ops": 0}
         self.cd_stats = {"remote": 0, "local": 0, "dispatched": 0, "received": 0, "failed": 0, "pushed_blocks": 0}
@@ -372,10 +376,29 @@ class ConnectorLeader:
         return max(1, ptp // self.tp_size)
 
     # ------------------------------------------------------ metadata build
+    def queue_remote_pull(self, pools: list, src_ids: list[int], g2_ids: list[int], timeout: float = 60.0) -> None:
+        """Have the workers copy another instance's G2 blocks ``src_ids`` (its pool exports
+        ``pools``, one per rank) into this instance's G2 ``g2_ids``; returns once every worker
+        reported the copy. Called from a remote-search thread: the op leaves with the next
+        step's metadata, so the scheduler must keep stepping meanwhile."""
+        ev = threading.Event()
+        with self._lock:
+            pid = next(self._pull_ids)
+            self._pulls[pid] = [ev, 0]
+            self._pull_ops.append(PullOp(pid, list(pools), [int(i) for i in src_ids], [int(i) for i in g2_ids]))
+        try:
+            if not ev.wait(timeout):
+                raise TimeoutError(f"remote pull {pid}: the workers did not report the copy in {timeout:.0f} s")
+        finally:
+            with self._lock:
+                self._pulls.pop(pid, None)
+
     def build_connector_meta(self, out: SchedulerOutputLite) -> bytes:
         self.iteration += 1
+        with self._lock:
+            pulls, self._pull_ops = self._pull_ops, []
         meta = ConnectorMetadata(step=out.step or self.iteration, onboard=self._onboard_ops, recv=self._recv_ops,
-                                 stage=self._stage_ops)
+                                 stage=self._stage_ops, pull=pulls)
         self._onboard_ops, self._recv_ops, self._stage_ops = [], [], []
         meta.spill = [SpillOp(g2, g3) for g2, g3 in self.engine.take_spill_ops(meta.step)]
         for req_id in out.preempted_req_ids:
@@ -446,6 +469,15 @@ class ConnectorLeader:
     def update_connector_output(self, finished_sending: set[str] | None = None,
                                 finished_recving: set[str] | None = None, worker_meta: dict | None = None,
                                 invalid_block_ids: set[int] | None = None) -> None:
+        if worker_meta and worker_meta.get("pulled"):
+            worker_meta = dict(worker_meta)
+            with self._lock:
+                for pid, n in worker_meta.pop("pulled").items():
+                    p = self._pulls.get(int(pid))
+                    if p is not None:
+                        p[1] += int(n)
+                        if p[1] >= self.num_workers:
+                            p[0].set()
         self.engine.on_worker_report(worker_meta)
         bad = set(invalid_block_ids or ())
         for req_id in finished_recving or ():

@@ -9,6 +9,7 @@ One msgpack map per scheduler step::
      "spill":   [[g2_ids, g3_ids], ...],              # G2 -> G3 after the offloads
      "push":    [[req_id, peer, src, dst, slot, seq, final, peer_tp], ...],
      "recv":    [[req_id, slot, seq, g1_ids, timeout_s, contributors], ...],
+     "pull":    [[pull_id, pools, src_ids, g2_ids], ...],
      "evict":   [req_id, ...]}
 
 ``push`` / ``recv`` carry conditional disaggregation: a prefill worker
@@ -17,6 +18,11 @@ pushes the listed G1 blocks of a request into the decode instance ``peer``
 forward pass runs, and after the pass publishes ``seq`` in mailbox ``slot``
 of that instance (``final``); the decode worker watches that mailbox slot
 and reports the request as received once the value lands.
+
+``pull`` carries remote search: each worker copies ``src_ids`` of another
+instance's G2 pool (``pools[rank]``, a shared-memory pool on this node) into
+``g2_ids`` of its own G2 pool and reports ``pull_id`` in its worker
+metadata; the leader registers those G2 blocks once every worker has.
 
 Parity: crates/kvbm-connector/src/connector/leader/mod.rs:551
 (serialize_metadata, JSON WireMetadata{plan, control}); msgpack here.
@@ -89,6 +95,16 @@ class RecvOp:
 
 
 @dataclass
+class PullOp:
+    """Remote search: copy another instance's G2 blocks ``src_ids`` into this instance's ``g2_ids``."""
+
+    pull_id: int
+    pools: list           # the holder's G2 pool exports, one per worker rank
+    src_ids: list[int]
+    g2_ids: list[int]
+
+
+@dataclass
 class ConnectorMetadata:
     step: int = 0
     onboard: list[OnboardOp] = field(default_factory=list)
@@ -98,6 +114,7 @@ class ConnectorMetadata:
     spill: list[SpillOp] = field(default_factory=list)
     push: list[PushOp] = field(default_factory=list)
     recv: list[RecvOp] = field(default_factory=list)
+    pull: list[PullOp] = field(default_factory=list)
 
     def encode(self) -> bytes:
         return msgpack.packb({
@@ -110,6 +127,7 @@ class ConnectorMetadata:
             "push": [[o.req_id, o.peer, o.src_ids, o.dst_ids, o.slot, o.seq, o.final, o.peer_tp]
                      for o in self.push],
             "recv": [[o.req_id, o.slot, o.seq, o.g1_ids, o.timeout_s, o.contributors] for o in self.recv],
+            "pull": [[o.pull_id, o.pools, o.src_ids, o.g2_ids] for o in self.pull],
         }, use_bin_type=True)
 
     @classmethod
@@ -118,7 +136,9 @@ class ConnectorMetadata:
         return cls(step=d["step"], onboard=[OnboardOp(*o) for o in d["onboard"]],
                    offload=[OffloadOp(*o) for o in d["offload"]], evict=list(d.get("evict", [])),
                    stage=[StageOp(*o) for o in d.get("stage", [])], spill=[SpillOp(*o) for o in d.get("spill", [])],
-                   push=[PushOp(*o) for o in d.get("push", [])], recv=[RecvOp(*o) for o in d.get("recv", [])])
+                   push=[PushOp(*o) for o in d.get("push", [])], recv=[RecvOp(*o) for o in d.get("recv", [])],
+                   pull=[PullOp(*o) for o in d.get("pull", [])])
 
     def empty(self) -> bool:
-        return not (self.onboard or self.offload or self.evict or self.stage or self.spill or self.push or self.recv)
+        return not (self.onboard or self.offload or self.evict or self.stage or self.spill or self.push or self.recv
+                    or self.pull)

@@ -134,6 +134,64 @@ def disagg_worker_enable(worker, cfg, tp_rank: int, tp_size: int) -> bool:
     return True
 
 
+def instance_id_for(cfg, vllm_config) -> int:
+    """This engine's instance id, the same in its scheduler and its workers: ``disagg.instance_id``
+    when set, else derived from vLLM's per-engine ``engine_id``."""
+    if cfg.disagg is not None and cfg.disagg.instance_id is not None:
+        return int(cfg.disagg.instance_id)
+    import uuid
+
+    eid = str(getattr(vllm_config.kv_transfer_config, "engine_id", "") or "")
+    try:
+        return uuid.UUID(eid).int >> 64
+    except ValueError:
+        return uuid.uuid5(uuid.NAMESPACE_OID, eid or "kvbm").int >> 64
+
+
+def g2_directory(cfg):
+    """Where an engine's workers publish their G2 pool files for remote search (on this node)."""
+    import os as _os
+
+    from ..engine.cd_plane import FilePeerDirectory
+
+    url = cfg.disagg.directory if cfg.disagg is not None else "file:///dev/shm/kvbm_pd"
+    root = url[len("file://"):] if url.startswith("file://") else "/dev/shm/kvbm_pd"
+    return FilePeerDirectory(_os.path.join(root, "g2"))
+
+
+class RemoteSearchPlane:
+    """A scheduler's side of remote search: its messenger (serving its own G2 blocks to other
+    instances as a holder), its hub registration and the search itself, whose pulls the
+    connector's workers run (``ConnectorLeader.queue_remote_pull``)."""
+
+    def __init__(self, cfg, leader: ConnectorLeader, instance_id: int, tp_size: int, block_size: int):
+        from ..engine.remote_search import RemoteHolder, RemoteSearch, RemoteSearchConfig
+        from ..hub.client import HubClient, HubRegistration
+        from ..runtime.messenger import Messenger
+
+        if cfg.hub is None or not cfg.hub.url:
+            raise ValueError("remote_search.enabled needs hub.url (the hub's indexer finds the holders)")
+        rs = cfg.remote_search
+        self.messenger = Messenger(instance_id)
+        self.hub = HubClient(cfg.hub.url)
+        self.registration = HubRegistration(self.hub, instance_id, features=["indexer", "p2p"],
+                                            address=self.messenger.address)
+        g2dir = g2_directory(cfg)
+        self.holder = RemoteHolder(leader.leader, [], self.messenger, pool_source=lambda: [
+            g2dir.lookup(instance_id, timeout_s=rs.timeout_secs, rank=r) for r in range(tp_size)])
+        self.search = RemoteSearch(leader.leader, [], self.messenger, self.hub, block_size,
+                                   RemoteSearchConfig(enabled=True, min_remote_tokens=rs.min_remote_tokens,
+                                                      max_query_hashes=rs.max_query_hashes, timeout=rs.timeout_secs),
+                                   copier=lambda pools, src, dst: leader.queue_remote_pull(
+                                       pools, src, dst, timeout=max(30.0, 6 * rs.timeout_secs)))
+        leader.remote = self.search
+
+    def close(self) -> None:
+        self.search.close()
+        self.registration.close()
+        self.messenger.close()
+
+
 def _base():
     from vllm.distributed.kv_transfer.kv_connector.v1.base import (KVConnectorBase_V1, KVConnectorMetadata,
                                                                   KVConnectorRole)
@@ -163,16 +221,21 @@ def _define():
         WorkerMetaBase = object
 
     class KvbmConnectorWorkerMetadata(WorkerMetaBase):
-        """Worker -> scheduler report: steps whose G1 -> G2 copies a worker finished (summed over workers)."""
+        """Worker -> scheduler report: steps whose G1 -> G2 copies / G2 -> G3 spills and remote pulls a
+        worker finished, summed over workers."""
 
         def __init__(self, data: dict):
             self.data = data
 
         def aggregate(self, other):
-            merged = {int(k): int(v) for k, v in self.data.get("offloaded", {}).items()}
-            for k, v in other.data.get("offloaded", {}).items():
-                merged[int(k)] = merged.get(int(k), 0) + int(v)
-            return KvbmConnectorWorkerMetadata({"offloaded": merged})
+            # every report kind (offloaded / spilled steps, pulled ids) maps an id to a worker count
+            out: dict = {}
+            for d in (self.data, other.data):
+                for kind, counts in (d or {}).items():
+                    m = out.setdefault(kind, {})
+                    for k, v in counts.items():
+                        m[int(k)] = m.get(int(k), 0) + int(v)
+            return KvbmConnectorWorkerMetadata(out)
 
     class KvbmConnector(Base):
         """KV Block Manager connector for vLLM (scheduler and worker roles)."""
@@ -185,6 +248,7 @@ def _define():
             from .worker import ConnectorWorker, blocks_for_bytes
 
             ktc = vllm_config.kv_transfer_config
+            self._vllm_config = vllm_config
             extra = getattr(ktc, "kv_connector_extra_config", {}) or {}
             self.info = extract_vllm_config_for_kvbm(vllm_config)
             bs = self.info["block_size"]
@@ -200,12 +264,17 @@ def _define():
                 # the G2/G3 presence events: to the configured sink (events.enabled) and/or the consolidator
                 self.consolidator = self._events = None
                 eps = get_consolidator_endpoints(vllm_config)
-                if eps is not None or cfg.events.enabled:
-                    from ..logical.events import events_from_config
+                iid = instance_id_for(cfg, vllm_config)
+                searching = bool(cfg.remote_search.enabled)
+                if eps is not None or cfg.events.enabled or searching:
+                    from ..logical.events import HubEventSink, events_from_config
 
-                    iid = int((cfg.disagg.instance_id if cfg.disagg else None) or os.getpid())
                     ev_cfg = cfg.events if cfg.events.enabled else dataclasses.replace(cfg.events, endpoint=None)
                     self._events = events_from_config(ev_cfg, iid, cfg.hub.url if cfg.hub else None)
+                    if searching and ev_cfg.endpoint != "hub" and cfg.hub is not None and cfg.hub.url:
+                        from ..hub.client import HubClient
+
+                        self._events.add_sink(HubEventSink(HubClient(cfg.hub.url)))  # holders for the indexer
                 if eps is not None:
                     from ..consolidator.service import start_leader_consolidator
 
@@ -222,6 +291,10 @@ def _define():
                                                num_workers=max(1, int(self.info.get("tensor_parallel_size", 1))),
                                                tp_size=max(1, int(self.info.get("tensor_parallel_size", 1))),
                                                **disagg_leader_kwargs(cfg))
+                self._remote = None
+                if searching:
+                    self._remote = RemoteSearchPlane(cfg, self._leader, iid,
+                                                     max(1, int(self.info.get("tensor_parallel_size", 1))), bs)
                 self._worker = None
             else:
                 cfg = KvbmConfig.for_worker(json.dumps(extra) if extra else None)
@@ -276,6 +349,9 @@ def _define():
         def _join_plane(self):
             tp = max(1, int(self.info.get("tensor_parallel_size", 1)))
             disagg_worker_enable(self._worker, self._cfg, int(self.info.get("rank", 0)) % tp, tp)
+            if self._cfg.remote_search.enabled and getattr(self._worker.worker, "g2_layout", None) is not None:
+                self._worker.tp_rank, self._worker.tp_size = int(self.info.get("rank", 0)) % tp, tp
+                self._worker.publish_g2(g2_directory(self._cfg), instance_id_for(self._cfg, self._vllm_config))
 
         def register_kv_caches(self, kv_caches):
             self._worker.register_kv_caches(dict(kv_caches))
@@ -329,6 +405,8 @@ def _define():
                 self._events.stop()
             if getattr(self, "consolidator", None) is not None:
                 self.consolidator.close()
+            if getattr(self, "_remote", None) is not None:
+                self._remote.close()
 
     globals()["KvbmConnector"] = KvbmConnector
     globals()["KvbmConnectorMetadata"] = KvbmConnectorMetadata

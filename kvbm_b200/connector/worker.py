@@ -89,6 +89,27 @@ class PeerConnection:
         self.mailbox.close()
 
 
+_MAPPED_POOLS: dict[str, KvLayout] = {}
+
+
+def run_remote_pull(op, g2: KvLayout, rank: int) -> int:
+    """Copy a remote-search pull into this worker's G2 pool: ``op.src_ids`` of the holder's
+    rank-``rank`` G2 pool (a shared-memory file on this node, mapped once and kept) into
+    ``op.g2_ids``. Returns the number of blocks copied."""
+    from ..engine.remote_search import _map_pool
+
+    pd = op.pools[rank if rank < len(op.pools) else 0]
+    path = (pd.get("extra") or {}).get("shm_path") or ""
+    src = _MAPPED_POOLS.get(path)
+    if src is None:
+        src = _map_pool(pd)
+        if src is None:
+            raise RuntimeError(f"remote pull {op.pull_id}: the holder's G2 pool {path!r} is not on this node")
+        _MAPPED_POOLS[path] = src
+    g2.scatter_blocks(list(op.g2_ids), src.gather_blocks(list(op.src_ids)))
+    return len(op.g2_ids)
+
+
 class ConnectorWorker:
     def __init__(self, config: KvbmConfig | None = None, rank: int = 0, device: int | None = None,
                  block_size: int = 16, num_kv_heads: int | None = None, head_size: int | None = None):
@@ -114,6 +135,7 @@ class ConnectorWorker:
         self.transfer_log: list | None = None
         self._pending_finished: set[str] = set()
         self._offload_steps: list[tuple[int, torch.cuda.Event]] = []
+        self._pulls_done: list[int] = []  # remote-search pulls copied into G2, reported once
         self._spill_steps: list[int] = []
         # conditional disaggregation
         self.layer_batch = max(1, int(self.config.transfer.layer_batch))
@@ -168,6 +190,15 @@ class ConnectorWorker:
         self._build_worker()
         return self.g1
 
+    def publish_g2(self, directory, instance_id: int) -> dict:
+        """Publish this worker's G2 pool (a shared-memory file) so another instance on the node can
+        pull matched blocks from it (remote search); returns the export."""
+        from ..engine.remote_search import pool_export
+
+        d = pool_export(self.worker.g2_layout)
+        directory.publish(int(instance_id), d, rank=self.tp_rank if self.tp_size > 1 else self.rank)
+        return d
+
     def register_layout(self, layout: KvLayout) -> KvLayout:
         """Use an already described G1 pool (a serving engine that allocates its KV through the block manager)."""
         self.g1 = layout
@@ -191,7 +222,8 @@ class ConnectorWorker:
                                     startup_benchmark=c.transfer.startup_benchmark)
         self.worker = Worker(self.rank, self.g1, g2_blocks=g2, g3_blocks=g3, g3_path=path, device=self.device,
                              capabilities=caps, engine=c.transfer.engine, disk_direct=c.cache.disk.use_direct_io,
-                             g2_numa_node=c.cache.host.numa_node, g2_hugepages=bool(c.cache.host.hugepages))
+                             g2_numa_node=c.cache.host.numa_node, g2_hugepages=bool(c.cache.host.hugepages),
+                             g2_shared=bool(c.remote_search.enabled))
 
     def handshake_metadata(self) -> dict:
         """Layout facts the leader needs to size its logical pools."""
@@ -321,6 +353,11 @@ class ConnectorWorker:
 
     def start_load_kv(self) -> None:
         meta = self._meta
+        for op in (meta.pull if meta is not None else ()):
+            # host-to-host copy of another instance's G2 blocks; the leader registers them (and only then
+            # matches and onboards them) once every worker reported
+            run_remote_pull(op, self.worker.g2_layout, self.tp_rank if self.tp_size > 1 else self.rank)
+            self._pulls_done.append(op.pull_id)
         now = time.monotonic()
         for op in (meta.recv if meta is not None else ()):
             self._recvs[op.req_id] = (op, now + op.timeout_s)
@@ -500,6 +537,9 @@ class ConnectorWorker:
             out["offloaded"] = done
         if spilled:
             out["spilled"] = spilled
+        if self._pulls_done:
+            out["pulled"] = {p: 1 for p in self._pulls_done}
+            self._pulls_done = []
         return out or None
 
     def get_block_ids_with_load_errors(self) -> set[int]:

@@ -43,6 +43,7 @@ import threading
 import time
 import warnings
 from dataclasses import dataclass
+from typing import Callable
 
 import numpy as np
 import torch
@@ -76,6 +77,11 @@ def pool_export(layout: KvLayout, shareable: bool = True) -> dict:
     return d
 
 
+def _block_bytes(d: dict) -> int:
+    """Bytes of one block of an exported pool (from its layout configuration)."""
+    return LayoutConfig(**LayoutDescriptor.from_dict(d).config).bytes_per_block
+
+
 def _map_pool(d: dict) -> KvLayout | None:
     """Map a peer's shared-file G2 pool into this process (None when not reachable)."""
     extra = d.get("extra") or {}
@@ -98,10 +104,14 @@ class RemoteHolder:
     """Serves transfer sessions on this instance's G2 blocks."""
 
     def __init__(self, leader, g2_layouts: list[KvLayout], messenger, sessions=None, lease_s: float = 60.0,
-                 shareable: bool = True):
+                 shareable: bool = True, pool_source: Callable[[], list[dict]] | None = None):
+        """``g2_layouts``: this process's G2 pools, one per worker rank; or, when the pools live in
+        worker processes (a connector's scheduler), ``pool_source`` returns their exports (and the
+        messenger read path, which needs the bytes here, is not offered)."""
         from ..parallel.session import SessionManager
 
         self.leader, self.layouts, self.messenger = leader, list(g2_layouts), messenger
+        self.pool_source = pool_source
         self.sessions = sessions or SessionManager()
         self.lease_s = lease_s  # pins of a session its initiator never closes are dropped after this
         self.shareable = shareable  # False: initiators read payload over the messenger
@@ -132,10 +142,13 @@ class RemoteHolder:
             self._pinned[s.session_id] = blocks
             self._opened[s.session_id] = time.monotonic()
         audit("transfer_session_opened", session=s.session_id, initiator=str(req["initiator"]), blocks=len(blocks))
-        return {"sid": s.session_id, "block_ids": [b.block_id for b in blocks],
-                "pools": [pool_export(l, self.shareable) for l in self.layouts]}
+        pools = self.pool_source() if self.pool_source is not None else [pool_export(l, self.shareable)
+                                                                          for l in self.layouts]
+        return {"sid": s.session_id, "block_ids": [b.block_id for b in blocks], "pools": pools}
 
     def _read(self, req: dict) -> bytes:
+        if not self.layouts:
+            raise RuntimeError("this holder's G2 pools live in its worker processes: map them by their files")
         with self._lock:
             blocks = self._pinned[req["sid"]]
         ids = [b.block_id for b in blocks[req["first"]: req["first"] + req["count"]]]
@@ -164,8 +177,13 @@ class RemoteSearch:
     """Initiator side: find a holder through the hub, pull into local G2."""
 
     def __init__(self, leader, g2_layouts: list[KvLayout], messenger, hub, block_size: int,
-                 config: RemoteSearchConfig | None = None):
+                 config: RemoteSearchConfig | None = None,
+                 copier: Callable[[list, list[int], list[int]], None] | None = None):
+        """``copier(pools, src_ids, dst_ids)``, when given, moves the bytes instead of this process
+        (a connector's scheduler hands the copy to its workers, whose G2 pools these are) and
+        returns once they landed; ``g2_layouts`` may then be empty."""
         self.leader, self.layouts, self.messenger, self.hub = leader, list(g2_layouts), messenger, hub
+        self.copier = copier
         self.block_size = block_size
         self.config = config or RemoteSearchConfig(enabled=True)
         self._pool = cf.ThreadPoolExecutor(max_workers=2, thread_name_prefix="kvbm-remote")
@@ -243,6 +261,15 @@ class RemoteSearch:
         dst, _ = got
         dst_ids = [b.block_id for b in dst]
         pools = resp["pools"]
+        if self.copier is not None:
+            try:
+                self.copier(pools, list(resp["block_ids"]), dst_ids)
+            except Exception:
+                for b in dst:
+                    b.release()
+                raise
+            self.stats["bytes"] += n * _block_bytes(pools[0])
+            return self._register_pulled(dst, hashes, n, sid)
         if len(pools) != len(self.layouts):
             raise ValueError(f"holder has {len(pools)} workers, this instance {len(self.layouts)}")
         for w, (pd, mine) in enumerate(zip(pools, self.layouts)):
@@ -264,6 +291,9 @@ class RemoteSearch:
                                 else mine.dtype).view(shape)
                 mine.scatter_blocks(dst_ids, data)
             self.stats["bytes"] += n * mine.config.bytes_per_block
+        return self._register_pulled(dst, hashes, n, sid)
+
+    def _register_pulled(self, dst, hashes: list[int], n: int, sid) -> int:
         registered = self.leader.g2.register_mutable(dst, hashes[:n])
         for b in registered:
             b.release()  # now an inactive (matchable) G2 block

@@ -44,7 +44,7 @@ class Worker:
     def __init__(self, rank: int, g1: KvLayout, g2_blocks: int = 0, g3_blocks: int = 0, g3_path: str | None = None,
                  device: int | None = None, capabilities: TransferCapabilities | None = None,
                  engine: str = "auto", bounce_blocks: int = 64, disk_direct: bool = True,
-                 g2_numa_node: int | str | None = None, g2_hugepages: bool = False):
+                 g2_numa_node: int | str | None = None, g2_hugepages: bool = False, g2_shared: bool = False):
         self.rank = rank
         self.device = device if device is not None else (g1.device if g1.device is not None else 0)
         self.tm = TransferManager(worker_id=rank, device=self.device, capabilities=capabilities)
@@ -55,8 +55,11 @@ class Worker:
         fc = KvBlockLayout.OPERATIONAL_NHD if g1.block_layout == KvBlockLayout.UNIVERSAL else g1.block_layout
         if g2_blocks:
             g2cfg = LayoutConfig(**{**cfg.__dict__, "num_blocks": g2_blocks})
-            self.g2_layout = KvLayout.allocate(g2cfg, "fully_contiguous", fc, location="pinned", device=self.device,
-                                               numa_node=g2_numa_node, hugepages=g2_hugepages)
+            # g2_shared: a named shared-memory file other instances on the node can map (remote search)
+            self.g2_layout = KvLayout.allocate(g2cfg, "fully_contiguous", fc,
+                                               location="shared" if g2_shared else "pinned", device=self.device,
+                                               numa_node=None if g2_shared else g2_numa_node,
+                                               hugepages=False if g2_shared else g2_hugepages)
             self.handles.g2 = self.tm.register_layout(self.g2_layout)
         if g3_blocks:
             g3cfg = LayoutConfig(**{**cfg.__dict__, "num_blocks": g3_blocks})

@@ -204,3 +204,88 @@ def test_leader_control_plane_modules(hub):
     finally:
         a.close()
         b.close()
+
+
+def test_vllm_connectors_pull_a_prefix_from_another_engine(hub, tmp_path):
+    """Two scheduler-role vLLM connectors with ``remote_search.enabled``: engine A offloads a
+    prompt to G2 (its G2 presence reaches the hub's indexer through the connector's event sink);
+    engine B's GNMT stalls on the same prompt while its remote search opens a session on A's
+    scheduler (A's pool exports come from the file its worker published) and hands the copy to
+    B's workers as a pull op; once they report it, B registers the blocks and matches them."""
+    import time
+    from types import SimpleNamespace
+
+    vllm_base = pytest.importorskip("vllm.distributed.kv_transfer.kv_connector.v1.base")
+    from test_vllm_connector import _request, _sched_output, _vllm_config
+
+    from kvbm_b200.connector import vllm_connector as vc
+    from kvbm_b200.connector.protocol import ConnectorMetadata
+    from kvbm_b200.connector.worker import run_remote_pull
+    from kvbm_b200.engine.remote_search import pool_export
+
+    def extra(iid):
+        return {"leader": {"cache": {"host": {"num_blocks": 32}}, "hub": {"url": hub.url},
+                           "remote_search": {"enabled": True, "timeout_secs": 5.0},
+                           "events": {"policy": "all", "window_ms": 5},
+                           "disagg": {"instance_id": iid, "directory": f"file://{tmp_path}"}}}
+
+    Role = vllm_base.KVConnectorRole
+    cfg = LayoutConfig.for_model(32, 2, 2, 64, BS)
+    # each engine's worker: a G2 pool in a shared-memory file, published where its scheduler finds it
+    pools = {}
+    for iid in (701, 702):
+        pools[iid] = KvLayout.allocate(cfg, "fully_contiguous", KvBlockLayout.OPERATIONAL_NHD, location="shared")
+        vc.g2_directory(SimpleNamespace(disagg=SimpleNamespace(directory=f"file://{tmp_path}"))).publish(
+            iid, pool_export(pools[iid]), rank=0)
+    a = vc.KvbmConnector(_vllm_config(extra(701)), Role.SCHEDULER)
+    b = vc.KvbmConnector(_vllm_config(extra(702)), Role.SCHEDULER)
+    try:
+        tokens = list(range(3000, 3000 + 5 * BS + 3))
+        ra = _request("a1", tokens)
+        deadline = time.monotonic() + 5
+        while (got := a.get_num_new_matched_tokens(ra, 0))[0] is None and time.monotonic() < deadline:
+            time.sleep(0.01)  # A searches too (no other holder yet): a stall, then a cold miss
+        assert got == (0, False)
+        a.update_state_after_alloc(ra, SimpleNamespace(get_block_ids=lambda: ([0, 1, 2, 3, 4, 5],)), 0)
+        m = ConnectorMetadata.decode(a.build_connector_meta(_sched_output([("a1", [0, 1, 2, 3, 4, 5])],
+                                                                          {"a1": len(tokens)})).metadata)
+        [off] = m.offload
+        fill_blocks(pools[701], off.g2_ids, FillPattern.RANDOM, seed=4)  # what A's worker copied out of G1
+        want = checksum_blocks(pools[701], off.g2_ids)
+        a.update_connector_output(SimpleNamespace(finished_sending={"a1"}, finished_recving=None,
+                                                  kv_connector_worker_meta=vc.KvbmConnectorWorkerMetadata(
+                                                      {"offloaded": {m.step: 1}}), invalid_block_ids=set()))
+        c = HubClient(hub.url)
+        hashes = sequence_hashes(tokens, BS)
+        deadline = time.monotonic() + 10
+        while not c.query(hashes[:5]).get("hit") and time.monotonic() < deadline:
+            time.sleep(0.01)  # A's presence events reach the indexer within an event window
+        assert c.query(hashes[:5])["holders"] == [701]
+        rb = _request("b1", tokens)
+        n = None
+        pull_meta = None
+        while time.monotonic() < deadline:
+            n, _ = b.get_num_new_matched_tokens(rb, 0)
+            if n is not None:
+                break
+            # B's workers: run whatever pull the step's metadata carries and report it
+            mb = ConnectorMetadata.decode(b.build_connector_meta(_sched_output([], {})).metadata)
+            done = {}
+            for op in mb.pull:
+                run_remote_pull(op, pools[702], 0)
+                done[op.pull_id] = 1
+                pull_meta = op
+            b.update_connector_output(SimpleNamespace(
+                finished_sending=None, finished_recving=None, invalid_block_ids=set(),
+                kv_connector_worker_meta=vc.KvbmConnectorWorkerMetadata({"pulled": done}) if done else None))
+            time.sleep(0.01)
+        assert n == 5 * BS, "B never matched the pulled prefix"
+        assert pull_meta is not None and len(pull_meta.src_ids) == 5
+        assert checksum_blocks(pools[702], pull_meta.g2_ids) == want  # same bytes in B's G2
+        assert b._remote.search.stats["pulled_blocks"] == 5
+        assert a._remote.holder.open_sessions() == 0  # A's session closed after the pull
+    finally:
+        a.shutdown()
+        b.shutdown()
+        for lay in pools.values():
+            lay.backing.close()
