@@ -258,10 +258,10 @@ def _define():
                 bpb = kv_block_bytes(self.info)
                 g2n = blocks_for_bytes(cfg.cache.host.cache_size_gb, cfg.cache.host.num_blocks, bpb)
                 g3n = blocks_for_bytes(cfg.cache.disk.cache_size_gb, cfg.cache.disk.num_blocks, bpb)
-                # KV-event consolidator: vLLM's G1 events and the block manager's G2/G3 presence in one stream
                 from .consolidator_config import get_consolidator_endpoints
 
-                # the G2/G3 presence events: to the configured sink (events.enabled) and/or the consolidator
+                # the G2/G3 presence events go to the configured sink (events.enabled), to the KV-event
+                # consolidator (merged with vLLM's G1 events) and, with remote search, to the hub's indexer
                 self.consolidator = self._events = None
                 eps = get_consolidator_endpoints(vllm_config)
                 iid = instance_id_for(cfg, vllm_config)
