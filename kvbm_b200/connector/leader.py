@@ -384,11 +384,13 @@ class ConnectorLeader:
         ev = threading.Event()
         with self._lock:
             pid = next(self._pull_ids)
-            self._pulls[pid] = [ev, 0]
+            self._pulls[pid] = [ev, 0, False]  # done event, workers reported, a worker failed
             self._pull_ops.append(PullOp(pid, list(pools), [int(i) for i in src_ids], [int(i) for i in g2_ids]))
         try:
             if not ev.wait(timeout):
                 raise TimeoutError(f"remote pull {pid}: the workers did not report the copy in {timeout:.0f} s")
+            if self._pulls[pid][2]:
+                raise RuntimeError(f"remote pull {pid}: a worker could not copy the holder's blocks")
         finally:
             with self._lock:
                 self._pulls.pop(pid, None)
@@ -469,13 +471,16 @@ class ConnectorLeader:
     def update_connector_output(self, finished_sending: set[str] | None = None,
                                 finished_recving: set[str] | None = None, worker_meta: dict | None = None,
                                 invalid_block_ids: set[int] | None = None) -> None:
-        if worker_meta and worker_meta.get("pulled"):
+        if worker_meta and (worker_meta.get("pulled") or worker_meta.get("pull_failed")):
             worker_meta = dict(worker_meta)
             with self._lock:
-                for pid, n in worker_meta.pop("pulled").items():
-                    p = self._pulls.get(int(pid))
-                    if p is not None:
+                for kind in ("pulled", "pull_failed"):
+                    for pid, n in (worker_meta.pop(kind, None) or {}).items():
+                        p = self._pulls.get(int(pid))
+                        if p is None:
+                            continue
                         p[1] += int(n)
+                        p[2] = p[2] or kind == "pull_failed"
                         if p[1] >= self.num_workers:
                             p[0].set()
         self.engine.on_worker_report(worker_meta)

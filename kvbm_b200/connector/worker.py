@@ -136,6 +136,7 @@ class ConnectorWorker:
         self._pending_finished: set[str] = set()
         self._offload_steps: list[tuple[int, torch.cuda.Event]] = []
         self._pulls_done: list[int] = []  # remote-search pulls copied into G2, reported once
+        self._pulls_failed: list[int] = []
         self._spill_steps: list[int] = []
         # conditional disaggregation
         self.layer_batch = max(1, int(self.config.transfer.layer_batch))
@@ -355,9 +356,16 @@ class ConnectorWorker:
         meta = self._meta
         for op in (meta.pull if meta is not None else ()):
             # host-to-host copy of another instance's G2 blocks; the leader registers them (and only then
-            # matches and onboards them) once every worker reported
-            run_remote_pull(op, self.worker.g2_layout, self.tp_rank if self.tp_size > 1 else self.rank)
-            self._pulls_done.append(op.pull_id)
+            # matches and onboards them) once every worker reported. A failed pull is reported, never
+            # raised into the forward pass: the request then prefills what it could not pull.
+            try:
+                run_remote_pull(op, self.worker.g2_layout, self.tp_rank if self.tp_size > 1 else self.rank)
+                self._pulls_done.append(op.pull_id)
+            except Exception as e:  # noqa: BLE001
+                from ..utils.tracing import audit
+
+                audit("remote_pull_failed", pull=op.pull_id, error=str(e))
+                self._pulls_failed.append(op.pull_id)
         now = time.monotonic()
         for op in (meta.recv if meta is not None else ()):
             self._recvs[op.req_id] = (op, now + op.timeout_s)
@@ -540,6 +548,9 @@ class ConnectorWorker:
         if self._pulls_done:
             out["pulled"] = {p: 1 for p in self._pulls_done}
             self._pulls_done = []
+        if self._pulls_failed:
+            out["pull_failed"] = {p: 1 for p in self._pulls_failed}
+            self._pulls_failed = []
         return out or None
 
     def get_block_ids_with_load_errors(self) -> set[int]:

@@ -211,3 +211,42 @@ def test_worker_reports_sent_only_for_requests_that_sent():
     w._send_seen.add("b")  # "b" offloaded; its copies have completed (no events left to wait for)
     assert w.get_finished({"a", "b"}) == ({"b"}, set())
     assert w.get_finished({"b"}) == (set(), set())  # reported once
+
+
+def test_remote_pull_reports_and_failures():
+    """A remote-search pull leaves with the next step's metadata and completes when every worker
+    reported it; a worker that could not copy makes the pull fail (the request then prefills)."""
+    import threading as th
+
+    g2 = BlockManager(8, 16, "lru", Tier.G2)
+    L = ConnectorLeader(InstanceLeader.scheduler_side(g2), 16, num_workers=2)
+    res = {}
+
+    def pull(name, **kw):
+        try:
+            L.queue_remote_pull([{"extra": {}}], [1, 2], [5, 6], timeout=5.0)
+            res[name] = "ok"
+        except Exception as e:  # noqa: BLE001
+            res[name] = type(e).__name__
+
+    t = th.Thread(target=pull, args=("a",))
+    t.start()
+    while True:
+        m = ConnectorMetadata.decode(L.build_connector_meta(SchedulerOutputLite(1)))
+        if m.pull:
+            break
+    [op] = m.pull
+    assert (op.src_ids, op.g2_ids) == ([1, 2], [5, 6])
+    L.update_connector_output(worker_meta={"pulled": {op.pull_id: 1}})
+    assert t.is_alive()  # one of two workers
+    L.update_connector_output(worker_meta={"pulled": {op.pull_id: 1}})
+    t.join(5)
+    assert res["a"] == "ok"
+    t = th.Thread(target=pull, args=("b",))
+    t.start()
+    while not (m := ConnectorMetadata.decode(L.build_connector_meta(SchedulerOutputLite(2)))).pull:
+        pass
+    L.update_connector_output(worker_meta={"pulled": {m.pull[0].pull_id: 1}, "offloaded": {}})
+    L.update_connector_output(worker_meta={"pull_failed": {m.pull[0].pull_id: 1}})
+    t.join(5)
+    assert res["b"] == "RuntimeError"
