@@ -134,6 +134,15 @@ class RemoteHolder:
         self._expire()
         hashes = [int(h) for h in req["hashes"]]
         blocks = self.leader.g2.match_blocks(hashes)
+        if (req.get("tiers") or {}).get("g3", True) and getattr(self.leader, "g3", None) is not None \
+                and len(self.leader.workers) and len(blocks) < len(hashes):
+            # the prefix continues in G3: stage it into G2 with this leader's workers first, so the
+            # session offers the whole match (the reference's synchronous find mode)
+            from .leader import FindMatchesOptions, StagingMode
+
+            for b in blocks:
+                b.release()
+            blocks = self.leader.find_matches(hashes, FindMatchesOptions(staging=StagingMode.FULL)).g2_blocks
         if not blocks:
             return {"sid": None, "block_ids": []}
         s = self.sessions.open(int(req["initiator"]), int(self.leader.instance_id))

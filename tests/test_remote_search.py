@@ -289,3 +289,45 @@ def test_vllm_connectors_pull_a_prefix_from_another_engine(hub, tmp_path):
         b.shutdown()
         for lay in pools.values():
             lay.backing.close()
+
+
+def test_holder_stages_a_g3_continuation_before_the_pull(hub):
+    """A holder whose prefix continues in G3 stages those blocks into G2 with its workers before
+    answering, so the initiator pulls the whole match (2 blocks from G2 + 3 from G3)."""
+    from kvbm_b200.physical.transfer import TransferCompleteNotification
+
+    c = HubClient(hub.url)
+    a = _Instance(801, c, KvBlockLayout.OPERATIONAL_NHD)
+    b = _Instance(802, c, KvBlockLayout.OPERATIONAL_NHD)
+    g3_layout = KvLayout.allocate(LayoutConfig.for_model(32, 2, 2, 64, BS), "fully_contiguous",
+                                  KvBlockLayout.OPERATIONAL_NHD, location="shared")
+
+    class StageWorker:  # moves G3 -> G2 bytes the way a worker's transfer manager does
+        def execute_local_transfer(self, src_tier, src_ids, dst_tier, dst_ids, layer_range=None):
+            assert (src_tier, dst_tier) == (Tier.G3, Tier.G2)
+            a.layout.scatter_blocks(list(dst_ids), g3_layout.gather_blocks(list(src_ids)))
+            return TransferCompleteNotification.ready()
+
+    try:
+        g3 = BlockManager(32, BS, "lru", Tier.G3, registry=a.g2.registry)
+        a.leader.g3, a.leader.workers = g3, ParallelWorkers([StageWorker()])
+        hashes = sequence_hashes(list(range(9000, 9000 + 5 * BS)), BS)
+        hot = a.g2.allocate_blocks(2)
+        fill_blocks(a.layout, [x.block_id for x in hot], FillPattern.RANDOM, seed=1)
+        cold = g3.allocate_blocks(3)
+        fill_blocks(g3_layout, [x.block_id for x in cold], FillPattern.RANDOM, seed=2)
+        want = checksum_blocks(a.layout, [x.block_id for x in hot]) + checksum_blocks(g3_layout,
+                                                                                       [x.block_id for x in cold])
+        for x in a.g2.register_mutable(hot, hashes[:2]) + g3.register_mutable(cold, hashes[2:]):
+            x.release()
+        c.publish_events(a.iid, [("create", hashes)])
+        rs = RemoteSearch(b.leader, [b.layout], b.msg, c, BS, RemoteSearchConfig(enabled=True))
+        assert rs.pull(801, hashes) == 5
+        got = b.g2.match_blocks(hashes)
+        assert checksum_blocks(b.layout, [x.block_id for x in got]) == want
+        assert a.g2.count_prefix(hashes) == 5  # the staged blocks stay in A's G2
+        rs.close()
+    finally:
+        a.close()
+        b.close()
+        g3_layout.backing.close()
