@@ -244,6 +244,15 @@ def main(argv=None) -> int:
     ct.add_argument("--timeout", type=float, default=10.0)
     ct.add_argument("action", choices=["modules", "describe", "metrics", "reset"])
     ct.add_argument("--tiers", default=None, help="reset: comma list of g2,g3 (default: every configured tier)")
+    cal = sub.add_parser("calibrate", help="run a prefill worker's calibration sweep through the hub")
+    cal.add_argument("--instance-id", type=int, required=True)
+    cal.add_argument("--seq", default=None, help="comma list of input lengths (default: the engine's ladder)")
+    cal.add_argument("--osl", type=int, default=None)
+    cal.add_argument("--seed", type=int, default=None)
+    cal.add_argument("--max-isl-fraction", type=float, default=None)
+    cal.add_argument("--no-warmup", action="store_true")
+    cal.add_argument("--force", action="store_true", help="re-run even when the worker has a cached result")
+    cal.add_argument("--timeout", type=float, default=1800.0)
     a = p.parse_args(argv)
     client = HubClient(a.hub)
     if a.cmd == "health":
@@ -276,6 +285,29 @@ def main(argv=None) -> int:
         except ControlError as e:
             print(f"kvbmctl: {e}", file=sys.stderr)
             return 2
+    elif a.cmd == "calibrate":
+        req = {k: v for k, v in {"seq": [int(x) for x in a.seq.split(",")] if a.seq else None, "osl": a.osl,
+                                  "seed": a.seed, "max_isl_fraction": a.max_isl_fraction,
+                                  "warmup": False if a.no_warmup else None}.items() if v is not None}
+        try:
+            res = client.run_calibration(a.instance_id, req, force=a.force, timeout=a.timeout)
+        except RuntimeError as e:
+            print(f"kvbmctl: {e}", file=sys.stderr)
+            return 2
+        if a.json:
+            out = res
+        else:
+            pm = res["results"]["performance_model"]
+            print(f"instance {a.instance_id}: {'cached' if res['from_cache'] else 'measured'} over "
+                  f"ISL {res['resolved']['seq']}, OSL {res['resolved']['osl']}")
+            print(f"  TTFT(us) = {pm['t2ft_intercept']:.1f} + {pm['t2ft_linear']:.4g}*ISL + "
+                  f"{pm['t2ft_quadratic']:.4g}*ISL^2   (R^2 {pm['t2ft_fit_r2']:.4f})")
+            print(f"  ITL(us)  = {pm['t2tl_intercept']:.1f} + {pm['t2tl_slope']:.4g}*position   "
+                  f"(R^2 {pm['t2tl_fit_r2']:.4f})")
+            print(f"  n_opt {res['results']['n_opt']}  n_att {res['results']['n_att']}")
+            for c_ in res["resolved"].get("clamps", []):
+                print(f"  clamp: {c_}")
+            return 0
     elif a.cmd == "p2p":
         out = run_p2p(a, client)
         if a.p2p == "pin" and out.get("sid") is not None:

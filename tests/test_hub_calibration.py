@@ -73,7 +73,7 @@ def test_analyze_recovers_the_model():
         analyze(tr[:3])
 
 
-def test_hub_triggers_a_sweep_through_the_prefill_worker():
+def test_hub_triggers_a_sweep_through_the_prefill_worker(capsys):
     from kvbm_b200.hub.calibrate_lambda import capture_calibration_defaults, make_calibrate_lambda
     from kvbm_b200.hub.client import HubClient, PrefillRouterHandler
     from kvbm_b200.hub.server import HubServer
@@ -124,8 +124,17 @@ def test_hub_triggers_a_sweep_through_the_prefill_worker():
         # the hub fed its router's TTFT model for this instance
         cal = client.router_counters()["calibration"][str(handler.instance_id)]
         assert cal["ttft_samples"] == 4 and "ttft_coeffs" in cal
-        # a second ask is served from the worker's cache unless forced
+        # a second ask is served from the worker's cache unless forced (here through kvbmctl)
         assert client.run_calibration(handler.instance_id, req, timeout=60)["from_cache"]
+        import json
+
+        from kvbm_b200.hub.kvbmctl import main as kvbmctl
+
+        assert kvbmctl(["--hub", hub.url, "--json", "calibrate", "--instance-id", str(handler.instance_id),
+                        "--seq", "256,512,1024,2048", "--osl", "6"]) == 0
+        assert json.loads(capsys.readouterr().out)["from_cache"]
+        assert kvbmctl(["--hub", hub.url, "calibrate", "--instance-id", str(handler.instance_id)]) == 0
+        assert "TTFT(us)" in capsys.readouterr().out
         # while a prefill is in flight the worker refuses to calibrate (409 from the hub)
         th = threading.Thread(target=lambda: handler._on_dispatch({"payload": ""}), daemon=True)
         th.start()
