@@ -194,7 +194,12 @@ class ConnectorLeader:
                                                             [self._workers[r][0] for r in sorted(self._workers)]), g3=g3)
         else:
             leader = InstanceLeader.scheduler_side(g2, g3)
-        self._impl = _Leader(leader, self.block_size,
+        objects = None
+        if cfg.object is not None:
+            from .object import make_object_store
+
+            objects = make_object_store(cfg.object)
+        self._impl = _Leader(leader, self.block_size, objects=objects,
                              offload_enabled=layout.get("g2_blocks", 0) > 0, num_workers=max(1, len(self._workers)))
         # operator / peer control plane on the runtime's messenger (describe, reset, metrics)
         import dataclasses

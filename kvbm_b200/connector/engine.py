@@ -35,7 +35,7 @@ import threading
 from dataclasses import dataclass, field
 
 from ..engine.leader import FindMatchesOptions, InstanceLeader
-from ..logical.manager import ImmutableBlock
+from ..logical.manager import ImmutableBlock, Tier
 from ..utils.tracing import audit
 
 
@@ -254,6 +254,19 @@ class LocalConnectorEngine(LeaderEngine):
         self.sessions.remove(session_id)
 
 
+class ObjectHit:
+    """A G4 (object store) match: no block pool holds it, so it has no block id and no reference."""
+
+    tier = Tier.G4
+    block_id = -1
+
+    def __init__(self, seq_hash: int):
+        self.sequence_hash = int(seq_hash)
+
+    def release(self) -> None:
+        pass
+
+
 class WorkerTierEngine(LocalConnectorEngine):
     """``LeaderEngine`` of a connector whose workers live in other processes.
 
@@ -275,13 +288,21 @@ class WorkerTierEngine(LocalConnectorEngine):
       policy and are queued as spill ops (:meth:`take_spill_ops`), the G3
       copies registered when the spill is reported.
 
+    With an object store (``objects``): the match continues past G2 / G3 into
+    G4 (every rank's object present), G4 hits get G2 destinations like G3
+    hits and are fetched by the workers before the onboard (fetch ops);
+    registered G2 blocks the store does not hold yet are uploaded by the
+    workers (store ops), their G2 references held until every worker
+    reported the upload.
+
     Parity: crates/kvbm-engine/src/tiering/engine/{local.rs, find.rs,
     offload.rs} (buffer, flush at finish_forward_pass), tiering/offload/
-    engine.rs:123 (register after the transfer), the G2 -> G3 auto-chain.
+    engine.rs:123 (register after the transfer), the G2 -> G3 auto-chain,
+    the G2 -> G4 chain with its object-presence policy, remote/search/g4.rs.
     """
 
     def __init__(self, leader: InstanceLeader, num_workers: int = 1, g2_policy=None, g3_policy=None,
-                 remote_search=None, sessions=None):
+                 remote_search=None, sessions=None, objects=None):
         from ..engine.offload import PresenceFilter
 
         super().__init__(leader, remote_search, sessions)
@@ -294,21 +315,35 @@ class WorkerTierEngine(LocalConnectorEngine):
         self._spill_queue: list[tuple[list[ImmutableBlock], list, list[int]]] = []
         # step -> (G3 mutables awaiting the spill copies, hashes, G2 sources held, worker reports so far)
         self._pending_g3: dict[int, tuple[list, list[int], list[ImmutableBlock], int]] = {}
-        self.stats = {"offloaded_blocks": 0, "staged_from_g3": 0, "spilled_to_g3": 0, "offload_ops": 0}
+        # G4: the store (presence checks here; the workers move the bytes), uploads queued / in flight
+        self.objects = objects
+        self._store_queue: list[tuple[list[ImmutableBlock], list[int]]] = []
+        self._pending_g4: dict[int, tuple[list[ImmutableBlock], list[int], int]] = {}
+        self.stats = {"offloaded_blocks": 0, "staged_from_g3": 0, "spilled_to_g3": 0, "offload_ops": 0,
+                      "staged_from_g4": 0, "stored_to_g4": 0}
+
+    def _in_store(self, seq_hash: int) -> bool:
+        return all(self.objects.has(self.objects.key(seq_hash, rank=r)) for r in range(self.num_workers))
 
     # ------------------------------------------------------------- find
     def match(self, hashes: list[int]) -> list[ImmutableBlock]:
         from ..engine.leader import StagingMode
 
         res = self.leader.find_matches(list(hashes), FindMatchesOptions(staging=StagingMode.PREPARE))
-        return res.g2_blocks + res.g3_held
+        out = res.g2_blocks + res.g3_held
+        if self.objects is not None:
+            for h in list(hashes)[len(out):]:  # the prefix continues in the object store
+                if not self._in_store(h):
+                    break
+                out.append(ObjectHit(h))
+        return out
 
     def prepare_staging(self, blocks: list[ImmutableBlock]):
         """(blocks the onboard can use, staging) - G3 hits get G2 destinations; without room in G2 the
         match stops before G3. ``staging`` is (G3 refs, G2 destinations, hashes) or None."""
         from ..logical.manager import Tier
 
-        g3 = [b for b in blocks if b.tier == Tier.G3]
+        g3 = [b for b in blocks if b.tier != Tier.G2]  # G3 blocks, then G4 hits
         if not g3:
             return blocks, None
         got = self.leader.g2.allocate_blocks_with_evictions(len(g3))
@@ -327,13 +362,15 @@ class WorkerTierEngine(LocalConnectorEngine):
             m.release()
 
     def finish_staging(self, staging) -> None:
-        """The stage ran before the onboard that was reported: the G2 copies hold the data now."""
+        """The stage / fetch ran before the onboard that was reported: the G2 copies hold the data now."""
         g3, dst, hashes = staging
         for b in self.leader.g2.register_mutable(dst, hashes):
             b.release()
         for b in g3:
             b.release()
-        self.stats["staged_from_g3"] += len(dst)
+        n4 = sum(1 for b in g3 if b.tier == Tier.G4)
+        self.stats["staged_from_g3"] += len(dst) - n4
+        self.stats["staged_from_g4"] += n4
 
     # ---------------------------------------------------------- offload
     def offload(self, request_id, hashes, g1_ids):
@@ -392,12 +429,51 @@ class WorkerTierEngine(LocalConnectorEngine):
         self._pending_g3[step] = (dsts, hs, srcs, 0)
         return ops
 
+    def take_store_ops(self, step: int) -> list[tuple[list[int], list[int]]]:
+        """G2 -> G4 uploads for this step's metadata: ``[(g2_ids, hashes)]``."""
+        if not self._store_queue:
+            return []
+        ops, refs, hs = [], [], []
+        for g2_refs, hashes in self._store_queue:
+            ops.append(([b.block_id for b in g2_refs], list(hashes)))
+            refs += g2_refs
+            hs += hashes
+        self._store_queue = []
+        self._pending_g4[step] = (refs, hs, 0)
+        return ops
+
+    def _chain_to_g4(self, imm: list[ImmutableBlock]) -> None:
+        if self.objects is None or not imm:
+            return
+        pending = {h for _, hs, _ in self._pending_g4.values() for h in hs}
+        pending |= {h for _, hs in self._store_queue for h in hs}
+        keep = [b for b in imm if b.sequence_hash not in pending and not self._in_store(b.sequence_hash)]
+        if keep:
+            self._store_queue.append(([b.clone() for b in keep], [b.sequence_hash for b in keep]))
+
+    def _register_stored(self, stored: dict) -> None:
+        for step, n in stored.items():
+            step = int(step)
+            entry = self._pending_g4.get(step)
+            if entry is None:
+                continue
+            refs, hashes, seen = entry
+            seen += int(n)
+            if seen < self.num_workers:
+                self._pending_g4[step] = (refs, hashes, seen)
+                continue
+            del self._pending_g4[step]
+            for b in refs:
+                b.release()
+            self.stats["stored_to_g4"] += len(hashes)
+
     # --------------------------------------------------- worker reports
     def on_worker_report(self, meta: dict | None) -> None:
         if not meta:
             return
         self._register_landed(meta.get("offloaded", {}))
         self._register_spilled(meta.get("spilled", {}))
+        self._register_stored(meta.get("stored", {}))
 
     def _register_landed(self, offloaded: dict) -> None:
         for step, n in offloaded.items():
@@ -413,6 +489,7 @@ class WorkerTierEngine(LocalConnectorEngine):
             del self._pending_g2[step]
             imm = self.leader.g2.register_mutable(blocks, hashes)
             self._chain_to_g3(imm)
+            self._chain_to_g4(imm)
             for b in imm:
                 b.release()  # cached in G2 (inactive, matchable)
 

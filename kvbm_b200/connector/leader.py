@@ -50,7 +50,8 @@ from ..logical.sequence import TokenBlockSequence
 from ..utils.metrics import CacheStatsTracker
 from ..utils.tracing import audit
 from .engine import WorkerTierEngine
-from .protocol import ConnectorMetadata, OffloadOp, OnboardOp, PullOp, PushOp, RecvOp, SpillOp, StageOp
+from .protocol import (ConnectorMetadata, FetchOp, OffloadOp, OnboardOp, PullOp, PushOp, RecvOp, SpillOp, StageOp,
+                       StoreOp)
 
 # kv_transfer_params key a decode instance puts on the requests it sends to a prefill instance
 REMOTE_DECODE_KEY = "kvbm_remote_decode"
@@ -149,7 +150,7 @@ class ConnectorLeader:
                  cd: ConditionalDisagg | None = None, plane=None, prefill_target=None, instance_id: int = 0,
                  mailbox_slots: int = 0, recv_timeout_s: float = 120.0, num_workers: int = 1,
                  g2_policy: OffloadPolicy | None = None, g3_policy: OffloadPolicy | None = None,
-                 tp_size: int = 1, directory=None):
+                 tp_size: int = 1, directory=None, objects=None):
         self.leader = leader
         self.remote = remote_search  # engine.remote_search.RemoteSearch, or None
         self.block_size = block_size
@@ -170,7 +171,9 @@ class ConnectorLeader:
         self.tp_size = tp_size          # this instance's TP degree (decode side: its ranks' head shards)
         self.directory = directory      # where prefill instances publish their TP degree
         # the tier engine behind the LeaderEngine seam: G2/G3 state driven by the workers' reports
-        self.engine = WorkerTierEngine(leader, num_workers=num_workers, g2_policy=g2_policy, g3_policy=g3_policy)
+        self.engine = WorkerTierEngine(leader, num_workers=num_workers, g2_policy=g2_policy, g3_policy=g3_policy,
+                                       objects=objects)
+        self._fetch_ops: list[FetchOp] = []
         # remote-search pulls the workers run (queued from the remote-search thread, emitted per step)
         self._pull_ops: list[PullOp] = []
         self._pulls: dict[int, list] = {}   # pull id -> [done event, workers reported]
@@ -328,9 +331,16 @@ class ConnectorLeader:
                 m.release()
             slot.staging = (g3[:k], dst[:k], hashes[:k]) if k else None
             if k:
-                self._stage_ops.append(StageOp(req_id, [b.block_id for b in g3[:k]], [m.block_id for m in dst[:k]]))
+                # G3 continuations are staged, G4 continuations fetched, into their G2 destinations
+                from_disk = [(b, m) for b, m in zip(g3[:k], dst[:k]) if b.tier == Tier.G3]
+                from_store = [(b, m) for b, m in zip(g3[:k], dst[:k]) if b.tier == Tier.G4]
+                if from_disk:
+                    self._stage_ops.append(StageOp(req_id, [b.block_id for b, _ in from_disk],
+                                                   [m.block_id for _, m in from_disk]))
+                if from_store:
+                    self._fetch_ops.append(FetchOp(req_id, [b.sequence_hash for b, _ in from_store],
+                                                   [m.block_id for _, m in from_store]))
                 src_ids += [m.block_id for m in dst[:k]]
-                pass
             take = [b for b in take if b.tier == Tier.G2]
         if n:
             self._onboard_ops.append(OnboardOp(req_id, src_ids, g1))
@@ -400,9 +410,10 @@ class ConnectorLeader:
         with self._lock:
             pulls, self._pull_ops = self._pull_ops, []
         meta = ConnectorMetadata(step=out.step or self.iteration, onboard=self._onboard_ops, recv=self._recv_ops,
-                                 stage=self._stage_ops, pull=pulls)
-        self._onboard_ops, self._recv_ops, self._stage_ops = [], [], []
+                                 stage=self._stage_ops, pull=pulls, fetch=self._fetch_ops)
+        self._onboard_ops, self._recv_ops, self._stage_ops, self._fetch_ops = [], [], [], []
         meta.spill = [SpillOp(g2, g3) for g2, g3 in self.engine.take_spill_ops(meta.step)]
+        meta.store = [StoreOp(g2, hs) for g2, hs in self.engine.take_store_ops(meta.step)]
         for req_id in out.preempted_req_ids:
             # The workers fence in-flight offloads of these requests before their G1 blocks are
             # reused (evict list). The request resumes from its token sequence with new G1 blocks;

@@ -10,6 +10,8 @@ One msgpack map per scheduler step::
      "push":    [[req_id, peer, src, dst, slot, seq, final, peer_tp], ...],
      "recv":    [[req_id, slot, seq, g1_ids, timeout_s, contributors], ...],
      "pull":    [[pull_id, pools, src_ids, g2_ids], ...],
+     "fetch":   [[req_id, hashes, g2_ids], ...],          # G4 -> G2 before the onboards
+     "store":   [[g2_ids, hashes], ...],                  # G2 -> G4 (uploads, reported per step)
      "evict":   [req_id, ...]}
 
 ``push`` / ``recv`` carry conditional disaggregation: a prefill worker
@@ -95,6 +97,24 @@ class RecvOp:
 
 
 @dataclass
+class FetchOp:
+    """G4 -> G2: read the objects of ``hashes`` (this worker's rank keys) into ``g2_ids`` before the
+    onboards of the same step."""
+
+    req_id: str
+    hashes: list[int]
+    g2_ids: list[int]
+
+
+@dataclass
+class StoreOp:
+    """G2 -> G4: upload registered G2 blocks ``g2_ids`` under ``hashes`` (this worker's rank keys)."""
+
+    g2_ids: list[int]
+    hashes: list[int]
+
+
+@dataclass
 class PullOp:
     """Remote search: copy another instance's G2 blocks ``src_ids`` into this instance's ``g2_ids``."""
 
@@ -115,6 +135,8 @@ class ConnectorMetadata:
     push: list[PushOp] = field(default_factory=list)
     recv: list[RecvOp] = field(default_factory=list)
     pull: list[PullOp] = field(default_factory=list)
+    fetch: list[FetchOp] = field(default_factory=list)
+    store: list[StoreOp] = field(default_factory=list)
 
     def encode(self) -> bytes:
         return msgpack.packb({
@@ -128,6 +150,9 @@ class ConnectorMetadata:
                      for o in self.push],
             "recv": [[o.req_id, o.slot, o.seq, o.g1_ids, o.timeout_s, o.contributors] for o in self.recv],
             "pull": [[o.pull_id, o.pools, o.src_ids, o.g2_ids] for o in self.pull],
+            # hashes are 192-bit: sent as decimal strings
+            "fetch": [[o.req_id, [str(h) for h in o.hashes], o.g2_ids] for o in self.fetch],
+            "store": [[o.g2_ids, [str(h) for h in o.hashes]] for o in self.store],
         }, use_bin_type=True)
 
     @classmethod
@@ -137,8 +162,10 @@ class ConnectorMetadata:
                    offload=[OffloadOp(*o) for o in d["offload"]], evict=list(d.get("evict", [])),
                    stage=[StageOp(*o) for o in d.get("stage", [])], spill=[SpillOp(*o) for o in d.get("spill", [])],
                    push=[PushOp(*o) for o in d.get("push", [])], recv=[RecvOp(*o) for o in d.get("recv", [])],
-                   pull=[PullOp(*o) for o in d.get("pull", [])])
+                   pull=[PullOp(*o) for o in d.get("pull", [])],
+                   fetch=[FetchOp(r, [int(h) for h in hs], g) for r, hs, g in d.get("fetch", [])],
+                   store=[StoreOp(g, [int(h) for h in hs]) for g, hs in d.get("store", [])])
 
     def empty(self) -> bool:
         return not (self.onboard or self.offload or self.evict or self.stage or self.spill or self.push or self.recv
-                    or self.pull)
+                    or self.pull or self.fetch or self.store)

@@ -134,6 +134,15 @@ def disagg_worker_enable(worker, cfg, tp_rank: int, tp_size: int) -> bool:
     return True
 
 
+def _object_store(cfg):
+    """The G4 store the scheduler checks presence in (the workers open their own), or None."""
+    if cfg.object is None:
+        return None
+    from ..object import make_object_store
+
+    return make_object_store(cfg.object)
+
+
 def instance_id_for(cfg, vllm_config) -> int:
     """This engine's instance id, the same in its scheduler and its workers: ``disagg.instance_id``
     when set, else derived from vLLM's per-engine ``engine_id``."""
@@ -290,7 +299,7 @@ def _define():
                                                decode_offload=os.getenv("KVBM_DECODE_OFFLOAD", "false") == "true",
                                                num_workers=max(1, int(self.info.get("tensor_parallel_size", 1))),
                                                tp_size=max(1, int(self.info.get("tensor_parallel_size", 1))),
-                                               **disagg_leader_kwargs(cfg))
+                                               objects=_object_store(cfg), **disagg_leader_kwargs(cfg))
                 self._remote = None
                 if searching:
                     self._remote = RemoteSearchPlane(cfg, self._leader, iid,

@@ -137,6 +137,9 @@ class ConnectorWorker:
         self._offload_steps: list[tuple[int, torch.cuda.Event]] = []
         self._pulls_done: list[int] = []  # remote-search pulls copied into G2, reported once
         self._pulls_failed: list[int] = []
+        self.objects = None           # engine.object_tier.ObjectTier over this worker's G2 pool (G4 configured)
+        self._store_pool = None
+        self._stores: list = []       # (step, future) of G2 -> G4 uploads
         self._spill_steps: list[int] = []
         # conditional disaggregation
         self.layer_batch = max(1, int(self.config.transfer.layer_batch))
@@ -191,6 +194,30 @@ class ConnectorWorker:
         self._build_worker()
         return self.g1
 
+    # ------------------------------------------------------------------ G4
+    def _fetch(self, op, meta) -> None:
+        """Read G4 objects into G2 before the onboard; a missing object makes the blocks it would
+        have filled load errors (the framework recomputes them)."""
+        if self.objects is None:
+            raise RuntimeError("a G4 fetch reached a worker without an object store configured")
+        ok = self.objects.get_into(list(op.hashes), list(op.g2_ids))
+        bad = {g for g, good in zip(op.g2_ids, ok) if not good}
+        if bad:
+            for on in meta.onboard:
+                if on.req_id == op.req_id:
+                    self._load_errors.update(g1 for g2, g1 in zip(on.g2_ids, on.g1_ids) if g2 in bad)
+
+    def _queue_stores(self, meta) -> None:
+        """Upload registered G2 blocks to G4 off the forward path; reported with the step."""
+        if self.objects is None:
+            raise RuntimeError("a G4 store reached a worker without an object store configured")
+        import concurrent.futures as cf
+
+        if self._store_pool is None:
+            self._store_pool = cf.ThreadPoolExecutor(max_workers=1, thread_name_prefix="kvbm-g4-store")
+        ops = [(list(o.hashes), list(o.g2_ids)) for o in meta.store]
+        self._stores.append((meta.step, self._store_pool.submit(lambda: [self.objects.put(h, g) for h, g in ops])))
+
     def publish_g2(self, directory, instance_id: int) -> dict:
         """Publish this worker's G2 pool (a shared-memory file) so another instance on the node can
         pull matched blocks from it (remote search); returns the export."""
@@ -221,6 +248,15 @@ class ConnectorWorker:
         caps = TransferCapabilities(allow_gds=c.transfer.allow_gds, allow_gpu_rdma=c.transfer.allow_gpu_rdma,
                                     cuda_graph_replay=c.transfer.cuda_graph_replay,
                                     startup_benchmark=c.transfer.startup_benchmark)
+        self._make_worker(c, g2, g3, path, caps)
+        if c.object is not None and g2:
+            from ..engine.object_tier import ObjectTier
+            from ..object import make_object_store
+
+            self.objects = ObjectTier(make_object_store(c.object), [self.worker.g2_layout], lock=c.object.lock,
+                                      rank_base=self.rank)
+
+    def _make_worker(self, c, g2, g3, path, caps) -> None:
         self.worker = Worker(self.rank, self.g1, g2_blocks=g2, g3_blocks=g3, g3_path=path, device=self.device,
                              capabilities=caps, engine=c.transfer.engine, disk_direct=c.cache.disk.use_direct_io,
                              g2_numa_node=c.cache.host.numa_node, g2_hugepages=bool(c.cache.host.hugepages),
@@ -369,7 +405,9 @@ class ConnectorWorker:
         now = time.monotonic()
         for op in (meta.recv if meta is not None else ()):
             self._recvs[op.req_id] = (op, now + op.timeout_s)
-        if meta is None or not (meta.onboard or meta.stage):
+        if meta is not None and meta.store:
+            self._queue_stores(meta)
+        if meta is None or not (meta.onboard or meta.stage or meta.fetch):
             self._layer_events = []
             return
         h2d, _ = self._streams()
@@ -380,6 +418,8 @@ class ConnectorWorker:
         for op in meta.stage:  # G3 -> G2 ahead of the onboards that read them
             w.tm.execute_transfer(w.handles.g3, op.g3_ids, w.handles.g2, op.g2_ids,
                                   TransferOptions(stream=h2d, engine=w.engine)).wait()
+        for op in meta.fetch:  # G4 -> G2 ahead of the onboards that read them
+            self._fetch(op, meta)
         self._layer_events = []
         if not meta.onboard:
             return
@@ -551,6 +591,13 @@ class ConnectorWorker:
         if self._pulls_failed:
             out["pull_failed"] = {p: 1 for p in self._pulls_failed}
             self._pulls_failed = []
+        stored = {}
+        while self._stores and self._stores[0][1].done():
+            step, fut = self._stores.pop(0)
+            fut.result()  # an upload error surfaces here
+            stored[step] = 1
+        if stored:
+            out["stored"] = stored
         return out or None
 
     def get_block_ids_with_load_errors(self) -> set[int]:
@@ -571,5 +618,7 @@ class ConnectorWorker:
             _LOCAL_SHARDS.pop((self.instance_id, self.tp_rank), None)
             self.mailbox.close()
             self.mailbox = None
+        if self._store_pool is not None:
+            self._store_pool.shutdown(wait=True)
         if self.worker is not None:
             self.worker.close()

@@ -41,13 +41,16 @@ def _host_ptr(layout: KvLayout, block_id: int) -> int:
 
 
 class ObjectTier:
-    def __init__(self, store, g2_layouts: list[KvLayout], lock: bool = False):
-        self.store, self.layouts, self.lock = store, list(g2_layouts), lock
+    """``g2_layouts``: the G2 pools of consecutive worker ranks starting at ``rank_base`` (a
+    connector worker process holds one pool: its own rank's)."""
+
+    def __init__(self, store, g2_layouts: list[KvLayout], lock: bool = False, rank_base: int = 0):
+        self.store, self.layouts, self.lock, self.rank_base = store, list(g2_layouts), lock, int(rank_base)
         self.nbytes = self.layouts[0].config.bytes_per_block
         self.stats = {"put_blocks": 0, "skipped_locked": 0, "staged_blocks": 0, "get_misses": 0}
 
     def keys(self, seq_hash: int) -> list[str]:
-        return [self.store.key(seq_hash, rank=r) for r in range(len(self.layouts))]
+        return [self.store.key(seq_hash, rank=self.rank_base + r) for r in range(len(self.layouts))]
 
     def contains(self, seq_hash: int) -> bool:
         return all(self.store.has(k) for k in self.keys(seq_hash))
@@ -62,7 +65,7 @@ class ObjectTier:
             todo.append((h, b))
         futs = []
         for r, lay in enumerate(self.layouts):
-            keys = [self.store.key(h, rank=r) for h, _ in todo]
+            keys = [self.store.key(h, rank=self.rank_base + r) for h, _ in todo]
             futs += self.store.put_blocks(keys, [_host_ptr(lay, b) for _, b in todo], self.nbytes)
         for f in futs:
             f.result()
@@ -79,6 +82,18 @@ class ObjectTier:
         return run
 
     # ------------------------------------------------------------ G4 -> G2
+    def get_into(self, hashes: list[int], g2_block_ids: list[int]) -> list[bool]:
+        """Read the blocks of ``hashes`` into G2 blocks ``g2_block_ids`` (this tier's ranks); per
+        block, whether every rank's object was there."""
+        ok = [True] * len(hashes)
+        for r, lay in enumerate(self.layouts):
+            keys = [self.store.key(h, rank=self.rank_base + r) for h in hashes]
+            res = self.store.get_blocks(keys, [_host_ptr(lay, b) for b in g2_block_ids], self.nbytes)
+            ok = [a and b for a, b in zip(ok, res)]
+        self.stats["get_misses"] += ok.count(False)
+        self.stats["staged_blocks"] += ok.count(True)
+        return ok
+
     def stage(self, hashes: list[int], g2: BlockManager) -> list[ImmutableBlock]:
         n = 0
         for h in hashes:  # longest prefix every rank holds
@@ -93,7 +108,7 @@ class ObjectTier:
         blocks, _ = got
         ok = [True] * n
         for r, lay in enumerate(self.layouts):
-            keys = [self.store.key(h, rank=r) for h in hashes[:n]]
+            keys = [self.store.key(h, rank=self.rank_base + r) for h in hashes[:n]]
             res = self.store.get_blocks(keys, [_host_ptr(lay, b.block_id) for b in blocks], self.nbytes)
             ok = [a and b for a, b in zip(ok, res)]
         good = 0
