@@ -44,7 +44,14 @@ async function refresh() {
     get("/v1/instances").then(d => fillTable("instances", d.instances, ["instance_id", "role", "features", "address"])),
     get("/v1/indexer/config").then(c => fillDl("indexer", c)),
     get("/v1/prefill-router/targets").then(t => fillTable("targets", t.targets, ["instance_id", "inflight", "tier"])),
-    get("/v1/prefill-router/counters").then(c => fillDl("router", c)),
+    get("/v1/prefill-router/counters").then(c => {
+      const { calibration, ...rest } = c;
+      fillDl("router", rest);
+      const fmt = v => (v || []).map(x => x.toPrecision(4)).join(", ");
+      fillTable("calibration", Object.entries(calibration || {}).map(([iid, m]) => ({
+        iid, ts: m.ttft_samples, tc: fmt(m.ttft_coeffs), is: m.itl_samples, ic: fmt(m.itl_coeffs),
+      })), ["iid", "ts", "tc", "is", "ic"]);
+    }),
   ];
   await Promise.allSettled(jobs);
 }

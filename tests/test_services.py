@@ -322,4 +322,9 @@ def test_hub_serves_its_web_ui(hub):
     assert '<script src="/app.js">' in page.text
     js = requests.get(hub.url + "/app.js", timeout=5)
     assert js.status_code == 200 and "/v1/instances" in js.text and "javascript" in js.headers["content-type"]
+    # every element id the script fills exists on the page
+    import re
+
+    for el in set(re.findall(r'fill(?:Dl|Table)\("([a-z_]+)"', js.text)):
+        assert f'id="{el}"' in page.text, el
     assert requests.get(hub.url + "/style.css", timeout=5).headers["content-type"].startswith("text/css")
