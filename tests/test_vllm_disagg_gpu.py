@@ -57,7 +57,7 @@ def _engine(model_dir, disagg):
     ktc = KVTransferConfig(kv_connector="KvbmConnector", kv_connector_module_path="kvbm_b200.connector.vllm_connector",
                            kv_role="kv_both", kv_connector_extra_config={"disagg": disagg})
     return LLM(model=model_dir, load_format="dummy", skip_tokenizer_init=True, enforce_eager=True,
-               gpu_memory_utilization=0.25, max_model_len=1024, block_size=16, dtype="bfloat16",
+               gpu_memory_utilization=0.15, max_model_len=1024, block_size=16, dtype="bfloat16",
                enable_prefix_caching=False, kv_transfer_config=ktc, seed=0)
 
 
@@ -150,6 +150,10 @@ def test_vllm_engines_disaggregated_through_the_connector(tmp_path):
     pytest.importorskip("vllm")
     if not torch.cuda.is_available():
         pytest.skip("needs a GPU")
+    import gc
+
+    gc.collect()
+    torch.cuda.empty_cache()  # earlier tests in this process must not hold the memory the engines ask for
     model_dir = _tiny_llama_dir(str(tmp_path / "tiny-llama"))
     root = str(tmp_path / "plane")
     os.makedirs(root)
