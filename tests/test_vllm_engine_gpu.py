@@ -46,6 +46,10 @@ def test_vllm_engine_outputs_identical_after_prefix_cache_reset(tmp_path, monkey
     from vllm.config import KVTransferConfig
     from vllm.inputs import TokensPrompt
 
+    import gc
+
+    gc.collect()
+    torch.cuda.empty_cache()  # vLLM sizes its cache from the memory free now
     model_dir = _tiny_llama_dir(str(tmp_path / "tiny-llama"))
     ktc = KVTransferConfig(kv_connector="KvbmConnector", kv_connector_module_path="kvbm_b200.connector.vllm_connector",
                            kv_role="kv_both",
