@@ -4,9 +4,10 @@ the prefill-router attach.
 Takes exactly the arguments of ``python -m vllm.entrypoints.openai.api_server``.
 Before the server starts serving, the engine is handed to
 :func:`kvbm_b200.hub.detect.try_wrap_engine`: when its connector
-configuration names a hub and the ``prefill`` role, the process registers
-with that hub's prefill router and serves routed prefills; otherwise it is
-plain vLLM. The handler is kept alive for the life of the server.
+configuration names the ``prefill`` role, the process registers with the
+hub's prefill router (``hub.url`` set) or serves the node's prefill plane
+under its ``disagg.instance_id`` (no hub); otherwise it is plain vLLM. The
+handler is kept alive for the life of the server.
 """
 
 from __future__ import annotations

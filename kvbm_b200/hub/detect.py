@@ -10,8 +10,9 @@ limits can be read) whose dispatch lambda turns every routed
 request into an ``engine.generate`` call (the prompt's token ids, one output
 token, ``kv_transfer_params`` naming the decode instance that waits for the
 KV) on the engine's event loop, and completes the router's call when that
-generation ends. Decode or aggregated engines, and engines with no hub, get
-``None``.
+generation ends. Without a hub, a prefill-role engine with a disaggregation
+instance id is served from the node's prefill plane instead
+(:class:`PlaneServer`). Decode or aggregated engines get ``None``.
 
 Parity: python/kvbm/hub/detect.py (try_wrap_engine), the dispatch lambda of
 python/kvbm/hub/dispatch_lambda.py, src/hub/prefill_router.rs:133-245.
@@ -84,11 +85,72 @@ def make_dispatch_lambda(engine: Any, loop: asyncio.AbstractEventLoop, max_token
     return dispatch
 
 
+class PlaneServer:
+    """Serves a prefill engine from the node's prefill plane when there is no hub: a thread takes
+    the dispatches addressed to ``instance_id`` (up to ``max_concurrency`` in flight) and hands each
+    to ``dispatch`` (the same lambda the hub's router would call)."""
+
+    def __init__(self, plane, instance_id: int, dispatch, max_concurrency: int = 4, poll_s: float = 0.2):
+        import threading
+
+        from ..engine.cd_plane import encode_dispatch
+
+        self.plane, self.instance_id, self.dispatch = plane, int(instance_id), dispatch
+        self.max_concurrency, self.poll_s = max_concurrency, poll_s
+        self._encode = encode_dispatch
+        self._inflight: list[CompletionEvent] = []
+        self.served = 0
+        self.failed = 0
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True, name="kvbm-plane-server")
+        self._t.start()
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            done = [e for e in self._inflight if e.is_set()]
+            self.failed += sum(1 for e in done if e.error is not None)
+            self._inflight = [e for e in self._inflight if not e.is_set()]
+            room = self.max_concurrency - len(self._inflight)
+            if room <= 0:
+                self._stop.wait(0.002)
+                continue
+            for d in self.plane.wait(self.instance_id, self.poll_s, limit=room):
+                raw = self._encode(d["request_id"], d["tokens"], d["params"], d["decode"], salt=d.get("salt"),
+                                   lora=d.get("lora"))
+                ev = CompletionEvent()
+                self._inflight.append(ev)
+                self.served += 1
+                try:
+                    self.dispatch({"payload": raw.hex()}, ev)
+                except Exception as e:  # noqa: BLE001 - one bad dispatch does not stop the server
+                    ev.fail(f"{type(e).__name__}: {e}")
+
+    def close(self) -> None:
+        self._stop.set()
+        self._t.join(timeout=2)
+
+
 def try_wrap_engine(vllm_config: Any, engine: Any, loop: asyncio.AbstractEventLoop | None = None,
-                    max_concurrency: int = 4, make_params=None) -> PrefillRouterHandler | None:
+                    max_concurrency: int = 4, make_params=None) -> PrefillRouterHandler | PlaneServer | None:
     hub_url, role = connector_settings(vllm_config)
-    if not hub_url or role != "prefill":
+    if role != "prefill":
         return None
+    if not hub_url:
+        # no hub: serve the node's prefill plane under this engine's disaggregation instance id
+        from ..engine.cd_plane import open_cd_services
+        from ..utils.config import KvbmConfig
+
+        ktc = getattr(vllm_config, "kv_transfer_config", None)
+        cfg = KvbmConfig.for_leader(dict(getattr(ktc, "kv_connector_extra_config", None) or {}), env={},
+                                    system_toml=None)
+        if cfg.disagg is None or cfg.disagg.instance_id is None:
+            return None
+        loop = loop or asyncio.get_running_loop()
+        plane, _ = open_cd_services(cfg.disagg.directory)
+        server = PlaneServer(plane, cfg.disagg.instance_id, make_dispatch_lambda(engine, loop, make_params=make_params),
+                             max_concurrency=max_concurrency)
+        log.info("prefill plane attached (instance %s, %s)", cfg.disagg.instance_id, cfg.disagg.directory)
+        return server
     loop = loop or asyncio.get_running_loop()
     # the calibrate handler is best effort: an engine whose limits cannot be read still serves prefills
     cal_lambda = cal_defaults = None

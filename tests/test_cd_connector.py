@@ -305,3 +305,52 @@ def test_file_plane_serves_each_dispatch_once_across_pollers(tmp_path):
     d.withdraw(5, rank=1)
     with pytest.raises(TimeoutError):
         d.lookup(5, timeout_s=0.05, rank=1)
+
+
+def test_prefill_engine_served_from_the_file_plane_without_a_hub(tmp_path):
+    """A prefill-role engine with a disaggregation instance id and no hub: try_wrap_engine serves
+    the node's file plane, so a decode leader's dispatch becomes that engine's generate call
+    carrying the decode instance in its kv_transfer_params."""
+    import asyncio
+    import time
+    from types import SimpleNamespace
+
+    from kvbm_b200.engine.cd_plane import FilePrefillPlane
+    from kvbm_b200.hub.detect import PlaneServer, try_wrap_engine
+
+    calls = []
+
+    class FakeAsyncEngine:
+        async def generate(self, prompt, params, request_id):
+            calls.append((request_id, prompt["prompt_token_ids"], params))
+            await asyncio.sleep(0.01)
+            yield SimpleNamespace(finished=True)
+
+    def cfg(disagg):
+        return SimpleNamespace(kv_transfer_config=SimpleNamespace(kv_connector_extra_config={"disagg": disagg}))
+
+    loop = asyncio.new_event_loop()
+    t = threading.Thread(target=loop.run_forever, daemon=True)
+    t.start()
+    url = f"file://{tmp_path}"
+    server = None
+    try:
+        assert try_wrap_engine(cfg({"role": "prefill", "directory": url}), FakeAsyncEngine(), loop) is None  # no id
+        server = try_wrap_engine(cfg({"role": "prefill", "instance_id": 7, "directory": url}), FakeAsyncEngine(),
+                                 loop, make_params=lambda n, p: {"max_tokens": n, "kv_transfer_params": p})
+        assert isinstance(server, PlaneServer)
+        L = decode_leader(FilePrefillPlane(str(tmp_path)))
+        L.create_slot(KvbmRequest("file-routed", list(range(40))))
+        assert L.get_num_new_matched_tokens("file-routed", 0) == (40, True)
+        L.update_state_after_alloc("file-routed", [4, 5, 6], 40)
+        deadline = time.monotonic() + 10
+        while not calls and time.monotonic() < deadline:
+            time.sleep(0.01)
+        [(rid, toks, params)] = calls
+        assert rid == "file-routed" and toks == list(range(40)) and params["max_tokens"] == 1
+        assert params["kv_transfer_params"][REMOTE_DECODE_KEY]["dst_ids"] == [4, 5, 6]
+        assert server.served == 1
+    finally:
+        if server is not None:
+            server.close()
+        loop.call_soon_threadsafe(loop.stop)
