@@ -34,7 +34,7 @@ def install_hook() -> None:
                 handler = try_wrap_engine(cfg, engine_client)
                 if handler is not None:
                     _HANDLERS.append(handler)
-                    print(f"kvbm prefill router attached (instance {handler.instance_id})", flush=True)
+                    print(f"kvbm prefill server attached (instance {handler.instance_id})", flush=True)
             except Exception as e:  # noqa: BLE001 - the server still serves as plain vLLM
                 log.warning("prefill-router attach failed: %s", e)
         return await original(engine_client, listen_address, sock, args, **kwargs)
