@@ -487,6 +487,9 @@ class WorkerTierEngine(LocalConnectorEngine):
                 self._pending_g2[step] = (blocks, hashes, seen)
                 continue
             del self._pending_g2[step]
+            if self.leader.g3 is None and self.objects is None:
+                self.leader.g2.register_mutable_released(blocks, hashes)  # cached in G2 (inactive, matchable)
+                continue
             imm = self.leader.g2.register_mutable(blocks, hashes)
             self._chain_to_g3(imm)
             self._chain_to_g4(imm)

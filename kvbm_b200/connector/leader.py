@@ -210,7 +210,7 @@ class ConnectorLeader:
         for b in slot.matched:
             b.release()
         slot.matched = []
-        hashes = slot.seq.sequence_hashes
+        hashes = slot.seq.hashes_view()
         start = num_computed_tokens // self.block_size
         if num_computed_tokens % self.block_size or start > len(hashes):
             return 0, False
@@ -438,8 +438,8 @@ class ConnectorLeader:
                 slot.g1.extend_block_ids(new_blocks)
             slot.num_computed_tokens = num_computed
             # computed complete blocks take their sequence hashes (assigned, in position order)
-            hashes = slot.seq.sequence_hashes
-            slot.g1.assign_pending(hashes[: num_computed // self.block_size])
+            hashes = slot.seq.hashes_view()
+            slot.g1.assign_pending(hashes, num_computed // self.block_size)
             if slot.push is not None:
                 self._advance_push(slot, num_computed, meta)
             if not self.offload_enabled:

@@ -119,6 +119,23 @@ class BlockStore:
         self._ids.discard(bid)
         return bid, v
 
+    def extend_unassigned(self, bids: Sequence[int]) -> None:
+        self._ids.update(bids)
+        self.unassigned.extend((b, None) for b in bids)
+
+    def stage_front(self, values: Sequence[Any]) -> None:
+        """Move the first ``len(values)`` unassigned ids to staged, pairing them with ``values``
+        (the ids stay in the store, so membership does not change)."""
+        pop, push = self.unassigned.popleft, self.staged.append
+        for v in values:
+            push((pop()[0], v))
+
+    def commit_all_staged(self) -> int:
+        n = len(self.staged)
+        self.assigned.extend(self.staged)
+        self.staged.clear()
+        return n
+
     def all_block_ids(self) -> list[int]:
         return [b for b, _ in self.assigned] + [b for b, _ in self.staged] + [b for b, _ in self.unassigned]
 
@@ -219,21 +236,21 @@ class ExternalBlockAssignments:
     def extend_block_ids(self, block_ids: Iterable[int]) -> None:
         """``block_ids`` is the full ordered list allocated to this set: ids already known must form a
         prefix (they are skipped), the rest are queued as unassigned."""
-        new, new_set, first_new = [], set(), None
-        for i, bid in enumerate(block_ids):
-            bid = int(bid)
-            if self._s.contains(bid):
-                if first_new is not None:
-                    raise OrderingViolation(bid, new[0], i, first_new)
-                continue
-            if bid in new_set:
-                raise DuplicateBlockId(bid)
-            new_set.add(bid)
-            if first_new is None:
-                first_new = i
-            new.append(bid)
-        for bid in new:
-            self._s.insert_unassigned(bid)
+        ids = [int(b) for b in block_ids]
+        known = self._s._ids
+        k = 0
+        while k < len(ids) and ids[k] in known:  # the known prefix is skipped
+            k += 1
+        new = ids[k:]
+        if new and (known.intersection(new) or len(set(new)) != len(new)):
+            seen = set()
+            for i, bid in enumerate(new, start=k):
+                if bid in known:
+                    raise OrderingViolation(bid, new[0], i, k)
+                if bid in seen:
+                    raise DuplicateBlockId(bid)
+                seen.add(bid)
+        self._s.extend_unassigned(new)
         self._order.extend(new)
 
     def extend_assigned(self, items: Iterable[tuple[int, int]]) -> int:
@@ -250,30 +267,29 @@ class ExternalBlockAssignments:
             self._order.extend(b for b, _ in items)
         return len(items)
 
-    def stage_pending(self, sequence_hashes: Sequence[int]) -> range:
-        """Pair unassigned ids with ``sequence_hashes[next_position():]`` (hash i of the whole
+    def stage_pending(self, sequence_hashes: Sequence[int], limit: int | None = None) -> range:
+        """Pair unassigned ids with ``sequence_hashes[next_position():limit]`` (hash i of the whole
         sequence at index i); returns the range of new staged indices."""
-        start_idx = len(self._s.staged)
-        start = self.next_position()
-        n = min(max(0, len(sequence_hashes) - start), len(self._s.unassigned))
-        for i in range(n):
-            p = hash_position(int(sequence_hashes[start + i]))
-            if p != start + i:
-                raise PositionMismatch(start + i, p, self._s.unassigned[i][0])
-        for i in range(n):
-            bid, _ = self._s.shift_unassigned()
-            self._s.insert_staged(bid, int(sequence_hashes[start + i]))
+        st = self._s
+        start_idx = len(st.staged)
+        start = self.offset + len(st.assigned) + start_idx
+        end = len(sequence_hashes) if limit is None else min(int(limit), len(sequence_hashes))
+        if end <= start or not st.unassigned:  # the per-step common case: nothing new to pair
+            return range(start_idx, start_idx)
+        n = min(end - start, len(st.unassigned))
+        vals = [int(h) for h in sequence_hashes[start: start + n]]
+        for i, h in enumerate(vals):
+            if (h >> 128) != start + i:  # a sequence hash carries its block position in its top bits
+                raise PositionMismatch(start + i, hash_position(h), st.unassigned[i][0])
+        st.stage_front(vals)
         return range(start_idx, start_idx + n)
 
     def commit_staged(self) -> range:
         start = len(self._s.assigned)
-        while self._s.staged:
-            bid, h = self._s.shift_staged()
-            self._s.insert_assigned(bid, h)
-        return range(start, len(self._s.assigned))
+        return range(start, start + self._s.commit_all_staged())
 
-    def assign_pending(self, sequence_hashes: Sequence[int]) -> range:
-        self.stage_pending(sequence_hashes)
+    def assign_pending(self, sequence_hashes: Sequence[int], limit: int | None = None) -> range:
+        self.stage_pending(sequence_hashes, limit)
         return self.commit_staged()
 
 

@@ -218,6 +218,15 @@ class BlockManager:
         return [ImmutableBlock(self, bid, h, "duplicate" if kind == 1 else "primary")
                 for (bid, kind), h in zip(res, hashes)]
 
+    def register_mutable_released(self, blocks: Sequence[MutableBlock], hashes: Sequence[int]) -> int:
+        """``register_mutable`` followed by releasing every handle, in two native calls: the
+        blocks become cached (inactive, matchable) without a Python handle per block."""
+        for b in blocks:
+            b._take()
+        res = self._pool.stage_and_register([b.block_id for b in blocks], list(hashes))
+        self._pool.release_many([bid for bid, _ in res])
+        return len(res)
+
     # --------------------------------------------------------------- match
     def match_blocks(self, seq_hashes: Sequence[int]) -> list[ImmutableBlock]:
         """Longest cached prefix of ``seq_hashes`` (stops at the first miss)."""

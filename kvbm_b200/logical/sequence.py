@@ -46,18 +46,27 @@ def sequence_hashes(tokens: Sequence[int] | np.ndarray, block_size: int, salt: s
 
 
 class TokenBlockSequence:
+    """Tokens of one request and the sequence hashes of its complete blocks.
+
+    Tokens live in a buffer that grows by doubling, so appending a decode
+    token costs O(1) and a block's hash is computed once, when its last token
+    arrives (the per-step path of a scheduler with hundreds of sequences)."""
+
     def __init__(self, tokens: Sequence[int] = (), block_size: int = 16, salt: str | int | None = None):
         self.block_size = block_size
         self.salt = salt_hash(salt)
-        self._tokens = np.asarray(tokens, dtype=np.int32)
-        self._hashes: list[int] = core.sequence_hashes(self._tokens, block_size, self.salt, None)
+        t = np.asarray(tokens, dtype=np.int32).ravel()
+        self._buf = np.empty(max(64, 2 * t.size), dtype=np.int32)
+        self._buf[: t.size] = t
+        self._n = int(t.size)
+        self._hashes: list[int] = core.sequence_hashes(t, block_size, self.salt, None)
 
     @property
     def tokens(self) -> np.ndarray:
-        return self._tokens
+        return self._buf[: self._n]
 
     def __len__(self) -> int:
-        return int(self._tokens.size)
+        return self._n
 
     @property
     def num_complete_blocks(self) -> int:
@@ -67,21 +76,44 @@ class TokenBlockSequence:
     def sequence_hashes(self) -> list[int]:
         return list(self._hashes)
 
+    def hashes_view(self) -> list[int]:
+        """The complete blocks' hashes without a copy (callers must not modify the list)."""
+        return self._hashes
+
     @property
     def partial_tokens(self) -> np.ndarray:
-        return self._tokens[len(self._hashes) * self.block_size:]
+        return self._buf[len(self._hashes) * self.block_size: self._n]
+
+    def _reserve(self, n: int) -> None:
+        if n > self._buf.size:
+            buf = np.empty(max(n, 2 * self._buf.size), dtype=np.int32)
+            buf[: self._n] = self._buf[: self._n]
+            self._buf = buf
 
     def append(self, tokens: Sequence[int] | int) -> list[int]:
         """Append tokens; returns the hashes of blocks completed by this call."""
-        add = np.atleast_1d(np.asarray(tokens, dtype=np.int32))
-        self._tokens = np.concatenate([self._tokens, add])
+        if isinstance(tokens, (list, tuple)) and len(tokens) == 1:
+            tokens = tokens[0]  # a decode step's one token
+        if isinstance(tokens, (int, np.integer)):
+            if self._n >= self._buf.size:
+                self._reserve(self._n + 1)
+            self._buf[self._n] = tokens
+            self._n += 1
+            if (self._n - len(self._hashes) * self.block_size) < self.block_size:
+                return []
+        else:
+            add = np.asarray(tokens, dtype=np.int32).ravel()
+            self._reserve(self._n + add.size)
+            self._buf[self._n: self._n + add.size] = add
+            self._n += int(add.size)
         start = len(self._hashes) * self.block_size
-        tail = self._tokens[start:]
+        if self._n - start < self.block_size:
+            return []
         parent_hash = self._hashes[-1] if self._hashes else None
-        new = core.sequence_hashes(tail, self.block_size, self.salt, parent_hash)
+        new = core.sequence_hashes(self._buf[start: self._n], self.block_size, self.salt, parent_hash)
         self._hashes.extend(new)
         return new
 
     def truncate(self, num_tokens: int) -> None:
-        self._tokens = self._tokens[:num_tokens]
-        self._hashes = self._hashes[: num_tokens // self.block_size]
+        self._n = min(self._n, int(num_tokens))
+        self._hashes = self._hashes[: self._n // self.block_size]

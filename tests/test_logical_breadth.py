@@ -189,3 +189,32 @@ def test_logical_assignments_stage_register_and_release():
     last.release()
     la.clear()
     assert la.is_empty() and mgr.active_len() == 0 and mgr.inactive_len() == 2
+
+
+def test_token_sequence_incremental_hashes_match_one_shot():
+    """Appending one token at a time, in chunks, or after a truncation gives the same block hashes
+    as hashing the whole token list at once (the buffer grows by doubling)."""
+    import numpy as np
+
+    from kvbm_b200.logical.sequence import TokenBlockSequence, sequence_hashes
+
+    rng = np.random.default_rng(3)
+    toks = rng.integers(0, 50000, 700).tolist()
+    for salt in (None, "lora-a"):
+        want = sequence_hashes(toks, 16, salt)
+        s = TokenBlockSequence(toks[:5], 16, salt)
+        i = 5
+        while i < len(toks):
+            k = int(rng.integers(1, 40))
+            if k == 1:
+                new = s.append(np.int64(toks[i]))
+            else:
+                new = s.append(toks[i: i + k])
+            i += k
+            assert all(h in want for h in new)
+        assert s.sequence_hashes == want and len(s) == len(toks) and list(s.tokens) == toks
+        assert list(s.partial_tokens) == toks[len(want) * 16:]
+        s.truncate(333)
+        assert s.sequence_hashes == want[: 333 // 16] and len(s) == 333
+        s.append(toks[333:])
+        assert s.sequence_hashes == want

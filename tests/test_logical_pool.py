@@ -322,3 +322,19 @@ def test_pool_micro_benchmark_runs():
     for api in ("native_batch_ns_per_block", "handles_ns_per_block"):
         assert set(out[api]) == {"match_active", "match_inactive", "drop"}
         assert all(v > 0 for v in out[api].values())
+
+
+def test_register_mutable_released_caches_without_handles():
+    from kvbm_b200.logical.manager import BlockManager, Tier
+    from kvbm_b200.logical.sequence import sequence_hashes
+
+    m = BlockManager(8, 16, "lru", Tier.G2)
+    hs = sequence_hashes(list(range(4 * 16)), 16)
+    blocks = m.allocate_blocks(4)
+    assert m.register_mutable_released(blocks, hs) == 4
+    assert m.inactive_len() == 4 and m.count_prefix(hs) == 4
+    got = m.match_blocks(hs)
+    assert [b.sequence_hash for b in got] == hs
+    for b in got:
+        b.release()
+    assert m.allocate_blocks_with_evictions(8) is not None  # four free + four evictable
