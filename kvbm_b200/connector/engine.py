@@ -311,7 +311,7 @@ class WorkerTierEngine(LocalConnectorEngine):
         self.g3_policy = g3_policy or (PresenceFilter(leader.g3) if leader.g3 is not None else None)
         self._buffer: list[tuple[str, list[int], list[int]]] = []
         # step -> (G2 mutables awaiting their copies, their hashes, worker reports so far)
-        self._pending_g2: dict[int, tuple[list, list[int], int]] = {}
+        self._pending_g2: dict[int, tuple[list[int], list[int], int]] = {}  # bare G2 ids owned until registered
         self._spill_queue: list[tuple[list[ImmutableBlock], list, list[int]]] = []
         # step -> (G3 mutables awaiting the spill copies, hashes, G2 sources held, worker reports so far)
         self._pending_g3: dict[int, tuple[list, list[int], list[ImmutableBlock], int]] = {}
@@ -397,12 +397,11 @@ class WorkerTierEngine(LocalConnectorEngine):
                     if h not in pending and self.g2_policy.keep(OffloadItem(h, b)) and not reg.is_present(h, tier)]
             if not todo:
                 continue
-            got = g2.allocate_blocks_with_evictions(len(todo))
-            if got is None:
+            dst = g2.allocate_ids_with_evictions(len(todo))  # bare ids: registered or released below
+            if dst is None:
                 continue  # G2 full of active blocks: skip this offload
-            dst, _ = got
             pending |= {h for h, _ in todo}
-            ops.append((rid, [b for _, b in todo], [d.block_id for d in dst]))
+            ops.append((rid, [b for _, b in todo], dst))
             dsts.extend(dst)
             hashes_all.extend(h for h, _ in todo)
             self.stats["offloaded_blocks"] += len(todo)
@@ -488,9 +487,9 @@ class WorkerTierEngine(LocalConnectorEngine):
                 continue
             del self._pending_g2[step]
             if self.leader.g3 is None and self.objects is None:
-                self.leader.g2.register_mutable_released(blocks, hashes)  # cached in G2 (inactive, matchable)
+                self.leader.g2.register_ids_released(blocks, hashes)  # cached in G2 (inactive, matchable)
                 continue
-            imm = self.leader.g2.register_mutable(blocks, hashes)
+            imm = self.leader.g2.register_ids(blocks, hashes)
             self._chain_to_g3(imm)
             self._chain_to_g4(imm)
             for b in imm:

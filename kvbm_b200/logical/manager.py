@@ -218,6 +218,29 @@ class BlockManager:
         return [ImmutableBlock(self, bid, h, "duplicate" if kind == 1 else "primary")
                 for (bid, kind), h in zip(res, hashes)]
 
+    def allocate_ids_with_evictions(self, count: int) -> list[int] | None:
+        """Like ``allocate_blocks_with_evictions`` but returns bare ids, without a handle per block:
+        the caller owns them and must hand every id back through ``register_ids`` /
+        ``register_ids_released`` or ``release_ids`` (bulk paths of a scheduler)."""
+        got = self._pool.allocate(count)
+        return None if got is None else list(got[0])
+
+    def release_ids(self, ids: Sequence[int]) -> None:
+        """Return allocated, never-registered ids to the reset pool."""
+        self._pool.release_mutable_many([int(i) for i in ids])
+
+    def register_ids(self, ids: Sequence[int], hashes: Sequence[int]) -> list[ImmutableBlock]:
+        """Register bare allocated ids under ``hashes``; one handle per registered block."""
+        res = self._pool.stage_and_register([int(i) for i in ids], list(hashes))
+        return [ImmutableBlock(self, bid, h, "duplicate" if kind == 1 else "primary")
+                for (bid, kind), h in zip(res, hashes)]
+
+    def register_ids_released(self, ids: Sequence[int], hashes: Sequence[int]) -> int:
+        """Register bare allocated ids and release them at once: cached (inactive, matchable)."""
+        res = self._pool.stage_and_register([int(i) for i in ids], list(hashes))
+        self._pool.release_many([bid for bid, _ in res])
+        return len(res)
+
     def register_mutable_released(self, blocks: Sequence[MutableBlock], hashes: Sequence[int]) -> int:
         """``register_mutable`` followed by releasing every handle, in two native calls: the
         blocks become cached (inactive, matchable) without a Python handle per block."""
