@@ -151,8 +151,8 @@ def run(args) -> list[dict]:
             back = KvLayout.allocate(cfg, "fully_contiguous", nhd)
             for engine in [e for e in CAST_ENGINES if e in args.engines.split(",")]:
                 kv_ops.set_cast_pipeline(engine != "tile1")
-                sq = {"tile_sw1": 1, "tile_sw2": 2, "tile_sw": 4}.get(engine, 0)
-            kv_ops.set_cast_softconv(sq, sq)
+                # tile / tile1: the dequantiser's default share; tile_sw*: that share of the conversions
+                kv_ops.set_cast_softconv(None, {"tile_sw1": 1, "tile_sw2": 2, "tile_sw": 4}.get(engine))
                 eng = "tile" if engine.startswith("tile") else engine
                 ms = _time(lambda: kv_ops.kv_transfer(b, d_ids, back, s_ids, engine=eng), args.iters,
                            args.warmup, flush)

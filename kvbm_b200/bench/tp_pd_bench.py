@@ -26,7 +26,6 @@ import argparse
 import json
 import math
 import os
-import statistics
 from datetime import timedelta
 
 import numpy as np
