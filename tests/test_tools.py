@@ -83,11 +83,10 @@ def test_every_source_file_compiles():
     """Every Python file of the package, the import-alias package and the bench entry point is valid
     Python (a syntax error in a rarely imported module, e.g. a bench, would otherwise go unnoticed)."""
     import pathlib
-    import py_compile
 
     root = pathlib.Path(__file__).resolve().parents[1]
     files = sorted(list((root / "kvbm_b200").rglob("*.py")) + list((root / "kvbm").rglob("*.py"))
                    + [root / "bench.py", root / "__graft_entry__.py"])
     assert len(files) > 50
     for f in files:
-        py_compile.compile(str(f), doraise=True, cfile="/dev/null")
+        compile(f.read_text(), str(f), "exec")
