@@ -90,3 +90,18 @@ def test_every_source_file_compiles():
     assert len(files) > 50
     for f in files:
         compile(f.read_text(), str(f), "exec")
+
+
+def test_bench_entry_points_parse_their_arguments():
+    """Every bench module (and bench.py) imports and answers --help on a machine without a GPU."""
+    import pathlib
+    import subprocess
+    import sys
+
+    root = pathlib.Path(__file__).resolve().parents[1]
+    mods = sorted(p.stem for p in (root / "kvbm_b200" / "bench").glob("*.py") if p.stem != "__init__")
+    assert "connector_bench" in mods and "kvbench" in mods
+    for m in mods:
+        r = subprocess.run([sys.executable, "-m", f"kvbm_b200.bench.{m}", "--help"], cwd=root, capture_output=True,
+                           text=True, timeout=120)
+        assert r.returncode == 0 and "usage" in r.stdout, (m, r.stderr[-500:])
