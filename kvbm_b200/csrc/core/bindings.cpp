@@ -358,6 +358,15 @@ PYBIND11_MODULE(_kvbm_core, m) {
         for (auto& [hi, lo] : r->second) insts.append((py::int_(hi) << py::int_(64)) | py::int_(lo));
         return py::make_tuple(to_py(r->first), insts);
       })
+      .def("by_position", [](PositionalIndex& ix, uint64_t position) {
+        py::list out;
+        for (auto& [lin, insts] : ix.at_position(position)) {
+          py::list holders;
+          for (auto& [hi, lo] : insts) holders.append((py::int_(hi) << py::int_(64)) | py::int_(lo));
+          out.append(py::make_tuple(py::int_(lin), holders));
+        }
+        return out;
+      })
       .def("num_positions", &PositionalIndex::num_positions)
       .def("dropped_out_of_range", &PositionalIndex::dropped)
       .def("num_entries", &PositionalIndex::num_entries);

@@ -224,6 +224,16 @@ class PositionalIndex {
     for (auto& [p, m] : buckets_) n += m.size();
     return n;
   }
+  // Every indexed block at one position bucket: (lineage word, holders), sorted by lineage.
+  std::vector<std::pair<uint64_t, std::vector<InstanceId>>> at_position(uint64_t position) const {
+    std::lock_guard<RankedMutex> g(mu_);
+    std::vector<std::pair<uint64_t, std::vector<InstanceId>>> out;
+    auto b = buckets_.find(position);
+    if (b == buckets_.end()) return out;
+    for (auto& [lin, insts] : b->second) out.emplace_back(lin, std::vector<InstanceId>(insts.begin(), insts.end()));
+    std::sort(out.begin(), out.end(), [](auto& a, auto& c) { return a.first < c.first; });
+    return out;
+  }
 
  private:
   mutable RankedMutex mu_{kRankPositionalIndex, "PositionalIndex"};

@@ -99,6 +99,18 @@ class HubClient:
                          params={"force": "true" if force else "false"},
                          json={"request": request or {}, "timeout": timeout}, timeout=timeout + 10)
 
+    def index_config(self) -> dict:
+        return self._req("GET", "/v1/indexer/config")
+
+    def index_instances(self) -> list[str]:
+        return self._req("GET", "/v1/indexer/instances")["instances"]
+
+    def index_by_position(self, position: int) -> dict:
+        return self._req("GET", "/v1/indexer/hashes/by_position", params={"position": int(position)})
+
+    def disagg_instances(self) -> dict:
+        return self._req("GET", "/v1/disagg/instances")
+
     def router_counters(self) -> dict:
         return self._req("GET", "/v1/prefill-router/counters")
 

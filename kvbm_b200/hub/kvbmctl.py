@@ -42,6 +42,7 @@ from __future__ import annotations
 import argparse
 import copy
 import json
+import os
 import sys
 
 from .client import HubClient
@@ -206,7 +207,8 @@ def run_control(a, client: HubClient):
 
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(prog="kvbmctl")
-    p.add_argument("--hub", default="http://127.0.0.1:1337")
+    p.add_argument("--hub", default=os.environ.get("KVBMCTL_HUB", "http://127.0.0.1:1337"),
+                   help="hub URL (default: $KVBMCTL_HUB, else http://127.0.0.1:1337)")
     p.add_argument("--json", action="store_true")
     sub = p.add_subparsers(dest="cmd", required=True)
     sub.add_parser("health")
@@ -244,6 +246,17 @@ def main(argv=None) -> int:
     ct.add_argument("--timeout", type=float, default=10.0)
     ct.add_argument("action", choices=["modules", "describe", "metrics", "reset"])
     ct.add_argument("--tiers", default=None, help="reset: comma list of g2,g3 (default: every configured tier)")
+    ix = sub.add_parser("indexer", help="query the hub's KV block index")
+    ixs = ix.add_subparsers(dest="ix", required=True)
+    ixs.add_parser("config")
+    ixs.add_parser("get-instances", help="instances registered to the indexer (not all of them emit events)")
+    bp = ixs.add_parser("by-pos", help="indexed blocks at a position bucket")
+    bp.add_argument("pos", type=int)
+    iq = ixs.add_parser("query", help="which instances hold a block hash (decimal or 0x, e.g. a by-pos hash_u128)")
+    iq.add_argument("hash")
+    dg = sub.add_parser("disagg", help="the hub's conditional-disaggregation registry")
+    dgs = dg.add_subparsers(dest="dg", required=True)
+    dgs.add_parser("instances", help="registered prefill / decode instances and the queue depth")
     cal = sub.add_parser("calibrate", help="run a prefill worker's calibration sweep through the hub")
     cal.add_argument("--instance-id", type=int, required=True)
     cal.add_argument("--seq", default=None, help="comma list of input lengths (default: the engine's ladder)")
@@ -285,6 +298,17 @@ def main(argv=None) -> int:
         except ControlError as e:
             print(f"kvbmctl: {e}", file=sys.stderr)
             return 2
+    elif a.cmd == "indexer":
+        if a.ix == "config":
+            out = client.index_config()
+        elif a.ix == "get-instances":
+            out = {"instances": client.index_instances()}
+        elif a.ix == "by-pos":
+            out = client.index_by_position(a.pos)
+        else:
+            out = client.query([int(a.hash, 0)])
+    elif a.cmd == "disagg":
+        out = client.disagg_instances()
     elif a.cmd == "calibrate":
         req = {k: v for k, v in {"seq": [int(x) for x in a.seq.split(",")] if a.seq else None, "osl": a.osl,
                                   "seed": a.seed, "max_isl_fraction": a.max_isl_fraction,

@@ -101,6 +101,7 @@ class HubServer:
         r.add_post("/v1/indexer/query", self._query)
         r.add_get("/v1/indexer/config", self._index_config)
         r.add_get("/v1/indexer/instances", self._index_instances)
+        r.add_get("/v1/indexer/hashes/by_position", self._index_by_position)
         r.add_post("/v1/disagg/enqueue", self._cd_enqueue)
         r.add_post("/v1/disagg/dequeue", self._cd_dequeue)
         r.add_get("/v1/disagg/instances", self._cd_instances)
@@ -211,6 +212,18 @@ class HubServer:
         return web.json_response({"block_size": self.block_size, "num_positions": self.index.num_positions(),
                                   "dropped_out_of_range": self.index.dropped_out_of_range(),
                                   "entries": self.index.num_entries()})
+
+    async def _index_by_position(self, req):
+        """Every indexed block at one position bucket: its lineage word, the sequence hash that a
+        query names (position, lineage; the index does not keep the parent word) and its holders."""
+        try:
+            pos = int(req.query["position"])
+        except (KeyError, ValueError):
+            return web.json_response({"error": "position=<int> is required"}, status=400)
+        rows = self.index.by_position(pos)
+        return web.json_response({"position": pos, "blocks": [
+            {"lineage": str(lin), "hash_u128": str((pos << 128) | lin), "holders": [str(h) for h in holders]}
+            for lin, holders in rows]})
 
     async def _index_instances(self, req):
         return web.json_response({"instances": [str(r.instance_id) for r in self.registry.list(feature="indexer")]})

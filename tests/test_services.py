@@ -328,3 +328,34 @@ def test_hub_serves_its_web_ui(hub):
     for el in set(re.findall(r'fill(?:Dl|Table)\("([a-z_]+)"', js.text)):
         assert f'id="{el}"' in page.text, el
     assert requests.get(hub.url + "/style.css", timeout=5).headers["content-type"].startswith("text/css")
+
+
+def test_kvbmctl_indexer_and_disagg_groups(hub, capsys, monkeypatch):
+    """kvbmctl's indexer group (config, get-instances, by-pos, query) and disagg instances, with the
+    hub URL taken from KVBMCTL_HUB."""
+    import json
+
+    from kvbm_b200.hub.client import HubClient
+    from kvbm_b200.hub.kvbmctl import main as kvbmctl
+    from kvbm_b200.logical.sequence import sequence_hashes
+
+    c = HubClient(hub.url)
+    c.register(91, features=["indexer"], address="tcp://127.0.0.1:1")
+    c.register(92, role="prefill", features=["prefill_router"], address="tcp://127.0.0.1:2")
+    hs = sequence_hashes(list(range(3 * 16)), 16)
+    c.publish_events(91, [("create", hs)])
+    monkeypatch.setenv("KVBMCTL_HUB", hub.url)
+
+    def run(*args):
+        assert kvbmctl(["--json", *args]) == 0
+        return json.loads(capsys.readouterr().out)
+
+    assert run("indexer", "config")["entries"] == 3
+    assert "91" in run("indexer", "get-instances")["instances"]
+    pos = run("indexer", "by-pos", "2")
+    assert pos["position"] == 2 and len(pos["blocks"]) == 1 and pos["blocks"][0]["holders"] == ["91"]
+    assert int(pos["blocks"][0]["lineage"]) == hs[2] & ((1 << 64) - 1)
+    q = run("indexer", "query", hex(hs[2]))
+    assert q["hit"] and q["holders"] == [91] and q["position"] == 2
+    assert run("indexer", "by-pos", "7")["blocks"] == []
+    assert "92" in run("disagg", "instances")["prefill"]
