@@ -388,3 +388,38 @@ def test_pipeline_timeout_reports_status_without_fault(bulk):
     torch.cuda.synchronize()
     kv_ops.check_transfer_status()
     assert torch.equal(dst.gather_blocks(d_ids), src.gather_blocks(s_ids))
+
+
+@pytest.mark.parametrize("layout", ["NHD", "HND"])
+@pytest.mark.parametrize("backend", [None, "async"])
+def test_tensor_level_kernels_api(layout, backend):
+    """``kvbm.kernels``: block stacks <-> universal tensors and <-> operational buffers, checked
+    exactly against PyTorch permutes / concatenation of the same tensors."""
+    from kvbm import kernels
+
+    nb, nh, nl, no, nt, hd = 2, 4, 3, 2, 16, 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    inner = (nt, nh, hd) if layout == "NHD" else (nh, nt, hd)
+    blocks = [[torch.randn(inner, generator=g, device="cuda").to(torch.bfloat16) for _ in range(nl * no)]
+              for _ in range(nb)]
+    unis = [torch.zeros((nh, nl, no, nt, hd), dtype=torch.bfloat16, device="cuda") for _ in range(nb)]
+    kernels.block_to_universal(blocks, unis, layout)
+    for b in range(nb):
+        for l in range(nl):
+            for o in range(no):
+                c = blocks[b][l * no + o]
+                want = c.transpose(0, 1) if layout == "NHD" else c  # [nh, nt, hd]
+                assert torch.equal(unis[b][:, l, o], want)
+    back = [[torch.zeros_like(c) for c in grp] for grp in blocks]
+    kernels.universal_to_block(unis, back, layout)
+    assert all(torch.equal(x, y) for gx, gy in zip(blocks, back) for x, y in zip(gx, gy))
+    ops = [torch.zeros((nl, no, nt * nh * hd), dtype=torch.bfloat16, device="cuda") for _ in range(nb)]
+    kernels.block_to_operational(blocks, ops, backend=backend)
+    for b in range(nb):
+        assert torch.equal(ops[b].reshape(-1), torch.cat([c.reshape(-1) for c in blocks[b]]))
+    back2 = [[torch.zeros_like(c) for c in grp] for grp in blocks]
+    kernels.operational_to_block(ops, back2, backend=backend)
+    assert all(torch.equal(x, y) for gx, gy in zip(blocks, back2) for x, y in zip(gx, gy))
+    one = torch.zeros((nh, nl, no, nt, hd), dtype=torch.bfloat16, device="cuda")
+    kernels.block_to_universal(blocks[0], one, layout)  # a single universal tensor is one block
+    assert torch.equal(one, unis[0])

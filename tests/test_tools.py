@@ -109,3 +109,21 @@ def test_bench_entry_points_parse_their_arguments(monkeypatch, capsys):
             runpy.run_module(f"kvbm_b200.bench.{m}", run_name="__main__")
         assert e.value.code in (0, None), m
         assert "usage" in capsys.readouterr().out, m
+
+
+def test_kernels_api_validates_arguments_without_a_gpu():
+    """``kvbm.kernels`` rejects bad layouts, backends and mismatched groups before touching a GPU."""
+    import torch
+
+    from kvbm import kernels
+
+    with pytest.raises(ValueError, match="layout"):
+        kernels.block_to_universal([[torch.zeros(1)]], [torch.zeros(1)], "XYZ")
+    with pytest.raises(ValueError, match="groups"):
+        kernels.block_to_universal([[torch.zeros(1)], [torch.zeros(1)]], [torch.zeros(1)], "NHD")
+    with pytest.raises(ValueError, match="backend"):
+        kernels.block_to_operational([[torch.zeros(1)]], [torch.zeros(1)], backend="dma")
+    with pytest.raises(ValueError, match="CUDA"):
+        kernels.block_to_operational([[torch.zeros(4)]], [torch.zeros(4)])
+    with pytest.raises(TypeError):
+        kernels.block_to_universal(torch.zeros(3), [torch.zeros(1)])
