@@ -137,7 +137,13 @@ def test_lazy_import_does_not_pull_vllm():
             "kvbm.vllm.sched_output", "kvbm.vllm.version_check", "kvbm.vllm.dim_probe", "kvbm.vllm.connector",
             "kvbm.vllm.connector.base", "kvbm.vllm.connector.leader", "kvbm.vllm.connector.worker",
             "kvbm.vllm.connector.pd", "kvbm.vllm.connector.protocols"]
-    code = f"import sys, importlib; [importlib.import_module(m) for m in {mods!r}]; print('vllm' in sys.modules)"
+    mods += ["kvbm.kernels"]
+    code = (f"import sys, importlib; [importlib.import_module(m) for m in {mods!r}]; "
+            "from kvbm import KvbmRuntime, ConnectorLeader, ConnectorWorker, KvbmRequest, KvbmVllmConfig, "
+            "SchedulerOutput, Tensor, kernels, _KERNELS_AVAILABLE; from kvbm.vllm import KvbmVllmConfig, "
+            "version_check; from kvbm.hub import CompletionEvent, PrefillRouterHandler, try_wrap_engine, "
+            "make_dispatch_lambda, make_calibrate_lambda, capture_calibration_defaults; "
+            "print('vllm' in sys.modules)")
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True)
     assert out.stdout.strip() == "False"
 
