@@ -300,6 +300,17 @@ def _define():
                                                num_workers=max(1, int(self.info.get("tensor_parallel_size", 1))),
                                                tp_size=max(1, int(self.info.get("tensor_parallel_size", 1))),
                                                objects=_object_store(cfg), **disagg_leader_kwargs(cfg))
+                self._metrics_server = None
+                if cfg.metrics.enabled:
+                    # Prometheus endpoint of the scheduler: pool occupancy, matches, cache hit rates
+                    from ..utils.metrics import KvbmCollector, serve_metrics
+
+                    col = KvbmCollector()
+                    col.add_pool("g2", g2)
+                    if g3 is not None:
+                        col.add_pool("g3", g3)
+                    col.cache = self._leader.stats
+                    self._metrics_server = serve_metrics(col, int(cfg.metrics.port))
                 self._remote = None
                 if searching:
                     self._remote = RemoteSearchPlane(cfg, self._leader, iid,
@@ -416,6 +427,9 @@ def _define():
                 self.consolidator.close()
             if getattr(self, "_remote", None) is not None:
                 self._remote.close()
+            srv = getattr(self, "_metrics_server", None)
+            if srv is not None and isinstance(srv, tuple):
+                srv[0].shutdown()  # (server, thread) from prometheus_client
 
     globals()["KvbmConnector"] = KvbmConnector
     globals()["KvbmConnectorMetadata"] = KvbmConnectorMetadata

@@ -253,3 +253,26 @@ def test_scheduler_connector_runs_the_consolidator(monkeypatch):
     assert cc._offset_port("tcp://*:5557", 2) == "tcp://*:5559" and cc._offset_port("inproc://c", 1) == "inproc://c_dp1"
     monkeypatch.setenv("DYN_KVBM_KV_EVENTS_CONSOLIDATOR_MODE", "weird")
     assert cc.get_consolidator_mode() == "dedup"
+
+
+def test_scheduler_connector_serves_prometheus_metrics():
+    """``metrics.enabled``: the scheduler-role connector serves its pools' and cache counters on
+    ``metrics.port`` under the reference's metric names."""
+    import socket
+    import urllib.request
+
+    from kvbm_b200.connector import vllm_connector as vc
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    conn = vc.KvbmConnector(_vllm_config({"leader": {"cache": {"host": {"num_blocks": 64}},
+                                                     "metrics": {"enabled": True, "port": port}}}),
+                            vllm_base.KVConnectorRole.SCHEDULER)
+    try:
+        conn.get_num_new_matched_tokens(_request("m", list(range(40))), 0)
+        body = urllib.request.urlopen(f"http://127.0.0.1:{port}/metrics", timeout=5).read().decode()
+        assert 'kvbm_reset_pool_size{tier="g2"} 64.0' in body
+        assert "kvbm_allocations_total" in body and "kvbm_host_cache_hit_rate" in body
+    finally:
+        conn.shutdown()
