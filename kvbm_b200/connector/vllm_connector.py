@@ -290,13 +290,26 @@ def _define():
                     self.consolidator = start_leader_consolidator(eps[0], eps[1], "vllm", bs, self._events)
                 if self._events is not None:
                     self._events.start()
+                # offload policies from the configuration; an access-frequency sketch when one needs it
+                from .. import _core_native as core
+                from ..engine.offload import make_policy
+
+                pol = cfg.offload
+                lfu = any("lfu" in p for p in pol.g1_to_g2.policies + pol.g2_to_g3.policies)
                 g2 = BlockManager(max(1, g2n), bs, cfg.cache.inactive_backend, Tier.G2,
                                   duplicate_policy=cfg.cache.duplicate_policy,
-                                  events=self._events.queue if self._events is not None else None)
+                                  events=self._events.queue if self._events is not None else None,
+                                  frequency=core.TinyLfu() if lfu and cfg.cache.inactive_backend != "multi_lru"
+                                  else None)
                 g3 = BlockManager(g3n, bs, cfg.cache.inactive_backend, Tier.G3, registry=g2.registry) if g3n else None
+                decode_offload = os.getenv("KVBM_DECODE_OFFLOAD")
                 self._leader = ConnectorLeader(InstanceLeader.scheduler_side(g2, g3), bs,
                                                offload_enabled=g2n > 0,
-                                               decode_offload=os.getenv("KVBM_DECODE_OFFLOAD", "false") == "true",
+                                               decode_offload=(pol.decode_offload if decode_offload is None
+                                                               else decode_offload == "true"),
+                                               g2_policy=make_policy(pol.g1_to_g2.policies, g2),
+                                               g3_policy=make_policy(pol.g2_to_g3.policies, g3) if g3 is not None
+                                               else None,
                                                num_workers=max(1, int(self.info.get("tensor_parallel_size", 1))),
                                                tp_size=max(1, int(self.info.get("tensor_parallel_size", 1))),
                                                objects=_object_store(cfg), **disagg_leader_kwargs(cfg))

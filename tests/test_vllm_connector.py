@@ -276,3 +276,23 @@ def test_scheduler_connector_serves_prometheus_metrics():
         assert "kvbm_allocations_total" in body and "kvbm_host_cache_hit_rate" in body
     finally:
         conn.shutdown()
+
+
+def test_scheduler_connector_applies_the_configured_offload_policies():
+    """``offload.*.policies`` reach the scheduler's tier engine; an LFU policy gets a frequency
+    sketch on the registry, so repeated accesses count."""
+    from kvbm_b200.connector import vllm_connector as vc
+    from kvbm_b200.engine.offload import PresenceAndLFUFilter, PresenceFilter
+
+    conn = vc.KvbmConnector(_vllm_config({"leader": {"cache": {"host": {"num_blocks": 64}},
+                                                     "offload": {"g1_to_g2": {"policies": ["presence_lfu"]}}}}),
+                            vllm_base.KVConnectorRole.SCHEDULER)
+    eng = conn._leader.engine
+    assert isinstance(eng.g2_policy, PresenceAndLFUFilter)
+    reg = conn._leader.leader.g2.registry
+    reg.touch(12345)
+    reg.touch(12345)
+    assert reg.frequency(12345) >= 2
+    plain = vc.KvbmConnector(_vllm_config({"leader": {"cache": {"host": {"num_blocks": 64}}}}),
+                             vllm_base.KVConnectorRole.SCHEDULER)
+    assert isinstance(plain._leader.engine.g2_policy, PresenceFilter)
