@@ -146,10 +146,9 @@ def _decode_main(model_dir, root, iid, prefill_iid, out_path):
                                               for r in received], "cd": cd, "lens": list(PROMPT_LENS)}, f)
 
 
-def test_vllm_engines_disaggregated_through_the_connector(tmp_path):
-    pytest.importorskip("vllm")
-    if not torch.cuda.is_available():
-        pytest.skip("needs a GPU")
+def _run_pair(tmp_path, prefill_gpu: str, decode_gpu: str):
+    """Start the prefill engine on ``prefill_gpu`` and the decode engine on ``decode_gpu`` (each process
+    sees only its own GPU) and check the disaggregated run."""
     import gc
 
     gc.collect()
@@ -160,20 +159,22 @@ def test_vllm_engines_disaggregated_through_the_connector(tmp_path):
     base = int.from_bytes(os.urandom(2), "little") * 16 + 4096
     pre_iid, dec_iid = base + 1, base + 2
     repo = os.path.dirname(os.path.dirname(HERE))
-    env = {**os.environ, "VLLM_ENABLE_V1_MULTIPROCESSING": "0", "CUDA_VISIBLE_DEVICES":
-           os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0],
+    env = {**os.environ, "VLLM_ENABLE_V1_MULTIPROCESSING": "0",
            "PYTHONPATH": os.pathsep.join([repo] + [p for p in [os.environ.get("PYTHONPATH")] if p])}
+    pre_env, dec_env = {**env, "CUDA_VISIBLE_DEVICES": prefill_gpu}, {**env, "CUDA_VISIBLE_DEVICES": decode_gpu}
     pre_out, dec_out = str(tmp_path / "prefill.json"), str(tmp_path / "decode.json")
-    pre = subprocess.Popen([sys.executable, HERE, "prefill", model_dir, root, str(pre_iid), pre_out], env=env)
+    pre = subprocess.Popen([sys.executable, HERE, "prefill", model_dir, root, str(pre_iid), pre_out], env=pre_env)
     dec = None
     try:
         deadline = time.monotonic() + 300
-        while not os.path.exists(os.path.join(root, "prefill.ready")):
+        # on one GPU the engines start one after the other (each sizes its cache from the free memory);
+        # on two GPUs the decode engine starts at once and its dispatches wait in the plane
+        while prefill_gpu == decode_gpu and not os.path.exists(os.path.join(root, "prefill.ready")):
             assert pre.poll() is None, f"prefill engine exited with {pre.returncode}"
             assert time.monotonic() < deadline, "prefill engine did not start"
             time.sleep(0.5)
         dec = subprocess.Popen([sys.executable, HERE, "decode", model_dir, root, str(dec_iid), str(pre_iid), dec_out],
-                               env=env)
+                               env=dec_env)
         assert dec.wait(timeout=600) == 0, "decode engine failed"
     finally:
         open(os.path.join(root, "stop"), "w").close()
@@ -210,6 +211,31 @@ def test_vllm_engines_disaggregated_through_the_connector(tmp_path):
             assert sums[i] == pushed[i], f"decode block {i}: checksum differs from the prefill block pushed there"
             checked += 1
     assert checked >= sum((p - 1) // 16 for p in PROMPT_LENS)
+
+
+def _visible_gpus() -> list[str]:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    ids = [g for g in vis.split(",") if g] if vis else [str(i) for i in range(torch.cuda.device_count())]
+    return ids
+
+
+def test_vllm_engines_disaggregated_through_the_connector(tmp_path):
+    pytest.importorskip("vllm")
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    g = _visible_gpus()[0]
+    _run_pair(tmp_path, g, g)
+
+
+@pytest.mark.multigpu
+def test_vllm_engines_on_two_gpus_push_over_nvlink(tmp_path):
+    """The same with each engine on its own GPU, each process seeing only that GPU: the prefill
+    engine's worker maps the decode engine's KV cache from the other GPU and pushes over NVLink."""
+    pytest.importorskip("vllm")
+    gpus = _visible_gpus() if torch.cuda.is_available() else []
+    if len(gpus) < 2:
+        pytest.skip("needs two GPUs")
+    _run_pair(tmp_path, gpus[1], gpus[0])
 
 
 if __name__ == "__main__":
