@@ -17,7 +17,6 @@ src/torch/mod.rs:140, src/vllm/config.rs:246, src/hub/prefill_router.rs.
 from __future__ import annotations
 
 import types
-from dataclasses import dataclass, field
 
 from . import __version__
 from .connector.leader import ConnectorLeader as _Leader
@@ -117,9 +116,32 @@ class Tensor:
         return self._t
 
 
-@dataclass
 class KvbmVllmConfig:
-    info: dict = field(default_factory=dict)
+    """The vLLM facts the block manager sizes itself from.
+
+    Built either from one flat mapping (``info``, this library's connector
+    form) or, as the reference's binding is, from a ``parallel`` and an
+    ``attention`` section (world size, ranks, TP/PP/DP degrees; block size,
+    block counts, cache dtype bytes, KV layout, head size, KV heads); both
+    forms expose ``info`` (flat), ``parallel`` and ``attention``."""
+
+    def __init__(self, info_or_parallel: dict | None = None, attention: dict | None = None):
+        if attention is None:
+            self.info = dict(info_or_parallel or {})
+            self.parallel = {k: self.info[k] for k in ("world_size", "rank", "tensor_parallel_size",
+                                                       "pipeline_parallel_size", "data_parallel_size",
+                                                       "data_parallel_rank") if k in self.info}
+            self.attention = {k: self.info[k] for k in ("block_size", "head_size", "num_kv_heads", "dtype_bytes",
+                                                        "cache_dtype", "num_layers") if k in self.info}
+        else:
+            self.parallel, self.attention = dict(info_or_parallel or {}), dict(attention)
+            self.info = {**self.parallel, **self.attention}
+
+    def __eq__(self, other) -> bool:
+        return isinstance(other, KvbmVllmConfig) and self.info == other.info
+
+    def __repr__(self) -> str:
+        return f"KvbmVllmConfig(parallel={self.parallel}, attention={self.attention})"
 
     @classmethod
     def from_vllm(cls, vllm_config) -> "KvbmVllmConfig":

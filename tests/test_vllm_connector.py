@@ -296,3 +296,22 @@ def test_scheduler_connector_applies_the_configured_offload_policies():
     plain = vc.KvbmConnector(_vllm_config({"leader": {"cache": {"host": {"num_blocks": 64}}}}),
                              vllm_base.KVConnectorRole.SCHEDULER)
     assert isinstance(plain._leader.engine.g2_policy, PresenceFilter)
+
+
+def test_reference_shaped_vllm_config(capsys):
+    """``kvbm.vllm.config.extract_vllm_config_for_kvbm`` returns a ``KvbmVllmConfig`` with the
+    reference's parallel / attention sections and prints the table on rank 0."""
+    from kvbm.vllm.config import extract_vllm_config_for_kvbm
+
+    from kvbm_b200._core import KvbmVllmConfig
+
+    c = extract_vllm_config_for_kvbm(_vllm_config({}))
+    assert isinstance(c, KvbmVllmConfig)
+    assert c.parallel["tensor_parallel_size"] == 1 and c.parallel["rank"] == 0
+    assert c.attention["block_size"] == 16 and c.attention["head_size"] == 64 and c.attention["num_heads"] == 2
+    assert c.attention["cache_dtype_bytes"] == 2 and c.info["block_size"] == 16
+    assert "Parallel:" in capsys.readouterr().out
+    extract_vllm_config_for_kvbm(_vllm_config({}), log_config=False)
+    assert capsys.readouterr().out == ""
+    flat = KvbmVllmConfig({"block_size": 16, "rank": 0})
+    assert flat.attention == {"block_size": 16} and flat.parallel == {"rank": 0}
