@@ -16,6 +16,7 @@ src/torch/mod.rs:140, src/vllm/config.rs:246, src/hub/prefill_router.rs.
 
 from __future__ import annotations
 
+import time
 import types
 
 from . import __version__
@@ -29,6 +30,7 @@ from .runtime.messenger import Messenger
 from .utils.config import KvbmConfig
 
 LAYOUT_HANDLER = "kvbm.connector.worker.get_layout_config"
+HANDLERS_HANDLER = "kvbm.runtime.handlers"   # the handler names a runtime's messenger serves
 
 
 def is_available() -> bool:
@@ -47,6 +49,7 @@ class KvbmRuntime:
     def __init__(self, config: KvbmConfig, role: str):
         self.config, self.role = config, role
         self.messenger = Messenger(bind=config.messenger.bind)
+        self.messenger.register_handler(HANDLERS_HANDLER, lambda _p: sorted(self.messenger._handlers))
         for iid, addr in (config.messenger.peers or {}).items():  # static discovery
             self.messenger.register_peer(int(iid), addr)
         self.hub = None
@@ -79,6 +82,19 @@ class KvbmRuntime:
 
     def register_peer(self, instance_id: int, address: str) -> None:
         self.messenger.register_peer(instance_id, address)
+
+    def wait_for_handler(self, instance_id: int, handler_name: str, timeout_s: float = 60.0) -> None:
+        """Block until peer ``instance_id`` serves ``handler_name`` (its messenger lists it)."""
+        deadline = time.monotonic() + timeout_s
+        last = None
+        while time.monotonic() < deadline:
+            try:
+                if handler_name in self.messenger.call(int(instance_id), HANDLERS_HANDLER, None, timeout=2.0):
+                    return
+            except Exception as e:  # noqa: BLE001 - the peer may not be up yet
+                last = e
+            time.sleep(0.05)
+        raise TimeoutError(f"peer {instance_id} did not serve {handler_name!r} within {timeout_s} s ({last})")
 
     def shutdown(self) -> None:
         if self._registration is not None:
@@ -172,11 +188,33 @@ class SchedulerOutput:
     def add_finished(self, request_ids: list[str]) -> None:
         self._lite.finished_req_ids.extend(request_ids)
 
+    def set_num_scheduled_tokens(self, counts: dict[str, int]) -> None:
+        self._sched = dict(counts)
+
+    def get_total_num_scheduled_tokens(self) -> int:
+        return sum(self._sched.values())
+
+    def set_preempted_req_ids(self, request_ids) -> None:
+        self._lite.preempted_req_ids = sorted(request_ids or [])
+
+    def serialize(self) -> bytes:
+        """The step as msgpack: iteration, per-request (new tokens, new blocks, computed tokens),
+        scheduled token counts, finished and preempted ids."""
+        import msgpack
+
+        return msgpack.packb({"iteration": self.iteration,
+                              "scheduled": {r: [list(t), list(b), int(c)] for r, (t, b, c) in
+                                            self._lite.scheduled.items()},
+                              "num_scheduled_tokens": dict(self._sched),
+                              "finished": list(self._lite.finished_req_ids),
+                              "preempted": list(self._lite.preempted_req_ids)}, use_bin_type=True)
+
     def lite(self) -> SchedulerOutputLite:
         out = SchedulerOutputLite(self.iteration)
         for rid, (toks, blocks, computed) in self._lite.scheduled.items():
             out.scheduled[rid] = (toks, blocks, computed + self._sched.get(rid, 0))
         out.finished_req_ids = list(self._lite.finished_req_ids)
+        out.preempted_req_ids = list(self._lite.preempted_req_ids)
         return out
 
 
@@ -262,6 +300,15 @@ class ConnectorLeader:
     def request_finished(self, request_id: str):
         return self._need().request_finished(request_id)
 
+    build_connector_meta = build_connector_metadata
+
+    def extend_slot_tokens(self, request_id: str, tokens: list[int]) -> None:
+        """Append tokens (e.g. generated ones) to a request's sequence outside a scheduler step."""
+        self._need().slots[request_id].seq.append(list(tokens))
+
+    def get_slot_total_tokens(self, request_id: str) -> int:
+        return len(self._need().slots[request_id].seq)
+
 
 class ConnectorWorker:
     """Worker-side connector bound to a runtime; serves its layout to the leader."""
@@ -297,6 +344,44 @@ class ConnectorWorker:
         out = self._impl.register_layout(layout)
         self._serve()
         return out
+
+    # the worker hooks, explicitly (the reference's binding names)
+    def bind_connector_metadata(self, metadata: bytes) -> None:
+        self._impl.bind_connector_metadata(metadata)
+
+    def clear_connector_metadata(self) -> None:
+        self._impl.clear_connector_metadata()
+
+    def start_load_kv(self) -> None:
+        self._impl.start_load_kv()
+
+    def wait_for_layer_load(self, layer) -> None:
+        self._impl.wait_for_layer_load(layer)
+
+    def save_kv_layer(self, layer, requests=None) -> None:
+        self._impl.save_kv_layer(layer, requests)
+
+    def wait_for_save(self) -> None:
+        self._impl.wait_for_save()
+
+    def get_finished(self, finished_req_ids=None):
+        return self._impl.get_finished(set(finished_req_ids or ()))
+
+    def get_failed_onboarding(self) -> set[int]:
+        """G1 block ids whose load failed (the framework recomputes them)."""
+        return self._impl.get_block_ids_with_load_errors()
+
+    def handle_preemptions(self, preempted_req_ids) -> None:
+        self._impl.handle_preemptions(preempted_req_ids)
+
+    def handshake_metadata(self) -> dict:
+        return self._impl.handshake_metadata()
+
+    def is_initialized(self) -> bool:
+        return self._impl.worker is not None
+
+    def shutdown(self) -> None:
+        self._impl.shutdown()
 
     def __getattr__(self, name):
         return getattr(self._impl, name)

@@ -185,3 +185,46 @@ def test_events_manager_batches_to_sinks():
     em.stop()
     assert got and got[0][0] == 9 and got[0][1][0][0] == "create" and len(got[0][1][0][1]) == 3
     del imm
+
+
+def test_core_binding_method_names():
+    """The ``kvbm._core`` classes answer the reference binding's method names: runtime handler
+    waits between two runtimes, scheduler-output accessors and serialisation, slot token access
+    on the leader, and the worker hooks."""
+    import msgpack
+
+    import kvbm._core as kc
+
+    worker_rt = kc.KvbmRuntime.build_worker('{"cache": {"host": {"num_blocks": 8}}}')
+    leader_rt = kc.KvbmRuntime.build_leader('{"cache": {"host": {"num_blocks": 8}}}')
+    try:
+        wid, waddr = worker_rt.peer_info()
+        leader_rt.register_peer(wid, waddr)
+        w = kc.ConnectorWorker(worker_rt, block_size=16, num_kv_heads=2, head_size=64)
+        leader_rt.wait_for_handler(wid, "kvbm.connector.worker.get_layout_config", timeout_s=5)
+        with pytest.raises(TimeoutError):
+            leader_rt.wait_for_handler(wid, "no.such.handler", timeout_s=0.3)
+        assert not w.is_initialized()
+        for name in ("bind_connector_metadata", "clear_connector_metadata", "start_load_kv", "wait_for_layer_load",
+                     "save_kv_layer", "wait_for_save", "get_finished", "get_failed_onboarding", "handle_preemptions",
+                     "handshake_metadata", "shutdown", "register_kv_caches", "register_cross_layers_kv_cache"):
+            assert callable(getattr(kc.ConnectorWorker, name)), name
+
+        so = kc.SchedulerOutput(3)
+        so.add_new_request("r", list(range(32)), [1, 2], 0)
+        so.set_num_scheduled_tokens({"r": 32})
+        so.set_preempted_req_ids({"p"})
+        assert so.get_total_num_scheduled_tokens() == 32
+        d = msgpack.unpackb(so.serialize(), raw=False)
+        assert d["iteration"] == 3 and d["scheduled"]["r"][1] == [1, 2] and d["preempted"] == ["p"]
+        assert so.lite().preempted_req_ids == ["p"]
+
+        leader = kc.ConnectorLeader(leader_rt, 16)
+        leader.initialize_workers(layout={"g2_blocks": 8, "g3_blocks": 0})
+        leader.create_slot(kc.KvbmRequest("r", list(range(20))))
+        leader.extend_slot_tokens("r", [7, 8, 9])
+        assert leader.get_slot_total_tokens("r") == 23 and leader.block_size == 16
+        assert leader.build_connector_meta == leader.build_connector_metadata
+    finally:
+        worker_rt.shutdown()
+        leader_rt.shutdown()
