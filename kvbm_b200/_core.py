@@ -259,8 +259,11 @@ class ConnectorLeader:
             from .object import make_object_store
 
             objects = make_object_store(cfg.object)
+        from .connector.vllm_connector import disagg_leader_kwargs
+
         self._impl = _Leader(leader, self.block_size, objects=objects,
-                             offload_enabled=layout.get("g2_blocks", 0) > 0, num_workers=max(1, len(self._workers)))
+                             offload_enabled=layout.get("g2_blocks", 0) > 0, num_workers=max(1, len(self._workers)),
+                             **disagg_leader_kwargs(cfg))
         # operator / peer control plane on the runtime's messenger (describe, reset, metrics)
         import dataclasses
         import json

@@ -228,3 +228,28 @@ def test_core_binding_method_names():
     finally:
         worker_rt.shutdown()
         leader_rt.shutdown()
+
+
+def test_core_leader_takes_the_disaggregation_settings(tmp_path):
+    """``kvbm._core.ConnectorLeader`` built from a decode-role configuration dispatches remote
+    prefills over the configured plane, like the vLLM adapter."""
+    import json
+
+    import kvbm._core as kc
+    from kvbm_b200.engine.cd_plane import FilePeerDirectory, FilePrefillPlane
+
+    cfg = {"cache": {"host": {"num_blocks": 16}},
+           "disagg": {"role": "decode", "instance_id": 5, "prefill_instance": 6, "selection": "always",
+                      "directory": f"file://{tmp_path}", "mailbox_slots": 2}}
+    rt = kc.KvbmRuntime.build_leader(json.dumps(cfg))
+    try:
+        FilePeerDirectory(str(tmp_path)).publish(6, {"tp": 1, "rank": 0, "instance": 6})
+        leader = kc.ConnectorLeader(rt, 16)
+        leader.initialize_workers(layout={"g2_blocks": 16, "g3_blocks": 0})
+        leader.create_slot(kc.KvbmRequest("d", list(range(40))))
+        assert leader.get_num_new_matched_tokens("d", 0) == (40, True)
+        leader.update_state_after_alloc("d", [1, 2, 3], 40)
+        [got] = FilePrefillPlane(str(tmp_path)).poll(6)
+        assert got["request_id"] == "d" and got["decode"]["instance"] == 5
+    finally:
+        rt.shutdown()
