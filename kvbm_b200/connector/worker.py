@@ -48,6 +48,7 @@ from ..engine.worker import Worker
 from ..physical.layout import KvLayout, LayoutDescriptor
 from ..physical.transfer import TransferCapabilities, TransferOptions
 from ..utils.config import KvbmConfig
+from ..utils.tracing import nvtx_range
 from .dim_probe import (KvDim, infer_from_shape, layout_from_cross_layer_tensor, layout_from_layer_tensors)
 from .protocol import ConnectorMetadata, PushOp
 
@@ -389,6 +390,10 @@ class ConnectorWorker:
         self._pushes = []
 
     def start_load_kv(self) -> None:
+        with nvtx_range("kvbm.connector.start_load_kv"):
+            self._start_load_kv()
+
+    def _start_load_kv(self) -> None:
         meta = self._meta
         for op in (meta.pull if meta is not None else ()):
             # host-to-host copy of another instance's G2 blocks; the leader registers them (and only then
@@ -478,6 +483,10 @@ class ConnectorWorker:
         st = torch.cuda.current_stream(self.device)
         from ..ops import kv_ops
 
+        with nvtx_range(f"kvbm.connector.push.layers{first}-{layer}"):
+            self._push_batch(first, layer, st, requests, kv_ops)
+
+    def _push_batch(self, first: int, layer: int, st, requests, kv_ops) -> None:
         for op, targets, src, dst in self._pushes:
             if requests is not None and op.req_id not in requests:
                 continue
@@ -495,6 +504,10 @@ class ConnectorWorker:
                                               * c.bytes_per_chunk * nh // c.num_heads))
 
     def wait_for_save(self) -> None:
+        with nvtx_range("kvbm.connector.wait_for_save"):
+            self._wait_for_save()
+
+    def _wait_for_save(self) -> None:
         meta = self._meta
         if meta is None:
             return
