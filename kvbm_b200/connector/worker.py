@@ -624,6 +624,14 @@ class ConnectorWorker:
                 ev.synchronize()
 
     def shutdown(self) -> None:
+        # leave the node's directory first: a pool entry outliving this process would name IPC
+        # handles nobody can open any more
+        withdraw = getattr(self.directory, "withdraw", None)
+        if withdraw is not None:
+            try:
+                withdraw(self.instance_id, rank=self.tp_rank)
+            except OSError:
+                pass
         for c in self._peers.values():
             c.close()
         self._peers.clear()

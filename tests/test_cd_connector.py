@@ -354,3 +354,18 @@ def test_prefill_engine_served_from_the_file_plane_without_a_hub(tmp_path):
         if server is not None:
             server.close()
         loop.call_soon_threadsafe(loop.stop)
+
+
+def test_worker_withdraws_its_directory_entry_on_shutdown(tmp_path):
+    """A connector worker that joined the plane removes its pool entry when it shuts down."""
+    from kvbm_b200.connector.worker import ConnectorWorker
+    from kvbm_b200.engine.cd_plane import FilePeerDirectory
+
+    d = FilePeerDirectory(str(tmp_path))
+    w = ConnectorWorker(device=0)
+    w.instance_id, w.directory, w.tp_rank = 9, d, 0
+    d.publish(9, {"tp": 1}, rank=0)
+    assert d.lookup(9, timeout_s=0.1) == {"tp": 1}
+    w.shutdown()
+    with pytest.raises(TimeoutError):
+        d.lookup(9, timeout_s=0.05)
