@@ -323,6 +323,8 @@ def _define():
                     if g3 is not None:
                         col.add_pool("g3", g3)
                     col.cache = self._leader.stats
+                    if self._leader.cd is not None:
+                        self._leader.cd.metrics = col.cd  # kvbm_cd_* counters from the decisions
                     self._metrics_server = serve_metrics(col, int(cfg.metrics.port))
                 self._remote = None
                 if searching:

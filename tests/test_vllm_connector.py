@@ -267,13 +267,16 @@ def test_scheduler_connector_serves_prometheus_metrics():
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     conn = vc.KvbmConnector(_vllm_config({"leader": {"cache": {"host": {"num_blocks": 64}},
-                                                     "metrics": {"enabled": True, "port": port}}}),
+                                                     "metrics": {"enabled": True, "port": port},
+                                                     "disagg": {"role": "decode", "instance_id": 1,
+                                                                "prefill_instance": 2, "selection": "never"}}}),
                             vllm_base.KVConnectorRole.SCHEDULER)
     try:
         conn.get_num_new_matched_tokens(_request("m", list(range(40))), 0)
         body = urllib.request.urlopen(f"http://127.0.0.1:{port}/metrics", timeout=5).read().decode()
         assert 'kvbm_reset_pool_size{tier="g2"} 64.0' in body
         assert "kvbm_allocations_total" in body and "kvbm_host_cache_hit_rate" in body
+        assert "kvbm_cd_decisions" in body
     finally:
         conn.shutdown()
 
