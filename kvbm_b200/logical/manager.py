@@ -116,7 +116,10 @@ class ImmutableBlock(_Handle):
     __slots__ = ("sequence_hash", "kind")
 
     def __init__(self, mgr, block_id, sequence_hash, kind: str = "primary"):
-        super().__init__(mgr, block_id)
+        # the base initialiser inlined: a prefix match builds one handle per hit
+        self._mgr = mgr
+        self.block_id = block_id
+        self._live = True
         self.sequence_hash = sequence_hash
         self.kind = kind
 
